@@ -1,0 +1,280 @@
+"""Serving benchmark: output tokens/s of the continuous-batching engine.
+
+Workload (Qwen2.5-7B architecture, bf16, random N(0, 0.02) weights from seed 0):
+256 concurrent requests, prompt lengths uniform in [512, 2048], token ids
+uniform over the 152064-entry vocab, 256 output tokens each (EOS ignored),
+chunked prefill with a 2048-token step budget, paged KV with 16-token blocks,
+sampling with the runtime defaults (T 0.7, top-k 40, top-p 0.9, repetition
+penalty 1.15).  One benchmark "step" serves the whole workload to completion.
+
+    python bench.py --gpus N --steps K --warmup W            (torchrun for N > 1)
+    python bench.py --impl reference ...                      reference arm
+
+The device-timed value brackets the K steps with CUDA events (barrier +
+synchronize on both sides, max over ranks).  The ``e2e`` value runs the same
+workload through ``LLMEngine.generate`` (the public API) and times it with the
+host clock; every engine step copies its inputs host->device from pinned
+memory and reads its sampled tokens back device->host.  Weights (15 GB) and
+the KV working set are far larger than the 126 MB L2, so no explicit L2
+flush is needed between steps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "output tok/s on 8×B200 (device-timed, max over ranks); p50 TTFT; p50 TPOT"
+REASON_BITS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+    0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+    0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=1)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="kapsl", choices=["kapsl", "reference"])
+    p.add_argument("--model", default="qwen2.5-7b")
+    p.add_argument("--num-requests", type=int, default=256)
+    p.add_argument("--min-prompt", type=int, default=512)
+    p.add_argument("--max-prompt", type=int, default=2048)
+    p.add_argument("--output-len", type=int, default=256)
+    p.add_argument("--chunk", type=int, default=2048)
+    p.add_argument("--parallel", default="dp", choices=["dp", "tp"])
+    p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--num-layers", type=int, default=0, help="override (testing only; invalid for the metric)")
+    p.add_argument("--warmup-scale", type=float, default=1.0,
+                   help="fraction of requests served by each warm-up step")
+    return p.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu),
+                 "--query-gpu=clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], 0.0, set()
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) < 4:
+                    continue
+                try:
+                    sm.append(float(parts[0]))
+                    mx = max(mx, float(parts[1]))
+                    bits = int(parts[3], 16) if parts[3].startswith("0x") else int(parts[3])
+                except ValueError:
+                    continue
+                for b, name in REASON_BITS.items():
+                    if bits & b and name != "gpu_idle":
+                        reasons.add(name)
+        except OSError:
+            pass
+        finally:
+            try:
+                os.unlink(self.path)
+            except OSError:
+                pass
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx or None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_workload(args, vocab: int, seed: int = 1):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(args.min_prompt, args.max_prompt + 1, size=args.num_requests)
+    return [rng.integers(0, vocab, size=int(n)).tolist() for n in lens]
+
+
+def reference_arm(args):
+    """The reference is a Rust/maturin project; it cannot be installed offline here."""
+    ref_dir = os.path.join(ROOT, "baseline", "_ref")
+    why = ("reference (kapsl-sdk, Rust crates + PyO3/maturin) is not installable offline: pip reports "
+           "BackendUnavailable 'No module named maturin' and no cargo/rustc toolchain exists; its LLM path "
+           "also needs ONNX Runtime binaries downloaded at build time")
+    if os.path.isdir(ref_dir) and any(n.startswith("kapsl_sdk") for n in os.listdir(ref_dir)):
+        why = "reference kapsl_sdk installed but it is a client only: no runtime server binary to serve the workload"
+    rank = int(os.environ.get("RANK", "0"))
+    if rank == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}))
+    return 0
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    assert world == args.gpus, f"--gpus {args.gpus} but WORLD_SIZE {world}"
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=dev)
+
+    from kapsl_sdk_b200._ext import cuda_ops
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.models.config import get_preset
+
+    cuda_ops()
+    cfg = get_preset(args.model)
+    if args.num_layers:
+        cfg.num_layers = args.num_layers
+    tp_comm = None
+    if args.parallel == "tp" and world > 1:
+        from kapsl_sdk_b200.parallel.tp import TPComm
+
+        tp_comm = TPComm.from_world()
+    ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
+                        max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph)
+    engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0)
+    # data-parallel replicas serve their own copy of the workload (weak scaling);
+    # tensor parallel shares one workload across the ranks (strong scaling).
+    prompts = make_workload(args, cfg.vocab_size, seed=1 + (rank if tp_comm is None else 0))
+    params = SamplingParams(max_new_tokens=args.output_len, temperature=0.7, top_k=40, top_p=0.9,
+                            repetition_penalty=1.15, ignore_eos=True)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def serve(ps):
+        seqs = [engine.add_request(f"bench-{serve.n}-{i}", p, params) for i, p in enumerate(ps)]
+        serve.n += 1
+        while engine.has_unfinished():
+            engine.step()
+        return seqs
+
+    serve.n = 0
+    nwarm = max(1, int(len(prompts) * args.warmup_scale))
+    for _ in range(args.warmup):
+        serve(prompts[:nwarm])
+    torch.cuda.synchronize()
+    barrier()
+
+    # ---------------- device-timed region
+    launches0 = engine.runner.launches
+    h2d0, d2h0 = engine.runner.stats["h2d_bytes"], engine.runner.stats["d2h_bytes"]
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    all_seqs = []
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        start.record()
+        for _ in range(args.steps):
+            all_seqs.extend(serve(prompts))
+        end.record()
+        torch.cuda.synchronize()
+        barrier()
+    ms = start.elapsed_time(end)
+    launches = engine.runner.launches - launches0
+    h2d = (engine.runner.stats["h2d_bytes"] - h2d0) / args.steps
+    d2h = (engine.runner.stats["d2h_bytes"] - d2h0) / args.steps
+    out_tokens = sum(len(s.output_ids) for s in all_seqs)
+    ttft = statistics.median([s.ttft() for s in all_seqs if s.ttft() is not None])
+    tpot = statistics.median([s.tpot() for s in all_seqs if s.tpot() is not None])
+
+    # ---------------- end to end through the public API (host clock)
+    barrier()
+    t0 = time.perf_counter()
+    outs = engine.generate(prompts, params)
+    torch.cuda.synchronize()
+    e2e_s = time.perf_counter() - t0
+    e2e_tokens = sum(len(o) for o in outs)
+    barrier()
+
+    vals = torch.tensor([ms, out_tokens, e2e_s, e2e_tokens, ttft, tpot], dtype=torch.float64, device=dev)
+    if world > 1:
+        gathered = [torch.zeros_like(vals) for _ in range(world)]
+        dist.all_gather(gathered, vals)
+        g = torch.stack(gathered)
+        ms_max = float(g[:, 0].max())
+        e2e_max = float(g[:, 2].max())
+        if tp_comm is None:
+            tot_tokens = float(g[:, 1].sum())
+            tot_e2e_tokens = float(g[:, 3].sum())
+        else:
+            tot_tokens = float(g[0, 1])
+            tot_e2e_tokens = float(g[0, 3])
+        ttft_all = float(g[:, 4].max())
+        tpot_all = float(g[:, 5].max())
+    else:
+        ms_max, e2e_max, tot_tokens, tot_e2e_tokens, ttft_all, tpot_all = ms, e2e_s, out_tokens, e2e_tokens, ttft, tpot
+    value = tot_tokens / (ms_max / 1000.0)
+    par = (f"tp{world}" if tp_comm is not None else f"dp{world}")
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True, "scaling": "weak" if tp_comm is None else "strong", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic token ids, random-init weights N(0,0.02) seed 0",
+            "config": {"model": "Qwen2.5-7B-arch" if args.model == "qwen2.5-7b" else args.model,
+                       "global_batch": args.num_requests * (world if tp_comm is None else 1),
+                       "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}] + {args.output_len} out",
+                       "parallelism": par, "chunked_prefill": args.chunk, "kv_block": 16,
+                       "l2": "inputs larger than L2 (15 GB weights, GB-scale KV), no flush",
+                       "num_layers": cfg.num_layers},
+            "p50_ttft_ms": round(ttft_all * 1000, 2), "p50_tpot_ms": round(tpot_all * 1000, 3),
+            "clocks": clocks.summary(),
+            "e2e": {"value": round(tot_e2e_tokens / e2e_max, 2), "unit": "output tokens/s",
+                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
+                    "api": "LLMEngine.generate"},
+            "gpu_launches": int(launches),
+        }
+        print(json.dumps(line))
+    engine.shutdown()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,239 @@
+// Python bindings of the sm_100a kernels (module kapsl_sdk_b200._cuda).
+// Every entry point validates device, dtype, shape and strides, then launches
+// on the current torch CUDA stream, so all of them are CUDA-graph capturable.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+using torch::Tensor;
+
+#define CHECK_CUDA_T(x, name) TORCH_CHECK((x).is_cuda(), name " must be a CUDA tensor")
+#define CHECK_DT(x, dt, name) TORCH_CHECK((x).scalar_type() == (dt), name " has the wrong dtype")
+
+inline __nv_bfloat16* bf(const Tensor& t) { return reinterpret_cast<__nv_bfloat16*>(t.data_ptr()); }
+inline cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void rmsnorm(Tensor out, Tensor x, Tensor w, double eps, c10::optional<Tensor> residual) {
+  CHECK_CUDA_T(x, "x");
+  CHECK_DT(x, at::kBFloat16, "x");
+  CHECK_DT(out, at::kBFloat16, "out");
+  CHECK_DT(w, at::kBFloat16, "weight");
+  TORCH_CHECK(x.dim() == 2 && out.dim() == 2 && x.stride(1) == 1 && out.stride(1) == 1, "rmsnorm: 2-D row-major");
+  const int H = (int)x.size(1);
+  TORCH_CHECK(w.numel() == H && out.size(1) == H && out.size(0) == x.size(0), "rmsnorm: shape mismatch");
+  __nv_bfloat16* r = nullptr;
+  int64_t rs = 0;
+  if (residual.has_value()) {
+    CHECK_DT(*residual, at::kBFloat16, "residual");
+    TORCH_CHECK(residual->size(0) == x.size(0) && residual->size(1) == H && residual->stride(1) == 1,
+                "rmsnorm: residual shape");
+    r = bf(*residual);
+    rs = residual->stride(0);
+  }
+  const c10::cuda::CUDAGuard g(x.device());
+  kapsl::launch_rmsnorm(bf(out), out.stride(0), bf(x), x.stride(0), r, rs, bf(w), (int)x.size(0), H, (float)eps,
+                        cur_stream());
+}
+
+void rope_kv_write(Tensor qkv, Tensor positions, c10::optional<Tensor> slots, Tensor cos_sin, Tensor k_cache,
+                   Tensor v_cache, int64_t Hq, int64_t Hkv, int64_t D) {
+  CHECK_DT(qkv, at::kBFloat16, "qkv");
+  CHECK_DT(positions, at::kInt, "positions");
+  CHECK_DT(cos_sin, at::kFloat, "cos_sin");
+  TORCH_CHECK(qkv.dim() == 2 && qkv.stride(1) == 1 && qkv.size(1) >= (Hq + 2 * Hkv) * D, "rope: qkv layout");
+  TORCH_CHECK(cos_sin.dim() == 2 && cos_sin.size(1) == D && cos_sin.is_contiguous(), "rope: cos_sin [max_pos, D]");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(1) == Hkv && k_cache.size(3) == D && k_cache.is_contiguous(),
+              "rope: k_cache [blocks, Hkv, BS, D]");
+  TORCH_CHECK(v_cache.sizes() == k_cache.sizes() && v_cache.is_contiguous(), "rope: v_cache layout");
+  const int64_t* sp = nullptr;
+  if (slots.has_value()) {
+    CHECK_DT(*slots, at::kLong, "slots");
+    TORCH_CHECK(slots->numel() >= qkv.size(0), "rope: slots too short");
+    sp = slots->data_ptr<int64_t>();
+  }
+  TORCH_CHECK(positions.numel() >= qkv.size(0), "rope: positions too short");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  kapsl::launch_rope_kv_write(bf(qkv), qkv.stride(0), positions.data_ptr<int32_t>(), sp, cos_sin.data_ptr<float>(),
+                              bf(k_cache), bf(v_cache), (int)qkv.size(0), (int)Hq, (int)Hkv, (int)D,
+                              (int)k_cache.size(2), cur_stream());
+}
+
+void silu_mul(Tensor out, Tensor x) {
+  CHECK_DT(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && x.size(1) == 2 * out.size(1) && x.size(0) == out.size(0),
+              "silu_mul: x [T, 2F], out [T, F]");
+  const c10::cuda::CUDAGuard g(x.device());
+  kapsl::launch_silu_mul(bf(out), bf(x), (int)x.size(0), (int)out.size(1), cur_stream());
+}
+
+void embedding(Tensor out, Tensor table, Tensor ids, int64_t vocab_start) {
+  CHECK_DT(table, at::kBFloat16, "table");
+  CHECK_DT(ids, at::kInt, "ids");
+  TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && out.size(1) == table.size(1), "embedding: layout");
+  TORCH_CHECK(out.size(0) <= ids.numel(), "embedding: ids too short");
+  const c10::cuda::CUDAGuard g(table.device());
+  kapsl::launch_embedding(bf(out), bf(table), ids.data_ptr<int32_t>(), (int)out.size(0), (int)table.size(1),
+                          vocab_start, table.size(0), cur_stream());
+}
+
+CUtensorMap cache_map(const Tensor& cache) {
+  TORCH_CHECK(cache.dim() == 4 && cache.is_contiguous() && cache.size(2) == 16 && cache.size(3) == 128,
+              "attention: cache must be [blocks, Hkv, 16, 128] contiguous");
+  CHECK_DT(cache, at::kBFloat16, "cache");
+  const uint64_t rows = (uint64_t)cache.size(0) * cache.size(1) * 16;
+  return kapsl::make_tmap_2d_bf16(cache.data_ptr(), rows, 128, 128, 16, 64, true);
+}
+
+int64_t decode_num_splits(int64_t B, int64_t Hkv, int64_t max_ctx) {
+  return kapsl::decode_attn_num_splits((int)B, (int)Hkv, (int)max_ctx, kapsl::gemm_num_sms());
+}
+
+void decode_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_tables, Tensor ctx_lens, Tensor out,
+                      int64_t Hq, int64_t Hkv, double scale, int64_t nsplit, c10::optional<Tensor> part_o,
+                      c10::optional<Tensor> part_lse, Tensor err) {
+  CHECK_DT(q, at::kBFloat16, "q");
+  CHECK_DT(out, at::kBFloat16, "out");
+  CHECK_DT(block_tables, at::kInt, "block_tables");
+  CHECK_DT(ctx_lens, at::kInt, "ctx_lens");
+  CHECK_DT(err, at::kInt, "err");
+  TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) >= Hq * 128, "decode: q [B, >=Hq*128]");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(1) >= Hq * 128, "decode: out [B, >=Hq*128]");
+  TORCH_CHECK(block_tables.dim() == 2 && block_tables.is_contiguous(), "decode: block_tables [B, max_blocks]");
+  const int B = (int)q.size(0);
+  TORCH_CHECK(block_tables.size(0) >= B && ctx_lens.numel() >= B && out.size(0) >= B, "decode: batch mismatch");
+  TORCH_CHECK(k_cache.size(1) == Hkv, "decode: Hkv mismatch");
+  float* po = nullptr;
+  float* pl = nullptr;
+  if (nsplit > 1) {
+    TORCH_CHECK(part_o.has_value() && part_lse.has_value(), "decode: split-KV needs scratch");
+    TORCH_CHECK(part_o->numel() >= (int64_t)B * Hq * nsplit * 128 && part_lse->numel() >= (int64_t)B * Hq * nsplit,
+                "decode: scratch too small");
+    po = part_o->data_ptr<float>();
+    pl = part_lse->data_ptr<float>();
+  }
+  const c10::cuda::CUDAGuard g(q.device());
+  CUtensorMap tk = cache_map(k_cache), tv = cache_map(v_cache);
+  kapsl::launch_decode_attention(tk, tv, bf(q), q.stride(0), block_tables.data_ptr<int32_t>(),
+                                 (int)block_tables.size(1), ctx_lens.data_ptr<int32_t>(), bf(out), out.stride(0), po,
+                                 pl, B, (int)Hq, (int)Hkv, (int)nsplit, (float)scale, err.data_ptr<int>(),
+                                 cur_stream());
+}
+
+void prefill_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor work, Tensor seq_info, Tensor block_tables,
+                       Tensor out, int64_t Hq, int64_t Hkv, double scale, Tensor err) {
+  CHECK_DT(q, at::kBFloat16, "q");
+  CHECK_DT(work, at::kInt, "work");
+  CHECK_DT(seq_info, at::kInt, "seq_info");
+  CHECK_DT(block_tables, at::kInt, "block_tables");
+  TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) >= Hq * 128, "prefill: q [T, >=Hq*128]");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "prefill: out row-major");
+  TORCH_CHECK(work.dim() == 2 && work.size(1) == 2 && work.is_contiguous(), "prefill: work [n, 2]");
+  TORCH_CHECK(seq_info.dim() == 2 && seq_info.size(1) == 4 && seq_info.is_contiguous(), "prefill: seq_info [S, 4]");
+  const c10::cuda::CUDAGuard g(q.device());
+  CUtensorMap tk = cache_map(k_cache), tv = cache_map(v_cache);
+  kapsl::launch_prefill_attention(tk, tv, bf(q), q.stride(0), work.data_ptr<int32_t>(), (int)work.size(0),
+                                  seq_info.data_ptr<int32_t>(), block_tables.data_ptr<int32_t>(),
+                                  (int)block_tables.size(1), bf(out), out.stride(0), (int)Hq, (int)Hkv, (float)scale,
+                                  err.data_ptr<int>(), cur_stream());
+}
+
+// rng and counts are per-sequence tables indexed by slots[row] (row itself when slots is None).
+void sample(Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, c10::optional<Tensor> rep_penalty,
+            c10::optional<Tensor> counts, c10::optional<Tensor> slots, Tensor rng, Tensor out) {
+  CHECK_DT(logits, at::kFloat, "logits");
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits [B, V]");
+  CHECK_DT(rng, at::kLong, "rng");
+  CHECK_DT(out, at::kInt, "out");
+  const int B = (int)logits.size(0);
+  TORCH_CHECK(temperature.numel() >= B && top_k.numel() >= B && top_p.numel() >= B && out.numel() >= B,
+              "sample: per-row parameter arrays too short");
+  TORCH_CHECK(slots.has_value() || rng.numel() >= B, "sample: rng table too short");
+  const float* rp = rep_penalty.has_value() ? rep_penalty->data_ptr<float>() : nullptr;
+  const int32_t* cn = counts.has_value() ? counts->data_ptr<int32_t>() : nullptr;
+  const int32_t* cr = nullptr;
+  if (slots.has_value()) {
+    CHECK_DT(*slots, at::kInt, "slots");
+    TORCH_CHECK(slots->numel() >= B, "sample: slots too short");
+    cr = slots->data_ptr<int32_t>();
+  }
+  if (cn) TORCH_CHECK(counts->size(-1) == logits.size(1), "sample: counts width must equal vocab");
+  const c10::cuda::CUDAGuard g(logits.device());
+  kapsl::launch_sample(logits.data_ptr<float>(), logits.stride(0), B, (int)logits.size(1),
+                       temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(), rp, cn, cr,
+                       reinterpret_cast<uint64_t*>(rng.data_ptr<int64_t>()), out.data_ptr<int32_t>(), cur_stream());
+}
+
+void count_tokens(Tensor counts, Tensor rows, Tensor ids) {
+  CHECK_DT(counts, at::kInt, "counts");
+  CHECK_DT(rows, at::kInt, "rows");
+  CHECK_DT(ids, at::kInt, "ids");
+  TORCH_CHECK(rows.numel() == ids.numel(), "count_tokens: rows/ids length");
+  const c10::cuda::CUDAGuard g(counts.device());
+  kapsl::launch_count_tokens(counts.data_ptr<int32_t>(), (int)counts.size(-1), rows.data_ptr<int32_t>(),
+                             ids.data_ptr<int32_t>(), (int)ids.numel(), cur_stream());
+}
+
+void gemm(Tensor A, Tensor B, Tensor C, int64_t epi, c10::optional<Tensor> bias, c10::optional<Tensor> res,
+          c10::optional<Tensor> workspace, Tensor err, int64_t force_bn, int64_t force_splits) {
+  CHECK_DT(A, at::kBFloat16, "A");
+  CHECK_DT(B, at::kBFloat16, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2, "gemm: 2-D operands");
+  TORCH_CHECK(A.stride(1) == 1 && B.stride(1) == 1 && C.stride(1) == 1, "gemm: K-contiguous A/B, row-major C");
+  const int64_t M = A.size(0), K = A.size(1), N = B.size(0);
+  TORCH_CHECK(B.size(1) == K, "gemm: K mismatch");
+  const bool f32 = C.scalar_type() == at::kFloat;
+  TORCH_CHECK(f32 || C.scalar_type() == at::kBFloat16, "gemm: C must be bf16 or fp32");
+  TORCH_CHECK(C.size(0) == M && C.size(1) == (epi == 3 ? N / 2 : N), "gemm: C shape");
+  TORCH_CHECK(!(f32 && epi != 0), "gemm: fp32 output only with the plain epilogue");
+  const __nv_bfloat16* bp = nullptr;
+  const __nv_bfloat16* rp = nullptr;
+  int64_t ldr = 0;
+  if (epi == 1) {
+    TORCH_CHECK(bias.has_value() && bias->numel() == N, "gemm: bias [N] required");
+    bp = bf(*bias);
+  }
+  if (epi == 2) {
+    TORCH_CHECK(res.has_value() && res->size(0) == M && res->size(1) == N && res->stride(1) == 1,
+                "gemm: residual [M, N] required");
+    rp = bf(*res);
+    ldr = res->stride(0);
+  }
+  float* ws = nullptr;
+  size_t wsb = 0;
+  if (workspace.has_value()) {
+    CHECK_DT(*workspace, at::kFloat, "workspace");
+    ws = workspace->data_ptr<float>();
+    wsb = workspace->numel() * sizeof(float);
+  }
+  const c10::cuda::CUDAGuard g(A.device());
+  kapsl::launch_gemm(bf(A), A.stride(0), bf(B), B.stride(0), C.data_ptr(), C.stride(0), f32, (int)M, (int)N, (int)K,
+                     (int)epi, bp, rp, ldr, ws, wsb, err.data_ptr<int>(), cur_stream(), (int)force_bn,
+                     (int)force_splits);
+}
+
+int64_t launch_count() { return (int64_t)kapsl::launch_count(); }
+int64_t num_sms() { return kapsl::gemm_num_sms(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "kapsl_sdk_b200 sm_100a kernels";
+  m.def("rmsnorm", &rmsnorm, "RMSNorm (optionally residual += x first)", py::arg("out"), py::arg("x"),
+        py::arg("weight"), py::arg("eps"), py::arg("residual") = py::none());
+  m.def("rope_kv_write", &rope_kv_write, "RoPE on q/k in place + paged KV write");
+  m.def("silu_mul", &silu_mul, "SwiGLU: out = silu(x[:, :F]) * x[:, F:]");
+  m.def("embedding", &embedding, "embedding gather (rows outside the shard are zero)");
+  m.def("decode_num_splits", &decode_num_splits);
+  m.def("decode_attention", &decode_attention, "paged split-KV decode attention");
+  m.def("prefill_attention", &prefill_attention, "paged chunked-prefill attention");
+  m.def("sample", &sample, "top-k/top-p/temperature/penalty sampler with per-row LCG");
+  m.def("count_tokens", &count_tokens, "counts[rows[i], ids[i]] += 1");
+  m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A @ B^T)");
+  m.def("launch_count", &launch_count, "kernels launched through this library so far");
+  m.def("num_sms", &num_sms);
+}

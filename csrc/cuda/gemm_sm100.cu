@@ -1,0 +1,527 @@
+// Persistent bf16 GEMM on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+//   C[M, N] = epilogue( A[M, K] . B[N, K]^T )        A, B: bf16, K contiguous
+//
+// Warp roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: one elected thread streams 128x64 A and BNx64 B
+//               tiles (128-byte swizzle) into a STAGES-deep smem ring.
+//   warp 1      MMA issuer: allocates TMEM, one thread issues
+//               tcgen05.mma.cta_group::1.kind::f16 (M=128, N=BN, K=16) from
+//               smem descriptors and commits to mbarriers.
+//   warps 2..5  epilogue: tcgen05.ld 32x32b rows out of TMEM (two accumulator
+//               buffers so tile i's epilogue overlaps tile i+1's mainloop),
+//               apply the fused op and store.
+//
+// Fused epilogues: plain, +bias[N], +residual[M,N] (may alias C), SwiGLU over
+// an interleaved gate/up weight (per BN-column tile: first BN/2 columns gate,
+// last BN/2 up) writing C[M, N/2].  Split-K writes fp32 partials that
+// `splitk_reduce_kernel` sums and finishes with the same epilogue.
+//
+// No cluster multicast is used anywhere in this file.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace kapsl {
+
+using bf16 = __nv_bfloat16;
+
+namespace gemm {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int kThreads = 192;
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// K-major, 128-byte swizzled operand tile: rows of 128 B, 8-row atoms of 1 KiB.
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);   // start address
+  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for SW128 K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: 8 rows * 128 B
+  d |= (uint64_t)1 << 46;                   // descriptor version (sm100)
+  d |= (uint64_t)2 << 61;                   // layout: SWIZZLE_128B
+  return d;
+}
+
+template <int BN>
+__host__ __device__ constexpr uint32_t instr_desc_bf16() {
+  return (1u << 4)                     // D format f32
+         | (1u << 7)                   // A format bf16
+         | (1u << 10)                  // B format bf16
+         | ((uint32_t)(BN >> 3) << 17)  // N
+         | ((uint32_t)(BM >> 4) << 24); // M
+}
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
+
+struct EpiArgs {
+  void* out;           // bf16 or fp32
+  int64_t ldc;         // elements
+  const bf16* bias;    // [N] or null
+  const bf16* res;     // [M, N] or null
+  int64_t ldr;
+  float* partial;      // split-K fp32 partials [splits, M, N]
+};
+
+// Store 32 consecutive columns (c0..c0+31) of one row.
+template <bool OUT_F32>
+__device__ __forceinline__ void store_row32(void* out, int64_t ldc, int row, int c0, int ncols_valid,
+                                            const float (&v)[32]) {
+  if (OUT_F32) {
+    float* dst = reinterpret_cast<float*>(out) + (int64_t)row * ldc + c0;
+    if (ncols_valid >= 32) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else {
+      for (int i = 0; i < ncols_valid; ++i) dst[i] = v[i];
+    }
+  } else {
+    bf16* dst = reinterpret_cast<bf16*>(out) + (int64_t)row * ldc + c0;
+    if (ncols_valid >= 32) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 u;
+        u.x = pack_bf16(v[8 * i + 0], v[8 * i + 1]);
+        u.y = pack_bf16(v[8 * i + 2], v[8 * i + 3]);
+        u.z = pack_bf16(v[8 * i + 4], v[8 * i + 5]);
+        u.w = pack_bf16(v[8 * i + 6], v[8 * i + 7]);
+        reinterpret_cast<uint4*>(dst)[i] = u;
+      }
+    } else {
+      for (int i = 0; i < ncols_valid; ++i) dst[i] = __float2bfloat16(v[i]);
+    }
+  }
+}
+
+__device__ __forceinline__ void load_bf16x32(const bf16* src, int nvalid, float (&v)[32]) {
+  if (nvalid >= 32) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 u = reinterpret_cast<const uint4*>(src)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = __bfloat1622float2(h[j]);
+        v[8 * i + 2 * j] = f.x;
+        v[8 * i + 2 * j + 1] = f.y;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = (i < nvalid) ? __bfloat162float(src[i]) : 0.f;
+  }
+}
+
+// EPI: 0 plain, 1 bias, 2 residual, 3 swiglu (interleaved), 4 split-K partial (fp32, raw)
+template <int BN, int STAGES, int EPI, bool OUT_F32>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
+                int N, int K, int splits, EpiArgs ep, int* __restrict__ err) {
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  constexpr uint32_t TMEM_COLS = (2 * BN <= 32) ? 32 : (2 * BN <= 64) ? 64 : (2 * BN <= 128) ? 128 : (2 * BN <= 256) ? 256 : 512;
+  constexpr uint32_t IDESC = instr_desc_bf16<BN>();
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int k_blocks_total = (K + BK - 1) / BK;
+  const int k_per_split = (k_blocks_total + splits - 1) / splits;
+  const int num_units = m_tiles * n_tiles * splits;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);
+    }
+    abort_sh = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) tmem_alloc(&tmem_base_sh, TMEM_COLS);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  // unit -> (m tile, n tile, split); m fastest so co-resident CTAs share B tiles in L2.
+  auto decode_unit = [&](int u, int& mt, int& nt, int& sp) {
+    sp = u % splits;
+    const int t = u / splits;
+    mt = t % m_tiles;
+    nt = t / m_tiles;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued_unwaited = 0;
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)&abort_sh; u += gridDim.x) {
+        int mt, nt, sp;
+        decode_unit(u, mt, nt, sp);
+        const int kb0 = sp * k_per_split;
+        const int kb1 = min(k_blocks_total, kb0 + k_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1)) {
+            abort_sh = 1;
+            atomicExch(err, 10);
+            break;
+          }
+          uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
+          tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, mt * BM);
+          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, nt * BN);
+          ++issued_unwaited;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      (void)issued_unwaited;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)&abort_sh; u += gridDim.x, ++it) {
+        int mt, nt, sp;
+        decode_unit(u, mt, nt, sp);
+        const int kb0 = sp * k_per_split;
+        const int kb1 = min(k_blocks_total, kb0 + k_per_split);
+        const int acc = it & 1;
+        const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1)) {
+          abort_sh = 1;
+          atomicExch(err, 11);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase)) {
+            abort_sh = 1;
+            atomicExch(err, 12);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
+          const uint32_t sb = sa + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = smem_desc_sw128(sa + k * 32);
+            const uint64_t bd = smem_desc_sw128(sb + k * 32);
+            mma_bf16(d_tmem, ad, bd, IDESC, (kb > kb0 || k > 0) ? 1u : 0u);
+          }
+          mma_commit(&empty_bar[stage]);  // frees the smem stage once these MMAs retire
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (*(volatile int*)&abort_sh) break;
+        mma_commit(&tfull_bar[acc]);  // accumulator ready for the epilogue
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps 2..5 -> TMEM lane quadrant warp % 4
+    const int quad = warp & 3;
+    int it = 0;
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++it) {
+      int mt, nt, sp;
+      decode_unit(u, mt, nt, sp);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+      const bool got = mbar_wait_bounded(&tfull_bar[acc], acc_phase);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) {
+          abort_sh = 1;
+          atomicExch(err, 13);
+        }
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * BM + quad * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      if (EPI == 3) {
+        // SwiGLU over interleaved [gate(BN/2) | up(BN/2)] columns of this tile.
+        constexpr int HALF = BN / 2;
+        const int out_c0 = nt * HALF;
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          float g[32], v[32];
+          tmem_ld32(tbase + c, g);
+          tmem_ld32(tbase + HALF + c, v);
+          if (row < M) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = silu(g[i]) * v[i];
+            const int nvalid = min(32, N / 2 - (out_c0 + c));
+            if (nvalid > 0) store_row32<OUT_F32>(ep.out, ep.ldc, row, out_c0 + c, nvalid, v);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(tbase + c, v);
+          const int col = nt * BN + c;
+          const int nvalid = min(32, N - col);
+          if (row < M && nvalid > 0) {
+            if (EPI == 4) {
+              float* dst = ep.partial + ((int64_t)sp * M + row) * N + col;
+              if (nvalid >= 32) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i)
+                  reinterpret_cast<float4*>(dst)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              } else {
+                for (int i = 0; i < nvalid; ++i) dst[i] = v[i];
+              }
+            } else {
+              if (EPI == 1) {
+                float bb[32];
+                load_bf16x32(ep.bias + col, nvalid, bb);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += bb[i];
+              } else if (EPI == 2) {
+                float rr[32];
+                load_bf16x32(ep.res + (int64_t)row * ep.ldr + col, nvalid, rr);
+#pragma unroll
+                for (int i = 0; i < 32; ++i) v[i] += rr[i];
+              }
+              store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
+}
+
+// Sum split-K partials and apply the epilogue.
+template <int EPI, bool OUT_F32>
+__global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, EpiArgs ep) {
+  const int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const int64_t total = (int64_t)M * N;
+  if (idx >= total) return;
+  float4 acc = reinterpret_cast<const float4*>(partial + idx)[0];
+  for (int s = 1; s < splits; ++s) {
+    float4 p = reinterpret_cast<const float4*>(partial + (int64_t)s * total + idx)[0];
+    acc.x += p.x;
+    acc.y += p.y;
+    acc.z += p.z;
+    acc.w += p.w;
+  }
+  const int row = (int)(idx / N);
+  const int col = (int)(idx % N);
+  float v[4] = {acc.x, acc.y, acc.z, acc.w};
+  if (EPI == 3) {
+    // interleaved gate/up: tile width 256 -> halves of 128
+    const int tile = col / 256, within = col % 256;
+    if (within >= 128) return;  // threads on the "up" half do nothing
+    float u[4];
+    const float4 pu = reinterpret_cast<const float4*>(partial + idx + 128)[0];
+    u[0] = pu.x;
+    u[1] = pu.y;
+    u[2] = pu.z;
+    u[3] = pu.w;
+    for (int s = 1; s < splits; ++s) {
+      float4 p = reinterpret_cast<const float4*>(partial + (int64_t)s * total + idx + 128)[0];
+      u[0] += p.x;
+      u[1] += p.y;
+      u[2] += p.z;
+      u[3] += p.w;
+    }
+    const int oc = tile * 128 + within;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float o = silu(v[i]) * u[i];
+      if (OUT_F32)
+        reinterpret_cast<float*>(ep.out)[(int64_t)row * ep.ldc + oc + i] = o;
+      else
+        reinterpret_cast<bf16*>(ep.out)[(int64_t)row * ep.ldc + oc + i] = __float2bfloat16(o);
+    }
+    return;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (EPI == 1) v[i] += __bfloat162float(ep.bias[col + i]);
+    if (EPI == 2) v[i] += __bfloat162float(ep.res[(int64_t)row * ep.ldr + col + i]);
+    if (OUT_F32)
+      reinterpret_cast<float*>(ep.out)[(int64_t)row * ep.ldc + col + i] = v[i];
+    else
+      reinterpret_cast<bf16*>(ep.out)[(int64_t)row * ep.ldc + col + i] = __float2bfloat16(v[i]);
+  }
+}
+
+template <int BN, int STAGES>
+constexpr size_t smem_bytes() {
+  return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
+}
+
+template <int BN, int STAGES, int EPI, bool F32>
+void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int splits, const EpiArgs& ep,
+                int grid, int* err, cudaStream_t st) {
+  auto kern = gemm_kernel<BN, STAGES, EPI, F32>;
+  constexpr size_t smem = smem_bytes<BN, STAGES>();
+  static int attr_dev = -1;
+  int dev;
+  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_dev = dev;
+  }
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, M, N, K, splits, ep, err);
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
+}  // namespace gemm
+
+int gemm_num_sms() {
+  static int n[16] = {0};
+  int dev;
+  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
+  if (dev < 16 && n[dev] == 0) KAPSL_CHECK_CUDA(cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev));
+  return dev < 16 ? n[dev] : 148;
+}
+
+// Chooses tile width and split-K so that the grid covers the SMs.
+void launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C, int64_t ldc, bool out_f32, int M,
+                 int N, int K, int epi, const bf16* bias, const bf16* res, int64_t ldr, float* workspace,
+                 size_t workspace_bytes, int* err, cudaStream_t st, int force_bn, int force_splits) {
+  using namespace gemm;
+  if (M == 0 || N == 0) return;
+  if (K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0) throw std::runtime_error("gemm: K and leading dims must be multiples of 8");
+  if (ldc % 8 != 0) throw std::runtime_error("gemm: ldc must be a multiple of 8");
+  if (epi == 3 && N % 256 != 0) throw std::runtime_error("gemm: SwiGLU epilogue needs N % 256 == 0");
+  const int sms = gemm_num_sms();
+  int bn = force_bn ? force_bn : 256;
+  if (!force_bn && epi != 3) {
+    // Narrow tiles when the wide grid would leave most SMs idle.
+    const int mt = (M + BM - 1) / BM;
+    const int t256 = mt * ((N + 255) / 256);
+    if (t256 < sms && N % 128 == 0) bn = 128;
+  }
+  if (epi == 3) bn = 256;
+  const int m_tiles = (M + BM - 1) / BM;
+  const int n_tiles = (N + bn - 1) / bn;
+  const int kblocks = (K + BK - 1) / BK;
+  int splits = 1;
+  if (force_splits > 0) {
+    splits = force_splits;
+  } else if (m_tiles * n_tiles < sms / 2 && kblocks >= 8) {
+    splits = std::min(std::min(kblocks / 4, 8), (sms + m_tiles * n_tiles - 1) / (m_tiles * n_tiles));
+    if (splits < 1) splits = 1;
+    if (splits > 1 && (size_t)splits * M * N * sizeof(float) > workspace_bytes) splits = 1;
+  }
+  if (splits > kblocks) splits = kblocks;
+  if (splits > 1 && (workspace == nullptr || (size_t)splits * M * N * sizeof(float) > workspace_bytes))
+    throw std::runtime_error("gemm: split-K needs a larger workspace");
+  if (splits > 1 && N % 4 != 0) throw std::runtime_error("gemm: split-K needs N % 4 == 0");
+  CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, BM, BK);
+  CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, bn, BK);
+  EpiArgs ep{C, ldc, bias, res, ldr, workspace};
+  const int units = m_tiles * n_tiles * splits;
+  const int grid = std::min(units, sms);
+  const int kepi = splits > 1 ? 4 : epi;
+#define KAPSL_GEMM_DISPATCH(BNV, ST)                                                    \
+  switch (kepi) {                                                                      \
+    case 0: out_f32 ? launch_cfg<BNV, ST, 0, true>(ta, tb, M, N, K, splits, ep, grid, err, st)   \
+                    : launch_cfg<BNV, ST, 0, false>(ta, tb, M, N, K, splits, ep, grid, err, st); break; \
+    case 1: launch_cfg<BNV, ST, 1, false>(ta, tb, M, N, K, splits, ep, grid, err, st); break;     \
+    case 2: launch_cfg<BNV, ST, 2, false>(ta, tb, M, N, K, splits, ep, grid, err, st); break;     \
+    case 3: launch_cfg<BNV, ST, 3, false>(ta, tb, M, N, K, splits, ep, grid, err, st); break;     \
+    case 4: launch_cfg<BNV, ST, 4, true>(ta, tb, M, N, K, splits, ep, grid, err, st); break;      \
+    default: throw std::runtime_error("gemm: bad epilogue");                            \
+  }
+  if (bn == 256) {
+    KAPSL_GEMM_DISPATCH(256, 4)
+  } else {
+    KAPSL_GEMM_DISPATCH(128, 6)
+  }
+#undef KAPSL_GEMM_DISPATCH
+  if (splits > 1) {
+    const int64_t total = (int64_t)M * N / 4;
+    const int blocks = (int)((total + 255) / 256);
+    switch (epi) {
+      case 0: out_f32 ? splitk_reduce_kernel<0, true><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep)
+                      : splitk_reduce_kernel<0, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
+      case 1: splitk_reduce_kernel<1, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
+      case 2: splitk_reduce_kernel<2, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
+      case 3: splitk_reduce_kernel<3, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
+    }
+    KAPSL_LAUNCH_CHECK();
+    note_launch();
+  }
+}
+
+}  // namespace kapsl

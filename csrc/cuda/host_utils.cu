@@ -1,0 +1,53 @@
+// Host-side helpers shared by all kernels: launch accounting and TMA
+// descriptor encoding.
+#include <atomic>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace kapsl {
+
+static std::atomic<uint64_t> g_launches{0};
+
+uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
+void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (!fn) throw std::runtime_error("cuTensorMapEncodeTiled is unavailable from the CUDA driver");
+  return fn;
+}
+
+CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols, uint64_t pitch_elems,
+                              uint32_t box_rows, uint32_t box_cols, bool swizzle128) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0)
+    throw std::runtime_error("TMA base address must be 16-byte aligned");
+  if ((pitch_elems * 2) % 16 != 0) throw std::runtime_error("TMA row pitch must be a multiple of 16 bytes");
+  if ((box_cols * 2) % 16 != 0) throw std::runtime_error("TMA box inner extent must be a multiple of 16 bytes");
+  if (swizzle128 && box_cols * 2 > 128) throw std::runtime_error("128B swizzle needs a box of <=128 bytes inner");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {pitch_elems * 2};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                               strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+  return m;
+}
+
+}  // namespace kapsl

@@ -1,0 +1,51 @@
+// Launchers of the sm_100a kernels (raw pointers + stream).  The torch
+// bindings in bindings.cpp validate tensors and call these.
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <cstddef>
+
+namespace kapsl {
+
+void launch_rmsnorm(__nv_bfloat16* out, int64_t out_stride, const __nv_bfloat16* x, int64_t x_stride,
+                    __nv_bfloat16* residual, int64_t res_stride, const __nv_bfloat16* w, int rows, int H, float eps,
+                    cudaStream_t st);
+
+void launch_rope_kv_write(__nv_bfloat16* qkv, int64_t qkv_stride, const int32_t* positions, const int64_t* slots,
+                          const float* cos_sin, __nv_bfloat16* k_cache, __nv_bfloat16* v_cache, int T, int Hq,
+                          int Hkv, int D, int block_size, cudaStream_t st);
+
+void launch_silu_mul(__nv_bfloat16* out, const __nv_bfloat16* x, int T, int F, cudaStream_t st);
+
+void launch_embedding(__nv_bfloat16* out, const __nv_bfloat16* table, const int32_t* ids, int T, int H,
+                      int64_t vocab_start, int64_t vocab_rows, cudaStream_t st);
+
+size_t decode_attn_smem_bytes();
+int decode_attn_num_splits(int B, int Hkv, int max_ctx, int num_sms);
+void launch_decode_attention(const CUtensorMap& tk, const CUtensorMap& tv, const __nv_bfloat16* q, int64_t q_stride,
+                             const int32_t* block_tables, int max_blocks, const int32_t* ctx_lens,
+                             __nv_bfloat16* out, int64_t out_stride, float* part_o, float* part_lse, int B, int Hq,
+                             int Hkv, int nsplit, float scale, int* err, cudaStream_t st);
+
+size_t prefill_attn_smem_bytes();
+void launch_prefill_attention(const CUtensorMap& tk, const CUtensorMap& tv, const __nv_bfloat16* q,
+                              int64_t q_stride, const int32_t* work, int num_work, const int32_t* seq_info,
+                              const int32_t* block_tables, int max_blocks, __nv_bfloat16* out, int64_t out_stride,
+                              int Hq, int Hkv, float scale, int* err, cudaStream_t st);
+
+void launch_sample(float* logits, int64_t stride, int B, int V, const float* temperature, const int32_t* top_k,
+                   const float* top_p, const float* rep_penalty, const int32_t* counts, const int32_t* slots,
+                   uint64_t* rng, int32_t* out, cudaStream_t st);
+void launch_count_tokens(int32_t* counts, int V, const int32_t* rows, const int32_t* ids, int n, cudaStream_t st);
+
+int gemm_num_sms();
+// epi: 0 plain, 1 +bias, 2 +residual, 3 SwiGLU over interleaved gate/up (N % 256 == 0, C is [M, N/2]).
+void launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, void* C, int64_t ldc,
+                 bool out_f32, int M, int N, int K, int epi, const __nv_bfloat16* bias, const __nv_bfloat16* res,
+                 int64_t ldr, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st, int force_bn,
+                 int force_splits);
+
+}  // namespace kapsl

@@ -1,0 +1,207 @@
+"""LLMEngine: continuous-batching generation loop over one GPU (one TP rank set).
+
+Counterpart of the reference ``LLMEngine`` (crates/kapsl-llm/src/engine.rs:816-2499):
+request ingestion with session continuation, seeds
+``splitmix64((seed ?? fnv1a(request_id)) ^ seq_id * golden)`` (seq ids from 1),
+KV admission control (``Overloaded`` above the soft limit, ``ResourceExhausted``
+above the hard one, engine.rs:2144-2263), scheduling, execution, sampling and
+stop handling (EOS, stop ids incl. BOS, max_new_tokens, max length).
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Optional
+
+import numpy as np
+import torch
+
+from ..engine_api import EngineError
+from ..models.config import ModelConfig
+from ..models.llama import CausalLM, ModelWeights, random_weights
+from ..ops import reference as ref
+from .block_manager import make_allocator
+from .kv_cache import KVLayout, KVPool
+from .model_runner import ModelRunner
+from .scheduler import Scheduler
+from .sequence import SamplingParams, Sequence, SequenceStatus
+
+
+@dataclass
+class StepOutput:
+    request_id: str
+    seq: Sequence
+    new_token: int
+    finished: bool
+
+
+@dataclass
+class EngineConfig:
+    max_num_seqs: int = 256
+    max_num_batched_tokens: int = 2048
+    max_model_len: int = 4096
+    block_size: int = 16
+    num_blocks: int = 0                 # 0 = size from memory
+    kv_memory_fraction: float = 0.85    # of free memory after weights
+    enable_prefix_cache: bool = True
+    eviction: str = "lru"
+    use_cuda_graph: bool = True
+    chunked_prefill: bool = True
+    max_session_tokens: int = 0         # 0 = max_model_len
+    kv_soft_limit_bytes: int = 0        # 0 = 90% of hard
+    kv_hard_limit_bytes: int = 0        # 0 = pool size
+
+
+class LLMEngine:
+    def __init__(self, cfg: ModelConfig, weights: Optional[ModelWeights] = None, device="cuda",
+                 engine_cfg: Optional[EngineConfig] = None, tp_comm=None, moe=None, seed: int = 0):
+        self.cfg = cfg
+        self.ecfg = engine_cfg or EngineConfig()
+        self.device = torch.device(device)
+        if weights is None:
+            tp = 1 if tp_comm is None else tp_comm.world_size
+            rank = 0 if tp_comm is None else tp_comm.rank
+            weights = random_weights(cfg, self.device, tp=tp, rank=rank, seed=seed)
+        self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe)
+        e = self.ecfg
+        layout = KVLayout(cfg.num_layers, self.model.hkv, cfg.head_dim, e.block_size)
+        nblocks = e.num_blocks
+        if nblocks <= 0:
+            free, _ = torch.cuda.mem_get_info(self.device)
+            reserve = 6 << 30  # activations, graphs, workspaces
+            nblocks = KVPool.blocks_for_bytes(layout, int(max(free - reserve, 1 << 30) * e.kv_memory_fraction))
+            if tp_comm is not None and tp_comm.world_size > 1:
+                nblocks = tp_comm.min_int(nblocks)
+        self.pool = KVPool(layout, nblocks, self.device)
+        self.allocator = make_allocator(nblocks, e.block_size, e.enable_prefix_cache, e.eviction)
+        self.scheduler = Scheduler(self.allocator, e.max_num_seqs, e.max_num_batched_tokens, e.chunked_prefill,
+                                   e.max_model_len)
+        self.runner = ModelRunner(self.model, self.pool, e.max_num_seqs, e.max_num_batched_tokens, e.max_model_len,
+                                  e.use_cuda_graph)
+        self._seq_ids = itertools.count(1)
+        self.sessions: dict[str, Sequence] = {}
+        self.finished: list[Sequence] = []
+        self.stop_ids = set(x for x in (cfg.eos_token_id, cfg.bos_token_id) if x is not None)
+        self.bytes_per_token = cfg.kv_bytes_per_token() // (1 if tp_comm is None else 1)
+        hard = e.kv_hard_limit_bytes or self.pool.nbytes
+        self.kv_hard = hard
+        self.kv_soft = e.kv_soft_limit_bytes or int(hard * 0.9)
+
+    # ------------------------------------------------------------ requests
+    def _reserved_bytes(self) -> int:
+        tot = 0
+        for s in list(self.scheduler.running) + list(self.scheduler.waiting):
+            tot += (len(s.prompt_ids) + s.params.max_new_tokens) * self.pool.layout.bytes_per_block() // \
+                self.pool.layout.block_size
+        return tot
+
+    def add_request(self, request_id: str, prompt_ids: list, params: Optional[SamplingParams] = None,
+                    session_id: Optional[str] = None, on_token: Optional[Callable] = None,
+                    admission_control: bool = False) -> Sequence:
+        params = params or SamplingParams()
+        prompt_ids = [int(t) for t in prompt_ids]
+        if not prompt_ids:
+            raise EngineError.invalid_input("empty prompt")
+        bad = [t for t in prompt_ids if t < 0 or t >= self.cfg.vocab_size]
+        if bad:
+            raise EngineError.invalid_input(f"token id {bad[0]} outside vocab of {self.cfg.vocab_size}")
+        if admission_control:
+            need = (len(prompt_ids) + params.max_new_tokens) * self.pool.layout.bytes_per_block() // \
+                self.pool.layout.block_size
+            cur = self._reserved_bytes()
+            if need > self.kv_hard:
+                raise EngineError.resource_exhausted(
+                    f"request needs {need} KV bytes, hard limit {self.kv_hard}")
+            if cur + need > self.kv_soft:
+                raise EngineError.overloaded(f"KV reservation {cur + need} bytes above soft limit {self.kv_soft}")
+        seq_id = next(self._seq_ids)
+        if session_id is not None and session_id in self.sessions:
+            # continue the session: new turn appended to the previous sequence's tokens
+            prev = self.sessions[session_id]
+            max_sess = self.ecfg.max_session_tokens or self.ecfg.max_model_len
+            history = prev.prompt_ids + prev.output_ids
+            if len(history) + len(prompt_ids) + params.max_new_tokens <= max_sess:
+                prompt_ids = history + prompt_ids
+        rng = ref.seed_state(params.seed, request_id, seq_id)
+        seq = Sequence(seq_id=seq_id, request_id=request_id, prompt_ids=prompt_ids, params=params, rng_state=rng,
+                       session_id=session_id, on_token=on_token)
+        if len(prompt_ids) + 1 > self.ecfg.max_model_len:
+            raise EngineError.invalid_input(
+                f"prompt of {len(prompt_ids)} tokens exceeds max_model_len {self.ecfg.max_model_len}")
+        self.scheduler.add(seq)
+        if session_id is not None:
+            self.sessions[session_id] = seq
+        return seq
+
+    def abort(self, request_id: str) -> None:
+        for s in self.scheduler.abort(request_id):
+            s.finish_time = time.perf_counter()
+            s.finish_reason = "aborted"
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work()
+
+    # ---------------------------------------------------------------- step
+    def _stop(self, s: Sequence, tok: int) -> Optional[str]:
+        p = s.params
+        if not p.ignore_eos and (tok in self.stop_ids or tok in p.stop_token_ids):
+            return "stop"
+        if len(s.output_ids) >= p.max_new_tokens:
+            return "length"
+        if s.length >= self.ecfg.max_model_len:
+            return "length"
+        return None
+
+    def step(self) -> list[StepOutput]:
+        batch = self.scheduler.schedule()
+        if batch.empty:
+            return []
+        if batch.admitted:
+            self.runner.admit(batch.admitted)
+        seqs, toks = self.runner.execute(batch)
+        now = time.perf_counter()
+        for s in batch.decode:
+            s.num_computed += 1
+        for s, n in batch.prefill:
+            s.num_computed += n
+        outs = []
+        for s, tok in zip(seqs, toks.tolist()):
+            s.output_ids.append(tok)
+            if s.first_token_time is None:
+                s.first_token_time = now
+            s.token_times.append(now)
+            reason = self._stop(s, tok)
+            if reason is not None:
+                s.finish_time = now
+                s.finish_reason = reason
+                keep = s.session_id is not None
+                self.scheduler.finish(s, SequenceStatus.FINISHED_STOPPED if reason == "stop"
+                                      else SequenceStatus.FINISHED_LENGTH, keep_blocks=False)
+                self.finished.append(s)
+                del keep
+            if s.on_token is not None:
+                s.on_token(s, tok, reason is not None)
+            outs.append(StepOutput(s.request_id, s, tok, reason is not None))
+        return outs
+
+    def generate(self, prompts: list, params: Optional[SamplingParams] = None) -> list[list[int]]:
+        """Run ``prompts`` (lists of token ids) to completion; returns output ids in order."""
+        seqs = [self.add_request(f"gen-{next(self._seq_ids)}-{i}", p, params) for i, p in enumerate(prompts)]
+        while self.has_unfinished():
+            self.step()
+        return [s.output_ids for s in seqs]
+
+    # ------------------------------------------------------------- metrics
+    def kv_stats(self) -> dict:
+        a = self.allocator
+        bpb = self.pool.layout.bytes_per_block()
+        return {
+            "blocks_total": a.num_blocks, "blocks_free": a.num_free(),
+            "bytes_capacity": a.num_blocks * bpb, "bytes_used": a.num_used() * bpb,
+            "sequences": len(self.scheduler.running), "evicted_blocks_total": a.evicted_blocks,
+            "preemptions": self.scheduler.num_preemptions,
+        }
+
+    def shutdown(self) -> None:
+        self.runner.release_graphs()

@@ -1,0 +1,71 @@
+"""GPU paged KV pool.
+
+One allocation holds every layer's K and V pages:
+``[layers, 2, num_blocks, kv_heads, block_size, head_dim]`` (bf16).  A page
+(block, kv head) is a contiguous 4 KiB run for head_dim 128, which is what the
+TMA-fed attention kernels load.  The reference keeps f16 pages in host RAM
+(crates/kapsl-llm/src/kv_cache.rs:823-1796) and copies them to the device
+every step; here the pages never leave HBM, and only block ids move.
+
+Also: CPU offload of whole sequences into pinned host memory (reference
+``CpuKvBlockStore``, kv_cache.rs:724-821, 940-1084).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+
+@dataclass
+class KVLayout:
+    num_layers: int
+    num_kv_heads: int
+    head_dim: int
+    block_size: int = 16
+    dtype: torch.dtype = torch.bfloat16
+
+    def bytes_per_block(self) -> int:
+        return self.num_layers * 2 * self.num_kv_heads * self.block_size * self.head_dim * \
+            torch.tensor([], dtype=self.dtype).element_size()
+
+
+class KVPool:
+    def __init__(self, layout: KVLayout, num_blocks: int, device):
+        self.layout = layout
+        self.num_blocks = num_blocks
+        self.device = torch.device(device)
+        L = layout
+        self.storage = torch.zeros(L.num_layers, 2, num_blocks, L.num_kv_heads, L.block_size, L.head_dim,
+                                   dtype=L.dtype, device=self.device)
+        self.k = [self.storage[i, 0] for i in range(L.num_layers)]
+        self.v = [self.storage[i, 1] for i in range(L.num_layers)]
+
+    @staticmethod
+    def blocks_for_bytes(layout: KVLayout, nbytes: int) -> int:
+        return max(1, nbytes // layout.bytes_per_block())
+
+    @property
+    def nbytes(self) -> int:
+        return self.storage.numel() * self.storage.element_size()
+
+    # ------------------------------------------------------------ offload
+    def offload(self, blocks: list[int]) -> torch.Tensor:
+        """Copy pages of ``blocks`` (all layers) into pinned host memory."""
+        idx = torch.as_tensor(blocks, dtype=torch.long, device=self.device)
+        host = torch.empty((self.layout.num_layers, 2, len(blocks)) + tuple(self.storage.shape[3:]),
+                           dtype=self.storage.dtype, pin_memory=True)
+        host.copy_(self.storage.index_select(2, idx), non_blocking=True)
+        return host
+
+    def restore(self, host: torch.Tensor, blocks: list[int]) -> None:
+        """Copy offloaded pages back into (possibly different) ``blocks``."""
+        idx = torch.as_tensor(blocks, dtype=torch.long, device=self.device)
+        self.storage.index_copy_(2, idx, host.to(self.device, non_blocking=True))
+
+    def copy_blocks(self, src: list[int], dst: list[int]) -> None:
+        """Duplicate pages (copy-on-write of a shared prefix block)."""
+        s = torch.as_tensor(src, dtype=torch.long, device=self.device)
+        d = torch.as_tensor(dst, dtype=torch.long, device=self.device)
+        self.storage.index_copy_(2, d, self.storage.index_select(2, s))

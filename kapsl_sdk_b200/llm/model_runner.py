@@ -1,0 +1,311 @@
+"""Builds device inputs for a scheduled batch, runs the model, samples.
+
+Host work per step is a handful of numpy writes into ONE pinned int32 staging
+buffer and ONE pinned int64 buffer, copied to the device with two async
+copies; every kernel input is a fixed view of the device copies.  Decode-only
+steps replay a CUDA graph captured per batch-size bucket (model forward +
+sampler + penalty-count update), so a decode step costs one graph launch.
+
+Reference counterpart: the per-step input preparation, KV gather/pack and
+sampling of crates/kapsl-llm/src/engine.rs:3170-3914 (batched decode) and
+2613-3168 (batched prefill), which run on the host around an ORT session.
+"""
+from __future__ import annotations
+
+import bisect
+import time
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .. import ops
+from .._ext import launch_count
+from ..models.llama import CausalLM, ForwardBatch
+from ..ops import reference as ref
+from .kv_cache import KVPool
+from .scheduler import ScheduledBatch
+from .sequence import Sequence
+
+
+class _Layout:
+    """Offsets of every input region inside the staging buffers."""
+
+    def __init__(self, max_tokens: int, max_seqs: int, max_blocks: int, max_work: int):
+        self.T, self.S, self.MB, self.W = max_tokens, max_seqs, max_blocks, max_work
+        o = 0
+        self.ids = o; o += max_tokens
+        self.pos = o; o += max_tokens
+        self.ctx = o; o += max_seqs
+        self.bt = o; o += max_seqs * max_blocks
+        self.work = o; o += max_work * 2
+        self.sinfo = o; o += max_seqs * 4
+        self.topk = o; o += max_seqs
+        self.sslot = o; o += max_seqs
+        self.temp = o; o += max_seqs
+        self.topp = o; o += max_seqs
+        self.pen = o; o += max_seqs
+        self.adm_slot = o; o += max_seqs
+        self.n32 = o
+        o = 0
+        self.slots = o; o += max_tokens
+        self.lidx = o; o += max_seqs
+        self.adm_rng = o; o += max_seqs
+        self.n64 = o
+
+
+class ModelRunner:
+    def __init__(self, model: CausalLM, pool: KVPool, max_num_seqs: int = 256, max_num_batched_tokens: int = 2048,
+                 max_model_len: int = 4096, use_cuda_graph: bool = True, graph_sizes: Optional[list] = None):
+        self.model = model
+        self.pool = pool
+        self.device = model.device
+        self.bs = pool.layout.block_size
+        self.max_seqs = max_num_seqs
+        self.max_tokens = max_num_batched_tokens + max_num_seqs
+        self.max_blocks = (max_model_len + self.bs - 1) // self.bs
+        self.vocab = model.cfg.vocab_size
+        S = max_num_seqs + 1  # one spare slot for graph padding rows
+        self.pad_slot = max_num_seqs
+        W = (max_num_batched_tokens + 63) // 64 + max_num_seqs
+        self.L = _Layout(self.max_tokens, S, self.max_blocks, W)
+        self.h32 = torch.zeros(self.L.n32, dtype=torch.int32, pin_memory=True)
+        self.h64 = torch.zeros(self.L.n64, dtype=torch.int64, pin_memory=True)
+        self.n32 = self.h32.numpy()
+        self.n64 = self.h64.numpy()
+        self.f32view = self.n32.view(np.float32)
+        self.d32 = torch.zeros(self.L.n32, dtype=torch.int32, device=self.device)
+        self.d64 = torch.zeros(self.L.n64, dtype=torch.int64, device=self.device)
+        # per-sequence device tables
+        self.rng_table = torch.zeros(S, dtype=torch.int64, device=self.device)
+        self.counts = torch.zeros(S, self.vocab, dtype=torch.int32, device=self.device)
+        self.out_tokens = torch.zeros(S, dtype=torch.int32, device=self.device)
+        self.h_out = torch.zeros(S, dtype=torch.int32, pin_memory=True)
+        self.use_graph = use_cuda_graph
+        self.graph_sizes = sorted(graph_sizes or self._default_graph_sizes(max_num_seqs))
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: dict[int, int] = {}
+        self.graph_pool = None
+        self.launches = 0  # kernels launched by steps (eager count + graph replays x graph size)
+        self.stats = {"steps": 0, "graph_steps": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+
+    @staticmethod
+    def _default_graph_sizes(max_seqs: int) -> list[int]:
+        sizes = [1, 2, 4, 8, 16, 24, 32]
+        s = 48
+        while s < max_seqs:
+            sizes.append(s)
+            s += 16 if s < 128 else 32
+        sizes.append(max_seqs)
+        return sorted(set(x for x in sizes if x <= max_seqs))
+
+    # ------------------------------------------------------------ views
+    def _v32(self, off: int, n: int) -> torch.Tensor:
+        return self.d32[off:off + n]
+
+    def _f32(self, off: int, n: int) -> torch.Tensor:
+        return self.d32[off:off + n].view(torch.float32)
+
+    def _bt(self, nrows: int) -> torch.Tensor:
+        return self.d32[self.L.bt:self.L.bt + nrows * self.max_blocks].view(nrows, self.max_blocks)
+
+    def _forward_batch(self, T: int, S: int, R: int, Bd: int, max_ctx: int, nwork: int, nsplit: int) -> ForwardBatch:
+        L = self.L
+        return ForwardBatch(
+            input_ids=self._v32(L.ids, T), positions=self._v32(L.pos, T), slots=self.d64[L.slots:L.slots + T],
+            block_tables=self._bt(max(S, 1)), ctx_lens=self._v32(L.ctx, max(S, 1)),
+            logits_idx=self.d64[L.lidx:L.lidx + R], num_tokens=T, num_decode=Bd, max_decode_ctx=max_ctx,
+            pf_work=self._v32(L.work, nwork * 2).view(nwork, 2) if nwork else None,
+            pf_seq_info=self._v32(L.sinfo, (S - Bd) * 4).view(S - Bd, 4) if S > Bd else None,
+            decode_splits=nsplit)
+
+    def _sample(self, logits: torch.Tensor, R: int) -> None:
+        L = self.L
+        ops.sample(logits, self._f32(L.temp, R), self._v32(L.topk, R), self._f32(L.topp, R), self.rng_table,
+                   self.out_tokens[:R], rep_penalty=self._f32(L.pen, R), counts=self.counts,
+                   slots=self._v32(L.sslot, R))
+        ops.count_tokens(self.counts, self._v32(L.sslot, R), self.out_tokens[:R])
+
+    # ------------------------------------------------------- host inputs
+    def _fill(self, batch: ScheduledBatch, pad_to: int = 0):
+        """Write the batch into the pinned staging buffers; returns shape info."""
+        L, n32, n64, f32 = self.L, self.n32, self.n64, self.f32view
+        MB = self.max_blocks
+        dec = batch.decode
+        Bd = len(dec)
+        t = 0
+        # decode rows
+        for i, s in enumerate(dec):
+            pos = s.length - 1
+            n32[L.ids + i] = s.output_ids[-1] if s.output_ids else s.prompt_ids[-1]
+            n32[L.pos + i] = pos
+            n64[L.slots + i] = s.block_ids[pos // self.bs] * self.bs + pos % self.bs
+            n32[L.ctx + i] = s.length
+            nb = len(s.block_ids)
+            n32[L.bt + i * MB:L.bt + i * MB + nb] = s.block_ids
+        t = Bd
+        Bpad = max(Bd, pad_to)
+        for i in range(Bd, Bpad):  # CUDA-graph padding rows: no KV write, 1-token context on block 0
+            n32[L.ids + i] = 0
+            n32[L.pos + i] = 0
+            n64[L.slots + i] = -1
+            n32[L.ctx + i] = 1
+            n32[L.bt + i * MB] = 0
+        t = Bpad
+        # prefill chunks
+        nwork = 0
+        sample_seqs = list(dec)
+        lrows = list(range(Bd))
+        for j, (s, n) in enumerate(batch.prefill):
+            row = Bpad + j
+            p0 = s.num_computed
+            npr = len(s.prompt_ids)
+            toks = s.prompt_ids[p0:p0 + n] if p0 + n <= npr else (s.prompt_ids + s.output_ids)[p0:p0 + n]
+            n32[L.ids + t:L.ids + t + n] = toks
+            pos = np.arange(p0, p0 + n, dtype=np.int64)
+            n32[L.pos + t:L.pos + t + n] = pos
+            blk = np.asarray(s.block_ids, dtype=np.int64)
+            n64[L.slots + t:L.slots + t + n] = blk[pos // self.bs] * self.bs + pos % self.bs
+            n32[L.ctx + row] = p0 + n
+            nb = len(s.block_ids)
+            n32[L.bt + row * MB:L.bt + row * MB + nb] = s.block_ids
+            si = L.sinfo + j * 4
+            n32[si:si + 4] = (t, n, p0 + n, row)
+            for t0 in range(0, n, 64):
+                n32[L.work + nwork * 2] = j
+                n32[L.work + nwork * 2 + 1] = t0
+                nwork += 1
+            if p0 + n >= s.length:  # chunk completes the prompt: sample from its last token
+                sample_seqs.append(s)
+                lrows.append(t + n - 1)
+            t += n
+        R = len(sample_seqs)
+        Rpad = max(R, pad_to) if pad_to else R
+        for r in range(Rpad):
+            if r < R:
+                s = sample_seqs[r]
+                n64[L.lidx + r] = lrows[r]
+                n32[L.sslot + r] = s.slot
+                f32[L.temp + r] = s.params.temperature
+                n32[L.topk + r] = s.params.top_k
+                f32[L.topp + r] = s.params.top_p
+                f32[L.pen + r] = s.params.repetition_penalty
+            else:
+                n64[L.lidx + r] = r
+                n32[L.sslot + r] = self.pad_slot
+                f32[L.temp + r] = 0.0
+                n32[L.topk + r] = 0
+                f32[L.topp + r] = 1.0
+                f32[L.pen + r] = 1.0
+        S = Bpad + len(batch.prefill)
+        return t, S, R, Rpad, Bd, Bpad, nwork, sample_seqs
+
+    def _h2d(self) -> None:
+        self.d32.copy_(self.h32, non_blocking=True)
+        self.d64.copy_(self.h64, non_blocking=True)
+        self.stats["h2d_bytes"] += self.h32.numel() * 4 + self.h64.numel() * 8
+
+    def admit(self, seqs: list) -> None:
+        """Initialise per-slot device state (LCG seed, penalty counts) for new sequences."""
+        if not seqs:
+            return
+        L = self.L
+        for i, s in enumerate(seqs):
+            self.n32[L.adm_slot + i] = s.slot
+            st = s.rng_state
+            self.n64[L.adm_rng + i] = st - (1 << 64) if st >= (1 << 63) else st
+        n = len(seqs)
+        # (H2D of the staging buffers happens in execute(); admission runs after it on the stream)
+        self._pending_admit = n
+        self._admit_prompts = [(s.slot, s.prompt_ids + s.output_ids) for s in seqs]
+
+    def _apply_admissions(self) -> None:
+        n = getattr(self, "_pending_admit", 0)
+        if not n:
+            return
+        L = self.L
+        slots_d = self._v32(L.adm_slot, n).long()
+        self.rng_table.index_copy_(0, slots_d, self.d64[L.adm_rng:L.adm_rng + n])
+        self.counts.index_fill_(0, slots_d, 0)
+        rows = np.concatenate([np.full(len(p), sl, dtype=np.int32) for sl, p in self._admit_prompts])
+        ids = np.concatenate([np.asarray(p, dtype=np.int32) for _, p in self._admit_prompts])
+        rows_t = torch.from_numpy(rows).pin_memory().to(self.device, non_blocking=True)
+        ids_t = torch.from_numpy(ids).pin_memory().to(self.device, non_blocking=True)
+        self.stats["h2d_bytes"] += rows.nbytes + ids.nbytes
+        ops.count_tokens(self.counts, rows_t, ids_t)
+        self._pending_admit = 0
+        self._admit_prompts = []
+
+    # ------------------------------------------------------------ execute
+    def execute(self, batch: ScheduledBatch) -> tuple[list, np.ndarray]:
+        """Run one step; returns (sequences that sampled, their new tokens)."""
+        decode_only = not batch.prefill and len(batch.decode) > 0
+        pad_to = 0
+        gsize = 0
+        if decode_only and self.use_graph:
+            k = bisect.bisect_left(self.graph_sizes, len(batch.decode))
+            if k < len(self.graph_sizes):
+                gsize = self.graph_sizes[k]
+                pad_to = gsize
+        T, S, R, Rpad, Bd, Bpad, nwork, sample_seqs = self._fill(batch, pad_to)
+        self._h2d()
+        self._apply_admissions()
+        c0 = launch_count()
+        if gsize:
+            g = self.graphs.get(gsize)
+            if g is None:
+                g = self._capture(gsize)
+            g.replay()
+            self.launches += self.graph_launches[gsize]
+            self.stats["graph_steps"] += 1
+        else:
+            max_ctx = int(self.n32[self.L.ctx:self.L.ctx + Bd].max()) if Bd else 0
+            fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, 0)
+            logits = self.model.forward(fb, self.pool.k, self.pool.v)
+            self._sample(logits, R)
+            self.launches += launch_count() - c0
+        self.h_out[:R].copy_(self.out_tokens[:R], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.stats["d2h_bytes"] += R * 4
+        self.stats["steps"] += 1
+        return sample_seqs, self.h_out[:R].numpy().copy()
+
+    def logits(self, batch: ScheduledBatch) -> torch.Tensor:
+        """Eager forward of ``batch`` returning the fp32 logits of its sampling
+        rows (decode rows, then prompt-completing chunks); nothing is sampled."""
+        T, S, R, Rpad, Bd, Bpad, nwork, _ = self._fill(batch, 0)
+        self._h2d()
+        max_ctx = int(self.n32[self.L.ctx:self.L.ctx + Bd].max()) if Bd else 0
+        fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, 0)
+        out = self.model.forward(fb, self.pool.k, self.pool.v)
+        torch.cuda.current_stream(self.device).synchronize()
+        return out
+
+    def _capture(self, B: int) -> torch.cuda.CUDAGraph:
+        """Capture forward+sample for a decode batch of ``B`` rows (inputs are the
+        staging views, already filled for this step)."""
+        max_ctx = self.max_blocks * self.bs
+        nsplit = int(ops.cuda_ops().decode_num_splits(B, self.model.hkv, max_ctx))
+        fb = self._forward_batch(B, B, B, B, max_ctx, 0, nsplit)
+        # warm up once outside capture (allocator, function attributes)
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            logits = self.model.forward(fb, self.pool.k, self.pool.v)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        # the warm-up wrote KV for real rows at their slots (same values as the replay will); fine.
+        g = torch.cuda.CUDAGraph()
+        c0 = launch_count()
+        with torch.cuda.graph(g, pool=self.graph_pool):
+            logits = self.model.forward(fb, self.pool.k, self.pool.v)
+            self._sample(logits, B)
+        self.graph_launches[B] = launch_count() - c0
+        if self.graph_pool is None:
+            self.graph_pool = g.pool()
+        self.graphs[B] = g
+        return g
+
+    def release_graphs(self) -> None:
+        self.graphs.clear()
+        self.graph_pool = None

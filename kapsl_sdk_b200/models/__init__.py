@@ -1,0 +1,1 @@
+"""kapsl_sdk_b200.models"""

@@ -1,0 +1,159 @@
+"""Model architecture descriptions and the presets served by this runtime.
+
+The reference runtime learns geometry from ``config.json`` / ONNX
+``past_key_values.*`` shapes (crates/kapsl-llm/src/engine.rs:1823-1994); here
+the same fields are read from HF ``config.json`` or GGUF metadata
+(:mod:`kapsl_sdk_b200.loaders`) into :class:`ModelConfig`.
+"""
+from __future__ import annotations
+
+import json
+import os
+from dataclasses import asdict, dataclass, field
+from typing import Optional
+
+
+@dataclass
+class ModelConfig:
+    name: str = "custom"
+    arch: str = "llama"  # llama | qwen2 | mixtral
+    vocab_size: int = 32000
+    hidden_size: int = 4096
+    intermediate_size: int = 11008
+    num_layers: int = 32
+    num_heads: int = 32
+    num_kv_heads: int = 32
+    head_dim: int = 128
+    rope_theta: float = 10000.0
+    rms_eps: float = 1e-5
+    qkv_bias: bool = False
+    tie_embeddings: bool = False
+    max_position: int = 32768
+    num_experts: int = 0
+    experts_per_token: int = 0
+    bos_token_id: Optional[int] = 1
+    eos_token_id: Optional[int] = 2
+    extra: dict = field(default_factory=dict)
+
+    @property
+    def q_size(self) -> int:
+        return self.num_heads * self.head_dim
+
+    @property
+    def kv_size(self) -> int:
+        return self.num_kv_heads * self.head_dim
+
+    @property
+    def is_moe(self) -> bool:
+        return self.num_experts > 0
+
+    def kv_bytes_per_token(self, dtype_bytes: int = 2) -> int:
+        """Bytes of K+V for one token over all layers (reference: L*H_kv*D*2*2, engine.rs:2144)."""
+        return self.num_layers * self.num_kv_heads * self.head_dim * 2 * dtype_bytes
+
+    def num_params(self) -> int:
+        d, f, L = self.hidden_size, self.intermediate_size, self.num_layers
+        attn = d * (self.q_size + 2 * self.kv_size) + self.q_size * d
+        mlp = 3 * d * f * (self.num_experts if self.is_moe else 1) + (d * self.num_experts if self.is_moe else 0)
+        emb = self.vocab_size * d * (1 if self.tie_embeddings else 2)
+        return L * (attn + mlp + 2 * d) + emb + d
+
+    def active_params(self) -> int:
+        """Parameters touched per token (MoE: only the routed experts)."""
+        if not self.is_moe:
+            return self.num_params()
+        d, f, L = self.hidden_size, self.intermediate_size, self.num_layers
+        attn = d * (self.q_size + 2 * self.kv_size) + self.q_size * d
+        mlp = 3 * d * f * self.experts_per_token + d * self.num_experts
+        emb = self.vocab_size * d * (1 if self.tie_embeddings else 2)
+        return L * (attn + mlp + 2 * d) + emb + d
+
+    def to_dict(self) -> dict:
+        return asdict(self)
+
+    @classmethod
+    def from_hf_config(cls, path_or_dict) -> "ModelConfig":
+        """Build from a HuggingFace ``config.json`` (path or dict)."""
+        if isinstance(path_or_dict, (str, os.PathLike)):
+            with open(path_or_dict) as f:
+                c = json.load(f)
+        else:
+            c = dict(path_or_dict)
+        mt = c.get("model_type", "llama")
+        arch = {"qwen2": "qwen2", "mixtral": "mixtral"}.get(mt, "llama")
+        heads = c.get("num_attention_heads", 32)
+        hidden = c.get("hidden_size", 4096)
+        eos = c.get("eos_token_id")
+        if isinstance(eos, list):
+            eos = eos[0] if eos else None
+        return cls(
+            name=c.get("_name_or_path", mt),
+            arch=arch,
+            vocab_size=c.get("vocab_size", 32000),
+            hidden_size=hidden,
+            intermediate_size=c.get("intermediate_size", 4 * hidden),
+            num_layers=c.get("num_hidden_layers", 32),
+            num_heads=heads,
+            num_kv_heads=c.get("num_key_value_heads", heads),
+            head_dim=c.get("head_dim", hidden // heads),
+            rope_theta=float(c.get("rope_theta", 10000.0)),
+            rms_eps=float(c.get("rms_norm_eps", 1e-5)),
+            qkv_bias=bool(c.get("attention_bias", arch == "qwen2")),
+            tie_embeddings=bool(c.get("tie_word_embeddings", False)),
+            max_position=int(c.get("max_position_embeddings", 32768)),
+            num_experts=int(c.get("num_local_experts", 0)),
+            experts_per_token=int(c.get("num_experts_per_tok", 0)),
+            bos_token_id=c.get("bos_token_id"),
+            eos_token_id=eos,
+        )
+
+
+def tiny_llama() -> ModelConfig:
+    """4 layers, d 512, 8/8 heads of 64, FFN 1408, vocab 32000 (CPU GGUF workload)."""
+    return ModelConfig(name="tiny-llama", arch="llama", vocab_size=32000, hidden_size=512, intermediate_size=1408,
+                       num_layers=4, num_heads=8, num_kv_heads=8, head_dim=64, rope_theta=10000.0, rms_eps=1e-5,
+                       max_position=4096)
+
+
+def qwen2_5_7b() -> ModelConfig:
+    """Qwen2.5-7B: 28 layers, d 3584, 28q/4kv heads of 128, FFN 18944, vocab 152064, theta 1e6, QKV bias."""
+    return ModelConfig(name="qwen2.5-7b", arch="qwen2", vocab_size=152064, hidden_size=3584, intermediate_size=18944,
+                       num_layers=28, num_heads=28, num_kv_heads=4, head_dim=128, rope_theta=1e6, rms_eps=1e-6,
+                       qkv_bias=True, max_position=32768, bos_token_id=151643, eos_token_id=151645)
+
+
+def llama3_70b() -> ModelConfig:
+    """Llama-3-70B: 80 layers, d 8192, 64q/8kv heads of 128, FFN 28672, vocab 128256, theta 5e5."""
+    return ModelConfig(name="llama-3-70b", arch="llama", vocab_size=128256, hidden_size=8192, intermediate_size=28672,
+                       num_layers=80, num_heads=64, num_kv_heads=8, head_dim=128, rope_theta=5e5, rms_eps=1e-5,
+                       max_position=8192, bos_token_id=128000, eos_token_id=128001)
+
+
+def llama3_8b() -> ModelConfig:
+    """Llama-3-8B: 32 layers, d 4096, 32q/8kv heads of 128, FFN 14336, vocab 128256, theta 5e5."""
+    return ModelConfig(name="llama-3-8b", arch="llama", vocab_size=128256, hidden_size=4096, intermediate_size=14336,
+                       num_layers=32, num_heads=32, num_kv_heads=8, head_dim=128, rope_theta=5e5, rms_eps=1e-5,
+                       max_position=16384, bos_token_id=128000, eos_token_id=128001)
+
+
+def mixtral_8x7b() -> ModelConfig:
+    """Mixtral-8x7B: 32 layers, d 4096, 32q/8kv heads, 8 experts top-2, expert FFN 14336, vocab 32000."""
+    return ModelConfig(name="mixtral-8x7b", arch="mixtral", vocab_size=32000, hidden_size=4096,
+                       intermediate_size=14336, num_layers=32, num_heads=32, num_kv_heads=8, head_dim=128,
+                       rope_theta=1e6, rms_eps=1e-5, max_position=32768, num_experts=8, experts_per_token=2)
+
+
+PRESETS = {
+    "tiny-llama": tiny_llama,
+    "qwen2.5-7b": qwen2_5_7b,
+    "llama-3-70b": llama3_70b,
+    "llama-3-8b": llama3_8b,
+    "mixtral-8x7b": mixtral_8x7b,
+}
+
+
+def get_preset(name: str, **overrides) -> ModelConfig:
+    cfg = PRESETS[name]()
+    for k, v in overrides.items():
+        setattr(cfg, k, v)
+    return cfg

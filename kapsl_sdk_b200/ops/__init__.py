@@ -1,0 +1,187 @@
+"""Functional wrappers over the sm_100a kernels.
+
+Every function here launches kernels from ``kapsl_sdk_b200._cuda`` on the
+current CUDA stream.  Plain fp32 PyTorch restatements of the same math live in
+:mod:`kapsl_sdk_b200.ops.reference`; the CPU backend and the numerics tests use
+them as the oracle.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from .._ext import cuda_ops
+
+EPI_PLAIN, EPI_BIAS, EPI_RESIDUAL, EPI_SWIGLU = 0, 1, 2, 3
+
+_err_bufs: dict[int, torch.Tensor] = {}
+
+
+def error_buffer(device: torch.device) -> torch.Tensor:
+    """Per-device int32[16] status words written by kernels whose bounded
+    waits time out (0 = ok).  Read with :func:`check_errors`."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _err_bufs.get(idx)
+    if buf is None:
+        buf = torch.zeros(16, dtype=torch.int32, device=device)
+        _err_bufs[idx] = buf
+    return buf
+
+
+def check_errors(device: torch.device) -> int:
+    """Return (and clear) the first non-zero kernel status word on ``device``."""
+    buf = error_buffer(device)
+    v = int(buf.max().item())
+    if v:
+        buf.zero_()
+    return v
+
+
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optional[torch.Tensor] = None,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """``out = rmsnorm(x [+ residual]) * weight``; with ``residual`` the sum is
+    also stored back into ``residual`` (pre-norm residual stream update)."""
+    if out is None:
+        out = torch.empty_like(x)
+    cuda_ops().rmsnorm(out, x, weight, float(eps), residual)
+    return out
+
+
+def rope_kv_write(qkv: torch.Tensor, positions: torch.Tensor, slots: Optional[torch.Tensor], cos_sin: torch.Tensor,
+                  k_cache: torch.Tensor, v_cache: torch.Tensor, num_heads: int, num_kv_heads: int,
+                  head_dim: int) -> None:
+    """Rotate q and k of ``qkv`` in place and write k, v into the paged cache."""
+    cuda_ops().rope_kv_write(qkv, positions, slots, cos_sin, k_cache, v_cache, num_heads, num_kv_heads, head_dim)
+
+
+def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    F = x.shape[1] // 2
+    if out is None:
+        out = torch.empty(x.shape[0], F, dtype=x.dtype, device=x.device)
+    cuda_ops().silu_mul(out, x)
+    return out
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    cuda_ops().embedding(out, table, ids, int(vocab_start))
+    return out
+
+
+def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] = None,
+           residual: Optional[torch.Tensor] = None, swiglu: bool = False, out: Optional[torch.Tensor] = None,
+           out_dtype: torch.dtype = torch.bfloat16, workspace: Optional[torch.Tensor] = None,
+           force_bn: int = 0, force_splits: int = 0) -> torch.Tensor:
+    """``out = epilogue(x @ weight.T)`` on the tcgen05 GEMM.
+
+    Exactly one of ``bias`` / ``residual`` / ``swiglu`` selects the fused
+    epilogue.  ``residual`` may be the same tensor as ``out`` (in-place
+    residual-stream update).  ``swiglu`` expects the gate/up weight interleaved
+    in 128-row blocks (see :func:`interleave_gate_up`) and returns [M, N/2].
+    """
+    M, N = x.shape[0], weight.shape[0]
+    epi = EPI_PLAIN
+    if bias is not None:
+        epi = EPI_BIAS
+    elif residual is not None:
+        epi = EPI_RESIDUAL
+    elif swiglu:
+        epi = EPI_SWIGLU
+    ncols = N // 2 if swiglu else N
+    if out is None:
+        out = torch.empty(M, ncols, dtype=out_dtype, device=x.device)
+    if workspace is None:
+        workspace = _workspace(x.device)
+    cuda_ops().gemm(x, weight, out, epi, bias, residual, workspace, error_buffer(x.device), force_bn, force_splits)
+    return out
+
+
+_ws: dict[int, torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, nbytes: int = 64 << 20) -> torch.Tensor:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    w = _ws.get(idx)
+    if w is None or w.numel() * 4 < nbytes:
+        w = torch.empty(nbytes // 4, dtype=torch.float32, device=device)
+        _ws[idx] = w
+    return w
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 128) -> torch.Tensor:
+    """[F, d] gate and up -> [2F, d] with alternating 128-row blocks
+    (gate_0, up_0, gate_1, up_1, ...), the layout the SwiGLU epilogue reads."""
+    F, d = gate.shape
+    assert F % block == 0, "intermediate size must be a multiple of 128"
+    g = gate.view(F // block, block, d)
+    u = up.view(F // block, block, d)
+    return torch.stack([g, u], dim=1).reshape(2 * F, d).contiguous()
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, block_tables: torch.Tensor,
+                     ctx_lens: torch.Tensor, num_heads: int, num_kv_heads: int, scale: Optional[float] = None,
+                     out: Optional[torch.Tensor] = None, num_splits: int = 0,
+                     scratch: Optional[tuple[torch.Tensor, torch.Tensor]] = None,
+                     max_ctx: Optional[int] = None) -> torch.Tensor:
+    """Paged decode attention (one query token per row of ``q``)."""
+    B = q.shape[0]
+    D = 128
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    if out is None:
+        out = torch.empty(B, num_heads * D, dtype=q.dtype, device=q.device)
+    ops = cuda_ops()
+    if num_splits <= 0:
+        mc = int(max_ctx) if max_ctx is not None else int(block_tables.shape[1]) * 16
+        num_splits = int(ops.decode_num_splits(B, num_kv_heads, mc))
+    po = pl = None
+    if num_splits > 1:
+        if scratch is None:
+            po = torch.empty(B * num_heads * num_splits * D, dtype=torch.float32, device=q.device)
+            pl = torch.empty(B * num_heads * num_splits, dtype=torch.float32, device=q.device)
+        else:
+            po, pl = scratch
+    ops.decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, num_heads, num_kv_heads, float(scale),
+                         num_splits, po, pl, error_buffer(q.device))
+    return out
+
+
+def prefill_work(q_lens: list[int], tile: int = 64) -> list[tuple[int, int]]:
+    """Work list of (sequence, first query row) tiles for :func:`prefill_attention`."""
+    work = []
+    for s, n in enumerate(q_lens):
+        for t0 in range(0, n, tile):
+            work.append((s, t0))
+    return work
+
+
+def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, work: torch.Tensor,
+                      seq_info: torch.Tensor, block_tables: torch.Tensor, num_heads: int, num_kv_heads: int,
+                      out: torch.Tensor, scale: Optional[float] = None) -> torch.Tensor:
+    """Chunked-prefill attention.  ``seq_info[s] = (q_start, q_len, ctx_len, bt_row)``;
+    the chunk's tokens sit at positions ``ctx_len - q_len .. ctx_len - 1``."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(128)
+    cuda_ops().prefill_attention(q, k_cache, v_cache, work, seq_info, block_tables, out, num_heads, num_kv_heads,
+                                 float(scale), error_buffer(q.device))
+    return out
+
+
+def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
+           rng_state: torch.Tensor, out: torch.Tensor, rep_penalty: Optional[torch.Tensor] = None,
+           counts: Optional[torch.Tensor] = None, slots: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Sample one token per row of fp32 ``logits`` (modified in place).
+
+    ``rng_state`` (int64 LCG states) and ``counts`` (per-id occurrence counts
+    for the repetition penalty) are per-sequence tables indexed by
+    ``slots[row]`` (or by the row itself when ``slots`` is None)."""
+    cuda_ops().sample(logits, temperature, top_k, top_p, rep_penalty, counts, slots, rng_state, out)
+    return out
+
+
+def count_tokens(counts: torch.Tensor, rows: torch.Tensor, ids: torch.Tensor) -> None:
+    cuda_ops().count_tokens(counts, rows, ids)
