@@ -177,7 +177,12 @@ def main():
     engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0)
     # data-parallel replicas serve their own copy of the workload (weak scaling);
     # tensor parallel shares one workload across the ranks (strong scaling).
-    prompts = make_workload(args, cfg.vocab_size, seed=1 + (rank if tp_comm is None else 0))
+    # A fresh prompt set for every pass (warm-up, timed, end-to-end), so no pass
+    # can reuse KV blocks that an earlier pass left in the prefix cache.
+    rank_seed = 1000 * (rank if tp_comm is None else 0)
+
+    def prompts_for(pass_idx: int):
+        return make_workload(args, cfg.vocab_size, seed=1 + rank_seed + pass_idx)
     params = SamplingParams(max_new_tokens=args.output_len, temperature=0.7, top_k=40, top_p=0.9,
                             repetition_penalty=1.15, ignore_eos=True)
 
@@ -193,9 +198,11 @@ def main():
         return seqs
 
     serve.n = 0
-    nwarm = max(1, int(len(prompts) * args.warmup_scale))
+    nwarm = max(1, int(args.num_requests * args.warmup_scale))
+    npass = 0
     for _ in range(args.warmup):
-        serve(prompts[:nwarm])
+        serve(prompts_for(npass)[:nwarm])
+        npass += 1
     torch.cuda.synchronize()
     barrier()
 
@@ -207,9 +214,10 @@ def main():
     with ClockSampler(local) as clocks:
         barrier()
         torch.cuda.synchronize()
+        timed_prompts = [prompts_for(npass + i) for i in range(args.steps)]
         start.record()
-        for _ in range(args.steps):
-            all_seqs.extend(serve(prompts))
+        for i in range(args.steps):
+            all_seqs.extend(serve(timed_prompts[i]))
         end.record()
         torch.cuda.synchronize()
         barrier()
@@ -223,8 +231,9 @@ def main():
 
     # ---------------- end to end through the public API (host clock)
     barrier()
+    e2e_prompts = prompts_for(npass + args.steps)
     t0 = time.perf_counter()
-    outs = engine.generate(prompts, params)
+    outs = engine.generate(e2e_prompts, params)
     torch.cuda.synchronize()
     e2e_s = time.perf_counter() - t0
     e2e_tokens = sum(len(o) for o in outs)

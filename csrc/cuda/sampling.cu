@@ -45,7 +45,8 @@ __global__ void __launch_bounds__(kSampThreads)
 
   __shared__ float s_val[kMaxTopK];
   __shared__ int s_idx[kMaxTopK];
-  __shared__ uint32_t s_hist[2048];
+  __shared__ uint32_t s_hist[32 * 256];  // one 256-bin histogram per warp
+  __shared__ uint32_t s_tot[256];
   __shared__ float s_redv[32];
   __shared__ int s_redi[32];
   __shared__ int s_misc[4];
@@ -88,43 +89,64 @@ __global__ void __launch_bounds__(kSampThreads)
     return;
   }
 
-  // Pass 0: penalty + temperature, written back in place (the row is scratch).
-  for (int v = tid; v < V; v += kSampThreads) {
-    float l = lg[v];
-    if (use_pen) l = apply_penalty(l, cnt[v], pen);
-    lg[v] = l / T;
+  // Pass 0: the repetition penalty touches only ids that occurred; they are
+  // rewritten in place (the row is scratch).  Temperature scaling preserves
+  // the order, so it is applied to the surviving candidates only.
+  if (use_pen) {
+    for (int v = tid; v < V; v += kSampThreads) {
+      const int c = cnt[v];
+      if (c > 0) lg[v] = apply_penalty(lg[v], c, pen);
+    }
   }
   int k = top_k[row];
   if (k <= 0 || k > V) k = V;
   if (k > kMaxTopK) k = kMaxTopK;  // candidates beyond 1024 are not kept
   __syncthreads();
 
-  // Radix select of the k-th largest key.
+  // Radix select of the k-th largest key: four 8-bit digits, one private
+  // histogram per warp, lanes with equal digits combined before the atomic.
   uint32_t prefix = 0, mask = 0;
   int remaining = k;
-  const int shifts[3] = {21, 10, 0};
-  const int widths[3] = {11, 11, 10};
-  for (int pass = 0; pass < 3; ++pass) {
-    const int nb = 1 << widths[pass];
-    for (int i = tid; i < nb; i += kSampThreads) s_hist[i] = 0;
+  const int warp = tid >> 5, lane = tid & 31;
+  uint32_t* whist = s_hist + warp * 256;
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 32 * 256; i += kSampThreads) s_hist[i] = 0;
     __syncthreads();
-    for (int v = tid; v < V; v += kSampThreads) {
-      const uint32_t key = float_key(lg[v]);
-      if ((key & mask) == prefix) atomicAdd(&s_hist[(key >> shifts[pass]) & (nb - 1)], 1u);
+    for (int base = 0; base < V; base += kSampThreads) {
+      const int v = base + tid;
+      bool hit = false;
+      uint32_t digit = 0;
+      if (v < V) {
+        const uint32_t key = float_key(lg[v]);
+        hit = (key & mask) == prefix;
+        digit = (key >> shift) & 0xFFu;
+      }
+      const unsigned hits = __ballot_sync(0xffffffffu, hit);
+      if (hit) {
+        const unsigned same = __match_any_sync(hits, digit);
+        if (lane == __ffs(same) - 1) atomicAdd(&whist[digit], (uint32_t)__popc(same));
+      }
+    }
+    __syncthreads();
+    if (tid < 256) {  // fold the per-warp histograms into warp 0's
+      uint32_t t = 0;
+      for (int w = 0; w < 32; ++w) t += s_hist[w * 256 + tid];
+      s_tot[tid] = t;
     }
     __syncthreads();
     if (tid == 0) {
-      int above = 0, d = nb - 1;
+      int above = 0, d = 255;
       for (; d > 0; --d) {
-        if (above + (int)s_hist[d] >= remaining) break;
-        above += s_hist[d];
+        if (above + (int)s_tot[d] >= remaining) break;
+        above += s_tot[d];
       }
       s_misc[0] = d;
       s_misc[1] = remaining - above;
     }
     __syncthreads();
-    prefix |= ((uint32_t)s_misc[0]) << shifts[pass];
-    mask |= ((uint32_t)(nb - 1)) << shifts[pass];
+    prefix |= ((uint32_t)s_misc[0]) << shift;
+    mask |= 0xFFu << shift;
     remaining = s_misc[1];
     __syncthreads();
   }
@@ -136,8 +158,9 @@ __global__ void __launch_bounds__(kSampThreads)
   __syncthreads();
   const int n_above = k - remaining;
   for (int v = tid; v < V; v += kSampThreads) {
-    const float l = lg[v];
-    const uint32_t key = float_key(l);
+    const float raw = lg[v];
+    const uint32_t key = float_key(raw);
+    const float l = raw / T;
     if (key > thr) {
       int p = atomicAdd(&s_misc[2], 1);
       if (p < kMaxTopK) {

@@ -66,18 +66,23 @@ class RadixPrefixIndex:
                 self.by_block[blocks[i]] = child
             node = child
 
-    def remove_block(self, block: int) -> None:
-        """Drop the node of ``block`` and its whole subtree (descendants are unreachable)."""
+    def remove_block(self, block: int) -> list[int]:
+        """Drop the node of ``block`` and its whole subtree; returns the blocks of
+        the removed descendants (they are unreachable from now on)."""
         node = self.by_block.get(block)
         if node is None:
-            return
+            return []
         stack = [node]
+        gone = []
         while stack:
             n = stack.pop()
             self.by_block.pop(n.block, None)
+            if n.block != block:
+                gone.append(n.block)
             stack.extend(n.children.values())
         if node.parent is not None:
             node.parent.children.pop(node.key, None)
+        return gone
 
     def __contains__(self, block: int) -> bool:
         return block in self.by_block
@@ -124,7 +129,10 @@ class BlockAllocator:
                 else:
                     b = min(self.cached_free)
                     del self.cached_free[b]
-                self.index.remove_block(b)
+                for d in self.index.remove_block(b):
+                    if d in self.cached_free:  # unreachable cached descendants become plain free
+                        del self.cached_free[d]
+                        self.free_list.append(d)
                 self.evicted_blocks += 1
             self.ref[b] = 1
             out.append(b)

@@ -10,6 +10,7 @@ stop handling (EOS, stop ids incl. BOS, max_new_tokens, max length).
 from __future__ import annotations
 
 import itertools
+import os
 import time
 from dataclasses import dataclass, field
 from typing import Callable, Optional
@@ -87,6 +88,10 @@ class LLMEngine:
         hard = e.kv_hard_limit_bytes or self.pool.nbytes
         self.kv_hard = hard
         self.kv_soft = e.kv_soft_limit_bytes or int(hard * 0.9)
+        self.profile = None
+        if os.environ.get("KAPSL_LLM_PROFILE", os.environ.get("KAPSL_LLM_PROFILE_DECODE", "0")) == "1":
+            self.profile = {"steps": 0, "decode_steps": 0, "tokens": 0, "schedule_s": 0.0, "prepare_s": 0.0,
+                            "gpu_wait_s": 0.0, "postprocess_s": 0.0}
 
     # ------------------------------------------------------------ requests
     def _reserved_bytes(self) -> int:
@@ -154,13 +159,25 @@ class LLMEngine:
         return None
 
     def step(self) -> list[StepOutput]:
+        prof = self.profile is not None
+        t0 = time.perf_counter() if prof else 0.0
         batch = self.scheduler.schedule()
         if batch.empty:
             return []
         if batch.admitted:
             self.runner.admit(batch.admitted)
+        t1 = time.perf_counter() if prof else 0.0
         seqs, toks = self.runner.execute(batch)
         now = time.perf_counter()
+        if prof:
+            p = self.profile
+            p["steps"] += 1
+            p["schedule_s"] += t1 - t0
+            p["prepare_s"] += self.runner.last_prepare_s
+            p["gpu_wait_s"] += now - t1 - self.runner.last_prepare_s
+            p["tokens"] += batch.num_tokens
+            if not batch.prefill:
+                p["decode_steps"] += 1
         for s in batch.decode:
             s.num_computed += 1
         for s, n in batch.prefill:
@@ -183,7 +200,14 @@ class LLMEngine:
             if s.on_token is not None:
                 s.on_token(s, tok, reason is not None)
             outs.append(StepOutput(s.request_id, s, tok, reason is not None))
+        if prof:
+            self.profile["postprocess_s"] += time.perf_counter() - now
         return outs
+
+    def profile_summary(self) -> dict:
+        """Per-phase host timings when ``KAPSL_LLM_PROFILE=1`` (reference:
+        KAPSL_LLM_PROFILE_DECODE, crates/kapsl-llm/src/engine.rs:102-115)."""
+        return dict(self.profile or {})
 
     def generate(self, prompts: list, params: Optional[SamplingParams] = None) -> list[list[int]]:
         """Run ``prompts`` (lists of token ids) to completion; returns output ids in order."""

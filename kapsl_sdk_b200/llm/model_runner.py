@@ -87,6 +87,7 @@ class ModelRunner:
         self.graph_launches: dict[int, int] = {}
         self.graph_pool = None
         self.launches = 0  # kernels launched by steps (eager count + graph replays x graph size)
+        self.last_prepare_s = 0.0
         self.stats = {"steps": 0, "graph_steps": 0, "h2d_bytes": 0, "d2h_bytes": 0}
 
     @staticmethod
@@ -242,25 +243,32 @@ class ModelRunner:
         decode_only = not batch.prefill and len(batch.decode) > 0
         pad_to = 0
         gsize = 0
-        if decode_only and self.use_graph:
+        bucket = 0
+        if decode_only:
             k = bisect.bisect_left(self.graph_sizes, len(batch.decode))
             if k < len(self.graph_sizes):
-                gsize = self.graph_sizes[k]
-                pad_to = gsize
+                bucket = self.graph_sizes[k]
+                if self.use_graph:
+                    gsize = pad_to = bucket
+        tp0 = time.perf_counter()
+        c0 = launch_count()
         T, S, R, Rpad, Bd, Bpad, nwork, sample_seqs = self._fill(batch, pad_to)
         self._h2d()
         self._apply_admissions()
-        c0 = launch_count()
+        self.last_prepare_s = time.perf_counter() - tp0
         if gsize:
             g = self.graphs.get(gsize)
             if g is None:
                 g = self._capture(gsize)
             g.replay()
-            self.launches += self.graph_launches[gsize]
+            self.launches += launch_count() - c0 + self.graph_launches[gsize]
             self.stats["graph_steps"] += 1
         else:
             max_ctx = int(self.n32[self.L.ctx:self.L.ctx + Bd].max()) if Bd else 0
-            fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, 0)
+            nsplit = 0
+            if bucket:  # same split-KV policy as the captured graphs, so both paths agree bitwise
+                nsplit = self._graph_splits(bucket)
+            fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, nsplit)
             logits = self.model.forward(fb, self.pool.k, self.pool.v)
             self._sample(logits, R)
             self.launches += launch_count() - c0
@@ -281,11 +289,14 @@ class ModelRunner:
         torch.cuda.current_stream(self.device).synchronize()
         return out
 
+    def _graph_splits(self, B: int) -> int:
+        return int(ops.cuda_ops().decode_num_splits(B, self.model.hkv, self.max_blocks * self.bs))
+
     def _capture(self, B: int) -> torch.cuda.CUDAGraph:
         """Capture forward+sample for a decode batch of ``B`` rows (inputs are the
         staging views, already filled for this step)."""
         max_ctx = self.max_blocks * self.bs
-        nsplit = int(ops.cuda_ops().decode_num_splits(B, self.model.hkv, max_ctx))
+        nsplit = self._graph_splits(B)
         fb = self._forward_batch(B, B, B, B, max_ctx, 0, nsplit)
         # warm up once outside capture (allocator, function attributes)
         s = torch.cuda.Stream(self.device)

@@ -47,9 +47,12 @@ def test_chunked_prefill_logits_match_dense():
             s.num_computed += 1
         for s, n in batch.prefill:
             s.num_computed += n
-        for r, s in enumerate(list(batch.decode) + done):
-            got[s.request_id] = lg[r].cpu()
+        nd = len(batch.decode)
+        for r, s in enumerate(batch.decode):
             s.output_ids.append(int(lg[r].argmax()))
+        for r, s in enumerate(done):  # rows after the decode rows: prompt-completing chunks
+            got[s.request_id] = lg[nd + r].cpu()
+            s.output_ids.append(int(lg[nd + r].argmax()))
     full = list(random_full_weights(cfg, torch.device("cuda", 0), seed=0, std=0.05))
     emb = full[0][1].cpu()
     head = full[1][1].cpu()
@@ -70,11 +73,13 @@ def test_generate_graph_matches_eager():
     outs = []
     for graphs in (True, False):
         eng = make_engine(cfg, use_cuda_graph=graphs)
-        outs.append(eng.generate(prompts, SamplingParams(max_new_tokens=24, seed=7, ignore_eos=True)))
+        outs.append(eng.generate(prompts, SamplingParams.greedy(24, ignore_eos=True)))
         assert all(len(o) == 24 for o in outs[-1])
         if graphs:
             assert eng.runner.stats["graph_steps"] > 0
         eng.shutdown()
+    # eager decode uses the graphs' batch bucket and split-KV count, and every
+    # kernel is row-independent, so padding must not change a single token
     assert outs[0] == outs[1]
 
 
