@@ -1,0 +1,237 @@
+// Python bindings of the C++ runtime (module kapsl_sdk_b200._native):
+// bincode wire codec, paged-KV block allocator, shared-memory transport and
+// the socket / SHM servers.
+#include <pybind11/pybind11.h>
+#include <pybind11/stl.h>
+
+#include "block_alloc.h"
+#include "server.h"
+#include "shm.h"
+#include "wire.h"
+
+namespace py = pybind11;
+using namespace kapsl;
+
+namespace {
+
+template <class T>
+std::optional<T> opt_get(const py::dict& d, const char* k) {
+  if (!d.contains(k)) return std::nullopt;
+  py::object v = d[k];
+  if (v.is_none()) return std::nullopt;
+  return v.cast<T>();
+}
+
+wire::Metadata metadata_from_py(const py::dict& d) {
+  wire::Metadata m;
+  m.request_id = opt_get<std::string>(d, "request_id");
+  m.timeout_ms = opt_get<uint64_t>(d, "timeout_ms");
+  if (auto p = opt_get<int>(d, "priority")) m.priority = (uint8_t)*p;
+  m.force_cpu = opt_get<bool>(d, "force_cpu");
+  m.model_version = opt_get<std::string>(d, "model_version");
+  m.auth_token = opt_get<std::string>(d, "auth_token");
+  m.max_new_tokens = opt_get<uint32_t>(d, "max_new_tokens");
+  m.temperature = opt_get<float>(d, "temperature");
+  m.top_p = opt_get<float>(d, "top_p");
+  m.top_k = opt_get<uint32_t>(d, "top_k");
+  m.repetition_penalty = opt_get<float>(d, "repetition_penalty");
+  m.seed = opt_get<uint64_t>(d, "seed");
+  m.stop_token_ids = opt_get<std::vector<uint32_t>>(d, "stop_token_ids");
+  return m;
+}
+
+wire::Request request_from_py(const py::dict& d) {
+  wire::Request r;
+  r.input = packet_from_py(d["input"]);
+  if (d.contains("additional_inputs") && !d["additional_inputs"].is_none())
+    for (auto item : d["additional_inputs"]) {
+      py::tuple t = item.cast<py::tuple>();
+      r.additional_inputs.push_back({t[0].cast<std::string>(), packet_from_py(t[1])});
+    }
+  r.session_id = opt_get<std::string>(d, "session_id");
+  if (d.contains("metadata") && !d["metadata"].is_none()) r.metadata = metadata_from_py(d["metadata"].cast<py::dict>());
+  return r;
+}
+
+py::dict hybrid_req_to_py(const wire::HybridRequest& h) {
+  py::dict d;
+  d["request_id"] = h.meta.request_id;
+  d["model_id"] = h.meta.model_id;
+  d["priority"] = h.meta.priority;
+  d["force_cpu"] = (bool)h.meta.force_cpu;
+  d["timestamp_ns"] = h.meta.timestamp_ns;
+  d["shm_offset"] = h.shm_offset;
+  d["shm_size"] = h.shm_size;
+  return d;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_native, m) {
+  m.doc() = "kapsl_sdk_b200 C++ runtime: wire codec, block allocator, SHM transport, servers";
+
+  static py::object out_of_blocks;  // Python class kapsl_sdk_b200.llm.block_manager.OutOfBlocks
+  py::register_exception_translator([](std::exception_ptr p) {
+    try {
+      if (p) std::rethrow_exception(p);
+    } catch (const OutOfBlocksError& e) {
+      if (!out_of_blocks) out_of_blocks = py::module_::import("kapsl_sdk_b200.llm.block_manager").attr("OutOfBlocks");
+      PyErr_SetString(out_of_blocks.ptr(), e.what());
+    } catch (const wire::DecodeError& e) {
+      PyErr_SetString(PyExc_ValueError, e.what());
+    }
+  });
+
+  // ---- wire
+  m.attr("OP_INFER") = wire::OP_INFER;
+  m.attr("OP_INFER_STREAM") = wire::OP_INFER_STREAM;
+  m.attr("OP_METRICS") = wire::OP_METRICS;
+  m.attr("OP_HYBRID_INFER") = wire::OP_HYBRID_INFER;
+  m.attr("STATUS_OK") = wire::STATUS_OK;
+  m.attr("STATUS_ERR") = wire::STATUS_ERR;
+  m.attr("STATUS_STREAM_CHUNK") = wire::STATUS_STREAM_CHUNK;
+  m.attr("STATUS_STREAM_END") = wire::STATUS_STREAM_END;
+  m.def("encode_packet", [](py::object shape, std::string dtype, py::bytes data) {
+    return py::bytes(wire::encode_packet(packet_from_py(py::make_tuple(shape, dtype, data))));
+  });
+  m.def("decode_packet", [](py::bytes b) { return packet_to_py(wire::decode_packet(std::string(b))); });
+  m.def("encode_request", [](py::dict d) { return py::bytes(wire::encode_request(request_from_py(d))); });
+  m.def("decode_request", [](py::bytes b) { return request_to_py(wire::decode_request(std::string(b))); });
+  m.def("encode_hybrid_request", [](py::dict d) {
+    wire::HybridRequest h;
+    h.meta.request_id = d["request_id"].cast<uint64_t>();
+    h.meta.model_id = d["model_id"].cast<uint32_t>();
+    h.meta.priority = opt_get<int>(d, "priority").value_or(0);
+    h.meta.force_cpu = opt_get<bool>(d, "force_cpu").value_or(false) ? 1 : 0;
+    h.meta.timestamp_ns = opt_get<uint64_t>(d, "timestamp_ns").value_or(0);
+    h.shm_offset = d["shm_offset"].cast<uint64_t>();
+    h.shm_size = d["shm_size"].cast<uint64_t>();
+    return py::bytes(wire::encode_hybrid_request(h));
+  });
+  m.def("decode_hybrid_request", [](py::bytes b) { return hybrid_req_to_py(wire::decode_hybrid_request(b)); });
+  m.def("decode_hybrid_response", [](py::bytes b) {
+    auto h = wire::decode_hybrid_response(b);
+    py::dict d;
+    d["request_id"] = h.meta.request_id;
+    d["status"] = h.meta.status;
+    d["latency_ns"] = h.meta.latency_ns;
+    d["shm_offset"] = h.shm_offset;
+    d["shm_size"] = h.shm_size;
+    return d;
+  });
+  m.def("request_header", [](uint32_t model, uint32_t op, uint32_t size) {
+    return py::bytes(wire::request_header(model, op, size));
+  });
+  m.def("response_header", [](uint32_t st, uint32_t size) { return py::bytes(wire::response_header(st, size)); });
+  m.def("validate_packet", [](py::object shape, std::string dtype, py::bytes data) {
+    return wire::validate_packet(packet_from_py(py::make_tuple(shape, dtype, data)));
+  });
+
+  // ---- block allocator
+  py::class_<BlockAllocator>(m, "BlockAllocator")
+      .def(py::init<int64_t, int, bool, std::string>(), py::arg("num_blocks"), py::arg("block_size") = 16,
+           py::arg("enable_prefix_cache") = true, py::arg("eviction") = "lru")
+      .def_property_readonly("num_blocks", &BlockAllocator::num_blocks)
+      .def_property_readonly("block_size", &BlockAllocator::block_size)
+      .def_property_readonly("evicted_blocks", &BlockAllocator::evicted_blocks)
+      .def("num_free", &BlockAllocator::num_free)
+      .def("num_used", &BlockAllocator::num_used)
+      .def("usage", &BlockAllocator::usage)
+      .def("refcount", &BlockAllocator::refcount)
+      .def("allocate", &BlockAllocator::allocate)
+      .def("incref", &BlockAllocator::incref)
+      .def("free", &BlockAllocator::free)
+      .def("match_prefix", &BlockAllocator::match_prefix)
+      .def("commit_prefix", &BlockAllocator::commit_prefix)
+      .def("is_cached", &BlockAllocator::is_cached);
+
+  // ---- shared memory
+  py::class_<shm::Region>(m, "ShmRegion")
+      .def_static("create", &shm::Region::create)
+      .def_static("open", &shm::Region::open)
+      .def_property_readonly("size", &shm::Region::size)
+      .def_property_readonly("name", &shm::Region::name)
+      .def("header", [](const shm::Region& r) {
+        const auto& h = r.header();
+        py::dict d;
+        d["magic"] = h.magic;
+        d["version"] = h.version;
+        d["request_queue_offset"] = h.request_queue_offset;
+        d["response_queue_offset"] = h.response_queue_offset;
+        d["tensor_pool_offset"] = h.tensor_pool_offset;
+        d["max_tensor_size"] = h.max_tensor_size;
+        d["notify_read_fd"] = h.notify_read_fd;
+        d["notify_write_fd"] = h.notify_write_fd;
+        return d;
+      })
+      .def("write_tensor", [](shm::Region& r, uint64_t off, py::object shape, std::string dtype, py::bytes data) {
+        shm::write_tensor(r, off, packet_from_py(py::make_tuple(shape, dtype, data)));
+      })
+      .def("read_tensor", [](const shm::Region& r, uint64_t off) { return packet_to_py(shm::read_tensor(r, off)); })
+      .def("read_bytes", [](const shm::Region& r, uint64_t off, uint64_t n) {
+        if (!r.in_bounds(off, n)) throw std::out_of_range("outside the region");
+        return py::bytes(reinterpret_cast<const char*>(r.base() + off), n);
+      })
+      .def("init_rings", [](shm::Region& r) {
+        shm::Ring<shm::ShmRequest>(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, true);
+        shm::Ring<shm::ShmResponse>(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, true);
+      })
+      .def("push_request", [](shm::Region& r, uint64_t request_id, uint32_t model_id, int priority, uint64_t off,
+                              uint64_t size) {
+        shm::ShmRequest q{};
+        q.meta.request_id = request_id;
+        q.meta.model_id = model_id;
+        q.meta.priority = (uint8_t)priority;
+        q.tensor_offset = off;
+        q.tensor_size = size;
+        return shm::Ring<shm::ShmRequest>(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, false).push(q);
+      })
+      .def("pop_request", [](shm::Region& r) -> py::object {
+        auto q = shm::Ring<shm::ShmRequest>(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, false).pop();
+        if (!q) return py::none();
+        return py::make_tuple(q->meta.request_id, q->meta.model_id, q->meta.priority, q->tensor_offset, q->tensor_size);
+      })
+      .def("pop_response", [](shm::Region& r) -> py::object {
+        auto q = shm::Ring<shm::ShmResponse>(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, false).pop();
+        if (!q) return py::none();
+        return py::make_tuple(q->meta.request_id, q->meta.status, q->result_offset, q->result_size, q->error_offset);
+      })
+      .def("ring_len", [](shm::Region& r, bool responses) {
+        return responses ? shm::Ring<shm::ShmResponse>(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, false).len()
+                         : shm::Ring<shm::ShmRequest>(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, false).len();
+      })
+      .def("read_error", [](const shm::Region& r, uint64_t off) { return shm::read_error(r, off); });
+
+  py::class_<shm::TieredAllocator>(m, "TieredAllocator")
+      .def(py::init<uint64_t, uint64_t, std::vector<uint64_t>, std::vector<uint32_t>, double>(), py::arg("base"),
+           py::arg("pool_bytes"), py::arg("class_sizes") = std::vector<uint64_t>{},
+           py::arg("weights") = std::vector<uint32_t>{}, py::arg("ttl_s") = 30.0)
+      .def("try_allocate", &shm::TieredAllocator::try_allocate)
+      .def("release", &shm::TieredAllocator::release)
+      .def("in_use", &shm::TieredAllocator::in_use)
+      .def("oldest_lease_ms", &shm::TieredAllocator::oldest_lease_ms)
+      .def("largest_slot", &shm::TieredAllocator::largest_slot)
+      .def("layout_summary", &shm::TieredAllocator::layout_summary);
+
+  // ---- servers
+  py::class_<WireServer>(m, "WireServer")
+      .def(py::init<py::object, std::optional<std::string>>(), py::arg("handler"), py::arg("auth_token") = py::none())
+      .def("listen_unix", &WireServer::listen_unix)
+      .def("listen_tcp", &WireServer::listen_tcp, py::arg("host") = "127.0.0.1", py::arg("port") = 9096)
+      .def("attach_shm", &WireServer::attach_shm)
+      .def("start", &WireServer::start)
+      .def("stop", &WireServer::stop, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("running", &WireServer::running)
+      .def_property_readonly("requests_served", &WireServer::requests_served);
+
+  py::class_<ShmServer>(m, "ShmServer")
+      .def(py::init<py::object, std::string, size_t, int>(), py::arg("handler"), py::arg("name"),
+           py::arg("size") = (size_t)256 << 20, py::arg("workers") = 4)
+      .def("start", &ShmServer::start)
+      .def("stop", &ShmServer::stop, py::call_guard<py::gil_scoped_release>())
+      .def_property_readonly("requests_served", &ShmServer::requests_served)
+      .def_property_readonly("pool_in_use", &ShmServer::pool_in_use)
+      .def_property_readonly("pool_oldest_lease_ms", &ShmServer::pool_oldest_lease_ms)
+      .def_property_readonly("pool_exhausted", &ShmServer::pool_exhausted)
+      .def_property_readonly("result_pool_base", &ShmServer::result_pool_base);
+}

@@ -1,0 +1,229 @@
+// Shared-memory transport: region layout, MPMC ring, tensor headers and slot
+// allocators.  Byte layout follows crates/kapsl-shm/src/memory.rs:4-118,
+// ring_buffer.rs:21-229 and server.rs:52-69:
+//
+//   offset 0       ShmHeader (48 B): magic "AIMO" 0x41494D4F, version 1,
+//                  request ring @4096, response ring @69632, tensor pool
+//                  @131072, max_tensor_size = size - 131072, notify fds
+//   offset 4096    Ring<ShmRequest>  (capacity argument 1024)
+//   offset 69632   Ring<ShmResponse> (capacity argument 1024)
+//   offset 131072  tensor pool: TensorHeader (80 B) + data; error blobs are
+//                  [u64 len][utf8]
+//
+// Ring: the first three T-sized slots hold head_reserved, head_committed and
+// tail (each an atomic size_t at the slot start); data slots follow; indices
+// wrap modulo (capacity - 3); one slot stays empty.  Producers reserve with a
+// CAS on head_reserved, write, then publish in reservation order with a CAS on
+// head_committed.  Consumers copy the slot and then CAS the tail (the copy is
+// taken before the slot is released, so a fast producer cannot overwrite it).
+#pragma once
+
+#include <stdint.h>
+
+#include <atomic>
+#include <chrono>
+#include <memory>
+#include <mutex>
+#include <optional>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "wire.h"
+
+namespace kapsl {
+namespace shm {
+
+constexpr uint32_t MAGIC = 0x41494D4F;
+constexpr uint32_t VERSION = 1;
+constexpr uint64_t REQ_RING_OFFSET = 4096;
+constexpr uint64_t RESP_RING_OFFSET = 4096 + 64 * 1024;
+constexpr uint64_t TENSOR_POOL_OFFSET = 128 * 1024;
+constexpr size_t RING_CAPACITY_ARG = 1024;
+
+struct ShmHeader {
+  uint32_t magic;
+  uint32_t version;
+  uint64_t request_queue_offset;
+  uint64_t response_queue_offset;
+  uint64_t tensor_pool_offset;
+  uint64_t max_tensor_size;
+  int32_t notify_read_fd;
+  int32_t notify_write_fd;
+};
+static_assert(sizeof(ShmHeader) == 48, "ShmHeader is 48 bytes");
+
+struct TensorHeader {
+  uint32_t ndim;
+  uint8_t dtype;  // 0 f32, 1 f64, 2 i32, 3 i64 (others are written as 0)
+  uint8_t pad[3];
+  int64_t shape[8];
+  uint64_t data_size;
+};
+static_assert(sizeof(TensorHeader) == 80, "TensorHeader is 80 bytes");
+
+struct ShmRequest {
+  wire::TransportRequestMeta meta;
+  uint64_t tensor_offset;
+  uint64_t tensor_size;
+};
+static_assert(sizeof(ShmRequest) == 40, "ShmRequest is 40 bytes");
+
+struct ShmResponse {
+  wire::TransportResponseMeta meta;
+  uint64_t result_offset;
+  uint64_t result_size;
+  uint64_t error_offset;  // 0 = no error
+};
+static_assert(sizeof(ShmResponse) == 48, "ShmResponse is 48 bytes");
+
+uint8_t dtype_code(const std::string& canonical);
+std::string dtype_from_code(uint8_t code);
+
+class Region {
+ public:
+  // Create (and own) a region; an existing object of that name is replaced.
+  static Region create(const std::string& name, size_t size);
+  static Region open(const std::string& name);
+  Region() = default;
+  Region(Region&& o) noexcept;
+  Region& operator=(Region&& o) noexcept;
+  Region(const Region&) = delete;
+  ~Region();
+
+  uint8_t* base() const { return base_; }
+  size_t size() const { return size_; }
+  const ShmHeader& header() const { return *reinterpret_cast<const ShmHeader*>(base_); }
+  const std::string& name() const { return name_; }
+  bool owner() const { return owner_; }
+  // Every offset/size coming from a peer is checked against the mapping.
+  bool in_bounds(uint64_t off, uint64_t len) const { return off <= size_ && len <= size_ - off; }
+
+ private:
+  uint8_t* base_ = nullptr;
+  size_t size_ = 0;
+  std::string name_;
+  bool owner_ = false;
+  int fds_[2] = {-1, -1};
+};
+
+template <class T>
+class Ring {
+ public:
+  static_assert(sizeof(T) >= sizeof(std::atomic<size_t>), "slot must hold an atomic index");
+  Ring(uint8_t* at, size_t capacity_arg, bool init) : slots_(reinterpret_cast<T*>(at)), cap_(capacity_arg - 3) {
+    if (init) {
+      new (&idx(0)) std::atomic<size_t>(0);
+      new (&idx(1)) std::atomic<size_t>(0);
+      new (&idx(2)) std::atomic<size_t>(0);
+    }
+  }
+  bool push(const T& item) {
+    for (;;) {
+      size_t reserved = idx(0).load(std::memory_order_relaxed);
+      size_t next = (reserved + 1) % cap_;
+      if (next == idx(2).load(std::memory_order_acquire)) return false;  // full
+      if (idx(0).compare_exchange_weak(reserved, next, std::memory_order_relaxed)) {
+        slots_[3 + reserved] = item;
+        size_t expect = reserved;
+        unsigned spins = 0;
+        while (!idx(1).compare_exchange_weak(expect, next, std::memory_order_release, std::memory_order_relaxed)) {
+          expect = reserved;
+          if ((++spins & 63) == 0) std::this_thread::yield();
+        }
+        return true;
+      }
+    }
+  }
+  std::optional<T> pop() {
+    for (;;) {
+      size_t tail = idx(2).load(std::memory_order_relaxed);
+      size_t committed = idx(1).load(std::memory_order_acquire);
+      if (tail == committed) return std::nullopt;
+      T item = slots_[3 + tail];
+      size_t next = (tail + 1) % cap_;
+      if (idx(2).compare_exchange_weak(tail, next, std::memory_order_release, std::memory_order_relaxed)) return item;
+    }
+  }
+  size_t len() const {
+    size_t c = idx(1).load(std::memory_order_acquire), t = idx(2).load(std::memory_order_acquire);
+    return c >= t ? c - t : cap_ - t + c;
+  }
+  size_t capacity() const { return cap_ - 1; }
+
+ private:
+  std::atomic<size_t>& idx(int i) const { return *reinterpret_cast<std::atomic<size_t>*>(&slots_[i]); }
+  T* slots_;
+  size_t cap_;
+};
+
+// Round-robin slot allocator with TTL leases (expired leases are reclaimed).
+class SlotAllocator {
+ public:
+  SlotAllocator(uint64_t base, uint64_t slot_size, uint64_t num_slots, double ttl_s = 30.0);
+  // force: when every slot is leased, take over the one leased longest ago
+  std::optional<uint64_t> try_allocate(uint64_t size, bool force = false);
+  bool release(uint64_t offset);
+  size_t in_use() const;
+  double oldest_lease_ms() const;
+  uint64_t slot_size() const { return slot_; }
+  uint64_t num_slots() const { return n_; }
+  uint64_t base() const { return base_; }
+
+ private:
+  using clock = std::chrono::steady_clock;
+  uint64_t base_, slot_, n_;
+  double ttl_s_;
+  mutable std::mutex mu_;
+  std::vector<std::optional<clock::time_point>> leases_;
+  uint64_t next_ = 0;
+};
+
+// Size classes 256 KiB, 1 MiB, 4 MiB, 16 MiB, 64 MiB (smallest fitting class
+// first, then larger ones).  Bytes are split across classes in proportion to
+// their weights, each class getting at least one slot when it fits.
+class TieredAllocator {
+ public:
+  TieredAllocator(uint64_t base, uint64_t pool_bytes, const std::vector<uint64_t>& class_sizes = {},
+                  const std::vector<uint32_t>& weights = {}, double ttl_s = 30.0);
+  std::optional<uint64_t> try_allocate(uint64_t size, bool force = false);
+  bool release(uint64_t offset);
+  size_t in_use() const;
+  double oldest_lease_ms() const;
+  uint64_t largest_slot() const;
+  std::string layout_summary() const;
+  const std::vector<std::unique_ptr<SlotAllocator>>& classes() const { return classes_; }
+
+ private:
+  std::vector<std::unique_ptr<SlotAllocator>> classes_;
+};
+
+// Slot leases shared by every client process of one region.  The slot layout
+// is the TieredAllocator's over [base, base + bytes); each slot has one 64-bit
+// lease word (0 = free, else the CLOCK_MONOTONIC expiry in ms) stored in the
+// unused tail of header page 0 (offset 64, up to 500 words), taken with a CAS.
+class SharedLeases {
+ public:
+  static constexpr uint64_t kWordsOffset = 64;
+  static constexpr size_t kMaxWords = 500;
+  SharedLeases(Region& r, uint64_t base, uint64_t bytes, double ttl_s = 30.0);
+  std::optional<uint64_t> try_allocate(uint64_t size);
+  bool release(uint64_t offset);
+  uint64_t largest_slot() const { return layout_.largest_slot(); }
+  std::string layout_summary() const { return layout_.layout_summary(); }
+
+ private:
+  TieredAllocator layout_;
+  std::atomic<uint64_t>* words_;
+  double ttl_s_;
+};
+
+// Tensor (header + data) helpers; return false / throw on out-of-bounds input.
+void write_tensor(Region& r, uint64_t off, const wire::Packet& p);
+wire::Packet read_tensor(const Region& r, uint64_t off);
+void write_error(Region& r, uint64_t off, const std::string& msg);
+std::string read_error(const Region& r, uint64_t off);
+uint64_t tensor_bytes(const wire::Packet& p);
+
+}  // namespace shm
+}  // namespace kapsl
