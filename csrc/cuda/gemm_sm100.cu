@@ -366,6 +366,273 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 1) tmem_dealloc(tmem_base, TMEM_COLS);
 }
 
+// ============================================================ 2-SM variant
+// A CTA pair (cluster of 2) computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256, N = 256, K = 16): CTA r TMA-loads rows
+// [r*128, r*128+128) of the A tile and rows [r*128, r*128+128) of the B tile
+// (half of N) into its own shared memory, signalling the leader's barrier.
+// The leader (rank 0) issues the MMAs; each CTA's TMEM receives its 128 rows
+// x 256 columns of the accumulator.  Commits are multicast to the barriers of
+// both CTAs; epilogue warps of both CTAs release an accumulator by arriving on
+// the leader's barrier.  Per CTA and k-block this moves 32 KiB of operands for
+// 2 x 128 x 256 x 64 MACs (the 1-SM 128 x 256 tile moves 48 KiB for half of that).
+// No TMA multicast is used.
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_2sm(void* smem_dst, const CUtensorMap* m, uint64_t* bar, int32_t x,
+                                                int32_t y) {
+  // mbarrier address with the peer bit cleared: transaction bytes land on CTA 0's barrier
+  const uint32_t mbar = smem_u32(bar) & 0xFEFFFFFFu;
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(mbar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void mma_bf16_2sm(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit_2sm_mc(uint64_t* bar) {
+  const uint16_t mask = 0x3;
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+          smem_u32(bar)),
+      "h"(mask)
+      : "memory");
+}
+
+template <int STAGES, int EPI, bool OUT_F32>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    gemm2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
+                   int N, int K, EpiArgs ep, int* __restrict__ err) {
+  constexpr int BN = 256;
+  constexpr int HALF_BYTES = 128 * BK * 2;  // 16 KiB: A half or B half
+  constexpr int STAGE_BYTES = 2 * HALF_BYTES;
+  constexpr uint32_t TMEM_COLS = 512;
+  constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2];
+  __shared__ __align__(8) uint64_t tempty_bar[2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cluster = blockIdx.x >> 1;
+  const int nclusters = gridDim.x >> 1;
+  const int m_tiles = (M + 255) / 256;
+  const int n_tiles = (N + BN - 1) / BN;
+  const int kblocks = (K + BK - 1) / BK;
+  const int units = m_tiles * n_tiles;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 8);  // 4 epilogue warps x 2 CTAs
+    }
+    abort_sh = 0;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base_sh)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_sh;
+
+  auto decode = [&](int u, int& mt, int& nt) {
+    mt = u % m_tiles;
+    nt = u / m_tiles;
+  };
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_a);
+      tma_prefetch_desc(&tmap_b);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int u = cluster; u < units && !*(volatile int*)&abort_sh; u += nclusters) {
+        int mt, nt;
+        decode(u, mt, nt);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1)) {
+            abort_sh = 1;
+            atomicExch(err, 20);
+            break;
+          }
+          uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
+          uint8_t* sb = sa + HALF_BYTES;
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
+          tma_load_2d_2sm(sa, &tmap_a, &full_bar[stage], kb * BK, mt * 256 + (int)rank * 128);
+          tma_load_2d_2sm(sb, &tmap_b, &full_bar[stage], kb * BK, nt * BN + (int)rank * 128);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int u = cluster; u < units && !*(volatile int*)&abort_sh; u += nclusters, ++it) {
+        const int acc = it & 1;
+        const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1)) {
+          abort_sh = 1;
+          atomicExch(err, 21);
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase)) {
+            abort_sh = 1;
+            atomicExch(err, 22);
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
+          const uint32_t sb = sa + HALF_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            mma_bf16_2sm(d_tmem, smem_desc_sw128(sa + k * 32), smem_desc_sw128(sb + k * 32), IDESC,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+          mma_commit_2sm_mc(&empty_bar[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (*(volatile int*)&abort_sh) break;
+        mma_commit_2sm_mc(&tfull_bar[acc]);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3;
+    const uint32_t leader_tempty0 = mapa_shared(smem_u32(&tempty_bar[0]), 0);
+    const uint32_t leader_tempty1 = mapa_shared(smem_u32(&tempty_bar[1]), 0);
+    int it = 0;
+    for (int u = cluster; u < units; u += nclusters, ++it) {
+      int mt, nt;
+      decode(u, mt, nt);
+      const int acc = it & 1;
+      const uint32_t acc_phase = (uint32_t)((it >> 1) & 1);
+      const bool got = mbar_wait_bounded(&tfull_bar[acc], acc_phase);
+      if (!__all_sync(0xffffffffu, got)) {
+        if (lane == 0) {
+          abort_sh = 1;
+          atomicExch(err, 23);
+        }
+        break;
+      }
+      tc_fence_after();
+      const int row = mt * 256 + (int)rank * 128 + quad * 32 + lane;
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      if (EPI == 3) {
+        constexpr int HALF = BN / 2;
+        const int out_c0 = nt * HALF;
+#pragma unroll 1
+        for (int c = 0; c < HALF; c += 32) {
+          float g[32], v[32];
+          tmem_ld32(tbase + c, g);
+          tmem_ld32(tbase + HALF + c, v);
+          if (row < M) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] = silu(g[i]) * v[i];
+            const int nvalid = min(32, N / 2 - (out_c0 + c));
+            if (nvalid > 0) store_row32<OUT_F32>(ep.out, ep.ldc, row, out_c0 + c, nvalid, v);
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+          float v[32];
+          tmem_ld32(tbase + c, v);
+          const int col = nt * BN + c;
+          const int nvalid = min(32, N - col);
+          if (row < M && nvalid > 0) {
+            if (EPI == 1) {
+              float bb[32];
+              load_bf16x32(ep.bias + col, nvalid, bb);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += bb[i];
+            } else if (EPI == 2) {
+              float rr[32];
+              load_bf16x32(ep.res + (int64_t)row * ep.ldr + col, nvalid, rr);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) v[i] += rr[i];
+            }
+            store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc ? leader_tempty1 : leader_tempty0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // no CTA leaves while its peer may still signal it
+  tc_fence_after();
+  if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+}
+
+template <int STAGES, int EPI, bool F32>
+void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& ep, int grid,
+                int* err, cudaStream_t st) {
+  auto kern = gemm2sm_kernel<STAGES, EPI, F32>;
+  constexpr size_t smem = (size_t)STAGES * 2 * 128 * BK * 2 + 1024;
+  static int attr_dev = -1;
+  int dev;
+  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
+  if (attr_dev != dev) {
+    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_dev = dev;
+  }
+  kern<<<grid, kThreads, smem, st>>>(ta, tb, M, N, K, ep, err);
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
 // Sum split-K partials and apply the epilogue.
 template <int EPI, bool OUT_F32>
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, EpiArgs ep) {
@@ -464,6 +731,29 @@ void launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C
   if (ldc % 8 != 0) throw std::runtime_error("gemm: ldc must be a multiple of 8");
   if (epi == 3 && N % 256 != 0) throw std::runtime_error("gemm: SwiGLU epilogue needs N % 256 == 0");
   const int sms = gemm_num_sms();
+  {
+    // 2-SM 256x256 tiles when they fill at least 3/4 of the CTA pairs (force_bn == 512 forces them)
+    const int nclusters = sms / 2;
+    const int units2 = ((M + 255) / 256) * ((N + 255) / 256);
+    const bool use2 = force_bn == 512 || (force_bn == 0 && force_splits == 0 && M >= 256 && units2 * 4 >= nclusters * 3);
+    if (use2) {
+      if (epi == 3 && N % 256 != 0) throw std::runtime_error("gemm: SwiGLU epilogue needs N % 256 == 0");
+      CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, 128, BK);
+      CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, BK);
+      EpiArgs ep{C, ldc, bias, res, ldr, workspace};
+      const int grid = 2 * std::min(units2, nclusters);
+      constexpr int ST = 6;
+      switch (epi) {
+        case 0: out_f32 ? launch_2sm<ST, 0, true>(ta, tb, M, N, K, ep, grid, err, st)
+                        : launch_2sm<ST, 0, false>(ta, tb, M, N, K, ep, grid, err, st); break;
+        case 1: launch_2sm<ST, 1, false>(ta, tb, M, N, K, ep, grid, err, st); break;
+        case 2: launch_2sm<ST, 2, false>(ta, tb, M, N, K, ep, grid, err, st); break;
+        case 3: launch_2sm<ST, 3, false>(ta, tb, M, N, K, ep, grid, err, st); break;
+        default: throw std::runtime_error("gemm: bad epilogue");
+      }
+      return;
+    }
+  }
   int bn = force_bn ? force_bn : 256;
   if (!force_bn && epi != 3) {
     // Narrow tiles when the wide grid would leave most SMs idle.

