@@ -60,12 +60,23 @@ class LLMEngine:
         self.cfg = cfg
         self.ecfg = engine_cfg or EngineConfig()
         self.device = torch.device(device)
+        e = self.ecfg
+        if self.device.type == "cpu":
+            from ..models.cpu_model import CPUCausalLM
+            from .cpu_runner import CPUModelRunner
+
+            self.model = weights if isinstance(weights, CPUCausalLM) else CPUCausalLM.random(cfg, seed)
+            layout = KVLayout(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, e.block_size, torch.float32)
+            nblocks = e.num_blocks or e.max_num_seqs * ((e.max_model_len + e.block_size - 1) // e.block_size)
+            self.pool = KVPool(layout, nblocks, self.device)
+            self.runner = CPUModelRunner(self.model, self.pool)
+            self._finish_init(cfg, e, nblocks, tp_comm)
+            return
         if weights is None:
             tp = 1 if tp_comm is None else tp_comm.world_size
             rank = 0 if tp_comm is None else tp_comm.rank
             weights = random_weights(cfg, self.device, tp=tp, rank=rank, seed=seed)
         self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe)
-        e = self.ecfg
         layout = KVLayout(cfg.num_layers, self.model.hkv, cfg.head_dim, e.block_size)
         nblocks = e.num_blocks
         if nblocks <= 0:
@@ -75,11 +86,14 @@ class LLMEngine:
             if tp_comm is not None and tp_comm.world_size > 1:
                 nblocks = tp_comm.min_int(nblocks)
         self.pool = KVPool(layout, nblocks, self.device)
+        self.runner = ModelRunner(self.model, self.pool, e.max_num_seqs, e.max_num_batched_tokens, e.max_model_len,
+                                  e.use_cuda_graph)
+        self._finish_init(cfg, e, nblocks, tp_comm)
+
+    def _finish_init(self, cfg: ModelConfig, e: EngineConfig, nblocks: int, tp_comm) -> None:
         self.allocator = make_allocator(nblocks, e.block_size, e.enable_prefix_cache, e.eviction)
         self.scheduler = Scheduler(self.allocator, e.max_num_seqs, e.max_num_batched_tokens, e.chunked_prefill,
                                    e.max_model_len)
-        self.runner = ModelRunner(self.model, self.pool, e.max_num_seqs, e.max_num_batched_tokens, e.max_model_len,
-                                  e.use_cuda_graph)
         self._seq_ids = itertools.count(1)
         self.sessions: dict[str, Sequence] = {}
         self.finished: list[Sequence] = []

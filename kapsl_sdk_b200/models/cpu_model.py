@@ -1,0 +1,105 @@
+"""fp32 CPU decoder over a paged KV pool (the CPU backend).
+
+Serves small models (the tiny-Llama GGUF workload) and is the reference for
+the GPU path.  The math is the plain statement in :mod:`kapsl_sdk_b200.ops.reference`;
+when the native CPU kernels are built (``kapsl_sdk_b200._native``) paged
+attention runs in C++ over the block table instead of gathering pages.
+
+Reference counterpart: the CPU kernels ``CpuAttention`` / ``CpuMlp``
+(crates/kapsl-kernels/src/attention/mod.rs:8-99, mlp/mod.rs:13-49), which the
+reference engine never calls; its CPU execution goes through ONNX Runtime or
+llama.cpp instead.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from ..ops import reference as ref
+from .config import ModelConfig
+
+
+class CPUCausalLM:
+    def __init__(self, cfg: ModelConfig, embed: torch.Tensor, lm_head: torch.Tensor, final_norm: torch.Tensor,
+                 layers: list):
+        f = lambda t: None if t is None else t.detach().to("cpu", torch.float32).contiguous()
+        self.cfg = cfg
+        self.embed = f(embed)
+        self.lm_head = f(lm_head)
+        self.final_norm = f(final_norm)
+        self.layers = []
+        for L in layers:
+            d = {k: f(v) for k, v in L.items()}
+            d["qkv"] = torch.cat([d["q"], d["k"], d["v"]], 0)
+            d["qkv_b"] = torch.cat([d["q_b"], d["k_b"], d["v_b"]]) if d.get("q_b") is not None else None
+            if not cfg.is_moe:
+                d["gate_up"] = torch.cat([d["gate"], d["up"]], 0)
+            self.layers.append(d)
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta)
+        self.hq, self.hkv, self.D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
+        self.scale = 1.0 / math.sqrt(self.D)
+        self.device = torch.device("cpu")
+
+    @classmethod
+    def random(cls, cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> "CPUCausalLM":
+        from .llama import random_full_weights
+
+        items = list(random_full_weights(cfg, torch.device("cpu"), seed, std))
+        return cls(cfg, items[0][1], items[1][1], torch.ones(cfg.hidden_size), [t for k, t in items[2:]])
+
+    def forward(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, seqs: list,
+                k_caches: list, v_caches: list, logits_rows: list) -> torch.Tensor:
+        """``seqs``: list of (row_start, n_tokens, ctx_len, block_ids) per sequence;
+        returns fp32 logits for ``logits_rows``."""
+        cfg = self.cfg
+        T = ids.numel()
+        D, hq, hkv = self.D, self.hq, self.hkv
+        h = self.embed[ids.long()]
+        bs = k_caches[0].shape[2]
+        blk = (slots // bs).long()
+        off = (slots % bs).long()
+        for li, L in enumerate(self.layers):
+            x, _ = ref.rmsnorm(h, L["in_norm"], cfg.rms_eps)
+            qkv = x @ L["qkv"].T
+            if L["qkv_b"] is not None:
+                qkv = qkv + L["qkv_b"]
+            q = ref.apply_rope(qkv[:, :hq * D].view(T, hq, D), positions, self.cos_sin)
+            k = ref.apply_rope(qkv[:, hq * D:(hq + hkv) * D].view(T, hkv, D), positions, self.cos_sin)
+            v = qkv[:, (hq + hkv) * D:].view(T, hkv, D)
+            kc, vc = k_caches[li], v_caches[li]
+            kc[blk, :, off] = k.to(kc.dtype)
+            vc[blk, :, off] = v.to(vc.dtype)
+            attn = torch.empty(T, hq * D)
+            for r0, n, ctx, blocks in seqs:
+                kk = ref.gather_paged(kc, blocks, ctx).float()
+                vv = ref.gather_paged(vc, blocks, ctx).float()
+                attn[r0:r0 + n] = ref.attention(q[r0:r0 + n], kk, vv, self.scale, ctx - n).reshape(n, hq * D)
+            h = h + attn @ L["o"].T
+            x, _ = ref.rmsnorm(h, L["post_norm"], cfg.rms_eps)
+            if cfg.is_moe:
+                h = h + self._moe(x, L)
+            else:
+                gu = x @ L["gate_up"].T
+                h = h + ref.silu_mul(gu) @ L["down"].T
+        xs, _ = ref.rmsnorm(h[logits_rows], self.final_norm, cfg.rms_eps)
+        return xs @ self.lm_head.T
+
+    def _moe(self, x: torch.Tensor, L: dict) -> torch.Tensor:
+        cfg = self.cfg
+        p = torch.softmax(x @ L["router"].T, -1)
+        topv, topi = p.topk(cfg.experts_per_token, -1)
+        topv = topv / topv.sum(-1, keepdim=True)
+        out = torch.zeros_like(x)
+        for e in range(cfg.num_experts):
+            sel = topi == e
+            rows = sel.any(-1).nonzero().flatten()
+            if rows.numel() == 0:
+                continue
+            w = (topv * sel).sum(-1)[rows]
+            xe = x[rows]
+            g = xe @ L["experts_gate"][e].T
+            u = xe @ L["experts_up"][e].T
+            out[rows] += w[:, None] * ((g * torch.sigmoid(g) * u) @ L["experts_down"][e].T)
+        return out

@@ -1,0 +1,97 @@
+"""End-to-end LLM serving on the CPU backend: LLMEngine (chunked prefill,
+paged KV, reference sampler) behind LLMBackend, served by the C++ socket
+server and consumed with the C++ client SDK."""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+import torch
+
+from kapsl_sdk_b200.engine_api import BinaryTensorPacket, InferenceRequest, RequestMetadata, TensorDtype
+from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+from kapsl_sdk_b200.llm.sequence import SamplingParams
+from kapsl_sdk_b200.models.config import ModelConfig
+
+
+def tiny_cfg(**kw):
+    c = ModelConfig(name="t", arch="llama", vocab_size=300, hidden_size=64, intermediate_size=128, num_layers=2,
+                    num_heads=4, num_kv_heads=2, head_dim=16, rope_theta=10000.0, max_position=512,
+                    bos_token_id=1, eos_token_id=2)
+    for k, v in kw.items():
+        setattr(c, k, v)
+    return c
+
+
+def cpu_engine(cfg, **kw):
+    return LLMEngine(cfg, device="cpu", engine_cfg=EngineConfig(max_num_seqs=4, max_num_batched_tokens=kw.pop(
+        "chunk", 32), max_model_len=256, num_blocks=64, **kw), seed=0)
+
+
+def test_chunked_prefill_matches_dense_oracle():
+    from kapsl_sdk_b200.models.llama import reference_forward
+
+    cfg = tiny_cfg()
+    eng = cpu_engine(cfg, chunk=16)
+    prompt = list(range(5, 45))
+    out = eng.generate([prompt], SamplingParams.greedy(6, ignore_eos=True))[0]
+    m = eng.model
+    layers = [{k: v for k, v in L.items()} for L in m.layers]
+    toks = list(prompt)
+    for _ in range(6):
+        lg = reference_forward(cfg, layers, m.embed, m.lm_head, m.final_norm, toks)[-1]
+        toks.append(int(lg.argmax()))
+    assert out == toks[len(prompt):]
+
+
+def test_reference_seeded_sampling_is_reproducible():
+    cfg = tiny_cfg()
+    p = SamplingParams(max_new_tokens=8, seed=1234, ignore_eos=True)
+    a = cpu_engine(cfg).generate([[3, 4, 5, 6]], p)[0]
+    b = cpu_engine(cfg).generate([[3, 4, 5, 6]], p)[0]
+    assert a == b and len(a) == 8
+
+
+def test_sessions_continue_previous_turn():
+    cfg = tiny_cfg()
+    eng = cpu_engine(cfg)
+    s1 = eng.add_request("a", [10, 11, 12], SamplingParams.greedy(3, ignore_eos=True), session_id="s")
+    while eng.has_unfinished():
+        eng.step()
+    s2 = eng.add_request("b", [13], SamplingParams.greedy(2, ignore_eos=True), session_id="s")
+    assert s2.prompt_ids == [10, 11, 12] + s1.output_ids + [13]
+    while eng.has_unfinished():
+        eng.step()
+    assert s2.num_cached_prefix > 0 or len(s2.prompt_ids) < 16
+
+
+def test_backend_stream_over_unix_socket():
+    from kapsl_sdk import KapslClient
+    from kapsl_sdk_b200.llm.backend import LLMBackend
+    from kapsl_sdk_b200.server import KapslServer
+
+    cfg = tiny_cfg(vocab_size=259 + 3)
+    backend = LLMBackend(cpu_engine(cfg))
+    d = tempfile.mkdtemp(prefix="kapsl-llm-")
+    path = os.path.join(d, "s.sock")
+    srv = KapslServer(models={0: backend}).listen_unix(path).start()
+    try:
+        c = KapslClient(path)
+        chunks = list(c.infer_stream(0, [1, 5], "string", b"hello"))
+        text = b"".join(chunks)
+        assert len(chunks) >= 1
+        # unary infer returns the concatenated text; greedy requests repeat exactly
+        # (seeded sampling mixes in the per-request sequence id, as the reference does)
+        req = InferenceRequest(BinaryTensorPacket([1, 5], TensorDtype.UTF8, b"hello"),
+                               metadata=RequestMetadata(request_id="fixed", max_new_tokens=5, temperature=0.0))
+        direct = backend.infer(req).data
+        again = backend.infer(req).data
+        assert direct == again
+        with pytest.raises(RuntimeError, match="expects Utf8"):
+            c.infer(0, [1], "float32", b"\0\0\0\0")
+        assert backend.health_check()
+        m = backend.metrics()
+        assert m.kv_cache_blocks_total == 64
+    finally:
+        srv.stop()
+        backend.unload()
