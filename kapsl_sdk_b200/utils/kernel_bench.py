@@ -1,0 +1,148 @@
+"""Kernel micro-benchmarks / profiling drivers for the sm_100a kernels.
+
+    python -m kapsl_sdk_b200.utils.kernel_bench gemm M N K [--epi plain|bias|residual|swiglu] [--time]
+    python -m kapsl_sdk_b200.utils.kernel_bench decode B CTX HQ HKV [--time]
+    python -m kapsl_sdk_b200.utils.kernel_bench prefill S CHUNK HQ HKV [--time]
+    python -m kapsl_sdk_b200.utils.kernel_bench sample B V [--time]
+
+Without ``--time`` each command launches the kernel 3 times (a capture target
+for ncu: ``-k regex:<kernel> -s 2 -c 1``).  With ``--time`` it reports the
+CUDA-event time over 20 launches after 3 warm-ups and the achieved
+FLOP/s or bytes/s.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import random
+
+import torch
+
+
+def _time(fn, iters: int = 20) -> float:
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def bench_gemm(M, N, K, epi, timed):
+    from .. import ops
+
+    dev = torch.device("cuda", 0)
+    a = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    b = torch.randn(N, K, device=dev, dtype=torch.bfloat16) / math.sqrt(K)
+    kw = {}
+    if epi == "bias":
+        kw["bias"] = torch.randn(N, device=dev, dtype=torch.bfloat16)
+    elif epi == "residual":
+        kw["residual"] = torch.randn(M, N, device=dev, dtype=torch.bfloat16)
+        kw["out"] = kw["residual"]
+    elif epi == "swiglu":
+        kw["swiglu"] = True
+    fn = lambda: ops.linear(a, b, **kw)
+    if not timed:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {"kernel": "gemm", "M": M, "N": N, "K": K}
+    ms = _time(fn)
+    return {"kernel": "gemm", "M": M, "N": N, "K": K, "epi": epi, "ms": ms, "tflops": 2 * M * N * K / ms / 1e9}
+
+
+def bench_decode(B, ctx, hq, hkv, timed):
+    from .. import ops
+
+    dev = torch.device("cuda", 0)
+    nb_seq = (ctx + 15) // 16
+    nblocks = B * nb_seq
+    kc = torch.randn(nblocks, hkv, 16, 128, device=dev, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    perm = list(range(nblocks))
+    random.Random(0).shuffle(perm)  # randomly permuted block tables
+    bt = torch.tensor(perm, dtype=torch.int32, device=dev).view(B, nb_seq)
+    q = torch.randn(B, hq * 128, device=dev, dtype=torch.bfloat16)
+    lens = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    out = torch.empty_like(q)
+    fn = lambda: ops.decode_attention(q, kc, vc, bt, lens, hq, hkv, out=out, max_ctx=ctx)
+    if not timed:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {"kernel": "decode_attention", "B": B, "ctx": ctx}
+    ms = _time(fn)
+    nbytes = 2 * B * ctx * hkv * 128 * 2
+    return {"kernel": "decode_attention", "B": B, "ctx": ctx, "hq": hq, "hkv": hkv, "ms": ms,
+            "GBps": nbytes / ms / 1e6}
+
+
+def bench_prefill(S, chunk, hq, hkv, timed):
+    from .. import ops
+
+    dev = torch.device("cuda", 0)
+    nb_seq = (chunk + 15) // 16
+    kc = torch.randn(S * nb_seq, hkv, 16, 128, device=dev, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = torch.arange(S * nb_seq, dtype=torch.int32, device=dev).view(S, nb_seq)
+    q = torch.randn(S * chunk, hq * 128, device=dev, dtype=torch.bfloat16)
+    out = torch.empty_like(q)
+    info = torch.tensor([(s * chunk, chunk, chunk, s) for s in range(S)], dtype=torch.int32, device=dev)
+    work = torch.tensor(ops.prefill_work([chunk] * S), dtype=torch.int32, device=dev)
+    fn = lambda: ops.prefill_attention(q, kc, vc, work, info, bt, hq, hkv, out)
+    if not timed:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {"kernel": "prefill_attention", "S": S, "chunk": chunk}
+    ms = _time(fn)
+    flops = S * hq * 128 * 4 * chunk * chunk / 2
+    return {"kernel": "prefill_attention", "S": S, "chunk": chunk, "ms": ms, "tflops": flops / ms / 1e9}
+
+
+def bench_sample(B, V, timed):
+    from .. import ops
+
+    dev = torch.device("cuda", 0)
+    logits = torch.randn(B, V, device=dev) * 3
+    temp = torch.full((B,), 0.7, device=dev)
+    topk = torch.full((B,), 40, dtype=torch.int32, device=dev)
+    topp = torch.full((B,), 0.9, device=dev)
+    rng = torch.arange(B, dtype=torch.int64, device=dev)
+    out = torch.empty(B, dtype=torch.int32, device=dev)
+    fn = lambda: ops.sample(logits, temp, topk, topp, rng, out)
+    if not timed:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {"kernel": "sample", "B": B, "V": V}
+    ms = _time(fn)
+    return {"kernel": "sample", "B": B, "V": V, "ms": ms, "GBps": B * V * 4 / ms / 1e6}
+
+
+def main(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("what", choices=["gemm", "decode", "prefill", "sample"])
+    p.add_argument("dims", nargs="+", type=int)
+    p.add_argument("--epi", default="plain", choices=["plain", "bias", "residual", "swiglu"])
+    p.add_argument("--time", action="store_true")
+    a = p.parse_args(argv)
+    if a.what == "gemm":
+        r = bench_gemm(*a.dims[:3], a.epi, a.time)
+    elif a.what == "decode":
+        r = bench_decode(*a.dims[:4], a.time)
+    elif a.what == "prefill":
+        r = bench_prefill(*a.dims[:4], a.time)
+    else:
+        r = bench_sample(*a.dims[:2], a.time)
+    print(json.dumps(r))
+
+
+if __name__ == "__main__":
+    main()
