@@ -107,8 +107,8 @@ class GGUFTokenizer:
                     pass
             if self.types[i] in (2, 3):  # unknown / control
                 continue
-            parts.extend(t.replace(self.SPACE, " ").encode("utf-8"))
-        out = parts.decode("utf-8", errors="replace")
+            parts.extend(t.encode("utf-8"))
+        out = parts.decode("utf-8", errors="replace").replace(self.SPACE, " ")
         return out[1:] if out.startswith(" ") else out
 
 

@@ -1,0 +1,336 @@
+"""GGUF model files: reading, block dequantization, Q4_K quantization, writing.
+
+Reference: GGUF models are served by llama.cpp (crates/kapsl-llm/src/gguf_backend.rs);
+here GGUF is parsed with the ``gguf`` package's reader/writer and the tensors
+are turned into this runtime's weight layout.  The quantized block formats are
+the GGML ones (they have to match to read real files):
+
+* Q8_0: 32 values, f16 scale ``d`` + 32 x int8; v = d * q
+* Q4_K: 256 values in 8 sub-blocks of 32; f16 ``d`` and ``dmin``, 12 bytes of
+  packed 6-bit (scale, min) pairs, 128 bytes of 4-bit quants; v = d*sc_j*q - dmin*m_j.
+  Quants of sub-blocks 2c and 2c+1 share bytes 32c..32c+31 (low / high nibble).
+* Q6_K: 256 values; 128 bytes of low 4 bits, 64 bytes of high 2 bits, 16 int8
+  sub-block scales, f16 ``d``; v = d * sc * (q - 32).
+
+Llama-architecture files store q/k projections permuted for interleaved rotary
+pairs; they are permuted back to the rotate-half layout the RoPE kernel uses.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import numpy as np
+import torch
+
+from ..models.config import ModelConfig
+
+QK_K = 256
+Q4_K_BYTES = 144
+Q6_K_BYTES = 210
+Q8_0_BYTES = 34
+
+
+# ------------------------------------------------------------ dequantization
+def _q4k_scale_min(sc: np.ndarray):
+    """sc: [nb, 12] uint8 -> scales, mins [nb, 8] (6-bit each)."""
+    s = np.empty((sc.shape[0], 8), np.uint8)
+    m = np.empty((sc.shape[0], 8), np.uint8)
+    s[:, :4] = sc[:, 0:4] & 63
+    m[:, :4] = sc[:, 4:8] & 63
+    s[:, 4:] = (sc[:, 8:12] & 0xF) | ((sc[:, 0:4] >> 6) << 4)
+    m[:, 4:] = (sc[:, 8:12] >> 4) | ((sc[:, 4:8] >> 6) << 4)
+    return s, m
+
+
+def dequant_q4_k(raw: np.ndarray) -> np.ndarray:
+    b = raw.reshape(-1, Q4_K_BYTES)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    dmin = b[:, 2:4].copy().view(np.float16).astype(np.float32)
+    s, m = _q4k_scale_min(b[:, 4:16])
+    qs = b[:, 16:144].reshape(-1, 4, 32)
+    q = np.empty((b.shape[0], 8, 32), np.float32)
+    q[:, 0::2] = qs & 0xF
+    q[:, 1::2] = qs >> 4
+    out = d[:, :, None] * s[:, :, None].astype(np.float32) * q - dmin[:, :, None] * m[:, :, None].astype(np.float32)
+    return out.reshape(-1)
+
+
+def dequant_q6_k(raw: np.ndarray) -> np.ndarray:
+    b = raw.reshape(-1, Q6_K_BYTES)
+    ql = b[:, 0:128].astype(np.int32)
+    qh = b[:, 128:192].astype(np.int32)
+    sc = b[:, 192:208].view(np.int8).astype(np.float32)
+    d = b[:, 208:210].copy().view(np.float16).astype(np.float32)
+    out = np.empty((b.shape[0], 256), np.float32)
+    for half in range(2):
+        L = ql[:, half * 64:(half + 1) * 64]
+        H = qh[:, half * 32:(half + 1) * 32]
+        S = sc[:, half * 8:(half + 1) * 8]
+        base = half * 128
+        q1 = (L[:, :32] & 0xF) | ((H & 3) << 4)
+        q2 = (L[:, 32:] & 0xF) | (((H >> 2) & 3) << 4)
+        q3 = (L[:, :32] >> 4) | (((H >> 4) & 3) << 4)
+        q4 = (L[:, 32:] >> 4) | (((H >> 6) & 3) << 4)
+        for j, q in enumerate((q1, q2, q3, q4)):
+            idx = np.arange(32) // 16
+            scl = S[:, idx + 2 * j]
+            out[:, base + 32 * j:base + 32 * j + 32] = d * scl * (q - 32)  # d: [nb, 1]
+    return out.reshape(-1)
+
+
+def dequant_q8_0(raw: np.ndarray) -> np.ndarray:
+    b = raw.reshape(-1, Q8_0_BYTES)
+    d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
+    q = b[:, 2:].view(np.int8).astype(np.float32)
+    return (d * q).reshape(-1)
+
+
+# -------------------------------------------------------------- quantization
+def quantize_q4_k(x: np.ndarray) -> np.ndarray:
+    """fp32 [n * 256] -> Q4_K bytes.  Per 32-value sub-block: min = max(0, -min(x)),
+    scale = (max(x) + min) / 15; the 8 scales and mins are then coded as 6-bit
+    multiples of the super-block ``d = max(scale) / 63`` and ``dmin = max(min) / 63``."""
+    x = np.asarray(x, np.float32).reshape(-1, 8, 32)
+    nb = x.shape[0]
+    lo = np.minimum(x.min(-1), 0.0)
+    hi = x.max(-1)
+    mins = -lo
+    scales = (hi - lo) / 15.0
+    d = scales.max(-1) / 63.0
+    dmin = mins.max(-1) / 63.0
+    d16 = d.astype(np.float16)
+    dm16 = dmin.astype(np.float16)
+    dq = np.where(d16 > 0, d16.astype(np.float32), 1.0)
+    dmq = np.where(dm16 > 0, dm16.astype(np.float32), 1.0)
+    sc = np.clip(np.rint(scales / dq[:, None]), 0, 63).astype(np.uint8)
+    mn = np.clip(np.rint(mins / dmq[:, None]), 0, 63).astype(np.uint8)
+    eff_s = d16.astype(np.float32)[:, None] * sc
+    eff_m = dm16.astype(np.float32)[:, None] * mn
+    q = np.where(eff_s[:, :, None] > 0, np.rint((x + eff_m[:, :, None]) / np.where(eff_s > 0, eff_s, 1)[:, :, None]), 0)
+    q = np.clip(q, 0, 15).astype(np.uint8)
+    out = np.zeros((nb, Q4_K_BYTES), np.uint8)
+    out[:, 0:2] = d16.reshape(-1, 1).view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = dm16.reshape(-1, 1).view(np.uint8).reshape(nb, 2)
+    p = np.zeros((nb, 12), np.uint8)
+    p[:, 0:4] = (sc[:, :4] & 63) | ((sc[:, 4:] >> 4) << 6)
+    p[:, 4:8] = (mn[:, :4] & 63) | ((mn[:, 4:] >> 4) << 6)
+    p[:, 8:12] = (sc[:, 4:] & 0xF) | ((mn[:, 4:] & 0xF) << 4)
+    out[:, 4:16] = p
+    qq = q.reshape(nb, 4, 2, 32)
+    out[:, 16:] = (qq[:, :, 0] | (qq[:, :, 1] << 4)).reshape(nb, 128)
+    return out.reshape(-1)
+
+
+# ------------------------------------------------------------------ reading
+def _permute_back(w: np.ndarray, n_head: int) -> np.ndarray:
+    """Undo the interleaved-rotary permutation of llama q/k rows."""
+    rows, cols = w.shape
+    hd = rows // n_head
+    return w.reshape(n_head, hd // 2, 2, cols).swapaxes(1, 2).reshape(rows, cols)
+
+
+def _permute(w: np.ndarray, n_head: int) -> np.ndarray:
+    rows, cols = w.shape
+    hd = rows // n_head
+    return w.reshape(n_head, 2, hd // 2, cols).swapaxes(1, 2).reshape(rows, cols)
+
+
+def tensor_to_numpy(t) -> np.ndarray:
+    """A gguf ReaderTensor -> fp32 array in (rows, cols) order."""
+    from gguf import GGMLQuantizationType as Q
+
+    shape = tuple(int(x) for x in reversed(t.shape))  # GGUF lists ne0 (innermost) first
+    raw = np.asarray(t.data)
+    tt = t.tensor_type
+    if tt == Q.F32:
+        a = raw.astype(np.float32)
+    elif tt == Q.F16:
+        a = raw.view(np.float16).astype(np.float32)
+    elif tt == Q.BF16:
+        a = (raw.view(np.uint16).astype(np.uint32) << 16).view(np.float32)
+    elif tt == Q.Q8_0:
+        a = dequant_q8_0(raw.view(np.uint8))
+    elif tt == Q.Q4_K:
+        a = dequant_q4_k(raw.view(np.uint8))
+    elif tt == Q.Q6_K:
+        a = dequant_q6_k(raw.view(np.uint8))
+    else:
+        raise ValueError(f"unsupported GGUF tensor type {tt.name} for {t.name}")
+    return a.reshape(shape)
+
+
+def _field(reader, key, default=None):
+    f = reader.fields.get(key)
+    if f is None:
+        return default
+    try:
+        v = f.contents()
+    except Exception:
+        v = f.parts[f.data[0]] if f.data else default
+        if hasattr(v, "tolist"):
+            v = v.tolist()
+            if isinstance(v, list) and len(v) == 1:
+                v = v[0]
+    return v
+
+
+def gguf_config(reader) -> ModelConfig:
+    arch = _field(reader, "general.architecture", "llama")
+    p = lambda k, d=None: _field(reader, f"{arch}.{k}", d)
+    heads = int(p("attention.head_count", 32))
+    hidden = int(p("embedding_length", 4096))
+    tokens = _field(reader, "tokenizer.ggml.tokens")
+    vocab = int(p("vocab_size", len(tokens) if tokens is not None else 32000))
+    return ModelConfig(
+        name=_field(reader, "general.name", arch) or arch, arch="qwen2" if arch == "qwen2" else "llama",
+        vocab_size=vocab, hidden_size=hidden, intermediate_size=int(p("feed_forward_length", 4 * hidden)),
+        num_layers=int(p("block_count", 32)), num_heads=heads, num_kv_heads=int(p("attention.head_count_kv", heads)),
+        head_dim=int(p("attention.key_length", hidden // heads)), rope_theta=float(p("rope.freq_base", 10000.0)),
+        rms_eps=float(p("attention.layer_norm_rms_epsilon", 1e-5)), qkv_bias=arch == "qwen2",
+        max_position=min(int(p("context_length", 4096)), 4096),
+        bos_token_id=_field(reader, "tokenizer.ggml.bos_token_id", 1),
+        eos_token_id=_field(reader, "tokenizer.ggml.eos_token_id", 2),
+    )
+
+
+def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
+    """Yields the runtime's full-tensor stream (see models.llama.random_full_weights)."""
+    from gguf import GGUFReader
+
+    r = GGUFReader(path)
+    cfg = cfg or gguf_config(r)
+    T = {t.name: t for t in r.tensors}
+    get = lambda n: torch.from_numpy(np.ascontiguousarray(tensor_to_numpy(T[n])))
+    permuted = _field(r, "general.architecture", "llama") == "llama"
+    emb = get("token_embd.weight")
+    yield "embed", emb
+    yield "lm_head", get("output.weight") if "output.weight" in T else emb
+    yield "final_norm", get("output_norm.weight")
+    for i in range(cfg.num_layers):
+        b = f"blk.{i}."
+        q = tensor_to_numpy(T[b + "attn_q.weight"])
+        k = tensor_to_numpy(T[b + "attn_k.weight"])
+        if permuted:
+            q = _permute_back(q, cfg.num_heads)
+            k = _permute_back(k, cfg.num_kv_heads)
+        full = {"q": torch.from_numpy(np.ascontiguousarray(q)), "k": torch.from_numpy(np.ascontiguousarray(k)),
+                "v": get(b + "attn_v.weight"), "o": get(b + "attn_output.weight"),
+                "in_norm": get(b + "attn_norm.weight"), "post_norm": get(b + "ffn_norm.weight"),
+                "gate": get(b + "ffn_gate.weight"), "up": get(b + "ffn_up.weight"),
+                "down": get(b + "ffn_down.weight")}
+        if b + "attn_q.bias" in T:
+            full["q_b"], full["k_b"], full["v_b"] = (get(b + "attn_q.bias"), get(b + "attn_k.bias"),
+                                                   get(b + "attn_v.bias"))
+        yield "layer", full
+
+
+def gguf_tokenizer(path: str):
+    from gguf import GGUFReader
+
+    from ..llm.tokenizer import GGUFTokenizer
+
+    r = GGUFReader(path)
+    toks = _field(r, "tokenizer.ggml.tokens")
+    if not toks:
+        return None
+    return GGUFTokenizer(toks, _field(r, "tokenizer.ggml.scores"), _field(r, "tokenizer.ggml.token_type"),
+                         _field(r, "tokenizer.ggml.bos_token_id", 1), _field(r, "tokenizer.ggml.eos_token_id", 2))
+
+
+def load_gguf_model(path: str, device, tp: int = 1, rank: int = 0):
+    from gguf import GGUFReader
+
+    from ..models.cpu_model import CPUCausalLM
+    from ..models.llama import weights_from_full
+
+    cfg = gguf_config(GGUFReader(path))
+    tok = gguf_tokenizer(path)
+    dev = torch.device(device)
+    stream = iter_gguf_full(path, cfg)
+    if dev.type == "cpu":
+        items = list(stream)
+        d = dict((k, v) for k, v in items if k != "layer")
+        return cfg, CPUCausalLM(cfg, d["embed"], d["lm_head"], d["final_norm"],
+                                [v for k, v in items if k == "layer"]), tok
+    gpu_stream = ((k, v.to(dev, torch.bfloat16) if isinstance(v, torch.Tensor)
+                   else {kk: vv.to(dev, torch.bfloat16) for kk, vv in v.items()}) for k, v in stream)
+    return cfg, weights_from_full(cfg, gpu_stream, dev, tp, rank), tok
+
+
+# ------------------------------------------------------------------ writing
+def synthetic_vocab(n: int) -> tuple:
+    """Tokens for a random-init model: <unk>, <s>, </s>, 256 byte tokens, then pieces."""
+    toks = ["<unk>", "<s>", "</s>"] + [f"<0x{b:02X}>" for b in range(256)]
+    types = [2, 3, 3] + [6] * 256
+    i = 0
+    while len(toks) < n:
+        toks.append(f"▁t{i}")
+        types.append(1)
+        i += 1
+    return toks[:n], [0.0] * n, types[:n]
+
+
+def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32") -> None:
+    """Serialize a full-tensor stream as a llama-architecture GGUF file.
+    ``quant``: "f32", "f16" or "q4_k" (2-D weights quantized, norms kept f32)."""
+    from gguf import GGMLQuantizationType as Q
+    from gguf import GGUFWriter
+
+    w = GGUFWriter(path, "llama")
+    w.add_name(cfg.name)
+    w.add_context_length(cfg.max_position)
+    w.add_embedding_length(cfg.hidden_size)
+    w.add_block_count(cfg.num_layers)
+    w.add_feed_forward_length(cfg.intermediate_size)
+    w.add_head_count(cfg.num_heads)
+    w.add_head_count_kv(cfg.num_kv_heads)
+    w.add_rope_freq_base(cfg.rope_theta)
+    w.add_layer_norm_rms_eps(cfg.rms_eps)
+    w.add_vocab_size(cfg.vocab_size)
+    toks, scores, types = synthetic_vocab(cfg.vocab_size)
+    w.add_tokenizer_model("llama")
+    w.add_token_list(toks)
+    w.add_token_scores(scores)
+    w.add_token_types(types)
+    w.add_bos_token_id(1)
+    w.add_eos_token_id(2)
+
+    def put(name, t: torch.Tensor, is_weight: bool):
+        a = t.detach().float().cpu().numpy()
+        if quant == "q4_k" and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
+            # quantized tensors are handed over as [rows, bytes per row]
+            w.add_tensor(name, quantize_q4_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q4_K)
+        elif quant == "f16" and a.ndim == 2:
+            w.add_tensor(name, a.astype(np.float16))
+        else:
+            w.add_tensor(name, np.ascontiguousarray(a.astype(np.float32)))
+
+    li = 0
+    saw_norm = False
+    for kind, t in full_stream:
+        if kind == "embed":
+            put("token_embd.weight", t, True)
+        elif kind == "lm_head":
+            put("output.weight", t, True)
+        elif kind == "final_norm":
+            put("output_norm.weight", t, False)
+            saw_norm = True
+        else:
+            b = f"blk.{li}."
+            put(b + "attn_norm.weight", t["in_norm"], False)
+            put(b + "ffn_norm.weight", t["post_norm"], False)
+            put(b + "attn_q.weight", torch.from_numpy(_permute(t["q"].float().cpu().numpy(), cfg.num_heads)), True)
+            put(b + "attn_k.weight", torch.from_numpy(_permute(t["k"].float().cpu().numpy(), cfg.num_kv_heads)), True)
+            put(b + "attn_v.weight", t["v"], True)
+            put(b + "attn_output.weight", t["o"], True)
+            put(b + "ffn_gate.weight", t["gate"], True)
+            put(b + "ffn_up.weight", t["up"], True)
+            put(b + "ffn_down.weight", t["down"], True)
+            li += 1
+    if not saw_norm:
+        put("output_norm.weight", torch.ones(cfg.hidden_size), False)
+    w.write_header_to_file()
+    w.write_kv_data_to_file()
+    w.write_tensors_to_file()
+    w.close()

@@ -1,0 +1,464 @@
+"""ONNX models without ONNX Runtime.
+
+No ``onnx`` / ``onnxruntime`` package exists here, so this module decodes the
+protobuf wire format of ``ModelProto`` directly (varints and length-delimited
+fields; field numbers from the public onnx.proto) and provides:
+
+* ``read_model`` -> graph nodes, inputs/outputs, initializers as numpy arrays
+  (raw_data or typed repeated fields; external data files next to the model);
+* ``OnnxGraph`` -> a PyTorch interpreter for an explicitly scoped op subset
+  (MatMul, Gemm, Add, Sub, Mul, Div, Relu, Sigmoid, Tanh, Softmax, Reshape,
+  Flatten, Transpose, Identity, Constant, Conv, MaxPool, AveragePool,
+  GlobalAveragePool, Concat, Gather, Unsqueeze, Squeeze, Cast, Erf, Sqrt, Pow,
+  ReduceMean, LayerNormalization, Shape, Slice).  Graphs using other ops are
+  rejected at load time with the op names listed;
+* ``load_onnx_llm`` -> LLM weights from initializers named like a HF
+  checkpoint (``model.layers.{i}.self_attn.q_proj.weight`` ...), the way an
+  ONNX export of a decoder keeps them.
+
+Reference: the reference serves any ONNX graph through ONNX Runtime
+(crates/kapsl-backends/src/onnx.rs) and LLM exports through ORT sessions.
+"""
+from __future__ import annotations
+
+import os
+import struct
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+import torch
+
+# TensorProto.DataType
+_NP = {1: np.float32, 2: np.uint8, 3: np.int8, 4: np.uint16, 5: np.int16, 6: np.int32, 7: np.int64, 9: np.bool_,
+       10: np.float16, 11: np.float64, 12: np.uint32, 13: np.uint64}
+BFLOAT16 = 16
+
+
+def _varint(b: bytes, i: int):
+    shift = v = 0
+    while True:
+        x = b[i]
+        i += 1
+        v |= (x & 0x7F) << shift
+        if x < 0x80:
+            return v, i
+        shift += 7
+
+
+def _fields(b: bytes):
+    """Yields (field_number, wire_type, value) over one message."""
+    i, n = 0, len(b)
+    while i < n:
+        key, i = _varint(b, i)
+        f, wt = key >> 3, key & 7
+        if wt == 0:
+            v, i = _varint(b, i)
+        elif wt == 1:
+            v = b[i:i + 8]
+            i += 8
+        elif wt == 2:
+            ln, i = _varint(b, i)
+            v = b[i:i + ln]
+            i += ln
+        elif wt == 5:
+            v = b[i:i + 4]
+            i += 4
+        else:
+            raise ValueError(f"unsupported protobuf wire type {wt}")
+        yield f, wt, v
+
+
+def _packed_varints(v, wt):
+    if wt == 0:
+        return [v]
+    out, i = [], 0
+    while i < len(v):
+        x, i = _varint(v, i)
+        out.append(x)
+    return out
+
+
+def _signed64(x: int) -> int:
+    return x - (1 << 64) if x >= 1 << 63 else x
+
+
+@dataclass
+class Node:
+    op: str
+    inputs: list
+    outputs: list
+    name: str = ""
+    attrs: dict = field(default_factory=dict)
+
+
+@dataclass
+class OnnxModel:
+    nodes: list
+    inputs: list
+    outputs: list
+    initializers: dict
+    opset: int = 13
+
+
+def _tensor(b: bytes, base_dir: Optional[str]) -> tuple:
+    dims, dtype, name, raw = [], 1, "", None
+    floats, int32s, int64s, doubles = [], [], [], []
+    ext = {}
+    for f, wt, v in _fields(b):
+        if f == 1:
+            dims += [_signed64(x) for x in _packed_varints(v, wt)]
+        elif f == 2:
+            dtype = v
+        elif f == 4:
+            floats += list(struct.unpack(f"<{len(v) // 4}f", v)) if wt == 2 else [struct.unpack("<f", v)[0]]
+        elif f == 5:
+            int32s += [_signed64(x) for x in _packed_varints(v, wt)]
+        elif f == 7:
+            int64s += [_signed64(x) for x in _packed_varints(v, wt)]
+        elif f == 8:
+            name = v.decode()
+        elif f == 9:
+            raw = bytes(v)
+        elif f == 10:
+            doubles += list(struct.unpack(f"<{len(v) // 8}d", v)) if wt == 2 else [struct.unpack("<d", v)[0]]
+        elif f == 13:
+            k = val = None
+            for ff, _, vv in _fields(v):
+                if ff == 1:
+                    k = vv.decode()
+                elif ff == 2:
+                    val = vv.decode()
+            ext[k] = val
+    if ext.get("location"):
+        with open(os.path.join(base_dir or ".", ext["location"]), "rb") as fh:
+            fh.seek(int(ext.get("offset", 0)))
+            ln = ext.get("length")
+            raw = fh.read(int(ln)) if ln else fh.read()
+    if dtype == BFLOAT16:
+        u16 = np.frombuffer(raw, np.uint16) if raw is not None else np.asarray(int32s, np.uint16)
+        arr = (u16.astype(np.uint32) << 16).view(np.float32)
+    elif raw is not None:
+        arr = np.frombuffer(raw, _NP[dtype]).copy()
+    elif dtype in (1,):
+        arr = np.asarray(floats, np.float32)
+    elif dtype == 11:
+        arr = np.asarray(doubles, np.float64)
+    elif dtype == 7:
+        arr = np.asarray(int64s, np.int64)
+    elif dtype == 10:
+        arr = np.asarray(int32s, np.uint16).view(np.float16)
+    else:
+        arr = np.asarray(int32s, _NP.get(dtype, np.int32))
+    return name, arr.reshape(dims) if dims else arr.reshape(())
+
+
+def _attr(b: bytes, base_dir):
+    name, val, kind = "", None, None
+    ints, floats, strs = [], [], []
+    for f, wt, v in _fields(b):
+        if f == 1:
+            name = v.decode()
+        elif f == 2:
+            val = struct.unpack("<f", v)[0]
+        elif f == 3:
+            val = _signed64(v)
+        elif f == 4:
+            val = v.decode(errors="replace")
+        elif f == 5:
+            val = _tensor(v, base_dir)[1]
+        elif f == 7:
+            floats += list(struct.unpack(f"<{len(v) // 4}f", v)) if wt == 2 else [struct.unpack("<f", v)[0]]
+        elif f == 8:
+            ints += [_signed64(x) for x in _packed_varints(v, wt)]
+        elif f == 9:
+            strs.append(v.decode(errors="replace"))
+        elif f == 20:
+            kind = v
+    if ints:
+        val = ints
+    elif floats:
+        val = floats
+    elif strs:
+        val = strs
+    return name, val
+
+
+def _value_info_name(b: bytes) -> str:
+    for f, _, v in _fields(b):
+        if f == 1:
+            return v.decode()
+    return ""
+
+
+def read_model(path: str) -> OnnxModel:
+    with open(path, "rb") as fh:
+        data = fh.read()
+    base = os.path.dirname(os.path.abspath(path))
+    graph = None
+    opset = 13
+    for f, _, v in _fields(data):
+        if f == 7:
+            graph = v
+        elif f == 8:
+            for ff, _, vv in _fields(v):
+                if ff == 2:
+                    opset = vv
+    if graph is None:
+        raise ValueError("ONNX file has no graph")
+    nodes, inputs, outputs, inits = [], [], [], {}
+    for f, _, v in _fields(graph):
+        if f == 1:
+            n = Node("", [], [])
+            for ff, _, vv in _fields(v):
+                if ff == 1:
+                    n.inputs.append(vv.decode())
+                elif ff == 2:
+                    n.outputs.append(vv.decode())
+                elif ff == 3:
+                    n.name = vv.decode()
+                elif ff == 4:
+                    n.op = vv.decode()
+                elif ff == 5:
+                    k, a = _attr(vv, base)
+                    n.attrs[k] = a
+            nodes.append(n)
+        elif f == 5:
+            k, a = _tensor(v, base)
+            inits[k] = a
+        elif f == 11:
+            inputs.append(_value_info_name(v))
+        elif f == 12:
+            outputs.append(_value_info_name(v))
+    inputs = [i for i in inputs if i not in inits]
+    return OnnxModel(nodes, inputs, outputs, inits, opset)
+
+
+# ---------------------------------------------------------- interpreter
+def _conv_pads(a, nd):
+    p = a.get("pads") or [0] * (2 * nd)
+    return p[:nd], p[nd:]
+
+
+class OnnxGraph:
+    SUPPORTED = {"MatMul", "Gemm", "Add", "Sub", "Mul", "Div", "Relu", "Sigmoid", "Tanh", "Softmax", "Reshape",
+                 "Flatten", "Transpose", "Identity", "Constant", "Conv", "MaxPool", "AveragePool",
+                 "GlobalAveragePool", "Concat", "Gather", "Unsqueeze", "Squeeze", "Cast", "Erf", "Sqrt", "Pow",
+                 "ReduceMean", "LayerNormalization", "Shape", "Slice", "Dropout", "BatchNormalization"}
+
+    def __init__(self, model: OnnxModel, device="cpu"):
+        bad = sorted({n.op for n in model.nodes} - self.SUPPORTED)
+        if bad:
+            raise ValueError(f"unsupported ONNX ops: {', '.join(bad)}")
+        self.m = model
+        self.device = torch.device(device)
+        self.consts = {k: torch.from_numpy(np.ascontiguousarray(v)).to(self.device) for k, v in model.initializers.items()}
+
+    def run(self, feeds: dict) -> dict:
+        env = dict(self.consts)
+        for k, v in feeds.items():
+            env[k] = v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v))
+            env[k] = env[k].to(self.device)
+        for n in self.m.nodes:
+            args = [env[i] if i else None for i in n.inputs]
+            outs = self._op(n, args)
+            if not isinstance(outs, (list, tuple)):
+                outs = [outs]
+            for name, val in zip(n.outputs, outs):
+                env[name] = val
+        return {o: env[o] for o in self.m.outputs}
+
+    def _op(self, n: Node, x: list):
+        a, op = n.attrs, n.op
+        F = torch.nn.functional
+        if op == "MatMul":
+            return torch.matmul(x[0], x[1])
+        if op == "Gemm":
+            A = x[0].T if a.get("transA") else x[0]
+            B = x[1].T if a.get("transB") else x[1]
+            y = a.get("alpha", 1.0) * (A @ B)
+            if len(x) > 2 and x[2] is not None:
+                y = y + a.get("beta", 1.0) * x[2]
+            return y
+        if op in ("Add", "Sub", "Mul", "Div", "Pow"):
+            f = {"Add": torch.add, "Sub": torch.sub, "Mul": torch.mul, "Div": torch.div, "Pow": torch.pow}[op]
+            return f(x[0], x[1])
+        if op == "Relu":
+            return torch.relu(x[0])
+        if op == "Sigmoid":
+            return torch.sigmoid(x[0])
+        if op == "Tanh":
+            return torch.tanh(x[0])
+        if op == "Erf":
+            return torch.erf(x[0])
+        if op == "Sqrt":
+            return torch.sqrt(x[0])
+        if op == "Softmax":
+            return torch.softmax(x[0], dim=a.get("axis", -1))
+        if op in ("Identity", "Dropout"):
+            return x[0]
+        if op == "Constant":
+            v = a.get("value")
+            return torch.from_numpy(np.ascontiguousarray(v)).to(self.device)
+        if op == "Reshape":
+            shape = [int(s) for s in x[1].tolist()]
+            shape = [x[0].shape[i] if s == 0 else s for i, s in enumerate(shape)]
+            return x[0].reshape(shape)
+        if op == "Flatten":
+            ax = a.get("axis", 1)
+            return x[0].reshape(int(np.prod(x[0].shape[:ax])) if ax else 1, -1)
+        if op == "Transpose":
+            perm = a.get("perm") or list(reversed(range(x[0].dim())))
+            return x[0].permute(*perm)
+        if op == "Conv":
+            nd = x[1].dim() - 2
+            lo, hi = _conv_pads(a, nd)
+            xin = F.pad(x[0], [p for pair in zip(reversed(lo), reversed(hi)) for p in pair]) if any(lo + hi) else x[0]
+            fn = {1: F.conv1d, 2: F.conv2d, 3: F.conv3d}[nd]
+            return fn(xin, x[1], x[2] if len(x) > 2 else None, stride=a.get("strides") or 1,
+                      dilation=a.get("dilations") or 1, groups=a.get("group", 1))
+        if op in ("MaxPool", "AveragePool"):
+            nd = x[0].dim() - 2
+            lo, hi = _conv_pads(a, nd)
+            xin = F.pad(x[0], [p for pair in zip(reversed(lo), reversed(hi)) for p in pair],
+                        value=float("-inf") if op == "MaxPool" else 0.0) if any(lo + hi) else x[0]
+            k = a["kernel_shape"]
+            s = a.get("strides") or k
+            fn = getattr(F, ("max" if op == "MaxPool" else "avg") + f"_pool{nd}d")
+            return fn(xin, k, s)
+        if op == "GlobalAveragePool":
+            return x[0].mean(dim=tuple(range(2, x[0].dim())), keepdim=True)
+        if op == "BatchNormalization":
+            return F.batch_norm(x[0], x[3], x[4], x[1], x[2], False, 0.0, a.get("epsilon", 1e-5))
+        if op == "Concat":
+            return torch.cat(x, dim=a.get("axis", 0))
+        if op == "Gather":
+            return torch.index_select(x[0], a.get("axis", 0), x[1].long().flatten()).reshape(
+                *x[0].shape[:a.get("axis", 0)], *x[1].shape, *x[0].shape[a.get("axis", 0) + 1:])
+        if op in ("Unsqueeze", "Squeeze"):
+            axes = a.get("axes") if "axes" in a else (x[1].tolist() if len(x) > 1 and x[1] is not None else None)
+            y = x[0]
+            if op == "Unsqueeze":
+                for ax in sorted(axes):
+                    y = y.unsqueeze(ax)
+                return y
+            return y.squeeze() if axes is None else y.squeeze(tuple(axes))
+        if op == "Cast":
+            to = a["to"]
+            return x[0].to({1: torch.float32, 6: torch.int32, 7: torch.int64, 10: torch.float16, 11: torch.float64,
+                            9: torch.bool, 16: torch.bfloat16}.get(to, torch.float32))
+        if op == "ReduceMean":
+            axes = a.get("axes") or (x[1].tolist() if len(x) > 1 and x[1] is not None else None)
+            return x[0].mean(dim=tuple(axes) if axes else None, keepdim=bool(a.get("keepdims", 1)))
+        if op == "LayerNormalization":
+            ax = a.get("axis", -1)
+            shape = x[0].shape[ax:]
+            return F.layer_norm(x[0], shape, x[1], x[2] if len(x) > 2 else None, a.get("epsilon", 1e-5))
+        if op == "Shape":
+            return torch.tensor(list(x[0].shape), dtype=torch.int64, device=self.device)
+        if op == "Slice":
+            starts, ends = x[1].tolist(), x[2].tolist()
+            axes = x[3].tolist() if len(x) > 3 and x[3] is not None else list(range(len(starts)))
+            steps = x[4].tolist() if len(x) > 4 and x[4] is not None else [1] * len(starts)
+            sl = [slice(None)] * x[0].dim()
+            for s, e, ax, st in zip(starts, ends, axes, steps):
+                sl[ax] = slice(s, e if e < (1 << 62) else None, st)
+            return x[0][tuple(sl)]
+        raise ValueError(f"unsupported ONNX op {op}")
+
+
+# ------------------------------------------------------------------ LLMs
+def load_onnx_llm(path: str, root: str, device, tp: int = 1, rank: int = 0):
+    """LLM weights from an ONNX export whose initializers keep HF names."""
+    from ..models.config import ModelConfig
+    from ..models.cpu_model import CPUCausalLM
+    from ..models.llama import weights_from_full
+
+    model = read_model(path)
+    cfg = ModelConfig.from_hf_config(os.path.join(root, "config.json"))
+    W = {k: torch.from_numpy(np.ascontiguousarray(v)).float() for k, v in model.initializers.items()}
+
+    def get(name):
+        if name in W:
+            return W[name]
+        raise ValueError(f"ONNX export lacks initializer {name}; only exports keeping HF tensor names are supported")
+
+    def stream():
+        emb = get("model.embed_tokens.weight")
+        yield "embed", emb
+        yield "lm_head", W.get("lm_head.weight", emb)
+        yield "final_norm", get("model.norm.weight")
+        for i in range(cfg.num_layers):
+            p = f"model.layers.{i}."
+            a = p + "self_attn."
+            full = {"q": get(a + "q_proj.weight"), "k": get(a + "k_proj.weight"), "v": get(a + "v_proj.weight"),
+                    "o": get(a + "o_proj.weight"), "in_norm": get(p + "input_layernorm.weight"),
+                    "post_norm": get(p + "post_attention_layernorm.weight"), "gate": get(p + "mlp.gate_proj.weight"),
+                    "up": get(p + "mlp.up_proj.weight"), "down": get(p + "mlp.down_proj.weight")}
+            if a + "q_proj.bias" in W:
+                full["q_b"], full["k_b"], full["v_b"] = W[a + "q_proj.bias"], W[a + "k_proj.bias"], W[a + "v_proj.bias"]
+            yield "layer", full
+
+    dev = torch.device(device)
+    if dev.type == "cpu":
+        items = list(stream())
+        d = dict((k, v) for k, v in items if k != "layer")
+        return cfg, CPUCausalLM(cfg, d["embed"], d["lm_head"], d["final_norm"],
+                                [v for k, v in items if k == "layer"]), None
+    conv = ((k, v.to(dev, torch.bfloat16) if isinstance(v, torch.Tensor)
+             else {kk: vv.to(dev, torch.bfloat16) for kk, vv in v.items()}) for k, v in stream())
+    return cfg, weights_from_full(cfg, conv, dev, tp, rank), None
+
+
+# ------------------------------------------------------------ writing
+def _enc_varint(x: int) -> bytes:
+    out = bytearray()
+    x &= (1 << 64) - 1
+    while True:
+        b = x & 0x7F
+        x >>= 7
+        out.append(b | (0x80 if x else 0))
+        if not x:
+            return bytes(out)
+
+
+def _key(f: int, wt: int) -> bytes:
+    return _enc_varint((f << 3) | wt)
+
+
+def _ld(f: int, b: bytes) -> bytes:
+    return _key(f, 2) + _enc_varint(len(b)) + b
+
+
+def encode_tensor(name: str, a: np.ndarray) -> bytes:
+    dt = {np.dtype(np.float32): 1, np.dtype(np.int64): 7, np.dtype(np.int32): 6, np.dtype(np.float16): 10}[a.dtype]
+    b = b"".join(_key(1, 0) + _enc_varint(d) for d in a.shape)
+    b += _key(2, 0) + _enc_varint(dt) + _ld(8, name.encode()) + _ld(9, np.ascontiguousarray(a).tobytes())
+    return b
+
+
+def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, opset: int = 13) -> bytes:
+    """Minimal ModelProto writer (for tests and synthetic exports)."""
+    g = b""
+    for n in nodes:
+        nb = b"".join(_ld(1, i.encode()) for i in n.inputs) + b"".join(_ld(2, o.encode()) for o in n.outputs)
+        nb += _ld(3, (n.name or n.op).encode()) + _ld(4, n.op.encode())
+        for k, v in n.attrs.items():
+            ab = _ld(1, k.encode())
+            if isinstance(v, float):
+                ab += _key(2, 5) + struct.pack("<f", v) + _key(20, 0) + _enc_varint(1)
+            elif isinstance(v, int):
+                ab += _key(3, 0) + _enc_varint(v) + _key(20, 0) + _enc_varint(2)
+            elif isinstance(v, (list, tuple)):
+                ab += b"".join(_key(8, 0) + _enc_varint(int(i)) for i in v) + _key(20, 0) + _enc_varint(7)
+            nb += _ld(5, ab)
+        g += _ld(1, nb)
+    g += _ld(2, b"graph")
+    for k, v in initializers.items():
+        g += _ld(5, encode_tensor(k, v))
+    for i in inputs:
+        g += _ld(11, _ld(1, i.encode()))
+    for o in outputs:
+        g += _ld(12, _ld(1, o.encode()))
+    m = _key(1, 0) + _enc_varint(8) + _ld(2, b"kapsl") + _ld(7, g) + _ld(8, _key(2, 0) + _enc_varint(opset))
+    return m

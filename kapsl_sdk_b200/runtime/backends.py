@@ -1,0 +1,262 @@
+"""Backends, the backend factory and the engine pool (crates/kapsl-backends).
+
+* ``OnnxBackend``: an :class:`Engine` over :class:`~kapsl_sdk_b200.loaders.onnx.OnnxGraph`
+  (GPU when available).  Shape-bucketed graph instances are kept in an LRU of
+  ``KAPSL_ORT_SESSION_BUCKETS`` entries (reference onnx.rs:367-441); inputs are
+  validated per dtype; additional named inputs are fed by name.
+* ``BackendFactory``: ``gguf`` and ``llm`` frameworks -> :class:`LLMBackend`,
+  ``onnx`` -> ``OnnxBackend``; provider order preferred -> fallbacks ->
+  fastest available (cuda, cpu); ``validate_requirements`` checks RAM, VRAM and
+  CUDA version against the probed devices and understands the multi-device
+  strategies pool / round-robin / data-parallel / pipeline / tensor-parallel /
+  auto (factory.rs:17-579).
+* ``EnginePool``: LRU ``(model_id, device_id) -> engine`` with health-checked
+  ``get``, an eviction callback, warm-up and a background health task
+  (engine_pool.rs:13-292).
+"""
+from __future__ import annotations
+
+import collections
+import os
+import threading
+import time
+from typing import Callable, Optional
+
+import numpy as np
+
+from ..engine_api import (BinaryTensorPacket, Engine, EngineError, EngineMetrics, EngineModelInfo,
+                          InferenceRequest, TensorDtype)
+from ..hal.device import DeviceInfo, probe
+from .loader import HardwareRequirements, Manifest
+
+
+class OnnxBackend(Engine):
+    def __init__(self, device: Optional[str] = None, max_buckets: Optional[int] = None):
+        import torch
+
+        self.device = device or ("cuda:0" if torch.cuda.is_available() else "cpu")
+        self.max_buckets = max_buckets or int(os.environ.get("KAPSL_ORT_SESSION_BUCKETS", "4"))
+        self.model = None
+        self.buckets: "collections.OrderedDict" = collections.OrderedDict()
+        self._lock = threading.Lock()
+        self._m = EngineMetrics()
+        self._times: list = []
+
+    def load(self, model_path: str) -> None:
+        from ..loaders.onnx import OnnxGraph, read_model
+
+        try:
+            self.model = read_model(model_path)
+            self.graph = OnnxGraph(self.model, self.device)
+        except (OSError, ValueError) as e:
+            raise EngineError.model_load(model_path, str(e))
+
+    def _graph_for(self, key):
+        with self._lock:
+            g = self.buckets.get(key)
+            if g is None:
+                g = self.graph
+                self.buckets[key] = g
+                if len(self.buckets) > self.max_buckets:
+                    self.buckets.popitem(last=False)
+            else:
+                self.buckets.move_to_end(key)
+            return g
+
+    def infer(self, request: InferenceRequest) -> BinaryTensorPacket:
+        import torch
+
+        if self.model is None:
+            raise EngineError.model_not_loaded()
+        request.input.validate()
+        if request.input.dtype is TensorDtype.UTF8:
+            raise EngineError.invalid_input("ONNX backend expects numeric input")
+        feeds = {self.model.inputs[0]: request.input.to_numpy()}
+        for nt in request.additional_inputs:
+            nt.tensor.validate()
+            feeds[nt.name] = nt.tensor.to_numpy()
+        missing = [n for n in self.model.inputs if n not in feeds]
+        if missing:
+            raise EngineError.invalid_input(f"missing model inputs: {missing}")
+        t0 = time.perf_counter()
+        g = self._graph_for(tuple(tuple(v.shape) for v in feeds.values()))
+        try:
+            with torch.no_grad():
+                out = g.run(feeds)[self.model.outputs[0]]
+        except Exception as e:
+            raise EngineError.inference(str(e))
+        dt = time.perf_counter() - t0
+        self._m.inference_time = dt
+        arr = out.detach().cpu().numpy()
+        if arr.dtype == np.float16 or arr.dtype == np.float64:
+            arr = arr.astype(np.float32) if arr.dtype == np.float16 else arr
+        if arr.dtype == np.bool_:
+            arr = arr.astype(np.uint8)
+        return BinaryTensorPacket.from_numpy(arr)
+
+    def model_info(self) -> EngineModelInfo:
+        if self.model is None:
+            return EngineModelInfo()
+        return EngineModelInfo(input_names=list(self.model.inputs), output_names=list(self.model.outputs),
+                               framework="onnx")
+
+    def metrics(self) -> EngineMetrics:
+        return self._m
+
+    def health_check(self) -> bool:
+        return self.model is not None
+
+    def unload(self) -> None:
+        self.model = None
+        self.buckets.clear()
+
+
+class BackendFactory:
+    PROVIDER_ORDER = ["tensorrt", "cuda", "coreml", "rocm", "directml", "openvino", "cpu"]
+
+    def __init__(self, device_info: Optional[DeviceInfo] = None):
+        self.info = device_info or probe()
+
+    def available_providers(self) -> list:
+        return (["cuda"] if self.info.has_cuda() else []) + ["cpu"]
+
+    def provider_chain(self, hw: HardwareRequirements) -> list:
+        avail = self.available_providers()
+        policy = os.environ.get("KAPSL_PROVIDER_POLICY", "fastest").lower()
+        chain = []
+        if hw.preferred_provider:
+            chain.append(hw.preferred_provider.lower())
+        chain += [p.lower() for p in hw.fallback_providers]
+        if policy == "fastest" or not chain:
+            chain += [p for p in self.PROVIDER_ORDER if p in avail]
+        seen = []
+        for p in chain:
+            p = "cuda" if p == "tensorrt" else p
+            if p in avail and p not in seen:
+                seen.append(p)
+        if "cpu" not in seen:
+            seen.append("cpu")
+        return seen
+
+    def validate_requirements(self, manifest: Manifest, provider: str = "cuda") -> list:
+        """Unmet requirements as messages (empty list = OK)."""
+        hw = manifest.hardware_requirements
+        errs = []
+        if hw.min_memory_mb and self.info.total_memory_mb and self.info.total_memory_mb < hw.min_memory_mb:
+            errs.append(f"needs {hw.min_memory_mb} MB RAM, host has {self.info.total_memory_mb} MB")
+        if provider == "cuda":
+            gpus = self.info.gpus()
+            ids = hw.gpu_device_ids or ([hw.device_id] if hw.device_id is not None else [])
+            strategy = (hw.strategy or "auto").lower()
+            if strategy in ("pipeline", "tensor-parallel", "data-parallel", "round-robin", "pool") and ids:
+                missing = [i for i in ids if i >= len(gpus)]
+                if missing:
+                    errs.append(f"strategy {strategy} needs GPUs {ids}; {len(gpus)} present")
+            if hw.min_vram_mb:
+                cand = [g for g in gpus if not ids or g.id in ids]
+                if not any(g.total_memory_mb >= hw.min_vram_mb for g in cand):
+                    errs.append(f"needs {hw.min_vram_mb} MB of GPU memory")
+            if hw.min_cuda_version and self.info.cuda_version:
+                def v(s):
+                    return tuple(int(x) for x in s.split(".")[:2])
+
+                if v(self.info.cuda_version) < v(hw.min_cuda_version):
+                    errs.append(f"needs CUDA {hw.min_cuda_version}, have {self.info.cuda_version}")
+            if not gpus:
+                errs.append("no CUDA device")
+        return errs
+
+    def create_backend(self, manifest: Manifest, model_path: str) -> Engine:
+        from ..llm.backend import LLMBackend
+
+        fw = manifest.framework.lower()
+        last = None
+        for provider in self.provider_chain(manifest.hardware_requirements):
+            if self.validate_requirements(manifest, provider) and provider != "cpu":
+                continue
+            try:
+                if fw in ("llm", "gguf"):
+                    from .loader import build_llm_engine
+
+                    dev = "cpu" if provider == "cpu" else f"cuda:{manifest.hardware_requirements.device_id or 0}"
+                    eng, tok, rc = build_llm_engine(model_path, device=dev)
+                    return LLMBackend(eng, tok, rc)
+                b = OnnxBackend(device="cpu" if provider == "cpu" else "cuda:0")
+                b.load(model_path)
+                return b
+            except EngineError as e:
+                last = e
+            except Exception as e:  # provider failure: fall back to the next one
+                last = EngineError.model_load(model_path, str(e))
+        raise last or EngineError.model_load(model_path, "no provider could load the model")
+
+
+class EnginePool:
+    def __init__(self, capacity: int = 8, on_evict: Optional[Callable] = None):
+        self.capacity = capacity
+        self.on_evict = on_evict
+        self._m: "collections.OrderedDict" = collections.OrderedDict()
+        self._lock = threading.RLock()
+        self._stop = threading.Event()
+        self._thread = None
+
+    def put(self, model_id: int, device_id: int, engine: Engine, warmup: bool = False) -> None:
+        if warmup:
+            engine.warmup()
+        with self._lock:
+            self._m[(model_id, device_id)] = engine
+            self._m.move_to_end((model_id, device_id))
+            while len(self._m) > self.capacity:
+                key, old = self._m.popitem(last=False)
+                self._evict(key, old)
+
+    def _evict(self, key, eng) -> None:
+        try:
+            eng.unload()
+        finally:
+            if self.on_evict:
+                self.on_evict(key)
+
+    def get(self, model_id: int, device_id: int) -> Optional[Engine]:
+        with self._lock:
+            eng = self._m.get((model_id, device_id))
+            if eng is None:
+                return None
+            if not eng.health_check():
+                del self._m[(model_id, device_id)]
+                self._evict((model_id, device_id), eng)
+                return None
+            self._m.move_to_end((model_id, device_id))
+            return eng
+
+    def remove(self, model_id: int, device_id: int) -> bool:
+        with self._lock:
+            eng = self._m.pop((model_id, device_id), None)
+        if eng is not None:
+            self._evict((model_id, device_id), eng)
+        return eng is not None
+
+    def __len__(self) -> int:
+        return len(self._m)
+
+    def check_health(self) -> int:
+        """Evict unhealthy engines; returns how many were removed."""
+        bad = []
+        with self._lock:
+            for k, e in list(self._m.items()):
+                if not e.health_check():
+                    bad.append((k, self._m.pop(k)))
+        for k, e in bad:
+            self._evict(k, e)
+        return len(bad)
+
+    def start_health_task(self, period_s: float = 10.0) -> None:
+        def run():
+            while not self._stop.wait(period_s):
+                self.check_health()
+
+        self._thread = threading.Thread(target=run, daemon=True, name="kapsl-engine-pool-health")
+        self._thread.start()
+
+    def stop(self) -> None:
+        self._stop.set()
