@@ -216,6 +216,59 @@ void gemm(Tensor A, Tensor B, Tensor C, int64_t epi, c10::optional<Tensor> bias,
                      (int)force_splits);
 }
 
+// ---- tensor parallel over NVLink peer memory
+template <class T>
+std::vector<T*> as_ptrs(const std::vector<int64_t>& v) {
+  std::vector<T*> out;
+  for (int64_t x : v) out.push_back(reinterpret_cast<T*>(x));
+  return out;
+}
+
+void gemm_scatter(Tensor A, Tensor B, std::vector<int64_t> peers, int64_t my_rank, int64_t rows_per_rank,
+                  int64_t ld_recv, Tensor err) {
+  CHECK_DT(A, at::kBFloat16, "A");
+  CHECK_DT(B, at::kBFloat16, "B");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 && A.size(1) == B.size(1),
+              "gemm_scatter: A [M, K], B [N, K]");
+  TORCH_CHECK(ld_recv >= B.size(0), "gemm_scatter: receive rows narrower than N");
+  const c10::cuda::CUDAGuard g(A.device());
+  auto p = as_ptrs<__nv_bfloat16>(peers);
+  kapsl::launch_gemm_scatter(bf(A), A.stride(0), bf(B), B.stride(0), p.data(), (int)p.size(), (int)my_rank,
+                             (int)rows_per_rank, ld_recv, (int)A.size(0), (int)B.size(0), (int)A.size(1),
+                             err.data_ptr<int>(), cur_stream());
+}
+
+void tp_reduce_ag(std::vector<int64_t> recv, std::vector<int64_t> hidden, std::vector<int64_t> flags, int64_t rank,
+                  int64_t rows_per_rank, int64_t rows_total, int64_t cols, int64_t ld, Tensor epoch_ctr, Tensor err) {
+  TORCH_CHECK(recv.size() == hidden.size() && recv.size() == flags.size(), "tp_reduce_ag: pointer tables differ");
+  CHECK_DT(epoch_ctr, at::kLong, "epoch_ctr");
+  const c10::cuda::CUDAGuard g(epoch_ctr.device());
+  auto r = as_ptrs<__nv_bfloat16>(recv);
+  auto h = as_ptrs<__nv_bfloat16>(hidden);
+  auto f = as_ptrs<int64_t>(flags);
+  kapsl::launch_tp_reduce_ag(r.data(), h.data(), f.data(), (int)r.size(), (int)rank, (int)rows_per_rank,
+                             (int)rows_total, (int)cols, ld, epoch_ctr.data_ptr<int64_t>(), err.data_ptr<int>(),
+                             kapsl::gemm_num_sms(), cur_stream());
+}
+
+int64_t symm_alloc(int64_t bytes) { return reinterpret_cast<int64_t>(kapsl::symm_alloc((size_t)bytes)); }
+void symm_free(int64_t p) { kapsl::symm_free(reinterpret_cast<void*>(p)); }
+py::bytes symm_handle(int64_t p) { return py::bytes(kapsl::symm_handle(reinterpret_cast<void*>(p))); }
+int64_t symm_open(py::bytes h) { return reinterpret_cast<int64_t>(kapsl::symm_open(std::string(h))); }
+void symm_close(int64_t p) { kapsl::symm_close(reinterpret_cast<void*>(p)); }
+
+// A tensor view over raw device memory (symmetric buffers); no ownership.
+Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, std::string dtype, int64_t device) {
+  at::ScalarType st;
+  if (dtype == "bfloat16") st = at::kBFloat16;
+  else if (dtype == "float32") st = at::kFloat;
+  else if (dtype == "int64") st = at::kLong;
+  else if (dtype == "int32") st = at::kInt;
+  else TORCH_CHECK(false, "tensor_from_ptr: unsupported dtype ", dtype);
+  auto opts = torch::TensorOptions().dtype(st).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), shape, opts);
+}
+
 int64_t launch_count() { return (int64_t)kapsl::launch_count(); }
 int64_t num_sms() { return kapsl::gemm_num_sms(); }
 
@@ -234,6 +287,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("sample", &sample, "top-k/top-p/temperature/penalty sampler with per-row LCG");
   m.def("count_tokens", &count_tokens, "counts[rows[i], ids[i]] += 1");
   m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A @ B^T)");
+  m.def("gemm_scatter", &gemm_scatter, "row-parallel GEMM storing rows into owner ranks' receive buffers");
+  m.def("tp_reduce_ag", &tp_reduce_ag, "barrier + reduce own rows + residual + all-gather push + barrier");
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_free", &symm_free);
+  m.def("symm_handle", &symm_handle);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("tensor_from_ptr", &tensor_from_ptr);
   m.def("launch_count", &launch_count, "kernels launched through this library so far");
   m.def("num_sms", &num_sms);
 }

@@ -107,7 +107,7 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
 }
-// 2-D tiled load, no multicast.  x = innermost (column) coordinate in elements.
+// 2-D tiled load into this CTA's shared memory.  x = innermost (column) coordinate in elements.
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m, uint64_t* bar,
                                             int32_t x, int32_t y) {
   asm volatile(

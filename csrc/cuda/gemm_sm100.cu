@@ -17,7 +17,8 @@
 // last BN/2 up) writing C[M, N/2].  Split-K writes fp32 partials that
 // `splitk_reduce_kernel` sums and finishes with the same epilogue.
 //
-// No cluster multicast is used anywhere in this file.
+// Operand tiles are loaded per CTA (each CTA reads its own tiles from local
+// HBM); EPI 5 stores rows into peer GPUs' receive buffers (tensor parallel).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -102,7 +103,18 @@ struct EpiArgs {
   const bf16* res;     // [M, N] or null
   int64_t ldr;
   float* partial;      // split-K fp32 partials [splits, M, N]
+  // EPI 5 (tensor-parallel scatter): row r belongs to rank r / rows_per_rank and
+  // is stored into that rank's receive slot [my_rank] over NVLink.
+  __nv_bfloat16* peers[8];
+  int rows_per_rank;
+  int my_rank;
 };
+
+__device__ __forceinline__ __nv_bfloat16* scatter_dst(const EpiArgs& ep, int row, int col) {
+  const int owner = row / ep.rows_per_rank;
+  const int local = row - owner * ep.rows_per_rank;
+  return ep.peers[owner] + ((int64_t)ep.my_rank * ep.rows_per_rank + local) * ep.ldc + col;
+}
 
 // Store 32 consecutive columns (c0..c0+31) of one row.
 template <bool OUT_F32>
@@ -350,7 +362,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] += rr[i];
               }
-              store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
+              if (EPI == 5)
+                store_row32<false>(scatter_dst(ep, row, col), 0, 0, 0, nvalid, v);
+              else
+                store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
             }
           }
         }
@@ -372,11 +387,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 // [r*128, r*128+128) of the A tile and rows [r*128, r*128+128) of the B tile
 // (half of N) into its own shared memory, signalling the leader's barrier.
 // The leader (rank 0) issues the MMAs; each CTA's TMEM receives its 128 rows
-// x 256 columns of the accumulator.  Commits are multicast to the barriers of
-// both CTAs; epilogue warps of both CTAs release an accumulator by arriving on
-// the leader's barrier.  Per CTA and k-block this moves 32 KiB of operands for
-// 2 x 128 x 256 x 64 MACs (the 1-SM 128 x 256 tile moves 48 KiB for half of that).
-// No TMA multicast is used.
+// x 256 columns of the accumulator.  MMA completion is signalled to the
+// barriers of both CTAs by one tcgen05.commit; epilogue warps of both CTAs
+// release an accumulator by arriving on the leader's barrier.  Per CTA and
+// k-block this moves 32 KiB of operands for 2 x 128 x 256 x 64 MACs (the 1-SM
+// 128 x 256 tile moves 48 KiB for half of that).  Every operand copy is a plain
+// per-CTA TMA load of this GPU's memory.
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -600,7 +616,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] += rr[i];
             }
-            store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
+            if (EPI == 5)
+              store_row32<false>(scatter_dst(ep, row, col), 0, 0, 0, nvalid, v);
+            else
+              store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
           }
         }
       }
@@ -719,6 +738,41 @@ int gemm_num_sms() {
   KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
   if (dev < 16 && n[dev] == 0) KAPSL_CHECK_CUDA(cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev));
   return dev < 16 ? n[dev] : 148;
+}
+
+// Tensor-parallel row-parallel GEMM: every output row is stored into the
+// receive buffer of the rank that owns it (peers[owner], slot my_rank) —
+// the reduce-scatter's transfer happens inside the epilogue, tile by tile.
+void launch_gemm_scatter(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, bf16* const* peers, int world,
+                         int my_rank, int rows_per_rank, int64_t ld_recv, int M, int N, int K, int* err,
+                         cudaStream_t st) {
+  using namespace gemm;
+  if (M == 0 || N == 0) return;
+  if (K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0 || ld_recv % 8 != 0)
+    throw std::runtime_error("gemm_scatter: K and leading dims must be multiples of 8");
+  if (world < 1 || world > 8 || rows_per_rank * world < M) throw std::runtime_error("gemm_scatter: bad row split");
+  EpiArgs ep{nullptr, ld_recv, nullptr, nullptr, 0, nullptr};
+  for (int i = 0; i < world; ++i) ep.peers[i] = peers[i];
+  ep.rows_per_rank = rows_per_rank;
+  ep.my_rank = my_rank;
+  const int sms = gemm_num_sms();
+  const int units2 = ((M + 255) / 256) * ((N + 255) / 256);
+  if (M >= 256 && units2 * 4 >= (sms / 2) * 3) {
+    CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, 128, BK);
+    CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, BK);
+    launch_2sm<6, 5, false>(ta, tb, M, N, K, ep, 2 * std::min(units2, sms / 2), err, st);
+    return;
+  }
+  const int m_tiles = (M + BM - 1) / BM;
+  const bool narrow = m_tiles * ((N + 255) / 256) < sms && N % 128 == 0;
+  const int bn = narrow ? 128 : 256;
+  CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, BM, BK);
+  CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, bn, BK);
+  const int units = m_tiles * ((N + bn - 1) / bn);
+  if (narrow)
+    launch_cfg<128, 6, 5, false>(ta, tb, M, N, K, 1, ep, std::min(units, sms), err, st);
+  else
+    launch_cfg<256, 4, 5, false>(ta, tb, M, N, K, 1, ep, std::min(units, sms), err, st);
 }
 
 // Chooses tile width and split-K so that the grid covers the SMs.

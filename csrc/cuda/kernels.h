@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <cstddef>
+#include <string>
 
 namespace kapsl {
 
@@ -47,5 +48,18 @@ void launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, in
                  bool out_f32, int M, int N, int K, int epi, const __nv_bfloat16* bias, const __nv_bfloat16* res,
                  int64_t ldr, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st, int force_bn,
                  int force_splits);
+
+// tensor parallel over NVLink peer memory (tp_comm.cu / gemm_sm100.cu)
+void launch_gemm_scatter(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb,
+                         __nv_bfloat16* const* peers, int world, int my_rank, int rows_per_rank, int64_t ld_recv,
+                         int M, int N, int K, int* err, cudaStream_t st);
+void launch_tp_reduce_ag(__nv_bfloat16* const* recv, __nv_bfloat16* const* hidden, int64_t* const* flags, int world,
+                         int rank, int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr,
+                         int* err, int num_sms, cudaStream_t st);
+void* symm_alloc(size_t bytes);
+void symm_free(void* p);
+std::string symm_handle(void* p);
+void* symm_open(const std::string& handle);
+void symm_close(void* p);
 
 }  // namespace kapsl

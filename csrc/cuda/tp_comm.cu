@@ -1,0 +1,187 @@
+// Tensor-parallel communication over NVLink peer memory (CUDA IPC mappings).
+//
+//  * symmetric buffers: each rank cudaMalloc's a region, exports its IPC handle,
+//    and maps every peer's region; kernels get a table of peer base pointers.
+//  * row-parallel reduction, fused with the residual add and the all-gather:
+//      GEMM epilogue (gemm_sm100.cu, EPI_SCATTER) stores each partial tile row
+//      into the receive slot [my_rank] of the rank that owns the row;
+//      tp_reduce_ag_kernel then, on each rank:
+//        1. barrier 1 ("my partials are out") with every peer,
+//        2. sums the world_size partials of its own rows in fp32, adds the
+//           residual, writes bf16 rows into its residual stream and pushes the
+//           same rows into every peer's residual stream (all-gather),
+//        3. barrier 2 ("my rows are out"), done by the last CTA to finish,
+//      so when the kernel completes every rank holds the full reduced hidden
+//      state.  Data crosses NVLink once in each direction (reduce-scatter +
+//      all-gather volume, no extra HBM round trip for the partials).
+//  * barriers: per-rank int64 flag words in symmetric memory, written with
+//    st.release.sys into the peers and polled with ld.acquire.sys; every wait is
+//    bounded by %globaltimer and records an error code instead of hanging.
+//    Epochs live in device memory, so the kernels can be captured in CUDA graphs.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace kapsl {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ void st_release_sys(int64_t* p, int64_t v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// flags layout per rank: [2 sites][8 peers] int64, then [2] epoch/done counters
+struct TPArgs {
+  bf16* recv[8];       // peer receive buffers: [world][rows_per_rank][ld] bf16 partials
+  bf16* hidden[8];     // peer residual streams [rows_pad][ld] bf16
+  int64_t* flags[8];   // peer flag words
+  int world;
+  int rank;
+  int rows_per_rank;
+  int rows_total;      // real rows (T)
+  int cols;
+  int64_t ld;
+  int64_t* epoch_ctr;  // local: [0] epoch, [1] finished-CTA counter
+  int* err;
+};
+
+__device__ bool wait_flags(const int64_t* flags_site, int world, int64_t epoch, uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int p = 0; p < world; ++p) {
+    while (ld_acquire_sys(flags_site + p) < epoch) {
+      if (globaltimer_ns() - t0 > timeout_ns) return false;
+    }
+  }
+  return true;
+}
+
+__global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
+  __shared__ int64_t epoch_sh;
+  __shared__ int ok_sh;
+  if (threadIdx.x == 0) {
+    epoch_sh = a.epoch_ctr[0] + 1;
+    ok_sh = 1;
+    if (blockIdx.x == 0) {
+      __threadfence_system();  // the previous kernel's peer stores are performed
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 0 * 8 + a.rank, epoch_sh);
+    }
+    if (!wait_flags(a.flags[a.rank] + 0 * 8, a.world, epoch_sh, 5000000000ull)) {
+      ok_sh = 0;
+      atomicExch(a.err, 30);
+    }
+  }
+  __syncthreads();
+  const int64_t epoch = epoch_sh;
+  if (ok_sh) {
+    // rows owned by this rank, 8 columns (16 B) per thread-iteration
+    const int r0 = a.rank * a.rows_per_rank;
+    const int nrows = max(0, min(a.rows_per_rank, a.rows_total - r0));
+    const int chunks = a.cols / 8;
+    const int64_t total = (int64_t)nrows * chunks;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+      const int lr = (int)(i / chunks), c = (int)(i % chunks);
+      float acc[8];
+      {
+        const uint4 h = *reinterpret_cast<const uint4*>(a.hidden[a.rank] + (int64_t)(r0 + lr) * a.ld + c * 8);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&h);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __bfloat1622float2(hp[j]);
+          acc[2 * j] = f.x;
+          acc[2 * j + 1] = f.y;
+        }
+      }
+      const bf16* mine = a.recv[a.rank];
+      for (int p = 0; p < a.world; ++p) {
+        const uint4 v = *reinterpret_cast<const uint4*>(mine + ((int64_t)p * a.rows_per_rank + lr) * a.ld + c * 8);
+        const __nv_bfloat162* vp = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __bfloat1622float2(vp[j]);
+          acc[2 * j] += f.x;
+          acc[2 * j + 1] += f.y;
+        }
+      }
+      uint4 o;
+      o.x = pack_bf16(acc[0], acc[1]);
+      o.y = pack_bf16(acc[2], acc[3]);
+      o.z = pack_bf16(acc[4], acc[5]);
+      o.w = pack_bf16(acc[6], acc[7]);
+      for (int p = 0; p < a.world; ++p)  // local copy first (p == rank) is just another destination
+        *reinterpret_cast<uint4*>(a.hidden[(a.rank + p) % a.world] + (int64_t)(r0 + lr) * a.ld + c * 8) = o;
+    }
+  }
+  // last CTA to finish: barrier 2 (every rank's rows are out), then bump the epoch
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int64_t done = atomicAdd(reinterpret_cast<unsigned long long*>(&a.epoch_ctr[1]), 1ull);
+    if (done == gridDim.x - 1) {
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch);
+      if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, 5000000000ull)) atomicExch(a.err, 31);
+      a.epoch_ctr[1] = 0;
+      a.epoch_ctr[0] = epoch;
+      __threadfence();
+    }
+  }
+}
+
+void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const* flags, int world, int rank,
+                         int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr, int* err,
+                         int num_sms, cudaStream_t st) {
+  if (world > 8) throw std::runtime_error("tp: at most 8 ranks");
+  if (cols % 8 != 0 || ld % 8 != 0) throw std::runtime_error("tp: columns must be a multiple of 8");
+  TPArgs a{};
+  for (int i = 0; i < world; ++i) {
+    a.recv[i] = recv[i];
+    a.hidden[i] = hidden[i];
+    a.flags[i] = flags[i];
+  }
+  a.world = world;
+  a.rank = rank;
+  a.rows_per_rank = rows_per_rank;
+  a.rows_total = rows_total;
+  a.cols = cols;
+  a.ld = ld;
+  a.epoch_ctr = epoch_ctr;
+  a.err = err;
+  const int64_t work = (int64_t)rows_per_rank * (cols / 8);
+  int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms);  // all CTAs co-resident
+  if (grid < 1) grid = 1;
+  tp_reduce_ag_kernel<<<grid, 256, 0, st>>>(a);
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
+// ------------------------------------------------------- symmetric memory
+void* symm_alloc(size_t bytes) {
+  void* p = nullptr;
+  KAPSL_CHECK_CUDA(cudaMalloc(&p, bytes));
+  KAPSL_CHECK_CUDA(cudaMemset(p, 0, bytes));
+  return p;
+}
+void symm_free(void* p) {
+  if (p) cudaFree(p);
+}
+std::string symm_handle(void* p) {
+  cudaIpcMemHandle_t h;
+  KAPSL_CHECK_CUDA(cudaIpcGetMemHandle(&h, p));
+  return std::string(reinterpret_cast<const char*>(&h), sizeof(h));
+}
+void* symm_open(const std::string& handle) {
+  if (handle.size() != sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("bad IPC handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  KAPSL_CHECK_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return p;
+}
+void symm_close(void* p) {
+  if (p) cudaIpcCloseMemHandle(p);
+}
+
+}  // namespace kapsl

@@ -209,8 +209,9 @@ def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: in
     """Shard a stream of full tensors (see :func:`random_full_weights`) for one rank."""
     plan = ShardPlan.make(cfg, tp, rank)
     V, d = cfg.vocab_size, cfg.hidden_size
-    vl = (V + tp - 1) // tp
-    v0 = rank * vl
+    # embedding and lm_head are replicated on every rank: each rank computes the
+    # same logits and samples the same token, so no gather of logits is needed
+    vl, v0 = V, 0
     w = ModelWeights(embed=None, lm_head=None, final_norm=torch.ones(d, device=device, dtype=torch.bfloat16),
                      vocab_start=v0, heads_local=plan.heads_local, kv_heads_local=plan.kv_heads_local,
                      ffn_local=cfg.intermediate_size // tp if not cfg.is_moe else cfg.intermediate_size)
@@ -266,6 +267,10 @@ class CausalLM:
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=self.device)
         self.qkv_width = (self.hq + 2 * self.hkv) * self.D
 
+    def configure_tp(self, max_tokens: int) -> None:
+        if self.tp is not None and self.tp.world_size > 1:
+            self.tp.configure(max_tokens, self.cfg.hidden_size)
+
     @property
     def tp_size(self) -> int:
         return 1 if self.tp is None else self.tp.world_size
@@ -274,9 +279,9 @@ class CausalLM:
         cfg = self.cfg
         T = fb.num_tokens
         Bd = fb.num_decode
-        h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start)
-        if self.tp_size > 1:
-            self.tp.all_reduce(h)
+        tp = self.tp_size > 1
+        h = self.tp.residual_stream(T) if tp else None  # symmetric memory in fused TP mode
+        h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start, out=h)
         attn = torch.empty(T, self.hq * self.D, dtype=torch.bfloat16, device=self.device)
         x = torch.empty_like(h)
         for li, L in enumerate(self.w.layers):
@@ -291,32 +296,22 @@ class CausalLM:
             if T > Bd:
                 ops.prefill_attention(qkv, k_caches[li], v_caches[li], fb.pf_work, fb.pf_seq_info, fb.block_tables,
                                       self.hq, self.hkv, attn, self.scale)
-            if self.tp_size == 1:
+            if not tp:
                 ops.linear(attn, L.w_o, residual=h, out=h)
-                ops.rmsnorm(h, L.post_norm, cfg.rms_eps, out=x)
             else:
-                o = self.tp.row_parallel_linear(attn, L.w_o)
-                ops.rmsnorm(o, L.post_norm, cfg.rms_eps, residual=h, out=x)
+                self.tp.row_parallel_residual(attn, L.w_o, h)
+            ops.rmsnorm(h, L.post_norm, cfg.rms_eps, out=x)
             if self.moe is not None:
-                mo = self.moe.forward(x, L)
-                if self.tp_size == 1 or self.moe.output_reduced:
-                    h.add_(mo)
-                else:
-                    self.tp.all_reduce(mo)
-                    h.add_(mo)
-            elif self.tp_size == 1:
+                self.moe.forward(x, L, h)  # adds the routed experts' output into h
+            elif not tp:
                 g = ops.linear(x, L.w_gu, swiglu=True)
                 ops.linear(g, L.w_down, residual=h, out=h)
             else:
                 g = ops.linear(x, L.w_gu, swiglu=True)
-                d_out = self.tp.row_parallel_linear(g, L.w_down)
-                h.add_(d_out)
+                self.tp.row_parallel_residual(g, L.w_down, h)
         xs = h.index_select(0, fb.logits_idx)
         xs = ops.rmsnorm(xs, self.w.final_norm, cfg.rms_eps)
-        logits = ops.linear(xs, self.w.lm_head, out_dtype=torch.float32)
-        if self.tp_size > 1:
-            logits = self.tp.gather_vocab(logits, cfg.vocab_size)
-        return logits
+        return ops.linear(xs, self.w.lm_head, out_dtype=torch.float32)
 
 
 def reference_forward(cfg: ModelConfig, full_layers: list, embed: torch.Tensor, lm_head: torch.Tensor,

@@ -1,0 +1,152 @@
+"""Tensor parallelism over NVLink 5 / NVSwitch.
+
+Layout (Megatron style): QKV and gate/up are column-parallel (each rank holds
+its heads / FFN slice), o_proj and down_proj are row-parallel (each rank holds
+the matching input slice and produces a partial sum).  The embedding and
+lm_head are replicated, so every rank ends each layer with the same residual
+stream, computes the same logits and samples the same token with the same
+per-sequence RNG state: the ranks stay in lock step without gathering logits
+or broadcasting tokens.
+
+Two reduction modes for the row-parallel layers:
+
+* ``"fused"`` (default): the GEMM epilogue stores every partial row directly
+  into the receive buffer of the rank that owns the row (peer memory mapped with
+  CUDA IPC); ``tp_reduce_ag`` then sums the owned rows, adds the residual and
+  pushes the reduced rows into every peer's residual stream, with bounded
+  flag barriers before and after.  Two kernels, NVLink traffic of one
+  reduce-scatter plus one all-gather, no extra HBM pass over the partials.
+* ``"nccl"``: plain GEMM, ``torch.distributed.all_reduce`` (NCCL, NVLS when
+  NCCL picks it), residual add — the baseline.
+
+Reference counterpart: ``MeshComm`` / ``NcclComm`` (crates/kapsl-hal/src/
+device_mesh.rs:427-500, nccl_comm.rs), which stage every collective through
+host memory and are not used by any model path.
+"""
+from __future__ import annotations
+
+import os
+from typing import Optional
+
+import torch
+
+from .. import ops
+from .._ext import cuda_ops
+
+
+class TPComm:
+    def __init__(self, world_size: int, rank: int, device, mode: str = "fused", group=None,
+                 max_tokens: int = 4096, hidden: int = 4096):
+        import torch.distributed as dist
+
+        assert mode in ("fused", "nccl")
+        self.dist = dist
+        self.world_size = world_size
+        self.rank = rank
+        self.device = torch.device(device)
+        self.mode = mode
+        self.group = group
+        self.hidden = hidden
+        self.max_tokens = max_tokens
+        self.bufs = None
+        if mode == "fused" and world_size > 1:
+            self._setup_symmetric(max_tokens, hidden)
+
+    @classmethod
+    def from_world(cls, mode: Optional[str] = None, max_tokens: int = 4096, hidden: int = 4096) -> "TPComm":
+        import torch.distributed as dist
+
+        mode = mode or os.environ.get("KAPSL_TP_MODE", "fused")
+        return cls(dist.get_world_size(), dist.get_rank(), torch.device("cuda", torch.cuda.current_device()), mode,
+                   max_tokens=max_tokens, hidden=hidden)
+
+    def configure(self, max_tokens: int, hidden: int) -> None:
+        """(Re)size the symmetric buffers once the model geometry is known."""
+        if self.mode == "fused" and self.world_size > 1 and (max_tokens > self.max_tokens or hidden != self.hidden
+                                                              or self.bufs is None):
+            self.close()
+            self.max_tokens, self.hidden = max_tokens, hidden
+            self._setup_symmetric(max_tokens, hidden)
+
+    # ------------------------------------------------------- symmetric memory
+    def _setup_symmetric(self, max_tokens: int, hidden: int) -> None:
+        c = cuda_ops()
+        W = self.world_size
+        rpr = (max_tokens + W - 1) // W
+        rows_pad = rpr * W
+        recv_bytes = W * rpr * hidden * 2
+        hid_bytes = rows_pad * hidden * 2
+        flag_bytes = 2 * 8 * 8
+        align = lambda n: (n + 255) // 256 * 256
+        total = align(recv_bytes) + align(hid_bytes) + align(flag_bytes)
+        base = c.symm_alloc(total)
+        handle = c.symm_handle(base)
+        handles = [None] * W
+        self.dist.all_gather_object(handles, handle, group=self.group)
+        bases = []
+        for p in range(W):
+            bases.append(base if p == self.rank else c.symm_open(handles[p]))
+        off_h = align(recv_bytes)
+        off_f = off_h + align(hid_bytes)
+        self.bufs = {
+            "base": base, "bases": bases, "rpr": rpr, "rows_pad": rows_pad,
+            "recv": [b for b in bases], "hidden": [b + off_h for b in bases], "flags": [b + off_f for b in bases],
+        }
+        dev = self.device.index
+        self.hidden_buf = c.tensor_from_ptr(base + off_h, [rows_pad, hidden], "bfloat16", dev)
+        self.epoch = torch.zeros(2, dtype=torch.int64, device=self.device)
+        torch.cuda.synchronize(self.device)
+        self.dist.barrier(group=self.group)
+
+    def close(self) -> None:
+        if self.bufs is None:
+            return
+        c = cuda_ops()
+        torch.cuda.synchronize(self.device)
+        self.dist.barrier(group=self.group)
+        for p, b in enumerate(self.bufs["bases"]):
+            if p != self.rank:
+                c.symm_close(b)
+        c.symm_free(self.bufs["base"])
+        self.bufs = None
+
+    # -------------------------------------------------------------- helpers
+    def min_int(self, v: int) -> int:
+        t = torch.tensor([int(v)], dtype=torch.int64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MIN, group=self.group)
+        return int(t.item())
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        self.dist.all_reduce(x, group=self.group)
+        return x
+
+    def residual_stream(self, T: int) -> Optional[torch.Tensor]:
+        """The symmetric residual stream rows [T, hidden] (fused mode), else None."""
+        if self.bufs is None:
+            return None
+        if T > self.bufs["rows_pad"]:
+            raise ValueError(f"{T} tokens exceed the tensor-parallel buffers ({self.bufs['rows_pad']})")
+        return self.hidden_buf[:T]
+
+    def row_parallel_linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """NCCL baseline: partial GEMM then all-reduce."""
+        y = ops.linear(x, w)
+        self.dist.all_reduce(y, group=self.group)
+        return y
+
+    def row_parallel_residual(self, x: torch.Tensor, w: torch.Tensor, h: torch.Tensor) -> None:
+        """h += all_reduce(x @ w.T) over the TP group; h is the residual stream."""
+        T = x.shape[0]
+        if self.bufs is None:
+            y = ops.linear(x, w)
+            self.dist.all_reduce(y, group=self.group)
+            h.add_(y)
+            return
+        b = self.bufs
+        W = self.world_size
+        rpr = (T + W - 1) // W
+        c = cuda_ops()
+        err = ops.error_buffer(x.device)
+        c.gemm_scatter(x, w, b["recv"], self.rank, rpr, self.hidden, err)
+        c.tp_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden, self.epoch,
+                       err)

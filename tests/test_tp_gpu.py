@@ -1,0 +1,105 @@
+"""Tensor parallelism on 2+ GPUs (skipped with fewer): the fused NVLink
+row-parallel reduction against the NCCL baseline and against TP1, driven as
+child processes (one per GPU) over NCCL with NVLS off."""
+import json
+import os
+import subprocess
+import sys
+import textwrap
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+WORKER = textwrap.dedent(r"""
+import json, os, sys, torch
+from datetime import timedelta
+import torch.distributed as dist
+sys.path.insert(0, os.environ["KAPSL_ROOT"])
+rank = int(os.environ["RANK"]); world = int(os.environ["WORLD_SIZE"])
+torch.cuda.set_device(rank)
+dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+from kapsl_sdk_b200 import ops
+from kapsl_sdk_b200.parallel.tp import TPComm
+from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+from kapsl_sdk_b200.llm.sequence import SamplingParams
+from kapsl_sdk_b200.models.config import ModelConfig
+dev = torch.device("cuda", rank)
+out = {}
+# 1) fused row-parallel reduction vs a dense reference
+torch.manual_seed(0)
+T, K, N = 300, 1024, 512
+x_full = torch.randn(T, K * world, device=dev, dtype=torch.bfloat16)
+w_full = torch.randn(N, K * world, device=dev, dtype=torch.bfloat16) / 50
+h0 = torch.randn(T, N, device=dev, dtype=torch.bfloat16)
+ref = h0.float() + x_full.float() @ w_full.float().T
+xs, ws = x_full[:, rank * K:(rank + 1) * K].contiguous(), w_full[:, rank * K:(rank + 1) * K].contiguous()
+for mode in ("fused", "nccl"):
+    tp = TPComm(world, rank, dev, mode, max_tokens=512, hidden=N)
+    h = tp.residual_stream(T) if mode == "fused" else torch.empty_like(h0)
+    h.copy_(h0)
+    for _ in range(3):  # repeated use exercises the epoch barriers
+        h.copy_(h0)
+        tp.row_parallel_residual(xs, ws, h)
+    torch.cuda.synchronize()
+    out[mode] = float((h.float() - ref).abs().max())
+    out[mode + "_err"] = ops.check_errors(dev)
+    tp.close()
+# 2) a small model: TP=world greedy tokens vs TP=1 on rank 0
+cfg = ModelConfig(name="s", arch="qwen2", vocab_size=1024, hidden_size=512, intermediate_size=1024, num_layers=2,
+                  num_heads=8, num_kv_heads=2, head_dim=128, max_position=1024, qkv_bias=True,
+                  bos_token_id=None, eos_token_id=None)
+prompts = [[(i * 37 + j) % 1000 for j in range(n)] for i, n in enumerate((40, 130, 7))]
+tp = TPComm(world, rank, dev, "fused")
+eng = LLMEngine(cfg, device=dev, engine_cfg=EngineConfig(max_num_seqs=8, max_num_batched_tokens=128,
+                max_model_len=512, num_blocks=256), tp_comm=tp, seed=0)
+toks = eng.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
+out["tp_tokens"] = toks
+out["engine_err"] = ops.check_errors(dev)
+eng.shutdown()
+tp.close()
+if rank == 0:
+    e1 = LLMEngine(cfg, device=dev, engine_cfg=EngineConfig(max_num_seqs=8, max_num_batched_tokens=128,
+                   max_model_len=512, num_blocks=256), seed=0)
+    out["tp1_tokens"] = e1.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
+print("RESULT " + json.dumps(out), flush=True)
+dist.barrier()
+dist.destroy_process_group()
+""")
+
+
+def _run(world):
+    env = dict(os.environ, KAPSL_ROOT=ROOT, NCCL_NVLS_ENABLE="0", MASTER_ADDR="127.0.0.1", MASTER_PORT="29561",
+               WORLD_SIZE=str(world))
+    procs = []
+    for r in range(world):
+        procs.append(subprocess.Popen([sys.executable, "-c", WORKER], env=dict(env, RANK=str(r), LOCAL_RANK=str(r)),
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for p in procs:
+        try:
+            o, _ = p.communicate(timeout=600)
+        except subprocess.TimeoutExpired:
+            p.kill()
+            o, _ = p.communicate()
+        outs.append((p.returncode, o))
+    return outs
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_tensor_parallel_two_gpus():
+    outs = _run(2)
+    res = []
+    for rc, o in outs:
+        line = [l for l in o.splitlines() if l.startswith("RESULT ")]
+        assert rc == 0 and line, o[-3000:]
+        res.append(json.loads(line[0][7:]))
+    for r in res:
+        assert r["fused_err"] == 0 and r["nccl_err"] == 0 and r["engine_err"] == 0
+        assert r["fused"] < 0.5 and r["nccl"] < 0.5, r
+    assert res[0]["tp_tokens"] == res[1]["tp_tokens"]  # ranks stay in lock step
+    same = sum(a == b for x, y in zip(res[0]["tp_tokens"], res[0]["tp1_tokens"]) for a, b in zip(x, y))
+    assert same >= 0.8 * sum(len(x) for x in res[0]["tp1_tokens"]), res[0]
