@@ -52,7 +52,11 @@ def parse_args():
     p.add_argument("--max-prompt", type=int, default=2048)
     p.add_argument("--output-len", type=int, default=256)
     p.add_argument("--chunk", type=int, default=2048)
-    p.add_argument("--parallel", default="dp", choices=["dp", "tp"])
+    p.add_argument("--parallel", default="tp", choices=["dp", "tp"],
+                   help="tp: one model over all N GPUs (the named TP=N config, strong scaling); "
+                        "dp: N independent replicas, each serving its own copy of the workload")
+    p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
+                   help="row-parallel reduction: fused NVLink kernels or the NCCL baseline")
     p.add_argument("--no-graph", action="store_true")
     p.add_argument("--num-layers", type=int, default=0, help="override (testing only; invalid for the metric)")
     p.add_argument("--warmup-scale", type=float, default=1.0,
@@ -171,7 +175,7 @@ def main():
     if args.parallel == "tp" and world > 1:
         from kapsl_sdk_b200.parallel.tp import TPComm
 
-        tp_comm = TPComm.from_world()
+        tp_comm = TPComm.from_world(mode=args.tp_mode)
     ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
                         max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph)
     engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0)
@@ -257,12 +261,12 @@ def main():
     else:
         ms_max, e2e_max, tot_tokens, tot_e2e_tokens, ttft_all, tpot_all = ms, e2e_s, out_tokens, e2e_tokens, ttft, tpot
     value = tot_tokens / (ms_max / 1000.0)
-    par = (f"tp{world}" if tp_comm is not None else f"dp{world}")
+    par = (f"tp{world}" + ("" if world == 1 else f"-{args.tp_mode}")) if args.parallel == "tp" else f"dp{world}"
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
-            "higher_is_better": True, "scaling": "weak" if tp_comm is None else "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if args.parallel == "tp" else "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic token ids, random-init weights N(0,0.02) seed 0",
             "config": {"model": "Qwen2.5-7B-arch" if args.model == "qwen2.5-7b" else args.model,
                        "global_batch": args.num_requests * (world if tp_comm is None else 1),

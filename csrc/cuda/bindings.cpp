@@ -251,6 +251,26 @@ void tp_reduce_ag(std::vector<int64_t> recv, std::vector<int64_t> hidden, std::v
                              kapsl::gemm_num_sms(), cur_stream());
 }
 
+void tp_pull_reduce_ag(std::vector<int64_t> partial, std::vector<int64_t> hidden, std::vector<int64_t> flags,
+                       int64_t rank, int64_t rows_per_rank, int64_t rows_total, int64_t cols, int64_t ld,
+                       Tensor epoch_ctr, Tensor err) {
+  TORCH_CHECK(partial.size() == hidden.size() && partial.size() == flags.size(), "tp_pull_reduce_ag: tables differ");
+  CHECK_DT(epoch_ctr, at::kLong, "epoch_ctr");
+  const c10::cuda::CUDAGuard g(epoch_ctr.device());
+  auto r = as_ptrs<__nv_bfloat16>(partial);
+  auto h = as_ptrs<__nv_bfloat16>(hidden);
+  auto f = as_ptrs<int64_t>(flags);
+  kapsl::launch_tp_pull_reduce_ag(r.data(), h.data(), f.data(), (int)r.size(), (int)rank, (int)rows_per_rank,
+                                  (int)rows_total, (int)cols, ld, epoch_ctr.data_ptr<int64_t>(), err.data_ptr<int>(),
+                                  kapsl::gemm_num_sms(), cur_stream());
+}
+
+void p2p_copy(int64_t dst, int64_t src, int64_t bytes, int64_t ctas_per_sm) {
+  TORCH_CHECK(bytes % 16 == 0 && dst % 16 == 0 && src % 16 == 0, "p2p_copy: 16-byte aligned sizes and addresses");
+  kapsl::launch_p2p_copy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, (int)ctas_per_sm,
+                         cur_stream());
+}
+
 int64_t symm_alloc(int64_t bytes) { return reinterpret_cast<int64_t>(kapsl::symm_alloc((size_t)bytes)); }
 void symm_free(int64_t p) { kapsl::symm_free(reinterpret_cast<void*>(p)); }
 py::bytes symm_handle(int64_t p) { return py::bytes(kapsl::symm_handle(reinterpret_cast<void*>(p))); }
@@ -289,6 +309,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A @ B^T)");
   m.def("gemm_scatter", &gemm_scatter, "row-parallel GEMM storing rows into owner ranks' receive buffers");
   m.def("tp_reduce_ag", &tp_reduce_ag, "barrier + reduce own rows + residual + all-gather push + barrier");
+  m.def("tp_pull_reduce_ag", &tp_pull_reduce_ag, "barrier + pull peers' partial rows + residual + all-gather push");
+  m.def("p2p_copy", &p2p_copy, "16-byte vector copy between (possibly peer-mapped) device addresses");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", &symm_free);
   m.def("symm_handle", &symm_handle);

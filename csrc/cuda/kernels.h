@@ -56,6 +56,10 @@ void launch_gemm_scatter(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat1
 void launch_tp_reduce_ag(__nv_bfloat16* const* recv, __nv_bfloat16* const* hidden, int64_t* const* flags, int world,
                          int rank, int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr,
                          int* err, int num_sms, cudaStream_t st);
+void launch_tp_pull_reduce_ag(__nv_bfloat16* const* partial, __nv_bfloat16* const* hidden, int64_t* const* flags,
+                              int world, int rank, int rows_per_rank, int rows_total, int cols, int64_t ld,
+                              int64_t* epoch_ctr, int* err, int num_sms, cudaStream_t st);
+void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st);
 void* symm_alloc(size_t bytes);
 void symm_free(void* p);
 std::string symm_handle(void* p);

@@ -130,6 +130,138 @@ __global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
   }
 }
 
+// Pull variant: every rank's GEMM wrote its full partial [T, cols] into its own
+// symmetric buffer (plain epilogue, local HBM bandwidth).  After barrier 1 each
+// rank reads the partials of its own rows from all peers with P2P loads (many
+// CTAs x 2 chunks in flight per thread), adds the residual, and pushes the
+// reduced rows to every peer; barrier 2 as above.
+template <int WORLD>
+__global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
+  __shared__ int64_t epoch_sh;
+  __shared__ int ok_sh;
+  if (threadIdx.x == 0) {
+    epoch_sh = a.epoch_ctr[0] + 1;
+    ok_sh = 1;
+    if (blockIdx.x == 0) {
+      a.epoch_ctr[2] = (int64_t)globaltimer_ns();  // phase stamps for profiling
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 0 * 8 + a.rank, epoch_sh);
+    }
+    if (!wait_flags(a.flags[a.rank] + 0 * 8, a.world, epoch_sh, 5000000000ull)) {
+      ok_sh = 0;
+      atomicExch(a.err, 32);
+    }
+    if (blockIdx.x == 0) a.epoch_ctr[3] = (int64_t)globaltimer_ns();
+  }
+  __syncthreads();
+  const int64_t epoch = epoch_sh;
+  if (ok_sh) {
+    const int r0 = a.rank * a.rows_per_rank;
+    const int nrows = max(0, min(a.rows_per_rank, a.rows_total - r0));
+    const int chunks = a.cols / 8;
+    const int64_t total = (int64_t)nrows * chunks;
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    const bf16* own_hidden = a.hidden[0];
+#pragma unroll
+    for (int p = 1; p < WORLD; ++p)
+      if (p == a.rank) own_hidden = a.hidden[p];
+    for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 2 * stride) {
+      uint4 v[2][WORLD];
+      uint4 hres[2];
+      int64_t off[2];
+      bool live[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {  // issue all loads of two chunks before any use
+        const int64_t i = i0 + u * stride;
+        live[u] = i < total;
+        const int64_t idx = live[u] ? i : i0;
+        const int lr = (int)(idx / chunks), c = (int)(idx % chunks);
+        off[u] = (int64_t)(r0 + lr) * a.ld + c * 8;
+        hres[u] = *reinterpret_cast<const uint4*>(own_hidden + off[u]);
+#pragma unroll
+        for (int p = 0; p < WORLD; ++p) v[u][p] = *reinterpret_cast<const uint4*>(a.recv[p] + off[u]);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        if (!live[u]) continue;
+        float acc[8];
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&hres[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          float2 f = __bfloat1622float2(hp[j]);
+          acc[2 * j] = f.x;
+          acc[2 * j + 1] = f.y;
+        }
+#pragma unroll
+        for (int p = 0; p < WORLD; ++p) {
+          const __nv_bfloat162* vp = reinterpret_cast<const __nv_bfloat162*>(&v[u][p]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float2 f = __bfloat1622float2(vp[j]);
+            acc[2 * j] += f.x;
+            acc[2 * j + 1] += f.y;
+          }
+        }
+        uint4 o;
+        o.x = pack_bf16(acc[0], acc[1]);
+        o.y = pack_bf16(acc[2], acc[3]);
+        o.z = pack_bf16(acc[4], acc[5]);
+        o.w = pack_bf16(acc[6], acc[7]);
+#pragma unroll
+        for (int p = 0; p < WORLD; ++p) *reinterpret_cast<uint4*>(a.hidden[p] + off[u]) = o;
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int64_t done = atomicAdd(reinterpret_cast<unsigned long long*>(&a.epoch_ctr[1]), 1ull);
+    if (done == gridDim.x - 1) {
+      a.epoch_ctr[4] = (int64_t)globaltimer_ns();
+      for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch);
+      if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, 5000000000ull)) atomicExch(a.err, 33);
+      a.epoch_ctr[5] = (int64_t)globaltimer_ns();
+      a.epoch_ctr[1] = 0;
+      a.epoch_ctr[0] = epoch;
+      __threadfence();
+    }
+  }
+}
+
+void launch_tp_pull_reduce_ag(bf16* const* partial, bf16* const* hidden, int64_t* const* flags, int world, int rank,
+                              int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr, int* err,
+                              int num_sms, cudaStream_t st) {
+  if (world > 8) throw std::runtime_error("tp: at most 8 ranks");
+  if (cols % 8 != 0 || ld % 8 != 0) throw std::runtime_error("tp: columns must be a multiple of 8");
+  TPArgs a{};
+  for (int i = 0; i < world; ++i) {
+    a.recv[i] = partial[i];
+    a.hidden[i] = hidden[i];
+    a.flags[i] = flags[i];
+  }
+  a.world = world;
+  a.rank = rank;
+  a.rows_per_rank = rows_per_rank;
+  a.rows_total = rows_total;
+  a.cols = cols;
+  a.ld = ld;
+  a.epoch_ctr = epoch_ctr;
+  a.err = err;
+  const int64_t work = (int64_t)rows_per_rank * (cols / 8);
+  // at most 4 CTAs of 256 threads per SM: every CTA is resident, so the barrier cannot deadlock
+  int grid = (int)std::min<int64_t>((work + 511) / 512, (int64_t)num_sms * 4);
+  if (grid < 1) grid = 1;
+  switch (world) {
+    case 1: tp_pull_reduce_ag_kernel<1><<<grid, 256, 0, st>>>(a); break;
+    case 2: tp_pull_reduce_ag_kernel<2><<<grid, 256, 0, st>>>(a); break;
+    case 4: tp_pull_reduce_ag_kernel<4><<<grid, 256, 0, st>>>(a); break;
+    case 8: tp_pull_reduce_ag_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    default: throw std::runtime_error("tp: world size must be 1, 2, 4 or 8");
+  }
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
 void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const* flags, int world, int rank,
                          int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr, int* err,
                          int num_sms, cudaStream_t st) {
@@ -153,6 +285,32 @@ void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const*
   int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms);  // all CTAs co-resident
   if (grid < 1) grid = 1;
   tp_reduce_ag_kernel<<<grid, 256, 0, st>>>(a);
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
+// ------------------------------------------------ NVLink bandwidth probe
+// dst[i] = src[i] in 16-byte vectors, UNROLL vectors in flight per thread; with
+// one side in a peer's memory this measures SM-driven NVLink reads or writes.
+template <int UNROLL>
+__global__ void __launch_bounds__(256) p2p_copy_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
+                                                      int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride * UNROLL) {
+    uint4 v[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+      if (i + u * stride < n) v[u] = src[i + u * stride];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u)
+      if (i + u * stride < n) dst[i + u * stride] = v[u];
+  }
+}
+
+void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st) {
+  const int64_t n = bytes / 16;
+  const int grid = gemm_num_sms() * ctas_per_sm;
+  p2p_copy_kernel<4><<<grid, 256, 0, st>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

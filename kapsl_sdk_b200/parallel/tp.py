@@ -39,7 +39,7 @@ class TPComm:
                  max_tokens: int = 4096, hidden: int = 4096):
         import torch.distributed as dist
 
-        assert mode in ("fused", "nccl")
+        assert mode in ("fused", "scatter", "nccl")
         self.dist = dist
         self.world_size = world_size
         self.rank = rank
@@ -49,7 +49,7 @@ class TPComm:
         self.hidden = hidden
         self.max_tokens = max_tokens
         self.bufs = None
-        if mode == "fused" and world_size > 1:
+        if mode != "nccl" and world_size > 1:
             self._setup_symmetric(max_tokens, hidden)
 
     @classmethod
@@ -62,7 +62,7 @@ class TPComm:
 
     def configure(self, max_tokens: int, hidden: int) -> None:
         """(Re)size the symmetric buffers once the model geometry is known."""
-        if self.mode == "fused" and self.world_size > 1 and (max_tokens > self.max_tokens or hidden != self.hidden
+        if self.mode != "nccl" and self.world_size > 1 and (max_tokens > self.max_tokens or hidden != self.hidden
                                                               or self.bufs is None):
             self.close()
             self.max_tokens, self.hidden = max_tokens, hidden
@@ -94,7 +94,9 @@ class TPComm:
         }
         dev = self.device.index
         self.hidden_buf = c.tensor_from_ptr(base + off_h, [rows_pad, hidden], "bfloat16", dev)
-        self.epoch = torch.zeros(2, dtype=torch.int64, device=self.device)
+        self.partial_buf = c.tensor_from_ptr(base, [rows_pad, hidden], "bfloat16", dev)  # pull mode: own partial
+        # [0] barrier epoch, [1] finished-CTA count, [2..5] %globaltimer phase stamps of the last call
+        self.epoch = torch.zeros(8, dtype=torch.int64, device=self.device)
         torch.cuda.synchronize(self.device)
         self.dist.barrier(group=self.group)
 
@@ -147,6 +149,11 @@ class TPComm:
         rpr = (T + W - 1) // W
         c = cuda_ops()
         err = ops.error_buffer(x.device)
-        c.gemm_scatter(x, w, b["recv"], self.rank, rpr, self.hidden, err)
-        c.tp_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden, self.epoch,
-                       err)
+        if self.mode == "scatter":
+            c.gemm_scatter(x, w, b["recv"], self.rank, rpr, self.hidden, err)
+            c.tp_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden,
+                           self.epoch, err)
+        else:
+            ops.linear(x, w, out=self.partial_buf[:T])
+            c.tp_pull_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden,
+                                self.epoch, err)
