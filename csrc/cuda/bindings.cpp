@@ -278,6 +278,82 @@ int64_t symm_open(py::bytes h) { return reinterpret_cast<int64_t>(kapsl::symm_op
 void symm_close(int64_t p) { kapsl::symm_close(reinterpret_cast<void*>(p)); }
 
 // A tensor view over raw device memory (symmetric buffers); no ownership.
+void grouped_gemm(Tensor A, Tensor B, Tensor C, int64_t N, int64_t num_groups, Tensor mtiles, int64_t epi,
+                  int64_t bn, int64_t splits, c10::optional<Tensor> workspace, Tensor err) {
+  CHECK_DT(A, at::kBFloat16, "A");
+  CHECK_DT(B, at::kBFloat16, "B");
+  CHECK_DT(C, at::kBFloat16, "C");
+  CHECK_DT(mtiles, at::kInt, "mtiles");
+  TORCH_CHECK(A.dim() == 2 && A.stride(1) == 1 && B.dim() == 2 && B.stride(1) == 1 && C.dim() == 2 &&
+                  C.stride(1) == 1, "grouped_gemm: row-major 2-D operands");
+  TORCH_CHECK(B.size(0) == N * num_groups && B.size(1) == A.size(1), "grouped_gemm: B must be [groups*N, K]");
+  const int64_t rows = A.size(0);
+  TORCH_CHECK(C.size(0) >= rows && C.size(1) >= (epi == 3 ? N / 2 : N), "grouped_gemm: C too small");
+  TORCH_CHECK(mtiles.numel() >= 1 + rows / 128, "grouped_gemm: tile table too short");
+  float* ws = nullptr;
+  size_t wsb = 0;
+  if (workspace.has_value()) {
+    CHECK_DT(*workspace, at::kFloat, "workspace");
+    ws = workspace->data_ptr<float>();
+    wsb = workspace->numel() * sizeof(float);
+  }
+  const c10::cuda::CUDAGuard g(A.device());
+  kapsl::launch_grouped_gemm(bf(A), A.stride(0), bf(B), B.stride(0), bf(C), C.stride(0), (int)rows, (int)N,
+                             (int)A.size(1), (int)num_groups, mtiles.data_ptr<int>(), (int)epi, (int)bn, (int)splits,
+                             ws, wsb, err.data_ptr<int>(), cur_stream());
+}
+
+void moe_route(Tensor x, Tensor wr, int64_t K, bool renorm, Tensor ids, Tensor wts) {
+  CHECK_DT(x, at::kBFloat16, "x");
+  CHECK_DT(wr, at::kBFloat16, "w_router");
+  CHECK_DT(ids, at::kInt, "ids");
+  CHECK_DT(wts, at::kFloat, "weights");
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1 && wr.is_contiguous() && wr.size(1) == x.size(1), "moe_route: shapes");
+  const int T = (int)x.size(0);
+  TORCH_CHECK(ids.numel() >= T * K && wts.numel() >= T * K, "moe_route: outputs too small");
+  const c10::cuda::CUDAGuard g(x.device());
+  kapsl::launch_moe_route(bf(x), x.stride(0), bf(wr), T, (int)x.size(1), (int)wr.size(0), (int)K, renorm,
+                          ids.data_ptr<int32_t>(), wts.data_ptr<float>(), cur_stream());
+}
+
+void moe_permute(Tensor ids, int64_t T, int64_t K, int64_t E, int64_t e_lo, int64_t el, int64_t max_rows, Tensor seg,
+                 Tensor pos, Tensor mtiles, Tensor src, Tensor err) {
+  for (auto* t : {&ids, &seg, &pos, &mtiles, &src}) CHECK_DT(*t, at::kInt, "moe_permute int32");
+  TORCH_CHECK(ids.numel() >= T * K && pos.numel() >= T * K && seg.numel() >= E + 1, "moe_permute: sizes");
+  TORCH_CHECK(mtiles.numel() >= 1 + max_rows / 128 && src.numel() >= max_rows, "moe_permute: tables too short");
+  const c10::cuda::CUDAGuard g(ids.device());
+  kapsl::launch_moe_permute(ids.data_ptr<int32_t>(), (int)T, (int)K, (int)E, (int)e_lo, (int)el, (int)max_rows,
+                            seg.data_ptr<int32_t>(), pos.data_ptr<int32_t>(), mtiles.data_ptr<int32_t>(),
+                            src.data_ptr<int32_t>(), err.data_ptr<int>(), cur_stream());
+}
+
+void moe_gather(Tensor x, Tensor src, Tensor mtiles, Tensor xs) {
+  CHECK_DT(x, at::kBFloat16, "x");
+  CHECK_DT(xs, at::kBFloat16, "xs");
+  TORCH_CHECK(x.stride(1) == 1 && xs.stride(1) == 1 && xs.size(1) == x.size(1), "moe_gather: shapes");
+  const c10::cuda::CUDAGuard g(x.device());
+  kapsl::launch_moe_gather(bf(x), x.stride(0), src.data_ptr<int32_t>(), mtiles.data_ptr<int32_t>(), bf(xs),
+                           xs.stride(0), (int)x.size(1), (int)xs.size(0), kapsl::gemm_num_sms(), cur_stream());
+}
+
+// y / hidden / flags: per-rank device addresses (world = len(y)); flags empty when world == 1.
+void moe_combine(std::vector<int64_t> y, std::vector<int64_t> hidden, std::vector<int64_t> flags, int64_t rank,
+                 Tensor ids, Tensor wts, Tensor pos, Tensor seg, int64_t T, int64_t K, int64_t el, int64_t cols,
+                 int64_t ld_y, int64_t ld_h, int64_t rows_per_rank, c10::optional<Tensor> epoch_ctr, Tensor err) {
+  const int world = (int)y.size();
+  TORCH_CHECK(hidden.size() == y.size() && (world == 1 || flags.size() == y.size()), "moe_combine: tables differ");
+  TORCH_CHECK(world == 1 || epoch_ctr.has_value(), "moe_combine: epoch counter needed for world > 1");
+  const c10::cuda::CUDAGuard g(ids.device());
+  auto yp = as_ptrs<const __nv_bfloat16>(y);
+  auto hp = as_ptrs<__nv_bfloat16>(hidden);
+  auto fp = as_ptrs<int64_t>(flags);
+  kapsl::launch_moe_combine(yp.data(), hp.data(), world > 1 ? fp.data() : nullptr, world, (int)rank,
+                            ids.data_ptr<int32_t>(), wts.data_ptr<float>(), pos.data_ptr<int32_t>(),
+                            seg.data_ptr<int32_t>(), (int)T, (int)K, (int)el, (int)cols, ld_y, ld_h,
+                            (int)rows_per_rank, epoch_ctr.has_value() ? epoch_ctr->data_ptr<int64_t>() : nullptr,
+                            err.data_ptr<int>(), kapsl::gemm_num_sms(), cur_stream());
+}
+
 Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, std::string dtype, int64_t device) {
   at::ScalarType st;
   if (dtype == "bfloat16") st = at::kBFloat16;
@@ -309,6 +385,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A @ B^T)");
   m.def("gemm_scatter", &gemm_scatter, "row-parallel GEMM storing rows into owner ranks' receive buffers");
   m.def("tp_reduce_ag", &tp_reduce_ag, "barrier + reduce own rows + residual + all-gather push + barrier");
+  m.def("grouped_gemm", &grouped_gemm, "grouped (per-expert) tcgen05 GEMM driven by a device tile table");
+  m.def("moe_route", &moe_route, "router logits + top-k + softmax weights");
+  m.def("moe_permute", &moe_permute, "stable expert sort of the top-k assignments (padded segments)");
+  m.def("moe_gather", &moe_gather, "gather token rows into the expert-sorted buffer");
+  m.def("moe_combine", &moe_combine, "weighted top-k combine + residual (+ peer pull and all-gather)");
   m.def("tp_pull_reduce_ag", &tp_pull_reduce_ag, "barrier + pull peers' partial rows + residual + all-gather push");
   m.def("p2p_copy", &p2p_copy, "16-byte vector copy between (possibly peer-mapped) device addresses");
   m.def("symm_alloc", &symm_alloc);

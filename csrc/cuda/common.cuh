@@ -103,6 +103,27 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ---- cross-GPU flags (symmetric memory) --------------------------------------
+__device__ __forceinline__ void st_release_sys(int64_t* p, int64_t v) {
+  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+// Waits until flags_site[p] >= epoch for every p < world; false after timeout_ns.
+__device__ __forceinline__ bool wait_flags(const int64_t* flags_site, int world, int64_t epoch,
+                                           uint64_t timeout_ns) {
+  const uint64_t t0 = globaltimer_ns();
+  for (int p = 0; p < world; ++p) {
+    while (ld_acquire_sys(flags_site + p) < epoch) {
+      if (globaltimer_ns() - t0 > timeout_ns) return false;
+    }
+  }
+  return true;
+}
+
 // ---- TMA -------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

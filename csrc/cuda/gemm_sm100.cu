@@ -108,6 +108,9 @@ struct EpiArgs {
   __nv_bfloat16* peers[8];
   int rows_per_rank;
   int my_rank;
+  // Grouped (MoE) mode: [0] = number of valid 128-row M tiles, [1 + i] = the
+  // expert (row block of B, N rows each) that M tile i multiplies with.
+  const int* group_mtiles;
 };
 
 __device__ __forceinline__ __nv_bfloat16* scatter_dst(const EpiArgs& ep, int row, int col) {
@@ -167,7 +170,9 @@ __device__ __forceinline__ void load_bf16x32(const bf16* src, int nvalid, float 
 }
 
 // EPI: 0 plain, 1 bias, 2 residual, 3 swiglu (interleaved), 4 split-K partial (fp32, raw)
-template <int BN, int STAGES, int EPI, bool OUT_F32>
+// GROUPED: A rows are expert-sorted segments padded to BM; M tile i uses the B
+// rows of expert ep.group_mtiles[1 + i] (B holds the experts stacked, N rows each).
+template <int BN, int STAGES, int EPI, bool OUT_F32, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
                 int N, int K, int splits, EpiArgs ep, int* __restrict__ err) {
@@ -187,7 +192,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ int abort_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m_tiles = (M + BM - 1) / BM;
+  const int m_tiles = GROUPED ? min(*ep.group_mtiles, (M + BM - 1) / BM) : (M + BM - 1) / BM;
   const int n_tiles = (N + BN - 1) / BN;
   const int k_blocks_total = (K + BK - 1) / BK;
   const int k_per_split = (k_blocks_total + splits - 1) / splits;
@@ -231,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode_unit(u, mt, nt, sp);
         const int kb0 = sp * k_per_split;
         const int kb1 = min(k_blocks_total, kb0 + k_per_split);
+        const int brow = GROUPED ? ep.group_mtiles[1 + mt] * N + nt * BN : nt * BN;
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1)) {
             abort_sh = 1;
@@ -241,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + A_BYTES;
           mbar_arrive_expect_tx(&full_bar[stage], STAGE_BYTES);
           tma_load_2d(sa, &tmap_a, &full_bar[stage], kb * BK, mt * BM);
-          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, nt * BN);
+          tma_load_2d(sb, &tmap_b, &full_bar[stage], kb * BK, brow);
           ++issued_unwaited;
           if (++stage == STAGES) {
             stage = 0;
@@ -668,6 +674,7 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int spli
   }
   const int row = (int)(idx / N);
   const int col = (int)(idx % N);
+  if (ep.group_mtiles != nullptr && row >= *ep.group_mtiles * BM) return;  // grouped: padding M tiles
   float v[4] = {acc.x, acc.y, acc.z, acc.w};
   if (EPI == 3) {
     // interleaved gate/up: tile width 256 -> halves of 128
@@ -713,10 +720,10 @@ constexpr size_t smem_bytes() {
   return (size_t)STAGES * (BM * BK * 2 + BN * BK * 2) + 1024;
 }
 
-template <int BN, int STAGES, int EPI, bool F32>
+template <int BN, int STAGES, int EPI, bool F32, bool GROUPED = false>
 void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, int splits, const EpiArgs& ep,
                 int grid, int* err, cudaStream_t st) {
-  auto kern = gemm_kernel<BN, STAGES, EPI, F32>;
+  auto kern = gemm_kernel<BN, STAGES, EPI, F32, GROUPED>;
   constexpr size_t smem = smem_bytes<BN, STAGES>();
   static int attr_dev = -1;
   int dev;
@@ -863,6 +870,64 @@ void launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C
       case 2: splitk_reduce_kernel<2, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
       case 3: splitk_reduce_kernel<3, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
     }
+    KAPSL_LAUNCH_CHECK();
+    note_launch();
+  }
+}
+
+
+// Grouped (MoE expert) GEMM: C[rows, N] = A[rows, K] x B[g]^T per 128-row M tile,
+// where the expert g of M tile i is mtiles[1 + i] and mtiles[0] is the number of
+// valid M tiles (both written on the device by the routing kernels, so the
+// launch needs no host synchronisation).  B is [num_groups * N, K].
+// epi 0: plain bf16 store; epi 3: SwiGLU over interleaved gate/up (C is [rows, N/2]).
+void launch_grouped_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, bf16* C, int64_t ldc, int rows,
+                         int N, int K, int num_groups, const int* mtiles, int epi, int bn, int splits,
+                         float* workspace, size_t workspace_bytes, int* err, cudaStream_t st) {
+  using namespace gemm;
+  if (rows == 0 || N == 0) return;
+  if (rows % BM != 0) throw std::runtime_error("grouped gemm: rows must be a multiple of 128");
+  if (K % 8 != 0 || lda % 8 != 0 || ldb % 8 != 0 || ldc % 8 != 0)
+    throw std::runtime_error("grouped gemm: K and leading dims must be multiples of 8");
+  if (epi != 0 && epi != 3) throw std::runtime_error("grouped gemm: epilogue must be 0 (plain) or 3 (SwiGLU)");
+  if (epi == 3 && N % 256 != 0) throw std::runtime_error("grouped gemm: SwiGLU needs N % 256 == 0");
+  if (N % 128 != 0) throw std::runtime_error("grouped gemm: N must be a multiple of 128");
+  const int sms = gemm_num_sms();
+  if (bn == 0) bn = (epi == 3 || (rows / BM) * (N / 256) >= sms) ? 256 : 128;
+  if (epi == 3) bn = 256;
+  if (bn != 128 && bn != 256) throw std::runtime_error("grouped gemm: tile width must be 128 or 256");
+  const int kblocks = (K + BK - 1) / BK;
+  if (splits < 1) splits = 1;
+  if (splits > kblocks) splits = kblocks;
+  if (splits > 1 && (workspace == nullptr || (size_t)splits * rows * N * sizeof(float) > workspace_bytes))
+    throw std::runtime_error("grouped gemm: split-K needs a larger workspace");
+  CUtensorMap ta = make_tmap_2d_bf16(A, rows, K, lda, BM, BK);
+  CUtensorMap tb = make_tmap_2d_bf16(B, (uint64_t)num_groups * N, K, ldb, bn, BK);
+  EpiArgs ep{C, ldc, nullptr, nullptr, 0, workspace};
+  ep.group_mtiles = mtiles;
+  const int units = (rows / BM) * (N / bn) * splits;  // upper bound; the kernel reads the valid count
+  const int grid = std::min(units, sms);
+  const int kepi = splits > 1 ? 4 : epi;
+  if (bn == 256) {
+    switch (kepi) {
+      case 0: launch_cfg<256, 4, 0, false, true>(ta, tb, rows, N, K, splits, ep, grid, err, st); break;
+      case 3: launch_cfg<256, 4, 3, false, true>(ta, tb, rows, N, K, splits, ep, grid, err, st); break;
+      case 4: launch_cfg<256, 4, 4, true, true>(ta, tb, rows, N, K, splits, ep, grid, err, st); break;
+    }
+  } else {
+    switch (kepi) {
+      case 0: launch_cfg<128, 6, 0, false, true>(ta, tb, rows, N, K, splits, ep, grid, err, st); break;
+      case 4: launch_cfg<128, 6, 4, true, true>(ta, tb, rows, N, K, splits, ep, grid, err, st); break;
+      default: throw std::runtime_error("grouped gemm: bad epilogue");
+    }
+  }
+  if (splits > 1) {
+    const int64_t total = (int64_t)rows * N / 4;
+    const int blocks = (int)((total + 255) / 256);
+    if (epi == 3)
+      splitk_reduce_kernel<3, false><<<blocks, 256, 0, st>>>(workspace, splits, rows, N, ep);
+    else
+      splitk_reduce_kernel<0, false><<<blocks, 256, 0, st>>>(workspace, splits, rows, N, ep);
     KAPSL_LAUNCH_CHECK();
     note_launch();
   }

@@ -49,6 +49,23 @@ void launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, in
                  int64_t ldr, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st, int force_bn,
                  int force_splits);
 
+// grouped (MoE expert) GEMM; mtiles = [valid 128-row tiles, expert of tile 0, ...] on the device
+void launch_grouped_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, __nv_bfloat16* C,
+                         int64_t ldc, int rows, int N, int K, int num_groups, const int* mtiles, int epi, int bn,
+                         int splits, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st);
+
+// mixture of experts (moe.cu)
+void launch_moe_route(const __nv_bfloat16* x, int64_t x_stride, const __nv_bfloat16* wr, int T, int d, int E, int K,
+                      bool renorm, int32_t* ids, float* wts, cudaStream_t st);
+void launch_moe_permute(const int32_t* ids, int T, int K, int E, int e_lo, int el, int max_rows, int32_t* seg,
+                        int32_t* pos, int32_t* mtiles, int32_t* src, int* err, cudaStream_t st);
+void launch_moe_gather(const __nv_bfloat16* x, int64_t x_stride, const int32_t* src, const int32_t* mtiles,
+                       __nv_bfloat16* xs, int64_t xs_stride, int d, int max_rows, int num_sms, cudaStream_t st);
+void launch_moe_combine(const __nv_bfloat16* const* y, __nv_bfloat16* const* hidden, int64_t* const* flags, int world,
+                        int rank, const int32_t* ids, const float* wts, const int32_t* pos, const int32_t* seg, int T,
+                        int K, int el, int cols, int64_t ld_y, int64_t ld_h, int rows_per_rank, int64_t* epoch_ctr,
+                        int* err, int num_sms, cudaStream_t st);
+
 // tensor parallel over NVLink peer memory (tp_comm.cu / gemm_sm100.cu)
 void launch_gemm_scatter(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb,
                          __nv_bfloat16* const* peers, int world, int my_rank, int rows_per_rank, int64_t ld_recv,

@@ -25,15 +25,6 @@ namespace kapsl {
 
 using bf16 = __nv_bfloat16;
 
-__device__ __forceinline__ void st_release_sys(int64_t* p, int64_t v) {
-  asm volatile("st.release.sys.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-__device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
-  int64_t v;
-  asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // flags layout per rank: [2 sites][8 peers] int64, then [2] epoch/done counters
 struct TPArgs {
   bf16* recv[8];       // peer receive buffers: [world][rows_per_rank][ld] bf16 partials
@@ -48,16 +39,6 @@ struct TPArgs {
   int64_t* epoch_ctr;  // local: [0] epoch, [1] finished-CTA counter
   int* err;
 };
-
-__device__ bool wait_flags(const int64_t* flags_site, int world, int64_t epoch, uint64_t timeout_ns) {
-  const uint64_t t0 = globaltimer_ns();
-  for (int p = 0; p < world; ++p) {
-    while (ld_acquire_sys(flags_site + p) < epoch) {
-      if (globaltimer_ns() - t0 > timeout_ns) return false;
-    }
-  }
-  return true;
-}
 
 __global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
   __shared__ int64_t epoch_sh;

@@ -76,6 +76,10 @@ class LLMEngine:
             tp = 1 if tp_comm is None else tp_comm.world_size
             rank = 0 if tp_comm is None else tp_comm.rank
             weights = random_weights(cfg, self.device, tp=tp, rank=rank, seed=seed)
+        if moe is None and cfg.is_moe:
+            from ..models.moe import MoE
+
+            moe = MoE(cfg, self.device, tp_comm)
         self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe)
         self.model.configure_tp(e.max_num_batched_tokens + e.max_num_seqs)
         layout = KVLayout(cfg.num_layers, self.model.hkv, cfg.head_dim, e.block_size)

@@ -270,6 +270,8 @@ class CausalLM:
     def configure_tp(self, max_tokens: int) -> None:
         if self.tp is not None and self.tp.world_size > 1:
             self.tp.configure(max_tokens, self.cfg.hidden_size)
+        if self.moe is not None:
+            self.moe.configure(max_tokens)
 
     @property
     def tp_size(self) -> int:

@@ -185,3 +185,49 @@ def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor,
 
 def count_tokens(counts: torch.Tensor, rows: torch.Tensor, ids: torch.Tensor) -> None:
     cuda_ops().count_tokens(counts, rows, ids)
+
+
+# ------------------------------------------------------------ mixture of experts
+def moe_route(x: torch.Tensor, w_router: torch.Tensor, top_k: int, renormalize: bool = True,
+              ids: Optional[torch.Tensor] = None, weights: Optional[torch.Tensor] = None):
+    """Router logits ``x @ w_router.T`` -> (expert ids int32 [T, k], weights fp32 [T, k])."""
+    T = x.shape[0]
+    if ids is None:
+        ids = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    if weights is None:
+        weights = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    cuda_ops().moe_route(x, w_router, top_k, renormalize, ids, weights)
+    return ids, weights
+
+
+def moe_permute(ids: torch.Tensor, num_experts: int, e_lo: int, e_local: int, max_rows: int, seg: torch.Tensor,
+                pos: torch.Tensor, mtiles: torch.Tensor, src: torch.Tensor) -> None:
+    """Stable expert sort of the [T, k] assignments (segments padded to 128 rows)."""
+    T, k = ids.shape
+    cuda_ops().moe_permute(ids, T, k, num_experts, e_lo, e_local, max_rows, seg, pos, mtiles, src,
+                           error_buffer(ids.device))
+
+
+def moe_gather(x: torch.Tensor, src: torch.Tensor, mtiles: torch.Tensor, xs: torch.Tensor) -> None:
+    cuda_ops().moe_gather(x, src, mtiles, xs)
+
+
+def grouped_linear(xs: torch.Tensor, w: torch.Tensor, n_per_group: int, mtiles: torch.Tensor,
+                   out: torch.Tensor, swiglu: bool = False, splits: int = 1, bn: int = 0,
+                   workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Per-expert GEMM over expert-sorted rows: tile i of ``xs`` times expert
+    ``mtiles[1 + i]`` of ``w`` ([groups * n_per_group, K])."""
+    groups = w.shape[0] // n_per_group
+    if splits > 1 and workspace is None:
+        workspace = _workspace(xs.device, splits * xs.shape[0] * n_per_group * 4)
+    cuda_ops().grouped_gemm(xs, w, out, n_per_group, groups, mtiles, 3 if swiglu else 0, bn, splits, workspace,
+                            error_buffer(xs.device))
+    return out
+
+
+def moe_combine(y_ptrs: list[int], hidden_ptrs: list[int], flag_ptrs: list[int], rank: int, ids: torch.Tensor,
+                weights: torch.Tensor, pos: torch.Tensor, seg: torch.Tensor, e_local: int, cols: int, ld_y: int,
+                ld_h: int, rows_per_rank: int, epoch: Optional[torch.Tensor] = None) -> None:
+    T, k = ids.shape
+    cuda_ops().moe_combine(y_ptrs, hidden_ptrs, flag_ptrs, rank, ids, weights, pos, seg, T, k, e_local, cols, ld_y,
+                           ld_h, rows_per_rank, epoch, error_buffer(ids.device))

@@ -10,12 +10,16 @@ or broadcasting tokens.
 
 Two reduction modes for the row-parallel layers:
 
-* ``"fused"`` (default): the GEMM epilogue stores every partial row directly
-  into the receive buffer of the rank that owns the row (peer memory mapped with
-  CUDA IPC); ``tp_reduce_ag`` then sums the owned rows, adds the residual and
-  pushes the reduced rows into every peer's residual stream, with bounded
-  flag barriers before and after.  Two kernels, NVLink traffic of one
-  reduce-scatter plus one all-gather, no extra HBM pass over the partials.
+* ``"fused"`` (default): each rank's GEMM writes its partial sums into its own
+  symmetric buffer (memory every peer maps with CUDA IPC); ``tp_pull_reduce_ag``
+  then, after a bounded flag barrier, loads the rows this rank owns from every
+  peer's partial buffer over NVLink, adds them and the residual, and stores the
+  reduced rows into every rank's residual stream (the all-gather), followed by
+  a second barrier.  NVLink traffic of one reduce-scatter plus one all-gather.
+* ``"scatter"``: the GEMM epilogue itself stores every partial row into the
+  receive slot of the rank that owns it (``gemm_scatter``), and
+  ``tp_reduce_ag`` sums the slots locally — the push variant of the same
+  reduction.
 * ``"nccl"``: plain GEMM, ``torch.distributed.all_reduce`` (NCCL, NVLS when
   NCCL picks it), residual add — the baseline.
 
@@ -36,7 +40,7 @@ from .._ext import cuda_ops
 
 class TPComm:
     def __init__(self, world_size: int, rank: int, device, mode: str = "fused", group=None,
-                 max_tokens: int = 4096, hidden: int = 4096):
+                 max_tokens: int = 4096, hidden: int = 4096, ep_rows: int = 0):
         import torch.distributed as dist
 
         assert mode in ("fused", "scatter", "nccl")
@@ -48,7 +52,9 @@ class TPComm:
         self.group = group
         self.hidden = hidden
         self.max_tokens = max_tokens
+        self.ep_rows = ep_rows
         self.bufs = None
+        self.ep_buf = None
         if mode != "nccl" and world_size > 1:
             self._setup_symmetric(max_tokens, hidden)
 
@@ -60,12 +66,14 @@ class TPComm:
         return cls(dist.get_world_size(), dist.get_rank(), torch.device("cuda", torch.cuda.current_device()), mode,
                    max_tokens=max_tokens, hidden=hidden)
 
-    def configure(self, max_tokens: int, hidden: int) -> None:
-        """(Re)size the symmetric buffers once the model geometry is known."""
+    def configure(self, max_tokens: int, hidden: int, ep_rows: int = 0) -> None:
+        """(Re)size the symmetric buffers once the model geometry is known.
+        ``ep_rows``: rows of the expert-output buffer that peers read in the
+        fused MoE combine (0 for dense models)."""
         if self.mode != "nccl" and self.world_size > 1 and (max_tokens > self.max_tokens or hidden != self.hidden
-                                                              or self.bufs is None):
+                                                              or ep_rows > self.ep_rows or self.bufs is None):
             self.close()
-            self.max_tokens, self.hidden = max_tokens, hidden
+            self.max_tokens, self.hidden, self.ep_rows = max_tokens, hidden, max(ep_rows, self.ep_rows)
             self._setup_symmetric(max_tokens, hidden)
 
     # ------------------------------------------------------- symmetric memory
@@ -77,8 +85,9 @@ class TPComm:
         recv_bytes = W * rpr * hidden * 2
         hid_bytes = rows_pad * hidden * 2
         flag_bytes = 2 * 8 * 8
+        ep_bytes = self.ep_rows * hidden * 2
         align = lambda n: (n + 255) // 256 * 256
-        total = align(recv_bytes) + align(hid_bytes) + align(flag_bytes)
+        total = align(recv_bytes) + align(hid_bytes) + align(flag_bytes) + align(ep_bytes)
         base = c.symm_alloc(total)
         handle = c.symm_handle(base)
         handles = [None] * W
@@ -88,11 +97,15 @@ class TPComm:
             bases.append(base if p == self.rank else c.symm_open(handles[p]))
         off_h = align(recv_bytes)
         off_f = off_h + align(hid_bytes)
+        off_e = off_f + align(flag_bytes)
         self.bufs = {
             "base": base, "bases": bases, "rpr": rpr, "rows_pad": rows_pad,
             "recv": [b for b in bases], "hidden": [b + off_h for b in bases], "flags": [b + off_f for b in bases],
+            "ep": [b + off_e for b in bases],
         }
         dev = self.device.index
+        self.ep_buf = (c.tensor_from_ptr(base + off_e, [self.ep_rows, hidden], "bfloat16", dev)
+                       if self.ep_rows else None)
         self.hidden_buf = c.tensor_from_ptr(base + off_h, [rows_pad, hidden], "bfloat16", dev)
         self.partial_buf = c.tensor_from_ptr(base, [rows_pad, hidden], "bfloat16", dev)  # pull mode: own partial
         # [0] barrier epoch, [1] finished-CTA count, [2..5] %globaltimer phase stamps of the last call
