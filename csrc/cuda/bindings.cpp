@@ -303,6 +303,52 @@ void grouped_gemm(Tensor A, Tensor B, Tensor C, int64_t N, int64_t num_groups, T
                              ws, wsb, err.data_ptr<int>(), cur_stream());
 }
 
+// Y[M, N] = X[M, K] . dequant(Wq[N, K/256 * 144 bytes])^T (+ residual)
+void gemm_q4k(Tensor X, Tensor Wq, Tensor Y, int64_t K, c10::optional<Tensor> res, c10::optional<Tensor> workspace,
+              int64_t force_splits, Tensor err) {
+  CHECK_DT(X, at::kBFloat16, "X");
+  CHECK_DT(Y, at::kBFloat16, "Y");
+  TORCH_CHECK(Wq.scalar_type() == at::kByte && Wq.dim() == 2 && Wq.is_contiguous(), "gemm_q4k: Wq uint8 [N, bytes]");
+  TORCH_CHECK(X.dim() == 2 && X.stride(1) == 1 && X.size(1) == K && Y.dim() == 2 && Y.stride(1) == 1,
+              "gemm_q4k: X [M, K], Y [M, N] row-major");
+  const int64_t M = X.size(0), N = Wq.size(0);
+  TORCH_CHECK(Y.size(0) >= M && Y.size(1) >= N, "gemm_q4k: Y too small");
+  const __nv_bfloat16* rp = nullptr;
+  int64_t ldr = 0;
+  if (res.has_value()) {
+    CHECK_DT(*res, at::kBFloat16, "res");
+    TORCH_CHECK(res->stride(1) == 1 && res->size(0) >= M && res->size(1) >= N, "gemm_q4k: residual shape");
+    rp = bf(*res);
+    ldr = res->stride(0);
+  }
+  float* ws = nullptr;
+  size_t wsb = 0;
+  if (workspace.has_value()) {
+    CHECK_DT(*workspace, at::kFloat, "workspace");
+    ws = workspace->data_ptr<float>();
+    wsb = workspace->numel() * sizeof(float);
+  }
+  const c10::cuda::CUDAGuard g(X.device());
+  kapsl::launch_gemm_q4k(bf(X), X.stride(0), Wq.data_ptr<uint8_t>(), Wq.size(1), bf(Y), Y.stride(0), (int)M, (int)N,
+                         (int)K, rp, ldr, ws, wsb, (int)force_splits, err.data_ptr<int>(), cur_stream());
+}
+
+void q4k_quantize(Tensor x, Tensor out) {
+  CHECK_DT(x, at::kBFloat16, "x");
+  TORCH_CHECK(x.is_contiguous() && out.is_contiguous() && out.scalar_type() == at::kByte, "q4k_quantize: layout");
+  TORCH_CHECK(out.numel() * 256 == x.numel() * 144, "q4k_quantize: output must hold numel/256 * 144 bytes");
+  const c10::cuda::CUDAGuard g(x.device());
+  kapsl::launch_q4k_quantize(bf(x), x.numel(), out.data_ptr<uint8_t>(), cur_stream());
+}
+
+void q4k_dequant(Tensor raw, Tensor out) {
+  CHECK_DT(out, at::kBFloat16, "out");
+  TORCH_CHECK(raw.is_contiguous() && out.is_contiguous() && raw.scalar_type() == at::kByte, "q4k_dequant: layout");
+  TORCH_CHECK(raw.numel() * 256 == out.numel() * 144, "q4k_dequant: sizes");
+  const c10::cuda::CUDAGuard g(raw.device());
+  kapsl::launch_q4k_dequant(raw.data_ptr<uint8_t>(), out.numel(), bf(out), cur_stream());
+}
+
 void moe_route(Tensor x, Tensor wr, int64_t K, bool renorm, Tensor ids, Tensor wts) {
   CHECK_DT(x, at::kBFloat16, "x");
   CHECK_DT(wr, at::kBFloat16, "w_router");
@@ -385,6 +431,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A @ B^T)");
   m.def("gemm_scatter", &gemm_scatter, "row-parallel GEMM storing rows into owner ranks' receive buffers");
   m.def("tp_reduce_ag", &tp_reduce_ag, "barrier + reduce own rows + residual + all-gather push + barrier");
+  m.def("gemm_q4k", &gemm_q4k, "GEMM with GGUF Q4_K weights dequantized into TMEM inside the mainloop");
+  m.def("q4k_quantize", &q4k_quantize, "bf16 -> GGUF Q4_K blocks");
+  m.def("q4k_dequant", &q4k_dequant, "GGUF Q4_K blocks -> bf16");
   m.def("grouped_gemm", &grouped_gemm, "grouped (per-expert) tcgen05 GEMM driven by a device tile table");
   m.def("moe_route", &moe_route, "router logits + top-k + softmax weights");
   m.def("moe_permute", &moe_permute, "stable expert sort of the top-k assignments (padded segments)");

@@ -36,12 +36,20 @@ void note_launch(uint64_t n = 1);
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols,
                               uint64_t pitch_elems, uint32_t box_rows,
                               uint32_t box_cols, bool swizzle128 = true);
+// 2-D uint8 tensor map without swizzle: rows x cols_bytes, row pitch in bytes.
+CUtensorMap make_tmap_2d_u8(const void* base, uint64_t rows, uint64_t cols_bytes, uint64_t pitch_bytes,
+                            uint32_t box_rows, uint32_t box_cols);
 
 // --------------------------------------------------------------- device side
 #ifdef __CUDACC__
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_min(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fminf(v, __shfl_xor_sync(0xffffffffu, v, o));
   return v;
 }
 __device__ __forceinline__ float warp_max(float v) {

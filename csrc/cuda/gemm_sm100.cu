@@ -21,6 +21,7 @@
 // HBM); EPI 5 stores rows into peer GPUs' receive buffers (tensor parallel).
 #include "common.cuh"
 #include "kernels.h"
+#include "tcgen05.cuh"
 
 namespace kapsl {
 
@@ -32,66 +33,11 @@ constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
 
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
-  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst_smem)),
-               "r"(ncols)
-               : "memory");
-  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-}
-__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
-  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
-}
-
-// K-major, 128-byte swizzled operand tile: rows of 128 B, 8-row atoms of 1 KiB.
-__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFF);   // start address
-  d |= (uint64_t)1 << 16;                   // leading byte offset (unused for SW128 K-major)
-  d |= (uint64_t)(1024 >> 4) << 32;         // stride byte offset: 8 rows * 128 B
-  d |= (uint64_t)1 << 46;                   // descriptor version (sm100)
-  d |= (uint64_t)2 << 61;                   // layout: SWIZZLE_128B
-  return d;
-}
+using namespace tc;
 
 template <int BN>
 __host__ __device__ constexpr uint32_t instr_desc_bf16() {
-  return (1u << 4)                     // D format f32
-         | (1u << 7)                   // A format bf16
-         | (1u << 10)                  // B format bf16
-         | ((uint32_t)(BN >> 3) << 17)  // N
-         | ((uint32_t)(BM >> 4) << 24); // M
-}
-
-__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void mma_commit(uint64_t* bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
-               : "memory");
-}
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-  uint32_t r[32];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
-      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+  return idesc_bf16<BM, BN>();
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); }
@@ -815,26 +761,36 @@ void launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C
       return;
     }
   }
+  const int m_tiles = (M + BM - 1) / BM;
+  const int kblocks = (K + BK - 1) / BK;
+  // Small-M GEMMs stream the weights: every SM must take part, but no unit may
+  // spill into a second wave, so splits = floor(SMs / tiles).
+  auto split_for = [&](int tiles) {
+    if (tiles >= sms / 2 || kblocks < 8) return 1;
+    int s = std::min(std::min(kblocks / 4, 16), sms / tiles);
+    if (s < 1) s = 1;
+    if (s > 1 && (size_t)s * M * N * sizeof(float) > workspace_bytes) s = 1;
+    return s;
+  };
   int bn = force_bn ? force_bn : 256;
-  if (!force_bn && epi != 3) {
-    // Narrow tiles when the wide grid would leave most SMs idle.
-    const int mt = (M + BM - 1) / BM;
-    const int t256 = mt * ((N + 255) / 256);
-    if (t256 < sms && N % 128 == 0) bn = 128;
+  if (!force_bn && epi != 3 && N % 128 == 0) {
+    // Narrow tiles when they keep more SMs streaming (ties go to the narrow tile,
+    // whose 6-stage ring keeps more bytes in flight per SM).
+    const int t256 = m_tiles * ((N + 255) / 256), t128 = m_tiles * (N / 128);
+    if (t256 < sms) {
+      const int u256 = t256 * split_for(t256), u128 = t128 * split_for(t128);
+      auto eff = [&](int u) { return (double)u / (double)(((u + sms - 1) / sms) * sms); };
+      bn = eff(u128) >= eff(u256) ? 128 : 256;
+    }
   }
   if (epi == 3) bn = 256;
-  const int m_tiles = (M + BM - 1) / BM;
   const int n_tiles = (N + bn - 1) / bn;
-  const int kblocks = (K + BK - 1) / BK;
-  int splits = 1;
-  if (force_splits > 0) {
-    splits = force_splits;
-  } else if (m_tiles * n_tiles < sms / 2 && kblocks >= 8) {
-    splits = std::min(std::min(kblocks / 4, 8), (sms + m_tiles * n_tiles - 1) / (m_tiles * n_tiles));
-    if (splits < 1) splits = 1;
-    if (splits > 1 && (size_t)splits * M * N * sizeof(float) > workspace_bytes) splits = 1;
-  }
+  int splits = force_splits > 0 ? force_splits : split_for(m_tiles * n_tiles);
   if (splits > kblocks) splits = kblocks;
+  if (splits > 1) {  // no empty split: every split gets ceil(kblocks / splits) blocks but the last
+    const int kps = (kblocks + splits - 1) / splits;
+    splits = (kblocks + kps - 1) / kps;
+  }
   if (splits > 1 && (workspace == nullptr || (size_t)splits * M * N * sizeof(float) > workspace_bytes))
     throw std::runtime_error("gemm: split-K needs a larger workspace");
   if (splits > 1 && N % 4 != 0) throw std::runtime_error("gemm: split-K needs N % 4 == 0");
@@ -899,6 +855,10 @@ void launch_grouped_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb,
   const int kblocks = (K + BK - 1) / BK;
   if (splits < 1) splits = 1;
   if (splits > kblocks) splits = kblocks;
+  if (splits > 1) {  // no empty split: every split gets ceil(kblocks / splits) blocks but the last
+    const int kps = (kblocks + splits - 1) / splits;
+    splits = (kblocks + kps - 1) / kps;
+  }
   if (splits > 1 && (workspace == nullptr || (size_t)splits * rows * N * sizeof(float) > workspace_bytes))
     throw std::runtime_error("grouped gemm: split-K needs a larger workspace");
   CUtensorMap ta = make_tmap_2d_bf16(A, rows, K, lda, BM, BK);

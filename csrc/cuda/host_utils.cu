@@ -50,4 +50,22 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols, ui
   return m;
 }
 
+// 2-D byte tensor map without swizzle (packed quantized blocks).
+CUtensorMap make_tmap_2d_u8(const void* base, uint64_t rows, uint64_t cols_bytes, uint64_t pitch_bytes,
+                            uint32_t box_rows, uint32_t box_cols) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base address must be 16-byte aligned");
+  if (pitch_bytes % 16 != 0) throw std::runtime_error("TMA row pitch must be a multiple of 16 bytes");
+  if (box_cols % 16 != 0 || box_cols > 256 || box_rows > 256) throw std::runtime_error("TMA byte box out of range");
+  CUtensorMap m;
+  cuuint64_t dims[2] = {cols_bytes, rows};
+  cuuint64_t strides[1] = {pitch_bytes};
+  cuuint32_t box[2] = {box_cols, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (u8) failed: " + std::to_string((int)r));
+  return m;
+}
+
 }  // namespace kapsl

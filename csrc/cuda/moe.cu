@@ -22,22 +22,46 @@ namespace kapsl {
 using bf16 = __nv_bfloat16;
 
 // ------------------------------------------------------------------ routing
-// One warp per token: logits = x . Wr^T (fp32), top-k (ties -> lower expert id),
-// weights = softmax over all experts at the chosen ids, renormalised over the
-// k chosen ones when `renorm` (Mixtral).  E <= 64.
-__global__ void __launch_bounds__(256) moe_route_kernel(const bf16* __restrict__ x, int64_t x_stride,
-                                                        const bf16* __restrict__ wr, int T, int d, int E, int K,
-                                                        int renorm, int32_t* __restrict__ ids,
-                                                        float* __restrict__ wts) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
-  const bf16* xr = x + (int64_t)warp * x_stride;
-  float lg[2] = {-INFINITY, -INFINITY};  // lane owns experts lane and lane + 32
-  for (int e = 0; e < E; ++e) {
+// One CTA per token: warp w computes the logits of experts w, w + 8, ... (fp32
+// dot products over d, four independent 16-byte loads in flight per lane);
+// warp 0 then takes the top-k (ties -> lower expert id) and the softmax
+// weights over all experts at the chosen ids, renormalised over the k chosen
+// ones when `renorm` (Mixtral).  E <= 64.
+constexpr int kRouteWarps = 8;
+
+__global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const bf16* __restrict__ x, int64_t x_stride,
+                                                                     const bf16* __restrict__ wr, int T, int d, int E,
+                                                                     int K, int renorm, int32_t* __restrict__ ids,
+                                                                     float* __restrict__ wts) {
+  __shared__ float logit_sh[64];
+  const int t = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bf16* xr = x + (int64_t)t * x_stride;
+  for (int e = warp; e < E; e += kRouteWarps) {
     const bf16* w = wr + (int64_t)e * d;
     float acc = 0.f;
-    for (int c = lane * 8; c < d; c += 256) {
+    int c = lane * 8;
+    for (; c + 3 * 256 < d; c += 4 * 256) {
+      uint4 xv[4], wv[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        xv[u] = *reinterpret_cast<const uint4*>(xr + c + u * 256);
+        wv[u] = *reinterpret_cast<const uint4*>(w + c + u * 256);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv[u]);
+        const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv[u]);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 a = __bfloat1622float2(xp[j]);
+          const float2 b = __bfloat1622float2(wp[j]);
+          acc = fmaf(a.x, b.x, acc);
+          acc = fmaf(a.y, b.y, acc);
+        }
+      }
+    }
+    for (; c < d; c += 256) {
       const uint4 xv = *reinterpret_cast<const uint4*>(xr + c);
       const uint4 wv = *reinterpret_cast<const uint4*>(w + c);
       const __nv_bfloat162* xp = reinterpret_cast<const __nv_bfloat162*>(&xv);
@@ -51,24 +75,26 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const bf16* __restrict__
       }
     }
     acc = warp_sum(acc);
-    if ((e & 31) == lane) lg[e >> 5] = acc;
+    if (lane == 0) logit_sh[e] = acc;
   }
-  // softmax denominator over all experts
+  __syncthreads();
+  if (warp != 0) return;
+  float lg[2];
+  lg[0] = lane < E ? logit_sh[lane] : -INFINITY;  // lane owns experts lane and lane + 32
+  lg[1] = lane + 32 < E ? logit_sh[lane + 32] : -INFINITY;
   const float mx = warp_max(fmaxf(lg[0], lg[1]));
   float se = 0.f;
   if (lane < E) se += __expf(lg[0] - mx);
   if (lane + 32 < E) se += __expf(lg[1] - mx);
   se = warp_sum(se);
   float sel_sum = 0.f;
-  float chosen_p[8];
-  int chosen_e[8];
-  float cur[2] = {lane < E ? lg[0] : -INFINITY, lane + 32 < E ? lg[1] : -INFINITY};
+  float my_p = 0.f;
+  int my_e = 0;
   for (int k = 0; k < K; ++k) {
-    // warp arg-max, lower expert id on ties
-    float bv = cur[0];
+    float bv = lg[0];
     int be = lane;
-    if (cur[1] > bv) {
-      bv = cur[1];
+    if (lg[1] > bv) {
+      bv = lg[1];
       be = lane + 32;
     }
 #pragma unroll
@@ -81,16 +107,16 @@ __global__ void __launch_bounds__(256) moe_route_kernel(const bf16* __restrict__
       }
     }
     const float p = __expf(bv - mx) / se;
-    chosen_p[k] = p;
-    chosen_e[k] = be;
-    sel_sum += p;
-    if ((be & 31) == lane) cur[be >> 5] = -INFINITY;
-  }
-  if (lane == 0) {
-    for (int k = 0; k < K; ++k) {
-      ids[(int64_t)warp * K + k] = chosen_e[k];
-      wts[(int64_t)warp * K + k] = renorm ? chosen_p[k] / sel_sum : chosen_p[k];
+    if (lane == k) {
+      my_p = p;
+      my_e = be;
     }
+    sel_sum += p;
+    if ((be & 31) == lane) lg[be >> 5] = -INFINITY;
+  }
+  if (lane < K) {
+    ids[(int64_t)t * K + lane] = my_e;
+    wts[(int64_t)t * K + lane] = renorm ? my_p / sel_sum : my_p;
   }
 }
 
@@ -300,8 +326,7 @@ void launch_moe_route(const bf16* x, int64_t x_stride, const bf16* wr, int T, in
   if (T == 0) return;
   if (E > kMaxExperts || K > 8 || K > E) throw std::runtime_error("moe_route: need E <= 64 and K <= min(8, E)");
   if (d % 8 != 0 || x_stride % 8 != 0) throw std::runtime_error("moe_route: d and stride must be multiples of 8");
-  const int blocks = (T * 32 + 255) / 256;
-  moe_route_kernel<<<blocks, 256, 0, st>>>(x, x_stride, wr, T, d, E, K, renorm ? 1 : 0, ids, wts);
+  moe_route_kernel<<<T, kRouteWarps * 32, 0, st>>>(x, x_stride, wr, T, d, E, K, renorm ? 1 : 0, ids, wts);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

@@ -31,6 +31,7 @@ class ModelConfig:
     max_position: int = 32768
     num_experts: int = 0
     experts_per_token: int = 0
+    weight_format: str = "bf16"  # bf16 | q4_k (GGUF k-quant linear layers, dequantized in the GEMM)
     bos_token_id: Optional[int] = 1
     eos_token_id: Optional[int] = 2
     extra: dict = field(default_factory=dict)
@@ -143,10 +144,19 @@ def mixtral_8x7b() -> ModelConfig:
                        rope_theta=1e6, rms_eps=1e-5, max_position=32768, num_experts=8, experts_per_token=2)
 
 
+def llama3_70b_q4k() -> ModelConfig:
+    """Llama-3-70B with GGUF Q4_K linear layers (embedding / lm_head kept bf16)."""
+    cfg = llama3_70b()
+    cfg.name = "llama-3-70b-q4k"
+    cfg.weight_format = "q4_k"
+    return cfg
+
+
 PRESETS = {
     "tiny-llama": tiny_llama,
     "qwen2.5-7b": qwen2_5_7b,
     "llama-3-70b": llama3_70b,
+    "llama-3-70b-q4k": llama3_70b_q4k,
     "llama-3-8b": llama3_8b,
     "mixtral-8x7b": mixtral_8x7b,
 }

@@ -156,8 +156,21 @@ def shard_layer(cfg: ModelConfig, plan: ShardPlan, full: dict, device, dtype=tor
     else:
         gate = _shard_rows(full["gate"], r, tp)
         up = _shard_rows(full["up"], r, tp)
-        lw.w_gu = ops.interleave_gate_up(gate, up).to(device, dtype).contiguous()
+        if cfg.weight_format == "q4_k":
+            lw.w_gu = torch.cat([gate, up], 0).to(device, dtype).contiguous()  # [gate; up] for the Q4_K path
+        else:
+            lw.w_gu = ops.interleave_gate_up(gate, up).to(device, dtype).contiguous()
         lw.w_down = _shard_cols(full["down"], r, tp).to(device, dtype).contiguous()
+    if cfg.weight_format == "q4_k":
+        from ..quantization import quantize_q4_k
+
+        lw.w_qkv = quantize_q4_k(lw.w_qkv)
+        lw.w_o = quantize_q4_k(lw.w_o)
+        if lw.w_gu is not None:
+            lw.w_gu = quantize_q4_k(lw.w_gu)
+            lw.w_down = quantize_q4_k(lw.w_down)
+    elif cfg.weight_format != "bf16":
+        raise ValueError(f"unsupported weight format {cfg.weight_format!r}")
     return lw
 
 

@@ -89,7 +89,7 @@ class MoE:
         units = est_mt * (n // bn)
         splits = 1
         if units < self.sms // 2 and k // 64 >= 8:
-            splits = max(1, min(8, _ceil(self.sms, units), k // 256))
+            splits = max(1, min(16, self.sms // units, k // 256))  # one wave, every SM streaming
         return bn, splits
 
     def forward(self, x: torch.Tensor, L, h: torch.Tensor) -> None:

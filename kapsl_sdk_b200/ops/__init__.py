@@ -83,6 +83,8 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     residual-stream update).  ``swiglu`` expects the gate/up weight interleaved
     in 128-row blocks (see :func:`interleave_gate_up`) and returns [M, N/2].
     """
+    if not isinstance(weight, torch.Tensor):
+        return _quant_linear(x, weight, bias, residual, swiglu, out, out_dtype, workspace)
     M, N = x.shape[0], weight.shape[0]
     epi = EPI_PLAIN
     if bias is not None:
@@ -97,6 +99,31 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     if workspace is None:
         workspace = _workspace(x.device)
     cuda_ops().gemm(x, weight, out, epi, bias, residual, workspace, error_buffer(x.device), force_bn, force_splits)
+    return out
+
+
+def _quant_linear(x, weight, bias, residual, swiglu, out, out_dtype, workspace) -> torch.Tensor:
+    """``linear`` for a :class:`~kapsl_sdk_b200.quantization.QuantWeight` (Q4_K):
+    the fused dequant GEMM, with residual fused; SwiGLU expects the gate and up
+    rows concatenated ([gate; up], not interleaved)."""
+    if weight.fmt != "q4_k":
+        raise ValueError(f"no fused kernel for weight format {weight.fmt!r}")
+    if out_dtype != torch.bfloat16:
+        raise ValueError("quantized linear layers produce bf16")
+    M, N = x.shape[0], weight.n
+    if workspace is None:
+        workspace = _workspace(x.device)
+    c = cuda_ops()
+    err = error_buffer(x.device)
+    if swiglu:
+        y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+        c.gemm_q4k(x, weight.raw, y, weight.k, None, workspace, 0, err)
+        return silu_mul(y, out)
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    c.gemm_q4k(x, weight.raw, out, weight.k, residual, workspace, 0, err)
+    if bias is not None:
+        out.add_(bias)
     return out
 
 

@@ -162,7 +162,7 @@ class TPComm:
         rpr = (T + W - 1) // W
         c = cuda_ops()
         err = ops.error_buffer(x.device)
-        if self.mode == "scatter":
+        if self.mode == "scatter" and isinstance(w, torch.Tensor):  # quantized weights take the pull path
             c.gemm_scatter(x, w, b["recv"], self.rank, rpr, self.hidden, err)
             c.tp_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden,
                            self.epoch, err)

@@ -1,1 +1,68 @@
-"""kapsl_sdk_b200.quantization"""
+"""Quantized weights.
+
+* :class:`QuantWeight` — a linear layer's weight kept in a block-quantized
+  format on the GPU; :func:`kapsl_sdk_b200.ops.linear` dispatches it to the
+  matching fused kernel (GGUF Q4_K: dequantized into tensor memory inside the
+  tcgen05 GEMM mainloop, csrc/cuda/gemm_q4k.cu).
+* :func:`quantize_q4_k` / :func:`dequantize_q4_k` — GPU quantizer (same
+  rounding steps as :func:`kapsl_sdk_b200.loaders.gguf.quantize_q4_k`) and
+  dequantizer.
+* :mod:`.safetensors_loaders` — GPTQ / AWQ / INT8 checkpoint readers.
+
+Reference counterpart: crates/kapsl-quantization (config.rs:3-30,
+tensor.rs:4-35, loader/*.rs) parses GPTQ/AWQ/INT8 tensors but has no dequant
+math and is not used by any model path; GGUF k-quants are served there by
+llama.cpp (crates/kapsl-llm/src/gguf_backend.rs:110-118).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+Q4_K_BLOCK = 256
+Q4_K_BYTES = 144
+
+
+@dataclass
+class QuantWeight:
+    """Weight [n, k] stored as rows of packed quantized blocks (uint8 [n, bytes_per_row])."""
+    raw: torch.Tensor
+    n: int
+    k: int
+    fmt: str = "q4_k"
+
+    @property
+    def shape(self) -> tuple:
+        return (self.n, self.k)
+
+    @property
+    def device(self) -> torch.device:
+        return self.raw.device
+
+    def nbytes(self) -> int:
+        return self.raw.numel()
+
+    def dequantize(self) -> torch.Tensor:
+        return dequantize_q4_k(self.raw, self.n, self.k)
+
+
+def quantize_q4_k(w: torch.Tensor) -> QuantWeight:
+    """bf16 [n, k] (k % 256 == 0) on the GPU -> Q4_K QuantWeight."""
+    from .._ext import cuda_ops
+
+    n, k = w.shape
+    if k % Q4_K_BLOCK:
+        raise ValueError(f"Q4_K needs the input dimension to be a multiple of 256 (got {k})")
+    w = w.to(torch.bfloat16).contiguous()
+    raw = torch.empty(n, k // Q4_K_BLOCK * Q4_K_BYTES, dtype=torch.uint8, device=w.device)
+    cuda_ops().q4k_quantize(w, raw)
+    return QuantWeight(raw, n, k, "q4_k")
+
+
+def dequantize_q4_k(raw: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    from .._ext import cuda_ops
+
+    out = torch.empty(n, k, dtype=torch.bfloat16, device=raw.device)
+    cuda_ops().q4k_dequant(raw.contiguous(), out)
+    return out
