@@ -132,6 +132,30 @@ __device__ __forceinline__ bool wait_flags(const int64_t* flags_site, int world,
   return true;
 }
 
+// Same contract as mbar_wait_bounded, but the thread asks to be suspended
+// inside try_wait (suspend-time hint) instead of spinning, so warps that wait
+// for long stretches do not take issue slots from the warps doing the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity,
+                                                uint64_t timeout_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, parity, 100000u)) return true;
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
+}
+
 // ---- TMA -------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");

@@ -11,18 +11,24 @@
 // The product is computed transposed, D[n, t] = W[n, :] . X[t, :], so that the
 // weights are the MMA's A operand and can live in tensor memory:
 //   warp 0       TMA: raw Q4_K rows (128 weight rows x 144 B per super-block)
-//                and X tiles (TT tokens x 64, 128-byte swizzle) into smem rings
+//   warp 2       TMA: X tiles (TT tokens x 64, 128-byte swizzle); two producers so
+//                the weight prefetch never waits behind the activation ring
 //   warp 1       MMA: tcgen05.mma.kind::f16 with A read from TMEM (128 x 16),
 //                B = the X tile from smem, D (128 x TT fp32) in TMEM
-//   warps 2..9   dequant: each thread owns one weight row (its TMEM lane) and
-//                half of every 64-wide k-block; nibbles -> bf16 pairs with a
-//                byte permute + exponent-bias trick, scaled with bf16x2 FMAs,
-//                written to TMEM with tcgen05.st (no smem round trip)
-//   warps 10..13 epilogue: tcgen05.ld of D rows, stores Y[t, n] (coalesced over
+//   warps 3..10  dequant: each thread owns one weight row (its TMEM lane) and
+//                one nibble half of every super-block; nibbles -> bf16 pairs with
+//                a byte permute + exponent-bias trick, scaled with bf16x2 FMAs,
+//                written to TMEM with tcgen05.st (no smem round trip).  The TMEM
+//                A ring holds whole super-blocks (4 k-blocks = 128 columns), so
+//                the dequant/MMA hand-off happens once per 256 weights.
+//   warps 11..14 epilogue: tcgen05.ld of D rows, stores Y[t, n] (coalesced over
 //                n across the warp), optional residual add or split-K partials
+// Waiting warps sleep in try_wait (suspend hint) instead of spinning.
 // The raw weights cross HBM once at 4.5 bits per weight; for small M the
 // kernel streams them at memory speed, for large M the MMAs (N = TT = 256)
 // amortise the dequant over 256 tokens.
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -38,20 +44,22 @@ constexpr int BK = 64;      // k per k-block
 constexpr int QK = 256;     // weights per super-block
 constexpr int QB = 144;     // bytes per super-block
 constexpr int RAW_BYTES = WT * QB;  // 18432
-constexpr int NRAW = 3;     // raw super-block stages
-constexpr int NA = 4;       // TMEM A slots (32 columns each)
 constexpr int kDequantWarps = 8;
 constexpr int kEpiWarps = 4;
-constexpr int kThreads = 32 * (2 + kDequantWarps + kEpiWarps);  // 448
+constexpr int kDqWarp0 = 3;  // warps: 0 raw TMA, 1 MMA, 2 X TMA, 3..10 dequant, 11..14 epilogue
+constexpr int kThreads = 32 * (kDqWarp0 + kDequantWarps + kEpiWarps);  // 480
 
 template <int TT>
 struct Cfg {
   static constexpr int NACC = TT <= 128 ? 2 : 1;
   static constexpr int NX = TT <= 64 ? 8 : (TT <= 128 ? 6 : 4);
+  static constexpr int NRAW = TT <= 128 ? 6 : 5;  // raw super-block stages (18 KiB each)
   static constexpr int X_BYTES = TT * BK * 2;
   static constexpr int A_COL0 = NACC * TT;
-  static constexpr int USED_COLS = A_COL0 + NA * 32;
-  static constexpr uint32_t TMEM_COLS = USED_COLS <= 256 ? 256 : 512;
+  // TMEM A slots of one super-block each (4 k-blocks x 32 columns), filling
+  // the 512 columns that the accumulators leave free.
+  static constexpr int NA = (512 - A_COL0) / 128;
+  static constexpr uint32_t TMEM_COLS = 512;
   static constexpr size_t SMEM = (size_t)NRAW * RAW_BYTES + (size_t)NX * X_BYTES + 1024;
 };
 
@@ -118,9 +126,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* xring = smem;                                  // NX x X_BYTES (1024-aligned, swizzled)
   uint8_t* rawring = smem + (size_t)C::NX * C::X_BYTES;   // NRAW x RAW_BYTES
-  __shared__ __align__(8) uint64_t raw_full[NRAW], raw_empty[NRAW];
+  __shared__ __align__(8) uint64_t raw_full[C::NRAW], raw_empty[C::NRAW];
   __shared__ __align__(8) uint64_t x_full[C::NX], x_empty[C::NX];
-  __shared__ __align__(8) uint64_t a_full[NA], a_empty[NA];
+  __shared__ __align__(8) uint64_t a_full[C::NA], a_empty[C::NA];
   __shared__ __align__(8) uint64_t acc_full[C::NACC], acc_empty[C::NACC];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
@@ -133,7 +141,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_units = n_tiles * t_tiles * a.splits;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NRAW; ++i) {
+    for (int i = 0; i < C::NRAW; ++i) {
       mbar_init(&raw_full[i], 1);
       mbar_init(&raw_empty[i], kDequantWarps);
     }
@@ -141,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&x_full[i], 1);
       mbar_init(&x_empty[i], 1);
     }
-    for (int i = 0; i < NA; ++i) {
+    for (int i = 0; i < C::NA; ++i) {
       mbar_init(&a_full[i], kDequantWarps);
       mbar_init(&a_empty[i], 1);
     }
@@ -165,33 +173,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     nt = r % n_tiles;
     sp = r / n_tiles;
   };
+  // Each unit walks its super-blocks from a unit-dependent offset, so the CTAs
+  // do not all read the same X tile (the same L2 lines) at the same moment.
+  auto rot_sb = [](int u, int sb0, int sb1, int sb) {
+    const int cnt = sb1 - sb0;
+    return sb0 + (sb - sb0 + (u * 7) % cnt) % cnt;
+  };
   auto fail = [&](int code) {
     abort_sh = 1;
     atomicExch(err, code);
   };
 
   if (warp == 0) {
-    // ------------------------------------------------------------ TMA producer
+    // ------------------------------------------------------------ raw Q4_K producer
     if (lane == 0) {
       tma_prefetch_desc(&tmap_w);
-      tma_prefetch_desc(&tmap_x);
-      int rs = 0, xs = 0;
-      uint32_t rph = 0, xph = 0;
+      int rs = 0;
+      uint32_t rph = 0;
       for (int u = blockIdx.x; u < num_units && !*(volatile int*)&abort_sh; u += gridDim.x) {
         int tt, nt, sp;
         decode_unit(u, tt, nt, sp);
         const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
         for (int sb = sb0; sb < sb1; ++sb) {
-          if (!mbar_wait_bounded(&raw_empty[rs], rph ^ 1)) { fail(60); break; }
+          if (!mbar_wait_sleep(&raw_empty[rs], rph ^ 1)) { fail(60); break; }
           mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
-          tma_load_2d(rawring + (size_t)rs * RAW_BYTES, &tmap_w, &raw_full[rs], sb * QB, nt * WT);
-          if (++rs == NRAW) { rs = 0; rph ^= 1; }
-          for (int i = 0; i < QK / BK; ++i) {
-            if (!mbar_wait_bounded(&x_empty[xs], xph ^ 1)) { fail(61); break; }
-            mbar_arrive_expect_tx(&x_full[xs], C::X_BYTES);
-            tma_load_2d(xring + (size_t)xs * C::X_BYTES, &tmap_x, &x_full[xs], (sb * 4 + i) * BK, tt * TT);
-            if (++xs == C::NX) { xs = 0; xph ^= 1; }
-          }
+          tma_load_2d(rawring + (size_t)rs * RAW_BYTES, &tmap_w, &raw_full[rs], rot_sb(u, sb0, sb1, sb) * QB,
+                      nt * WT);
+          if (++rs == C::NRAW) { rs = 0; rph ^= 1; }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 2) {
+    // ------------------------------------------------------------ X (activation) producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmap_x);
+      int xs = 0;
+      uint32_t xph = 0;
+      for (int u = blockIdx.x; u < num_units && !*(volatile int*)&abort_sh; u += gridDim.x) {
+        int tt, nt, sp;
+        decode_unit(u, tt, nt, sp);
+        const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
+        for (int kb = sb0 * 4; kb < sb1 * 4; ++kb) {
+          if (!mbar_wait_sleep(&x_empty[xs], xph ^ 1)) { fail(61); break; }
+          mbar_arrive_expect_tx(&x_full[xs], C::X_BYTES);
+          tma_load_2d(xring + (size_t)xs * C::X_BYTES, &tmap_x, &x_full[xs],
+                      (rot_sb(u, sb0, sb1, kb >> 2) * 4 + (kb & 3)) * BK, tt * TT);
+          if (++xs == C::NX) { xs = 0; xph ^= 1; }
         }
       }
     }
@@ -208,94 +236,112 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
         const int acc = C::NACC == 2 ? (it & 1) : 0;
         const uint32_t acc_ph = C::NACC == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
-        if (!mbar_wait_bounded(&acc_empty[acc], acc_ph ^ 1)) { fail(62); break; }
+        if (!mbar_wait_sleep(&acc_empty[acc], acc_ph ^ 1)) { fail(62); break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TT);
-        bool first = true;
-        for (int kb = sb0 * 4; kb < sb1 * 4; ++kb) {
-          if (!mbar_wait_bounded(&x_full[xs], xph) || !mbar_wait_bounded(&a_full[as], aph)) { fail(63); break; }
-          tc_fence_after();
-          const uint32_t xa = smem_u32(xring + (size_t)xs * C::X_BYTES);
-          const uint32_t a_tmem = tmem_base + (uint32_t)(C::A_COL0 + as * 32);
+        bool first = true, ok = true;
+        for (int sb = sb0; sb < sb1 && ok; ++sb) {
+          if (!mbar_wait_sleep(&a_full[as], aph)) { fail(63); ok = false; break; }
+          const uint32_t a_tmem = tmem_base + (uint32_t)(C::A_COL0 + as * 128);
+          for (int i = 0; i < QK / BK; ++i) {
+            if (!mbar_wait_sleep(&x_full[xs], xph)) { fail(63); ok = false; break; }
+            tc_fence_after();
+            const uint32_t xa = smem_u32(xring + (size_t)xs * C::X_BYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            mma_bf16_tmem_a(d_tmem, a_tmem + k * 8, smem_desc_sw128(xa + k * 32), IDESC, first ? 0u : 1u);
-            first = false;
+            for (int k = 0; k < BK / 16; ++k) {
+              mma_bf16_tmem_a(d_tmem, a_tmem + i * 32 + k * 8, smem_desc_sw128(xa + k * 32), IDESC,
+                              first ? 0u : 1u);
+              first = false;
+            }
+            mma_commit(&x_empty[xs]);
+            if (++xs == C::NX) { xs = 0; xph ^= 1; }
           }
-          mma_commit(&x_empty[xs]);
+          if (!ok) break;
           mma_commit(&a_empty[as]);
-          if (++xs == C::NX) { xs = 0; xph ^= 1; }
-          if (++as == NA) { as = 0; aph ^= 1; }
+          if (++as == C::NA) { as = 0; aph ^= 1; }
         }
-        if (*(volatile int*)&abort_sh) break;
+        if (!ok || *(volatile int*)&abort_sh) break;
         mma_commit(&acc_full[acc]);
       }
     }
     __syncwarp();
-  } else if (warp < 2 + kDequantWarps) {
+  } else if (warp < kDqWarp0 + kDequantWarps) {
     // ------------------------------------------------------------ dequant
-    const int dw = warp - 2;
+    const int dw = warp - kDqWarp0;
     const int quad = warp & 3;        // TMEM lane quadrant this warp may access
-    const int half = dw >> 2;         // 0: low nibbles (first sub-block), 1: high
     const int row = quad * 32 + lane; // weight row inside the tile
-    int rs = 0, as = 0;
-    uint32_t rph = 0, aph = 0;
-    for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
-      int tt, nt, sp;
-      decode_unit(u, tt, nt, sp);
-      const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
-      bool stop = false;
-      for (int sb = sb0; sb < sb1 && !stop; ++sb) {
-        const bool got = mbar_wait_bounded(&raw_full[rs], rph);
-        if (!__all_sync(0xffffffffu, got)) {
-          if (lane == 0) fail(64);
-          stop = true;
-          break;
-        }
-        const uint8_t* blk = rawring + (size_t)rs * RAW_BYTES + (size_t)row * QB;
-        const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
-        const float d = half_bits_to_float(hdr.x & 0xFFFFu);
-        const float dmin = half_bits_to_float(hdr.x >> 16);
-        const uint32_t scw[3] = {hdr.y, hdr.z, hdr.w};
-#pragma unroll
-        for (int i = 0; i < QK / BK; ++i) {
-          int sc, mn;
-          scale_min_w(scw, 2 * i + half, i < 2, sc, mn);
-          const float dsf = d * (float)sc;
-          const float dmf = dmin * (float)mn;
-          const __nv_bfloat162 ds = __floats2bfloat162_rn(dsf, dsf);
-          const __nv_bfloat162 ndm = __floats2bfloat162_rn(-dmf, -dmf);
-          const uint4 q0 = *reinterpret_cast<const uint4*>(blk + 16 + 32 * i);
-          const uint4 q1 = *reinterpret_cast<const uint4*>(blk + 32 + 32 * i);
-          const int sh = 4 * half;
-          const uint32_t w[8] = {q0.x >> sh, q0.y >> sh, q0.z >> sh, q0.w >> sh,
-                                 q1.x >> sh, q1.y >> sh, q1.z >> sh, q1.w >> sh};
-          uint32_t r[16];  // column c = weights (2c, 2c + 1) of this sub-block
-#pragma unroll
-          for (int j = 0; j < 8; ++j) {
-            r[2 * j] = dq_pair(w[j], 0x4140u, ds, ndm);
-            r[2 * j + 1] = dq_pair(w[j], 0x4342u, ds, ndm);
+    const uint32_t lane_base = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)C::A_COL0;
+    // HALF 0: low nibbles (first sub-block of each 64-group), 1: high nibbles.
+    auto run = [&](auto half_c) {
+      constexpr int HALF = decltype(half_c)::value;
+      int rs = 0, as = 0;
+      uint32_t rph = 0, aph = 0;
+      for (int u = blockIdx.x; u < num_units; u += gridDim.x) {
+        int tt, nt, sp;
+        decode_unit(u, tt, nt, sp);
+        const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
+        bool stop = false;
+        for (int sb = sb0; sb < sb1; ++sb) {
+          const bool got = mbar_wait_sleep(&raw_full[rs], rph);
+          if (!__all_sync(0xffffffffu, got)) {
+            if (lane == 0) fail(64);
+            stop = true;
+            break;
           }
-          const bool free_slot = mbar_wait_bounded(&a_empty[as], aph ^ 1);
+          const uint8_t* blk = rawring + (size_t)rs * RAW_BYTES + (size_t)row * QB;
+          const uint4 hdr = *reinterpret_cast<const uint4*>(blk);
+          const float d = half_bits_to_float(hdr.x & 0xFFFFu);
+          const float dmin = half_bits_to_float(hdr.x >> 16);
+          const uint32_t scw[3] = {hdr.y, hdr.z, hdr.w};
+          uint4 qv[4][2];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            qv[i][0] = *reinterpret_cast<const uint4*>(blk + 16 + 32 * i);
+            qv[i][1] = *reinterpret_cast<const uint4*>(blk + 32 + 32 * i);
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&raw_empty[rs]);  // the stage's bytes are in registers
+          if (++rs == C::NRAW) { rs = 0; rph ^= 1; }
+          const bool free_slot = mbar_wait_sleep(&a_empty[as], aph ^ 1);
           if (!__all_sync(0xffffffffu, free_slot)) {
             if (lane == 0) fail(65);
             stop = true;
             break;
           }
           tc_fence_after();
-          tmem_st16(tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(C::A_COL0 + as * 32 + half * 16), r);
+          // four k-blocks: 32 weights (16 packed columns) each, four stores, one wait
+#pragma unroll
+          for (int i = 0; i < QK / BK; ++i) {
+            int sc, mn;
+            scale_min_w(scw, 2 * i + HALF, i < 2, sc, mn);
+            const float dsf = d * (float)sc;
+            const float dmf = dmin * (float)mn;
+            const __nv_bfloat162 ds = __floats2bfloat162_rn(dsf, dsf);
+            const __nv_bfloat162 ndm = __floats2bfloat162_rn(-dmf, -dmf);
+            const uint32_t w[8] = {qv[i][0].x >> (4 * HALF), qv[i][0].y >> (4 * HALF), qv[i][0].z >> (4 * HALF),
+                                   qv[i][0].w >> (4 * HALF), qv[i][1].x >> (4 * HALF), qv[i][1].y >> (4 * HALF),
+                                   qv[i][1].z >> (4 * HALF), qv[i][1].w >> (4 * HALF)};
+            uint32_t r[16];  // column c = weights (2c, 2c + 1) of this sub-block
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              r[2 * j] = dq_pair(w[j], 0x4140u, ds, ndm);
+              r[2 * j + 1] = dq_pair(w[j], 0x4342u, ds, ndm);
+            }
+            tmem_st16(lane_base + (uint32_t)(as * 128 + i * 32 + HALF * 16), r);
+          }
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(&a_full[as]);
-          if (++as == NA) { as = 0; aph ^= 1; }
+          if (++as == C::NA) { as = 0; aph ^= 1; }
         }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&raw_empty[rs]);
-        if (++rs == NRAW) { rs = 0; rph ^= 1; }
+        if (stop || *(volatile int*)&abort_sh) break;
       }
-      if (stop || *(volatile int*)&abort_sh) break;
-    }
+    };
+    if (dw >= 4)
+      run(std::integral_constant<int, 1>{});
+    else
+      run(std::integral_constant<int, 0>{});
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;
@@ -305,7 +351,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_unit(u, tt, nt, sp);
       const int acc = C::NACC == 2 ? (it & 1) : 0;
       const uint32_t acc_ph = C::NACC == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
-      const bool got = mbar_wait_bounded(&acc_full[acc], acc_ph);
+      const bool got = mbar_wait_sleep(&acc_full[acc], acc_ph);
       if (!__all_sync(0xffffffffu, got)) {
         if (lane == 0) fail(66);
         break;

@@ -1,6 +1,7 @@
 """Kernel micro-benchmarks / profiling drivers for the sm_100a kernels.
 
     python -m kapsl_sdk_b200.utils.kernel_bench gemm M N K [--epi plain|bias|residual|swiglu] [--time]
+    python -m kapsl_sdk_b200.utils.kernel_bench gemm_q4k M N K [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench decode B CTX HQ HKV [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench prefill S CHUNK HQ HKV [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench sample B V [--time]
@@ -126,15 +127,41 @@ def bench_sample(B, V, timed):
     return {"kernel": "sample", "B": B, "V": V, "ms": ms, "GBps": B * V * 4 / ms / 1e6}
 
 
+def bench_gemm_q4k(M, N, K, timed):
+    """GEMM with GGUF Q4_K weights (dequantized in the mainloop); reports the
+    Q4_K bytes streamed per second and the FLOP rate, plus the same GEMM with
+    bf16 weights for comparison."""
+    from .. import ops
+    from ..quantization import quantize_q4_k
+
+    dev = torch.device("cuda", 0)
+    w = (torch.randn(N, K, device=dev) * 0.02).to(torch.bfloat16)
+    qw = quantize_q4_k(w)
+    x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    fn = lambda: ops.linear(x, qw, out=out)
+    if not timed:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {"kernel": "gemm_q4k", "M": M, "N": N, "K": K}
+    ms = _time(fn)
+    ms_bf16 = _time(lambda: ops.linear(x, w, out=out))
+    return {"kernel": "gemm_q4k", "M": M, "N": N, "K": K, "ms": ms, "q4k_GBps": qw.nbytes() / ms / 1e6,
+            "tflops": 2 * M * N * K / ms / 1e9, "bf16_weights_ms": ms_bf16}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemm", "decode", "prefill", "sample"])
+    p.add_argument("what", choices=["gemm", "gemm_q4k", "decode", "prefill", "sample"])
     p.add_argument("dims", nargs="+", type=int)
     p.add_argument("--epi", default="plain", choices=["plain", "bias", "residual", "swiglu"])
     p.add_argument("--time", action="store_true")
     a = p.parse_args(argv)
     if a.what == "gemm":
         r = bench_gemm(*a.dims[:3], a.epi, a.time)
+    elif a.what == "gemm_q4k":
+        r = bench_gemm_q4k(*a.dims[:3], a.time)
     elif a.what == "decode":
         r = bench_decode(*a.dims[:4], a.time)
     elif a.what == "prefill":
