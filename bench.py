@@ -1,6 +1,8 @@
 """Serving benchmark: output tokens/s of the continuous-batching engine.
 
-Workload (Qwen2.5-7B architecture, bf16, random N(0, 0.02) weights from seed 0):
+``--workload`` picks the model and request shape (see ``WORKLOADS``); the
+default, the headline configuration, is
+(Qwen2.5-7B architecture, bf16, random N(0, 0.02) weights from seed 0):
 256 concurrent requests, prompt lengths uniform in [512, 2048], token ids
 uniform over the 152064-entry vocab, 256 output tokens each (EOS ignored),
 chunked prefill with a 2048-token step budget, paged KV with 16-token blocks,
@@ -40,17 +42,33 @@ REASON_BITS = {
 }
 
 
+# Serving workloads: synthetic uniform-random token ids, random-init weights.
+WORKLOADS = {
+    # 256 concurrent requests, prompts U[512, 2048], 256 output tokens
+    "qwen2.5-7b": dict(model="qwen2.5-7b", num_requests=256, min_prompt=512, max_prompt=2048, output_len=256),
+    # 128 requests, 1024-token prompts, 256 output tokens; 8 experts top-2
+    "mixtral-8x7b": dict(model="mixtral-8x7b", num_requests=128, min_prompt=1024, max_prompt=1024, output_len=256),
+    # 64 requests, 4096-token prompts, 512 output tokens; GGUF Q4_K linear layers
+    "llama-3-70b-q4k": dict(model="llama-3-70b-q4k", num_requests=64, min_prompt=4096, max_prompt=4096,
+                            output_len=512),
+}
+MODEL_LABEL = {"qwen2.5-7b": "Qwen2.5-7B-arch", "mixtral-8x7b": "Mixtral-8x7B-arch",
+               "llama-3-70b-q4k": "Llama-3-70B-arch Q4_K"}
+
+
 def parse_args():
     p = argparse.ArgumentParser()
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=1)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", default="kapsl", choices=["kapsl", "reference"])
-    p.add_argument("--model", default="qwen2.5-7b")
-    p.add_argument("--num-requests", type=int, default=256)
-    p.add_argument("--min-prompt", type=int, default=512)
-    p.add_argument("--max-prompt", type=int, default=2048)
-    p.add_argument("--output-len", type=int, default=256)
+    p.add_argument("--workload", default="qwen2.5-7b", choices=sorted(WORKLOADS),
+                   help="named serving workload (model + request shape); the flags below override it")
+    p.add_argument("--model", default=None)
+    p.add_argument("--num-requests", type=int, default=None)
+    p.add_argument("--min-prompt", type=int, default=None)
+    p.add_argument("--max-prompt", type=int, default=None)
+    p.add_argument("--output-len", type=int, default=None)
     p.add_argument("--chunk", type=int, default=2048)
     p.add_argument("--parallel", default="tp", choices=["dp", "tp"],
                    help="tp: one model over all N GPUs (the named TP=N config, strong scaling); "
@@ -61,7 +79,11 @@ def parse_args():
     p.add_argument("--num-layers", type=int, default=0, help="override (testing only; invalid for the metric)")
     p.add_argument("--warmup-scale", type=float, default=1.0,
                    help="fraction of requests served by each warm-up step")
-    return p.parse_args()
+    a = p.parse_args()
+    for k, v in WORKLOADS[a.workload].items():
+        if getattr(a, k) is None:
+            setattr(a, k, v)
+    return a
 
 
 class ClockSampler:
@@ -179,6 +201,7 @@ def main():
     ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
                         max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph)
     engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0)
+    weight_gb = (torch.cuda.memory_allocated(dev) - engine.pool.storage.numel() * engine.pool.storage.element_size()) / 1e9
     # data-parallel replicas serve their own copy of the workload (weak scaling);
     # tensor parallel shares one workload across the ranks (strong scaling).
     # A fresh prompt set for every pass (warm-up, timed, end-to-end), so no pass
@@ -268,11 +291,11 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
             "higher_is_better": True, "scaling": "strong" if args.parallel == "tp" else "weak", "vs_baseline": None,
             "dtype": "bf16", "data": "synthetic token ids, random-init weights N(0,0.02) seed 0",
-            "config": {"model": "Qwen2.5-7B-arch" if args.model == "qwen2.5-7b" else args.model,
+            "config": {"model": MODEL_LABEL.get(args.model, args.model),
                        "global_batch": args.num_requests * (world if tp_comm is None else 1),
                        "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}] + {args.output_len} out",
                        "parallelism": par, "chunked_prefill": args.chunk, "kv_block": 16,
-                       "l2": "inputs larger than L2 (15 GB weights, GB-scale KV), no flush",
+                       "l2": f"inputs larger than L2 ({weight_gb:.0f} GB weights, GB-scale KV), no flush",
                        "num_layers": cfg.num_layers},
             "p50_ttft_ms": round(ttft_all * 1000, 2), "p50_tpot_ms": round(tpot_all * 1000, 3),
             "clocks": clocks.summary(),

@@ -305,7 +305,7 @@ void grouped_gemm(Tensor A, Tensor B, Tensor C, int64_t N, int64_t num_groups, T
 
 // Y[M, N] = X[M, K] . dequant(Wq[N, K/256 * 144 bytes])^T (+ residual)
 void gemm_q4k(Tensor X, Tensor Wq, Tensor Y, int64_t K, c10::optional<Tensor> res, c10::optional<Tensor> workspace,
-              int64_t force_splits, Tensor err) {
+              int64_t force_splits, bool tiled, Tensor err) {
   CHECK_DT(X, at::kBFloat16, "X");
   CHECK_DT(Y, at::kBFloat16, "Y");
   TORCH_CHECK(Wq.scalar_type() == at::kByte && Wq.dim() == 2 && Wq.is_contiguous(), "gemm_q4k: Wq uint8 [N, bytes]");
@@ -330,7 +330,7 @@ void gemm_q4k(Tensor X, Tensor Wq, Tensor Y, int64_t K, c10::optional<Tensor> re
   }
   const c10::cuda::CUDAGuard g(X.device());
   kapsl::launch_gemm_q4k(bf(X), X.stride(0), Wq.data_ptr<uint8_t>(), Wq.size(1), bf(Y), Y.stride(0), (int)M, (int)N,
-                         (int)K, rp, ldr, ws, wsb, (int)force_splits, err.data_ptr<int>(), cur_stream());
+                         (int)K, rp, ldr, ws, wsb, (int)force_splits, tiled, err.data_ptr<int>(), cur_stream());
 }
 
 void q4k_quantize(Tensor x, Tensor out) {

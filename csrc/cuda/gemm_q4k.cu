@@ -69,6 +69,10 @@ struct Q4Args {
   const bf16* res;    // residual [M, ldr] (EPI 2) or null
   int64_t ldr;
   float* partial;     // split-K fp32 partials [splits, M, N]
+  // Tile-contiguous weights (null: row-major through the tensor map): the
+  // 128 rows x 144 bytes of weight tile nt, super-block sb start at
+  // tiled + (nt * nsb + sb) * RAW_BYTES, one bulk copy per super-block.
+  const uint8_t* tiled;
   int M, N, K, splits;
 };
 
@@ -197,8 +201,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int sb = sb0; sb < sb1; ++sb) {
           if (!mbar_wait_sleep(&raw_empty[rs], rph ^ 1)) { fail(60); break; }
           mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
-          tma_load_2d(rawring + (size_t)rs * RAW_BYTES, &tmap_w, &raw_full[rs], rot_sb(u, sb0, sb1, sb) * QB,
-                      nt * WT);
+          const int sbr = rot_sb(u, sb0, sb1, sb);
+          if (a.tiled)
+            bulk_load(rawring + (size_t)rs * RAW_BYTES, a.tiled + ((size_t)nt * nsb + sbr) * RAW_BYTES, RAW_BYTES,
+                      &raw_full[rs]);
+          else
+            tma_load_2d(rawring + (size_t)rs * RAW_BYTES, &tmap_w, &raw_full[rs], sbr * QB, nt * WT);
           if (++rs == C::NRAW) { rs = 0; rph ^= 1; }
         }
       }
@@ -494,7 +502,7 @@ void launch_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const Q4Args& a, i
 
 void launch_gemm_q4k(const __nv_bfloat16* X, int64_t ldx, const uint8_t* Wq, int64_t w_pitch, __nv_bfloat16* Y,
                      int64_t ldy, int M, int N, int K, const __nv_bfloat16* res, int64_t ldr, float* workspace,
-                     size_t workspace_bytes, int force_splits, int* err, cudaStream_t st) {
+                     size_t workspace_bytes, int force_splits, bool tiled, int* err, cudaStream_t st) {
   using namespace q4k;
   if (M == 0 || N == 0) return;
   if (K % QK != 0) throw std::runtime_error("gemm_q4k: K must be a multiple of 256");
@@ -514,9 +522,11 @@ void launch_gemm_q4k(const __nv_bfloat16* X, int64_t ldx, const uint8_t* Wq, int
   }
   if (splits > 1 && (workspace == nullptr || (size_t)splits * M * N * sizeof(float) > workspace_bytes))
     splits = 1;
+  if (tiled && (N % WT != 0 || (reinterpret_cast<uintptr_t>(Wq) & 15) != 0))
+    throw std::runtime_error("gemm_q4k: tile-contiguous weights need N % 128 == 0 and a 16-byte aligned base");
   CUtensorMap tw = make_tmap_2d_u8(Wq, N, (uint64_t)w_pitch, (uint64_t)w_pitch, WT, QB);
   CUtensorMap tx = make_tmap_2d_bf16(X, M, K, ldx, TT, BK);
-  Q4Args a{Y, ldy, res, ldr, workspace, M, N, K, splits};
+  Q4Args a{Y, ldy, res, ldr, workspace, tiled ? Wq : nullptr, M, N, K, splits};
   const int grid = std::min(tiles * splits, sms);
   const int epi = splits > 1 ? 4 : (res ? 2 : 0);
 #define KAPSL_Q4_DISPATCH(TTV)                                            \

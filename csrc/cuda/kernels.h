@@ -54,10 +54,11 @@ void launch_grouped_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat1
                          int64_t ldc, int rows, int N, int K, int num_groups, const int* mtiles, int epi, int bn,
                          int splits, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st);
 
-// GGUF Q4_K weights (gemm_q4k.cu): Y = X . dequant(Wq)^T (+ res); Wq rows are packed 144-byte blocks
+// GGUF Q4_K weights (gemm_q4k.cu): Y = X . dequant(Wq)^T (+ res); Wq rows are packed 144-byte blocks,
+// or (tiled) [N/128][K/256][128 rows][144 B] so each weight tile's super-block is contiguous
 void launch_gemm_q4k(const __nv_bfloat16* X, int64_t ldx, const uint8_t* Wq, int64_t w_pitch, __nv_bfloat16* Y,
                      int64_t ldy, int M, int N, int K, const __nv_bfloat16* res, int64_t ldr, float* workspace,
-                     size_t workspace_bytes, int force_splits, int* err, cudaStream_t st);
+                     size_t workspace_bytes, int force_splits, bool tiled, int* err, cudaStream_t st);
 void launch_q4k_quantize(const __nv_bfloat16* x, int64_t n, uint8_t* out, cudaStream_t st);
 void launch_q4k_dequant(const uint8_t* raw, int64_t n, __nv_bfloat16* out, cudaStream_t st);
 

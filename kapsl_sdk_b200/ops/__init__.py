@@ -117,11 +117,11 @@ def _quant_linear(x, weight, bias, residual, swiglu, out, out_dtype, workspace) 
     err = error_buffer(x.device)
     if swiglu:
         y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-        c.gemm_q4k(x, weight.raw, y, weight.k, None, workspace, 0, err)
+        c.gemm_q4k(x, weight.raw, y, weight.k, None, workspace, 0, weight.tiled, err)
         return silu_mul(y, out)
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
-    c.gemm_q4k(x, weight.raw, out, weight.k, residual, workspace, 0, err)
+    c.gemm_q4k(x, weight.raw, out, weight.k, residual, workspace, 0, weight.tiled, err)
     if bias is not None:
         out.add_(bias)
     return out

@@ -26,11 +26,16 @@ Q4_K_BYTES = 144
 
 @dataclass
 class QuantWeight:
-    """Weight [n, k] stored as rows of packed quantized blocks (uint8 [n, bytes_per_row])."""
+    """Weight [n, k] stored as packed quantized blocks (uint8, n * bytes_per_row bytes).
+
+    ``tiled``: the Q4_K blocks are reordered tile-major, [n/128][k/256][128 rows][144 B],
+    so each 128-row tile's super-block is one contiguous 18 KiB copy for the GEMM
+    (the row-major GGUF order needs one strided 144-byte piece per row)."""
     raw: torch.Tensor
     n: int
     k: int
     fmt: str = "q4_k"
+    tiled: bool = False
 
     @property
     def shape(self) -> tuple:
@@ -43,12 +48,34 @@ class QuantWeight:
     def nbytes(self) -> int:
         return self.raw.numel()
 
+    def row_major(self) -> torch.Tensor:
+        """The blocks in GGUF row order (uint8 [n, k/256 * 144])."""
+        if not self.tiled:
+            return self.raw
+        nsb = self.k // Q4_K_BLOCK
+        return self.raw.view(self.n // 128, nsb, 128, Q4_K_BYTES).permute(0, 2, 1, 3).reshape(self.n, -1)
+
     def dequantize(self) -> torch.Tensor:
-        return dequantize_q4_k(self.raw, self.n, self.k)
+        return dequantize_q4_k(self.row_major().contiguous(), self.n, self.k)
 
 
-def quantize_q4_k(w: torch.Tensor) -> QuantWeight:
-    """bf16 [n, k] (k % 256 == 0) on the GPU -> Q4_K QuantWeight."""
+def tile_q4_k(raw: torch.Tensor, n: int, k: int) -> torch.Tensor:
+    """Row-major Q4_K blocks [n, k/256 * 144] -> tile-major order (n % 128 == 0)."""
+    nsb = k // Q4_K_BLOCK
+    return raw.view(n // 128, 128, nsb, Q4_K_BYTES).permute(0, 2, 1, 3).contiguous().view(n, nsb * Q4_K_BYTES)
+
+
+def from_gguf_blocks(raw: torch.Tensor, n: int, k: int, tiled: bool = True) -> QuantWeight:
+    """Wrap GGUF Q4_K bytes (row-major, as stored in the file) for the fused GEMM."""
+    raw = raw.reshape(n, k // Q4_K_BLOCK * Q4_K_BYTES)
+    if tiled and n % 128 == 0:
+        return QuantWeight(tile_q4_k(raw, n, k), n, k, "q4_k", True)
+    return QuantWeight(raw.contiguous(), n, k, "q4_k", False)
+
+
+def quantize_q4_k(w: torch.Tensor, tiled: bool = True) -> QuantWeight:
+    """bf16 [n, k] (k % 256 == 0) on the GPU -> Q4_K QuantWeight (tile-major
+    when ``tiled`` and n % 128 == 0)."""
     from .._ext import cuda_ops
 
     n, k = w.shape
@@ -57,7 +84,7 @@ def quantize_q4_k(w: torch.Tensor) -> QuantWeight:
     w = w.to(torch.bfloat16).contiguous()
     raw = torch.empty(n, k // Q4_K_BLOCK * Q4_K_BYTES, dtype=torch.uint8, device=w.device)
     cuda_ops().q4k_quantize(w, raw)
-    return QuantWeight(raw, n, k, "q4_k")
+    return from_gguf_blocks(raw, n, k, tiled)
 
 
 def dequantize_q4_k(raw: torch.Tensor, n: int, k: int) -> torch.Tensor:

@@ -21,7 +21,7 @@ def test_quantize_matches_reference_bytes():
     w = _w(64, 1024, 0)
     w[3, :256] = 0  # an all-zero super-block
     w[5, 256:512] = torch.abs(w[5, 256:512])  # no negative values: min 0
-    qw = quantize_q4_k(w.cuda())
+    qw = quantize_q4_k(w.cuda(), tiled=False)
     ref = np_quant(w.float().numpy().reshape(-1)).reshape(64, -1)
     got = qw.raw.cpu().numpy()
     assert got.shape == ref.shape
@@ -33,21 +33,26 @@ def test_dequant_matches_reference():
     from kapsl_sdk_b200.quantization import quantize_q4_k
 
     w = _w(32, 2048, 1)
-    qw = quantize_q4_k(w.cuda())
+    qw = quantize_q4_k(w.cuda(), tiled=False)
     got = qw.dequantize().float().cpu()
     ref = torch.from_numpy(dequant_q4_k(qw.raw.cpu().numpy().reshape(-1))).view(32, 2048)
+    w2 = _w(256, 512, 2)
+    qr, qt = quantize_q4_k(w2.cuda(), tiled=False), quantize_q4_k(w2.cuda())  # row-major / tile-major
+    assert qt.tiled and torch.equal(qt.row_major().cpu(), qr.raw.cpu())
+    assert torch.equal(qt.dequantize(), qr.dequantize())
     torch.testing.assert_close(got, ref.to(torch.bfloat16).float(), atol=0, rtol=0)
     assert (got - w.float()).abs().max() < 0.01  # a 4-bit code of N(0, 0.02) values
 
 
 @pytest.mark.parametrize("M,N,K", [(1, 128, 256), (5, 384, 1024), (64, 1280, 8192), (100, 256, 4096),
                                    (128, 1000, 768), (300, 512, 2048), (1030, 256, 512)])
-def test_gemm_q4k(M, N, K):
+@pytest.mark.parametrize("tiled", [True, False])
+def test_gemm_q4k(M, N, K, tiled):
     from kapsl_sdk_b200 import ops
     from kapsl_sdk_b200.quantization import quantize_q4_k
 
     dev = torch.device("cuda", 0)
-    qw = quantize_q4_k(_w(N, K, M + N).to(dev))
+    qw = quantize_q4_k(_w(N, K, M + N).to(dev), tiled=tiled)
     x = (torch.randn(M, K, generator=torch.Generator().manual_seed(K)) * 0.5).to(dev, torch.bfloat16)
     y = ops.linear(x, qw)
     ref = x.float() @ qw.dequantize().float().T
@@ -69,7 +74,7 @@ def test_gemm_q4k_split_and_residual():
     ref = x.float() @ qw.dequantize().float().T + res.float()
     for splits in (1, 3, 16):
         out = res.clone()
-        cuda_ops().gemm_q4k(x, qw.raw, out, K, out, ops._workspace(dev), splits, ops.error_buffer(dev))
+        cuda_ops().gemm_q4k(x, qw.raw, out, K, out, ops._workspace(dev), splits, qw.tiled, ops.error_buffer(dev))
         err = (out.float() - ref).abs().max().item()
         assert err <= 0.02 * ref.abs().max().item() + 1e-2, (splits, err)
     assert ops.check_errors(dev) == 0
