@@ -400,6 +400,29 @@ void moe_combine(std::vector<int64_t> y, std::vector<int64_t> hidden, std::vecto
                             err.data_ptr<int>(), kapsl::gemm_num_sms(), cur_stream());
 }
 
+// Copy blocks src_ids[i] -> dst_ids[i] of every plane (layer x K/V) from the local
+// pool `src` into the pool at `dst_ptr` (typically a peer GPU's pool mapped by CUDA IPC).
+void kv_push(Tensor src, int64_t dst_ptr, Tensor src_ids, Tensor dst_ids, int64_t planes, int64_t dst_blocks_per_plane) {
+  CHECK_DT(src_ids, at::kInt, "src_ids");
+  CHECK_DT(dst_ids, at::kInt, "dst_ids");
+  TORCH_CHECK(src.is_contiguous() && src.dim() >= 3, "kv_push: src pool [layers, 2, blocks, ...] contiguous");
+  TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "kv_push: id lists differ in length");
+  const int64_t src_blocks = src.size(2);
+  const int64_t block_bytes = src.numel() / (src.size(0) * src.size(1) * src_blocks) * src.element_size();
+  TORCH_CHECK(planes == src.size(0) * src.size(1), "kv_push: plane count mismatch");
+  const c10::cuda::CUDAGuard g(src.device());
+  kapsl::launch_kv_push(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), src_ids.data_ptr<int32_t>(),
+                        dst_ids.data_ptr<int32_t>(), (int)src_ids.numel(), (int)planes, src_blocks,
+                        dst_blocks_per_plane, block_bytes, kapsl::gemm_num_sms(), cur_stream());
+}
+
+// Asynchronous copy on the current stream (copy engine) between device addresses,
+// either of which may be a peer GPU's memory mapped by CUDA IPC.
+void copy_async(int64_t dst_ptr, int64_t src_ptr, int64_t bytes) {
+  KAPSL_CHECK_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(dst_ptr), reinterpret_cast<const void*>(src_ptr),
+                                   (size_t)bytes, cudaMemcpyDeviceToDevice, cur_stream()));
+}
+
 Tensor tensor_from_ptr(int64_t ptr, std::vector<int64_t> shape, std::string dtype, int64_t device) {
   at::ScalarType st;
   if (dtype == "bfloat16") st = at::kBFloat16;
@@ -439,6 +462,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &moe_permute, "stable expert sort of the top-k assignments (padded segments)");
   m.def("moe_gather", &moe_gather, "gather token rows into the expert-sorted buffer");
   m.def("moe_combine", &moe_combine, "weighted top-k combine + residual (+ peer pull and all-gather)");
+  m.def("kv_push", &kv_push, "KV connector: copy pool blocks into a (peer) pool over NVLink");
+  m.def("copy_async", &copy_async, "cudaMemcpyAsync on the current stream (copy-engine baseline)");
   m.def("tp_pull_reduce_ag", &tp_pull_reduce_ag, "barrier + pull peers' partial rows + residual + all-gather push");
   m.def("p2p_copy", &p2p_copy, "16-byte vector copy between (possibly peer-mapped) device addresses");
   m.def("symm_alloc", &symm_alloc);

@@ -74,6 +74,11 @@ void launch_moe_combine(const __nv_bfloat16* const* y, __nv_bfloat16* const* hid
                         int K, int el, int cols, int64_t ld_y, int64_t ld_h, int rows_per_rank, int64_t* epoch_ctr,
                         int* err, int num_sms, cudaStream_t st);
 
+// disaggregated prefill/decode: push KV blocks into a peer pool (kv_connector.cu)
+void launch_kv_push(const void* src_pool, void* dst_pool, const int32_t* src_ids, const int32_t* dst_ids, int nblocks,
+                    int planes, int64_t src_blocks_per_plane, int64_t dst_blocks_per_plane, int64_t block_bytes,
+                    int num_sms, cudaStream_t st);
+
 // tensor parallel over NVLink peer memory (tp_comm.cu / gemm_sm100.cu)
 void launch_gemm_scatter(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb,
                          __nv_bfloat16* const* peers, int world, int my_rank, int rows_per_rank, int64_t ld_recv,

@@ -52,6 +52,7 @@ class EngineConfig:
     max_session_tokens: int = 0         # 0 = max_model_len
     kv_soft_limit_bytes: int = 0        # 0 = 90% of hard
     kv_hard_limit_bytes: int = 0        # 0 = pool size
+    shareable_kv: bool = False          # pool mappable by another process (disaggregated decode side)
 
 
 class LLMEngine:
@@ -90,7 +91,7 @@ class LLMEngine:
             nblocks = KVPool.blocks_for_bytes(layout, int(max(free - reserve, 1 << 30) * e.kv_memory_fraction))
             if tp_comm is not None and tp_comm.world_size > 1:
                 nblocks = tp_comm.min_int(nblocks)
-        self.pool = KVPool(layout, nblocks, self.device)
+        self.pool = KVPool(layout, nblocks, self.device, shareable=e.shareable_kv)
         self.runner = ModelRunner(self.model, self.pool, e.max_num_seqs, e.max_num_batched_tokens, e.max_model_len,
                                   e.use_cuda_graph)
         self._finish_init(cfg, e, nblocks, tp_comm)
@@ -107,6 +108,10 @@ class LLMEngine:
         hard = e.kv_hard_limit_bytes or self.pool.nbytes
         self.kv_hard = hard
         self.kv_soft = e.kv_soft_limit_bytes or int(hard * 0.9)
+        # Disaggregated prefill: called with the sequences that finish in a step,
+        # before their KV blocks go back to the allocator (the KV connector copies
+        # them out on the same stream, so later reuse of the blocks is ordered after it).
+        self.kv_export: Optional[Callable] = None
         self.profile = None
         if os.environ.get("KAPSL_LLM_PROFILE", os.environ.get("KAPSL_LLM_PROFILE_DECODE", "0")) == "1":
             self.profile = {"steps": 0, "decode_steps": 0, "tokens": 0, "schedule_s": 0.0, "prepare_s": 0.0,
@@ -158,6 +163,31 @@ class LLMEngine:
             self.sessions[session_id] = seq
         return seq
 
+    def add_prefilled(self, request_id: str, prompt_ids: list, first_token: int, block_ids: list,
+                      params: Optional[SamplingParams] = None, rng_state: Optional[int] = None) -> Sequence:
+        """Adopt a sequence whose prompt KV another engine computed and wrote into
+        ``block_ids`` of this engine's pool (disaggregated decode).  ``rng_state``
+        is the sampler state after the first token was drawn."""
+        params = params or SamplingParams()
+        seq_id = next(self._seq_ids)
+        if rng_state is None:
+            rng_state = ref.seed_state(params.seed, request_id, seq_id)
+        seq = Sequence(seq_id=seq_id, request_id=request_id, prompt_ids=[int(t) for t in prompt_ids],
+                       params=params, rng_state=rng_state)
+        seq.output_ids.append(int(first_token))
+        seq.block_ids = list(block_ids)
+        seq.num_computed = len(seq.prompt_ids)
+        seq.first_token_time = time.perf_counter()
+        seq.token_times.append(seq.first_token_time)
+        if self._stop(seq, int(first_token)) is not None:
+            seq.finish_time = seq.first_token_time
+            seq.finish_reason = "length"
+            self.scheduler.finish(seq, SequenceStatus.FINISHED_LENGTH)
+            self.finished.append(seq)
+            return seq
+        self.scheduler.add(seq)
+        return seq
+
     def abort(self, request_id: str) -> None:
         for s in self.scheduler.abort(request_id):
             s.finish_time = time.perf_counter()
@@ -202,20 +232,25 @@ class LLMEngine:
         for s, n in batch.prefill:
             s.num_computed += n
         outs = []
+        reasons = []
         for s, tok in zip(seqs, toks.tolist()):
             s.output_ids.append(tok)
             if s.first_token_time is None:
                 s.first_token_time = now
             s.token_times.append(now)
-            reason = self._stop(s, tok)
+            reasons.append(self._stop(s, tok))
+        if self.kv_export is not None:
+            done = [s for s, r in zip(seqs, reasons) if r is not None]
+            if done:
+                self.kv_export(done)
+        for s, reason in zip(seqs, reasons):
+            tok = s.output_ids[-1]
             if reason is not None:
                 s.finish_time = now
                 s.finish_reason = reason
-                keep = s.session_id is not None
                 self.scheduler.finish(s, SequenceStatus.FINISHED_STOPPED if reason == "stop"
                                       else SequenceStatus.FINISHED_LENGTH, keep_blocks=False)
                 self.finished.append(s)
-                del keep
             if s.on_token is not None:
                 s.on_token(s, tok, reason is not None)
             outs.append(StepOutput(s.request_id, s, tok, reason is not None))
@@ -248,3 +283,5 @@ class LLMEngine:
 
     def shutdown(self) -> None:
         self.runner.release_graphs()
+        if hasattr(self.pool, "close"):
+            self.pool.close()

@@ -32,15 +32,45 @@ class KVLayout:
 
 
 class KVPool:
-    def __init__(self, layout: KVLayout, num_blocks: int, device):
+    def __init__(self, layout: KVLayout, num_blocks: int, device, shareable: bool = False):
+        """``shareable``: allocate the pages with cudaMalloc so that another process
+        (the prefill side of a disaggregated deployment) can map them with CUDA IPC
+        and write KV blocks into them directly."""
         self.layout = layout
         self.num_blocks = num_blocks
         self.device = torch.device(device)
         L = layout
-        self.storage = torch.zeros(L.num_layers, 2, num_blocks, L.num_kv_heads, L.block_size, L.head_dim,
-                                   dtype=L.dtype, device=self.device)
+        shape = (L.num_layers, 2, num_blocks, L.num_kv_heads, L.block_size, L.head_dim)
+        self._raw = 0
+        if shareable and self.device.type == "cuda":
+            from .._ext import cuda_ops
+
+            c = cuda_ops()
+            nbytes = L.bytes_per_block() * num_blocks
+            with torch.cuda.device(self.device):
+                self._raw = c.symm_alloc(nbytes)  # zero-filled
+                self.storage = c.tensor_from_ptr(self._raw, list(shape), "bfloat16", self.device.index)
+        else:
+            self.storage = torch.zeros(shape, dtype=L.dtype, device=self.device)
         self.k = [self.storage[i, 0] for i in range(L.num_layers)]
         self.v = [self.storage[i, 1] for i in range(L.num_layers)]
+
+    def ipc_handle(self) -> str:
+        """CUDA IPC handle of a shareable pool (see ``shareable``)."""
+        if not self._raw:
+            raise RuntimeError("KV pool was not allocated shareable")
+        from .._ext import cuda_ops
+
+        return cuda_ops().symm_handle(self._raw)
+
+    def close(self) -> None:
+        if self._raw:
+            from .._ext import cuda_ops
+
+            torch.cuda.synchronize(self.device)
+            self.storage = None
+            cuda_ops().symm_free(self._raw)
+            self._raw = 0
 
     @staticmethod
     def blocks_for_bytes(layout: KVLayout, nbytes: int) -> int:

@@ -2,6 +2,7 @@
 
     python -m kapsl_sdk_b200.utils.kernel_bench gemm M N K [--epi plain|bias|residual|swiglu] [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench gemm_q4k M N K [--time]
+    python -m kapsl_sdk_b200.utils.kernel_bench moe T E D F [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench decode B CTX HQ HKV [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench prefill S CHUNK HQ HKV [--time]
     python -m kapsl_sdk_b200.utils.kernel_bench sample B V [--time]
@@ -127,6 +128,38 @@ def bench_sample(B, V, timed):
     return {"kernel": "sample", "B": B, "V": V, "ms": ms, "GBps": B * V * 4 / ms / 1e6}
 
 
+def bench_moe(T, E, d, F, timed, top_k=2):
+    """One MoE FFN layer (route, permute, gather, grouped gate/up + SwiGLU,
+    grouped down, combine) on T tokens with E experts, single GPU."""
+    import types
+
+    from .. import ops
+    from ..models.config import ModelConfig
+    from ..models.moe import MoE
+
+    dev = torch.device("cuda", 0)
+    cfg = ModelConfig(hidden_size=d, intermediate_size=F, num_experts=E, experts_per_token=top_k)
+    L = types.SimpleNamespace(
+        w_router=(torch.randn(E, d, device=dev) * 0.02).to(torch.bfloat16),
+        w_experts_gu=(torch.randn(E, 2 * F, d, device=dev) * 0.02).to(torch.bfloat16),
+        w_experts_down=(torch.randn(E, d, F, device=dev) * 0.02).to(torch.bfloat16))
+    moe = MoE(cfg, dev)
+    moe.configure(T)
+    x = torch.randn(T, d, device=dev).to(torch.bfloat16)
+    h = torch.zeros(T, d, device=dev, dtype=torch.bfloat16)
+    fn = lambda: moe.forward(x, L, h)
+    if not timed:
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return {"kernel": "moe", "T": T, "E": E}
+    ms = _time(fn)
+    flops = 2 * T * top_k * 3 * d * F
+    wbytes = 3 * E * d * F * 2
+    return {"kernel": "moe", "T": T, "E": E, "d": d, "F": F, "ms": ms, "tflops": flops / ms / 1e9,
+            "weight_GBps": wbytes / ms / 1e6}
+
+
 def bench_gemm_q4k(M, N, K, timed):
     """GEMM with GGUF Q4_K weights (dequantized in the mainloop); reports the
     Q4_K bytes streamed per second and the FLOP rate, plus the same GEMM with
@@ -153,7 +186,7 @@ def bench_gemm_q4k(M, N, K, timed):
 
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemm", "gemm_q4k", "decode", "prefill", "sample"])
+    p.add_argument("what", choices=["gemm", "gemm_q4k", "moe", "decode", "prefill", "sample"])
     p.add_argument("dims", nargs="+", type=int)
     p.add_argument("--epi", default="plain", choices=["plain", "bias", "residual", "swiglu"])
     p.add_argument("--time", action="store_true")
@@ -162,6 +195,8 @@ def main(argv=None):
         r = bench_gemm(*a.dims[:3], a.epi, a.time)
     elif a.what == "gemm_q4k":
         r = bench_gemm_q4k(*a.dims[:3], a.time)
+    elif a.what == "moe":
+        r = bench_moe(*a.dims[:4], a.time)
     elif a.what == "decode":
         r = bench_decode(*a.dims[:4], a.time)
     elif a.what == "prefill":
