@@ -52,8 +52,11 @@ WORKLOADS = {
     "llama-3-70b-q4k": dict(model="llama-3-70b-q4k", num_requests=64, min_prompt=4096, max_prompt=4096,
                             output_len=512),
 }
+# disaggregated prefill/decode (``--parallel pd``): 32 requests, 8192-token prompts, 128 output tokens
+WORKLOADS["llama-3-8b-pd"] = dict(model="llama-3-8b", num_requests=32, min_prompt=8192, max_prompt=8192,
+                                  output_len=128)
 MODEL_LABEL = {"qwen2.5-7b": "Qwen2.5-7B-arch", "mixtral-8x7b": "Mixtral-8x7B-arch",
-               "llama-3-70b-q4k": "Llama-3-70B-arch Q4_K"}
+               "llama-3-70b-q4k": "Llama-3-70B-arch Q4_K", "llama-3-8b": "Llama-3-8B-arch"}
 
 
 def parse_args():
@@ -70,9 +73,12 @@ def parse_args():
     p.add_argument("--max-prompt", type=int, default=None)
     p.add_argument("--output-len", type=int, default=None)
     p.add_argument("--chunk", type=int, default=2048)
-    p.add_argument("--parallel", default="tp", choices=["dp", "tp"],
+    p.add_argument("--parallel", default="tp", choices=["dp", "tp", "pd"],
                    help="tp: one model over all N GPUs (the named TP=N config, strong scaling); "
-                        "dp: N independent replicas, each serving its own copy of the workload")
+                        "dp: N independent replicas, each serving its own copy of the workload; "
+                        "pd: disaggregated, prefill on GPUs [0, N/2) and decode on [N/2, N), TP N/2 each")
+    p.add_argument("--kv-mode", default="p2p", choices=["p2p", "copy"],
+                   help="pd: KV transfer by the P2P push kernel or the copy-engine baseline")
     p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
                    help="row-parallel reduction: fused NVLink kernels or the NCCL baseline")
     p.add_argument("--no-graph", action="store_true")
@@ -190,6 +196,8 @@ def main():
     from kapsl_sdk_b200.models.config import get_preset
 
     cuda_ops()
+    if args.parallel == "pd":
+        return run_pd(args, dev, world, rank, local)
     cfg = get_preset(args.model)
     if args.num_layers:
         cfg.num_layers = args.num_layers
@@ -309,6 +317,85 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def run_pd(args, dev, world: int, rank: int, local: int) -> int:
+    """Disaggregated prefill/decode through the KV connector; device-timed over
+    whole serving passes (barrier + synchronize on both sides, max over ranks)."""
+    import torch
+    import torch.distributed as dist
+
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.models.config import get_preset
+    from kapsl_sdk_b200.parallel.disagg import Disaggregated
+    from kapsl_sdk_b200.parallel.tp import TPComm
+
+    if world < 2:
+        raise SystemExit("--parallel pd needs at least 2 GPUs")
+    cfg = get_preset(args.model)
+    if args.num_layers:
+        cfg.num_layers = args.num_layers
+
+    def make(role, group, gi, n):
+        tp = TPComm(n, gi, dev, args.tp_mode, group=group) if n > 1 else None
+        ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
+                            max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph,
+                            shareable_kv=(role == "decode"))
+        return LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp, seed=0)
+
+    d = Disaggregated(make, mode=args.kv_mode)
+    params = SamplingParams(max_new_tokens=args.output_len, temperature=0.7, top_k=40, top_p=0.9,
+                            repetition_penalty=1.15, ignore_eos=True)
+    nwarm = max(1, int(args.num_requests * args.warmup_scale))
+    for i in range(args.warmup):
+        d.serve(make_workload(args, cfg.vocab_size, seed=1 + i)[:nwarm], params)
+    torch.cuda.synchronize()
+    dist.barrier()
+    launches0 = d.engine.runner.launches
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    seqs = []
+    with ClockSampler(local) as clocks:
+        dist.barrier()
+        torch.cuda.synchronize()
+        batches = [make_workload(args, cfg.vocab_size, seed=100 + i) for i in range(args.steps)]
+        start.record()
+        for b in batches:
+            _, s = d.serve(b, params)
+            seqs.extend(s or [])
+        end.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+    ms = start.elapsed_time(end)
+    out_tokens = sum(len(s.output_ids) for s in seqs)
+    ttft = statistics.median([s.ttft() for s in seqs]) if seqs else 0.0
+    tpot = statistics.median([s.tpot() for s in seqs if s.tpot() is not None]) if seqs else 0.0
+    vals = torch.tensor([ms, out_tokens, ttft, tpot, d.engine.runner.launches - launches0], dtype=torch.float64,
+                        device=dev)
+    g = [torch.zeros_like(vals) for _ in range(world)]
+    dist.all_gather(g, vals)
+    g = torch.stack(g)
+    P = world // 2
+    ms_max = float(g[:, 0].max())
+    tokens = float(g[P, 1])
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": round(tokens / (ms_max / 1000.0), 2), "unit": "output tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic token ids, random-init weights N(0,0.02) seed 0",
+            "config": {"model": MODEL_LABEL.get(args.model, args.model), "global_batch": args.num_requests,
+                       "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}] + {args.output_len} out",
+                       "parallelism": f"pd: prefill tp{P} + decode tp{P}, kv {args.kv_mode}",
+                       "chunked_prefill": args.chunk, "kv_block": 16,
+                       "l2": "inputs larger than L2 (GB-scale weights and KV), no flush"},
+            "p50_ttft_ms": round(float(g[P, 2]) * 1000, 2), "p50_tpot_ms": round(float(g[P, 3]) * 1000, 3),
+            "clocks": clocks.summary(), "gpu_launches": int(g[:, 4].sum())}))
+    d.close()
+    d.engine.shutdown()
+    dist.barrier()
+    dist.destroy_process_group()
     return 0
 
 

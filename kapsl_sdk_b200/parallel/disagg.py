@@ -273,6 +273,7 @@ class DecodeWorker(_Worker):
             assert job.k == k
             self.conn.receive(job.k, job.blocks)
             job.seq = self.engine.add_prefilled(job.request_id, job.prompt, tok, job.blocks, job.params, rng)
+            job.seq.arrival = job.t_submit  # TTFT counts from submission to the decode side
         if self.engine.has_unfinished():
             self.engine.step()
         return bool(self.waiting) or self.engine.has_unfinished()
@@ -283,42 +284,65 @@ class DecodeWorker(_Worker):
             self.store.set(f"{self.ns}/stop", str(self.next_job).encode())
 
 
+class Disaggregated:
+    """One rank's part of a disaggregated deployment: builds the groups, the
+    engine and the KV connector once; ``serve`` runs one batch of requests
+    (every rank of the default process group calls each method)."""
+
+    def __init__(self, make_engine, mode: str = "p2p", ns: str = "pd"):
+        import torch.distributed as dist
+
+        world, self.rank = dist.get_world_size(), dist.get_rank()
+        self.pr, self.dr, self.gp, self.gd, np_, nd = _groups(world)
+        self.P = len(self.pr)
+        self.store = dist.distributed_c10d._get_default_store()
+        self.role = "prefill" if self.rank < self.P else "decode"
+        self.gi = self.rank if self.role == "prefill" else self.rank - self.P
+        self.engine = make_engine(self.role, np_ if self.role == "prefill" else nd, self.gi, self.P)
+        self.mode, self.ns, self.passes = mode, ns, 0
+        # decode ranks publish their pools before the prefill ranks map them
+        if self.role == "decode":
+            self.conn = KVConnector(self.engine.pool, self.role, self.gi, self.store, ns, mode)
+        dist.barrier()
+        if self.role == "prefill":
+            self.conn = KVConnector(self.engine.pool, self.role, self.gi, self.store, ns, mode)
+
+    def serve(self, prompts: list, params: SamplingParams, timeout_s: float = 600.0):
+        """Returns (outputs, sequences) in prompt order on decode ranks, (None, None) on prefill ranks."""
+        ns = f"{self.ns}/{self.passes}"
+        self.passes += 1
+        if self.role == "prefill":
+            w = PrefillWorker(self.engine, self.conn, self.store, ns, self.gp, self.pr[0], self.gi == 0, self.gi)
+        else:
+            w = DecodeWorker(self.engine, self.conn, self.store, ns, self.gd, self.dr[0], self.gi == 0, self.P)
+            for i, p in enumerate(prompts):
+                w.submit(f"{ns}-{i}", p, params)
+            w.stop()
+        t0 = time.perf_counter()
+        while w.poll_and_step():
+            if time.perf_counter() - t0 > timeout_s:
+                raise TimeoutError(f"{self.role} rank {self.rank}: disaggregated serving did not finish "
+                                   f"in {timeout_s} s")
+        self.engine.kv_export = None
+        if self.role == "prefill":
+            return None, None
+        return [j.seq.output_ids for j in w.submitted], [j.seq for j in w.submitted]
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self.engine.pool.device.type == "cuda":
+            torch.cuda.synchronize(self.engine.pool.device)
+        dist.barrier()
+        self.conn.close()
+
+
 def serve_disaggregated(make_engine, prompts: list, params: SamplingParams, mode: str = "p2p",
                         ns: str = "pd", timeout_s: float = 600.0):
-    """Run ``prompts`` through a prefill group and a decode group (every rank of
-    the default process group calls this).  ``make_engine(role, tp_group,
-    rank_in_group, group_size)`` builds the rank's engine (the decode side with
-    ``shareable_kv`` for the p2p/copy modes).  Returns, on decode ranks, the
-    output token lists in prompt order (None on prefill ranks) and the
-    sequences."""
-    import torch.distributed as dist
-
-    world, rank = dist.get_world_size(), dist.get_rank()
-    pr, dr, gp, gd, np_, nd = _groups(world)
-    P = len(pr)
-    store = dist.distributed_c10d._get_default_store()
-    role = "prefill" if rank < P else "decode"
-    gi = rank if role == "prefill" else rank - P
-    engine = make_engine(role, np_ if role == "prefill" else nd, gi, P)
-    # decode ranks publish their pools before the prefill ranks map them
-    conn = KVConnector(engine.pool, role, gi, store, ns, mode) if role == "decode" else None
-    dist.barrier()
-    if role == "prefill":
-        conn = KVConnector(engine.pool, role, gi, store, ns, mode)
-        w = PrefillWorker(engine, conn, store, ns, gp, pr[0], gi == 0, gi)
-    else:
-        w = DecodeWorker(engine, conn, store, ns, gd, dr[0], gi == 0, P)
-        for i, p in enumerate(prompts):
-            w.submit(f"pd-{i}", p, params)
-        w.stop()
-    t0 = time.perf_counter()
-    while w.poll_and_step():
-        if time.perf_counter() - t0 > timeout_s:
-            raise TimeoutError(f"{role} rank {rank}: disaggregated serving did not finish in {timeout_s} s")
-    if role == "decode":
-        torch.cuda.synchronize() if engine.pool.device.type == "cuda" else None
-    dist.barrier()
-    conn.close()
-    outs = [j.seq.output_ids for j in w.submitted] if role == "decode" else None
-    seqs = [j.seq for j in w.submitted] if role == "decode" else None
-    return engine, outs, seqs
+    """One-shot helper: build a :class:`Disaggregated` deployment, serve
+    ``prompts`` and close the connector.  Returns (engine, outputs, sequences);
+    outputs and sequences are None on prefill ranks."""
+    d = Disaggregated(make_engine, mode, ns)
+    outs, seqs = d.serve(prompts, params, timeout_s)
+    d.close()
+    return d.engine, outs, seqs
