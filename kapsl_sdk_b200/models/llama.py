@@ -102,6 +102,18 @@ class ShardPlan:
         return out
 
 
+def ffn_shard_size(cfg: ModelConfig, tp: int) -> int:
+    """Per-rank FFN width: F / tp rounded up to the GEMM tile (128; 256 for Q4_K,
+    whose blocks span 256 inputs).  Ranks past F hold zero gate/up rows and zero
+    down columns (e.g. Qwen2.5-7B's 18944 over 8 ranks: 2368 -> 2432)."""
+    align = 256 if cfg.weight_format == "q4_k" else 128
+    return -(-cfg.intermediate_size // (tp * align)) * align
+
+
+def _pad_rows(w: torch.Tensor, n: int) -> torch.Tensor:
+    return w if w.shape[0] == n else torch.cat([w, w.new_zeros(n - w.shape[0], *w.shape[1:])], 0)
+
+
 def _shard_rows(w: torch.Tensor, rank: int, tp: int) -> torch.Tensor:
     n = w.shape[0] // tp
     return w[rank * n:(rank + 1) * n]
@@ -154,13 +166,14 @@ def shard_layer(cfg: ModelConfig, plan: ShardPlan, full: dict, device, dtype=tor
         lw.w_experts_gu = torch.stack(gu).to(device, dtype).contiguous()
         lw.w_experts_down = full["experts_down"][e0:e0 + el].to(device, dtype).contiguous()
     else:
-        gate = _shard_rows(full["gate"], r, tp)
-        up = _shard_rows(full["up"], r, tp)
+        Fp = ffn_shard_size(cfg, tp) * tp
+        gate = _shard_rows(_pad_rows(full["gate"], Fp), r, tp)
+        up = _shard_rows(_pad_rows(full["up"], Fp), r, tp)
         if cfg.weight_format == "q4_k":
             lw.w_gu = torch.cat([gate, up], 0).to(device, dtype).contiguous()  # [gate; up] for the Q4_K path
         else:
             lw.w_gu = ops.interleave_gate_up(gate, up).to(device, dtype).contiguous()
-        lw.w_down = _shard_cols(full["down"], r, tp).to(device, dtype).contiguous()
+        lw.w_down = _shard_cols(_pad_rows(full["down"].T, Fp).T, r, tp).to(device, dtype).contiguous()
     if cfg.weight_format == "q4_k":
         from ..quantization import quantize_q4_k
 
@@ -227,7 +240,7 @@ def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: in
     vl, v0 = V, 0
     w = ModelWeights(embed=None, lm_head=None, final_norm=torch.ones(d, device=device, dtype=torch.bfloat16),
                      vocab_start=v0, heads_local=plan.heads_local, kv_heads_local=plan.kv_heads_local,
-                     ffn_local=cfg.intermediate_size // tp if not cfg.is_moe else cfg.intermediate_size)
+                     ffn_local=ffn_shard_size(cfg, tp) if not cfg.is_moe else cfg.intermediate_size)
     for kind, t in full_iter:
         if kind == "embed":
             w.embed = t[v0:v0 + vl].to(device, torch.bfloat16).contiguous()

@@ -1,6 +1,7 @@
-"""Tensor parallelism on 2+ GPUs (skipped with fewer): the fused NVLink
-row-parallel reduction against the NCCL baseline and against TP1, driven as
-child processes (one per GPU) over NCCL with NVLS off."""
+"""Tensor and expert parallelism on 2, 4 or 8 GPUs (skipped with fewer): the
+fused NVLink row-parallel reduction against the NCCL baseline and against
+TP1 (with padded query heads at 8 ranks), and an expert-parallel MoE model
+against one GPU, driven as child processes (one per GPU) over NCCL with NVLS off."""
 import json
 import os
 import subprocess
@@ -49,8 +50,9 @@ for mode in ("fused", "nccl"):
     out[mode + "_err"] = ops.check_errors(dev)
     tp.close()
 # 2) a small model: TP=world greedy tokens vs TP=1 on rank 0
+# 12 query heads over 2 KV heads: at 8 ranks each KV group of 6 is padded to 8 query heads
 cfg = ModelConfig(name="s", arch="qwen2", vocab_size=1024, hidden_size=512, intermediate_size=1024, num_layers=2,
-                  num_heads=8, num_kv_heads=2, head_dim=128, max_position=1024, qkv_bias=True,
+                  num_heads=12, num_kv_heads=2, head_dim=128, max_position=1024, qkv_bias=True,
                   bos_token_id=None, eos_token_id=None)
 prompts = [[(i * 37 + j) % 1000 for j in range(n)] for i, n in enumerate((40, 130, 7))]
 tp = TPComm(world, rank, dev, "fused")
@@ -65,6 +67,21 @@ if rank == 0:
     e1 = LLMEngine(cfg, device=dev, engine_cfg=EngineConfig(max_num_seqs=8, max_num_batched_tokens=128,
                    max_model_len=512, num_blocks=256), seed=0)
     out["tp1_tokens"] = e1.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
+# 3) mixture of experts: experts split over the ranks (fused peer-pull combine) vs one GPU
+mcfg = ModelConfig(name="m", arch="mixtral", vocab_size=1024, hidden_size=512, intermediate_size=512, num_layers=2,
+                   num_heads=8, num_kv_heads=8, head_dim=128, max_position=1024, num_experts=8,
+                   experts_per_token=2, bos_token_id=None, eos_token_id=None)
+tp = TPComm(world, rank, dev, "fused")
+eng = LLMEngine(mcfg, device=dev, engine_cfg=EngineConfig(max_num_seqs=8, max_num_batched_tokens=128,
+                max_model_len=512, num_blocks=256), tp_comm=tp, seed=0)
+out["ep_tokens"] = eng.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
+out["ep_err"] = ops.check_errors(dev)
+eng.shutdown()
+tp.close()
+if rank == 0:
+    e1 = LLMEngine(mcfg, device=dev, engine_cfg=EngineConfig(max_num_seqs=8, max_num_batched_tokens=128,
+                   max_model_len=512, num_blocks=256), seed=0)
+    out["ep1_tokens"] = e1.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
 print("RESULT " + json.dumps(out), flush=True)
 dist.barrier()
 dist.destroy_process_group()
@@ -90,16 +107,19 @@ def _run(world):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_tensor_parallel_two_gpus():
-    outs = _run(2)
+def test_tensor_and_expert_parallel():
+    world = 1 << (min(torch.cuda.device_count(), 8).bit_length() - 1)  # 2, 4 or 8 ranks
+    outs = _run(world)
     res = []
     for rc, o in outs:
         line = [l for l in o.splitlines() if l.startswith("RESULT ")]
         assert rc == 0 and line, o[-3000:]
         res.append(json.loads(line[0][7:]))
     for r in res:
-        assert r["fused_err"] == 0 and r["nccl_err"] == 0 and r["engine_err"] == 0
+        assert r["fused_err"] == 0 and r["nccl_err"] == 0 and r["engine_err"] == 0 and r["ep_err"] == 0
         assert r["fused"] < 0.5 and r["nccl"] < 0.5, r
-    assert res[0]["tp_tokens"] == res[1]["tp_tokens"]  # ranks stay in lock step
-    same = sum(a == b for x, y in zip(res[0]["tp_tokens"], res[0]["tp1_tokens"]) for a, b in zip(x, y))
-    assert same >= 0.8 * sum(len(x) for x in res[0]["tp1_tokens"]), res[0]
+    for key in ("tp_tokens", "ep_tokens"):
+        assert all(r[key] == res[0][key] for r in res)  # ranks stay in lock step
+    for key, ref in (("tp_tokens", "tp1_tokens"), ("ep_tokens", "ep1_tokens")):
+        same = sum(a == b for x, y in zip(res[0][key], res[0][ref]) for a, b in zip(x, y))
+        assert same >= 0.8 * sum(len(x) for x in res[0][ref]), (key, res[0][key], res[0][ref])
