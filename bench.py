@@ -52,6 +52,9 @@ WORKLOADS = {
     "llama-3-70b-q4k": dict(model="llama-3-70b-q4k", num_requests=64, min_prompt=4096, max_prompt=4096,
                             output_len=512),
 }
+# CPU backend served over a Unix socket (KapslClient.infer_stream), f32 GGUF tiny Llama:
+# 4 requests of 128 token ids, greedy 64 output tokens (no GPU)
+WORKLOADS["tiny-llama-cpu"] = dict(model="tiny-llama", num_requests=4, min_prompt=128, max_prompt=128, output_len=64)
 # disaggregated prefill/decode (``--parallel pd``): 32 requests, 8192-token prompts, 128 output tokens
 WORKLOADS["llama-3-8b-pd"] = dict(model="llama-3-8b", num_requests=32, min_prompt=8192, max_prompt=8192,
                                   output_len=128)
@@ -174,6 +177,8 @@ def main():
     args = parse_args()
     if args.impl == "reference":
         return reference_arm(args)
+    if args.workload == "tiny-llama-cpu":
+        return run_cpu_serving(args)
 
     import numpy as np
     import torch
@@ -317,6 +322,108 @@ def main():
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+    return 0
+
+
+def _cpu_server(gguf: str, sock: str, num_requests: int, chunk: int, max_len: int, output_len: int) -> None:
+    """Server process of the CPU workload: GGUF -> CPU engine -> LLMBackend -> socket server."""
+    from kapsl_sdk_b200.llm.backend import LLMBackend, RuntimeConfig
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.loaders.gguf import load_gguf_model
+    from kapsl_sdk_b200.server import KapslServer
+
+    cfg, model, tok = load_gguf_model(gguf, "cpu")
+    engine = LLMEngine(cfg, weights=model, device="cpu",
+                       engine_cfg=EngineConfig(max_num_seqs=num_requests, max_num_batched_tokens=chunk,
+                                               max_model_len=max_len, block_size=16, num_blocks=num_requests * 16),
+                       seed=0)
+    rc = RuntimeConfig(sampling=SamplingParams.greedy(output_len, ignore_eos=True))
+    backend = LLMBackend(engine, tokenizer=tok, runtime_config=rc)
+    srv = KapslServer(models={0: backend}).listen_unix(sock).start()
+    while srv is not None:  # keep the server object alive until the process is terminated
+        time.sleep(3600)
+
+
+def run_cpu_serving(args) -> int:
+    """Tiny Llama f32 GGUF on the CPU backend behind the socket server (its own
+    process), driven by concurrent KapslClient.infer_stream calls with
+    token-id prompts.  Host-timed on the client side (there is no device); a
+    step serves all requests to completion."""
+    import multiprocessing as mp
+    import threading
+
+    import numpy as np
+    import torch
+
+    from kapsl_sdk import KapslClient
+    from kapsl_sdk_b200.loaders.gguf import write_gguf_model
+    from kapsl_sdk_b200.models.config import get_preset
+    from kapsl_sdk_b200.models.llama import random_full_weights
+
+    cfg = get_preset(args.model)
+    tmp = tempfile.mkdtemp(prefix="kapsl-bench-")
+    gguf = os.path.join(tmp, "tiny-llama-f32.gguf")
+    write_gguf_model(gguf, cfg, random_full_weights(cfg, torch.device("cpu"), seed=0, std=0.02), quant="f32")
+    sock = os.path.join(tmp, "kapsl.sock")
+    proc = mp.get_context("spawn").Process(target=_cpu_server, daemon=True, args=(
+        gguf, sock, args.num_requests, args.chunk, args.max_prompt + args.output_len + 16, args.output_len))
+    proc.start()
+    t_wait = time.perf_counter()
+    while not os.path.exists(sock):
+        if not proc.is_alive() or time.perf_counter() - t_wait > 300:
+            raise SystemExit(f"CPU server did not come up (exit code {proc.exitcode})")
+        time.sleep(0.1)
+
+    def one_pass(seed: int):
+        prompts = make_workload(args, cfg.vocab_size, seed=seed)
+        stats = [None] * len(prompts)
+
+        def run(i):
+            c = KapslClient(sock)
+            data = np.asarray(prompts[i], dtype=np.int32).tobytes()
+            t0 = time.perf_counter()
+            times = []
+            for _ in c.infer_stream(0, [1, len(prompts[i])], "int32", data):
+                times.append(time.perf_counter())
+            stats[i] = (t0, times)
+
+        th = [threading.Thread(target=run, args=(i,)) for i in range(len(prompts))]
+        t0 = time.perf_counter()
+        for t in th:
+            t.start()
+        for t in th:
+            t.join()
+        return time.perf_counter() - t0, stats
+
+    try:
+        for i in range(args.warmup):
+            one_pass(1000 + i)
+        walls, all_stats = [], []
+        for i in range(args.steps):
+            w, st = one_pass(1 + i)  # the first timed pass uses the workload's seed 1
+            walls.append(w)
+            all_stats.extend(st)
+    finally:
+        proc.terminate()
+        proc.join(10)
+    tokens = sum(len(t) for _, t in all_stats)
+    wall = sum(walls)
+    ttft = statistics.median([t[0] - t0 for t0, t in all_stats])
+    tpot = statistics.median([(t[-1] - t[0]) / (len(t) - 1) for _, t in all_stats if len(t) > 1])
+    print(json.dumps({
+        "metric": METRIC, "value": round(tokens / wall, 2), "unit": "output tokens/s", "n_gpus": 0,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(wall / args.steps * 1000, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic token ids (seed 1), random-init weights N(0,0.02) seed 0, f32 GGUF",
+        "config": {"model": "tiny-Llama (4 layers, d 512, 8/8 heads of 64, FFN 1408, vocab 32000)",
+                   "global_batch": args.num_requests, "seq_len": f"{args.max_prompt} prompt + {args.output_len} out",
+                   "parallelism": "cpu", "kv_block": 16, "timing": "host clock, client side",
+                   "api": "KapslClient.infer_stream over a Unix socket (token-id prompts), server in its own process"},
+        "p50_ttft_ms": round(ttft * 1000, 2), "p50_tpot_ms": round(tpot * 1000, 3),
+        "e2e": {"value": round(tokens / wall, 2), "unit": "output tokens/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0, "api": "KapslClient.infer_stream"},
+        "gpu_launches": 0}))
     return 0
 
 

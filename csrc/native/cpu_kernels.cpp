@@ -1,0 +1,211 @@
+// fp32 CPU kernels of the CPU backend (see cpu_kernels.h), parallel over a
+// small persistent thread pool.
+//
+// Reference counterpart: crates/kapsl-kernels/src/attention/mod.rs:8-99 (naive
+// f32 attention without a block table) and src/mlp/mod.rs:7-49 (SwiGLU); the
+// reference runs everything else inside ONNX Runtime.  Here attention reads
+// the paged KV cache directly through the block table with an online
+// softmax (one pass over the keys), parallel over (query row, head).
+#include "cpu_kernels.h"
+
+#include <algorithm>
+#include <cmath>
+#include <condition_variable>
+#include <functional>
+#include <mutex>
+#include <thread>
+#include <vector>
+
+namespace kapsl {
+namespace cpu {
+
+namespace {
+
+// Persistent worker threads; parallel_for splits [0, n) into one contiguous
+// range per thread (the calling thread takes the first).  Small ranges run
+// inline.  (`#pragma omp simd` still vectorises the inner loops.)
+class Pool {
+ public:
+  static Pool& get() {
+    static Pool p;
+    return p;
+  }
+  void run(int64_t n, int64_t min_per_thread, const std::function<void(int64_t, int64_t)>& fn) {
+    const int64_t want = std::min<int64_t>((int64_t)workers_.size() + 1, std::max<int64_t>(1, n / min_per_thread));
+    if (want <= 1) {
+      fn(0, n);
+      return;
+    }
+    std::unique_lock<std::mutex> call(call_mu_);  // one parallel region at a time
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      fn_ = &fn;
+      n_ = n;
+      parts_ = want;
+      pending_ = (int)want - 1;
+      ++gen_;
+    }
+    cv_.notify_all();
+    fn(0, chunk(0));
+    std::unique_lock<std::mutex> lk(mu_);
+    done_cv_.wait(lk, [&] { return pending_ == 0; });
+  }
+
+ private:
+  Pool() {
+    const unsigned hc = std::max(1u, std::thread::hardware_concurrency());
+    for (unsigned i = 1; i < hc; ++i) workers_.emplace_back([this, i] { loop((int)i); });
+  }
+  ~Pool() {
+    {
+      std::lock_guard<std::mutex> lk(mu_);
+      stop_ = true;
+    }
+    cv_.notify_all();
+    for (auto& t : workers_) t.join();
+  }
+  int64_t chunk(int64_t part) const { return std::min(n_, (n_ * (part + 1) + parts_ - 1) / parts_); }
+  void loop(int id) {
+    uint64_t seen = 0;
+    while (true) {
+      const std::function<void(int64_t, int64_t)>* fn;
+      int64_t b, e;
+      {
+        std::unique_lock<std::mutex> lk(mu_);
+        cv_.wait(lk, [&] { return stop_ || gen_ != seen; });
+        if (stop_) return;
+        seen = gen_;
+        if (id >= parts_) continue;
+        fn = fn_;
+        b = (n_ * id + parts_ - 1) / parts_;
+        e = std::min(n_, (n_ * (id + 1) + parts_ - 1) / parts_);
+      }
+      if (b < e) (*fn)(b, e);
+      std::lock_guard<std::mutex> lk(mu_);
+      if (--pending_ == 0) done_cv_.notify_one();
+    }
+  }
+  std::vector<std::thread> workers_;
+  std::mutex mu_, call_mu_;
+  std::condition_variable cv_, done_cv_;
+  const std::function<void(int64_t, int64_t)>* fn_ = nullptr;
+  int64_t n_ = 0, parts_ = 1;
+  int pending_ = 0;
+  uint64_t gen_ = 0;
+  bool stop_ = false;
+};
+
+template <class F>
+void parallel_for(int64_t n, int64_t min_per_thread, F&& body) {
+  const std::function<void(int64_t, int64_t)> fn = [&](int64_t b, int64_t e) {
+    for (int64_t i = b; i < e; ++i) body(i);
+  };
+  Pool::get().run(n, min_per_thread, fn);
+}
+
+}  // namespace
+
+void rmsnorm(const float* x, const float* w, float* out, int64_t rows, int64_t d, float eps) {
+  parallel_for(rows, 4, [&](int64_t r) {
+    const float* xr = x + r * d;
+    float* o = out + r * d;
+    double ss = 0.0;
+#pragma omp simd reduction(+ : ss)
+    for (int64_t i = 0; i < d; ++i) ss += (double)xr[i] * xr[i];
+    const float inv = 1.0f / std::sqrt((float)(ss / (double)d) + eps);
+#pragma omp simd
+    for (int64_t i = 0; i < d; ++i) o[i] = xr[i] * inv * w[i];
+  });
+}
+
+void rope(float* x, const int64_t* pos, const float* cos_sin, int64_t T, int64_t H, int64_t D) {
+  const int64_t half = D / 2;
+  parallel_for(T * H, 16, [&](int64_t th) {
+    {
+      const int64_t t = th / H, h = th % H;
+      const float* c = cos_sin + pos[t] * D;
+      const float* s = c + half;
+      float* v = x + (t * H + h) * D;
+#pragma omp simd
+      for (int64_t i = 0; i < half; ++i) {
+        const float a = v[i], b = v[i + half];
+        v[i] = a * c[i] - b * s[i];
+        v[i + half] = b * c[i] + a * s[i];
+      }
+    }
+  });
+}
+
+void kv_write(const float* k, const float* v, const int64_t* slots, float* k_cache, float* v_cache, int64_t T,
+              int64_t Hkv, int64_t bs, int64_t D) {
+  parallel_for(T * Hkv, 64, [&](int64_t th) {
+    {
+      const int64_t t = th / Hkv, h = th % Hkv;
+      const int64_t slot = slots[t];
+      if (slot < 0) return;
+      const int64_t blk = slot / bs, off = slot % bs;
+      const int64_t dst = ((blk * Hkv + h) * bs + off) * D;
+      std::copy(k + (t * Hkv + h) * D, k + (t * Hkv + h + 1) * D, k_cache + dst);
+      std::copy(v + (t * Hkv + h) * D, v + (t * Hkv + h + 1) * D, v_cache + dst);
+    }
+  });
+}
+
+void paged_attention(const float* q, const float* k_cache, const float* v_cache, const int64_t* row0,
+                     const int64_t* nq, const int64_t* ctx, const int32_t* block_tables, int64_t max_blocks,
+                     int64_t num_seqs, int64_t Hq, int64_t Hkv, int64_t bs, int64_t D, float scale, float* out) {
+  // work items: (sequence, query index, head)
+  std::vector<int64_t> seq_of_row, qi_of_row;
+  for (int64_t s = 0; s < num_seqs; ++s)
+    for (int64_t i = 0; i < nq[s]; ++i) {
+      seq_of_row.push_back(s);
+      qi_of_row.push_back(i);
+    }
+  const int64_t rows = (int64_t)seq_of_row.size();
+  const int64_t group = Hq / Hkv;
+  parallel_for(rows * Hq, 1, [&](int64_t rh) {
+    const int64_t r = rh / Hq, h = rh % Hq;
+    float acc[512];  // D <= 512
+    const int64_t s = seq_of_row[r], i = qi_of_row[r];
+    const int64_t row = row0[s] + i;
+    const int64_t limit = ctx[s] - nq[s] + i + 1;  // keys [0, limit) are visible
+    const int64_t kvh = h / group;
+    const float* qv = q + (row * Hq + h) * D;
+    const int32_t* bt = block_tables + s * max_blocks;
+    float m = -INFINITY, l = 0.f;
+    std::fill(acc, acc + D, 0.f);
+    for (int64_t j = 0; j < limit; ++j) {
+      const int64_t base = (((int64_t)bt[j / bs] * Hkv + kvh) * bs + j % bs) * D;
+      const float* kv = k_cache + base;
+      float dot = 0.f;
+#pragma omp simd reduction(+ : dot)
+      for (int64_t e = 0; e < D; ++e) dot += qv[e] * kv[e];
+      const float sc = dot * scale;
+      const float mn = std::max(m, sc);
+      const float corr = std::exp(m - mn);  // exp(-inf) = 0 on the first key
+      const float p = std::exp(sc - mn);
+      l = l * corr + p;
+      const float* vv = v_cache + base;
+#pragma omp simd
+      for (int64_t e = 0; e < D; ++e) acc[e] = acc[e] * corr + p * vv[e];
+      m = mn;
+    }
+    float* o = out + (row * Hq + h) * D;
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma omp simd
+    for (int64_t e = 0; e < D; ++e) o[e] = acc[e] * inv;
+  });
+}
+
+void silu_mul(const float* x, float* out, int64_t T, int64_t F) {
+  parallel_for(T, 1, [&](int64_t t) {
+    const float* g = x + t * 2 * F;
+    const float* u = g + F;
+    float* o = out + t * F;
+#pragma omp simd
+    for (int64_t j = 0; j < F; ++j) o[j] = g[j] / (1.f + std::exp(-g[j])) * u[j];
+  });
+}
+
+}  // namespace cpu
+}  // namespace kapsl

@@ -1,0 +1,34 @@
+// fp32 CPU kernels of the CPU backend (threads over rows / heads, inner loops
+// written for the compiler's vectoriser).  Matrix products stay with the BLAS that
+// PyTorch links; everything between them runs here.
+#pragma once
+#include <cstdint>
+
+namespace kapsl {
+namespace cpu {
+
+// out[t] = x[t] * rsqrt(mean(x[t]^2) + eps) * w      (out may alias x)
+void rmsnorm(const float* x, const float* w, float* out, int64_t rows, int64_t d, float eps);
+
+// Rotate-half RoPE in place on x [T, H, D]; cos_sin [max_pos, D] holds cos in
+// the first half and sin in the second.
+void rope(float* x, const int64_t* pos, const float* cos_sin, int64_t T, int64_t H, int64_t D);
+
+// Write K/V rows [T, Hkv, D] into paged caches [blocks, Hkv, bs, D] at flat
+// slots (block * bs + offset); slots < 0 are skipped.
+void kv_write(const float* k, const float* v, const int64_t* slots, float* k_cache, float* v_cache, int64_t T,
+              int64_t Hkv, int64_t bs, int64_t D);
+
+// Causal attention over paged KV for a batch of sequences.  Sequence s owns
+// query rows [row0[s], row0[s] + nq[s]) whose KV length is ctx[s] (the queries
+// are the last nq[s] positions); its pages are block_tables[s * max_blocks ...].
+// D <= 512.
+void paged_attention(const float* q, const float* k_cache, const float* v_cache, const int64_t* row0,
+                     const int64_t* nq, const int64_t* ctx, const int32_t* block_tables, int64_t max_blocks,
+                     int64_t num_seqs, int64_t Hq, int64_t Hkv, int64_t bs, int64_t D, float scale, float* out);
+
+// out[t, j] = silu(x[t, j]) * x[t, F + j]
+void silu_mul(const float* x, float* out, int64_t T, int64_t F);
+
+}  // namespace cpu
+}  // namespace kapsl

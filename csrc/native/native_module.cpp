@@ -1,10 +1,12 @@
 // Python bindings of the C++ runtime (module kapsl_sdk_b200._native):
 // bincode wire codec, paged-KV block allocator, shared-memory transport and
 // the socket / SHM servers.
+#include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 #include <pybind11/stl.h>
 
 #include "block_alloc.h"
+#include "cpu_kernels.h"
 #include "server.h"
 #include "shm.h"
 #include "wire.h"
@@ -67,7 +69,56 @@ py::dict hybrid_req_to_py(const wire::HybridRequest& h) {
 
 }  // namespace
 
+namespace {
+using F32 = py::array_t<float, py::array::c_style>;
+using I64 = py::array_t<int64_t, py::array::c_style>;
+using I32 = py::array_t<int32_t, py::array::c_style>;
+
+void need(bool ok, const char* msg) {
+  if (!ok) throw std::invalid_argument(msg);
+}
+
+void cpu_module(py::module_& m) {
+  auto c = m.def_submodule("cpu", "fp32 CPU kernels of the CPU backend");
+  c.def("rmsnorm", [](F32 x, F32 w, F32 out, float eps) {
+    need(x.ndim() == 2 && out.size() == x.size() && w.size() == x.shape(1), "rmsnorm: x [T, d], w [d], out like x");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::rmsnorm(x.data(), w.data(), out.mutable_data(), x.shape(0), x.shape(1), eps);
+  });
+  c.def("rope", [](F32 x, I64 pos, F32 cos_sin) {
+    need(x.ndim() == 3 && pos.size() == x.shape(0) && cos_sin.ndim() == 2 && cos_sin.shape(1) == x.shape(2),
+         "rope: x [T, H, D], positions [T], cos_sin [max_pos, D]");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::rope(x.mutable_data(), pos.data(), cos_sin.data(), x.shape(0), x.shape(1), x.shape(2));
+  });
+  c.def("kv_write", [](F32 k, F32 v, I64 slots, F32 kc, F32 vc) {
+    need(k.ndim() == 3 && kc.ndim() == 4 && kc.shape(1) == k.shape(1) && kc.shape(3) == k.shape(2) &&
+             slots.size() == k.shape(0) && v.size() == k.size() && vc.size() == kc.size(),
+         "kv_write: k/v [T, Hkv, D], caches [blocks, Hkv, bs, D]");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::kv_write(k.data(), v.data(), slots.data(), kc.mutable_data(), vc.mutable_data(), k.shape(0),
+                         k.shape(1), kc.shape(2), k.shape(2));
+  });
+  c.def("paged_attention", [](F32 q, F32 kc, F32 vc, I64 row0, I64 nq, I64 ctx, I32 bt, float scale, F32 out) {
+    need(q.ndim() == 3 && kc.ndim() == 4 && bt.ndim() == 2 && out.size() == q.size() && q.shape(2) <= 512,
+         "paged_attention: shapes (head_dim <= 512)");
+    need(row0.size() == nq.size() && nq.size() == ctx.size() && bt.shape(0) >= row0.size(),
+         "paged_attention: per-sequence arrays differ");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::paged_attention(q.data(), kc.data(), vc.data(), row0.data(), nq.data(), ctx.data(), bt.data(),
+                                bt.shape(1), row0.size(), q.shape(1), kc.shape(1), kc.shape(2), q.shape(2), scale,
+                                out.mutable_data());
+  });
+  c.def("silu_mul", [](F32 x, F32 out) {
+    need(x.ndim() == 2 && x.shape(1) % 2 == 0 && out.size() == x.size() / 2, "silu_mul: x [T, 2F], out [T, F]");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::silu_mul(x.data(), out.mutable_data(), x.shape(0), x.shape(1) / 2);
+  });
+}
+}  // namespace
+
 PYBIND11_MODULE(_native, m) {
+  cpu_module(m);
   m.doc() = "kapsl_sdk_b200 C++ runtime: wire codec, block allocator, SHM transport, servers";
 
   static py::object out_of_blocks;  // Python class kapsl_sdk_b200.llm.block_manager.OutOfBlocks

@@ -30,6 +30,8 @@ import uuid
 from dataclasses import dataclass, field, replace
 from typing import Iterator, Optional
 
+import numpy as np
+
 from ..engine_api import (BinaryTensorPacket, Engine, EngineError, EngineMetrics, EngineModelInfo,
                           InferenceRequest, TensorDtype)
 from .sequence import SamplingParams
@@ -274,17 +276,26 @@ class LLMBackend(Engine):
         return s
 
     def infer_stream(self, request: InferenceRequest) -> Iterator[BinaryTensorPacket]:
+        """Utf8 input -> streamed text deltas (the reference's behaviour).  An int32 or
+        int64 input is taken as prompt token ids (no template, no BOS) and the
+        stream carries each new token id as an int32 [1, 1] packet; the
+        reference accepts text only."""
         if self.engine is None:
             raise EngineError.model_not_loaded()
-        if request.input.dtype is not TensorDtype.UTF8:
-            raise EngineError.invalid_input("LLM backend expects Utf8 input")
-        try:
-            prompt = request.input.data.decode("utf-8")
-        except UnicodeDecodeError:
-            raise EngineError.invalid_input("Invalid UTF-8 input")
-        if self.rc.use_chat_template:
-            prompt = f"{self.rc.prompt_prefix}{prompt}{self.rc.prompt_suffix}"
-        ids = self.tokenizer.encode(prompt, add_bos=self.rc.add_bos)
+        as_ids = request.input.dtype in (TensorDtype.INT32, TensorDtype.INT64)
+        if as_ids:
+            ids = np.frombuffer(request.input.data, dtype=np.int32 if request.input.dtype is TensorDtype.INT32
+                                else np.int64).astype(np.int64).tolist()
+        else:
+            if request.input.dtype is not TensorDtype.UTF8:
+                raise EngineError.invalid_input("LLM backend expects Utf8 input")
+            try:
+                prompt = request.input.data.decode("utf-8")
+            except UnicodeDecodeError:
+                raise EngineError.invalid_input("Invalid UTF-8 input")
+            if self.rc.use_chat_template:
+                prompt = f"{self.rc.prompt_prefix}{prompt}{self.rc.prompt_suffix}"
+            ids = self.tokenizer.encode(prompt, add_bos=self.rc.add_bos)
         if not ids:
             raise EngineError.invalid_input("empty prompt")
         rid = (request.metadata.request_id if request.metadata and request.metadata.request_id else None) \
@@ -292,7 +303,28 @@ class LLMBackend(Engine):
         p = _Pending(rid, ids, self._params_for(request), request.session_id, request.cancellation)
         self._stats["requests"] += 1
         self._inbox.put(p)
-        return self._stream(p)
+        return self._stream_ids(p) if as_ids else self._stream(p)
+
+    def _stream_ids(self, p: _Pending) -> Iterator[BinaryTensorPacket]:
+        finished = False
+        try:
+            while True:
+                item = p.out.get()
+                if isinstance(item, EngineError):
+                    self._stats["errors"] += 1
+                    raise item
+                tok, done, reason = item
+                yield BinaryTensorPacket([1, 1], TensorDtype.INT32, np.int32(tok).tobytes())
+                if done:
+                    finished = True
+                    return
+        finally:
+            if not finished and p.cancel is None:
+                from ..engine_api import CancellationToken
+
+                tok = CancellationToken()
+                tok.cancel()
+                p.cancel = tok
 
     def _stream(self, p: _Pending) -> Iterator[BinaryTensorPacket]:
         toks: list = []

@@ -13,8 +13,10 @@ llama.cpp instead.
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
+import numpy as np
 import torch
 
 from ..ops import reference as ref
@@ -41,6 +43,14 @@ class CPUCausalLM:
         self.hq, self.hkv, self.D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         self.scale = 1.0 / math.sqrt(self.D)
         self.device = torch.device("cpu")
+        self._k = None  # C++ CPU kernels (kapsl_sdk_b200._native.cpu) when built
+        if os.environ.get("KAPSL_CPU_KERNELS", "native") == "native":
+            try:
+                from .._ext import native
+
+                self._k = native().cpu
+            except Exception:
+                self._k = None
 
     @classmethod
     def random(cls, cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> "CPUCausalLM":
@@ -53,6 +63,8 @@ class CPUCausalLM:
                 k_caches: list, v_caches: list, logits_rows: list) -> torch.Tensor:
         """``seqs``: list of (row_start, n_tokens, ctx_len, block_ids) per sequence;
         returns fp32 logits for ``logits_rows``."""
+        if self._k is not None:
+            return self._forward_native(ids, positions, slots, seqs, k_caches, v_caches, logits_rows)
         cfg = self.cfg
         T = ids.numel()
         D, hq, hkv = self.D, self.hq, self.hkv
@@ -84,6 +96,51 @@ class CPUCausalLM:
                 gu = x @ L["gate_up"].T
                 h = h + ref.silu_mul(gu) @ L["down"].T
         xs, _ = ref.rmsnorm(h[logits_rows], self.final_norm, cfg.rms_eps)
+        return xs @ self.lm_head.T
+
+    def _forward_native(self, ids, positions, slots, seqs, k_caches, v_caches, logits_rows) -> torch.Tensor:
+        """Same computation with the C++ CPU kernels between the BLAS matmuls."""
+        k_ = self._k
+        cfg = self.cfg
+        T = ids.numel()
+        D, hq, hkv = self.D, self.hq, self.hkv
+        h = self.embed[ids.long()].contiguous()
+        pos = positions.to(torch.int64).contiguous().numpy()
+        sl = slots.to(torch.int64).contiguous().numpy()
+        row0 = np.array([r for r, _, _, _ in seqs], dtype=np.int64)
+        nq = np.array([n for _, n, _, _ in seqs], dtype=np.int64)
+        ctx = np.array([c for _, _, c, _ in seqs], dtype=np.int64)
+        mb = max(len(b) for _, _, _, b in seqs)
+        bt = np.zeros((len(seqs), mb), dtype=np.int32)
+        for i, (_, _, _, b) in enumerate(seqs):
+            bt[i, :len(b)] = b
+        cs = self.cos_sin.numpy()
+        x = torch.empty_like(h)
+        attn = torch.empty(T, hq, D)
+        for li, L in enumerate(self.layers):
+            k_.rmsnorm(h.numpy(), L["in_norm"].numpy(), x.numpy(), cfg.rms_eps)
+            qkv = x @ L["qkv"].T
+            if L["qkv_b"] is not None:
+                qkv += L["qkv_b"]
+            q = qkv[:, :hq * D].contiguous().view(T, hq, D)
+            kk = qkv[:, hq * D:(hq + hkv) * D].contiguous().view(T, hkv, D)
+            vv = qkv[:, (hq + hkv) * D:].contiguous().view(T, hkv, D)
+            k_.rope(q.numpy(), pos, cs)
+            k_.rope(kk.numpy(), pos, cs)
+            kc, vc = k_caches[li], v_caches[li]
+            k_.kv_write(kk.numpy(), vv.numpy(), sl, kc.numpy(), vc.numpy())
+            k_.paged_attention(q.numpy(), kc.numpy(), vc.numpy(), row0, nq, ctx, bt, self.scale, attn.numpy())
+            h += attn.view(T, hq * D) @ L["o"].T
+            k_.rmsnorm(h.numpy(), L["post_norm"].numpy(), x.numpy(), cfg.rms_eps)
+            if cfg.is_moe:
+                h += self._moe(x, L)
+            else:
+                gu = x @ L["gate_up"].T
+                act = torch.empty(T, gu.shape[1] // 2)
+                k_.silu_mul(gu.numpy(), act.numpy())
+                h += act @ L["down"].T
+        xs = h[logits_rows].contiguous()
+        k_.rmsnorm(xs.numpy(), self.final_norm.numpy(), xs.numpy(), cfg.rms_eps)
         return xs @ self.lm_head.T
 
     def _moe(self, x: torch.Tensor, L: dict) -> torch.Tensor:

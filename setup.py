@@ -56,13 +56,13 @@ def native_extensions():
             "kapsl_sdk_b200._native",
             native_src,
             include_dirs=[os.path.join(ROOT, "csrc", "native")],
-            extra_compile_args=CXX_FLAGS + ["-pthread"],
+            extra_compile_args=CXX_FLAGS + ["-pthread", "-fopenmp-simd", "-mavx2", "-mfma"],
             extra_link_args=["-pthread", "-lrt"],
             cxx_std=17,
         ))
     sdk_src = _rel(glob.glob(os.path.join(ROOT, "csrc", "sdk", "*.cpp")))
     if sdk_src:
-        wire = [s for s in native_src if os.path.basename(s) in ("wire.cpp", "shm.cpp")]
+        wire = [s for s in native_src if os.path.basename(s) in ("wire.cpp", "shm.cpp")]  # the SDK needs no CPU kernels
         exts.append(Pybind11Extension(
             "kapsl_sdk.kapsl_sdk",
             sdk_src + wire,

@@ -89,6 +89,10 @@ def test_backend_stream_over_unix_socket():
         assert direct == again
         with pytest.raises(RuntimeError, match="expects Utf8"):
             c.infer(0, [1], "float32", b"\0\0\0\0")
+        # token-id prompts stream one int32 token per packet
+        ids = np.array([5, 9, 13, 40], dtype=np.int32)
+        toks = [np.frombuffer(b, np.int32)[0] for b in c.infer_stream(0, [1, 4], "int32", ids.tobytes())]
+        assert 1 <= len(toks) <= backend.rc.sampling.max_new_tokens and all(0 <= t < cfg.vocab_size for t in toks)
         assert backend.health_check()
         m = backend.metrics()
         assert m.kv_cache_blocks_total == 64
