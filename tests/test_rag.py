@@ -1,0 +1,135 @@
+"""RAG: connector JSON-lines protocol, a sidecar connector installed as an
+extension, ingestion into the SQLite vector store, ACL-filtered queries and
+prompt assembly."""
+import base64
+import json
+import os
+import sys
+import textwrap
+
+import pytest
+
+from kapsl_sdk_b200 import rag
+from kapsl_sdk_b200.rag import protocol as P
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+CONNECTOR = textwrap.dedent("""
+    import base64, os, sys
+    sys.path.insert(0, {root!r})
+    from kapsl_sdk_b200.rag import Connector, ConnectorError, serve_stdio
+    from kapsl_sdk_b200.rag.protocol import DocumentDelta, DocumentPayload, ExternalAcl, SourceDescriptor
+    DOCS = {{
+        "a": ("The B200 has 148 SMs and 180 GB of HBM3e memory.", ExternalAcl()),
+        "b": ("NVLink 5 gives 900 GB/s per direction per GPU.", ExternalAcl(allow_groups=["eng"])),
+        "c": ("Secret roadmap text that only admins may read.", ExternalAcl(allow_users=["alice"],
+                                                                            deny_groups=["contractors"])),
+    }}
+    class Docs(Connector):
+        def validate_config(self, config):
+            if not isinstance(config, dict) or "root" not in config:
+                raise ConnectorError("invalid input", "config needs 'root'")
+        def list_sources(self, config):
+            return [SourceDescriptor("kb", "Knowledge base", "folder", {{"owner": os.environ.get("OWNER", "")}})]
+        def sync(self, source_id, cursor):
+            return [DocumentDelta(k, "upsert", None, None, {{"source": "kb", "title": "doc-" + k}}, acl)
+                    for k, (_, acl) in DOCS.items()]
+        def fetch_document(self, document_id):
+            text, acl = DOCS[document_id]
+            return DocumentPayload(document_id, "text/plain", base64.b64encode(text.encode()).decode(),
+                                   {{"source": "kb", "title": "doc-" + document_id}}, acl)
+    serve_stdio(Docs())
+""")
+
+
+def test_protocol_encoding():
+    line = P.encode_request("1", "Sync", {"source_id": "s", "cursor": None})
+    assert json.loads(line) == {"id": "1", "method": "Sync", "params": {"source_id": "s", "cursor": None}}
+    assert json.loads(P.encode_request("2", "Health")) == {"id": "2", "method": "Health"}
+    assert json.loads(P.encode_ok("3", "Unit")) == {"id": "3", "status": "Ok", "result": {"type": "Unit"}}
+    assert P.decode_response(P.encode_ok("4", "Health", "ok")) == ("4", "Health", "ok")
+    with pytest.raises(P.ConnectorRemoteError, match="boom"):
+        P.decode_response(P.encode_err("5", "boom"))
+    with pytest.raises(ValueError):
+        P.encode_request("6", "Nope")
+
+
+def test_sidecar_extension_ingest_query_prompt(tmp_path):
+    src = tmp_path / "src"
+    src.mkdir()
+    (src / "connector.py").write_text(CONNECTOR.format(root=ROOT))
+    (src / "manifest.json").write_text(json.dumps({
+        "id": "docs", "name": "Docs", "version": "0.1.0", "runtime": "sidecar", "capabilities": ["sync"],
+        "auth": ["none"], "permissions": [], "entrypoint": "connector.py"}))
+    reg = rag.ExtensionRegistry(str(tmp_path / "ext"))
+    reg.install_from_dir(str(src))
+    assert [e.id for e in reg.discover()] == ["docs"]
+    mgr = rag.ExtensionManager(reg, str(tmp_path / "cfg"))
+    mgr.set_workspace_config("ws1", "docs", {"root": "/data", "env": {"OWNER": "team"}})
+    assert mgr.list_configs("ws1") == ["docs"]
+    client = mgr.launch_connector("ws1", "docs")
+    try:
+        assert client.health() == "ok"
+        client.validate_config({"root": "/data"})
+        with pytest.raises(P.ConnectorRemoteError, match="invalid input"):
+            client.validate_config({})
+        with pytest.raises(P.ConnectorRemoteError, match="unsupported operation"):
+            client.transform_prompt({}, "hi")
+        (source,) = client.list_sources({"root": "/data"})
+        assert source.id == "kb" and source.metadata["owner"] == "team"
+        deltas = client.sync("kb")
+        store = rag.SqliteVectorStore(str(tmp_path / "v.db"))
+        pipe = rag.IngestionPipeline(rag.PlainTextParser(), rag.SimpleChunker(6, 2), rag.HashEmbedder(128), store)
+        ctx = rag.IngestionContext("t", "ws1", "kb")
+        docs = rag.FsDocStore(str(tmp_path / "docs"))
+        n = 0
+        for d in deltas:
+            payload = client.fetch_document(d.id)
+            docs.put(rag.DocKey("t", "ws1", "kb", d.id), base64.b64decode(payload.bytes_b64))
+            n += pipe.ingest(ctx, payload)
+        assert n >= 3
+        assert docs.get(rag.DocKey("t", "ws1", "kb", "a")).startswith(b"The B200")
+    finally:
+        client.shutdown()
+
+    emb = rag.HashEmbedder(128)
+    q = emb.embed(["HBM3e memory SMs"])[0]
+    anon = store.query(rag.VectorQuery(q, 10, "t", "ws1"))
+    assert {r.chunk.doc_id for r in anon} == {"a"}  # b needs group eng, c needs alice
+    eng = store.query(rag.VectorQuery(q, 10, "t", "ws1", allowed_groups=["eng"]))
+    assert {r.chunk.doc_id for r in eng} == {"a", "b"}
+    alice = store.query(rag.VectorQuery(q, 10, "t", "ws1", allowed_users=["alice"]))
+    assert "c" in {r.chunk.doc_id for r in alice}
+    contractor = store.query(rag.VectorQuery(q, 10, "t", "ws1", allowed_users=["alice"],
+                                             allowed_groups=["contractors"]))
+    assert "c" not in {r.chunk.doc_id for r in contractor}
+    assert anon[0].score >= anon[-1].score and anon[0].chunk.doc_id == "a"
+    assert store.query(rag.VectorQuery(q, 10, "other", "ws1")) == []
+
+    chunks = [rag.RagChunk(r.chunk.id, r.chunk.text, r.score, r.chunk.metadata) for r in eng]
+    p = rag.build_rag_prompt(chunks, rag.RagPromptConfig(max_per_source=2))
+    assert p.context.startswith("[1] ") and "Source: doc-" in p.context and len(p.citations) == 2
+
+
+def test_prompt_rules():
+    C = rag.RagChunk
+    chunks = [C("x1", "alpha beta gamma", 0.9, {"source": "s1"}), C("x2", "Alpha  BETA gamma", 0.8, {"source": "s2"}),
+              C("x3", "delta epsilon", 0.7, {"source": "s1"}), C("x4", "zeta eta theta", 0.6, {"source": "s1"}),
+              C("x5", "low", -1.0, {})]
+    p = rag.build_rag_prompt(chunks, rag.RagPromptConfig(max_context_tokens=4, max_per_source=2))
+    assert [c.chunk_id for c in p.citations] == ["x1", "x3"]  # x2 duplicate text, x4 over the per-source cap
+    assert p.context == "[1] alpha beta gamma\nSource: s1\n\n[2] delta\nSource: s1"
+    assert p.truncated and p.total_context_tokens == 4
+    q = rag.build_rag_prompt(chunks[:1], rag.RagPromptConfig(citation_style="inline"))
+    assert q.context == "alpha beta gamma (1)\nSource: s1"
+    e = rag.build_rag_prompt([chunks[-1]])
+    assert e.context == "" and e.fallback_message == "No relevant documents found."
+
+
+def test_chunker_and_wasm_runtime():
+    doc = rag.ParsedDocument("d", " ".join(str(i) for i in range(10)))
+    cs = rag.SimpleChunker(4, 1).chunk(doc)
+    assert [c.text for c in cs] == ["0 1 2 3", "3 4 5 6", "6 7 8 9"] and cs[1].id == "d:1"
+    assert cs[2].metadata["chunk_index"] == "2"
+    with pytest.raises(RuntimeError, match="WASM"):
+        rag.WasmRuntime()
