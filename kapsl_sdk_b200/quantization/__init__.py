@@ -7,7 +7,8 @@
 * :func:`quantize_q4_k` / :func:`dequantize_q4_k` — GPU quantizer (same
   rounding steps as :func:`kapsl_sdk_b200.loaders.gguf.quantize_q4_k`) and
   dequantizer.
-* :mod:`.safetensors_loaders` — GPTQ / AWQ / INT8 checkpoint readers.
+* :mod:`.safetensors_loaders` — GPTQ / AWQ / INT8 checkpoint readers with the
+  dequantization math.
 
 Reference counterpart: crates/kapsl-quantization (config.rs:3-30,
 tensor.rs:4-35, loader/*.rs) parses GPTQ/AWQ/INT8 tensors but has no dequant
