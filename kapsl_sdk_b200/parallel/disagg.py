@@ -307,8 +307,10 @@ class Disaggregated:
         if self.role == "prefill":
             self.conn = KVConnector(self.engine.pool, self.role, self.gi, self.store, ns, mode)
 
-    def serve(self, prompts: list, params: SamplingParams, timeout_s: float = 600.0):
-        """Returns (outputs, sequences) in prompt order on decode ranks, (None, None) on prefill ranks."""
+    def serve(self, prompts: list, params: SamplingParams, timeout_s: float = 600.0, health=None):
+        """Returns (outputs, sequences) in prompt order on decode ranks, (None, None) on prefill ranks.
+        ``health``: a started :class:`~kapsl_sdk_b200.parallel.health.HeartbeatMonitor`; it is
+        checked between steps, so a lost peer raises ``RankFailure`` here."""
         ns = f"{self.ns}/{self.passes}"
         self.passes += 1
         if self.role == "prefill":
@@ -320,6 +322,8 @@ class Disaggregated:
             w.stop()
         t0 = time.perf_counter()
         while w.poll_and_step():
+            if health is not None:
+                health.check()
             if time.perf_counter() - t0 > timeout_s:
                 raise TimeoutError(f"{self.role} rank {self.rank}: disaggregated serving did not finish "
                                    f"in {timeout_s} s")

@@ -1,0 +1,169 @@
+"""Failure detection with faults injected on the host (no GPU involved): a rank
+that dies, a rank that never joins a collective, corrupted and truncated
+frames and dropped connections at the socket server, and KV admission limits."""
+import os
+import socket
+import struct
+import subprocess
+import sys
+import tempfile
+import textwrap
+import time
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+HB_WORKER = textwrap.dedent("""
+    import os, sys, time
+    sys.path.insert(0, {root!r})
+    from datetime import timedelta
+    import torch.distributed as dist
+    from kapsl_sdk_b200.parallel.health import HeartbeatMonitor, RankFailure
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dist.init_process_group("gloo", timeout=timedelta(seconds=20))
+    store = dist.distributed_c10d._get_default_store()
+    hb = HeartbeatMonitor(store, rank, world, interval_s=0.2, timeout_s=2.0).start()
+    dist.barrier()
+    if rank == 2:
+        os._exit(17)  # crash between steps, no cleanup
+    t0 = time.time()
+    while True:  # the serving loop: one "step" per 50 ms, health check between steps
+        time.sleep(0.05)
+        try:
+            hb.check()
+        except RankFailure as e:
+            print("DETECTED", e.ranks, round(time.time() - t0, 2), flush=True)
+            break
+        if time.time() - t0 > 30:
+            print("MISSED", flush=True)
+            break
+    hb.stop()
+    os._exit(0)
+""")
+
+
+def _spawn(script: str, world: int, timeout: float = 60.0):
+    port = _port()
+    procs = [subprocess.Popen([sys.executable, "-c", script], stdout=subprocess.PIPE, stderr=subprocess.STDOUT,
+                              text=True, env=dict(os.environ, RANK=str(r), WORLD_SIZE=str(world),
+                                                  MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port)))
+             for r in range(world)]
+    outs = []
+    for p in procs:
+        try:
+            o, _ = p.communicate(timeout=timeout)
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            raise
+        outs.append((p.returncode, o))
+    return outs
+
+
+def test_dead_rank_is_detected_between_steps():
+    outs = _spawn(HB_WORKER.format(root=ROOT), 3)
+    assert outs[2][0] == 17
+    for rc, o in outs[:2]:
+        assert rc == 0 and "DETECTED [2]" in o, o[-2000:]
+        detect_s = float(o.split("DETECTED [2]")[1].split()[0])
+        assert detect_s < 10
+
+
+NOJOIN_WORKER = textwrap.dedent("""
+    import os, sys, time
+    from datetime import timedelta
+    import torch, torch.distributed as dist
+    rank = int(os.environ["RANK"])
+    dist.init_process_group("gloo", timeout=timedelta(seconds=3))
+    if rank == 1:
+        time.sleep(8)  # never joins the collective in time
+        os._exit(0)
+    t0 = time.time()
+    try:
+        dist.all_reduce(torch.ones(4))
+        print("NO_ERROR", flush=True)
+    except Exception as e:
+        print("RAISED", type(e).__name__, round(time.time() - t0, 1), flush=True)
+    os._exit(0)
+""")
+
+
+def test_collective_with_missing_rank_raises_instead_of_hanging():
+    outs = _spawn(NOJOIN_WORKER, 2)
+    assert "RAISED" in outs[0][1], outs[0][1][-2000:]
+    assert float(outs[0][1].split("RAISED")[1].split()[1]) < 8
+
+
+def test_server_survives_corrupted_truncated_and_dropped_requests():
+    from kapsl_sdk import KapslClient
+    from kapsl_sdk_b200.engine_api import BinaryTensorPacket, Engine, TensorDtype
+    from kapsl_sdk_b200.server import KapslServer
+
+    class Echo(Engine):
+        def infer(self, request):
+            return request.input
+
+        def load(self, path):
+            pass
+
+        def unload(self):
+            pass
+
+    d = tempfile.mkdtemp(prefix="kapsl-fd-")
+    path = os.path.join(d, "s.sock")
+    srv = KapslServer(models={0: Echo()}).listen_unix(path).start()
+    try:
+        def raw(payload: bytes, header=None):
+            s = socket.socket(socket.AF_UNIX)
+            s.connect(path)
+            s.sendall(header if header is not None else struct.pack("<III", 0, 1, len(payload)))
+            s.sendall(payload)
+            return s
+
+        # 1) garbage payload -> ERR frame, connection still usable by the server
+        s = raw(b"\xff" * 40)
+        hdr = s.recv(8)
+        status = struct.unpack("<II", hdr)[0] if len(hdr) == 8 else None
+        s.close()
+        assert status == 1
+        # 2) header announces more bytes than sent, then the client disconnects
+        s = raw(b"\x00" * 10, header=struct.pack("<III", 0, 1, 1000))
+        s.close()
+        # 3) connect and drop immediately
+        s = socket.socket(socket.AF_UNIX)
+        s.connect(path)
+        s.close()
+        time.sleep(0.2)
+        # the server keeps serving well-formed requests
+        c = KapslClient(path)
+        out = c.infer(0, [1, 4], "float32", np.arange(4, dtype=np.float32).tobytes())
+        assert np.frombuffer(out, np.float32).tolist() == [0, 1, 2, 3]
+    finally:
+        srv.stop()
+
+
+def test_kv_admission_limits():
+    from kapsl_sdk_b200.engine_api import EngineError
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.models.config import ModelConfig
+
+    cfg = ModelConfig(name="t", vocab_size=300, hidden_size=64, intermediate_size=128, num_layers=2, num_heads=4,
+                      num_kv_heads=2, head_dim=16, max_position=512)
+    eng = LLMEngine(cfg, device="cpu", engine_cfg=EngineConfig(max_num_seqs=4, max_num_batched_tokens=32,
+                    max_model_len=512, num_blocks=8), seed=0)  # 8 blocks x 16 tokens
+    with pytest.raises(EngineError) as e:
+        eng.add_request("big", list(range(3, 200)), SamplingParams(max_new_tokens=100), admission_control=True)
+    assert "ResourceExhausted" in type(e.value).__name__ or "hard limit" in str(e.value)
+    eng.add_request("a", list(range(3, 50)), SamplingParams(max_new_tokens=40), admission_control=True)
+    with pytest.raises(EngineError, match="soft limit"):
+        eng.add_request("b", list(range(3, 40)), SamplingParams(max_new_tokens=10), admission_control=True)
