@@ -112,6 +112,8 @@ class LLMEngine:
         # before their KV blocks go back to the allocator (the KV connector copies
         # them out on the same stream, so later reuse of the blocks is ordered after it).
         self.kv_export: Optional[Callable] = None
+        # KAPSL_NVTX=1: NVTX ranges per step and phase for Nsight timelines (GPU engines)
+        self._nvtx = os.environ.get("KAPSL_NVTX", "0") == "1" and self.device.type == "cuda"
         self.profile = None
         if os.environ.get("KAPSL_LLM_PROFILE", os.environ.get("KAPSL_LLM_PROFILE_DECODE", "0")) == "1":
             self.profile = {"steps": 0, "decode_steps": 0, "tokens": 0, "schedule_s": 0.0, "prepare_s": 0.0,
@@ -210,13 +212,26 @@ class LLMEngine:
     def step(self) -> list[StepOutput]:
         prof = self.profile is not None
         t0 = time.perf_counter() if prof else 0.0
+        nv = self._nvtx
+        if nv:
+            torch.cuda.nvtx.range_push("kapsl.step")
+            torch.cuda.nvtx.range_push("schedule")
         batch = self.scheduler.schedule()
+        if nv:
+            torch.cuda.nvtx.range_pop()
         if batch.empty:
+            if nv:
+                torch.cuda.nvtx.range_pop()
             return []
         if batch.admitted:
             self.runner.admit(batch.admitted)
         t1 = time.perf_counter() if prof else 0.0
+        if nv:
+            torch.cuda.nvtx.range_push(f"execute T={batch.num_tokens} decode={len(batch.decode)}")
         seqs, toks = self.runner.execute(batch)
+        if nv:
+            torch.cuda.nvtx.range_pop()
+            torch.cuda.nvtx.range_pop()
         now = time.perf_counter()
         if prof:
             p = self.profile

@@ -84,6 +84,16 @@ class KapslMetrics:
         return generate_latest(self.registry)
 
 
+def serve_metrics(metrics: KapslMetrics, port: int = 9100, addr: str = "127.0.0.1"):
+    """Expose ``metrics`` over HTTP (``GET /metrics``, Prometheus text format) from a
+    daemon thread; returns the HTTP server (``shutdown()`` to stop).  The reference
+    registers the same metrics but ships no exporter."""
+    from prometheus_client import start_http_server
+
+    server, _thread = start_http_server(port, addr=addr, registry=metrics.registry)
+    return server
+
+
 class MonitoringMiddleware(Engine):
     def __init__(self, inner: Engine, metrics: KapslMetrics, model: str = "model", version: str = "1"):
         self.inner = inner

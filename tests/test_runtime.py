@@ -322,3 +322,20 @@ def test_backend_factory_requirements():
     assert len(errs) == 3
     assert f.provider_chain(man.hardware_requirements) == ["cuda", "cpu"]
     assert BackendFactory(DeviceInfo(8, 64000, [])).provider_chain(man.hardware_requirements) == ["cpu"]
+
+
+def test_metrics_http_exporter():
+    import urllib.request
+
+    from kapsl_sdk_b200.monitor import KapslMetrics, serve_metrics
+
+    m = KapslMetrics()
+    m.out_tokens.labels("llm").inc(7)
+    m.ttft.labels("llm").observe(0.12)
+    srv = serve_metrics(m, port=0)
+    try:
+        port = srv.server_address[1]
+        body = urllib.request.urlopen(f"http://127.0.0.1:{port}/metrics", timeout=5).read().decode()
+        assert 'kapsl_output_tokens_total{model="llm"} 7.0' in body and "kapsl_ttft_seconds_bucket" in body
+    finally:
+        srv.shutdown()
