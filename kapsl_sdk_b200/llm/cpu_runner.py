@@ -61,8 +61,12 @@ class CPUModelRunner:
         ids, pos, slots, seqs, rows, sample = self._prepare(batch)
         self.last_prepare_s = time.perf_counter() - t0
         with torch.no_grad():
-            lg = self.model.forward(ids, pos, slots, seqs, self.pool.k, self.pool.v, rows).numpy()
+            out = self.model.forward(ids, pos, slots, seqs, self.pool.k, self.pool.v, rows)
         toks = np.zeros(len(sample), dtype=np.int64)
+        if out is None:  # an earlier pipeline stage: the last stage samples and broadcasts
+            self.stats["steps"] += 1
+            return sample, toks
+        lg = out.numpy()
         for r, s in enumerate(sample):
             p = s.params
             row = lg[r]

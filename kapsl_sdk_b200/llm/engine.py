@@ -57,17 +57,26 @@ class EngineConfig:
 
 class LLMEngine:
     def __init__(self, cfg: ModelConfig, weights: Optional[ModelWeights] = None, device="cuda",
-                 engine_cfg: Optional[EngineConfig] = None, tp_comm=None, moe=None, seed: int = 0):
+                 engine_cfg: Optional[EngineConfig] = None, tp_comm=None, moe=None, seed: int = 0, pp_stage=None):
+        """``pp_stage``: a :class:`~kapsl_sdk_b200.parallel.pp.PipelineStage`; the engine then
+        holds that stage's layers (and their KV pages) and steps in micro-batches."""
         self.cfg = cfg
         self.ecfg = engine_cfg or EngineConfig()
         self.device = torch.device(device)
+        self.pp = pp_stage
         e = self.ecfg
+        nlayers = len(pp_stage.layers) if pp_stage is not None else cfg.num_layers
         if self.device.type == "cpu":
             from ..models.cpu_model import CPUCausalLM
             from .cpu_runner import CPUModelRunner
 
-            self.model = weights if isinstance(weights, CPUCausalLM) else CPUCausalLM.random(cfg, seed)
-            layout = KVLayout(cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, e.block_size, torch.float32)
+            if isinstance(weights, CPUCausalLM):
+                self.model = weights
+                self.model.stage = pp_stage
+            else:
+                self.model = CPUCausalLM.random(cfg, seed, layers=pp_stage.layers if pp_stage else None,
+                                                stage=pp_stage)
+            layout = KVLayout(nlayers, cfg.num_kv_heads, cfg.head_dim, e.block_size, torch.float32)
             nblocks = e.num_blocks or e.max_num_seqs * ((e.max_model_len + e.block_size - 1) // e.block_size)
             self.pool = KVPool(layout, nblocks, self.device)
             self.runner = CPUModelRunner(self.model, self.pool)
@@ -76,14 +85,17 @@ class LLMEngine:
         if weights is None:
             tp = 1 if tp_comm is None else tp_comm.world_size
             rank = 0 if tp_comm is None else tp_comm.rank
-            weights = random_weights(cfg, self.device, tp=tp, rank=rank, seed=seed)
+            weights = random_weights(cfg, self.device, tp=tp, rank=rank, seed=seed,
+                                     layers=pp_stage.layers if pp_stage else None)
         if moe is None and cfg.is_moe:
             from ..models.moe import MoE
 
             moe = MoE(cfg, self.device, tp_comm)
-        self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe)
+        self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe, stage=pp_stage)
         self.model.configure_tp(e.max_num_batched_tokens + e.max_num_seqs)
-        layout = KVLayout(cfg.num_layers, self.model.hkv, cfg.head_dim, e.block_size)
+        if pp_stage is not None:
+            e.use_cuda_graph = False  # stages exchange hidden states inside the step
+        layout = KVLayout(nlayers, self.model.hkv, cfg.head_dim, e.block_size)
         nblocks = e.num_blocks
         if nblocks <= 0:
             free, _ = torch.cuda.mem_get_info(self.device)
@@ -223,12 +235,15 @@ class LLMEngine:
             if nv:
                 torch.cuda.nvtx.range_pop()
             return []
-        if batch.admitted:
-            self.runner.admit(batch.admitted)
         t1 = time.perf_counter() if prof else 0.0
         if nv:
             torch.cuda.nvtx.range_push(f"execute T={batch.num_tokens} decode={len(batch.decode)}")
-        seqs, toks = self.runner.execute(batch)
+        if self.pp is not None:
+            seqs, toks = self._pipeline_execute(batch)
+        else:
+            if batch.admitted:
+                self.runner.admit(batch.admitted)
+            seqs, toks = self.runner.execute(batch)
         if nv:
             torch.cuda.nvtx.range_pop()
             torch.cuda.nvtx.range_pop()
@@ -272,6 +287,23 @@ class LLMEngine:
         if prof:
             self.profile["postprocess_s"] += time.perf_counter() - now
         return outs
+
+    def _pipeline_execute(self, batch):
+        """One step as micro-batches through this pipeline stage; tokens come from the last stage."""
+        from ..parallel.pp import split_batch
+
+        seqs, parts = [], []
+        for sb in split_batch(batch, self.pp.micro_batches):
+            if sb.admitted:
+                self.runner.admit(sb.admitted)
+            s, t = self.runner.execute(sb)
+            seqs += s
+            parts.append(np.asarray(t, dtype=np.int64))
+        toks = torch.from_numpy(np.concatenate(parts) if parts else np.zeros(0, np.int64))
+        if self.device.type == "cuda":
+            toks = toks.to(self.device)
+        toks = self.pp.broadcast_tokens(toks)
+        return seqs, toks.cpu().numpy()
 
     def profile_summary(self) -> dict:
         """Per-phase host timings when ``KAPSL_LLM_PROFILE=1`` (reference:

@@ -270,7 +270,8 @@ class ModelRunner:
                 nsplit = self._graph_splits(bucket)
             fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, nsplit)
             logits = self.model.forward(fb, self.pool.k, self.pool.v)
-            self._sample(logits, R)
+            if logits is not None:  # None: an earlier pipeline stage (the last stage samples)
+                self._sample(logits, R)
             self.launches += launch_count() - c0
         self.h_out[:R].copy_(self.out_tokens[:R], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()

@@ -43,6 +43,7 @@ class CPUCausalLM:
         self.hq, self.hkv, self.D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         self.scale = 1.0 / math.sqrt(self.D)
         self.device = torch.device("cpu")
+        self.stage = None  # PipelineStage when this model holds one pipeline stage's layers
         self._k = None  # C++ CPU kernels (kapsl_sdk_b200._native.cpu) when built
         if os.environ.get("KAPSL_CPU_KERNELS", "native") == "native":
             try:
@@ -53,11 +54,19 @@ class CPUCausalLM:
                 self._k = None
 
     @classmethod
-    def random(cls, cfg: ModelConfig, seed: int = 0, std: float = 0.02) -> "CPUCausalLM":
+    def random(cls, cfg: ModelConfig, seed: int = 0, std: float = 0.02, layers: Optional[range] = None,
+               stage=None) -> "CPUCausalLM":
+        """Random weights from ``seed``; with ``layers`` (a pipeline stage's range) only
+        those layers are kept, drawn from the same stream as the full model."""
         from .llama import random_full_weights
 
         items = list(random_full_weights(cfg, torch.device("cpu"), seed, std))
-        return cls(cfg, items[0][1], items[1][1], torch.ones(cfg.hidden_size), [t for k, t in items[2:]])
+        full = [t for k, t in items[2:]]
+        if layers is not None:
+            full = [full[i] for i in layers]
+        m = cls(cfg, items[0][1], items[1][1], torch.ones(cfg.hidden_size), full)
+        m.stage = stage
+        return m
 
     def forward(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor, seqs: list,
                 k_caches: list, v_caches: list, logits_rows: list) -> torch.Tensor:
@@ -68,7 +77,7 @@ class CPUCausalLM:
         cfg = self.cfg
         T = ids.numel()
         D, hq, hkv = self.D, self.hq, self.hkv
-        h = self.embed[ids.long()]
+        h = self._stage_input(ids)
         bs = k_caches[0].shape[2]
         blk = (slots // bs).long()
         off = (slots % bs).long()
@@ -95,6 +104,9 @@ class CPUCausalLM:
             else:
                 gu = x @ L["gate_up"].T
                 h = h + ref.silu_mul(gu) @ L["down"].T
+        if self.stage is not None and not self.stage.last:
+            self.stage.send_hidden(h)
+            return None
         xs, _ = ref.rmsnorm(h[logits_rows], self.final_norm, cfg.rms_eps)
         return xs @ self.lm_head.T
 
@@ -104,7 +116,7 @@ class CPUCausalLM:
         cfg = self.cfg
         T = ids.numel()
         D, hq, hkv = self.D, self.hq, self.hkv
-        h = self.embed[ids.long()].contiguous()
+        h = self._stage_input(ids).contiguous()
         pos = positions.to(torch.int64).contiguous().numpy()
         sl = slots.to(torch.int64).contiguous().numpy()
         row0 = np.array([r for r, _, _, _ in seqs], dtype=np.int64)
@@ -139,9 +151,18 @@ class CPUCausalLM:
                 act = torch.empty(T, gu.shape[1] // 2)
                 k_.silu_mul(gu.numpy(), act.numpy())
                 h += act @ L["down"].T
+        if self.stage is not None and not self.stage.last:
+            self.stage.send_hidden(h)
+            return None
         xs = h[logits_rows].contiguous()
         k_.rmsnorm(xs.numpy(), self.final_norm.numpy(), xs.numpy(), cfg.rms_eps)
         return xs @ self.lm_head.T
+
+    def _stage_input(self, ids: torch.Tensor) -> torch.Tensor:
+        """Token embeddings, or (later pipeline stages) the previous stage's hidden state."""
+        if self.stage is not None and not self.stage.first:
+            return self.stage.recv_hidden(ids.numel(), self.cfg.hidden_size, torch.float32, self.device)
+        return self.embed[ids.long()]
 
     def _moe(self, x: torch.Tensor, L: dict) -> torch.Tensor:
         cfg = self.cfg

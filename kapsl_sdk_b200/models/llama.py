@@ -231,8 +231,10 @@ def random_full_weights(cfg: ModelConfig, device, seed: int = 0, std: float = 0.
         yield "layer", random_layer(cfg, layer, gen, device, std)
 
 
-def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: int = 0) -> ModelWeights:
-    """Shard a stream of full tensors (see :func:`random_full_weights`) for one rank."""
+def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: int = 0,
+                      layers: Optional[range] = None) -> ModelWeights:
+    """Shard a stream of full tensors (see :func:`random_full_weights`) for one rank;
+    ``layers`` keeps only a pipeline stage's layer range."""
     plan = ShardPlan.make(cfg, tp, rank)
     V, d = cfg.vocab_size, cfg.hidden_size
     # embedding and lm_head are replicated on every rank: each rank computes the
@@ -241,6 +243,7 @@ def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: in
     w = ModelWeights(embed=None, lm_head=None, final_norm=torch.ones(d, device=device, dtype=torch.bfloat16),
                      vocab_start=v0, heads_local=plan.heads_local, kv_heads_local=plan.kv_heads_local,
                      ffn_local=ffn_shard_size(cfg, tp) if not cfg.is_moe else cfg.intermediate_size)
+    layer_idx = 0
     for kind, t in full_iter:
         if kind == "embed":
             w.embed = t[v0:v0 + vl].to(device, torch.bfloat16).contiguous()
@@ -249,15 +252,18 @@ def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: in
         elif kind == "final_norm":
             w.final_norm = t.to(device, torch.bfloat16).contiguous()
         else:
-            w.layers.append(shard_layer(cfg, plan, t, device))
+            li = layer_idx
+            layer_idx += 1
+            if layers is None or li in layers:
+                w.layers.append(shard_layer(cfg, plan, t, device))
     return w
 
 
 def random_weights(cfg: ModelConfig, device, tp: int = 1, rank: int = 0, seed: int = 0,
-                   std: float = 0.02) -> ModelWeights:
+                   std: float = 0.02, layers: Optional[range] = None) -> ModelWeights:
     """Random-init weights N(0, std) from ``seed``; every rank draws the same full
     tensors layer by layer and keeps its shard, so TP results match TP1."""
-    return weights_from_full(cfg, random_full_weights(cfg, device, seed, std), device, tp, rank)
+    return weights_from_full(cfg, random_full_weights(cfg, device, seed, std), device, tp, rank, layers)
 
 
 @dataclass
@@ -280,12 +286,13 @@ class ForwardBatch:
 class CausalLM:
     """GPU decoder over a paged KV cache, one instance per rank."""
 
-    def __init__(self, cfg: ModelConfig, weights: ModelWeights, device, tp_comm=None, moe=None):
+    def __init__(self, cfg: ModelConfig, weights: ModelWeights, device, tp_comm=None, moe=None, stage=None):
         self.cfg = cfg
         self.w = weights
         self.device = torch.device(device)
         self.tp = tp_comm
         self.moe = moe
+        self.stage = stage  # PipelineStage: ``weights.layers`` are this stage's layers only
         self.hq = weights.heads_local
         self.hkv = weights.kv_heads_local
         self.D = cfg.head_dim
@@ -309,7 +316,12 @@ class CausalLM:
         Bd = fb.num_decode
         tp = self.tp_size > 1
         h = self.tp.residual_stream(T) if tp else None  # symmetric memory in fused TP mode
-        h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start, out=h)
+        st = self.stage
+        if st is not None and not st.first:  # later pipeline stage: the previous stage's hidden state
+            hin = st.recv_hidden(T, cfg.hidden_size, torch.bfloat16, self.device)
+            h = hin if h is None else h.copy_(hin)
+        else:
+            h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start, out=h)
         attn = torch.empty(T, self.hq * self.D, dtype=torch.bfloat16, device=self.device)
         x = torch.empty_like(h)
         for li, L in enumerate(self.w.layers):
@@ -337,6 +349,9 @@ class CausalLM:
             else:
                 g = ops.linear(x, L.w_gu, swiglu=True)
                 self.tp.row_parallel_residual(g, L.w_down, h)
+        if st is not None and not st.last:
+            st.send_hidden(h[:T].clone())
+            return None
         xs = h.index_select(0, fb.logits_idx)
         xs = ops.rmsnorm(xs, self.w.final_norm, cfg.rms_eps)
         return ops.linear(xs, self.w.lm_head, out_dtype=torch.float32)
