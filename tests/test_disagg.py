@@ -84,14 +84,19 @@ def _reference_outputs(device="cpu"):
     return eng.generate(PROMPTS, SamplingParams.greedy(12, ignore_eos=True))
 
 
-def test_disaggregated_cpu_matches_single_engine():
+@pytest.mark.parametrize("world", [2, 4])
+def test_disaggregated_cpu_matches_single_engine(world):
+    """world 4: two prefill and two decode ranks (replicated CPU engines stand in for
+    tensor-parallel ranks), which exercises the group leaders, broadcasts and the
+    all-ranks completion protocol."""
     import json
 
     script = WORKER_CPU.format(root=ROOT, tests=os.path.join(ROOT, "tests"))
-    outs = _launch(script, 2)
-    line = [l for l in outs[1].splitlines() if l.startswith("OUT")][0]
-    got = json.loads(line[3:])
-    assert got == _reference_outputs()
+    outs = _launch(script, world)
+    ref = _reference_outputs()
+    for r in range(world // 2, world):
+        line = [l for l in outs[r].splitlines() if l.startswith("OUT")][0]
+        assert json.loads(line[3:]) == ref
 
 
 def test_block_runs():
