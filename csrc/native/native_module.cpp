@@ -264,6 +264,38 @@ PYBIND11_MODULE(_native, m) {
       .def("largest_slot", &shm::TieredAllocator::largest_slot)
       .def("layout_summary", &shm::TieredAllocator::layout_summary);
 
+  py::class_<shm::ModelPools>(m, "ModelPools")
+      .def(py::init([](uint64_t base, uint64_t total_bytes, py::list models, double ttl_s) {
+             // models: [(model_id, pool_bytes[, class_sizes[, weights]]), ...]
+             std::vector<shm::ModelPoolSpec> specs;
+             for (auto item : models) {
+               auto t = item.cast<py::tuple>();
+               shm::ModelPoolSpec s{t[0].cast<uint32_t>(), t[1].cast<uint64_t>(), {}, {}};
+               if (t.size() > 2) s.class_sizes = t[2].cast<std::vector<uint64_t>>();
+               if (t.size() > 3) s.weights = t[3].cast<std::vector<uint32_t>>();
+               specs.push_back(std::move(s));
+             }
+             return std::make_unique<shm::ModelPools>(base, total_bytes, specs, ttl_s);
+           }),
+           py::arg("base"), py::arg("total_bytes"), py::arg("models"), py::arg("ttl_s") = 30.0)
+      .def("try_allocate", &shm::ModelPools::try_allocate, py::arg("model_id"), py::arg("size"),
+           py::arg("force") = false)
+      .def("release", &shm::ModelPools::release)
+      .def("has_pool", &shm::ModelPools::has_pool)
+      .def("range", [](const shm::ModelPools& p, std::optional<uint32_t> id) { return p.range(id.value_or(UINT32_MAX)); },
+           py::arg("model_id") = py::none())
+      .def("usage", [](const shm::ModelPools& p, std::optional<uint32_t> id) {
+             const shm::PoolUsage u = id ? p.model_usage(*id) : p.shared_usage();
+             return py::make_tuple(u.in_use, u.oldest_lease_ms);
+           }, py::arg("model_id") = py::none())
+      .def("total_usage", [](const shm::ModelPools& p) {
+        const shm::PoolUsage u = p.total_usage();
+        return py::make_tuple(u.in_use, u.oldest_lease_ms);
+      })
+      .def("layout_summary", &shm::ModelPools::layout_summary)
+      .def_static("plan", &shm::ModelPools::plan, py::arg("total_bytes"), py::arg("weights"), py::arg("reserve_pct") = 10,
+                  py::arg("min_pool") = (uint64_t)64 << 10);
+
   // ---- servers
   py::class_<WireServer>(m, "WireServer")
       .def(py::init<py::object, std::optional<std::string>>(), py::arg("handler"), py::arg("auth_token") = py::none())
@@ -276,8 +308,16 @@ PYBIND11_MODULE(_native, m) {
       .def_property_readonly("requests_served", &WireServer::requests_served);
 
   py::class_<ShmServer>(m, "ShmServer")
-      .def(py::init<py::object, std::string, size_t, int>(), py::arg("handler"), py::arg("name"),
-           py::arg("size") = (size_t)256 << 20, py::arg("workers") = 4)
+      .def(py::init<py::object, std::string, size_t, int, std::map<uint32_t, uint32_t>>(), py::arg("handler"),
+           py::arg("name"), py::arg("size") = (size_t)256 << 20, py::arg("workers") = 4,
+           py::arg("model_weights") = std::map<uint32_t, uint32_t>{})
+      .def("pool_usage", [](const ShmServer& s, std::optional<uint32_t> id) -> py::tuple {
+             const shm::PoolUsage u = !s.pools() ? shm::PoolUsage{}
+                                      : id       ? s.pools()->model_usage(*id)
+                                                 : s.pools()->shared_usage();
+             return py::make_tuple(u.in_use, u.oldest_lease_ms);
+           }, py::arg("model_id") = py::none())
+      .def("pool_layout", [](const ShmServer& s) { return s.pools() ? s.pools()->layout_summary() : std::string(); })
       .def("start", &ShmServer::start)
       .def("stop", &ShmServer::stop, py::call_guard<py::gil_scoped_release>())
       .def_property_readonly("requests_served", &ShmServer::requests_served)

@@ -394,7 +394,8 @@ bool WireServer::handle_frame(int fd, uint32_t model_id, uint32_t op, const std:
 }
 
 // --------------------------------------------------------------- ShmServer
-ShmServer::ShmServer(py::object handler, const std::string& name, size_t size, int workers)
+ShmServer::ShmServer(py::object handler, const std::string& name, size_t size, int workers,
+                     const std::map<uint32_t, uint32_t>& model_weights)
     : handler_(std::move(handler)), workers_(std::max(1, workers)) {
   region_ = std::make_unique<shm::Region>(shm::Region::create(name, size));
   shm::Ring<shm::ShmRequest>(region_->base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, true);
@@ -402,7 +403,12 @@ ShmServer::ShmServer(py::object handler, const std::string& name, size_t size, i
   const auto& h = region_->header();
   const uint64_t half = h.max_tensor_size / 2;
   result_base_ = h.tensor_pool_offset + half;
-  alloc_ = std::make_unique<shm::TieredAllocator>(result_base_, h.max_tensor_size - half);
+  // result slots: one sub-pool per model sized by its weight, plus the shared overflow pool
+  const uint64_t bytes = h.max_tensor_size - half;
+  std::vector<shm::ModelPoolSpec> specs;
+  for (auto& [id, b] : shm::ModelPools::plan(bytes, {model_weights.begin(), model_weights.end()}))
+    specs.push_back(shm::ModelPoolSpec{id, b, {}, {}});
+  alloc_ = std::make_unique<shm::ModelPools>(result_base_, bytes, specs);
 }
 
 ShmServer::~ShmServer() {
@@ -481,7 +487,7 @@ void ShmServer::process(const shm::ShmRequest& req) {
   }
   if (err.empty()) {
     const uint64_t need = shm::tensor_bytes(out);
-    auto slot = alloc_->try_allocate(need, /*force=*/true);
+    auto slot = alloc_->try_allocate(req.meta.model_id, need, /*force=*/true);
     if (!slot) {
       exhausted_.fetch_add(1);
       err = "SHM tensor pool exhausted (required=" + std::to_string(need) + " bytes)";
@@ -493,7 +499,7 @@ void ShmServer::process(const shm::ShmRequest& req) {
   }
   if (!err.empty()) {
     resp.meta.status = 1;
-    auto slot = alloc_->try_allocate(8 + err.size(), /*force=*/true);
+    auto slot = alloc_->try_allocate(req.meta.model_id, 8 + err.size(), /*force=*/true);
     if (slot) {
       shm::write_error(*region_, *slot, err);
       resp.error_offset = *slot;

@@ -81,13 +81,15 @@ class WireServer {
 
 class ShmServer {
  public:
-  ShmServer(py::object handler, const std::string& name, size_t size, int workers);
+  ShmServer(py::object handler, const std::string& name, size_t size, int workers,
+            const std::map<uint32_t, uint32_t>& model_weights = {});
   ~ShmServer();
   void start();
   void stop();
   uint64_t requests_served() const { return served_.load(); }
-  size_t pool_in_use() const { return alloc_ ? alloc_->in_use() : 0; }
-  double pool_oldest_lease_ms() const { return alloc_ ? alloc_->oldest_lease_ms() : 0.0; }
+  size_t pool_in_use() const { return alloc_ ? alloc_->total_usage().in_use : 0; }
+  double pool_oldest_lease_ms() const { return alloc_ ? alloc_->total_usage().oldest_lease_ms : 0.0; }
+  const shm::ModelPools* pools() const { return alloc_.get(); }
   uint64_t pool_exhausted() const { return exhausted_.load(); }
   uint64_t result_pool_base() const { return result_base_; }
 
@@ -98,7 +100,7 @@ class ShmServer {
 
   py::object handler_;
   std::unique_ptr<shm::Region> region_;
-  std::unique_ptr<shm::TieredAllocator> alloc_;
+  std::unique_ptr<shm::ModelPools> alloc_;
   uint64_t result_base_ = 0;
   int workers_;
   std::atomic<bool> running_{false};

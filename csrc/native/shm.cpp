@@ -244,6 +244,98 @@ std::string TieredAllocator::layout_summary() const {
   return s;
 }
 
+// ------------------------------------------------------- per-model pools
+ModelPools::ModelPools(uint64_t base, uint64_t total_bytes, const std::vector<ModelPoolSpec>& models, double ttl_s) {
+  const uint64_t end = base + total_bytes;
+  uint64_t cursor = base;
+  for (const auto& m : models) {
+    const uint64_t bytes = std::min<uint64_t>(m.pool_bytes, end - cursor);
+    if (bytes == 0 || pools_.count(m.model_id)) continue;
+    pools_[m.model_id] = Pool{cursor, cursor + bytes,
+                              std::make_unique<TieredAllocator>(cursor, bytes, m.class_sizes, m.weights, ttl_s)};
+    cursor += bytes;
+  }
+  shared_ = Pool{cursor, end, std::make_unique<TieredAllocator>(cursor, std::max<uint64_t>(end - cursor, 1),
+                                                                std::vector<uint64_t>{}, std::vector<uint32_t>{}, ttl_s)};
+}
+
+std::optional<uint64_t> ModelPools::try_allocate(uint32_t model_id, uint64_t size, bool force) {
+  auto it = pools_.find(model_id);
+  TieredAllocator* own = it != pools_.end() ? it->second.alloc.get() : nullptr;
+  TieredAllocator* shared = shared_.end != shared_.base ? shared_.alloc.get() : nullptr;
+  for (int f = 0; f <= (force ? 1 : 0); ++f) {
+    if (own)
+      if (auto o = own->try_allocate(size, f == 1)) return o;
+    if (shared)
+      if (auto o = shared->try_allocate(size, f == 1)) return o;
+  }
+  return std::nullopt;
+}
+
+bool ModelPools::release(uint64_t offset) {
+  for (auto& [id, p] : pools_)
+    if (offset >= p.base && offset < p.end) return p.alloc->release(offset);
+  if (offset >= shared_.base && offset < shared_.end) return shared_.alloc->release(offset);
+  return false;
+}
+
+static PoolUsage usage_of(const TieredAllocator& a) { return PoolUsage{a.in_use(), a.oldest_lease_ms()}; }
+
+PoolUsage ModelPools::model_usage(uint32_t model_id) const {
+  auto it = pools_.find(model_id);
+  return it == pools_.end() ? PoolUsage{} : usage_of(*it->second.alloc);
+}
+PoolUsage ModelPools::shared_usage() const {
+  return shared_.end == shared_.base ? PoolUsage{} : usage_of(*shared_.alloc);
+}
+PoolUsage ModelPools::total_usage() const {
+  PoolUsage t = shared_usage();
+  for (auto& [id, p] : pools_) {
+    const PoolUsage u = usage_of(*p.alloc);
+    t.in_use += u.in_use;
+    t.oldest_lease_ms = std::max(t.oldest_lease_ms, u.oldest_lease_ms);
+  }
+  return t;
+}
+
+std::pair<uint64_t, uint64_t> ModelPools::range(uint32_t model_id) const {
+  if (model_id == UINT32_MAX) return {shared_.base, shared_.end};
+  auto it = pools_.find(model_id);
+  if (it == pools_.end()) return {0, 0};
+  return {it->second.base, it->second.end};
+}
+
+std::string ModelPools::layout_summary() const {
+  std::string s;
+  for (auto& [id, p] : pools_) s += "model " + std::to_string(id) + ": " + p.alloc->layout_summary() + "; ";
+  s += "shared: " + (shared_.end == shared_.base ? std::string("none") : shared_.alloc->layout_summary());
+  return s;
+}
+
+std::vector<std::pair<uint32_t, uint64_t>> ModelPools::plan(uint64_t total_bytes,
+                                                            std::vector<std::pair<uint32_t, uint32_t>> weights,
+                                                            uint32_t reserve_pct, uint64_t min_pool) {
+  std::sort(weights.begin(), weights.end());
+  uint64_t wsum = 0;
+  for (auto& w : weights) {
+    w.second = std::clamp<uint32_t>(w.second, 1, 1000);
+    wsum += w.second;
+  }
+  const uint64_t reserve = std::max<uint64_t>((uint64_t)((unsigned __int128)total_bytes * reserve_pct / 100), min_pool);
+  const uint64_t avail = total_bytes > reserve ? total_bytes - reserve : 0;
+  std::vector<std::pair<uint32_t, uint64_t>> out;
+  uint64_t given = 0;
+  for (size_t i = 0; i < weights.size(); ++i) {
+    const uint64_t bytes = i + 1 == weights.size()
+                               ? avail - std::min(given, avail)
+                               : (uint64_t)((unsigned __int128)avail * weights[i].second / std::max<uint64_t>(wsum, 1));
+    if (bytes < min_pool) continue;
+    out.emplace_back(weights[i].first, bytes);
+    given += bytes;
+  }
+  return out;
+}
+
 // ------------------------------------------------------------ shared leases
 static uint64_t monotonic_ms() {
   timespec ts;

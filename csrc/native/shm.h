@@ -23,6 +23,7 @@
 #include <atomic>
 #include <chrono>
 #include <memory>
+#include <map>
 #include <mutex>
 #include <optional>
 #include <string>
@@ -196,6 +197,57 @@ class TieredAllocator {
 
  private:
   std::vector<std::unique_ptr<SlotAllocator>> classes_;
+};
+
+// Per-model sub-pools carved from one contiguous range: each model gets its own
+// TieredAllocator over [cursor, cursor + pool_bytes) in the order given, and
+// the bytes left over form a shared overflow pool with the default classes.
+// An allocation tries the model's pool first, then the shared pool (unknown
+// model ids go straight to the shared pool); a release finds its pool by
+// offset range.  Reference: crates/kapsl-shm/src/allocator.rs:436-560
+// (per-model allocator) and crates/kapsl-shm/src/server.rs:241-300 (sizing).
+struct ModelPoolSpec {
+  uint32_t model_id;
+  uint64_t pool_bytes;
+  std::vector<uint64_t> class_sizes;  // empty: default classes
+  std::vector<uint32_t> weights;
+};
+
+struct PoolUsage {
+  size_t in_use = 0;
+  double oldest_lease_ms = 0;
+};
+
+class ModelPools {
+ public:
+  ModelPools(uint64_t base, uint64_t total_bytes, const std::vector<ModelPoolSpec>& models, double ttl_s = 30.0);
+  // force: when both pools are full, take over the oldest lease (model pool first)
+  std::optional<uint64_t> try_allocate(uint32_t model_id, uint64_t size, bool force = false);
+  bool release(uint64_t offset);
+  PoolUsage model_usage(uint32_t model_id) const;  // zeros when the model has no pool
+  PoolUsage shared_usage() const;
+  PoolUsage total_usage() const;
+  bool has_pool(uint32_t model_id) const { return pools_.count(model_id) != 0; }
+  // (base, end) of a model's pool, or of the shared pool for model_id == UINT32_MAX
+  std::pair<uint64_t, uint64_t> range(uint32_t model_id) const;
+  std::string layout_summary() const;
+
+  // Pool sizes for models weighted by expected concurrency: a reserve of
+  // reserve_pct percent (at least min_pool bytes) stays shared, the rest is
+  // split by weight (clamped to [1, 1000]) over models in id order, the last
+  // taking the rounding remainder; slices under min_pool bytes are dropped
+  // (those models use the shared pool).
+  static std::vector<std::pair<uint32_t, uint64_t>> plan(uint64_t total_bytes,
+                                                         std::vector<std::pair<uint32_t, uint32_t>> weights,
+                                                         uint32_t reserve_pct = 10, uint64_t min_pool = 64 << 10);
+
+ private:
+  struct Pool {
+    uint64_t base, end;
+    std::unique_ptr<TieredAllocator> alloc;
+  };
+  std::map<uint32_t, Pool> pools_;
+  Pool shared_;
 };
 
 // Slot leases shared by every client process of one region.  The slot layout

@@ -15,6 +15,16 @@ DEFAULT_TCP_PORT = 9096
 DEFAULT_SHM_NAME = "kapsl-shm-default"
 
 
+def _peak_concurrency(target) -> int:
+    eng = getattr(target, "engine", target)
+    try:
+        v = eng.model_info().peak_concurrency if hasattr(eng, "model_info") else None
+    except Exception:
+        v = None
+    v = v or getattr(target, "peak_concurrency", None) or 1
+    return min(max(int(v), 1), 1000)
+
+
 class KapslServer:
     def __init__(self, models: Optional[dict] = None, lookup=None, api_token: Optional[str] = None):
         """``models`` maps model id -> target (object with infer/infer_stream, or an
@@ -49,8 +59,17 @@ class KapslServer:
         self.tcp_port = self.wire.listen_tcp(host, port)
         return self
 
-    def serve_shm(self, name: str = DEFAULT_SHM_NAME, size: int = 256 << 20, workers: int = 4) -> "KapslServer":
-        self.shm = self._native.ShmServer(self.dispatcher, name, size, workers)
+    def serve_shm(self, name: str = DEFAULT_SHM_NAME, size: int = 256 << 20, workers: int = 4,
+                  model_weights: Optional[dict] = None) -> "KapslServer":
+        """Result slots come from one sub-pool per model, sized in proportion to
+        ``model_weights`` (model id -> expected concurrency; by default each
+        model's ``peak_concurrency`` from ``model_info()`` or as an attribute,
+        else 1), plus a shared overflow
+        pool of 10% that also serves unknown model ids."""
+        if model_weights is None:
+            model_weights = {mid: _peak_concurrency(t) for mid, t in self.models.items()}
+        self.shm = self._native.ShmServer(self.dispatcher, name, size, workers,
+                                          {int(k): max(1, int(v)) for k, v in model_weights.items()})
         self.wire.attach_shm(name)  # hybrid requests read/write the same region
         return self
 

@@ -224,3 +224,57 @@ def test_shm_rejects_out_of_bounds_offsets():
         assert "outside" in region.read_error(err_off)
     finally:
         srv.stop()
+
+
+def test_model_pools_allocator():
+    """Per-model sub-pools with a shared overflow pool: model pool first, spill
+    to the shared pool, unknown ids to the shared pool, release by offset range."""
+    from kapsl_sdk_b200._ext import native
+
+    P = native().ModelPools
+    MiB = 1 << 20
+    plan = dict(P.plan(100 * MiB, [(7, 1), (3, 3)]))
+    assert set(plan) == {3, 7}
+    assert plan[3] == 3 * (90 * MiB) // 4 and plan[3] + plan[7] == 90 * MiB  # 10% stays shared
+    # model 0's slice (under 64 KiB) is dropped and the last model takes the rest
+    assert P.plan(1 << 20, [(0, 1), (1, 1000)]) == [(1, (1 << 20) - (1 << 20) // 10)]
+
+    pools = P(4096, 10 * MiB, [(0, 2 * MiB, [MiB], [1]), (1, 3 * MiB, [MiB], [1])], ttl_s=60.0)
+    b0, e0 = pools.range(0)
+    b1, e1 = pools.range(1)
+    bs, es = pools.range()
+    assert (b0, e0, b1, e1, es) == (4096, 4096 + 2 * MiB, e0, e0 + 3 * MiB, 4096 + 10 * MiB) and bs == e1
+    got0 = [pools.try_allocate(0, MiB) for _ in range(2)]
+    assert all(b0 <= o < e0 for o in got0)
+    spill = pools.try_allocate(0, MiB)  # model 0's pool is full -> shared pool
+    assert bs <= spill < es
+    other = pools.try_allocate(42, 1000)  # no pool of its own
+    assert bs <= other < es
+    assert pools.usage(0)[0] == 2 and pools.usage(1)[0] == 0 and pools.usage()[0] == 2
+    assert pools.total_usage()[0] == 4
+    assert pools.try_allocate(1, 8 * MiB) is None  # larger than every slot of both pools
+    assert pools.release(got0[0]) and pools.usage(0)[0] == 1
+    assert pools.try_allocate(0, MiB) == got0[0]
+    assert pools.release(spill) and not pools.release(es + 10)
+    assert "model 0" in pools.layout_summary() and "shared" in pools.layout_summary()
+
+
+def test_shm_server_per_model_pools():
+    from kapsl_sdk import KapslShmClient
+
+    name = f"kapsl-pm-{uuid.uuid4().hex[:8]}"
+    a, b = EchoTarget(), EchoTarget()
+    b.peak_concurrency = 3
+    from kapsl_sdk_b200.server import KapslServer
+
+    srv = KapslServer(models={0: a, 1: b}).serve_shm(name, size=64 << 20, workers=2).start()
+    try:
+        layout = srv.shm.pool_layout()
+        assert "model 0" in layout and "model 1" in layout and "shared" in layout
+        c = KapslShmClient(name)  # requests model 0
+        for i in range(3):
+            assert c.infer([1], "int32", struct.pack("<i", i)) == struct.pack("<i", i)
+        assert srv.shm.pool_usage(0)[0] == 3 and srv.shm.pool_usage(1)[0] == 0
+        assert srv.shm.pool_in_use == 3
+    finally:
+        srv.stop()
