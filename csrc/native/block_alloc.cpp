@@ -1,5 +1,7 @@
 #include "block_alloc.h"
 
+#include <algorithm>
+
 namespace kapsl {
 
 BlockAllocator::BlockAllocator(int64_t num_blocks, int block_size, bool enable_prefix_cache,
@@ -10,39 +12,28 @@ BlockAllocator::BlockAllocator(int64_t num_blocks, int block_size, bool enable_p
   ref_.assign(num_blocks, 0);
   free_list_.reserve(num_blocks);
   for (int64_t b = num_blocks - 1; b >= 0; --b) free_list_.push_back(b);
-  lru_pos_.resize(num_blocks);
+  cached_key_.resize(num_blocks);
   in_cached_.assign(num_blocks, 0);
+  prio_.assign(num_blocks, 0);
   by_block_.assign(num_blocks, nullptr);
 }
 
 void BlockAllocator::cached_push(int64_t b) {
   in_cached_[b] = 1;
   ++cached_count_;
-  if (lru_) {
-    lru_list_.push_back(b);
-    lru_pos_[b] = std::prev(lru_list_.end());
-  } else {
-    fifo_set_.insert(b);
-  }
+  cached_key_[b] = Key{prio_[b], lru_ ? tick_++ : (uint64_t)b, b};
+  cached_.insert(cached_key_[b]);
 }
 
 void BlockAllocator::cached_erase(int64_t b) {
   if (!in_cached_[b]) return;
   in_cached_[b] = 0;
   --cached_count_;
-  if (lru_)
-    lru_list_.erase(lru_pos_[b]);
-  else
-    fifo_set_.erase(b);
+  cached_.erase(cached_key_[b]);
 }
 
 int64_t BlockAllocator::cached_pop() {
-  int64_t b;
-  if (lru_) {
-    b = lru_list_.front();
-  } else {
-    b = *fifo_set_.begin();
-  }
+  const int64_t b = std::get<2>(*cached_.begin());
   cached_erase(b);
   return b;
 }
@@ -57,6 +48,7 @@ void BlockAllocator::remove_block_node(int64_t b) {
     stack.pop_back();
     if (x->block >= 0) {
       by_block_[x->block] = nullptr;
+      prio_[x->block] = 0;
       // descendants are unreachable now: unused ones go back to the plain free list
       if (x->block != b && in_cached_[x->block]) {
         cached_erase(x->block);
@@ -129,7 +121,8 @@ std::vector<int64_t> BlockAllocator::match_prefix(const std::vector<int32_t>& to
   return out;
 }
 
-void BlockAllocator::commit_prefix(const std::vector<int32_t>& tokens, const std::vector<int64_t>& blocks) {
+void BlockAllocator::commit_prefix(const std::vector<int32_t>& tokens, const std::vector<int64_t>& blocks,
+                                   int priority) {
   if (!prefix_) return;
   Node* node = &root_;
   const size_t nfull = std::min(tokens.size() / block_size_, blocks.size());
@@ -150,6 +143,7 @@ void BlockAllocator::commit_prefix(const std::vector<int32_t>& tokens, const std
     } else {
       node = it->second.get();
     }
+    prio_[node->block] = std::max(prio_[node->block], priority);
   }
 }
 

@@ -2,7 +2,9 @@
 // the scheduler).  Semantics match kapsl_sdk_b200.llm.block_manager.BlockAllocator:
 //   * free list with lowest-id-first reuse;
 //   * blocks whose refcount drops to 0 but that name a cached prefix stay
-//     reusable ("cached free") until evicted, LRU by last release or FIFO by id;
+//     reusable ("cached free") until evicted: lowest priority first (the
+//     highest priority of the sequences that committed or reused the block),
+//     then LRU by last release or FIFO by id;
 //   * prefix match over full blocks, capped at len-1 tokens so the last token is
 //     always recomputed.
 // Reference: crates/kapsl-llm/src/block_manager.rs:5-277, kv_cache.rs:640-696,
@@ -11,11 +13,11 @@
 
 #include <stdint.h>
 
-#include <list>
 #include <memory>
 #include <set>
 #include <stdexcept>
 #include <string>
+#include <tuple>
 #include <unordered_map>
 #include <vector>
 
@@ -52,7 +54,7 @@ class BlockAllocator {
   void incref(const std::vector<int64_t>& blocks);
   void free(const std::vector<int64_t>& blocks);
   std::vector<int64_t> match_prefix(const std::vector<int32_t>& tokens);
-  void commit_prefix(const std::vector<int32_t>& tokens, const std::vector<int64_t>& blocks);
+  void commit_prefix(const std::vector<int32_t>& tokens, const std::vector<int64_t>& blocks, int priority = 0);
   bool is_cached(int64_t b) const { return by_block_[b] != nullptr; }
 
  private:
@@ -73,11 +75,13 @@ class BlockAllocator {
   bool lru_;
   std::vector<int> ref_;
   std::vector<int64_t> free_list_;  // back() = next to hand out
-  // cached-free blocks
-  std::list<int64_t> lru_list_;
-  std::vector<std::list<int64_t>::iterator> lru_pos_;
+  // cached-free blocks ordered by (priority, release tick or block id)
+  using Key = std::tuple<int, uint64_t, int64_t>;
+  std::set<Key> cached_;
+  std::vector<Key> cached_key_;
   std::vector<uint8_t> in_cached_;
-  std::set<int64_t> fifo_set_;
+  std::vector<int> prio_;
+  uint64_t tick_ = 0;
   size_t cached_count_ = 0;
   uint64_t evicted_ = 0;
   Node root_;

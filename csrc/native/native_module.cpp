@@ -193,7 +193,8 @@ PYBIND11_MODULE(_native, m) {
       .def("incref", &BlockAllocator::incref)
       .def("free", &BlockAllocator::free)
       .def("match_prefix", &BlockAllocator::match_prefix)
-      .def("commit_prefix", &BlockAllocator::commit_prefix)
+      .def("commit_prefix", &BlockAllocator::commit_prefix, py::arg("tokens"), py::arg("blocks"),
+           py::arg("priority") = 0)
       .def("is_cached", &BlockAllocator::is_cached);
 
   // ---- shared memory

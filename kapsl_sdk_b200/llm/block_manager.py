@@ -9,13 +9,14 @@ Counterparts in the reference:
 
 Here the blocks index a GPU pool; the C++ allocator in ``kapsl_sdk_b200._native``
 implements the same interface and is used when built (``NativeBlockAllocator``).
-Freed blocks that hold a cached prefix stay reusable until evicted (LRU by
-last access, or FIFO by block id).
+Freed blocks that hold a cached prefix stay reusable until evicted: lowest
+priority first (the highest priority of the sequences that committed the
+block; reference kv_cache.rs:1107-1154 orders inactive sequences the same
+way), then LRU by last release or FIFO by block id.
 """
 from __future__ import annotations
 
 import itertools
-from collections import OrderedDict
 from typing import Optional
 
 
@@ -52,19 +53,22 @@ class RadixPrefixIndex:
             node = child
         return out
 
-    def insert(self, tokens: list, blocks: list[int]) -> None:
-        node = self.root
+    def insert(self, tokens: list, blocks: list[int]) -> list[int]:
+        """Returns the blocks the index names along the path of ``tokens``."""
+        node, path = self.root, []
         nfull = min(len(tokens) // self.bs, len(blocks))
         for i in range(nfull):
             key = tuple(tokens[i * self.bs:(i + 1) * self.bs])
             child = node.children.get(key)
             if child is None:
                 if blocks[i] in self.by_block:  # block already names another prefix
-                    return
+                    break
                 child = _RadixNode(node, key, blocks[i])
                 node.children[key] = child
                 self.by_block[blocks[i]] = child
             node = child
+            path.append(child.block)
+        return path
 
     def remove_block(self, block: int) -> list[int]:
         """Drop the node of ``block`` and its whole subtree; returns the blocks of
@@ -100,7 +104,8 @@ class BlockAllocator:
         self.eviction = eviction
         self.ref = [0] * num_blocks
         self.free_list: list[int] = list(range(num_blocks - 1, -1, -1))  # pop() -> lowest id first
-        self.cached_free: "OrderedDict[int, None]" = OrderedDict()  # refcount 0 but holding a prefix
+        self.cached_free: dict = {}  # refcount 0 but holding a prefix -> eviction key
+        self.prio: dict = {}  # block -> highest priority of the sequences that committed it
         self.index = RadixPrefixIndex(block_size)
         self.evicted_blocks = 0
         self._tick = itertools.count()
@@ -124,12 +129,11 @@ class BlockAllocator:
             if self.free_list:
                 b = self.free_list.pop()
             else:
-                if self.eviction == "lru":
-                    b, _ = self.cached_free.popitem(last=False)
-                else:
-                    b = min(self.cached_free)
-                    del self.cached_free[b]
+                b = min(self.cached_free, key=self.cached_free.__getitem__)
+                del self.cached_free[b]
+                self.prio.pop(b, None)
                 for d in self.index.remove_block(b):
+                    self.prio.pop(d, None)
                     if d in self.cached_free:  # unreachable cached descendants become plain free
                         del self.cached_free[d]
                         self.free_list.append(d)
@@ -152,8 +156,8 @@ class BlockAllocator:
             self.ref[b] = r
             if r == 0:
                 if self.enable_prefix_cache and b in self.index:
-                    self.cached_free[b] = None
-                    self.cached_free.move_to_end(b)
+                    # eviction order: lowest priority first, then LRU (release tick) or FIFO (id)
+                    self.cached_free[b] = (self.prio.get(b, 0), next(self._tick) if self.eviction == "lru" else b)
                 else:
                     self.free_list.append(b)
 
@@ -167,10 +171,12 @@ class BlockAllocator:
         self.incref(blocks)
         return blocks
 
-    def commit_prefix(self, tokens: list, blocks: list[int]) -> None:
-        """Register every full block of ``tokens`` (whose KV is computed)."""
+    def commit_prefix(self, tokens: list, blocks: list[int], priority: int = 0) -> None:
+        """Register every full block of ``tokens`` (whose KV is computed); the
+        blocks' eviction priority rises to ``priority``."""
         if self.enable_prefix_cache:
-            self.index.insert(tokens, blocks)
+            for b in self.index.insert(tokens, blocks):
+                self.prio[b] = max(self.prio.get(b, 0), priority)
 
 
 def make_allocator(num_blocks: int, block_size: int = 16, enable_prefix_cache: bool = True,

@@ -53,6 +53,8 @@ class EngineConfig:
     kv_soft_limit_bytes: int = 0        # 0 = 90% of hard
     kv_hard_limit_bytes: int = 0        # 0 = pool size
     shareable_kv: bool = False          # pool mappable by another process (disaggregated decode side)
+    preemption: str = "recompute"       # or "swap": preempted KV pages go to host memory
+    swap_space_bytes: int = 4 << 30     # host memory for swapped pages
 
 
 class LLMEngine:
@@ -111,7 +113,9 @@ class LLMEngine:
     def _finish_init(self, cfg: ModelConfig, e: EngineConfig, nblocks: int, tp_comm) -> None:
         self.allocator = make_allocator(nblocks, e.block_size, e.enable_prefix_cache, e.eviction)
         self.scheduler = Scheduler(self.allocator, e.max_num_seqs, e.max_num_batched_tokens, e.chunked_prefill,
-                                   e.max_model_len)
+                                   e.max_model_len, e.preemption,
+                                   e.swap_space_bytes // self.pool.layout.bytes_per_block())
+        self._swapped_kv: dict = {}  # seq_id -> host copy of its computed pages
         self._seq_ids = itertools.count(1)
         self.sessions: dict[str, Sequence] = {}
         self.finished: list[Sequence] = []
@@ -206,6 +210,7 @@ class LLMEngine:
         for s in self.scheduler.abort(request_id):
             s.finish_time = time.perf_counter()
             s.finish_reason = "aborted"
+            self._swapped_kv.pop(s.seq_id, None)
 
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
@@ -229,6 +234,8 @@ class LLMEngine:
             torch.cuda.nvtx.range_push("kapsl.step")
             torch.cuda.nvtx.range_push("schedule")
         batch = self.scheduler.schedule()
+        if batch.preempted or batch.swap_in:
+            self._apply_preemptions(batch)
         if nv:
             torch.cuda.nvtx.range_pop()
         if batch.empty:
@@ -288,6 +295,20 @@ class LLMEngine:
             self.profile["postprocess_s"] += time.perf_counter() - now
         return outs
 
+    def _apply_preemptions(self, batch) -> None:
+        """Keep the sampler stream of preempted sequences (the GPU runner holds the
+        LCG state per slot on the device) and move swapped pages: restores first,
+        then copies out, all queued before this step's kernels."""
+        table = getattr(self.runner, "rng_table", None)
+        if batch.preempted and table is not None:
+            idx = torch.as_tensor(batch.preempted_slots, dtype=torch.long, device=table.device)
+            for s, v in zip(batch.preempted, table.index_select(0, idx).tolist()):
+                s.rng_state = v & ((1 << 64) - 1)
+        for s, blocks in batch.swap_in:
+            self.pool.restore(self._swapped_kv.pop(s.seq_id), blocks)
+        for s, blocks in batch.swap_out:
+            self._swapped_kv[s.seq_id] = self.pool.offload(blocks)
+
     def _pipeline_execute(self, batch):
         """One step as micro-batches through this pipeline stage; tokens come from the last stage."""
         from ..parallel.pp import split_batch
@@ -325,7 +346,8 @@ class LLMEngine:
             "blocks_total": a.num_blocks, "blocks_free": a.num_free(),
             "bytes_capacity": a.num_blocks * bpb, "bytes_used": a.num_used() * bpb,
             "sequences": len(self.scheduler.running), "evicted_blocks_total": a.evicted_blocks,
-            "preemptions": self.scheduler.num_preemptions,
+            "preemptions": self.scheduler.num_preemptions, "swapped": len(self.scheduler.swapped),
+            "swap_out_total": self.scheduler.num_swap_out, "swap_in_total": self.scheduler.num_swap_in,
         }
 
     def shutdown(self) -> None:

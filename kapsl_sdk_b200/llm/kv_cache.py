@@ -85,7 +85,7 @@ class KVPool:
         """Copy pages of ``blocks`` (all layers) into pinned host memory."""
         idx = torch.as_tensor(blocks, dtype=torch.long, device=self.device)
         host = torch.empty((self.layout.num_layers, 2, len(blocks)) + tuple(self.storage.shape[3:]),
-                           dtype=self.storage.dtype, pin_memory=True)
+                           dtype=self.storage.dtype, pin_memory=self.device.type == "cuda")
         host.copy_(self.storage.index_select(2, idx), non_blocking=True)
         return host
 

@@ -8,8 +8,15 @@ their blocks) and adds chunked prefill: each step has a budget of
 ``max_num_batched_tokens``; running decodes take one token each, then prompt
 chunks fill the rest, so long prompts never stall decoding.
 
-Preemption frees a victim's blocks and re-queues it for recomputation (the
-victim is the lowest-priority, latest-arrived running sequence).
+Preemption (the victim is the lowest-priority, latest-arrived running
+sequence) either frees the victim's blocks and re-queues it for recomputation
+("recompute"), or, with ``preemption="swap"``, moves the pages holding its
+computed KV to host memory and parks it in the swapped queue ("swap", while
+the host swap space has room).  Each step first swaps parked sequences back
+in, oldest first, when their pages fit with one free block left per running
+sequence (reference scheduler.rs:69-297: swap-in FIFO before admission).
+The engine performs the page copies the batch lists (``swap_in`` before
+``swap_out``, both before the step's kernels, on the same stream).
 """
 from __future__ import annotations
 
@@ -25,7 +32,10 @@ class ScheduledBatch:
     decode: list = field(default_factory=list)    # sequences generating one token
     prefill: list = field(default_factory=list)   # (sequence, chunk_len)
     preempted: list = field(default_factory=list)
-    admitted: list = field(default_factory=list)  # moved from waiting to running this step
+    preempted_slots: list = field(default_factory=list)  # their slots before preemption
+    admitted: list = field(default_factory=list)  # moved from waiting/swapped to running this step
+    swap_out: list = field(default_factory=list)  # (sequence, blocks to copy to host, in order)
+    swap_in: list = field(default_factory=list)   # (sequence, blocks to restore into)
 
     @property
     def num_tokens(self) -> int:
@@ -38,7 +48,10 @@ class ScheduledBatch:
 
 class Scheduler:
     def __init__(self, allocator, max_num_seqs: int = 256, max_num_batched_tokens: int = 2048,
-                 chunked_prefill: bool = True, max_model_len: int = 32768):
+                 chunked_prefill: bool = True, max_model_len: int = 32768, preemption: str = "recompute",
+                 swap_blocks: int = 0):
+        if preemption not in ("recompute", "swap"):
+            raise ValueError("preemption must be 'recompute' or 'swap'")
         self.alloc = allocator
         self.bs = allocator.block_size
         self.max_num_seqs = max_num_seqs
@@ -49,6 +62,12 @@ class Scheduler:
         self.running: list[Sequence] = []
         self.free_slots = list(range(max_num_seqs - 1, -1, -1))
         self.num_preemptions = 0
+        self.preemption = preemption
+        self.swap_capacity = swap_blocks if preemption == "swap" else 0
+        self.swap_used = 0
+        self.swapped: deque[Sequence] = deque()
+        self.num_swap_out = 0
+        self.num_swap_in = 0
 
     def add(self, seq: Sequence) -> None:
         if seq.length > self.max_model_len:
@@ -56,7 +75,7 @@ class Scheduler:
         self.waiting.append(seq)
 
     def has_work(self) -> bool:
-        return bool(self.waiting or self.running)
+        return bool(self.waiting or self.running or self.swapped)
 
     # -------------------------------------------------------------- helpers
     def _blocks_needed(self, seq: Sequence, upto: int) -> int:
@@ -81,25 +100,61 @@ class Scheduler:
             self.free_slots.append(seq.slot)
             seq.slot = -1
 
-    def _preempt_one(self, protect: Sequence, scheduled: set) -> bool:
+    def _computed_blocks(self, seq: Sequence) -> int:
+        return (seq.num_computed + self.bs - 1) // self.bs
+
+    def _preempt_one(self, protect: Sequence, scheduled: set, out: ScheduledBatch) -> bool:
         victims = [s for s in self.running if s is not protect and id(s) not in scheduled]
         if not victims:
             return False
         victim = min(victims, key=lambda s: (s.params.priority, -s.arrival))
         self.running.remove(victim)
+        out.preempted.append(victim)
+        out.preempted_slots.append(victim.slot)
+        self.num_preemptions += 1
+        nkeep = self._computed_blocks(victim)
+        if 0 < nkeep and self.swap_used + nkeep <= self.swap_capacity:
+            out.swap_out.append((victim, list(victim.block_ids[:nkeep])))
+            self._release(victim)
+            self.swap_used += nkeep
+            victim.status = SequenceStatus.SWAPPED
+            self.swapped.append(victim)
+            self.num_swap_out += 1
+            return True
         self._release(victim)
         victim.num_computed = 0
         victim.num_cached_prefix = 0
         victim.status = SequenceStatus.WAITING
         self.waiting.appendleft(victim)
-        self.num_preemptions += 1
         return True
+
+    def _swap_in(self, out: ScheduledBatch, fresh: set) -> None:
+        while self.swapped and len(self.running) < self.max_num_seqs:
+            seq = self.swapped[0]
+            n = self._computed_blocks(seq)
+            if self.alloc.num_free() < n + len(self.running):
+                break  # keep a block of headroom per running sequence
+            blocks = self.alloc.allocate(n)
+            self.swapped.popleft()
+            self.swap_used -= n
+            seq.block_ids = list(blocks)
+            seq.status = SequenceStatus.RUNNING
+            seq.slot = self.free_slots.pop()
+            self.running.append(seq)
+            out.swap_in.append((seq, list(blocks)))
+            out.admitted.append(seq)
+            fresh.add(id(seq))
+            self.num_swap_in += 1
 
     # ------------------------------------------------------------- schedule
     def schedule(self) -> ScheduledBatch:
         out = ScheduledBatch()
         budget = self.max_tokens
         scheduled: set = set()
+        # 0) swapped sequences come back first (protected from preemption this step)
+        fresh: set = set()
+        if self.swapped:
+            self._swap_in(out, fresh)
         # 1) running sequences: decodes and unfinished prompt chunks, in arrival order
         for seq in list(self.running):
             if seq not in self.running:  # preempted while making room for an earlier one
@@ -109,10 +164,9 @@ class Scheduler:
             if not seq.in_prefill:
                 ok = True
                 while not self._grow(seq, seq.length):
-                    if not self._preempt_one(seq, scheduled):
+                    if not self._preempt_one(seq, scheduled | fresh, out):
                         ok = False
                         break
-                    out.preempted.append(self.waiting[0])
                 if not ok:
                     if not scheduled:
                         raise OutOfBlocks("KV pool too small for a single sequence")
@@ -126,10 +180,9 @@ class Scheduler:
                     continue
                 ok = True
                 while not self._grow(seq, seq.num_computed + n):
-                    if not self._preempt_one(seq, scheduled):
+                    if not self._preempt_one(seq, scheduled | fresh, out):
                         ok = False
                         break
-                    out.preempted.append(self.waiting[0])
                 if not ok:
                     if not scheduled:
                         raise OutOfBlocks("KV pool too small for a single sequence")
@@ -137,8 +190,8 @@ class Scheduler:
                 out.prefill.append((seq, n))
                 scheduled.add(id(seq))
                 budget -= n
-        # 2) admit waiting sequences
-        while self.waiting and budget > 0 and len(self.running) < self.max_num_seqs:
+        # 2) admit waiting sequences (not while swapped ones wait for room: no starvation)
+        while self.waiting and not self.swapped and budget > 0 and len(self.running) < self.max_num_seqs:
             seq = self.waiting[0]
             if seq.num_computed == 0 and not seq.block_ids:
                 cached = self.alloc.match_prefix(seq.all_ids)
@@ -168,13 +221,16 @@ class Scheduler:
             self.running.remove(seq)
         elif seq in self.waiting:
             self.waiting.remove(seq)
+        elif seq in self.swapped:
+            self.swapped.remove(seq)
+            self.swap_used -= self._computed_blocks(seq)
         if seq.block_ids and seq.num_computed > 0:
-            self.alloc.commit_prefix(seq.all_ids[:seq.num_computed], seq.block_ids)
+            self.alloc.commit_prefix(seq.all_ids[:seq.num_computed], seq.block_ids, int(seq.params.priority))
         if not keep_blocks:
             self._release(seq)
 
     def abort(self, request_id: str) -> list[Sequence]:
-        hit = [s for s in list(self.running) + list(self.waiting) if s.request_id == request_id]
+        hit = [s for s in list(self.running) + list(self.waiting) + list(self.swapped) if s.request_id == request_id]
         for s in hit:
             self.finish(s, SequenceStatus.FINISHED_ABORTED)
         return hit

@@ -63,6 +63,29 @@ def test_lru_eviction_of_cached_blocks(impl):
     assert a.match_prefix([1, 2, 3, 4, 5]) == [] or True
 
 
+@pytest.mark.parametrize("impl", [0, 1])
+@pytest.mark.parametrize("eviction", ["lru", "fifo"])
+def test_low_priority_prefixes_are_evicted_first(impl, eviction):
+    a = both(n=4, bs=2, eviction=eviction)[impl]
+    hi, lo = a.allocate(1), a.allocate(1)
+    a.commit_prefix([1, 2], hi, priority=3)
+    a.commit_prefix([7, 8], lo, priority=0)
+    a.free(hi)  # released first: plain LRU/FIFO would evict it first
+    a.free(lo)
+    a.allocate(2)  # the two never-used blocks
+    assert a.allocate(1) == lo and a.evicted_blocks == 1
+    assert a.match_prefix([1, 2, 9]) == hi  # the high-priority prefix survived
+    # reuse by a sequence of higher priority raises a block's priority
+    a.free(hi)
+    x = a.allocate(1)
+    a.commit_prefix([5, 6], x, priority=0)
+    a.free(x)
+    m = a.match_prefix([5, 6, 0])
+    a.commit_prefix([5, 6], m, priority=9)
+    a.free(m)
+    assert a.allocate(1) == hi  # priority 3 < 9
+
+
 @pytest.mark.parametrize("seed", range(5))
 def test_python_and_cpp_allocators_agree(seed):
     rnd = random.Random(seed)
@@ -84,8 +107,9 @@ def test_python_and_cpp_allocators_agree(seed):
                 held.append((toks, ok[0]))
         elif op < 0.6 and held:
             toks, blks = held[rnd.randrange(len(held))]
-            py.commit_prefix(toks, blks)
-            cc.commit_prefix(toks, blks)
+            prio = rnd.choice([0, 0, 1, 5])
+            py.commit_prefix(toks, blks, prio)
+            cc.commit_prefix(toks, blks, prio)
         elif op < 0.8 and held:
             toks, blks = held.pop(rnd.randrange(len(held)))
             py.free(blks)
@@ -140,6 +164,46 @@ def test_preemption_frees_blocks_for_earlier_sequences():
     out = s.schedule()
     assert [q.seq_id for q in out.decode] == [1]
     assert b.status == SequenceStatus.WAITING and b.num_computed == 0 and s.num_preemptions == 1
+
+
+def test_swap_preemption_parks_and_restores_pages():
+    alloc = make_allocator(6, 16)
+    s = Scheduler(alloc, max_num_seqs=4, max_num_batched_tokens=4096, preemption="swap", swap_blocks=8)
+    a, b = mkseq(1, 48), mkseq(2, 48)
+    s.add(a)
+    s.add(b)
+    out = s.schedule()
+    for q, n in out.prefill:
+        q.num_computed += n
+        q.output_ids.append(1)
+    old_b = list(b.block_ids)
+    out = s.schedule()  # a needs a 4th block, none free: b is swapped out
+    assert [q.seq_id for q in out.decode] == [1]
+    assert out.preempted == [b] and out.swap_out == [(b, old_b)] and out.preempted_slots != [-1]
+    assert b.status == SequenceStatus.SWAPPED and b.num_computed == 48 and s.swap_used == 3
+    # a new request waits while b is parked
+    c = mkseq(3, 8)
+    s.add(c)
+    a.num_computed += 1
+    a.output_ids.append(2)
+    out = s.schedule()
+    assert c not in [q for q, _ in out.prefill] and not out.swap_in  # 2 free < 3 + 1 headroom
+    s.finish(a, SequenceStatus.FINISHED_LENGTH)
+    out = s.schedule()
+    assert [q for q, _ in out.swap_in] == [b] and len(out.swap_in[0][1]) == 3 and b in out.admitted
+    assert b.status == SequenceStatus.RUNNING and s.swap_used == 0 and s.num_swap_in == 1
+    assert b in out.decode and c in [q for q, _ in out.prefill]  # swapped first, then admission
+    # no host room: preemption falls back to recomputation
+    s2 = Scheduler(make_allocator(6, 16), max_num_seqs=4, max_num_batched_tokens=4096, preemption="swap",
+                   swap_blocks=2)
+    x, y = mkseq(1, 48), mkseq(2, 48)
+    s2.add(x)
+    s2.add(y)
+    for q, n in s2.schedule().prefill:
+        q.num_computed += n
+        q.output_ids.append(1)
+    out = s2.schedule()
+    assert not out.swap_out and y.status == SequenceStatus.WAITING and y.num_computed == 0
 
 
 def test_finish_keeps_prefix_for_reuse():

@@ -21,7 +21,7 @@ def make_engine(cfg, **kw):
     dev = torch.device("cuda", 0)
     w = random_weights(cfg, dev, seed=0, std=0.05)
     ecfg = EngineConfig(max_num_seqs=16, max_num_batched_tokens=kw.pop("chunk", 256), max_model_len=1024,
-                        num_blocks=512, **kw)
+                        num_blocks=kw.pop("num_blocks", 512), **kw)
     return LLMEngine(cfg, weights=w, device=dev, engine_cfg=ecfg)
 
 
@@ -95,3 +95,25 @@ def test_prefix_cache_reuse_and_preemption():
         eng.step()
     assert seq.num_cached_prefix == 96
     assert seq.output_ids == a
+
+
+@pytest.mark.parametrize("mode", ["recompute", "swap"])
+def test_preemption_keeps_sampled_outputs(mode):
+    """Too few KV blocks force preemptions; the sampler state of a preempted
+    sequence is read back from its device slot, so a recomputed or swapped
+    sequence continues the same random stream as in a roomy pool."""
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+
+    cfg = small_cfg()
+    prompts = [list(range(50 + i, 150 + i)) for i in range(6)]
+    p = SamplingParams(max_new_tokens=40, temperature=0.8, top_k=40, top_p=0.9, repetition_penalty=1.1,
+                       ignore_eos=True)
+    want = make_engine(cfg).generate(prompts, p)
+    eng = make_engine(cfg, num_blocks=24, preemption=mode)
+    got = eng.generate(prompts, p)
+    st = eng.kv_stats()
+    assert st["preemptions"] > 0
+    if mode == "swap":
+        assert st["swap_out_total"] > 0 and st["swap_in_total"] == st["swap_out_total"]
+    agree = sum(int(a == b) for g, w in zip(got, want) for a, b in zip(g, w))
+    assert agree >= 0.9 * sum(len(w) for w in want), (agree, got, want)

@@ -52,6 +52,25 @@ def test_reference_seeded_sampling_is_reproducible():
     assert a == b and len(a) == 8
 
 
+@pytest.mark.parametrize("mode", ["recompute", "swap"])
+def test_preemption_keeps_outputs(mode):
+    """A pool too small for the batch forces preemptions; recomputed or swapped
+    sequences continue their sampler streams, so outputs match a roomy pool."""
+    cfg = tiny_cfg()
+    prompts = [list(range(3 + i, 43 + i)) for i in range(4)]
+    p = SamplingParams(max_new_tokens=24, ignore_eos=True)
+    want = cpu_engine(cfg).generate(prompts, p)
+    eng = LLMEngine(
+        cfg, device="cpu", engine_cfg=EngineConfig(max_num_seqs=4, max_num_batched_tokens=32, max_model_len=256,
+                                                   num_blocks=9, preemption=mode), seed=0)
+    got = eng.generate(prompts, p)
+    st = eng.kv_stats()
+    assert got == want
+    assert st["preemptions"] > 0
+    if mode == "swap":
+        assert st["swap_out_total"] > 0 and st["swap_in_total"] == st["swap_out_total"] and not eng._swapped_kv
+
+
 def test_sessions_continue_previous_turn():
     cfg = tiny_cfg()
     eng = cpu_engine(cfg)
