@@ -416,6 +416,22 @@ void kv_push(Tensor src, int64_t dst_ptr, Tensor src_ids, Tensor dst_ids, int64_
                         dst_blocks_per_plane, block_bytes, kapsl::gemm_num_sms(), cur_stream());
 }
 
+// Block gather/scatter between any two device-accessible pools (this GPU's
+// memory, a peer's through CUDA IPC, or pinned host memory through unified
+// addressing): planes x blocks of block_bytes each, src_ids[i] -> dst_ids[i].
+// Used for KV swap-out to and swap-in from host memory in one launch.
+void kv_copy_blocks(int64_t src_ptr, int64_t dst_ptr, Tensor src_ids, Tensor dst_ids, int64_t planes,
+                    int64_t src_blocks_per_plane, int64_t dst_blocks_per_plane, int64_t block_bytes) {
+  CHECK_DT(src_ids, at::kInt, "src_ids");
+  CHECK_DT(dst_ids, at::kInt, "dst_ids");
+  TORCH_CHECK(src_ids.is_cuda() && dst_ids.is_cuda(), "kv_copy_blocks: id lists on the GPU");
+  TORCH_CHECK(src_ids.numel() == dst_ids.numel(), "kv_copy_blocks: id lists differ in length");
+  const c10::cuda::CUDAGuard g(src_ids.device());
+  kapsl::launch_kv_push(reinterpret_cast<const void*>(src_ptr), reinterpret_cast<void*>(dst_ptr),
+                        src_ids.data_ptr<int32_t>(), dst_ids.data_ptr<int32_t>(), (int)src_ids.numel(), (int)planes,
+                        src_blocks_per_plane, dst_blocks_per_plane, block_bytes, kapsl::gemm_num_sms(), cur_stream());
+}
+
 // Asynchronous copy on the current stream (copy engine) between device addresses,
 // either of which may be a peer GPU's memory mapped by CUDA IPC.
 void copy_async(int64_t dst_ptr, int64_t src_ptr, int64_t bytes) {
@@ -463,6 +479,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_gather", &moe_gather, "gather token rows into the expert-sorted buffer");
   m.def("moe_combine", &moe_combine, "weighted top-k combine + residual (+ peer pull and all-gather)");
   m.def("kv_push", &kv_push, "KV connector: copy pool blocks into a (peer) pool over NVLink");
+  m.def("kv_copy_blocks", &kv_copy_blocks, "KV block gather/scatter between device-accessible pools (host swap)");
   m.def("copy_async", &copy_async, "cudaMemcpyAsync on the current stream (copy-engine baseline)");
   m.def("tp_pull_reduce_ag", &tp_pull_reduce_ag, "barrier + pull peers' partial rows + residual + all-gather push");
   m.def("p2p_copy", &p2p_copy, "16-byte vector copy between (possibly peer-mapped) device addresses");

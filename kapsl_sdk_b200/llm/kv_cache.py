@@ -52,6 +52,7 @@ class KVPool:
                 self.storage = c.tensor_from_ptr(self._raw, list(shape), "bfloat16", self.device.index)
         else:
             self.storage = torch.zeros(shape, dtype=L.dtype, device=self.device)
+        self._in_flight: list = []  # (event, pinned host copy) read by a queued restore
         self.k = [self.storage[i, 0] for i in range(L.num_layers)]
         self.v = [self.storage[i, 1] for i in range(L.num_layers)]
 
@@ -82,17 +83,39 @@ class KVPool:
 
     # ------------------------------------------------------------ offload
     def offload(self, blocks: list[int]) -> torch.Tensor:
-        """Copy pages of ``blocks`` (all layers) into pinned host memory."""
-        idx = torch.as_tensor(blocks, dtype=torch.long, device=self.device)
-        host = torch.empty((self.layout.num_layers, 2, len(blocks)) + tuple(self.storage.shape[3:]),
+        """Copy pages of ``blocks`` (all layers) into host memory (pinned on a GPU
+        pool: one kernel writes them straight into it over unified addressing)."""
+        L = self.layout
+        host = torch.empty((L.num_layers, 2, len(blocks)) + tuple(self.storage.shape[3:]),
                            dtype=self.storage.dtype, pin_memory=self.device.type == "cuda")
-        host.copy_(self.storage.index_select(2, idx), non_blocking=True)
+        if self.device.type == "cuda" and blocks:
+            src = torch.as_tensor(blocks, dtype=torch.int32).to(self.device, non_blocking=True)
+            dst = torch.arange(len(blocks), dtype=torch.int32, device=self.device)
+            self._copy(self.storage.data_ptr(), host.data_ptr(), src, dst, self.num_blocks, len(blocks))
+        elif blocks:
+            host.copy_(self.storage.index_select(2, torch.as_tensor(blocks, dtype=torch.long)))
         return host
 
     def restore(self, host: torch.Tensor, blocks: list[int]) -> None:
         """Copy offloaded pages back into (possibly different) ``blocks``."""
-        idx = torch.as_tensor(blocks, dtype=torch.long, device=self.device)
-        self.storage.index_copy_(2, idx, host.to(self.device, non_blocking=True))
+        if self.device.type == "cuda" and blocks:
+            src = torch.arange(len(blocks), dtype=torch.int32, device=self.device)
+            dst = torch.as_tensor(blocks, dtype=torch.int32).to(self.device, non_blocking=True)
+            self._copy(host.data_ptr(), self.storage.data_ptr(), src, dst, len(blocks), self.num_blocks)
+            # the kernel reads ``host`` later on the stream: keep it until then
+            ev = torch.cuda.Event()
+            ev.record()
+            self._in_flight.append((ev, host))
+        elif blocks:
+            self.storage.index_copy_(2, torch.as_tensor(blocks, dtype=torch.long), host)
+        self._in_flight = [(e, h) for e, h in self._in_flight if not e.query()]
+
+    def _copy(self, src_ptr: int, dst_ptr: int, src_ids, dst_ids, src_blocks: int, dst_blocks: int) -> None:
+        from .._ext import cuda_ops
+
+        L = self.layout
+        cuda_ops().kv_copy_blocks(src_ptr, dst_ptr, src_ids, dst_ids, L.num_layers * 2, src_blocks, dst_blocks,
+                                  L.bytes_per_block() // (L.num_layers * 2))
 
     def copy_blocks(self, src: list[int], dst: list[int]) -> None:
         """Duplicate pages (copy-on-write of a shared prefix block)."""
