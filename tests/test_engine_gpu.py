@@ -98,22 +98,66 @@ def test_prefix_cache_reuse_and_preemption():
 
 
 @pytest.mark.parametrize("mode", ["recompute", "swap"])
-def test_preemption_keeps_sampled_outputs(mode):
-    """Too few KV blocks force preemptions; the sampler state of a preempted
-    sequence is read back from its device slot, so a recomputed or swapped
-    sequence continues the same random stream as in a roomy pool."""
+def test_preemption_keeps_sampler_state_and_kv(mode):
+    """Too few KV blocks force preemptions.  (1) The LCG state of each preempted
+    sequence, read back from its device slot, equals its seed advanced once per
+    sampled token, so it continues the same random stream when it resumes.
+    (2) Greedy outputs mostly match a roomy pool (the decode split-KV count
+    follows the batch size, so a near-tie can flip a token and the rest of
+    that sequence; page contents are checked bit for bit in the pool test)."""
     from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.ops import reference as ref
 
     cfg = small_cfg()
     prompts = [list(range(50 + i, 150 + i)) for i in range(6)]
-    p = SamplingParams(max_new_tokens=40, temperature=0.8, top_k=40, top_p=0.9, repetition_penalty=1.1,
-                       ignore_eos=True)
-    want = make_engine(cfg).generate(prompts, p)
     eng = make_engine(cfg, num_blocks=24, preemption=mode)
-    got = eng.generate(prompts, p)
+    seen = []
+    orig = eng._apply_preemptions
+
+    def spy(batch):
+        orig(batch)
+        seen.extend((s, s.rng_state, len(s.output_ids)) for s in batch.preempted)
+
+    eng._apply_preemptions = spy
+    p = SamplingParams(max_new_tokens=40, temperature=0.8, top_k=40, top_p=0.9, ignore_eos=True)
+    seqs = [eng.add_request(f"r{i}", q, p) for i, q in enumerate(prompts)]
+    while eng.has_unfinished():
+        eng.step()
+    assert all(len(s.output_ids) == 40 for s in seqs)
+    assert any(n > 0 for _, _, n in seen), "no sequence was preempted after sampling"
+    for s, st, n in seen:
+        x = ref.seed_state(None, s.request_id, s.seq_id)
+        for _ in range(n):
+            x = (x * 6364136223846793005 + 1) & ((1 << 64) - 1)
+        assert st == x, (s.request_id, n)
     st = eng.kv_stats()
-    assert st["preemptions"] > 0
     if mode == "swap":
-        assert st["swap_out_total"] > 0 and st["swap_in_total"] == st["swap_out_total"]
-    agree = sum(int(a == b) for g, w in zip(got, want) for a, b in zip(g, w))
-    assert agree >= 0.9 * sum(len(w) for w in want), (agree, got, want)
+        assert st["swap_out_total"] > 0 and st["swap_in_total"] == st["swap_out_total"] and not eng._swapped_kv
+
+    g = SamplingParams.greedy(40, ignore_eos=True)
+    want = make_engine(cfg).generate(prompts, g)
+    tight = make_engine(cfg, num_blocks=24, preemption=mode)
+    got = tight.generate(prompts, g)
+    assert tight.kv_stats()["preemptions"] > 0
+    agree = sum(int(a == b) for x, y in zip(got, want) for a, b in zip(x, y))
+    assert agree >= 0.75 * sum(len(w) for w in want), (agree, got, want)
+    assert sum(int(x == y) for x, y in zip(got, want)) >= 4, (got, want)
+
+
+def test_kv_pool_offload_restore_bitwise():
+    """Swap-out gathers pages into pinned host memory and swap-in scatters them
+    into other pages, both with the block-copy kernel: bit-exact round trip."""
+    from kapsl_sdk_b200.llm.kv_cache import KVLayout, KVPool
+
+    pool = KVPool(KVLayout(num_layers=3, num_kv_heads=2, head_dim=128, block_size=16), 40, "cuda:0")
+    pool.storage.copy_(torch.randn(pool.storage.shape, device="cuda:0").to(torch.bfloat16))
+    before = pool.storage.clone()
+    host = pool.offload([5, 9, 2, 31])
+    torch.cuda.synchronize()
+    assert host.is_pinned()
+    assert torch.equal(host.to("cuda:0"), before[:, :, [5, 9, 2, 31]])
+    pool.restore(host, [11, 3, 7, 0])
+    torch.cuda.synchronize()
+    assert torch.equal(pool.storage[:, :, [11, 3, 7, 0]], before[:, :, [5, 9, 2, 31]])
+    untouched = [b for b in range(40) if b not in (11, 3, 7, 0)]
+    assert torch.equal(pool.storage[:, :, untouched], before[:, :, untouched])
