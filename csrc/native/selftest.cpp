@@ -1,0 +1,324 @@
+// Standalone self-test of the C++ runtime pieces that run without Python: the
+// SHM region and MPMC rings, the slot / tiered / per-model allocators, the
+// cross-process lease words, the paged-KV block allocator, the bincode codec and
+// the CPU kernels' thread pool.  Built with -fsanitize=thread and with
+// -fsanitize=address,undefined so races and memory errors in this code show up
+// on the host (device code has its own bounds checks).
+//
+//   g++ -std=c++17 -O1 -g -fsanitize=thread selftest.cpp shm.cpp wire.cpp \
+//       block_alloc.cpp cpu_kernels.cpp -I. -pthread -lrt -o selftest && ./selftest
+//
+// Exit status 0 means every check passed; each failed check prints one line.
+#include <unistd.h>
+
+#include <algorithm>
+#include <atomic>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <random>
+#include <set>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "block_alloc.h"
+#include "cpu_kernels.h"
+#include "shm.h"
+#include "wire.h"
+
+using namespace kapsl;
+
+static int g_failures = 0;
+#define CHECK(cond, ...)                                   \
+  do {                                                     \
+    if (!(cond)) {                                         \
+      ++g_failures;                                        \
+      std::fprintf(stderr, "FAIL %s:%d: ", __FILE__, __LINE__); \
+      std::fprintf(stderr, __VA_ARGS__);                   \
+      std::fprintf(stderr, "\n");                          \
+    }                                                      \
+  } while (0)
+
+static std::string region_name(const char* tag) {
+  return std::string("kapsl-selftest-") + tag + "-" + std::to_string(getpid());
+}
+
+// Producers and consumers hammer one ring; every item arrives exactly once.
+static void test_ring_mpmc() {
+  shm::Region r = shm::Region::create(region_name("ring"), 1 << 20);
+  shm::Ring<shm::ShmRequest> init(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, true);
+  constexpr int P = 4, C = 4, N = 5000;
+  std::vector<std::atomic<uint8_t>> seen(P * N);
+  for (auto& s : seen) s.store(0);
+  std::atomic<int> got{0};
+  std::vector<std::thread> ts;
+  for (int p = 0; p < P; ++p)
+    ts.emplace_back([&, p] {
+      shm::Ring<shm::ShmRequest> q(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, false);
+      for (int i = 0; i < N; ++i) {
+        shm::ShmRequest it{};
+        it.meta.request_id = (uint64_t)p * N + i;
+        it.tensor_offset = it.meta.request_id * 7;
+        while (!q.push(it)) std::this_thread::yield();
+      }
+    });
+  for (int c = 0; c < C; ++c)
+    ts.emplace_back([&] {
+      shm::Ring<shm::ShmRequest> q(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, false);
+      const auto t0 = std::chrono::steady_clock::now();
+      while (got.load() < P * N && std::chrono::steady_clock::now() - t0 < std::chrono::seconds(60)) {
+        auto it = q.pop();
+        if (!it) {
+          std::this_thread::yield();
+          continue;
+        }
+        const uint64_t id = it->meta.request_id;
+        CHECK(id < (uint64_t)P * N && it->tensor_offset == id * 7, "ring: corrupt item %llu", (unsigned long long)id);
+        if (id < (uint64_t)P * N) CHECK(seen[id].fetch_add(1) == 0, "ring: item %llu twice", (unsigned long long)id);
+        got.fetch_add(1);
+      }
+    });
+  for (auto& t : ts) t.join();
+  CHECK(got.load() == P * N, "ring: %d of %d items arrived", got.load(), P * N);
+}
+
+// The SHM client pattern: clients share one response ring, pop whatever is at
+// the tail and push back responses addressed to someone else.  Every client
+// must receive all of its own responses.
+static void test_ring_repush() {
+  shm::Region r = shm::Region::create(region_name("repush"), 1 << 20);
+  shm::Ring<shm::ShmResponse> init(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, true);
+  constexpr int K = 4, N = 500;
+  std::atomic<int> done{0};
+  std::vector<std::thread> ts;
+  ts.emplace_back([&] {  // the server: responses for every client, interleaved
+    shm::Ring<shm::ShmResponse> q(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, false);
+    for (int i = 0; i < N; ++i)
+      for (int k = 0; k < K; ++k) {
+        shm::ShmResponse it{};
+        it.meta.request_id = ((uint64_t)k << 32) | (uint64_t)i;
+        // keep room for the clients' pushes back (a full ring would leave every
+        // client holding a popped response it cannot return)
+        while (q.len() > 64) std::this_thread::yield();
+        while (!q.push(it)) std::this_thread::yield();
+      }
+  });
+  for (int k = 0; k < K; ++k)
+    ts.emplace_back([&, k] {
+      shm::Ring<shm::ShmResponse> q(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, false);
+      std::vector<uint8_t> mine(N, 0);
+      int have = 0;
+      const auto t0 = std::chrono::steady_clock::now();
+      while (have < N && std::chrono::steady_clock::now() - t0 < std::chrono::seconds(60)) {
+        auto it = q.pop();
+        if (!it) {
+          std::this_thread::yield();
+          continue;
+        }
+        const uint64_t owner = it->meta.request_id >> 32, idx = it->meta.request_id & 0xffffffffu;
+        if ((int)owner != k) {
+          while (!q.push(*it)) std::this_thread::yield();
+          continue;
+        }
+        CHECK(idx < (uint64_t)N && !mine[idx], "repush: client %d got %llu twice", k, (unsigned long long)idx);
+        if (idx < (uint64_t)N) mine[idx] = 1;
+        ++have;
+      }
+      CHECK(have == N, "repush: client %d got %d of %d responses", k, have, N);
+      done.fetch_add(1);
+    });
+  for (auto& t : ts) t.join();
+}
+
+// Concurrent allocate / release on the per-model pools: no offset is ever
+// handed to two holders at once.
+static void test_model_pools() {
+  const uint64_t MiB = 1 << 20;
+  auto plan = shm::ModelPools::plan(64 * MiB, {{1, 3}, {2, 1}});
+  std::vector<shm::ModelPoolSpec> specs;
+  for (auto& [id, b] : plan) specs.push_back({id, b, {256 << 10, MiB}, {3, 1}});
+  shm::ModelPools pools(4096, 64 * MiB, specs, 60.0);
+  std::mutex mu;
+  std::set<uint64_t> held;
+  std::vector<std::thread> ts;
+  for (int t = 0; t < 6; ++t)
+    ts.emplace_back([&, t] {
+      std::mt19937 rng(t);
+      std::vector<uint64_t> mine;
+      for (int i = 0; i < 4000; ++i) {
+        if (mine.size() < 8 && rng() % 3) {
+          const uint32_t model = rng() % 4;  // 0 and 3 have no pool of their own
+          const uint64_t size = 1 + rng() % (MiB - 1);
+          if (auto o = pools.try_allocate(model, size)) {
+            std::lock_guard<std::mutex> g(mu);
+            CHECK(held.insert(*o).second, "pools: offset %llu handed out twice", (unsigned long long)*o);
+            mine.push_back(*o);
+          }
+        } else if (!mine.empty()) {
+          const uint64_t o = mine.back();
+          mine.pop_back();
+          {
+            std::lock_guard<std::mutex> g(mu);
+            held.erase(o);
+          }
+          CHECK(pools.release(o), "pools: release of %llu failed", (unsigned long long)o);
+        }
+      }
+      for (uint64_t o : mine) {
+        {
+          std::lock_guard<std::mutex> g(mu);
+          held.erase(o);
+        }
+        pools.release(o);
+      }
+    });
+  for (auto& t : ts) t.join();
+  CHECK(pools.total_usage().in_use == 0, "pools: %zu slots still leased", pools.total_usage().in_use);
+}
+
+// Two lease tables over one region (two client processes): exclusive slots.
+static void test_shared_leases() {
+  shm::Region r = shm::Region::create(region_name("lease"), 8 << 20);
+  const uint64_t base = shm::TENSOR_POOL_OFFSET, bytes = r.size() - base;
+  std::mutex mu;
+  std::set<uint64_t> held;
+  std::vector<std::thread> ts;
+  for (int t = 0; t < 4; ++t)
+    ts.emplace_back([&, t] {
+      shm::SharedLeases leases(r, base, bytes, 60.0);
+      std::mt19937 rng(100 + t);
+      for (int i = 0; i < 3000; ++i) {
+        if (auto o = leases.try_allocate(1 + rng() % (200 << 10))) {
+          {
+            std::lock_guard<std::mutex> g(mu);
+            CHECK(held.insert(*o).second, "leases: offset %llu leased twice", (unsigned long long)*o);
+          }
+          std::this_thread::yield();
+          {
+            std::lock_guard<std::mutex> g(mu);
+            held.erase(*o);
+          }
+          CHECK(leases.release(*o), "leases: release failed");
+        }
+      }
+    });
+  for (auto& t : ts) t.join();
+}
+
+// Random allocate / free / prefix traffic on the block allocator; the free
+// count always balances.
+static void test_block_allocator() {
+  for (const char* ev : {"lru", "fifo"}) {
+    BlockAllocator a(64, 4, true, ev);
+    std::mt19937 rng(7);
+    std::vector<std::pair<std::vector<int32_t>, std::vector<int64_t>>> held;
+    for (int step = 0; step < 20000; ++step) {
+      const int op = rng() % 10;
+      if (op < 4) {
+        const int n = 1 + rng() % 5;
+        try {
+          auto b = a.allocate(n);
+          std::vector<int32_t> toks(4 * n);
+          for (auto& x : toks) x = rng() % 3;
+          held.push_back({toks, b});
+        } catch (const OutOfBlocksError&) {
+        }
+      } else if (op < 6 && !held.empty()) {
+        auto& h = held[rng() % held.size()];
+        a.commit_prefix(h.first, h.second, (int)(rng() % 4));
+      } else if (op < 8 && !held.empty()) {
+        const size_t i = rng() % held.size();
+        a.free(held[i].second);
+        held.erase(held.begin() + i);
+      } else {
+        std::vector<int32_t> toks(1 + rng() % 20);
+        for (auto& x : toks) x = rng() % 3;
+        auto m = a.match_prefix(toks);
+        if (!m.empty()) held.push_back({std::vector<int32_t>(toks.begin(), toks.begin() + 4 * m.size()), m});
+      }
+      int64_t used = 0;
+      for (auto& h : held) used += (int64_t)h.second.size();
+      CHECK(a.num_used() <= used, "blocks: %lld used but %lld held", (long long)a.num_used(), (long long)used);
+    }
+    for (auto& h : held) a.free(h.second);
+    CHECK(a.num_free() == 64, "blocks: %lld free after releasing everything", (long long)a.num_free());
+  }
+}
+
+// Round trips, then every truncated prefix of an encoded request must be
+// rejected without reading past the payload.
+static void test_wire() {
+  std::mt19937 rng(3);
+  for (int i = 0; i < 200; ++i) {
+    wire::Request req;
+    req.input.shape = {1 + (int64_t)(rng() % 4), 1 + (int64_t)(rng() % 5)};
+    req.input.dtype = "float32";
+    req.input.data.assign(req.input.shape[0] * req.input.shape[1] * 4, (char)(rng() & 0xff));
+    if (rng() % 2) req.session_id = "s" + std::to_string(i);
+    if (rng() % 2) {
+      wire::Metadata m;
+      m.request_id = "r" + std::to_string(i);
+      if (rng() % 2) m.auth_token = "tok";
+      if (rng() % 2) m.temperature = 0.5f;
+      if (rng() % 2) m.stop_token_ids = std::vector<uint32_t>{1, 2, 3};
+      req.metadata = m;
+    }
+    const std::string enc = wire::encode_request(req);
+    wire::Request back = wire::decode_request(enc);
+    CHECK(back.input.data == req.input.data && back.input.shape == req.input.shape &&
+              back.session_id == req.session_id,
+          "wire: round trip %d", i);
+    for (size_t n = 0; n < enc.size(); n += 1 + enc.size() / 64) {
+      try {
+        wire::decode_request(enc.substr(0, n));
+      } catch (const std::exception&) {
+      }
+    }
+  }
+}
+
+// The CPU kernels' worker pool from several caller threads at once.
+static void test_cpu_pool() {
+  const int64_t rows = 257, d = 300;
+  std::vector<std::thread> ts;
+  for (int t = 0; t < 3; ++t)
+    ts.emplace_back([&, t] {
+      std::mt19937 rng(t);
+      std::uniform_real_distribution<float> U(-1, 1);
+      std::vector<float> x(rows * d), w(d), out(rows * d);
+      for (auto& v : x) v = U(rng);
+      for (auto& v : w) v = U(rng);
+      cpu::rmsnorm(x.data(), w.data(), out.data(), rows, d, 1e-5f);
+      for (int64_t r = 0; r < rows; r += 37) {
+        double ss = 0;
+        for (int64_t j = 0; j < d; ++j) ss += (double)x[r * d + j] * x[r * d + j];
+        const double inv = 1.0 / std::sqrt(ss / d + 1e-5);
+        for (int64_t j = 0; j < d; j += 29)
+          CHECK(std::fabs(out[r * d + j] - x[r * d + j] * inv * w[j]) < 1e-4, "cpu pool: rmsnorm row %lld",
+                (long long)r);
+      }
+    });
+  for (auto& t : ts) t.join();
+}
+
+int main(int argc, char** argv) {
+  const std::pair<const char*, void (*)()> tests[] = {
+      {"ring_mpmc", test_ring_mpmc},         {"ring_repush", test_ring_repush}, {"model_pools", test_model_pools},
+      {"shared_leases", test_shared_leases}, {"block_allocator", test_block_allocator}, {"wire", test_wire},
+      {"cpu_pool", test_cpu_pool}};
+  for (auto& [name, fn] : tests) {
+    if (argc > 1 && std::string(argv[1]) != name) continue;
+    const auto t0 = std::chrono::steady_clock::now();
+    fn();
+    std::printf("%s %.2fs\n", name, std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count());
+    std::fflush(stdout);
+  }
+  if (g_failures) {
+    std::fprintf(stderr, "%d check(s) failed\n", g_failures);
+    return 1;
+  }
+  std::printf("selftest ok\n");
+  return 0;
+}

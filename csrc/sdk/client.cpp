@@ -455,7 +455,10 @@ class KapslShmClient {
           auto r = resp.pop();
           if (r) {
             if (r->meta.request_id != rid) {
-              resp.push(*r);  // another client's response: put it back
+              // another client's response: put it back (retry while the ring is full,
+              // dropping it would leave its owner waiting until its timeout)
+              while (!resp.push(*r) && std::chrono::steady_clock::now() - t0 < std::chrono::seconds(5))
+                std::this_thread::yield();
             } else {
               if (r->meta.status != 0) {
                 err = r->error_offset ? shm::read_error(*region_, r->error_offset) : "Unknown error";
