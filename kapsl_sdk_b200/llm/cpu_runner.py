@@ -25,6 +25,9 @@ class CPUModelRunner:
     def admit(self, seqs: list) -> None:
         return None
 
+    def reset_slots(self, seqs: list) -> None:
+        return None  # sampler state and penalty counts live on the host sequences
+
     def _prepare(self, batch: ScheduledBatch):
         ids, pos, slots, seqs, rows, sample = [], [], [], [], [], []
         t = 0

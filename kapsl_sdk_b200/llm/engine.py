@@ -212,6 +212,39 @@ class LLMEngine:
             s.finish_reason = "aborted"
             self._swapped_kv.pop(s.seq_id, None)
 
+    def rollback(self, request_id: str, length: int) -> int:
+        """Truncate the live request ``request_id`` to its first ``length`` tokens
+        (prompt + output); generation then continues from there.  Returns the
+        number of sequences changed."""
+        table = getattr(self.runner, "rng_table", None)
+        hit = [s for s in list(self.scheduler.running) + list(self.scheduler.waiting) + list(self.scheduler.swapped)
+               if s.request_id == request_id]
+        readmit = []
+        for s in hit:
+            self._swapped_kv.pop(s.seq_id, None)
+            running = s in self.scheduler.running
+            if running and table is not None:  # keep the sampler stream (state lives in the slot)
+                s.rng_state = int(table[s.slot].item()) & ((1 << 64) - 1)
+            self.scheduler.rollback(s, length)
+            if running and s in self.scheduler.running:
+                readmit.append(s)
+        if readmit:
+            self.runner.reset_slots(readmit)  # penalty counts from the kept tokens, sampler state
+        return len(hit)
+
+    def rollback_session(self, session_id: str, length: int) -> None:
+        """Drop the history of ``session_id`` past its first ``length`` tokens; the
+        next turn continues from the shortened history (its cached prefix pages
+        are reused up to there)."""
+        s = self.sessions.get(session_id)
+        if s is None:
+            raise KeyError(session_id)
+        if s.status.finished:
+            ids = s.all_ids[:length]
+            s.prompt_ids, s.output_ids = ids, []
+        else:
+            self.rollback(s.request_id, length)
+
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work()
 

@@ -220,6 +220,20 @@ class ModelRunner:
         self._pending_admit = n
         self._admit_prompts = [(s.slot, s.prompt_ids + s.output_ids) for s in seqs]
 
+    def reset_slots(self, seqs: list) -> None:
+        """Re-initialise the per-slot state (LCG state, penalty counts) of running
+        sequences now, on the current stream (between steps, e.g. after a rollback)."""
+        if not seqs:
+            return
+        slots = torch.as_tensor([s.slot for s in seqs], dtype=torch.long).to(self.device)
+        rng = torch.as_tensor([s.rng_state - (1 << 64) if s.rng_state >= (1 << 63) else s.rng_state for s in seqs],
+                              dtype=torch.int64).to(self.device)
+        self.rng_table.index_copy_(0, slots, rng)
+        self.counts.index_fill_(0, slots, 0)
+        rows = np.concatenate([np.full(len(s.all_ids), s.slot, dtype=np.int32) for s in seqs])
+        ids = np.concatenate([np.asarray(s.all_ids, dtype=np.int32) for s in seqs])
+        ops.count_tokens(self.counts, torch.from_numpy(rows).to(self.device), torch.from_numpy(ids).to(self.device))
+
     def _apply_admissions(self) -> None:
         n = getattr(self, "_pending_admit", 0)
         if not n:

@@ -229,6 +229,33 @@ class Scheduler:
         if not keep_blocks:
             self._release(seq)
 
+    def rollback(self, seq: Sequence, length: int) -> None:
+        """Truncate ``seq`` to its first ``length`` tokens (prompt, then output).
+        KV of positions below ``length - 1`` stays; the last kept token is
+        recomputed by the next step, which also samples the next token.  Pages
+        past the new length go back to the allocator; a swapped sequence drops
+        its host copy and is recomputed (reference kv_cache.rs:1156-1203)."""
+        if length >= seq.length or length < 1:
+            return
+        npr = len(seq.prompt_ids)
+        if length <= npr:
+            seq.prompt_ids = seq.prompt_ids[:length]
+            seq.output_ids = []
+        else:
+            seq.output_ids = seq.output_ids[:length - npr]
+        if seq in self.swapped:
+            self.swapped.remove(seq)
+            self.swap_used -= self._computed_blocks(seq)
+            seq.num_computed = 0
+            seq.status = SequenceStatus.WAITING
+            self.waiting.appendleft(seq)
+            return
+        seq.num_computed = min(seq.num_computed, length - 1)
+        keep = (length + self.bs - 1) // self.bs
+        if len(seq.block_ids) > keep:
+            self.alloc.free(seq.block_ids[keep:])
+            seq.block_ids = seq.block_ids[:keep]
+
     def abort(self, request_id: str) -> list[Sequence]:
         hit = [s for s in list(self.running) + list(self.waiting) + list(self.swapped) if s.request_id == request_id]
         for s in hit:

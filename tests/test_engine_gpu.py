@@ -161,3 +161,24 @@ def test_kv_pool_offload_restore_bitwise():
     assert torch.equal(pool.storage[:, :, [11, 3, 7, 0]], before[:, :, [5, 9, 2, 31]])
     untouched = [b for b in range(40) if b not in (11, 3, 7, 0)]
     assert torch.equal(pool.storage[:, :, untouched], before[:, :, untouched])
+
+
+def test_rollback_regenerates_greedy():
+    """Rollback keeps the KV below the cut and resets the slot's penalty counts;
+    greedy decoding regenerates the tokens that were cut."""
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+
+    cfg = small_cfg()
+    prompt = list(range(100, 300))
+    g = SamplingParams(max_new_tokens=16, temperature=0.0, top_k=0, top_p=1.0, repetition_penalty=1.3,
+                       ignore_eos=True)
+    full = make_engine(cfg).generate([prompt], g)[0]
+    eng = make_engine(cfg)
+    seq = eng.add_request("r", prompt, g)
+    while len(seq.output_ids) < 10:
+        eng.step()
+    assert eng.rollback("r", len(prompt) + 4) == 1
+    assert seq.output_ids == full[:4]
+    while eng.has_unfinished():
+        eng.step()
+    assert seq.output_ids == full

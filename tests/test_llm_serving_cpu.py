@@ -71,6 +71,48 @@ def test_preemption_keeps_outputs(mode):
         assert st["swap_out_total"] > 0 and st["swap_in_total"] == st["swap_out_total"] and not eng._swapped_kv
 
 
+def test_rollback_truncates_and_regenerates():
+    """Rolling a live request back keeps the KV below the cut; greedy decoding
+    then regenerates exactly the tokens that were cut."""
+    cfg = tiny_cfg()
+    prompt = list(range(5, 45))
+    full = cpu_engine(cfg).generate([prompt], SamplingParams.greedy(12, ignore_eos=True))[0]
+    eng = cpu_engine(cfg)
+    seq = eng.add_request("r", prompt, SamplingParams.greedy(12, ignore_eos=True))
+    while len(seq.output_ids) < 8:
+        eng.step()
+    blocks_before = len(seq.block_ids)
+    assert eng.rollback("r", len(prompt) + 3) == 1
+    assert seq.output_ids == full[:3] and seq.num_computed == len(prompt) + 2
+    assert len(seq.block_ids) <= blocks_before
+    while eng.has_unfinished():
+        eng.step()
+    assert seq.output_ids == full
+    # back into the prompt: the prompt itself is cut, then generation restarts from it
+    seq2 = eng.add_request("r2", prompt, SamplingParams.greedy(5, ignore_eos=True))
+    while len(seq2.output_ids) < 2:
+        eng.step()
+    eng.rollback("r2", 30)
+    assert seq2.prompt_ids == prompt[:30] and seq2.output_ids == []
+    while eng.has_unfinished():
+        eng.step()
+    want = cpu_engine(cfg).generate([prompt[:30]], SamplingParams.greedy(5, ignore_eos=True))[0]
+    assert seq2.output_ids == want
+    assert eng.allocator.num_free() == eng.allocator.num_blocks
+
+
+def test_session_rollback_shortens_history():
+    cfg = tiny_cfg()
+    eng = cpu_engine(cfg)
+    s1 = eng.add_request("a", [10, 11, 12, 13], SamplingParams.greedy(4, ignore_eos=True), session_id="s")
+    while eng.has_unfinished():
+        eng.step()
+    first = s1.output_ids[0]
+    eng.rollback_session("s", 5)
+    s2 = eng.add_request("b", [20], SamplingParams.greedy(2, ignore_eos=True), session_id="s")
+    assert s2.prompt_ids == [10, 11, 12, 13, first, 20]
+
+
 def test_sessions_continue_previous_turn():
     cfg = tiny_cfg()
     eng = cpu_engine(cfg)
