@@ -339,10 +339,10 @@ def _cpu_server(gguf: str, sock: str, num_requests: int, chunk: int, max_len: in
                                                max_model_len=max_len, block_size=16, num_blocks=num_requests * 16),
                        seed=0)
     rc = RuntimeConfig(sampling=SamplingParams.greedy(output_len, ignore_eos=True))
-    backend = LLMBackend(engine, tokenizer=tok, runtime_config=rc)
+    backend = LLMBackend(engine, tokenizer=tok, runtime_config=rc, own_thread=False)
     srv = KapslServer(models={0: backend}).listen_unix(sock).start()
-    while srv is not None:  # keep the server object alive until the process is terminated
-        time.sleep(3600)
+    backend.run()  # the engine loop on the thread that built the model (one OpenMP team)
+    srv.stop()
 
 
 def run_cpu_serving(args) -> int:

@@ -1,5 +1,7 @@
-// fp32 CPU kernels of the CPU backend (see cpu_kernels.h), parallel over a
-// small persistent thread pool.
+// fp32 CPU kernels of the CPU backend (see cpu_kernels.h).  In the Python
+// module they run on OpenMP from PyTorch's libgomp, so the worker team that
+// serves torch's GEMMs also serves these kernels; built without OpenMP (the
+// standalone sanitizer build) they use a small persistent thread pool.
 //
 // Reference counterpart: crates/kapsl-kernels/src/attention/mod.rs:8-99 (naive
 // f32 attention without a block table) and src/mlp/mod.rs:7-49 (SwiGLU); the
@@ -16,10 +18,36 @@
 #include <thread>
 #include <vector>
 
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
 namespace kapsl {
 namespace cpu {
 
 namespace {
+
+#ifdef _OPENMP
+// Items [0, n) in static contiguous chunks over at most one thread per `grain` items.
+template <class F>
+void parallel_for(int64_t n, int64_t grain, F&& body) {
+  const int64_t parts = std::min<int64_t>(omp_get_max_threads(), std::max<int64_t>(1, n / std::max<int64_t>(grain, 1)));
+  if (parts <= 1) {
+    for (int64_t i = 0; i < n; ++i) body(i);
+    return;
+  }
+  // the full team every time (a changing team size makes libgomp rebuild it);
+  // threads past `parts` have no range
+#pragma omp parallel
+  {
+    const int64_t id = omp_get_thread_num();
+    if (id < parts) {
+      const int64_t b = n * id / parts, e = n * (id + 1) / parts;
+      for (int64_t i = b; i < e; ++i) body(i);
+    }
+  }
+}
+#else
 
 // Persistent worker threads; parallel_for splits [0, n) into one contiguous
 // range per thread (the calling thread takes the first).  Small ranges run
@@ -102,6 +130,7 @@ void parallel_for(int64_t n, int64_t min_per_thread, F&& body) {
   };
   Pool::get().run(n, min_per_thread, fn);
 }
+#endif
 
 }  // namespace
 
@@ -198,12 +227,15 @@ void paged_attention(const float* q, const float* k_cache, const float* v_cache,
 }
 
 void silu_mul(const float* x, float* out, int64_t T, int64_t F) {
-  parallel_for(T, 1, [&](int64_t t) {
+  // chunks of up to 1024 features of one row; a thread per 16 chunks at least
+  const int64_t per_row = (F + 1023) / 1024;
+  parallel_for(T * per_row, 16, [&](int64_t c) {
+    const int64_t t = c / per_row, j0 = (c % per_row) * 1024, j1 = std::min<int64_t>(F, j0 + 1024);
     const float* g = x + t * 2 * F;
     const float* u = g + F;
     float* o = out + t * F;
 #pragma omp simd
-    for (int64_t j = 0; j < F; ++j) o[j] = g[j] / (1.f + std::exp(-g[j])) * u[j];
+    for (int64_t j = j0; j < j1; ++j) o[j] = g[j] / (1.f + std::exp(-g[j])) * u[j];
   });
 }
 

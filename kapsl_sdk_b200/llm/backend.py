@@ -156,10 +156,16 @@ class _Pending:
 
 
 class LLMBackend(Engine):
-    """Engine over an LLMEngine run by a dedicated thread."""
+    """Engine over an LLMEngine run by a dedicated thread.
+
+    ``load(path)`` builds the model on that thread, so all of a CPU model's
+    compute happens on one thread and uses one OpenMP worker team (PyTorch's
+    libgomp throttles its workers when two threads each drive a team, which
+    slows every matmul).  A caller that builds the engine itself can pass
+    ``own_thread=False`` and run the loop on its own thread with :meth:`run`."""
 
     def __init__(self, engine=None, tokenizer=None, runtime_config: Optional[RuntimeConfig] = None,
-                 admission_control: bool = False):
+                 admission_control: bool = False, own_thread: bool = True):
         self.engine = engine
         self.tokenizer = tokenizer
         self.rc = runtime_config or RuntimeConfig()
@@ -168,34 +174,75 @@ class LLMBackend(Engine):
         self._live: dict = {}
         self._thread: Optional[threading.Thread] = None
         self._stop = threading.Event()
+        self._loop_done = threading.Event()
+        self._caller_loop = False
         self._lock = threading.Lock()
         self._stats = {"requests": 0, "errors": 0, "tokens": 0, "busy_s": 0.0}
         self._peak = 0
         if engine is not None:
-            self._start()
+            self._default_tokenizer()
+            if own_thread:
+                self._start()
 
     # -------------------------------------------------------------- load
     def load(self, model_path: str) -> None:
-        """Load a model directory or package (see :mod:`kapsl_sdk_b200.runtime.loader`)."""
+        """Load a model directory or package (see :mod:`kapsl_sdk_b200.runtime.loader`)
+        on the engine thread, which then serves it."""
         from ..runtime.loader import build_llm_engine
 
-        self.engine, self.tokenizer, self.rc = build_llm_engine(model_path)
-        self._start()
+        ready, err = threading.Event(), []
 
-    def _start(self) -> None:
+        def body():
+            try:
+                self.engine, self.tokenizer, self.rc = build_llm_engine(model_path)
+                self._default_tokenizer()
+            except BaseException as e:  # reported to the caller of load()
+                err.append(e)
+                return
+            finally:
+                ready.set()
+            self._loop()
+
+        self._stop.clear()
+        self._thread = threading.Thread(target=body, name="kapsl-llm-engine", daemon=True)
+        self._thread.start()
+        ready.wait()
+        if err:
+            self._thread.join()
+            self._thread = None
+            raise err[0]
+
+    def run(self) -> None:
+        """Serve on the calling thread until :meth:`unload` (for ``own_thread=False``)."""
+        self._stop.clear()
+        self._caller_loop = True
+        self._loop_done.clear()
+        self._thread = threading.current_thread()
+        try:
+            self._loop()
+        finally:
+            self._loop_done.set()
+
+    def _default_tokenizer(self) -> None:
         if self.tokenizer is None:
             from .tokenizer import ByteTokenizer
 
             c = self.engine.cfg
             self.tokenizer = ByteTokenizer(c.vocab_size, c.bos_token_id, c.eos_token_id)
+
+    def _start(self) -> None:
         self._stop.clear()
         self._thread = threading.Thread(target=self._loop, name="kapsl-llm-engine", daemon=True)
         self._thread.start()
 
     def unload(self) -> None:
         self._stop.set()
-        if self._thread is not None:
-            self._thread.join(timeout=30)
+        t = self._thread
+        if t is not None and t is not threading.current_thread():
+            if self._caller_loop:  # run() on a caller's thread: wait for the loop, not the thread
+                self._loop_done.wait(timeout=30)
+            else:
+                t.join(timeout=30)
         self._thread = None
         if self.engine is not None:
             self.engine.shutdown()

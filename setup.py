@@ -50,14 +50,22 @@ def native_extensions():
     from pybind11.setup_helpers import Pybind11Extension
 
     exts = []
-    native_src = _rel(glob.glob(os.path.join(ROOT, "csrc", "native", "*.cpp")))
+    # selftest.cpp is a standalone program (sanitizer builds), not part of the module
+    native_src = [s for s in _rel(glob.glob(os.path.join(ROOT, "csrc", "native", "*.cpp")))
+                  if os.path.basename(s) != "selftest.cpp"]
     if native_src:
+        # The CPU kernels use OpenMP from PyTorch's own libgomp, so one worker team serves
+        # both torch's GEMMs and these kernels (a second thread pool would compete for the
+        # cores and make libgomp throttle its spinning).
+        import torch
+
+        torch_lib = os.path.join(os.path.dirname(torch.__file__), "lib")
         exts.append(Pybind11Extension(
             "kapsl_sdk_b200._native",
             native_src,
             include_dirs=[os.path.join(ROOT, "csrc", "native")],
-            extra_compile_args=CXX_FLAGS + ["-pthread", "-fopenmp-simd", "-mavx2", "-mfma"],
-            extra_link_args=["-pthread", "-lrt"],
+            extra_compile_args=CXX_FLAGS + ["-pthread", "-fopenmp", "-mavx2", "-mfma"],
+            extra_link_args=["-pthread", "-lrt", f"-L{torch_lib}", "-l:libgomp.so.1", f"-Wl,-rpath,{torch_lib}"],
             cxx_std=17,
         ))
     sdk_src = _rel(glob.glob(os.path.join(ROOT, "csrc", "sdk", "*.cpp")))
