@@ -86,3 +86,67 @@ def test_stage_split_and_microbatches():
     parts = split_batch(b, 2)
     assert sum(len(p.decode) for p in parts) == 3 and sum(len(p.prefill) for p in parts) == 2
     assert [s for p in parts for s in p.admitted] == [seqs[4]]
+
+
+WORKER_GPU = textwrap.dedent("""
+    import json, os, sys
+    sys.path.insert(0, {root!r})
+    from datetime import timedelta
+    import torch, torch.distributed as dist
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.models.config import ModelConfig
+    from kapsl_sdk_b200.parallel.pp import PipelineStage
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    c = ModelConfig(name="s", arch="llama", vocab_size=2048, hidden_size=512, intermediate_size=1024, num_layers=5,
+                    num_heads=4, num_kv_heads=2, head_dim=128, rope_theta=5e5, max_position=4096,
+                    bos_token_id=None, eos_token_id=None)
+    prompts = [list(range(5, 5 + n)) for n in (300, 77, 500, 16, 129)]
+    ecfg = EngineConfig(max_num_seqs=8, max_num_batched_tokens=256, max_model_len=1024, num_blocks=300)
+    st = PipelineStage(rank, world, c.num_layers, micro_batches=2)
+    eng = LLMEngine(c, device=dev, engine_cfg=ecfg, seed=0, pp_stage=st)
+    out = eng.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
+    if rank == world - 1:
+        ref = LLMEngine(c, device=dev, engine_cfg=EngineConfig(max_num_seqs=8, max_num_batched_tokens=256,
+                        max_model_len=1024, num_blocks=300, use_cuda_graph=False), seed=0)
+        want = ref.generate(prompts, SamplingParams.greedy(12, ignore_eos=True))
+        agree = sum(int(a == b) for o, w in zip(out, want) for a, b in zip(o, w))
+        print("AGREE", agree, sum(len(w) for w in want), flush=True)
+        ref.shutdown()
+    eng.shutdown()
+    dist.destroy_process_group()
+""")
+
+
+@pytest.mark.gpu
+def test_pipeline_two_gpus_matches_single_gpu():
+    """Two pipeline stages on two GPUs (NCCL point-to-point hidden states,
+    micro-batches) against one GPU holding every layer."""
+    import torch
+
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    port = _port()
+    procs = []
+    for r in range(2):
+        env = dict(os.environ, RANK=str(r), WORLD_SIZE="2", LOCAL_RANK=str(r), MASTER_ADDR="127.0.0.1",
+                   MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        procs.append(subprocess.Popen([sys.executable, "-c", WORKER_GPU.format(root=ROOT)], env=env,
+                                      stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True))
+    outs = []
+    for p in procs:
+        try:
+            o, _ = p.communicate(timeout=300)
+        except subprocess.TimeoutExpired:
+            for q in procs:
+                q.kill()
+            raise
+        outs.append((p.returncode, o))
+    for rc, o in outs:
+        assert rc == 0, o[-3000:]
+    line = [l for l in outs[1][1].splitlines() if l.startswith("AGREE")][0]
+    agree, total = (int(x) for x in line.split()[1:])
+    assert agree >= 0.9 * total, line
