@@ -129,29 +129,34 @@ class ModelRunner:
 
     # ------------------------------------------------------- host inputs
     def _fill(self, batch: ScheduledBatch, pad_to: int = 0):
-        """Write the batch into the pinned staging buffers; returns shape info."""
+        """Write the batch into the pinned staging buffers; returns shape info.
+        Decode rows and sampling rows are written as whole arrays (one numpy
+        assignment per field), not element by element."""
         L, n32, n64, f32 = self.L, self.n32, self.n64, self.f32view
-        MB = self.max_blocks
+        MB, bs = self.max_blocks, self.bs
         dec = batch.decode
         Bd = len(dec)
-        t = 0
         # decode rows
-        for i, s in enumerate(dec):
-            pos = s.length - 1
-            n32[L.ids + i] = s.output_ids[-1] if s.output_ids else s.prompt_ids[-1]
-            n32[L.pos + i] = pos
-            n64[L.slots + i] = s.block_ids[pos // self.bs] * self.bs + pos % self.bs
-            n32[L.ctx + i] = s.length
-            nb = len(s.block_ids)
-            n32[L.bt + i * MB:L.bt + i * MB + nb] = s.block_ids
-        t = Bd
+        if Bd:
+            lens = np.array([s.length for s in dec], dtype=np.int64)
+            pos = lens - 1
+            bts = [s.block_table() for s in dec]
+            nbs = np.array([len(b) for b in bts], dtype=np.int64)
+            flat = np.concatenate(bts)
+            starts = np.cumsum(nbs) - nbs
+            n32[L.ids:L.ids + Bd] = [s.output_ids[-1] if s.output_ids else s.prompt_ids[-1] for s in dec]
+            n32[L.pos:L.pos + Bd] = pos
+            n64[L.slots:L.slots + Bd] = flat[starts + pos // bs].astype(np.int64) * bs + pos % bs
+            n32[L.ctx:L.ctx + Bd] = lens
+            # block-table rows: element g of `flat` (row i) goes to L.bt + i * MB + (g - starts[i])
+            n32[L.bt + np.arange(flat.size) + np.repeat(np.arange(Bd, dtype=np.int64) * MB - starts, nbs)] = flat
         Bpad = max(Bd, pad_to)
-        for i in range(Bd, Bpad):  # CUDA-graph padding rows: no KV write, 1-token context on block 0
-            n32[L.ids + i] = 0
-            n32[L.pos + i] = 0
-            n64[L.slots + i] = -1
-            n32[L.ctx + i] = 1
-            n32[L.bt + i * MB] = 0
+        if Bpad > Bd:  # CUDA-graph padding rows: no KV write, 1-token context on block 0
+            n32[L.ids + Bd:L.ids + Bpad] = 0
+            n32[L.pos + Bd:L.pos + Bpad] = 0
+            n64[L.slots + Bd:L.slots + Bpad] = -1
+            n32[L.ctx + Bd:L.ctx + Bpad] = 1
+            n32[L.bt + np.arange(Bd, Bpad, dtype=np.int64) * MB] = 0
         t = Bpad
         # prefill chunks
         nwork = 0
@@ -163,41 +168,38 @@ class ModelRunner:
             npr = len(s.prompt_ids)
             toks = s.prompt_ids[p0:p0 + n] if p0 + n <= npr else (s.prompt_ids + s.output_ids)[p0:p0 + n]
             n32[L.ids + t:L.ids + t + n] = toks
-            pos = np.arange(p0, p0 + n, dtype=np.int64)
-            n32[L.pos + t:L.pos + t + n] = pos
-            blk = np.asarray(s.block_ids, dtype=np.int64)
-            n64[L.slots + t:L.slots + t + n] = blk[pos // self.bs] * self.bs + pos % self.bs
+            ppos = np.arange(p0, p0 + n, dtype=np.int64)
+            n32[L.pos + t:L.pos + t + n] = ppos
+            blk = s.block_table()
+            n64[L.slots + t:L.slots + t + n] = blk[ppos // bs].astype(np.int64) * bs + ppos % bs
             n32[L.ctx + row] = p0 + n
-            nb = len(s.block_ids)
-            n32[L.bt + row * MB:L.bt + row * MB + nb] = s.block_ids
+            n32[L.bt + row * MB:L.bt + row * MB + len(blk)] = blk
             si = L.sinfo + j * 4
             n32[si:si + 4] = (t, n, p0 + n, row)
-            for t0 in range(0, n, 64):
-                n32[L.work + nwork * 2] = j
-                n32[L.work + nwork * 2 + 1] = t0
-                nwork += 1
+            k = (n + 63) // 64  # 64-token work items of this chunk
+            n32[L.work + 2 * nwork:L.work + 2 * (nwork + k):2] = j
+            n32[L.work + 2 * nwork + 1:L.work + 2 * (nwork + k):2] = np.arange(0, n, 64, dtype=np.int32)
+            nwork += k
             if p0 + n >= s.length:  # chunk completes the prompt: sample from its last token
                 sample_seqs.append(s)
                 lrows.append(t + n - 1)
             t += n
         R = len(sample_seqs)
         Rpad = max(R, pad_to) if pad_to else R
-        for r in range(Rpad):
-            if r < R:
-                s = sample_seqs[r]
-                n64[L.lidx + r] = lrows[r]
-                n32[L.sslot + r] = s.slot
-                f32[L.temp + r] = s.params.temperature
-                n32[L.topk + r] = s.params.top_k
-                f32[L.topp + r] = s.params.top_p
-                f32[L.pen + r] = s.params.repetition_penalty
-            else:
-                n64[L.lidx + r] = r
-                n32[L.sslot + r] = self.pad_slot
-                f32[L.temp + r] = 0.0
-                n32[L.topk + r] = 0
-                f32[L.topp + r] = 1.0
-                f32[L.pen + r] = 1.0
+        if R:
+            n64[L.lidx:L.lidx + R] = lrows
+            n32[L.sslot:L.sslot + R] = [s.slot for s in sample_seqs]
+            f32[L.temp:L.temp + R] = [s.params.temperature for s in sample_seqs]
+            n32[L.topk:L.topk + R] = [s.params.top_k for s in sample_seqs]
+            f32[L.topp:L.topp + R] = [s.params.top_p for s in sample_seqs]
+            f32[L.pen:L.pen + R] = [s.params.repetition_penalty for s in sample_seqs]
+        if Rpad > R:
+            n64[L.lidx + R:L.lidx + Rpad] = np.arange(R, Rpad, dtype=np.int64)
+            n32[L.sslot + R:L.sslot + Rpad] = self.pad_slot
+            f32[L.temp + R:L.temp + Rpad] = 0.0
+            n32[L.topk + R:L.topk + Rpad] = 0
+            f32[L.topp + R:L.topp + Rpad] = 1.0
+            f32[L.pen + R:L.pen + Rpad] = 1.0
         S = Bpad + len(batch.prefill)
         return t, S, R, Rpad, Bd, Bpad, nwork, sample_seqs
 

@@ -11,6 +11,8 @@ import time
 from dataclasses import dataclass, field
 from typing import Callable, Optional
 
+import numpy as np
+
 
 @dataclass
 class SamplingParams:
@@ -64,6 +66,16 @@ class Sequence:
     session_id: Optional[str] = None
     on_token: Optional[Callable] = None
     finish_reason: Optional[str] = None
+    _bt: Optional[tuple] = field(default=None, repr=False)  # (block_ids list, its length, int32 copy)
+
+    def block_table(self) -> np.ndarray:
+        """``block_ids`` as an int32 array, rebuilt only when the list was replaced
+        or grew (the scheduler only appends to it or assigns a new list)."""
+        c, bl = self._bt, self.block_ids
+        if c is None or c[0] is not bl or c[1] != len(bl):
+            c = (bl, len(bl), np.asarray(bl, dtype=np.int32))
+            self._bt = c
+        return c[2]
 
     @property
     def all_ids(self) -> list:
