@@ -157,8 +157,8 @@ class Scheduler:
             self._swap_in(out, fresh)
         # 1) running sequences: decodes and unfinished prompt chunks, in arrival order
         for seq in list(self.running):
-            if seq not in self.running:  # preempted while making room for an earlier one
-                continue
+            if out.preempted and any(seq is v for v in out.preempted):
+                continue  # preempted while making room for an earlier one
             if budget <= 0:
                 break
             if not seq.in_prefill:
