@@ -9,6 +9,7 @@
 #include "cpu_kernels.h"
 #include "server.h"
 #include "shm.h"
+#include "wasm.h"
 #include "wire.h"
 
 namespace py = pybind11;
@@ -130,8 +131,97 @@ PYBIND11_MODULE(_native, m) {
       PyErr_SetString(out_of_blocks.ptr(), e.what());
     } catch (const wire::DecodeError& e) {
       PyErr_SetString(PyExc_ValueError, e.what());
+    } catch (const wasm::LoadError& e) {
+      PyErr_SetString(PyExc_ValueError, (std::string("wasm module rejected: ") + e.what()).c_str());
+    } catch (const wasm::Trap& e) {
+      PyErr_SetString(PyExc_RuntimeError, (std::string("wasm trap: ") + e.what()).c_str());
     }
   });
+
+  // ---- WebAssembly connectors (WASI preview1)
+  m.def("wasm_run",
+        [](py::bytes module, py::bytes stdin_data, std::vector<std::pair<std::string, std::string>> env,
+           std::vector<std::tuple<std::string, std::string, bool>> preopens, uint64_t fuel, double timeout_s,
+           size_t stdout_cap, size_t stderr_cap) {
+          wasm::WasiConfig cfg;
+          cfg.stdin_data = stdin_data;
+          cfg.env = std::move(env);
+          cfg.preopens = std::move(preopens);
+          cfg.stdout_cap = stdout_cap;
+          cfg.stderr_cap = stderr_cap;
+          wasm::RunLimits lim;
+          lim.fuel = fuel;
+          lim.timeout_s = timeout_s;
+          const std::string bytes = module;
+          wasm::WasiResult res;
+          {
+            py::gil_scoped_release nogil;
+            res = wasm::run_wasi(bytes, cfg, lim);
+          }
+          return py::make_tuple(res.exit_code, py::bytes(res.out), py::bytes(res.err));
+        },
+        py::arg("module"), py::arg("stdin") = py::bytes(), py::arg("env") = std::vector<std::pair<std::string, std::string>>{},
+        py::arg("preopens") = std::vector<std::tuple<std::string, std::string, bool>>{},
+        py::arg("fuel") = (uint64_t)4000000000ull, py::arg("timeout_s") = 30.0,
+        py::arg("stdout_cap") = (size_t)4 << 20, py::arg("stderr_cap") = (size_t)256 << 10,
+        "Run a WASI command module's _start once; returns (exit code, stdout, stderr)");
+  m.def("wasm_call",
+        [](py::bytes module, const std::string& name, py::list args, uint64_t fuel) {
+          // instantiate a module without imports and call one export (values typed by its signature)
+          const std::string bytes = module;
+          wasm::RunLimits lim;
+          lim.fuel = fuel;
+          auto none = [](const std::string&, const std::string&, const wasm::FuncType&) { return wasm::HostFn{}; };
+          wasm::Instance inst(wasm::Module::parse(bytes), none, lim);
+          const uint32_t f = inst.export_func(name);
+          const wasm::FuncType t = inst.type_of(f);
+          if (args.size() != t.params.size()) throw std::invalid_argument("wrong number of arguments");
+          std::vector<uint64_t> in;
+          for (size_t i = 0; i < t.params.size(); ++i) {
+            const uint8_t ty = t.params[i];
+            if (ty == wasm::F32) {
+              const float v = args[i].cast<float>();
+              uint32_t u;
+              std::memcpy(&u, &v, 4);
+              in.push_back(u);
+            } else if (ty == wasm::F64) {
+              const double v = args[i].cast<double>();
+              uint64_t u;
+              std::memcpy(&u, &v, 8);
+              in.push_back(u);
+            } else if (ty == wasm::I32) {
+              in.push_back((uint32_t)args[i].cast<int64_t>());
+            } else {
+              in.push_back((uint64_t)args[i].cast<int64_t>());
+            }
+          }
+          std::vector<uint64_t> out;
+          {
+            py::gil_scoped_release nogil;
+            out = inst.call(f, in);
+          }
+          py::list res;
+          for (size_t i = 0; i < t.results.size(); ++i) {
+            const uint8_t ty = t.results[i];
+            if (ty == wasm::F32) {
+              float v;
+              const uint32_t u = (uint32_t)out[i];
+              std::memcpy(&v, &u, 4);
+              res.append(v);
+            } else if (ty == wasm::F64) {
+              double v;
+              std::memcpy(&v, &out[i], 8);
+              res.append(v);
+            } else if (ty == wasm::I32) {
+              res.append((int32_t)(uint32_t)out[i]);
+            } else {
+              res.append((int64_t)out[i]);
+            }
+          }
+          return res;
+        },
+        py::arg("module"), py::arg("name"), py::arg("args") = py::list(), py::arg("fuel") = (uint64_t)1000000000ull,
+        "Instantiate an import-free module and call one exported function");
 
   // ---- wire
   m.attr("OP_INFER") = wire::OP_INFER;

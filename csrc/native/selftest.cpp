@@ -26,6 +26,7 @@
 #include "block_alloc.h"
 #include "cpu_kernels.h"
 #include "shm.h"
+#include "wasm.h"
 #include "wire.h"
 
 using namespace kapsl;
@@ -303,11 +304,81 @@ static void test_cpu_pool() {
   for (auto& t : ts) t.join();
 }
 
+// A module with recursion, br_table, bulk memory, a mutable global, memory.grow
+// and call_indirect (exports fib, switch, bulk, dispatch); then random byte
+// flips of it, each of which must load-fail, trap or run, never corrupt memory.
+static const char* kModuleHex =
+    "0061736d01000000011c0560017e017e60017f017f6000017f60027f7f017f60037f7f7f017f03060500010203040404"
+    "017000020504010101020606017f0141050b0722040366696200000673776974636800010462756c6b00020864697370"
+    "6174636800040907010041000b01030a8f01051c002000420253047e200005200042017d1000200042027d10007c0b0b"
+    "2200024002400240024020000e03000102030b410a0f0b41140f0b411e0f0b41e3000b390041e40041004105fc080000"
+    "41c80141e4004105fc0a000041ac0241c1004103fc0b0041c80128000041ac022d00006a23006a410140006a0b070020"
+    "0020016a0b0b002000200120021103000b0b1102010568656c6c6f0041100b0401020304";
+
+static std::string unhex(const char* h) {
+  std::string out;
+  for (size_t i = 0; h[i] && h[i + 1]; i += 2) out.push_back((char)std::stoi(std::string(h + i, 2), nullptr, 16));
+  return out;
+}
+
+static void test_wasm() {
+  const std::string mod = unhex(kModuleHex);
+  auto none = [](const std::string&, const std::string&, const wasm::FuncType&) { return wasm::HostFn{}; };
+  {
+    wasm::Instance in(wasm::Module::parse(mod), none);
+    CHECK(in.invoke("fib", {20})[0] == 6765, "wasm: fib(20)");
+    CHECK(in.invoke("switch", {1})[0] == 20 && in.invoke("switch", {7})[0] == 99, "wasm: br_table");
+    const uint32_t want = (uint32_t)(0x6c6c6568u + 0x41u + 5u + 1u);
+    CHECK((uint32_t)in.invoke("bulk", {})[0] == want, "wasm: bulk memory");
+    CHECK(in.invoke("dispatch", {2, 3, 0})[0] == 5, "wasm: call_indirect");
+    bool trapped = false;
+    try {
+      in.invoke("dispatch", {2, 3, 1});
+    } catch (const wasm::Trap&) {
+      trapped = true;
+    }
+    CHECK(trapped, "wasm: null table entry must trap");
+  }
+  std::mt19937 rng(11);
+  int ran = 0, rejected = 0, trapped = 0, other = 0;
+  for (int it = 0; it < 3000; ++it) {
+    std::string m = mod;
+    for (int k = 0, n = 1 + (int)(rng() % 3); k < n; ++k) m[rng() % m.size()] = (char)(rng() & 0xff);
+    try {
+      wasm::RunLimits lim;
+      lim.fuel = 200000;
+      lim.max_pages = 64;
+      wasm::Instance in(wasm::Module::parse(m), none, lim);
+      for (const char* f : {"fib", "switch", "bulk", "dispatch"}) {
+        try {
+          const uint32_t fi = in.export_func(f);
+          std::vector<uint64_t> args(in.type_of(fi).params.size(), 3);
+          in.call(fi, args);
+          ++ran;
+        } catch (const wasm::Trap&) {
+          ++trapped;
+        } catch (const wasm::LoadError&) {
+          ++rejected;
+        }
+      }
+    } catch (const wasm::LoadError&) {
+      ++rejected;
+    } catch (const wasm::Trap&) {
+      ++trapped;
+    } catch (const std::out_of_range& e) {
+      ++other;
+      if (getenv("SELFTEST_VERBOSE")) std::printf("out_of_range: %s\n", e.what());
+    }
+  }
+  CHECK(ran > 0 && rejected > 0, "wasm fuzz: ran %d, rejected %d, trapped %d", ran, rejected, trapped);
+  if (getenv("SELFTEST_VERBOSE")) std::printf("wasm fuzz: ran %d, rejected %d, trapped %d, other %d\n", ran, rejected, trapped, other);
+}
+
 int main(int argc, char** argv) {
   const std::pair<const char*, void (*)()> tests[] = {
       {"ring_mpmc", test_ring_mpmc},         {"ring_repush", test_ring_repush}, {"model_pools", test_model_pools},
       {"shared_leases", test_shared_leases}, {"block_allocator", test_block_allocator}, {"wire", test_wire},
-      {"cpu_pool", test_cpu_pool}};
+      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm}};
   for (auto& [name, fn] : tests) {
     if (argc > 1 && std::string(argv[1]) != name) continue;
     const auto t0 = std::chrono::steady_clock::now();

@@ -3,9 +3,12 @@
 * :class:`SidecarRuntime` — the connector is a child process speaking JSON
   lines on stdin/stdout; every request has a deadline (a hung connector
   raises ``TimeoutError`` and is killed instead of blocking the host).
-* :class:`WasmRuntime` — the reference instantiates WASM connectors with
-  wasmtime (crates/kapsl-rag/src/runtime/mod.rs:39-331); no WASM engine is
-  available in this environment, so constructing one raises with that reason.
+* :class:`WasmRuntime` — a connector compiled to a WASI preview1 command
+  module, run by the in-repo interpreter (``_native.wasm_run``): one
+  instantiation per request, the request line on stdin, the last non-empty
+  stdout line as the response, with the environment and preopened
+  directories the workspace grants (reference: wasmtime in
+  crates/kapsl-rag/src/runtime/mod.rs:198-331).
 * :class:`ExtensionRegistry` / :class:`ExtensionManager` — install connector
   directories (``manifest.json`` + entrypoint), keep per-workspace configs,
   launch sidecars with validated environment and paths
@@ -66,9 +69,42 @@ class SidecarRuntime:
 
 
 class WasmRuntime:
-    def __init__(self, *a, **kw):
-        raise RuntimeError("WASM connectors need a WASM engine (wasmtime), which is not available in this "
-                           "environment; package the connector as a sidecar")
+    def __init__(self, path: str, env: Optional[dict] = None, preopens: Optional[list] = None,
+                 timeout_s: float = 30.0, fuel: int = 4_000_000_000):
+        """``preopens``: (host dir, guest path, read only) triples."""
+        from .._ext import native
+
+        self._native = native()
+        with open(path, "rb") as f:
+            self.module = f.read()
+        self.env = []
+        for k, v in (env or {}).items():
+            if not k or "\0" in k or "\0" in str(v):
+                raise ValueError("env key must be non-empty and key/value cannot contain NUL")
+            self.env.append((str(k), str(v)))
+        self.preopens = []
+        for host, guest, ro in preopens or []:
+            if not os.path.isabs(host):
+                raise ValueError("preopened host path must be absolute")
+            if not guest or not guest.startswith("/") or "\0" in guest:
+                raise ValueError("preopened guest path must be absolute")
+            self.preopens.append((str(host), str(guest), bool(ro)))
+        self.timeout_s = timeout_s
+        self.fuel = fuel
+        self.last_stderr = b""
+
+    def send(self, line: str) -> str:
+        code, out, err = self._native.wasm_run(self.module, (line + "\n").encode(), self.env, self.preopens,
+                                               self.fuel, self.timeout_s)
+        self.last_stderr = err
+        lines = [l for l in out.decode("utf-8").splitlines() if l.strip()]
+        if not lines:
+            raise ConnectionError(f"connector exited (code {code}) without a response: "
+                                  f"{err.decode('utf-8', 'replace')[-300:]}")
+        return lines[-1]
+
+    def close(self) -> None:
+        pass
 
 
 class ConnectorClient:
@@ -205,9 +241,13 @@ class ExtensionManager:
         ext = {e.id: e for e in self.registry.discover()}.get(connector_id)
         if ext is None:
             raise FileNotFoundError(f"extension {connector_id!r} is not installed")
-        if ext.manifest.runtime != "sidecar":
-            return ConnectorClient(WasmRuntime())
         cfg = self.get_workspace_config(workspace, connector_id) or {}
+        if ext.manifest.runtime == "wasm":
+            wasi = cfg.get("wasi") or {}
+            preopens = [(d["host_path"], d["guest_path"], bool(d.get("read_only", False)))
+                        for d in wasi.get("preopen_dirs") or []]
+            return ConnectorClient(WasmRuntime(ext.entrypoint(), env=wasi.get("env") or {}, preopens=preopens,
+                                               timeout_s=timeout_s))
         env = {"PATH": os.environ.get("PATH", "")}
         for k, v in (cfg.get("env") or {}).items():
             _validate_env(k, str(v))

@@ -1,5 +1,6 @@
 """The C++ runtime pieces that run without Python (SHM region and rings,
-allocators, lease words, block allocator, bincode codec, CPU kernel pool)
+allocators, lease words, block allocator, bincode codec, CPU kernel pool,
+WebAssembly decoder and interpreter with randomly corrupted modules)
 built as one standalone program under ThreadSanitizer and under
 AddressSanitizer + UndefinedBehaviorSanitizer, run here on the CPU."""
 import os
@@ -10,7 +11,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SRC = os.path.join(ROOT, "csrc", "native")
-FILES = ["selftest.cpp", "shm.cpp", "wire.cpp", "block_alloc.cpp", "cpu_kernels.cpp"]
+FILES = ["selftest.cpp", "shm.cpp", "wire.cpp", "block_alloc.cpp", "cpu_kernels.cpp", "wasm.cpp"]
 
 
 def _build(tmp_path, flags):

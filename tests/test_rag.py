@@ -126,10 +126,8 @@ def test_prompt_rules():
     assert e.context == "" and e.fallback_message == "No relevant documents found."
 
 
-def test_chunker_and_wasm_runtime():
+def test_chunker():
     doc = rag.ParsedDocument("d", " ".join(str(i) for i in range(10)))
     cs = rag.SimpleChunker(4, 1).chunk(doc)
     assert [c.text for c in cs] == ["0 1 2 3", "3 4 5 6", "6 7 8 9"] and cs[1].id == "d:1"
     assert cs[2].metadata["chunk_index"] == "2"
-    with pytest.raises(RuntimeError, match="WASM"):
-        rag.WasmRuntime()
