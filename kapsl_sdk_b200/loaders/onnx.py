@@ -244,7 +244,18 @@ class OnnxGraph:
     SUPPORTED = {"MatMul", "Gemm", "Add", "Sub", "Mul", "Div", "Relu", "Sigmoid", "Tanh", "Softmax", "Reshape",
                  "Flatten", "Transpose", "Identity", "Constant", "Conv", "MaxPool", "AveragePool",
                  "GlobalAveragePool", "Concat", "Gather", "Unsqueeze", "Squeeze", "Cast", "Erf", "Sqrt", "Pow",
-                 "ReduceMean", "LayerNormalization", "Shape", "Slice", "Dropout", "BatchNormalization"}
+                 "ReduceMean", "LayerNormalization", "Shape", "Slice", "Dropout", "BatchNormalization",
+                 # elementwise
+                 "Exp", "Log", "Neg", "Abs", "Reciprocal", "Floor", "Ceil", "Round", "Sign", "Sin", "Cos", "Not",
+                 "IsNaN", "Softplus", "Softsign", "Elu", "Selu", "LeakyRelu", "HardSigmoid", "HardSwish", "Gelu",
+                 "Clip", "PRelu", "Max", "Min", "Sum", "Mean", "Equal", "Less", "Greater", "LessOrEqual",
+                 "GreaterOrEqual", "And", "Or", "Xor", "Mod", "Where", "LogSoftmax",
+                 # shapes
+                 "Expand", "Tile", "Split", "Pad", "ConstantOfShape", "Range", "Size", "Resize", "Trilu", "CumSum",
+                 # reductions / selection
+                 "ReduceSum", "ReduceMax", "ReduceMin", "ReduceProd", "ReduceL2", "ArgMax", "ArgMin", "TopK",
+                 # layers
+                 "InstanceNormalization", "ConvTranspose", "Einsum", "GlobalMaxPool"}
 
     def __init__(self, model: OnnxModel, device="cpu"):
         bad = sorted({n.op for n in model.nodes} - self.SUPPORTED)
@@ -364,6 +375,180 @@ class OnnxGraph:
             for s, e, ax, st in zip(starts, ends, axes, steps):
                 sl[ax] = slice(s, e if e < (1 << 62) else None, st)
             return x[0][tuple(sl)]
+        return self._op_more(n, x)
+
+    def _op_more(self, n: Node, x: list):
+        """Operators beyond the core set (opset 13+ semantics: axes / k / pads
+        arrive as inputs where that opset moved them there)."""
+        a, op = n.attrs, n.op
+        F = torch.nn.functional
+        unary = {"Exp": torch.exp, "Log": torch.log, "Neg": torch.neg, "Abs": torch.abs,
+                 "Reciprocal": torch.reciprocal, "Floor": torch.floor, "Ceil": torch.ceil, "Round": torch.round,
+                 "Sign": torch.sign, "Sin": torch.sin, "Cos": torch.cos, "Not": torch.logical_not,
+                 "IsNaN": torch.isnan, "Softplus": F.softplus, "Softsign": F.softsign}
+        if op in unary:
+            return unary[op](x[0])
+        if op == "Elu":
+            return F.elu(x[0], alpha=a.get("alpha", 1.0))
+        if op == "Selu":
+            al, ga = a.get("alpha", 1.67326319217681884765625), a.get("gamma", 1.05070102214813232421875)
+            return ga * torch.where(x[0] > 0, x[0], al * (torch.exp(x[0]) - 1))
+        if op == "LeakyRelu":
+            return F.leaky_relu(x[0], a.get("alpha", 0.01))
+        if op == "HardSigmoid":
+            return torch.clamp(a.get("alpha", 0.2) * x[0] + a.get("beta", 0.5), 0.0, 1.0)
+        if op == "HardSwish":
+            return x[0] * torch.clamp(x[0] / 6 + 0.5, 0.0, 1.0)
+        if op == "Gelu":
+            ap = a.get("approximate", "none")
+            return F.gelu(x[0], approximate=ap.decode() if isinstance(ap, bytes) else ap)
+        if op == "Clip":
+            lo = x[1] if len(x) > 1 and x[1] is not None else a.get("min")
+            hi = x[2] if len(x) > 2 and x[2] is not None else a.get("max")
+            y = x[0]
+            if lo is not None:
+                y = torch.maximum(y, torch.as_tensor(lo, dtype=y.dtype, device=y.device))
+            if hi is not None:
+                y = torch.minimum(y, torch.as_tensor(hi, dtype=y.dtype, device=y.device))
+            return y
+        if op == "PRelu":
+            return torch.where(x[0] >= 0, x[0], x[0] * x[1])
+        if op in ("Max", "Min", "Sum", "Mean"):
+            y = x[0]
+            for z in x[1:]:
+                y = {"Max": torch.maximum, "Min": torch.minimum}.get(op, torch.add)(y, z)
+            return y / len(x) if op == "Mean" else y
+        cmp = {"Equal": torch.eq, "Less": torch.lt, "Greater": torch.gt, "LessOrEqual": torch.le,
+               "GreaterOrEqual": torch.ge, "And": torch.logical_and, "Or": torch.logical_or,
+               "Xor": torch.logical_xor}
+        if op in cmp:
+            return cmp[op](x[0], x[1])
+        if op == "Mod":
+            return torch.fmod(x[0], x[1]) if a.get("fmod", 0) else torch.remainder(x[0], x[1])
+        if op == "Where":
+            return torch.where(x[0].bool(), x[1], x[2])
+        if op == "LogSoftmax":
+            return torch.log_softmax(x[0], dim=a.get("axis", -1))
+        if op == "Expand":
+            shape = [int(v) for v in x[1].tolist()]
+            nd = max(len(shape), x[0].dim())
+            src = [1] * (nd - x[0].dim()) + list(x[0].shape)
+            shape = [1] * (nd - len(shape)) + shape
+            out = [max(s, t) if s == 1 or t == 1 else t for s, t in zip(src, shape)]
+            return x[0].reshape(src).expand(out)
+        if op == "Tile":
+            return x[0].repeat(*[int(v) for v in x[1].tolist()])
+        if op == "Split":
+            ax = a.get("axis", 0)
+            if len(x) > 1 and x[1] is not None:
+                sizes = [int(v) for v in x[1].tolist()]
+            elif a.get("split"):
+                sizes = list(a["split"])
+            else:
+                k = a.get("num_outputs", len(n.outputs))
+                d = x[0].shape[ax]
+                sizes = [-(-d // k)] * (k - 1) + [d - -(-d // k) * (k - 1)]
+            return list(torch.split(x[0], sizes, dim=ax))
+        if op == "Pad":
+            pads = [int(v) for v in (x[1].tolist() if len(x) > 1 and x[1] is not None else a.get("pads", []))]
+            value = float(x[2].item()) if len(x) > 2 and x[2] is not None else float(a.get("value", 0.0))
+            nd = x[0].dim()
+            axes = ([int(v) for v in x[3].tolist()] if len(x) > 3 and x[3] is not None else list(range(nd)))
+            axes = [ax % nd for ax in axes]
+            full = [0] * (2 * nd)
+            for i, ax in enumerate(axes):
+                full[ax], full[nd + ax] = pads[i], pads[len(axes) + i]
+            tp = []
+            for ax in reversed(range(nd)):
+                tp += [full[ax], full[nd + ax]]
+            mode = a.get("mode", "constant")
+            mode = mode.decode() if isinstance(mode, bytes) else mode
+            if mode == "constant":
+                return F.pad(x[0], tp, value=value)
+            if mode not in ("reflect", "edge"):
+                raise ValueError(f"Pad mode {mode!r} is not supported")
+            pairs = [(full[ax], full[nd + ax]) for ax in range(nd)]
+            return torch.from_numpy(np.pad(x[0].cpu().numpy(), pairs, mode=mode)).to(self.device)
+        if op == "ConstantOfShape":
+            v = a.get("value")
+            arr = np.asarray(v if v is not None else np.zeros(1, np.float32)).reshape(-1)
+            return torch.full([int(s) for s in x[0].tolist()], arr[0].item(),
+                              dtype=torch.from_numpy(arr[:1].copy()).dtype, device=self.device)
+        if op == "Range":
+            return torch.arange(x[0].item(), x[1].item(), x[2].item(), device=self.device).to(x[0].dtype)
+        if op == "Size":
+            return torch.tensor(x[0].numel(), dtype=torch.int64, device=self.device)
+        if op == "Resize":
+            mode = a.get("mode", "nearest")
+            mode = mode.decode() if isinstance(mode, bytes) else mode
+            sizes = x[3] if len(x) > 3 and x[3] is not None and x[3].numel() else None
+            scales = x[2] if len(x) > 2 and x[2] is not None and x[2].numel() else None
+            if sizes is not None:
+                out = [int(v) for v in sizes.tolist()][2:]
+                kw = {"size": out}
+            else:
+                kw = {"scale_factor": [float(v) for v in scales.tolist()][2:]}
+            if mode == "nearest":
+                return F.interpolate(x[0], mode="nearest", **kw)
+            ctm = a.get("coordinate_transformation_mode", "half_pixel")
+            ctm = ctm.decode() if isinstance(ctm, bytes) else ctm
+            lin = {3: "linear", 4: "bilinear", 5: "trilinear"}[x[0].dim()]
+            return F.interpolate(x[0], mode=lin, align_corners=ctm == "align_corners", **kw)
+        if op == "Trilu":
+            k = int(x[1].item()) if len(x) > 1 and x[1] is not None else 0
+            return torch.triu(x[0], k) if a.get("upper", 1) else torch.tril(x[0], k)
+        if op == "CumSum":
+            ax = int(x[1].item())
+            y = x[0].flip(ax) if a.get("reverse", 0) else x[0]
+            c = torch.cumsum(y, ax)
+            if a.get("exclusive", 0):
+                c = c - y
+            return c.flip(ax) if a.get("reverse", 0) else c
+        if op in ("ReduceSum", "ReduceMax", "ReduceMin", "ReduceProd", "ReduceL2"):
+            axes = a.get("axes") or (x[1].tolist() if len(x) > 1 and x[1] is not None else None)
+            keep = bool(a.get("keepdims", 1))
+            if not axes:
+                if a.get("noop_with_empty_axes", 0) and op == "ReduceSum":
+                    return x[0]
+                axes = list(range(x[0].dim()))
+            y = x[0]
+            if op == "ReduceSum":
+                return y.sum(dim=tuple(axes), keepdim=keep)
+            if op == "ReduceL2":
+                return y.pow(2).sum(dim=tuple(axes), keepdim=keep).sqrt()
+            for ax in sorted((ax % y.dim() for ax in axes), reverse=True):
+                y = {"ReduceMax": lambda t: t.amax(ax, keepdim=True), "ReduceMin": lambda t: t.amin(ax, keepdim=True),
+                     "ReduceProd": lambda t: t.prod(ax, keepdim=True)}[op](y)
+            if not keep:
+                for ax in sorted((ax % x[0].dim() for ax in axes), reverse=True):
+                    y = y.squeeze(ax)
+            return y
+        if op in ("ArgMax", "ArgMin"):
+            ax, keep = a.get("axis", 0), bool(a.get("keepdims", 1))
+            y = x[0].flip(ax) if a.get("select_last_index", 0) else x[0]
+            r = (torch.argmax if op == "ArgMax" else torch.argmin)(y, dim=ax, keepdim=keep)
+            return (y.shape[ax] - 1 - r) if a.get("select_last_index", 0) else r
+        if op == "TopK":
+            k = int(x[1].reshape(-1)[0].item())
+            v, i = torch.topk(x[0], k, dim=a.get("axis", -1), largest=bool(a.get("largest", 1)),
+                              sorted=bool(a.get("sorted", 1)))
+            return [v, i]
+        if op == "InstanceNormalization":
+            return F.instance_norm(x[0], weight=x[1], bias=x[2], eps=a.get("epsilon", 1e-5))
+        if op == "GlobalMaxPool":
+            return x[0].amax(dim=tuple(range(2, x[0].dim())), keepdim=True)
+        if op == "ConvTranspose":
+            nd = x[1].dim() - 2
+            lo, hi = _conv_pads(a, nd)
+            if lo != hi:
+                raise ValueError("ConvTranspose with asymmetric pads is not supported")
+            fn = {1: F.conv_transpose1d, 2: F.conv_transpose2d, 3: F.conv_transpose3d}[nd]
+            return fn(x[0], x[1], x[2] if len(x) > 2 else None, stride=a.get("strides") or 1, padding=lo,
+                      output_padding=a.get("output_padding") or 0, groups=a.get("group", 1),
+                      dilation=a.get("dilations") or 1)
+        if op == "Einsum":
+            eq = a["equation"]
+            return torch.einsum(eq.decode() if isinstance(eq, bytes) else eq, *x)
         raise ValueError(f"unsupported ONNX op {op}")
 
 
@@ -451,6 +636,10 @@ def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, o
                 ab += _key(3, 0) + _enc_varint(v) + _key(20, 0) + _enc_varint(2)
             elif isinstance(v, (list, tuple)):
                 ab += b"".join(_key(8, 0) + _enc_varint(int(i)) for i in v) + _key(20, 0) + _enc_varint(7)
+            elif isinstance(v, str):
+                ab += _ld(4, v.encode()) + _key(20, 0) + _enc_varint(3)
+            elif isinstance(v, np.ndarray):
+                ab += _ld(5, encode_tensor(k, v)) + _key(20, 0) + _enc_varint(4)
             nb += _ld(5, ab)
         g += _ld(1, nb)
     g += _ld(2, b"graph")
