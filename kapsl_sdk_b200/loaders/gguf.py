@@ -191,7 +191,25 @@ def gguf_config(reader) -> ModelConfig:
         max_position=min(int(p("context_length", 4096)), 4096),
         bos_token_id=_field(reader, "tokenizer.ggml.bos_token_id", 1),
         eos_token_id=_field(reader, "tokenizer.ggml.eos_token_id", 2),
+        rope_scaling=_gguf_rope_scaling(reader, arch),
     )
+
+
+def _gguf_rope_scaling(reader, arch: str) -> Optional[dict]:
+    """RoPE scaling from GGUF: per-frequency divisors stored as the
+    ``rope_freqs.weight`` tensor (Llama 3.1 exports), else the
+    ``{arch}.rope.scaling.*`` keys (linear / yarn)."""
+    for t in reader.tensors:
+        if t.name == "rope_freqs.weight":
+            return {"rope_type": "freq_factors", "factors": [float(v) for v in np.asarray(t.data).reshape(-1)]}
+    kind = _field(reader, f"{arch}.rope.scaling.type")
+    if kind in (None, "none"):
+        return None
+    rs = {"rope_type": str(kind), "factor": float(_field(reader, f"{arch}.rope.scaling.factor", 1.0))}
+    orig = _field(reader, f"{arch}.rope.scaling.original_context_length")
+    if orig is not None:
+        rs["original_max_position_embeddings"] = int(orig)
+    return rs
 
 
 def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
@@ -305,6 +323,17 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
             w.add_tensor(name, a.astype(np.float16))
         else:
             w.add_tensor(name, np.ascontiguousarray(a.astype(np.float32)))
+
+    rs = cfg.rope_scaling or {}
+    if rs.get("rope_type") == "freq_factors":
+        w.add_tensor("rope_freqs.weight", np.asarray(rs["factors"], dtype=np.float32))
+    elif rs.get("rope_type") in ("linear", "yarn"):
+        w.add_string("llama.rope.scaling.type", rs["rope_type"])
+        w.add_float32("llama.rope.scaling.factor", float(rs.get("factor", 1.0)))
+        if "original_max_position_embeddings" in rs:
+            w.add_uint32("llama.rope.scaling.original_context_length", int(rs["original_max_position_embeddings"]))
+    elif rs:
+        raise ValueError(f"GGUF cannot store RoPE scaling {rs.get('rope_type')!r}; use frequency factors")
 
     li = 0
     saw_norm = False

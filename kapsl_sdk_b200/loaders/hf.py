@@ -119,5 +119,7 @@ def save_hf_model(root: str, cfg: ModelConfig, full_stream) -> None:
           "rms_norm_eps": cfg.rms_eps, "attention_bias": cfg.qkv_bias, "tie_word_embeddings": cfg.tie_embeddings,
           "max_position_embeddings": cfg.max_position, "bos_token_id": cfg.bos_token_id,
           "eos_token_id": cfg.eos_token_id}
+    if cfg.rope_scaling:
+        hf["rope_scaling"] = dict(cfg.rope_scaling)
     with open(os.path.join(root, "config.json"), "w") as f:
         json.dump(hf, f)

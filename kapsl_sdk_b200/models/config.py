@@ -32,6 +32,7 @@ class ModelConfig:
     num_experts: int = 0
     experts_per_token: int = 0
     weight_format: str = "bf16"  # bf16 | q4_k (GGUF k-quant linear layers, dequantized in the GEMM)
+    rope_scaling: Optional[dict] = None  # HF rope_scaling (linear | llama3 | yarn) or GGUF frequency factors
     bos_token_id: Optional[int] = 1
     eos_token_id: Optional[int] = 2
     extra: dict = field(default_factory=dict)
@@ -106,7 +107,30 @@ class ModelConfig:
             experts_per_token=int(c.get("num_experts_per_tok", 0)),
             bos_token_id=c.get("bos_token_id"),
             eos_token_id=eos,
+            rope_scaling=_rope_scaling(c),
         )
+
+
+def _rope_scaling(c: dict) -> Optional[dict]:
+    """HF ``rope_scaling`` (older configs name the kind ``type``), with the
+    original context length defaulted from the config; the check happens here
+    so an unsupported kind fails at load time."""
+    rs = c.get("rope_scaling")
+    if not rs:
+        return None
+    rs = dict(rs)
+    kind = rs.get("rope_type", rs.get("type", "default"))
+    rs["rope_type"] = kind
+    if kind == "default":
+        return None
+    if kind in ("yarn", "llama3"):
+        rs.setdefault("original_max_position_embeddings", c.get("original_max_position_embeddings",
+                                                                c.get("max_position_embeddings", 4096)))
+    from ..ops.reference import rope_inv_freq
+
+    rope_inv_freq(c.get("head_dim", c.get("hidden_size", 4096) // c.get("num_attention_heads", 32)),
+                  float(c.get("rope_theta", 10000.0)), rs)
+    return rs
 
 
 def tiny_llama() -> ModelConfig:

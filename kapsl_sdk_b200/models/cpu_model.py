@@ -39,7 +39,7 @@ class CPUCausalLM:
             if not cfg.is_moe:
                 d["gate_up"] = torch.cat([d["gate"], d["up"]], 0)
             self.layers.append(d)
-        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta)
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, scaling=cfg.rope_scaling)
         self.hq, self.hkv, self.D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
         self.scale = 1.0 / math.sqrt(self.D)
         self.device = torch.device("cpu")

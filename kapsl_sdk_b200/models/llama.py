@@ -297,7 +297,8 @@ class CausalLM:
         self.hkv = weights.kv_heads_local
         self.D = cfg.head_dim
         self.scale = 1.0 / math.sqrt(self.D)
-        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=self.device)
+        self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=self.device,
+                                         scaling=cfg.rope_scaling)
         self.qkv_width = (self.hq + 2 * self.hkv) * self.D
 
     def configure_tp(self, max_tokens: int) -> None:
@@ -362,7 +363,7 @@ def reference_forward(cfg: ModelConfig, full_layers: list, embed: torch.Tensor, 
     """fp32 dense forward over one sequence (oracle for the paged GPU path).
     Returns logits [len(tokens), V]."""
     D = cfg.head_dim
-    cs = ref.rope_cos_sin(cfg.max_position, D, cfg.rope_theta)
+    cs = ref.rope_cos_sin(cfg.max_position, D, cfg.rope_theta, scaling=cfg.rope_scaling)
     ids = torch.tensor(tokens)
     pos = torch.arange(len(tokens))
     h = embed.float()[ids]

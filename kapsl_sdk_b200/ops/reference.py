@@ -23,12 +23,81 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, residual: Optiona
     return xf * torch.rsqrt(var + eps) * weight.float(), xf
 
 
-def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device=None) -> torch.Tensor:
-    """[max_pos, head_dim] fp32 table: cos in the first half, sin in the second."""
+def rope_inv_freq(head_dim: int, theta: float, scaling: Optional[dict] = None) -> tuple:
+    """Rotary inverse frequencies (float64 [head_dim / 2]) and the factor that
+    scales cos/sin, for the RoPE scaling of HF ``rope_scaling`` / GGUF metadata:
+
+    * ``linear``: every frequency divided by ``factor`` (position interpolation);
+    * ``llama3``: wavelengths above ``original_max_position_embeddings /
+      low_freq_factor`` divided by ``factor``, below ``... / high_freq_factor``
+      kept, a linear blend in between (Llama 3.1);
+    * ``yarn``: per-dimension blend of extrapolated and interpolated
+      frequencies over the ramp between the dimensions that rotate
+      ``beta_fast`` and ``beta_slow`` times in the original context, with
+      cos/sin scaled by ``attention_factor`` (default 0.1 ln(factor) + 1)
+      (Peng et al., "YaRN", 2023);
+    * ``freq_factors``: explicit per-frequency divisors (GGUF ``rope_freqs``).
+    Scalings that depend on the live sequence length (dynamic NTK, LongRoPE)
+    are refused rather than approximated by a fixed table."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    if not scaling:
+        return inv, 1.0
+    kind = scaling.get("rope_type", scaling.get("type", "default"))
+    if kind in ("default", None):
+        return inv, 1.0
+    factor = float(scaling.get("factor", 1.0))
+    if kind == "linear":
+        return inv / factor, 1.0
+    if kind == "freq_factors":
+        f = torch.as_tensor(scaling["factors"], dtype=torch.float64)
+        if f.numel() != inv.numel():
+            raise ValueError(f"rope frequency factors: {f.numel()} values for {inv.numel()} frequencies")
+        return inv / f, 1.0
+    if kind == "llama3":
+        orig = float(scaling["original_max_position_embeddings"])
+        lo, hi = float(scaling.get("low_freq_factor", 1.0)), float(scaling.get("high_freq_factor", 4.0))
+        wavelen = 2 * math.pi / inv
+        smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        blended = (1 - smooth) * inv / factor + smooth * inv
+        out = torch.where(wavelen > orig / lo, inv / factor, blended)
+        return torch.where(wavelen < orig / hi, inv, out), 1.0
+    if kind == "yarn":
+        orig = float(scaling.get("original_max_position_embeddings", 4096))
+        beta_fast, beta_slow = float(scaling.get("beta_fast", 32.0)), float(scaling.get("beta_slow", 1.0))
+        attn = scaling.get("attention_factor")
+        if attn is None:
+            mscale = float(scaling.get("mscale", 1.0) or 1.0)
+            mscale_all = float(scaling.get("mscale_all_dim", 0.0) or 0.0)
+
+            def m(s, k):
+                return 1.0 if s <= 1 else 0.1 * k * math.log(s) + 1.0
+
+            attn = m(factor, mscale) / m(factor, mscale_all) if mscale_all else m(factor, 1.0)
+
+        def corr_dim(rotations):
+            return head_dim * math.log(orig / (rotations * 2 * math.pi)) / (2 * math.log(theta))
+
+        low = corr_dim(beta_fast)
+        high = corr_dim(beta_slow)
+        if scaling.get("truncate", True):
+            low, high = math.floor(low), math.ceil(high)
+        low, high = max(low, 0), min(high, head_dim - 1)
+        if low == high:
+            high += 0.001
+        ramp = ((torch.arange(head_dim // 2, dtype=torch.float64) - low) / (high - low)).clamp(0.0, 1.0)
+        extrap = 1 - ramp
+        return inv / factor * (1 - extrap) + inv * extrap, float(attn)
+    raise ValueError(f"RoPE scaling {kind!r} depends on the live sequence length; not supported")
+
+
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device=None, scaling: Optional[dict] = None
+                 ) -> torch.Tensor:
+    """[max_pos, head_dim] fp32 table: cos in the first half, sin in the second
+    (``scaling``: see :func:`rope_inv_freq`)."""
+    inv, attn = rope_inv_freq(head_dim, theta, scaling)
     t = torch.arange(max_pos, dtype=torch.float64)
     f = torch.outer(t, inv)
-    return torch.cat([f.cos(), f.sin()], dim=1).float().to(device)
+    return (torch.cat([f.cos(), f.sin()], dim=1) * attn).float().to(device)
 
 
 def apply_rope(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
