@@ -175,8 +175,13 @@ def _field(reader, key, default=None):
     return v
 
 
+GGUF_ARCHS = ("llama", "qwen2", "phi3")
+
+
 def gguf_config(reader) -> ModelConfig:
     arch = _field(reader, "general.architecture", "llama")
+    if arch not in GGUF_ARCHS:
+        raise ValueError(f"GGUF architecture {arch!r} is not supported (supported: {', '.join(GGUF_ARCHS)})")
     p = lambda k, d=None: _field(reader, f"{arch}.{k}", d)
     heads = int(p("attention.head_count", 32))
     hidden = int(p("embedding_length", 4096))
@@ -200,6 +205,8 @@ def _gguf_rope_scaling(reader, arch: str) -> Optional[dict]:
     ``rope_freqs.weight`` tensor (Llama 3.1 exports), else the
     ``{arch}.rope.scaling.*`` keys (linear / yarn)."""
     for t in reader.tensors:
+        if t.name in ("rope_factors_long.weight", "rope_factors_short.weight"):
+            raise ValueError("LongRoPE (rope_factors_long/short) depends on the live sequence length; not supported")
         if t.name == "rope_freqs.weight":
             return {"rope_type": "freq_factors", "factors": [float(v) for v in np.asarray(t.data).reshape(-1)]}
     kind = _field(reader, f"{arch}.rope.scaling.type")
@@ -227,16 +234,24 @@ def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
     yield "final_norm", get("output_norm.weight")
     for i in range(cfg.num_layers):
         b = f"blk.{i}."
-        q = tensor_to_numpy(T[b + "attn_q.weight"])
-        k = tensor_to_numpy(T[b + "attn_k.weight"])
+        if b + "attn_qkv.weight" in T:  # Phi-3: fused [q; k; v]
+            qkv = tensor_to_numpy(T[b + "attn_qkv.weight"])
+            q, k, v = np.split(qkv, [cfg.q_size, cfg.q_size + cfg.kv_size], 0)
+        else:
+            q = tensor_to_numpy(T[b + "attn_q.weight"])
+            k = tensor_to_numpy(T[b + "attn_k.weight"])
+            v = tensor_to_numpy(T[b + "attn_v.weight"])
         if permuted:
             q = _permute_back(q, cfg.num_heads)
             k = _permute_back(k, cfg.num_kv_heads)
         full = {"q": torch.from_numpy(np.ascontiguousarray(q)), "k": torch.from_numpy(np.ascontiguousarray(k)),
-                "v": get(b + "attn_v.weight"), "o": get(b + "attn_output.weight"),
+                "v": torch.from_numpy(np.ascontiguousarray(v)), "o": get(b + "attn_output.weight"),
                 "in_norm": get(b + "attn_norm.weight"), "post_norm": get(b + "ffn_norm.weight"),
-                "gate": get(b + "ffn_gate.weight"), "up": get(b + "ffn_up.weight"),
                 "down": get(b + "ffn_down.weight")}
+        if b + "ffn_gate.weight" in T:
+            full["gate"], full["up"] = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
+        else:  # Phi-3: ffn_up holds [gate; up]
+            full["gate"], full["up"] = torch.chunk(get(b + "ffn_up.weight"), 2, 0)
         if b + "attn_q.bias" in T:
             full["q_b"], full["k_b"], full["v_b"] = (get(b + "attn_q.bias"), get(b + "attn_k.bias"),
                                                    get(b + "attn_v.bias"))
@@ -289,13 +304,17 @@ def synthetic_vocab(n: int) -> tuple:
     return toks[:n], [0.0] * n, types[:n]
 
 
-def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32") -> None:
-    """Serialize a full-tensor stream as a llama-architecture GGUF file.
+def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32", arch: str = "llama") -> None:
+    """Serialize a full-tensor stream as a GGUF file of architecture ``arch``
+    ("llama": q/k rows permuted as llama.cpp stores them; "phi3": fused
+    attn_qkv and [gate; up] in ffn_up, no permutation).
     ``quant``: "f32", "f16" or "q4_k" (2-D weights quantized, norms kept f32)."""
     from gguf import GGMLQuantizationType as Q
     from gguf import GGUFWriter
 
-    w = GGUFWriter(path, "llama")
+    if arch not in ("llama", "phi3"):
+        raise ValueError(f"cannot write GGUF architecture {arch!r}")
+    w = GGUFWriter(path, arch)
     w.add_name(cfg.name)
     w.add_context_length(cfg.max_position)
     w.add_embedding_length(cfg.hidden_size)
@@ -328,10 +347,10 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
     if rs.get("rope_type") == "freq_factors":
         w.add_tensor("rope_freqs.weight", np.asarray(rs["factors"], dtype=np.float32))
     elif rs.get("rope_type") in ("linear", "yarn"):
-        w.add_string("llama.rope.scaling.type", rs["rope_type"])
-        w.add_float32("llama.rope.scaling.factor", float(rs.get("factor", 1.0)))
+        w.add_string(f"{arch}.rope.scaling.type", rs["rope_type"])
+        w.add_float32(f"{arch}.rope.scaling.factor", float(rs.get("factor", 1.0)))
         if "original_max_position_embeddings" in rs:
-            w.add_uint32("llama.rope.scaling.original_context_length", int(rs["original_max_position_embeddings"]))
+            w.add_uint32(f"{arch}.rope.scaling.original_context_length", int(rs["original_max_position_embeddings"]))
     elif rs:
         raise ValueError(f"GGUF cannot store RoPE scaling {rs.get('rope_type')!r}; use frequency factors")
 
@@ -349,12 +368,20 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
             b = f"blk.{li}."
             put(b + "attn_norm.weight", t["in_norm"], False)
             put(b + "ffn_norm.weight", t["post_norm"], False)
-            put(b + "attn_q.weight", torch.from_numpy(_permute(t["q"].float().cpu().numpy(), cfg.num_heads)), True)
-            put(b + "attn_k.weight", torch.from_numpy(_permute(t["k"].float().cpu().numpy(), cfg.num_kv_heads)), True)
-            put(b + "attn_v.weight", t["v"], True)
+            if arch == "phi3":
+                put(b + "attn_qkv.weight", torch.cat([t["q"], t["k"], t["v"]], 0), True)
+            else:
+                put(b + "attn_q.weight", torch.from_numpy(_permute(t["q"].float().cpu().numpy(), cfg.num_heads)),
+                    True)
+                put(b + "attn_k.weight", torch.from_numpy(_permute(t["k"].float().cpu().numpy(), cfg.num_kv_heads)),
+                    True)
+                put(b + "attn_v.weight", t["v"], True)
             put(b + "attn_output.weight", t["o"], True)
-            put(b + "ffn_gate.weight", t["gate"], True)
-            put(b + "ffn_up.weight", t["up"], True)
+            if arch == "phi3":
+                put(b + "ffn_up.weight", torch.cat([t["gate"], t["up"]], 0), True)
+            else:
+                put(b + "ffn_gate.weight", t["gate"], True)
+                put(b + "ffn_up.weight", t["up"], True)
             put(b + "ffn_down.weight", t["down"], True)
             li += 1
     if not saw_norm:

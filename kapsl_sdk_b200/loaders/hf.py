@@ -1,11 +1,13 @@
 """HuggingFace checkpoints (``config.json`` + ``*.safetensors``) for the
-Llama / Qwen2 / Mixtral families.
+Llama / Mistral / Qwen2 / Mixtral / Phi-3 families.
 
 Tensor names ``model.embed_tokens.weight``, ``lm_head.weight``, ``model.norm.weight``,
 ``model.layers.{i}.{input_layernorm, post_attention_layernorm}.weight``,
 ``self_attn.{q,k,v,o}_proj.{weight,bias}``, ``mlp.{gate,up,down}_proj.weight`` and,
 for Mixtral, ``block_sparse_moe.gate.weight`` / ``experts.{e}.w{1,3,2}.weight``
-are mapped to this runtime's full-tensor stream, then sharded per rank.
+are mapped to this runtime's full-tensor stream, then sharded per rank.  Phi-3's
+fused ``self_attn.qkv_proj`` and ``mlp.gate_up_proj`` are split into the same
+tensors.
 """
 from __future__ import annotations
 
@@ -47,9 +49,14 @@ def iter_hf_full(root: str, cfg: ModelConfig):
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
         a = p + "self_attn."
-        full = {"q": st.get(a + "q_proj.weight"), "k": st.get(a + "k_proj.weight"), "v": st.get(a + "v_proj.weight"),
-                "o": st.get(a + "o_proj.weight"), "in_norm": st.get(p + "input_layernorm.weight"),
+        full = {"o": st.get(a + "o_proj.weight"), "in_norm": st.get(p + "input_layernorm.weight"),
                 "post_norm": st.get(p + "post_attention_layernorm.weight")}
+        if st.has(a + "qkv_proj.weight"):  # Phi-3: fused [q; k; v]
+            full["q"], full["k"], full["v"] = torch.split(st.get(a + "qkv_proj.weight"),
+                                                          [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)
+        else:
+            full["q"], full["k"], full["v"] = (st.get(a + "q_proj.weight"), st.get(a + "k_proj.weight"),
+                                               st.get(a + "v_proj.weight"))
         if st.has(a + "q_proj.bias"):
             full["q_b"], full["k_b"], full["v_b"] = (st.get(a + "q_proj.bias"), st.get(a + "k_proj.bias"),
                                                    st.get(a + "v_proj.bias"))
@@ -59,6 +66,9 @@ def iter_hf_full(root: str, cfg: ModelConfig):
             full["experts_gate"] = torch.stack([st.get(f"{m}experts.{e}.w1.weight") for e in range(cfg.num_experts)])
             full["experts_up"] = torch.stack([st.get(f"{m}experts.{e}.w3.weight") for e in range(cfg.num_experts)])
             full["experts_down"] = torch.stack([st.get(f"{m}experts.{e}.w2.weight") for e in range(cfg.num_experts)])
+        elif st.has(p + "mlp.gate_up_proj.weight"):  # Phi-3: fused [gate; up]
+            full["gate"], full["up"] = torch.chunk(st.get(p + "mlp.gate_up_proj.weight"), 2, 0)
+            full["down"] = st.get(p + "mlp.down_proj.weight")
         else:
             full["gate"] = st.get(p + "mlp.gate_proj.weight")
             full["up"] = st.get(p + "mlp.up_proj.weight")

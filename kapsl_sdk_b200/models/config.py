@@ -13,6 +13,11 @@ from dataclasses import asdict, dataclass, field
 from typing import Optional
 
 
+# HF model_type -> the runtime's layer family (Mistral and Phi-3 are Llama-shaped
+# decoders; Phi-3's fused projections are split by the checkpoint loader)
+HF_MODEL_TYPES = {"llama": "llama", "mistral": "llama", "phi3": "llama", "qwen2": "qwen2", "mixtral": "mixtral"}
+
+
 @dataclass
 class ModelConfig:
     name: str = "custom"
@@ -82,9 +87,18 @@ class ModelConfig:
         else:
             c = dict(path_or_dict)
         mt = c.get("model_type", "llama")
-        arch = {"qwen2": "qwen2", "mixtral": "mixtral"}.get(mt, "llama")
+        if mt not in HF_MODEL_TYPES:
+            raise ValueError(f"model_type {mt!r} is not supported (supported: {', '.join(sorted(HF_MODEL_TYPES))})")
+        arch = HF_MODEL_TYPES[mt]
+        if float(c.get("partial_rotary_factor", 1.0)) != 1.0:
+            raise ValueError("partial rotary embeddings are not supported")
         heads = c.get("num_attention_heads", 32)
         hidden = c.get("hidden_size", 4096)
+        max_pos = int(c.get("max_position_embeddings", 32768))
+        window = c.get("sliding_window") if c.get("use_sliding_window", True) else None
+        if window and int(window) < max_pos:
+            # sliding-window attention equals full attention up to the window: serve that far exactly
+            max_pos = int(window)
         eos = c.get("eos_token_id")
         if isinstance(eos, list):
             eos = eos[0] if eos else None
@@ -102,7 +116,7 @@ class ModelConfig:
             rms_eps=float(c.get("rms_norm_eps", 1e-5)),
             qkv_bias=bool(c.get("attention_bias", arch == "qwen2")),
             tie_embeddings=bool(c.get("tie_word_embeddings", False)),
-            max_position=int(c.get("max_position_embeddings", 32768)),
+            max_position=max_pos,
             num_experts=int(c.get("num_local_experts", 0)),
             experts_per_token=int(c.get("num_experts_per_tok", 0)),
             bos_token_id=c.get("bos_token_id"),
