@@ -175,7 +175,7 @@ def _field(reader, key, default=None):
     return v
 
 
-GGUF_ARCHS = ("llama", "qwen2", "phi3")
+GGUF_ARCHS = ("llama", "qwen2", "qwen3", "phi3")
 
 
 def gguf_config(reader) -> ModelConfig:
@@ -188,7 +188,8 @@ def gguf_config(reader) -> ModelConfig:
     tokens = _field(reader, "tokenizer.ggml.tokens")
     vocab = int(p("vocab_size", len(tokens) if tokens is not None else 32000))
     return ModelConfig(
-        name=_field(reader, "general.name", arch) or arch, arch="qwen2" if arch == "qwen2" else "llama",
+        name=_field(reader, "general.name", arch) or arch, arch=arch if arch in ("qwen2", "qwen3") else "llama",
+        qk_norm=arch == "qwen3",
         vocab_size=vocab, hidden_size=hidden, intermediate_size=int(p("feed_forward_length", 4 * hidden)),
         num_layers=int(p("block_count", 32)), num_heads=heads, num_kv_heads=int(p("attention.head_count_kv", heads)),
         head_dim=int(p("attention.key_length", hidden // heads)), rope_theta=float(p("rope.freq_base", 10000.0)),
@@ -252,6 +253,8 @@ def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
             full["gate"], full["up"] = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
         else:  # Phi-3: ffn_up holds [gate; up]
             full["gate"], full["up"] = torch.chunk(get(b + "ffn_up.weight"), 2, 0)
+        if b + "attn_q_norm.weight" in T:  # Qwen3
+            full["q_norm"], full["k_norm"] = get(b + "attn_q_norm.weight"), get(b + "attn_k_norm.weight")
         if b + "attn_q.bias" in T:
             full["q_b"], full["k_b"], full["v_b"] = (get(b + "attn_q.bias"), get(b + "attn_k.bias"),
                                                    get(b + "attn_v.bias"))
@@ -312,7 +315,7 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
     from gguf import GGMLQuantizationType as Q
     from gguf import GGUFWriter
 
-    if arch not in ("llama", "phi3"):
+    if arch not in ("llama", "phi3", "qwen3"):
         raise ValueError(f"cannot write GGUF architecture {arch!r}")
     w = GGUFWriter(path, arch)
     w.add_name(cfg.name)
@@ -370,6 +373,12 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
             put(b + "ffn_norm.weight", t["post_norm"], False)
             if arch == "phi3":
                 put(b + "attn_qkv.weight", torch.cat([t["q"], t["k"], t["v"]], 0), True)
+            elif arch == "qwen3":  # stored unpermuted, with per-head q/k norms
+                put(b + "attn_q.weight", t["q"], True)
+                put(b + "attn_k.weight", t["k"], True)
+                put(b + "attn_v.weight", t["v"], True)
+                put(b + "attn_q_norm.weight", t["q_norm"], False)
+                put(b + "attn_k_norm.weight", t["k_norm"], False)
             else:
                 put(b + "attn_q.weight", torch.from_numpy(_permute(t["q"].float().cpu().numpy(), cfg.num_heads)),
                     True)

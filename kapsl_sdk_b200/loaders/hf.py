@@ -57,6 +57,8 @@ def iter_hf_full(root: str, cfg: ModelConfig):
         else:
             full["q"], full["k"], full["v"] = (st.get(a + "q_proj.weight"), st.get(a + "k_proj.weight"),
                                                st.get(a + "v_proj.weight"))
+        if st.has(a + "q_norm.weight"):  # Qwen3
+            full["q_norm"], full["k_norm"] = st.get(a + "q_norm.weight"), st.get(a + "k_norm.weight")
         if st.has(a + "q_proj.bias"):
             full["q_b"], full["k_b"], full["v_b"] = (st.get(a + "q_proj.bias"), st.get(a + "k_proj.bias"),
                                                    st.get(a + "v_proj.bias"))
@@ -116,13 +118,16 @@ def save_hf_model(root: str, cfg: ModelConfig, full_stream) -> None:
             t[p + "post_attention_layernorm.weight"] = v["post_norm"]
             if v.get("q_b") is not None:
                 t[a + "q_proj.bias"], t[a + "k_proj.bias"], t[a + "v_proj.bias"] = v["q_b"], v["k_b"], v["v_b"]
+            if v.get("q_norm") is not None:
+                t[a + "q_norm.weight"], t[a + "k_norm.weight"] = v["q_norm"], v["k_norm"]
             if "gate" in v:
                 t[p + "mlp.gate_proj.weight"], t[p + "mlp.up_proj.weight"] = v["gate"], v["up"]
                 t[p + "mlp.down_proj.weight"] = v["down"]
             li += 1
     t.setdefault("model.norm.weight", torch.ones(cfg.hidden_size))
     save_file({k: x.detach().contiguous().cpu() for k, x in t.items()}, os.path.join(root, "model.safetensors"))
-    hf = {"model_type": "qwen2" if cfg.arch == "qwen2" else "llama", "vocab_size": cfg.vocab_size,
+    hf = {"model_type": "qwen3" if cfg.qk_norm else ("qwen2" if cfg.arch == "qwen2" else "llama"),
+          "vocab_size": cfg.vocab_size,
           "hidden_size": cfg.hidden_size, "intermediate_size": cfg.intermediate_size,
           "num_hidden_layers": cfg.num_layers, "num_attention_heads": cfg.num_heads,
           "num_key_value_heads": cfg.num_kv_heads, "head_dim": cfg.head_dim, "rope_theta": cfg.rope_theta,

@@ -15,13 +15,14 @@ from typing import Optional
 
 # HF model_type -> the runtime's layer family (Mistral and Phi-3 are Llama-shaped
 # decoders; Phi-3's fused projections are split by the checkpoint loader)
-HF_MODEL_TYPES = {"llama": "llama", "mistral": "llama", "phi3": "llama", "qwen2": "qwen2", "mixtral": "mixtral"}
+HF_MODEL_TYPES = {"llama": "llama", "mistral": "llama", "phi3": "llama", "qwen2": "qwen2", "mixtral": "mixtral",
+                  "qwen3": "qwen3"}
 
 
 @dataclass
 class ModelConfig:
     name: str = "custom"
-    arch: str = "llama"  # llama | qwen2 | mixtral
+    arch: str = "llama"  # llama | qwen2 | qwen3 | mixtral
     vocab_size: int = 32000
     hidden_size: int = 4096
     intermediate_size: int = 11008
@@ -38,6 +39,7 @@ class ModelConfig:
     experts_per_token: int = 0
     weight_format: str = "bf16"  # bf16 | q4_k (GGUF k-quant linear layers, dequantized in the GEMM)
     rope_scaling: Optional[dict] = None  # HF rope_scaling (linear | llama3 | yarn) or GGUF frequency factors
+    qk_norm: bool = False  # per-head RMSNorm of q and k before RoPE (Qwen3); CPU backend only
     bos_token_id: Optional[int] = 1
     eos_token_id: Optional[int] = 2
     extra: dict = field(default_factory=dict)
@@ -122,6 +124,7 @@ class ModelConfig:
             bos_token_id=c.get("bos_token_id"),
             eos_token_id=eos,
             rope_scaling=_rope_scaling(c),
+            qk_norm=mt == "qwen3",
         )
 
 

@@ -86,8 +86,12 @@ class CPUCausalLM:
             qkv = x @ L["qkv"].T
             if L["qkv_b"] is not None:
                 qkv = qkv + L["qkv_b"]
-            q = ref.apply_rope(qkv[:, :hq * D].view(T, hq, D), positions, self.cos_sin)
-            k = ref.apply_rope(qkv[:, hq * D:(hq + hkv) * D].view(T, hkv, D), positions, self.cos_sin)
+            q, k = qkv[:, :hq * D].view(T, hq, D), qkv[:, hq * D:(hq + hkv) * D].view(T, hkv, D)
+            if L.get("q_norm") is not None:  # Qwen3: per-head RMSNorm before RoPE
+                q = ref.rmsnorm(q, L["q_norm"], cfg.rms_eps)[0]
+                k = ref.rmsnorm(k, L["k_norm"], cfg.rms_eps)[0]
+            q = ref.apply_rope(q, positions, self.cos_sin)
+            k = ref.apply_rope(k, positions, self.cos_sin)
             v = qkv[:, (hq + hkv) * D:].view(T, hkv, D)
             kc, vc = k_caches[li], v_caches[li]
             kc[blk, :, off] = k.to(kc.dtype)
@@ -137,6 +141,10 @@ class CPUCausalLM:
             q = qkv[:, :hq * D].contiguous().view(T, hq, D)
             kk = qkv[:, hq * D:(hq + hkv) * D].contiguous().view(T, hkv, D)
             vv = qkv[:, (hq + hkv) * D:].contiguous().view(T, hkv, D)
+            if L.get("q_norm") is not None:  # Qwen3: per-head RMSNorm before RoPE
+                qn, kn = q.view(T * hq, D), kk.view(T * hkv, D)
+                k_.rmsnorm(qn.numpy(), L["q_norm"].numpy(), qn.numpy(), cfg.rms_eps)
+                k_.rmsnorm(kn.numpy(), L["k_norm"].numpy(), kn.numpy(), cfg.rms_eps)
             k_.rope(q.numpy(), pos, cs)
             k_.rope(kk.numpy(), pos, cs)
             kc, vc = k_caches[li], v_caches[li]

@@ -200,6 +200,9 @@ def random_layer(cfg: ModelConfig, layer: int, gen: torch.Generator, device, std
         "in_norm": torch.ones(d, device=device, dtype=torch.bfloat16),
         "post_norm": torch.ones(d, device=device, dtype=torch.bfloat16),
     }
+    if cfg.qk_norm:
+        full["q_norm"] = torch.ones(D, device=device, dtype=torch.bfloat16) + rn(D) * 10
+        full["k_norm"] = torch.ones(D, device=device, dtype=torch.bfloat16) + rn(D) * 10
     if cfg.qkv_bias:
         full["q_b"] = rn(cfg.num_heads * D)
         full["k_b"] = rn(cfg.num_kv_heads * D)
@@ -287,6 +290,8 @@ class CausalLM:
     """GPU decoder over a paged KV cache, one instance per rank."""
 
     def __init__(self, cfg: ModelConfig, weights: ModelWeights, device, tp_comm=None, moe=None, stage=None):
+        if cfg.qk_norm:
+            raise ValueError("per-head q/k normalisation (Qwen3) runs on the CPU backend only")
         self.cfg = cfg
         self.w = weights
         self.device = torch.device(device)
@@ -376,8 +381,12 @@ def reference_forward(cfg: ModelConfig, full_layers: list, embed: torch.Tensor, 
             q = q + full["q_b"].float()
             k = k + full["k_b"].float()
             v = v + full["v_b"].float()
-        q = ref.apply_rope(q.view(-1, cfg.num_heads, D), pos, cs)
-        k = ref.apply_rope(k.view(-1, cfg.num_kv_heads, D), pos, cs)
+        q, k = q.view(-1, cfg.num_heads, D), k.view(-1, cfg.num_kv_heads, D)
+        if full.get("q_norm") is not None:  # Qwen3: per-head RMSNorm before RoPE
+            q = ref.rmsnorm(q, full["q_norm"], cfg.rms_eps)[0]
+            k = ref.rmsnorm(k, full["k_norm"], cfg.rms_eps)[0]
+        q = ref.apply_rope(q, pos, cs)
+        k = ref.apply_rope(k, pos, cs)
         v = v.view(-1, cfg.num_kv_heads, D)
         a = ref.attention(q, k, v, 1.0 / math.sqrt(D), 0).reshape(len(tokens), -1)
         h = h + a @ full["o"].float().T

@@ -97,3 +97,50 @@ def test_unsupported_gguf_architecture_is_refused():
     w.close()
     with pytest.raises(ValueError, match="GGUF architecture 'gemma' is not supported"):
         gguf_config(GGUFReader(p))
+
+
+def qwen3_tiny():
+    return ModelConfig(name="q3", arch="qwen3", vocab_size=300, hidden_size=64, intermediate_size=128, num_layers=2,
+                       num_heads=4, num_kv_heads=2, head_dim=16, max_position=256, bos_token_id=None,
+                       eos_token_id=None, qk_norm=True)
+
+
+def test_qwen3_qk_norm_cpu_matches_oracle_and_round_trips():
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.loaders.gguf import load_gguf_model, write_gguf_model
+    from kapsl_sdk_b200.loaders.hf import load_hf_model, save_hf_model
+    from kapsl_sdk_b200.models.llama import random_full_weights, reference_forward
+
+    cfg = qwen3_tiny()
+    prompt = list(range(11, 70))
+    ecfg = EngineConfig(max_num_seqs=2, max_num_batched_tokens=64, max_model_len=200, num_blocks=32)
+    eng = LLMEngine(cfg, device="cpu", engine_cfg=ecfg, seed=0)
+    out = eng.generate([prompt], SamplingParams.greedy(6, ignore_eos=True))[0]
+    m = eng.model
+    assert all("q_norm" in L for L in m.layers)
+    toks = list(prompt)
+    for _ in range(6):
+        toks.append(int(reference_forward(cfg, m.layers, m.embed, m.lm_head, m.final_norm, toks)[-1].argmax()))
+    assert out == toks[len(prompt):]
+    # the norms change the result (they are not ones)
+    plain = ModelConfig(**{**cfg.to_dict(), "qk_norm": False, "arch": "qwen2"})
+    no_norm = [{k: v for k, v in L.items() if k not in ("q_norm", "k_norm")} for L in m.layers]
+    assert not torch.allclose(reference_forward(cfg, m.layers, m.embed, m.lm_head, m.final_norm, prompt),
+                              reference_forward(plain, no_norm, m.embed, m.lm_head, m.final_norm, prompt))
+    d = tempfile.mkdtemp()
+    save_hf_model(os.path.join(d, "hf"), cfg, random_full_weights(cfg, torch.device("cpu"), seed=5, std=0.1))
+    c_hf, m_hf, _ = load_hf_model(os.path.join(d, "hf"), "cpu")
+    assert c_hf.qk_norm and c_hf.arch == "qwen3"
+    p = os.path.join(d, "q3.gguf")
+    write_gguf_model(p, cfg, random_full_weights(cfg, torch.device("cpu"), seed=5, std=0.1), arch="qwen3")
+    c_g, m_g, _ = load_gguf_model(p, "cpu")
+    assert c_g.qk_norm
+    assert _greedy(c_hf, m_hf, prompt) == _greedy(c_g, m_g, prompt)
+
+
+def test_qwen3_is_refused_on_the_gpu_path():
+    from kapsl_sdk_b200.llm.engine import LLMEngine
+
+    with pytest.raises(ValueError, match="CPU backend only"):
+        LLMEngine(qwen3_tiny(), device="cuda")
