@@ -84,8 +84,9 @@ class LLMEngine:
             self.runner = CPUModelRunner(self.model, self.pool)
             self._finish_init(cfg, e, nblocks, tp_comm)
             return
-        if cfg.qk_norm:
-            raise ValueError("per-head q/k normalisation (Qwen3) runs on the CPU backend only")
+        if cfg.cpu_only:
+            raise ValueError(f"{cfg.arch} layers (q/k norms, GeGLU, soft-capping or sliding windows) run on the "
+                             "CPU backend only")
         if weights is None:
             tp = 1 if tp_comm is None else tp_comm.world_size
             rank = 0 if tp_comm is None else tp_comm.rank

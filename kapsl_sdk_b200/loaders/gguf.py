@@ -175,7 +175,7 @@ def _field(reader, key, default=None):
     return v
 
 
-GGUF_ARCHS = ("llama", "qwen2", "qwen3", "phi3")
+GGUF_ARCHS = ("llama", "qwen2", "qwen3", "phi3", "gemma", "gemma2")
 
 
 def gguf_config(reader) -> ModelConfig:
@@ -188,8 +188,9 @@ def gguf_config(reader) -> ModelConfig:
     tokens = _field(reader, "tokenizer.ggml.tokens")
     vocab = int(p("vocab_size", len(tokens) if tokens is not None else 32000))
     return ModelConfig(
-        name=_field(reader, "general.name", arch) or arch, arch=arch if arch in ("qwen2", "qwen3") else "llama",
-        qk_norm=arch == "qwen3",
+        name=_field(reader, "general.name", arch) or arch,
+        arch=arch if arch in ("qwen2", "qwen3", "gemma", "gemma2") else "llama",
+        qk_norm=arch == "qwen3", **_gguf_gemma(reader, arch, hidden, int(p("attention.key_length", hidden // heads))),
         vocab_size=vocab, hidden_size=hidden, intermediate_size=int(p("feed_forward_length", 4 * hidden)),
         num_layers=int(p("block_count", 32)), num_heads=heads, num_kv_heads=int(p("attention.head_count_kv", heads)),
         head_dim=int(p("attention.key_length", hidden // heads)), rope_theta=float(p("rope.freq_base", 10000.0)),
@@ -199,6 +200,20 @@ def gguf_config(reader) -> ModelConfig:
         eos_token_id=_field(reader, "tokenizer.ggml.eos_token_id", 2),
         rope_scaling=_gguf_rope_scaling(reader, arch),
     )
+
+
+def _gguf_gemma(reader, arch: str, hidden: int, head_dim: int) -> dict:
+    """Gemma options from GGUF (norm weights there already include the +1)."""
+    if arch not in ("gemma", "gemma2"):
+        return {}
+    out = dict(act="gelu_tanh", embed_scale=hidden ** 0.5, tie_embeddings=True)
+    if arch == "gemma2":
+        window = int(_field(reader, "gemma2.attention.sliding_window", 0) or 0)
+        out.update(attn_softcap=float(_field(reader, "gemma2.attn_logit_softcapping", 0.0) or 0.0),
+                   final_softcap=float(_field(reader, "gemma2.final_logit_softcapping", 0.0) or 0.0),
+                   attn_scale=float(_field(reader, "gemma2.attention.scale", head_dim ** -0.5)),
+                   sliding_window=window, sliding_pattern=2 if window else 0)
+    return out
 
 
 def _gguf_rope_scaling(reader, arch: str) -> Optional[dict]:
@@ -249,6 +264,9 @@ def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
                 "v": torch.from_numpy(np.ascontiguousarray(v)), "o": get(b + "attn_output.weight"),
                 "in_norm": get(b + "attn_norm.weight"), "post_norm": get(b + "ffn_norm.weight"),
                 "down": get(b + "ffn_down.weight")}
+        if b + "post_attention_norm.weight" in T:  # Gemma 2 sandwich norms
+            full["attn_out_norm"] = get(b + "post_attention_norm.weight")
+            full["mlp_out_norm"] = get(b + "post_ffw_norm.weight")
         if b + "ffn_gate.weight" in T:
             full["gate"], full["up"] = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
         else:  # Phi-3: ffn_up holds [gate; up]
@@ -315,7 +333,7 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
     from gguf import GGMLQuantizationType as Q
     from gguf import GGUFWriter
 
-    if arch not in ("llama", "phi3", "qwen3"):
+    if arch not in ("llama", "phi3", "qwen3", "gemma2"):
         raise ValueError(f"cannot write GGUF architecture {arch!r}")
     w = GGUFWriter(path, arch)
     w.add_name(cfg.name)
@@ -346,6 +364,12 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
         else:
             w.add_tensor(name, np.ascontiguousarray(a.astype(np.float32)))
 
+    if arch == "gemma2":
+        w.add_float32("gemma2.attn_logit_softcapping", cfg.attn_softcap)
+        w.add_float32("gemma2.final_logit_softcapping", cfg.final_softcap)
+        w.add_uint32("gemma2.attention.sliding_window", cfg.sliding_window)
+        w.add_float32("gemma2.attention.scale", cfg.attn_scale or cfg.head_dim ** -0.5)
+        w.add_uint32("gemma2.attention.key_length", cfg.head_dim)
     rs = cfg.rope_scaling or {}
     if rs.get("rope_type") == "freq_factors":
         w.add_tensor("rope_freqs.weight", np.asarray(rs["factors"], dtype=np.float32))
@@ -373,6 +397,12 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
             put(b + "ffn_norm.weight", t["post_norm"], False)
             if arch == "phi3":
                 put(b + "attn_qkv.weight", torch.cat([t["q"], t["k"], t["v"]], 0), True)
+            elif arch == "gemma2":  # unpermuted; norms carry the +1; sandwich norms
+                put(b + "attn_q.weight", t["q"], True)
+                put(b + "attn_k.weight", t["k"], True)
+                put(b + "attn_v.weight", t["v"], True)
+                put(b + "post_attention_norm.weight", t["attn_out_norm"], False)
+                put(b + "post_ffw_norm.weight", t["mlp_out_norm"], False)
             elif arch == "qwen3":  # stored unpermuted, with per-head q/k norms
                 put(b + "attn_q.weight", t["q"], True)
                 put(b + "attn_k.weight", t["k"], True)

@@ -42,15 +42,26 @@ class _SafeTensors:
 
 def iter_hf_full(root: str, cfg: ModelConfig):
     st = _SafeTensors(root)
+    gemma = cfg.arch in ("gemma", "gemma2")
+
+    def norm(name):  # Gemma stores w for a (1 + w) RMSNorm scale
+        w = st.get(name)
+        return w.float() + 1.0 if gemma else w
+
     emb = st.get("model.embed_tokens.weight")
     yield "embed", emb
     yield "lm_head", st.get("lm_head.weight") if st.has("lm_head.weight") else emb
-    yield "final_norm", st.get("model.norm.weight")
+    yield "final_norm", norm("model.norm.weight")
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
         a = p + "self_attn."
-        full = {"o": st.get(a + "o_proj.weight"), "in_norm": st.get(p + "input_layernorm.weight"),
-                "post_norm": st.get(p + "post_attention_layernorm.weight")}
+        full = {"o": st.get(a + "o_proj.weight"), "in_norm": norm(p + "input_layernorm.weight")}
+        if cfg.arch == "gemma2":  # sandwich norms around attention and MLP
+            full["attn_out_norm"] = norm(p + "post_attention_layernorm.weight")
+            full["post_norm"] = norm(p + "pre_feedforward_layernorm.weight")
+            full["mlp_out_norm"] = norm(p + "post_feedforward_layernorm.weight")
+        else:
+            full["post_norm"] = norm(p + "post_attention_layernorm.weight")
         if st.has(a + "qkv_proj.weight"):  # Phi-3: fused [q; k; v]
             full["q"], full["k"], full["v"] = torch.split(st.get(a + "qkv_proj.weight"),
                                                           [cfg.q_size, cfg.kv_size, cfg.kv_size], 0)

@@ -8,6 +8,7 @@ the same fields are read from HF ``config.json`` or GGUF metadata
 from __future__ import annotations
 
 import json
+import math
 import os
 from dataclasses import asdict, dataclass, field
 from typing import Optional
@@ -16,13 +17,13 @@ from typing import Optional
 # HF model_type -> the runtime's layer family (Mistral and Phi-3 are Llama-shaped
 # decoders; Phi-3's fused projections are split by the checkpoint loader)
 HF_MODEL_TYPES = {"llama": "llama", "mistral": "llama", "phi3": "llama", "qwen2": "qwen2", "mixtral": "mixtral",
-                  "qwen3": "qwen3"}
+                  "qwen3": "qwen3", "gemma": "gemma", "gemma2": "gemma2"}
 
 
 @dataclass
 class ModelConfig:
     name: str = "custom"
-    arch: str = "llama"  # llama | qwen2 | qwen3 | mixtral
+    arch: str = "llama"  # llama | qwen2 | qwen3 | mixtral | gemma | gemma2
     vocab_size: int = 32000
     hidden_size: int = 4096
     intermediate_size: int = 11008
@@ -40,6 +41,32 @@ class ModelConfig:
     weight_format: str = "bf16"  # bf16 | q4_k (GGUF k-quant linear layers, dequantized in the GEMM)
     rope_scaling: Optional[dict] = None  # HF rope_scaling (linear | llama3 | yarn) or GGUF frequency factors
     qk_norm: bool = False  # per-head RMSNorm of q and k before RoPE (Qwen3); CPU backend only
+    # Gemma-family options (CPU backend only)
+    act: str = "silu"              # gated-MLP activation: silu | gelu_tanh
+    embed_scale: float = 1.0       # token embeddings multiplied by this (Gemma: sqrt(hidden))
+    attn_scale: Optional[float] = None  # attention logit scale (default 1/sqrt(head_dim))
+    attn_softcap: float = 0.0      # logits -> cap * tanh(logits / cap) when > 0
+    final_softcap: float = 0.0
+    sliding_window: int = 0        # local attention window of the sliding layers
+    sliding_pattern: int = 0       # layer i is sliding iff i % pattern != pattern - 1 (0: none)
+    layer_types: Optional[list] = None  # explicit "sliding_attention" / "full_attention" per layer
+
+    def layer_window(self, i: int) -> int:
+        """Key window of layer ``i`` (0: full causal attention)."""
+        if not self.sliding_window:
+            return 0
+        if self.layer_types:
+            return self.sliding_window if self.layer_types[i] == "sliding_attention" else 0
+        if self.sliding_pattern and i % self.sliding_pattern != self.sliding_pattern - 1:
+            return self.sliding_window
+        return 0
+
+    @property
+    def cpu_only(self) -> bool:
+        """Features the GPU kernels do not implement."""
+        return (self.qk_norm or self.act != "silu" or self.embed_scale != 1.0 or self.attn_scale is not None or
+                self.attn_softcap > 0 or self.final_softcap > 0 or self.sliding_pattern > 0 or
+                bool(self.layer_types))
     bos_token_id: Optional[int] = 1
     eos_token_id: Optional[int] = 2
     extra: dict = field(default_factory=dict)
@@ -89,6 +116,11 @@ class ModelConfig:
         else:
             c = dict(path_or_dict)
         mt = c.get("model_type", "llama")
+        rp = c.get("rope_parameters")  # transformers >= 5 keeps rope_theta and the scaling here
+        if isinstance(rp, dict) and "rope_theta" in rp:
+            c.setdefault("rope_theta", rp["rope_theta"])
+            if rp.get("rope_type", "default") != "default" and not c.get("rope_scaling"):
+                c["rope_scaling"] = {k: v for k, v in rp.items() if k != "rope_theta"}
         if mt not in HF_MODEL_TYPES:
             raise ValueError(f"model_type {mt!r} is not supported (supported: {', '.join(sorted(HF_MODEL_TYPES))})")
         arch = HF_MODEL_TYPES[mt]
@@ -98,6 +130,19 @@ class ModelConfig:
         hidden = c.get("hidden_size", 4096)
         max_pos = int(c.get("max_position_embeddings", 32768))
         window = c.get("sliding_window") if c.get("use_sliding_window", True) else None
+        gemma = {}
+        if mt in ("gemma", "gemma2"):
+            act = c.get("hidden_activation") or c.get("hidden_act") or "gelu_pytorch_tanh"
+            if act not in ("gelu_pytorch_tanh", "gelu"):
+                raise ValueError(f"Gemma activation {act!r} is not supported")
+            gemma = dict(act="gelu_tanh", embed_scale=math.sqrt(hidden))
+            if mt == "gemma2":
+                gemma.update(attn_softcap=float(c.get("attn_logit_softcapping") or 0.0),
+                             final_softcap=float(c.get("final_logit_softcapping") or 0.0),
+                             attn_scale=float(c.get("query_pre_attn_scalar", c.get("head_dim", 256))) ** -0.5,
+                             sliding_window=int(window or 0), sliding_pattern=2 if window else 0,
+                             layer_types=list(c["layer_types"]) if c.get("layer_types") else None)
+            window = None  # handled per layer
         if window and int(window) < max_pos:
             # sliding-window attention equals full attention up to the window: serve that far exactly
             max_pos = int(window)
@@ -117,7 +162,7 @@ class ModelConfig:
             rope_theta=float(c.get("rope_theta", 10000.0)),
             rms_eps=float(c.get("rms_norm_eps", 1e-5)),
             qkv_bias=bool(c.get("attention_bias", arch == "qwen2")),
-            tie_embeddings=bool(c.get("tie_word_embeddings", False)),
+            tie_embeddings=bool(c.get("tie_word_embeddings", mt in ("gemma", "gemma2"))),
             max_position=max_pos,
             num_experts=int(c.get("num_local_experts", 0)),
             experts_per_token=int(c.get("num_experts_per_tok", 0)),
@@ -125,6 +170,7 @@ class ModelConfig:
             eos_token_id=eos,
             rope_scaling=_rope_scaling(c),
             qk_norm=mt == "qwen3",
+            **gemma,
         )
 
 

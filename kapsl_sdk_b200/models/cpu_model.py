@@ -41,7 +41,7 @@ class CPUCausalLM:
             self.layers.append(d)
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, scaling=cfg.rope_scaling)
         self.hq, self.hkv, self.D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
-        self.scale = 1.0 / math.sqrt(self.D)
+        self.scale = cfg.attn_scale if cfg.attn_scale is not None else 1.0 / math.sqrt(self.D)
         self.device = torch.device("cpu")
         self.stage = None  # PipelineStage when this model holds one pipeline stage's layers
         self._k = None  # C++ CPU kernels (kapsl_sdk_b200._native.cpu) when built
@@ -52,6 +52,9 @@ class CPUCausalLM:
                 self._k = native().cpu
             except Exception:
                 self._k = None
+        if (cfg.act != "silu" or cfg.embed_scale != 1.0 or cfg.attn_softcap or cfg.final_softcap
+                or cfg.sliding_pattern or any("attn_out_norm" in L for L in self.layers)):
+            self._k = None  # GeGLU / soft-capping / windows / sandwich norms: the PyTorch statement
 
     @classmethod
     def random(cls, cfg: ModelConfig, seed: int = 0, std: float = 0.02, layers: Optional[range] = None,
@@ -79,6 +82,7 @@ class CPUCausalLM:
         D, hq, hkv = self.D, self.hq, self.hkv
         h = self._stage_input(ids)
         bs = k_caches[0].shape[2]
+        layer_ids = self.layer_ids
         blk = (slots // bs).long()
         off = (slots % bs).long()
         for li, L in enumerate(self.layers):
@@ -97,22 +101,33 @@ class CPUCausalLM:
             kc[blk, :, off] = k.to(kc.dtype)
             vc[blk, :, off] = v.to(vc.dtype)
             attn = torch.empty(T, hq * D)
+            win = cfg.layer_window(layer_ids[li])
             for r0, n, ctx, blocks in seqs:
                 kk = ref.gather_paged(kc, blocks, ctx).float()
                 vv = ref.gather_paged(vc, blocks, ctx).float()
-                attn[r0:r0 + n] = ref.attention(q[r0:r0 + n], kk, vv, self.scale, ctx - n).reshape(n, hq * D)
-            h = h + attn @ L["o"].T
+                attn[r0:r0 + n] = ref.attention(q[r0:r0 + n], kk, vv, self.scale, ctx - n, cfg.attn_softcap,
+                                                win).reshape(n, hq * D)
+            o = attn @ L["o"].T
+            if "attn_out_norm" in L:  # Gemma 2: norm of the attention output before the residual add
+                o, _ = ref.rmsnorm(o, L["attn_out_norm"], cfg.rms_eps)
+            h = h + o
             x, _ = ref.rmsnorm(h, L["post_norm"], cfg.rms_eps)
             if cfg.is_moe:
                 h = h + self._moe(x, L)
             else:
                 gu = x @ L["gate_up"].T
-                h = h + ref.silu_mul(gu) @ L["down"].T
+                y = (ref.gelu_tanh_mul(gu) if cfg.act == "gelu_tanh" else ref.silu_mul(gu)) @ L["down"].T
+                if "mlp_out_norm" in L:
+                    y, _ = ref.rmsnorm(y, L["mlp_out_norm"], cfg.rms_eps)
+                h = h + y
         if self.stage is not None and not self.stage.last:
             self.stage.send_hidden(h)
             return None
         xs, _ = ref.rmsnorm(h[logits_rows], self.final_norm, cfg.rms_eps)
-        return xs @ self.lm_head.T
+        logits = xs @ self.lm_head.T
+        if cfg.final_softcap > 0:
+            logits = torch.tanh(logits / cfg.final_softcap) * cfg.final_softcap
+        return logits
 
     def _forward_native(self, ids, positions, slots, seqs, k_caches, v_caches, logits_rows) -> torch.Tensor:
         """Same computation with the C++ CPU kernels between the BLAS matmuls."""
@@ -166,11 +181,17 @@ class CPUCausalLM:
         k_.rmsnorm(xs.numpy(), self.final_norm.numpy(), xs.numpy(), cfg.rms_eps)
         return xs @ self.lm_head.T
 
+    @property
+    def layer_ids(self) -> list:
+        """Global index of each held layer (a pipeline stage holds a contiguous range)."""
+        return list(self.stage.layers) if self.stage is not None else list(range(len(self.layers)))
+
     def _stage_input(self, ids: torch.Tensor) -> torch.Tensor:
         """Token embeddings, or (later pipeline stages) the previous stage's hidden state."""
         if self.stage is not None and not self.stage.first:
             return self.stage.recv_hidden(ids.numel(), self.cfg.hidden_size, torch.float32, self.device)
-        return self.embed[ids.long()]
+        h = self.embed[ids.long()]
+        return h * self.cfg.embed_scale if self.cfg.embed_scale != 1.0 else h
 
     def _moe(self, x: torch.Tensor, L: dict) -> torch.Tensor:
         cfg = self.cfg

@@ -290,8 +290,9 @@ class CausalLM:
     """GPU decoder over a paged KV cache, one instance per rank."""
 
     def __init__(self, cfg: ModelConfig, weights: ModelWeights, device, tp_comm=None, moe=None, stage=None):
-        if cfg.qk_norm:
-            raise ValueError("per-head q/k normalisation (Qwen3) runs on the CPU backend only")
+        if cfg.cpu_only:
+            raise ValueError(f"{cfg.arch} layers (q/k norms, GeGLU, soft-capping or sliding windows) run on the "
+                             "CPU backend only")
         self.cfg = cfg
         self.w = weights
         self.device = torch.device(device)

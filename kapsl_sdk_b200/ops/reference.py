@@ -116,17 +116,32 @@ def silu_mul(x: torch.Tensor) -> torch.Tensor:
     return g * torch.sigmoid(g) * u
 
 
-def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal_offset: int) -> torch.Tensor:
-    """q: [Sq, Hq, D]; k, v: [Sk, Hkv, D]; query i sees keys <= causal_offset + i."""
+def gelu_tanh_mul(x: torch.Tensor) -> torch.Tensor:
+    """GeGLU with the tanh approximation of GELU: gelu(g) * u over [g | u]."""
+    F = x.shape[-1] // 2
+    g, u = x[..., :F].float(), x[..., F:].float()
+    return torch.nn.functional.gelu(g, approximate="tanh") * u
+
+
+def attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float, causal_offset: int,
+              softcap: float = 0.0, window: int = 0) -> torch.Tensor:
+    """q: [Sq, Hq, D]; k, v: [Sk, Hkv, D]; query i sees keys <= causal_offset + i
+    (and, with ``window``, only the last ``window`` of them); ``softcap`` > 0
+    maps the scaled logits through cap * tanh(s / cap)."""
     Sq, Hq, D = q.shape
     Sk, Hkv, _ = k.shape
     g = Hq // Hkv
     kk = k.float().repeat_interleave(g, dim=1)
     vv = v.float().repeat_interleave(g, dim=1)
     s = torch.einsum("qhd,khd->hqk", q.float(), kk) * scale
+    if softcap > 0:
+        s = torch.tanh(s / softcap) * softcap
     qi = torch.arange(Sq)[:, None] + causal_offset
     ki = torch.arange(Sk)[None, :]
-    s = s.masked_fill((ki > qi)[None], float("-inf"))
+    masked = ki > qi
+    if window:
+        masked = masked | (qi - ki >= window)
+    s = s.masked_fill(masked[None], float("-inf"))
     p = torch.softmax(s, dim=-1)
     return torch.einsum("hqk,khd->qhd", p, vv)
 

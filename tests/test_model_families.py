@@ -75,8 +75,8 @@ def test_mistral_window_and_refusals():
     c = ModelConfig.from_hf_config({"model_type": "mistral", "hidden_size": 256, "num_attention_heads": 4,
                                     "max_position_embeddings": 32768, "sliding_window": None})
     assert c.max_position == 32768
-    with pytest.raises(ValueError, match="model_type 'gemma' is not supported"):
-        ModelConfig.from_hf_config({"model_type": "gemma"})
+    with pytest.raises(ValueError, match="model_type 'falcon' is not supported"):
+        ModelConfig.from_hf_config({"model_type": "falcon"})
     with pytest.raises(ValueError, match="partial rotary"):
         ModelConfig.from_hf_config({"model_type": "phi3", "partial_rotary_factor": 0.5})
 
@@ -88,14 +88,14 @@ def test_unsupported_gguf_architecture_is_refused():
     from kapsl_sdk_b200.loaders.gguf import gguf_config
 
     p = os.path.join(tempfile.mkdtemp(), "g.gguf")
-    w = GGUFWriter(p, "gemma")
+    w = GGUFWriter(p, "falcon")
     w.add_block_count(1)
     w.add_tensor("token_embd.weight", np.zeros((4, 4), np.float32))
     w.write_header_to_file()
     w.write_kv_data_to_file()
     w.write_tensors_to_file()
     w.close()
-    with pytest.raises(ValueError, match="GGUF architecture 'gemma' is not supported"):
+    with pytest.raises(ValueError, match="GGUF architecture 'falcon' is not supported"):
         gguf_config(GGUFReader(p))
 
 
