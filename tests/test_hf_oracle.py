@@ -20,6 +20,7 @@ FAMILIES = {
     "gemma": ("GemmaConfig", "GemmaForCausalLM", {}),
     "gemma2": ("Gemma2Config", "Gemma2ForCausalLM", {"sliding_window": 6, "attn_logit_softcapping": 8.0,
                                                      "final_logit_softcapping": 5.0, "query_pre_attn_scalar": 24}),
+    "mixtral": ("MixtralConfig", "MixtralForCausalLM", {"num_local_experts": 4, "num_experts_per_tok": 2}),
     "llama3-rope": ("LlamaConfig", "LlamaForCausalLM", {"rope_theta": 500000.0, "rope_scaling": {
         "rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
         "original_max_position_embeddings": 64}}),
