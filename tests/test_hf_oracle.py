@@ -101,3 +101,23 @@ def test_gemma2_gguf_round_trip_matches_transformers(tmp_path):
     eng = LLMEngine(c2, weights=m2, device="cpu", engine_cfg=EngineConfig(
         max_num_seqs=2, max_num_batched_tokens=16, max_model_len=128, num_blocks=32), seed=0)
     assert eng.generate([prompt], SamplingParams.greedy(8, ignore_eos=True))[0] == toks[len(prompt):]
+
+
+@pytest.mark.parametrize("family", ["llama", "qwen2", "mixtral", "llama3-rope"])
+def test_gpu_oracle_matches_transformers(family, tmp_path):
+    """models.llama.reference_forward is the fp32 oracle of the GPU kernel
+    tests; on the GPU families it must equal transformers' forward."""
+    from kapsl_sdk_b200.loaders.hf import iter_hf_full
+    from kapsl_sdk_b200.models.config import ModelConfig
+    from kapsl_sdk_b200.models.llama import reference_forward
+
+    hf, path = build(family, tmp_path)
+    cfg = ModelConfig.from_hf_config(path + "/config.json")
+    items = list(iter_hf_full(path, cfg))
+    d = dict((k, v) for k, v in items if k != "layer")
+    layers = [v for k, v in items if k == "layer"]
+    prompt = [5 + (7 * i) % 300 for i in range(23)]
+    got = reference_forward(cfg, layers, d["embed"], d["lm_head"], d["final_norm"], prompt)
+    with torch.no_grad():
+        want = hf(torch.tensor([prompt])).logits[0].float()
+    assert torch.allclose(got, want, atol=2e-4, rtol=1e-4), (got - want).abs().max()
