@@ -142,6 +142,35 @@ void prefill_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor work, Te
                                   err.data_ptr<int>(), cur_stream());
 }
 
+// tcgen05 version of prefill_attention; work items hold prefill_attn_tc_tokens(Hq, Hkv) tokens.
+void prefill_attention_tc(Tensor q, Tensor k_cache, Tensor v_cache, Tensor work, Tensor seq_info,
+                          Tensor block_tables, Tensor out, int64_t Hq, int64_t Hkv, double scale, Tensor err) {
+  CHECK_DT(q, at::kBFloat16, "q");
+  CHECK_DT(work, at::kInt, "work");
+  CHECK_DT(seq_info, at::kInt, "seq_info");
+  CHECK_DT(block_tables, at::kInt, "block_tables");
+  TORCH_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) >= Hq * 128, "prefill (tc): q [T, >=Hq*128]");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1, "prefill (tc): out row-major");
+  TORCH_CHECK(work.dim() == 2 && work.size(1) == 2 && work.is_contiguous(), "prefill (tc): work [n, 2]");
+  TORCH_CHECK(seq_info.dim() == 2 && seq_info.size(1) == 4 && seq_info.is_contiguous(), "prefill (tc): seq_info");
+  const c10::cuda::CUDAGuard g(q.device());
+  const int gq = (int)(Hq / Hkv);
+  const int tpc = kapsl::prefill_attn_tc_tokens_per_cta((int)Hq, (int)Hkv);
+  const uint64_t dims[3] = {128, (uint64_t)Hq, (uint64_t)q.size(0)};
+  const uint64_t strides[2] = {256, (uint64_t)q.stride(0) * 2};
+  const uint32_t box[3] = {64, (uint32_t)gq, (uint32_t)tpc};
+  CUtensorMap tq = kapsl::make_tmap_3d_bf16(q.data_ptr(), dims, strides, box, true);
+  CUtensorMap tk = cache_map(k_cache), tv = cache_map(v_cache);
+  kapsl::launch_prefill_attention_tc(tq, tk, tv, work.data_ptr<int32_t>(), (int)work.size(0),
+                                     seq_info.data_ptr<int32_t>(), block_tables.data_ptr<int32_t>(),
+                                     (int)block_tables.size(1), (int)Hq, (int)Hkv, (float)scale, bf(out),
+                                     out.stride(0), err.data_ptr<int>(), cur_stream());
+}
+
+int64_t prefill_attn_tc_tokens(int64_t Hq, int64_t Hkv) {
+  return kapsl::prefill_attn_tc_tokens_per_cta((int)Hq, (int)Hkv);
+}
+
 // rng and counts are per-sequence tables indexed by slots[row] (row itself when slots is None).
 void sample(Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, c10::optional<Tensor> rep_penalty,
             c10::optional<Tensor> counts, c10::optional<Tensor> slots, Tensor rng, Tensor out) {
@@ -478,6 +507,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_permute", &moe_permute, "stable expert sort of the top-k assignments (padded segments)");
   m.def("moe_gather", &moe_gather, "gather token rows into the expert-sorted buffer");
   m.def("moe_combine", &moe_combine, "weighted top-k combine + residual (+ peer pull and all-gather)");
+  m.def("prefill_attention_tc", &prefill_attention_tc,
+        "tcgen05 chunked-prefill attention (work items of prefill_attn_tc_tokens tokens)");
+  m.def("prefill_attn_tc_tokens", &prefill_attn_tc_tokens, "query tokens per CTA of prefill_attention_tc");
   m.def("kv_push", &kv_push, "KV connector: copy pool blocks into a (peer) pool over NVLink");
   m.def("kv_copy_blocks", &kv_copy_blocks, "KV block gather/scatter between device-accessible pools (host swap)");
   m.def("copy_async", &copy_async, "cudaMemcpyAsync on the current stream (copy-engine baseline)");

@@ -50,6 +50,27 @@ CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t rows, uint64_t cols, ui
   return m;
 }
 
+// 3-D bf16 tensor map: dims innermost first, strides of dims 1 and 2 in bytes.
+CUtensorMap make_tmap_3d_bf16(const void* base, const uint64_t (&dims)[3], const uint64_t (&strides_bytes)[2],
+                              const uint32_t (&box)[3], bool swizzle128) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15) != 0) throw std::runtime_error("TMA base address must be 16-byte aligned");
+  if (strides_bytes[0] % 16 != 0 || strides_bytes[1] % 16 != 0)
+    throw std::runtime_error("TMA strides must be multiples of 16 bytes");
+  if ((box[0] * 2) % 16 != 0 || (swizzle128 && box[0] * 2 > 128) || box[1] > 256 || box[2] > 256)
+    throw std::runtime_error("TMA 3-D box out of range");
+  CUtensorMap m;
+  cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+  cuuint64_t st[2] = {strides_bytes[0], strides_bytes[1]};
+  cuuint32_t b[3] = {box[0], box[1], box[2]};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), d, st, b, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) throw std::runtime_error("cuTensorMapEncodeTiled (3-D) failed: " + std::to_string((int)r));
+  return m;
+}
+
 // 2-D byte tensor map without swizzle (packed quantized blocks).
 CUtensorMap make_tmap_2d_u8(const void* base, uint64_t rows, uint64_t cols_bytes, uint64_t pitch_bytes,
                             uint32_t box_rows, uint32_t box_cols) {

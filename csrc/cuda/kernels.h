@@ -37,6 +37,16 @@ void launch_prefill_attention(const CUtensorMap& tk, const CUtensorMap& tv, cons
                               const int32_t* block_tables, int max_blocks, __nv_bfloat16* out, int64_t out_stride,
                               int Hq, int Hkv, float scale, int* err, cudaStream_t st);
 
+// tcgen05 prefill attention (attention_tc.cu): work items of prefill_attn_tc_tokens_per_cta tokens
+int prefill_attn_tc_tokens_per_cta(int Hq, int Hkv);
+size_t prefill_attn_tc_smem_bytes();
+void launch_prefill_attention_tc(const CUtensorMap& q_map, const CUtensorMap& k_map, const CUtensorMap& v_map,
+                                 const int32_t* work, int nwork, const int32_t* seq_info,
+                                 const int32_t* block_tables, int max_blocks, int Hq, int Hkv, float scale,
+                                 __nv_bfloat16* out, int64_t out_stride, int* err, cudaStream_t st);
+CUtensorMap make_tmap_3d_bf16(const void* base, const uint64_t (&dims)[3], const uint64_t (&strides_bytes)[2],
+                              const uint32_t (&box)[3], bool swizzle128);
+
 void launch_sample(float* logits, int64_t stride, int B, int V, const float* temperature, const int32_t* top_k,
                    const float* top_p, const float* rep_penalty, const int32_t* counts, const int32_t* slots,
                    uint64_t* rng, int32_t* out, cudaStream_t st);

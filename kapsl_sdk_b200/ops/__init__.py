@@ -198,6 +198,24 @@ def prefill_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Ten
     return out
 
 
+def prefill_attention_tc(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, work: torch.Tensor,
+                         seq_info: torch.Tensor, block_tables: torch.Tensor, num_heads: int, num_kv_heads: int,
+                         out: torch.Tensor, scale: Optional[float] = None) -> torch.Tensor:
+    """:func:`prefill_attention` on the tcgen05 kernel; ``work`` from
+    ``prefill_work(q_lens, tile=prefill_tc_tile(num_heads, num_kv_heads))``."""
+    if scale is None:
+        scale = 1.0 / math.sqrt(128)
+    cuda_ops().prefill_attention_tc(q, k_cache, v_cache, work, seq_info, block_tables, out, num_heads, num_kv_heads,
+                                    float(scale), error_buffer(q.device))
+    return out
+
+
+def prefill_tc_tile(num_heads: int, num_kv_heads: int) -> int:
+    """Query tokens per CTA of the tcgen05 prefill kernel: its 128 MMA rows hold
+    every query head of one KV head for floor(128 / group) tokens."""
+    return 128 // (num_heads // num_kv_heads)
+
+
 def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
            rng_state: torch.Tensor, out: torch.Tensor, rep_penalty: Optional[torch.Tensor] = None,
            counts: Optional[torch.Tensor] = None, slots: Optional[torch.Tensor] = None) -> torch.Tensor:
