@@ -1,5 +1,6 @@
 """Numerics of every sm_100a kernel against plain fp32 PyTorch restatements."""
 import math
+import os
 import random
 
 import numpy as np
@@ -207,6 +208,40 @@ def test_prefill_attention(dev, Hq, Hkv):
     work = ops.prefill_work([n for _, n in specs])
     ops.prefill_attention(q, kc, vc, torch.tensor(work, dtype=torch.int32, device=dev),
                           torch.tensor(seq_info, dtype=torch.int32, device=dev), bt, Hq, Hkv, out)
+    scale = 1 / math.sqrt(D)
+    for s, (c, n) in enumerate(specs):
+        k = ref.gather_paged(kc.cpu(), tables[s], c + n)
+        v = ref.gather_paged(vc.cpu(), tables[s], c + n)
+        q0 = seq_info[s][0]
+        exp = ref.attention(q[q0:q0 + n].view(n, Hq, D).cpu(), k, v, scale, c)
+        close(out[q0:q0 + n].view(n, Hq, D), exp, 0.02)
+
+
+@pytest.mark.skipif(os.environ.get("KAPSL_TEST_TC_PREFILL") != "1",
+                    reason="tcgen05 prefill attention has not run on a GPU yet; enable with KAPSL_TEST_TC_PREFILL=1")
+@pytest.mark.parametrize("Hq,Hkv", [(32, 8), (28, 4), (8, 8)])
+def test_prefill_attention_tc(dev, Hq, Hkv):
+    """The tcgen05 prefill kernel against the fp32 statement (same cases as the mma.sync kernel)."""
+    from kapsl_sdk_b200 import ops
+    from kapsl_sdk_b200.ops import reference as ref
+
+    specs = [(0, 130), (200, 64), (1000, 77), (16, 1), (0, 300)]
+    lens = [c + n for c, n in specs]
+    kc, vc, bt, tables = _paged_setup(dev, lens, Hkv, seed=1)
+    D = 128
+    T = sum(n for _, n in specs)
+    q = torch.randn(T, Hq * D, device=dev, dtype=torch.bfloat16)
+    out = torch.zeros(T, Hq * D, device=dev, dtype=torch.bfloat16)
+    seq_info = []
+    t = 0
+    for s, (c, n) in enumerate(specs):
+        seq_info.append((t, n, c + n, s))
+        t += n
+    work = ops.prefill_work([n for _, n in specs], tile=ops.prefill_tc_tile(Hq, Hkv))
+    ops.prefill_attention_tc(q, kc, vc, torch.tensor(work, dtype=torch.int32, device=dev),
+                             torch.tensor(seq_info, dtype=torch.int32, device=dev), bt, Hq, Hkv, out)
+    torch.cuda.synchronize()
+    assert ops.check_errors(torch.device(dev)) == 0
     scale = 1 / math.sqrt(D)
     for s, (c, n) in enumerate(specs):
         k = ref.gather_paged(kc.cpu(), tables[s], c + n)
