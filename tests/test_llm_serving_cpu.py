@@ -160,3 +160,55 @@ def test_backend_stream_over_unix_socket():
     finally:
         srv.stop()
         backend.unload()
+
+
+def test_backend_serves_on_the_callers_thread():
+    """own_thread=False: the engine loop runs in run() on the calling thread
+    (the thread that built the model keeps the only OpenMP team), and unload()
+    from another thread ends it."""
+    import threading
+
+    from kapsl_sdk_b200.llm.backend import LLMBackend
+
+    cfg = tiny_cfg(vocab_size=259 + 3)
+    backend = LLMBackend(cpu_engine(cfg), own_thread=False)
+    assert backend._thread is None
+    req = InferenceRequest(BinaryTensorPacket([1, 4], TensorDtype.INT32, np.array([5, 9, 13, 40], np.int32).tobytes()),
+                           metadata=RequestMetadata(max_new_tokens=4, temperature=0.0))
+    out = []
+    t = threading.Thread(target=lambda: (out.extend(backend.infer_stream(req)), backend.unload()))
+    t.start()
+    backend.run()  # returns after unload()
+    t.join(30)
+    assert len(out) >= 1 and not t.is_alive()
+
+
+def test_backend_load_builds_on_the_engine_thread(tmp_path):
+    import threading
+
+    from kapsl_sdk_b200.llm.backend import LLMBackend
+    from kapsl_sdk_b200.loaders.gguf import write_gguf_model
+    from kapsl_sdk_b200.models.llama import random_full_weights
+
+    cfg = tiny_cfg(vocab_size=320)
+    p = str(tmp_path / "m.gguf")
+    write_gguf_model(p, cfg, random_full_weights(cfg, torch.device("cpu"), seed=0), quant="f32")
+    seen = {}
+    import kapsl_sdk_b200.runtime.loader as loader
+
+    orig = loader.build_llm_engine
+
+    def spy(path, *a, **kw):
+        seen["thread"] = threading.current_thread().name
+        return orig(path, *a, **kw)
+
+    loader.build_llm_engine = spy
+    try:
+        be = LLMBackend()
+        be.load(p)
+        assert seen["thread"] == "kapsl-llm-engine" and be.health_check()
+        be.unload()
+        with pytest.raises(Exception):
+            LLMBackend().load(str(tmp_path / "missing.gguf"))
+    finally:
+        loader.build_llm_engine = orig
