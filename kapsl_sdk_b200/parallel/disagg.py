@@ -38,6 +38,7 @@ crates/kapsl-llm/src/kv_cache.rs:640-1796).
 """
 from __future__ import annotations
 
+import os
 import pickle
 import time
 from dataclasses import dataclass, field
@@ -204,6 +205,11 @@ class PrefillWorker(_Worker):
             ev = self.conn.push(s.block_ids[:nblk], job.blocks[:nblk], job.k)
             self.pending.append((ev, job, s.output_ids[-1], _advance_rng(s.rng_state, s.params)))
 
+    def progress(self) -> str:
+        return (f"jobs seen {self.next_job}/{self.total}, prefilling {len(self.jobs)}, pushes in flight "
+                f"{len(self.pending)}, engine busy {self.engine.has_unfinished()}, "
+                f"free blocks {self.engine.allocator.num_free()}")
+
     def poll_and_step(self) -> bool:
         new = []
         total = self.total
@@ -278,6 +284,10 @@ class DecodeWorker(_Worker):
             self.engine.step()
         return bool(self.waiting) or self.engine.has_unfinished()
 
+    def progress(self) -> str:
+        return (f"submitted {len(self.submitted)}, waiting for KV {len(self.waiting)}, "
+                f"engine busy {self.engine.has_unfinished()}, free blocks {self.engine.allocator.num_free()}")
+
     def stop(self) -> None:
         """Tell the prefill side that no job beyond those submitted will come."""
         if self.is_leader:
@@ -321,12 +331,18 @@ class Disaggregated:
                 w.submit(f"{ns}-{i}", p, params)
             w.stop()
         t0 = time.perf_counter()
+        debug = os.environ.get("KAPSL_PD_DEBUG", "0") == "1"
+        last_log = t0
         while w.poll_and_step():
             if health is not None:
                 health.check()
-            if time.perf_counter() - t0 > timeout_s:
+            now = time.perf_counter()
+            if debug and now - last_log > 5.0:
+                print(f"[pd] {self.role} rank {self.rank} t={now - t0:.1f}s {w.progress()}", flush=True)
+                last_log = now
+            if now - t0 > timeout_s:
                 raise TimeoutError(f"{self.role} rank {self.rank}: disaggregated serving did not finish "
-                                   f"in {timeout_s} s")
+                                   f"in {timeout_s} s ({w.progress()})")
         self.engine.kv_export = None
         if self.role == "prefill":
             return None, None
