@@ -289,7 +289,10 @@ def gguf_tokenizer(path: str):
     if not toks:
         return None
     return GGUFTokenizer(toks, _field(r, "tokenizer.ggml.scores"), _field(r, "tokenizer.ggml.token_type"),
-                         _field(r, "tokenizer.ggml.bos_token_id", 1), _field(r, "tokenizer.ggml.eos_token_id", 2))
+                         _field(r, "tokenizer.ggml.bos_token_id", 1), _field(r, "tokenizer.ggml.eos_token_id", 2),
+                         model=str(_field(r, "tokenizer.ggml.model", "llama")),
+                         merges=_field(r, "tokenizer.ggml.merges"), pre=_field(r, "tokenizer.ggml.pre"),
+                         add_space_prefix=bool(_field(r, "tokenizer.ggml.add_space_prefix", True)))
 
 
 def load_gguf_model(path: str, device, tp: int = 1, rank: int = 0):
