@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 #include <condition_variable>
 #include <functional>
 #include <mutex>
@@ -236,6 +237,97 @@ void silu_mul(const float* x, float* out, int64_t T, int64_t F) {
     float* o = out + t * F;
 #pragma omp simd
     for (int64_t j = j0; j < j1; ++j) o[j] = g[j] / (1.f + std::exp(-g[j])) * u[j];
+  });
+}
+
+// ------------------------------------------------------------------ Q4_K
+namespace {
+
+constexpr int64_t kQK = 256, kQ4KBytes = 144;
+
+// IEEE half -> float (exact; subnormals, infinities and NaN included).
+inline float half_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1Fu, man = h & 0x3FFu;
+  uint32_t bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {  // subnormal: normalise
+      int e = -1;
+      do {
+        ++e;
+        man <<= 1;
+      } while (!(man & 0x400u));
+      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3FFu) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7F800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 127 - 15) << 23) | (man << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, 4);
+  return f;
+}
+
+// Dequantize one 256-value block into out[0..255].
+inline void q4k_block(const uint8_t* b, float* out) {
+  uint16_t dh, mh;
+  std::memcpy(&dh, b, 2);
+  std::memcpy(&mh, b + 2, 2);
+  const float d = half_to_float(dh), dmin = half_to_float(mh);
+  const uint8_t* sc = b + 4;
+  const uint8_t* qs = b + 16;
+  for (int j = 0; j < 8; ++j) {
+    uint8_t s, m;
+    if (j < 4) {
+      s = sc[j] & 63;
+      m = sc[j + 4] & 63;
+    } else {
+      s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+      m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+    }
+    const float ds = d * s, mm = dmin * m;
+    const uint8_t* q = qs + (j / 2) * 32;
+    const int shift = (j & 1) * 4;
+    float* o = out + j * 32;
+#pragma omp simd
+    for (int i = 0; i < 32; ++i) o[i] = ds * (float)((q[i] >> shift) & 0xF) - mm;
+  }
+}
+
+}  // namespace
+
+void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K) {
+  const int64_t nb = K / kQK;
+  parallel_for(n1 - n0, 8, [&](int64_t r) {
+    const uint8_t* row = w + (n0 + r) * nb * kQ4KBytes;
+    for (int64_t b = 0; b < nb; ++b) q4k_block(row + b * kQ4KBytes, out + r * K + b * kQK);
+  });
+}
+
+void q4k_matmul(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K) {
+  const int64_t nb = K / kQK;
+  parallel_for(N, 16, [&](int64_t n) {
+    float buf[kQK];
+    float acc[16];
+    const uint8_t* row = w + n * nb * kQ4KBytes;
+    for (int64_t t0 = 0; t0 < T; t0 += 16) {  // up to 16 activation rows share each dequantized block
+      const int64_t tn = std::min<int64_t>(16, T - t0);
+      for (int64_t t = 0; t < tn; ++t) acc[t] = 0.f;
+      for (int64_t b = 0; b < nb; ++b) {
+        q4k_block(row + b * kQ4KBytes, buf);
+        for (int64_t t = 0; t < tn; ++t) {
+          const float* xr = x + (t0 + t) * K + b * kQK;
+          float s = 0.f;
+#pragma omp simd reduction(+ : s)
+          for (int i = 0; i < kQK; ++i) s += xr[i] * buf[i];
+          acc[t] += s;
+        }
+      }
+      for (int64_t t = 0; t < tn; ++t) y[(t0 + t) * N + n] = acc[t];
+    }
   });
 }
 

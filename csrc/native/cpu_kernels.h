@@ -30,5 +30,13 @@ void paged_attention(const float* q, const float* k_cache, const float* v_cache,
 // out[t, j] = silu(x[t, j]) * x[t, F + j]
 void silu_mul(const float* x, float* out, int64_t T, int64_t F);
 
+// GGUF Q4_K weights kept quantized: w holds N rows of K / 256 blocks of 144
+// bytes (f16 d, f16 dmin, 12 bytes of 6-bit scale/min pairs, 128 bytes of
+// 4-bit quants; v = d * sc * q - dmin * m).
+// y[t, n] = sum_k x[t, k] * w[n, k]            (x [T, K], y [T, N] fp32)
+void q4k_matmul(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K);
+// out[(n - n0), k] = w[n, k] for rows n0 <= n < n1 (fp32)
+void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K);
+
 }  // namespace cpu
 }  // namespace kapsl

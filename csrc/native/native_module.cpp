@@ -110,6 +110,21 @@ void cpu_module(py::module_& m) {
                                 bt.shape(1), row0.size(), q.shape(1), kc.shape(1), kc.shape(2), q.shape(2), scale,
                                 out.mutable_data());
   });
+  using U8 = py::array_t<uint8_t, py::array::c_style>;
+  c.def("q4k_matmul", [](F32 x, U8 w, F32 y) {
+    need(x.ndim() == 2 && w.ndim() == 2 && y.ndim() == 2, "q4k_matmul: x [T, K], w [N, K/256*144], y [T, N]");
+    const int64_t T = x.shape(0), K = x.shape(1), N = w.shape(0);
+    need(K % 256 == 0 && w.shape(1) == K / 256 * 144 && y.shape(0) == T && y.shape(1) == N, "q4k_matmul: shapes");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::q4k_matmul(x.data(), w.data(), y.mutable_data(), T, N, K);
+  });
+  c.def("q4k_dequant_rows", [](U8 w, int64_t n0, int64_t n1, F32 out) {
+    need(w.ndim() == 2 && 0 <= n0 && n0 <= n1 && n1 <= w.shape(0), "q4k_dequant_rows: rows");
+    const int64_t K = w.shape(1) / 144 * 256;
+    need(out.ndim() == 2 && out.shape(0) == n1 - n0 && out.shape(1) == K, "q4k_dequant_rows: out [n1 - n0, K]");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::q4k_dequant_rows(w.data(), out.mutable_data(), n0, n1, K);
+  });
   c.def("silu_mul", [](F32 x, F32 out) {
     need(x.ndim() == 2 && x.shape(1) % 2 == 0 && out.size() == x.size() / 2, "silu_mul: x [T, 2F], out [T, F]");
     py::gil_scoped_release nogil;

@@ -235,33 +235,68 @@ def _gguf_rope_scaling(reader, arch: str) -> Optional[dict]:
     return rs
 
 
-def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
-    """Yields the runtime's full-tensor stream (see models.llama.random_full_weights)."""
+def _q4k_rows(t):
+    """A 2-D Q4_K tensor as kept-quantized rows (None for other types)."""
+    from gguf import GGMLQuantizationType as Q
+
+    from ..quantization import Q4KRows
+
+    if t.tensor_type != Q.Q4_K or len(t.shape) != 2:
+        return None
+    n, k = int(t.shape[1]), int(t.shape[0])
+    return Q4KRows(np.asarray(t.data).view(np.uint8).reshape(n, k // QK_K * Q4_K_BYTES), k)
+
+
+def _row_perm(rows: int, n_head: int) -> np.ndarray:
+    """Row order of _permute_back as an index array."""
+    return _permute_back(np.arange(rows)[:, None], n_head)[:, 0]
+
+
+def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None, keep_q4k: bool = False):
+    """Yields the runtime's full-tensor stream (see models.llama.random_full_weights).
+    ``keep_q4k``: 2-D Q4_K projection weights stay quantized (``Q4KRows``) for the CPU backend."""
     from gguf import GGUFReader
 
     r = GGUFReader(path)
     cfg = cfg or gguf_config(r)
     T = {t.name: t for t in r.tensors}
-    get = lambda n: torch.from_numpy(np.ascontiguousarray(tensor_to_numpy(T[n])))
+
+    def get(n):
+        if keep_q4k:
+            q = _q4k_rows(T[n])
+            if q is not None:
+                return q
+        return torch.from_numpy(np.ascontiguousarray(tensor_to_numpy(T[n])))
+
+    def permute(w, n_head):
+        if isinstance(w, torch.Tensor):
+            return torch.from_numpy(np.ascontiguousarray(_permute_back(w.numpy(), n_head)))
+        return w.take(_row_perm(w.n, n_head))
+
+    def split(w, sizes):
+        if isinstance(w, torch.Tensor):
+            return torch.split(w, sizes, 0)
+        out, a = [], 0
+        for n in sizes:
+            out.append(w.rows(a, a + n))
+            a += n
+        return out
+
     permuted = _field(r, "general.architecture", "llama") == "llama"
-    emb = get("token_embd.weight")
+    emb = torch.from_numpy(np.ascontiguousarray(tensor_to_numpy(T["token_embd.weight"])))
     yield "embed", emb
     yield "lm_head", get("output.weight") if "output.weight" in T else emb
     yield "final_norm", get("output_norm.weight")
     for i in range(cfg.num_layers):
         b = f"blk.{i}."
         if b + "attn_qkv.weight" in T:  # Phi-3: fused [q; k; v]
-            qkv = tensor_to_numpy(T[b + "attn_qkv.weight"])
-            q, k, v = np.split(qkv, [cfg.q_size, cfg.q_size + cfg.kv_size], 0)
+            q, k, v = split(get(b + "attn_qkv.weight"), [cfg.q_size, cfg.kv_size, cfg.kv_size])
         else:
-            q = tensor_to_numpy(T[b + "attn_q.weight"])
-            k = tensor_to_numpy(T[b + "attn_k.weight"])
-            v = tensor_to_numpy(T[b + "attn_v.weight"])
+            q, k, v = get(b + "attn_q.weight"), get(b + "attn_k.weight"), get(b + "attn_v.weight")
         if permuted:
-            q = _permute_back(q, cfg.num_heads)
-            k = _permute_back(k, cfg.num_kv_heads)
-        full = {"q": torch.from_numpy(np.ascontiguousarray(q)), "k": torch.from_numpy(np.ascontiguousarray(k)),
-                "v": torch.from_numpy(np.ascontiguousarray(v)), "o": get(b + "attn_output.weight"),
+            q = permute(q, cfg.num_heads)
+            k = permute(k, cfg.num_kv_heads)
+        full = {"q": q, "k": k, "v": v, "o": get(b + "attn_output.weight"),
                 "in_norm": get(b + "attn_norm.weight"), "post_norm": get(b + "ffn_norm.weight"),
                 "down": get(b + "ffn_down.weight")}
         if b + "post_attention_norm.weight" in T:  # Gemma 2 sandwich norms
@@ -270,7 +305,8 @@ def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None):
         if b + "ffn_gate.weight" in T:
             full["gate"], full["up"] = get(b + "ffn_gate.weight"), get(b + "ffn_up.weight")
         else:  # Phi-3: ffn_up holds [gate; up]
-            full["gate"], full["up"] = torch.chunk(get(b + "ffn_up.weight"), 2, 0)
+            gu = get(b + "ffn_up.weight")
+            full["gate"], full["up"] = split(gu, [gu.shape[0] // 2, gu.shape[0] // 2])
         if b + "attn_q_norm.weight" in T:  # Qwen3
             full["q_norm"], full["k_norm"] = get(b + "attn_q_norm.weight"), get(b + "attn_k_norm.weight")
         if b + "attn_q.bias" in T:
@@ -304,7 +340,9 @@ def load_gguf_model(path: str, device, tp: int = 1, rank: int = 0):
     cfg = gguf_config(GGUFReader(path))
     tok = gguf_tokenizer(path)
     dev = torch.device(device)
-    stream = iter_gguf_full(path, cfg)
+    # on the CPU backend Q4_K projections stay quantized (KAPSL_CPU_Q4K=0 dequantizes them at load)
+    keep = dev.type == "cpu" and os.environ.get("KAPSL_CPU_Q4K", "1") == "1"
+    stream = iter_gguf_full(path, cfg, keep_q4k=keep)
     if dev.type == "cpu":
         items = list(stream)
         d = dict((k, v) for k, v in items if k != "layer")

@@ -20,13 +20,29 @@ import numpy as np
 import torch
 
 from ..ops import reference as ref
+from ..quantization import Q4KRows
 from .config import ModelConfig
+
+
+def _mm(x: torch.Tensor, w) -> torch.Tensor:
+    """x @ w.T for an fp32 weight or kept-quantized Q4_K rows."""
+    return w.matmul(x) if isinstance(w, Q4KRows) else x @ w.T
+
+
+def _cat_rows(parts: list):
+    """Row-concatenation of weights (quantized rows stay quantized when all parts are)."""
+    if all(isinstance(p, Q4KRows) for p in parts):
+        return Q4KRows.cat(parts)
+    return torch.cat([p.dequantize() if isinstance(p, Q4KRows) else p for p in parts], 0)
 
 
 class CPUCausalLM:
     def __init__(self, cfg: ModelConfig, embed: torch.Tensor, lm_head: torch.Tensor, final_norm: torch.Tensor,
                  layers: list):
-        f = lambda t: None if t is None else t.detach().to("cpu", torch.float32).contiguous()
+        def f(t):
+            if t is None or isinstance(t, Q4KRows):
+                return t
+            return t.detach().to("cpu", torch.float32).contiguous()
         self.cfg = cfg
         self.embed = f(embed)
         self.lm_head = f(lm_head)
@@ -34,10 +50,10 @@ class CPUCausalLM:
         self.layers = []
         for L in layers:
             d = {k: f(v) for k, v in L.items()}
-            d["qkv"] = torch.cat([d["q"], d["k"], d["v"]], 0)
+            d["qkv"] = _cat_rows([d["q"], d["k"], d["v"]])
             d["qkv_b"] = torch.cat([d["q_b"], d["k_b"], d["v_b"]]) if d.get("q_b") is not None else None
             if not cfg.is_moe:
-                d["gate_up"] = torch.cat([d["gate"], d["up"]], 0)
+                d["gate_up"] = _cat_rows([d["gate"], d["up"]])
             self.layers.append(d)
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, scaling=cfg.rope_scaling)
         self.hq, self.hkv, self.D = cfg.num_heads, cfg.num_kv_heads, cfg.head_dim
@@ -87,7 +103,7 @@ class CPUCausalLM:
         off = (slots % bs).long()
         for li, L in enumerate(self.layers):
             x, _ = ref.rmsnorm(h, L["in_norm"], cfg.rms_eps)
-            qkv = x @ L["qkv"].T
+            qkv = _mm(x, L["qkv"])
             if L["qkv_b"] is not None:
                 qkv = qkv + L["qkv_b"]
             q, k = qkv[:, :hq * D].view(T, hq, D), qkv[:, hq * D:(hq + hkv) * D].view(T, hkv, D)
@@ -107,7 +123,7 @@ class CPUCausalLM:
                 vv = ref.gather_paged(vc, blocks, ctx).float()
                 attn[r0:r0 + n] = ref.attention(q[r0:r0 + n], kk, vv, self.scale, ctx - n, cfg.attn_softcap,
                                                 win).reshape(n, hq * D)
-            o = attn @ L["o"].T
+            o = _mm(attn, L["o"])
             if "attn_out_norm" in L:  # Gemma 2: norm of the attention output before the residual add
                 o, _ = ref.rmsnorm(o, L["attn_out_norm"], cfg.rms_eps)
             h = h + o
@@ -115,8 +131,8 @@ class CPUCausalLM:
             if cfg.is_moe:
                 h = h + self._moe(x, L)
             else:
-                gu = x @ L["gate_up"].T
-                y = (ref.gelu_tanh_mul(gu) if cfg.act == "gelu_tanh" else ref.silu_mul(gu)) @ L["down"].T
+                gu = _mm(x, L["gate_up"])
+                y = _mm(ref.gelu_tanh_mul(gu) if cfg.act == "gelu_tanh" else ref.silu_mul(gu), L["down"])
                 if "mlp_out_norm" in L:
                     y, _ = ref.rmsnorm(y, L["mlp_out_norm"], cfg.rms_eps)
                 h = h + y
@@ -124,7 +140,7 @@ class CPUCausalLM:
             self.stage.send_hidden(h)
             return None
         xs, _ = ref.rmsnorm(h[logits_rows], self.final_norm, cfg.rms_eps)
-        logits = xs @ self.lm_head.T
+        logits = _mm(xs, self.lm_head)
         if cfg.final_softcap > 0:
             logits = torch.tanh(logits / cfg.final_softcap) * cfg.final_softcap
         return logits
@@ -150,7 +166,7 @@ class CPUCausalLM:
         attn = torch.empty(T, hq, D)
         for li, L in enumerate(self.layers):
             k_.rmsnorm(h.numpy(), L["in_norm"].numpy(), x.numpy(), cfg.rms_eps)
-            qkv = x @ L["qkv"].T
+            qkv = _mm(x, L["qkv"])
             if L["qkv_b"] is not None:
                 qkv += L["qkv_b"]
             q = qkv[:, :hq * D].contiguous().view(T, hq, D)
@@ -165,21 +181,21 @@ class CPUCausalLM:
             kc, vc = k_caches[li], v_caches[li]
             k_.kv_write(kk.numpy(), vv.numpy(), sl, kc.numpy(), vc.numpy())
             k_.paged_attention(q.numpy(), kc.numpy(), vc.numpy(), row0, nq, ctx, bt, self.scale, attn.numpy())
-            h += attn.view(T, hq * D) @ L["o"].T
+            h += _mm(attn.view(T, hq * D), L["o"])
             k_.rmsnorm(h.numpy(), L["post_norm"].numpy(), x.numpy(), cfg.rms_eps)
             if cfg.is_moe:
                 h += self._moe(x, L)
             else:
-                gu = x @ L["gate_up"].T
+                gu = _mm(x, L["gate_up"])
                 act = torch.empty(T, gu.shape[1] // 2)
                 k_.silu_mul(gu.numpy(), act.numpy())
-                h += act @ L["down"].T
+                h += _mm(act, L["down"])
         if self.stage is not None and not self.stage.last:
             self.stage.send_hidden(h)
             return None
         xs = h[logits_rows].contiguous()
         k_.rmsnorm(xs.numpy(), self.final_norm.numpy(), xs.numpy(), cfg.rms_eps)
-        return xs @ self.lm_head.T
+        return _mm(xs, self.lm_head)
 
     @property
     def layer_ids(self) -> list:

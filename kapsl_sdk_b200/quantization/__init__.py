@@ -94,3 +94,65 @@ def dequantize_q4_k(raw: torch.Tensor, n: int, k: int) -> torch.Tensor:
     out = torch.empty(n, k, dtype=torch.bfloat16, device=raw.device)
     cuda_ops().q4k_dequant(raw.contiguous(), out)
     return out
+
+
+class Q4KRows:
+    """GGUF Q4_K weight rows kept quantized for the CPU backend: ``raw`` is
+    uint8 [N, K / 256 * 144] (one row per output feature), multiplied by the C++
+    kernel (``_native.cpu.q4k_matmul``) for short activations and by row
+    blocks dequantized into a BLAS matmul for long ones."""
+
+    BLOCK = 144
+
+    def __init__(self, raw, k: int):
+        import numpy as np
+
+        self.raw = np.ascontiguousarray(raw, dtype=np.uint8)
+        self.k = int(k)
+        if self.raw.ndim != 2 or self.k % 256 or self.raw.shape[1] != self.k // 256 * self.BLOCK:
+            raise ValueError("Q4_K rows: raw must be [N, K / 256 * 144] with K a multiple of 256")
+
+    @property
+    def n(self) -> int:
+        return self.raw.shape[0]
+
+    @property
+    def shape(self) -> tuple:
+        return (self.n, self.k)
+
+    def rows(self, a: int, b: int) -> "Q4KRows":
+        return Q4KRows(self.raw[a:b], self.k)
+
+    def take(self, idx) -> "Q4KRows":
+        return Q4KRows(self.raw[idx], self.k)
+
+    @staticmethod
+    def cat(parts: list) -> "Q4KRows":
+        import numpy as np
+
+        return Q4KRows(np.concatenate([p.raw for p in parts], 0), parts[0].k)
+
+    def dequantize(self) -> torch.Tensor:
+        from .._ext import native
+
+        out = torch.empty(self.n, self.k, dtype=torch.float32)
+        native().cpu.q4k_dequant_rows(self.raw, 0, self.n, out.numpy())
+        return out
+
+    def matmul(self, x: torch.Tensor, row_block: int = 2048) -> torch.Tensor:
+        """x [T, K] fp32 -> x @ W.T [T, N]."""
+        from .._ext import native
+
+        cpu = native().cpu
+        x = x.float().contiguous()
+        y = torch.empty(x.shape[0], self.n, dtype=torch.float32)
+        if x.shape[0] <= 16:
+            cpu.q4k_matmul(x.numpy(), self.raw, y.numpy())
+            return y
+        buf = torch.empty(min(row_block, self.n), self.k, dtype=torch.float32)
+        for n0 in range(0, self.n, row_block):
+            n1 = min(self.n, n0 + row_block)
+            w = buf[:n1 - n0]
+            cpu.q4k_dequant_rows(self.raw, n0, n1, w.numpy())
+            y[:, n0:n1] = x @ w.T
+        return y

@@ -1,0 +1,53 @@
+"""GGUF Q4_K weights kept quantized on the CPU backend: the C++ kernel and the
+row-block path match a dense matmul with the dequantized weights, and an
+engine on a Q4_K GGUF serves the same tokens quantized as dequantized."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from kapsl_sdk_b200.loaders.gguf import dequant_q4_k, quantize_q4_k
+from kapsl_sdk_b200.quantization import Q4KRows
+
+
+@pytest.mark.parametrize("T", [1, 5, 16, 17, 40])
+def test_q4k_rows_matmul_matches_dequantized(T):
+    rng = np.random.default_rng(T)
+    N, K = 96, 512
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.1
+    raw = quantize_q4_k(w.reshape(-1)).reshape(N, -1)
+    q = Q4KRows(raw, K)
+    dense = torch.from_numpy(dequant_q4_k(raw.reshape(-1)).reshape(N, K))
+    assert torch.equal(q.dequantize(), dense)
+    x = torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32))
+    torch.testing.assert_close(q.matmul(x, row_block=32), x @ dense.T, rtol=1e-4, atol=1e-4)
+    sub = q.take(np.array([5, 1, 7])).rows(1, 3)
+    assert torch.equal(sub.dequantize(), dense[[1, 7]])
+
+
+def test_engine_on_q4k_gguf_keeps_weights_quantized(tmp_path, monkeypatch):
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.loaders.gguf import load_gguf_model, write_gguf_model
+    from kapsl_sdk_b200.models.config import ModelConfig
+    from kapsl_sdk_b200.models.llama import random_full_weights
+
+    cfg = ModelConfig(name="q", arch="llama", vocab_size=300, hidden_size=256, intermediate_size=512, num_layers=2,
+                      num_heads=4, num_kv_heads=2, head_dim=64, max_position=256, bos_token_id=None,
+                      eos_token_id=None)
+    p = str(tmp_path / "m.gguf")
+    write_gguf_model(p, cfg, random_full_weights(cfg, torch.device("cpu"), seed=1, std=0.05), quant="q4_k")
+    c_q, m_q, _ = load_gguf_model(p, "cpu")
+    assert isinstance(m_q.layers[0]["qkv"], Q4KRows) and isinstance(m_q.layers[0]["down"], Q4KRows)
+    monkeypatch.setenv("KAPSL_CPU_Q4K", "0")
+    c_d, m_d, _ = load_gguf_model(p, "cpu")
+    assert isinstance(m_d.layers[0]["qkv"], torch.Tensor)
+    torch.testing.assert_close(m_q.layers[0]["qkv"].dequantize(), m_d.layers[0]["qkv"])
+    prompt = list(range(11, 60))
+    outs = []
+    for c, m in ((c_q, m_q), (c_d, m_d)):
+        eng = LLMEngine(c, weights=m, device="cpu", engine_cfg=EngineConfig(
+            max_num_seqs=2, max_num_batched_tokens=32, max_model_len=128, num_blocks=32), seed=0)
+        outs.append(eng.generate([prompt], SamplingParams.greedy(8, ignore_eos=True))[0])
+    assert outs[0] == outs[1]
