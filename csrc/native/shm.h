@@ -16,12 +16,21 @@
 // CAS on head_reserved, write, then publish in reservation order with a CAS on
 // head_committed.  Consumers copy the slot and then CAS the tail (the copy is
 // taken before the slot is released, so a fast producer cannot overwrite it).
+// The indices wrap, so a thread stalled between reading an index and its CAS
+// for a full turn of the ring would succeed on a stale value (ABA).  To rule
+// that out, this library's producers and consumers each take a side lock
+// first: 8-byte words at byte 8 of the head_reserved slot (producers) and of
+// the tail slot (consumers), bytes that the index layout leaves unused.  A
+// lock word holds the holder's CLOCK_MONOTONIC time in ns (shifted left 10,
+// low bits a per-thread tag); a holder older than one second is presumed dead
+// and its lock is taken over.
 #pragma once
 
 #include <stdint.h>
 
 #include <atomic>
 #include <chrono>
+#include <functional>
 #include <memory>
 #include <map>
 #include <mutex>
@@ -111,15 +120,19 @@ class Region {
 template <class T>
 class Ring {
  public:
-  static_assert(sizeof(T) >= sizeof(std::atomic<size_t>), "slot must hold an atomic index");
+  static_assert(sizeof(T) >= 2 * sizeof(std::atomic<size_t>), "slot must hold an index and a lock word");
   Ring(uint8_t* at, size_t capacity_arg, bool init) : slots_(reinterpret_cast<T*>(at)), cap_(capacity_arg - 3) {
     if (init) {
       new (&idx(0)) std::atomic<size_t>(0);
       new (&idx(1)) std::atomic<size_t>(0);
       new (&idx(2)) std::atomic<size_t>(0);
+      new (&lock_word(0)) std::atomic<uint64_t>(0);
+      new (&lock_word(2)) std::atomic<uint64_t>(0);
     }
   }
   bool push(const T& item) {
+    SideLock g(lock_word(0));
+    if (!g.held) return false;  // another producer holds the lock; the caller retries like on a full ring
     for (;;) {
       size_t reserved = idx(0).load(std::memory_order_relaxed);
       size_t next = (reserved + 1) % cap_;
@@ -137,6 +150,8 @@ class Ring {
     }
   }
   std::optional<T> pop() {
+    SideLock g(lock_word(2));
+    if (!g.held) return std::nullopt;
     for (;;) {
       size_t tail = idx(2).load(std::memory_order_relaxed);
       size_t committed = idx(1).load(std::memory_order_acquire);
@@ -153,7 +168,45 @@ class Ring {
   size_t capacity() const { return cap_ - 1; }
 
  private:
+  // Held for a slot copy and two index updates.  Waits up to ~2 ms for the
+  // lock (then reports it not held, which callers treat like an empty or full
+  // ring and retry); takes over a lock whose holder stamped it more than one
+  // second ago.
+  struct SideLock {
+    std::atomic<uint64_t>& w;
+    uint64_t token = 0;
+    bool held = false;
+    explicit SideLock(std::atomic<uint64_t>& word) : w(word) {
+      static thread_local const uint64_t tag =
+          (std::hash<std::thread::id>{}(std::this_thread::get_id()) & 1023) | 1;
+      for (unsigned spins = 0; spins < 20000; ++spins) {
+        const uint64_t now = now_ns();
+        token = (now << 10) | tag;
+        uint64_t cur = w.load(std::memory_order_relaxed);
+        if (cur == 0 || (now > (cur >> 10) && now - (cur >> 10) > 1000000000ull)) {
+          if (w.compare_exchange_strong(cur, token, std::memory_order_acquire, std::memory_order_relaxed)) {
+            held = true;
+            return;
+          }
+        }
+        if ((spins & 15) == 15) std::this_thread::yield();
+      }
+    }
+    ~SideLock() {
+      if (!held) return;
+      uint64_t expect = token;
+      w.compare_exchange_strong(expect, 0, std::memory_order_release, std::memory_order_relaxed);
+    }
+    static uint64_t now_ns() {
+      return (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                 std::chrono::steady_clock::now().time_since_epoch())
+          .count();
+    }
+  };
   std::atomic<size_t>& idx(int i) const { return *reinterpret_cast<std::atomic<size_t>*>(&slots_[i]); }
+  std::atomic<uint64_t>& lock_word(int i) const {
+    return *reinterpret_cast<std::atomic<uint64_t>*>(reinterpret_cast<uint8_t*>(&slots_[i]) + 8);
+  }
   T* slots_;
   size_t cap_;
 };
