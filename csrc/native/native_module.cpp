@@ -9,6 +9,7 @@
 #include "cpu_kernels.h"
 #include "server.h"
 #include "shm.h"
+#include "text_index.h"
 #include "wasm.h"
 #include "wire.h"
 
@@ -152,6 +153,64 @@ PYBIND11_MODULE(_native, m) {
       PyErr_SetString(PyExc_RuntimeError, (std::string("wasm trap: ") + e.what()).c_str());
     }
   });
+
+  // ---- text indexing: suffix arrays and Unigram lattices (tokenizer training)
+  auto tx = m.def_submodule("text", "suffix arrays, repeated substrings and Unigram lattices");
+  tx.def("suffix_array", [](const std::u32string& s) {
+    return text::suffix_array(std::vector<int32_t>(s.begin(), s.end()));
+  }, "Start offsets of the suffixes of a string (code points) in lexicographic order");
+  tx.def("lcp_array", [](const std::u32string& s) {
+    const std::vector<int32_t> v(s.begin(), s.end());
+    return text::lcp_array(v, text::suffix_array(v));
+  });
+  tx.def("repeated_substrings", [](const std::u32string& s) {
+    std::vector<text::SubstringNode> nodes;
+    {
+      py::gil_scoped_release nogil;
+      nodes = text::repeated_substrings(std::vector<int32_t>(s.begin(), s.end()));
+    }
+    py::list out;
+    for (const auto& nd : nodes) out.append(py::make_tuple(s.substr(nd.offset, nd.length), nd.freq));
+    return out;
+  }, "Internal nodes of the suffix tree as (substring, occurrences), bottom-up, root (\"\") last");
+  tx.def("top_repeated_substrings", [](const std::u32string& s, int32_t max_len, size_t limit,
+                                      const std::u32string& banned, const std::u32string& not_inner) {
+    std::vector<text::SubstringNode> nodes;
+    {
+      py::gil_scoped_release nogil;
+      nodes = text::top_repeated_substrings(std::vector<int32_t>(s.begin(), s.end()), max_len, limit,
+                                            std::vector<int32_t>(banned.begin(), banned.end()),
+                                            std::vector<int32_t>(not_inner.begin(), not_inner.end()));
+    }
+    py::list out;
+    for (const auto& nd : nodes) out.append(py::make_tuple(s.substr(nd.offset, nd.length), nd.freq));
+    return out;
+  }, py::arg("text"), py::arg("max_len"), py::arg("limit"), py::arg("banned") = std::u32string(),
+     py::arg("not_inner") = std::u32string(),
+     "Repeated substrings of 2..max_len code points with the largest occurrences * length, best first");
+  py::class_<text::UnigramModel>(tx, "UnigramModel")
+      .def(py::init<const std::vector<std::u32string>&, const std::vector<double>&, int>(), py::arg("pieces"),
+           py::arg("scores"), py::arg("unk_id") = -1)
+      .def("encode", &text::UnigramModel::encode, py::call_guard<py::gil_scoped_release>())
+      .def("encode_batch", [](const text::UnigramModel& u, const std::vector<std::u32string>& texts) {
+        std::vector<std::vector<int32_t>> out(texts.size());
+        py::gil_scoped_release nogil;
+        for (size_t i = 0; i < texts.size(); ++i) out[i] = u.encode(texts[i]);
+        return out;
+      })
+      .def("expected_counts", [](const text::UnigramModel& u, const std::vector<std::u32string>& words,
+                                 const std::vector<double>& freqs) {
+        std::vector<double> counts;
+        double ll;
+        {
+          py::gil_scoped_release nogil;
+          ll = u.expected_counts(words, freqs, counts);
+        }
+        return py::make_tuple(counts, ll);
+      }, "(expected count of every piece, sum of freq * log Z) over the words")
+      .def("alternative", &text::UnigramModel::alternative)
+      .def("alternative_scores", &text::UnigramModel::alternative_scores, py::call_guard<py::gil_scoped_release>())
+      .def("__len__", &text::UnigramModel::size);
 
   // ---- WebAssembly connectors (WASI preview1)
   m.def("wasm_run",
