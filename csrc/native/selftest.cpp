@@ -26,6 +26,7 @@
 #include "block_alloc.h"
 #include "cpu_kernels.h"
 #include "shm.h"
+#include "text_index.h"
 #include "wasm.h"
 #include "wire.h"
 
@@ -374,11 +375,63 @@ static void test_wasm() {
   if (getenv("SELFTEST_VERBOSE")) std::printf("wasm fuzz: ran %d, rejected %d, trapped %d, other %d\n", ran, rejected, trapped, other);
 }
 
+// Suffix arrays against a plain sort, repeated substrings against their
+// definition, and the Unigram lattice on random inputs (out-of-bounds reads
+// show up under the address sanitizer).
+static void test_text_index() {
+  uint64_t seed = 0x9E3779B97F4A7C15ull;
+  auto rnd = [&]() {
+    seed ^= seed << 13;
+    seed ^= seed >> 7;
+    seed ^= seed << 17;
+    return seed;
+  };
+  for (int trial = 0; trial < 300; ++trial) {
+    const int n = (int)(rnd() % 200), k = 1 + (int)(rnd() % 5);
+    std::vector<int32_t> s(n);
+    for (auto& c : s) c = (int32_t)(rnd() % k) * 1000003;  // sparse symbol values
+    const std::vector<int32_t> sa = text::suffix_array(s);
+    std::vector<int32_t> ref(n);
+    for (int i = 0; i < n; ++i) ref[i] = i;
+    std::sort(ref.begin(), ref.end(), [&](int a, int b) {
+      return std::lexicographical_compare(s.begin() + a, s.end(), s.begin() + b, s.end());
+    });
+    CHECK(sa == ref, "suffix array differs from a plain sort (n=%d)", n);
+    const auto nodes = text::repeated_substrings(s);
+    for (const auto& nd : nodes) {
+      int count = 0;
+      for (int i = 0; i + nd.length <= n; ++i)
+        count += std::equal(s.begin() + nd.offset, s.begin() + nd.offset + nd.length, s.begin() + i);
+      CHECK(count == nd.freq || nd.length == 0, "substring count %d != %d", count, nd.freq);
+    }
+    std::vector<std::u32string> pieces{U"a", U"b", U"c"};
+    std::vector<double> scores{-1.0, -2.0, -3.0};
+    for (int p = 0; p < 10; ++p) {
+      std::u32string t;
+      for (int j = 0, len = 2 + (int)(rnd() % 4); j < len; ++j) t.push_back(U'a' + (char32_t)(rnd() % 4));
+      pieces.push_back(t);
+      scores.push_back(-(double)(rnd() % 100) / 10.0);
+    }
+    pieces.push_back(U"<unk>");
+    scores.push_back(0.0);
+    text::UnigramModel m(pieces, scores, (int)pieces.size() - 1);
+    std::u32string w;
+    for (int j = 0, len = (int)(rnd() % 30); j < len; ++j) w.push_back(U'a' + (char32_t)(rnd() % 4));
+    const auto ids = m.encode(w);
+    size_t covered = 0;
+    for (int32_t id : ids) covered += id == (int32_t)pieces.size() - 1 ? 1 : pieces[id].size();
+    CHECK(covered == w.size(), "segmentation covers %zu of %zu", covered, w.size());
+    std::vector<double> counts;
+    m.expected_counts({w, w + U"ab"}, {1.0, 2.0}, counts);
+    (void)m.alternative_scores();
+  }
+}
+
 int main(int argc, char** argv) {
   const std::pair<const char*, void (*)()> tests[] = {
       {"ring_mpmc", test_ring_mpmc},         {"ring_repush", test_ring_repush}, {"model_pools", test_model_pools},
       {"shared_leases", test_shared_leases}, {"block_allocator", test_block_allocator}, {"wire", test_wire},
-      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm}};
+      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm},               {"text_index", test_text_index}};
   for (auto& [name, fn] : tests) {
     if (argc > 1 && std::string(argv[1]) != name) continue;
     const auto t0 = std::chrono::steady_clock::now();
