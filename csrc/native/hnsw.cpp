@@ -1,0 +1,213 @@
+#include "hnsw.h"
+
+#include <algorithm>
+#include <cmath>
+#include <mutex>
+#include <queue>
+#include <stdexcept>
+
+#ifdef __AVX2__
+#include <immintrin.h>
+#endif
+
+namespace kapsl {
+namespace rag {
+
+namespace {
+
+// Visited marks without clearing: a per-thread array of epochs.
+struct Visited {
+  std::vector<uint32_t> mark;
+  uint32_t epoch = 0;
+  void reset(size_t n) {
+    if (mark.size() < n) mark.resize(n, 0);
+    if (++epoch == 0) {  // wrapped: clear once
+      std::fill(mark.begin(), mark.end(), 0);
+      epoch = 1;
+    }
+  }
+  bool test_and_set(int32_t i) {
+    if (mark[i] == epoch) return true;
+    mark[i] = epoch;
+    return false;
+  }
+};
+
+Visited& visited() {
+  static thread_local Visited v;
+  return v;
+}
+
+}  // namespace
+
+Hnsw::Hnsw(int dim, int M, int ef_construction, uint64_t seed)
+    : dim_(dim), M_(M), M0_(2 * M), efc_(ef_construction), ml_(1.0 / std::log((double)std::max(M, 2))), rng_(seed) {
+  if (dim <= 0 || M < 2 || ef_construction < 1) throw std::invalid_argument("hnsw: bad dim / M / ef_construction");
+}
+
+float Hnsw::dist(const float* a, int32_t b) const {
+  const float* v = vec(b);
+  int i = 0;
+  float s = 0.f;
+#ifdef __AVX2__
+  __m256 acc0 = _mm256_setzero_ps(), acc1 = _mm256_setzero_ps();
+  for (; i + 16 <= dim_; i += 16) {
+    acc0 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i), _mm256_loadu_ps(v + i), acc0);
+    acc1 = _mm256_fmadd_ps(_mm256_loadu_ps(a + i + 8), _mm256_loadu_ps(v + i + 8), acc1);
+  }
+  const __m256 acc = _mm256_add_ps(acc0, acc1);
+  const __m128 h = _mm_add_ps(_mm256_castps256_ps128(acc), _mm256_extractf128_ps(acc, 1));
+  const __m128 h2 = _mm_add_ps(h, _mm_movehl_ps(h, h));
+  s = _mm_cvtss_f32(_mm_add_ss(h2, _mm_shuffle_ps(h2, h2, 1)));
+#endif
+  for (; i < dim_; ++i) s += a[i] * v[i];
+  return 1.f - s;
+}
+
+int32_t Hnsw::greedy(const float* q, int32_t ep, int level) const {
+  float d = dist(q, ep);
+  for (bool moved = true; moved;) {
+    moved = false;
+    for (int32_t n : links_[ep][level]) {
+      const float dn = dist(q, n);
+      if (dn < d) {
+        d = dn;
+        ep = n;
+        moved = true;
+      }
+    }
+  }
+  return ep;
+}
+
+std::vector<Hnsw::Cand> Hnsw::beam(const float* q, int32_t ep, int ef, int level) const {
+  Visited& vis = visited();
+  vis.reset(links_.size());
+  std::priority_queue<Cand, std::vector<Cand>, std::greater<Cand>> frontier;  // nearest on top
+  std::priority_queue<Cand> best;                                             // farthest on top
+  const float d0 = dist(q, ep);
+  vis.test_and_set(ep);
+  frontier.push({d0, ep});
+  best.push({d0, ep});
+  while (!frontier.empty()) {
+    const Cand c = frontier.top();
+    if (c.first > best.top().first && (int)best.size() >= ef) break;
+    frontier.pop();
+    for (int32_t n : links_[c.second][level]) {
+      if (vis.test_and_set(n)) continue;
+      const float dn = dist(q, n);
+      if ((int)best.size() < ef || dn < best.top().first) {
+        frontier.push({dn, n});
+        best.push({dn, n});
+        if ((int)best.size() > ef) best.pop();
+      }
+    }
+  }
+  std::vector<Cand> out(best.size());
+  for (size_t i = out.size(); i-- > 0;) {
+    out[i] = best.top();
+    best.pop();
+  }
+  return out;
+}
+
+std::vector<int32_t> Hnsw::select(std::vector<Cand> cand, int m) const {
+  std::sort(cand.begin(), cand.end());
+  std::vector<int32_t> kept;
+  for (const Cand& c : cand) {
+    if ((int)kept.size() >= m) break;
+    bool good = true;
+    for (int32_t r : kept)
+      if (dist(vec(c.second), r) < c.first) {
+        good = false;
+        break;
+      }
+    if (good) kept.push_back(c.second);
+  }
+  // fill up with the nearest discarded ones so sparse regions keep degree
+  for (const Cand& c : cand) {
+    if ((int)kept.size() >= m) break;
+    if (std::find(kept.begin(), kept.end(), c.second) == kept.end()) kept.push_back(c.second);
+  }
+  return kept;
+}
+
+int64_t Hnsw::add(const float* in) {
+  std::lock_guard<std::mutex> turn(turn_);
+  std::unique_lock<std::shared_mutex> lock(mu_);
+  const int32_t id = (int32_t)links_.size();
+  double norm = 0.0;
+  for (int i = 0; i < dim_; ++i) norm += (double)in[i] * in[i];
+  const float inv = norm > 0.0 ? (float)(1.0 / std::sqrt(norm)) : 0.f;
+  for (int i = 0; i < dim_; ++i) data_.push_back(in[i] * inv);
+  std::uniform_real_distribution<double> u(std::nextafter(0.0, 1.0), 1.0);
+  const int level = (int)std::floor(-std::log(u(rng_)) * ml_);
+  links_.emplace_back(level + 1);
+  removed_.push_back(0);
+  const float* q = vec(id);
+  if (entry_ < 0) {
+    entry_ = id;
+    top_ = level;
+    return id;
+  }
+  int32_t ep = entry_;
+  for (int l = top_; l > level; --l) ep = greedy(q, ep, l);
+  for (int l = std::min(level, top_); l >= 0; --l) {
+    std::vector<Cand> w = beam(q, ep, efc_, l);
+    const int mmax = l == 0 ? M0_ : M_;
+    links(id, l) = select(w, M_);
+    for (int32_t n : links_[id][l]) {
+      std::vector<int32_t>& nl = links(n, l);
+      nl.push_back(id);
+      if ((int)nl.size() > mmax) {
+        std::vector<Cand> c;
+        c.reserve(nl.size());
+        for (int32_t x : nl) c.push_back({dist(vec(n), x), x});
+        nl = select(std::move(c), mmax);
+      }
+    }
+    ep = w.front().second;
+  }
+  if (level > top_) {
+    top_ = level;
+    entry_ = id;
+  }
+  return id;
+}
+
+void Hnsw::remove(int64_t label) {
+  std::lock_guard<std::mutex> turn(turn_);
+  std::unique_lock<std::shared_mutex> lock(mu_);
+  if (label >= 0 && label < (int64_t)removed_.size()) removed_[label] = 1;
+}
+
+int64_t Hnsw::size() const {
+  std::shared_lock<std::shared_mutex> lock(mu_);
+  return (int64_t)links_.size();
+}
+
+std::vector<std::pair<float, int64_t>> Hnsw::search(const float* qin, int k, int ef, const uint8_t* allowed,
+                                                    int64_t allowed_len) const {
+  { std::lock_guard<std::mutex> turn(turn_); }  // wait behind a writer that is queued
+  std::shared_lock<std::shared_mutex> lock(mu_);
+  std::vector<std::pair<float, int64_t>> out;
+  if (entry_ < 0 || k <= 0) return out;
+  std::vector<float> q(qin, qin + dim_);
+  double norm = 0.0;
+  for (float v : q) norm += (double)v * v;
+  if (norm == 0.0) return out;
+  const float inv = (float)(1.0 / std::sqrt(norm));
+  for (float& v : q) v *= inv;
+  int32_t ep = entry_;
+  for (int l = top_; l > 0; --l) ep = greedy(q.data(), ep, l);
+  for (const Cand& c : beam(q.data(), ep, std::max(ef, k), 0)) {
+    if (removed_[c.second]) continue;
+    if (allowed && (c.second >= allowed_len || !allowed[c.second])) continue;
+    out.push_back({1.f - c.first, c.second});
+    if ((int)out.size() >= k) break;
+  }
+  return out;
+}
+
+}  // namespace rag
+}  // namespace kapsl

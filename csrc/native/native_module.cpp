@@ -7,6 +7,7 @@
 
 #include "block_alloc.h"
 #include "cpu_kernels.h"
+#include "hnsw.h"
 #include "server.h"
 #include "shm.h"
 #include "text_index.h"
@@ -211,6 +212,51 @@ PYBIND11_MODULE(_native, m) {
       .def("alternative", &text::UnigramModel::alternative)
       .def("alternative_scores", &text::UnigramModel::alternative_scores, py::call_guard<py::gil_scoped_release>())
       .def("__len__", &text::UnigramModel::size);
+
+  // ---- RAG: approximate nearest-neighbour index (cosine)
+  auto rg = m.def_submodule("rag", "vector index of the RAG store");
+  py::class_<rag::Hnsw>(rg, "Hnsw")
+      .def(py::init<int, int, int, uint64_t>(), py::arg("dim"), py::arg("M") = 16, py::arg("ef_construction") = 200,
+           py::arg("seed") = 42)
+      .def("add", [](rag::Hnsw& h, py::array_t<float, py::array::c_style | py::array::forcecast> x) {
+        if (x.ndim() < 1 || x.ndim() > 2 || x.shape(x.ndim() - 1) != h.dim())
+          throw std::invalid_argument("hnsw.add: expected [dim] or [n, dim] float32");
+        const int64_t n = x.ndim() == 1 ? 1 : x.shape(0);
+        py::array_t<int64_t> labels(n);
+        auto L = labels.mutable_unchecked<1>();
+        const float* p = x.data();
+        py::gil_scoped_release nogil;
+        for (int64_t i = 0; i < n; ++i) L(i) = h.add(p + i * h.dim());
+        return labels;
+      }, "Insert vectors; returns their labels (0, 1, 2, ... in insertion order)")
+      .def("remove", &rag::Hnsw::remove)
+      .def("search", [](const rag::Hnsw& h, py::array_t<float, py::array::c_style | py::array::forcecast> q, int k,
+                        int ef, py::object allowed) {
+        if (q.size() != h.dim()) throw std::invalid_argument("hnsw.search: query has the wrong dimension");
+        py::array_t<uint8_t, py::array::c_style | py::array::forcecast> mask;
+        const uint8_t* mp = nullptr;
+        int64_t ml = 0;
+        if (!allowed.is_none()) {
+          mask = allowed.cast<py::array_t<uint8_t, py::array::c_style | py::array::forcecast>>();
+          mp = mask.data();
+          ml = mask.size();
+        }
+        std::vector<std::pair<float, int64_t>> r;
+        {
+          py::gil_scoped_release nogil;
+          r = h.search(q.data(), k, ef, mp, ml);
+        }
+        py::array_t<float> sc((py::ssize_t)r.size());
+        py::array_t<int64_t> lb((py::ssize_t)r.size());
+        for (size_t i = 0; i < r.size(); ++i) {
+          sc.mutable_at(i) = r[i].first;
+          lb.mutable_at(i) = r[i].second;
+        }
+        return py::make_tuple(sc, lb);
+      }, py::arg("query"), py::arg("k"), py::arg("ef") = 64, py::arg("allowed") = py::none(),
+         "(cosine similarities, labels), best first; `allowed` is a uint8 mask over labels")
+      .def("__len__", &rag::Hnsw::size)
+      .def_property_readonly("dim", &rag::Hnsw::dim);
 
   // ---- WebAssembly connectors (WASI preview1)
   m.def("wasm_run",

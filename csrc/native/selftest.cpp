@@ -25,6 +25,7 @@
 
 #include "block_alloc.h"
 #include "cpu_kernels.h"
+#include "hnsw.h"
 #include "shm.h"
 #include "text_index.h"
 #include "wasm.h"
@@ -427,11 +428,39 @@ static void test_text_index() {
   }
 }
 
+// HNSW: one writer inserting while readers search (the index's lock), then
+// the nearest neighbour of an inserted vector is itself.
+static void test_hnsw() {
+  rag::Hnsw h(16, 8, 64, 3);
+  std::mt19937 gen(5);
+  std::normal_distribution<float> nd;
+  std::vector<float> data(2000 * 16);
+  for (auto& v : data) v = nd(gen);
+  h.add(data.data());
+  std::atomic<bool> done{false};
+  std::vector<std::thread> readers;
+  for (int t = 0; t < 3; ++t)
+    readers.emplace_back([&, t] {
+      std::vector<uint8_t> allow(2000, 1);
+      while (!done.load())
+        for (int i = 0; i < 50; ++i) (void)h.search(data.data() + 16 * ((i * 37 + t) % 2000), 5, 32, allow.data(), 2000);
+    });
+  for (int i = 1; i < 2000; ++i) h.add(data.data() + 16 * i);
+  done = true;
+  for (auto& t : readers) t.join();
+  int self = 0;
+  for (int i = 0; i < 2000; i += 20) {
+    auto r = h.search(data.data() + 16 * i, 1, 64, nullptr, 0);
+    self += !r.empty() && r[0].second == i;
+  }
+  CHECK(self >= 95, "hnsw: only %d of 100 vectors find themselves", self);
+}
+
 int main(int argc, char** argv) {
   const std::pair<const char*, void (*)()> tests[] = {
       {"ring_mpmc", test_ring_mpmc},         {"ring_repush", test_ring_repush}, {"model_pools", test_model_pools},
       {"shared_leases", test_shared_leases}, {"block_allocator", test_block_allocator}, {"wire", test_wire},
-      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm},               {"text_index", test_text_index}};
+      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm},               {"text_index", test_text_index}, {"hnsw", test_hnsw}};
   for (auto& [name, fn] : tests) {
     if (argc > 1 && std::string(argv[1]) != name) continue;
     const auto t0 = std::chrono::steady_clock::now();

@@ -8,8 +8,9 @@ chunks of the tenant/workspace (and optional sources) that pass the ACL
 never when a deny list matches), scores them by cosine similarity and
 returns the top k at or above ``min_score``.  Scoring is one matrix-vector
 product over the candidate embeddings (torch; on the GPU when asked), not a
-Python loop (reference: crates/kapsl-rag/src/vector/mod.rs:26-359 scores
-row by row; storage/mod.rs:18-70 for the document store).
+Python loop, over rows kept resident after the first query, or an HNSW
+graph search for large scopes (reference: crates/kapsl-rag/src/vector/mod.rs:26-359
+reads and scores every row per query; storage/mod.rs:18-70 for the document store).
 """
 from __future__ import annotations
 
@@ -128,13 +129,91 @@ def _json_list(s: Optional[str]) -> list:
     return [x for x in v if isinstance(x, str)] if isinstance(v, list) else []
 
 
+class _Scope:
+    """Resident copy of one (tenant, workspace): unit-norm embeddings per row,
+    row fields, ACLs, an alive mask (deleted or replaced rows stay as dead
+    rows) and, when asked for, an HNSW graph whose labels are the row numbers."""
+
+    def __init__(self, dim: int, use_hnsw: bool):
+        from .. import _native
+
+        self.dim = dim
+        self.rows, self.acls, self.sources, self.raw, self.pos = [], [], [], [], {}
+        self.emb = np.zeros((0, dim), np.float32)
+        self.alive = np.zeros(0, bool)
+        self.public = np.zeros(0, bool)  # no allow and no deny lists
+        self.hnsw = _native.rag.Hnsw(dim) if use_hnsw else None
+        self._pending = []
+        self._dev = None  # (device, tensor) copy of emb for flat scoring
+
+    def tensor(self, device: str):
+        import torch
+
+        if self._dev is None or self._dev[0] != device:
+            self._dev = (device, torch.from_numpy(self.emb).to(device))
+        return self._dev[1]
+
+    def add(self, row: tuple, acl: AccessControl, emb: np.ndarray) -> None:
+        old = self.pos.get(row[0])
+        if old is not None:
+            self.kill(old)
+        n = len(self.rows)
+        self.pos[row[0]] = n
+        self.rows.append(row)
+        self.acls.append(acl)
+        self.sources.append(row[3])
+        self.raw.append(emb)
+        norm = float(np.linalg.norm(emb))
+        self._pending.append((emb / norm if norm > 0 else emb, not (acl.allow_users or acl.allow_groups or
+                                                                     acl.deny_users or acl.deny_groups)))
+
+    def flush(self) -> None:
+        if not self._pending:
+            return
+        e = np.stack([x for x, _ in self._pending]).astype(np.float32)
+        self.emb = np.concatenate([self.emb, e])
+        self._dev = None
+        self.alive = np.concatenate([self.alive, np.ones(len(e), bool)])
+        self.public = np.concatenate([self.public, np.array([p for _, p in self._pending], bool)])
+        if self.hnsw is not None:
+            self.hnsw.add(e)
+        self._pending = []
+
+    def kill(self, n: int) -> None:
+        self.flush()
+        self.alive[n] = False
+        if self.hnsw is not None:
+            self.hnsw.remove(n)
+
+
 class SqliteVectorStore:
-    def __init__(self, path: str, device: str = "cpu"):
+    """``index="flat"`` scores every candidate row with one matrix-vector product
+    (torch, on ``device``); ``index="hnsw"`` searches an HNSW graph
+    (``_native.rag.Hnsw``) when more than ``exact_below`` rows pass the filters,
+    and scores exactly below that.  Rows stay resident per (tenant, workspace)
+    after the first query; writes through this object update that copy, and a
+    commit by another connection (SQLite's ``data_version``) drops it."""
+
+    def __init__(self, path: str, device: str = "cpu", index: str = "flat", ef_search: int = 96,
+                 exact_below: int = 4096):
+        if index not in ("flat", "hnsw"):
+            raise ValueError(f"unknown vector index {index!r}")
         self._conn = sqlite3.connect(path, check_same_thread=False)
         self._lock = threading.Lock()
-        self.device = device
+        self.device, self.index, self.ef_search, self.exact_below = device, index, ef_search, exact_below
+        self._scopes: dict = {}
         with self._lock:
             self._conn.executescript(_SCHEMA)
+            self._version = self._data_version()
+
+    def _data_version(self) -> int:
+        return self._conn.execute("PRAGMA data_version").fetchone()[0]
+
+    def _check_version(self) -> None:
+        v = self._data_version()
+        if v != self._version:  # another connection committed
+            self._scopes.clear()
+            self._version = v
 
     def upsert(self, chunks: list) -> None:
         rows = [(c.id, c.tenant_id, c.workspace_id, c.source_id, c.doc_id, int(c.chunk_index), c.text,
@@ -142,56 +221,106 @@ class SqliteVectorStore:
                  json.dumps(c.acl.allow_users), json.dumps(c.acl.allow_groups), json.dumps(c.acl.deny_users),
                  json.dumps(c.acl.deny_groups), int(time.time())) for c in chunks]
         with self._lock:
+            self._check_version()
             self._conn.executemany("INSERT OR REPLACE INTO rag_chunks VALUES (?,?,?,?,?,?,?,?,?,?,?,?,?,?)", rows)
             self._conn.commit()
+            for r in rows:
+                self._mirror_row(r)
+
+    def _mirror_row(self, r: tuple) -> None:
+        for key in list(self._scopes):
+            if key[:2] != (r[1], r[2]):
+                continue
+            sc = self._scopes[key]
+            old = sc.pos.pop(r[0], None)
+            if old is not None:
+                sc.kill(old)
+            e = np.frombuffer(r[7], dtype="<f4")
+            if e.shape[0] == sc.dim:
+                sc.add(r[:7] + r[8:9], AccessControl(_json_list(r[9]), _json_list(r[10]), _json_list(r[11]),
+                                                     _json_list(r[12])), e)
 
     def delete_by_doc(self, tenant_id: str, workspace_id: str, source_id: str, doc_id: str) -> int:
         with self._lock:
+            self._check_version()
             cur = self._conn.execute("DELETE FROM rag_chunks WHERE tenant_id=? AND workspace_id=? AND source_id=? "
                                      "AND doc_id=?", (tenant_id, workspace_id, source_id, doc_id))
             self._conn.commit()
+            for key, sc in self._scopes.items():
+                if key[:2] != (tenant_id, workspace_id):
+                    continue
+                for n, row in enumerate(sc.rows):
+                    if row[3] == source_id and row[4] == doc_id and sc.pos.get(row[0]) == n:
+                        del sc.pos[row[0]]
+                        sc.kill(n)
             return cur.rowcount
+
+    def _scope(self, tenant_id: str, workspace_id: str, dim: int) -> _Scope:
+        key = (tenant_id, workspace_id, dim)
+        sc = self._scopes.get(key)
+        if sc is None:
+            sc = _Scope(dim, self.index == "hnsw")
+            rows = self._conn.execute(
+                "SELECT id, tenant_id, workspace_id, source_id, doc_id, chunk_index, text, embedding, metadata_json, "
+                "acl_allow_users, acl_allow_groups, acl_deny_users, acl_deny_groups FROM rag_chunks "
+                "WHERE tenant_id = ? AND workspace_id = ?", (tenant_id, workspace_id)).fetchall()
+            for r in rows:
+                e = np.frombuffer(r[7], dtype="<f4")
+                if e.shape[0] == dim:
+                    sc.add(r[:7] + r[8:9], AccessControl(_json_list(r[9]), _json_list(r[10]), _json_list(r[11]),
+                                                         _json_list(r[12])), e)
+            self._scopes[key] = sc
+        sc.flush()
+        return sc
 
     def query(self, q: VectorQuery) -> list:
         import torch
 
         if not q.query_embedding:
             raise ValueError("query embedding is empty")
-        sql = ("SELECT id, tenant_id, workspace_id, source_id, doc_id, chunk_index, text, embedding, metadata_json, "
-               "acl_allow_users, acl_allow_groups, acl_deny_users, acl_deny_groups FROM rag_chunks "
-               "WHERE tenant_id = ? AND workspace_id = ?")
-        args = [q.tenant_id, q.workspace_id]
-        if q.source_ids:
-            sql += " AND source_id IN (" + ", ".join("?" * len(q.source_ids)) + ")"
-            args += list(q.source_ids)
+        v = np.asarray(q.query_embedding, dtype=np.float32)
         with self._lock:
-            rows = self._conn.execute(sql, args).fetchall()
-        users, groups = set(q.allowed_users), set(q.allowed_groups)
-        dim = len(q.query_embedding)
-        keep, embs = [], []
-        for r in rows:
-            e = np.frombuffer(r[7], dtype="<f4")
-            if e.shape[0] != dim:
-                continue
-            acl = AccessControl(_json_list(r[9]), _json_list(r[10]), _json_list(r[11]), _json_list(r[12]))
-            if not _allowed(users, groups, acl.allow_users, acl.allow_groups):
-                continue
-            if _denied(users, groups, acl.deny_users, acl.deny_groups):
-                continue
-            keep.append((r, acl))
-            embs.append(e)
-        if not keep:
-            return []
-        m = torch.from_numpy(np.stack(embs)).to(self.device)
-        v = torch.tensor(q.query_embedding, dtype=torch.float32, device=self.device)
-        norms = m.norm(dim=1) * v.norm()
-        scores = torch.where(norms > 0, (m @ v) / norms.clamp_min(1e-30), torch.zeros_like(norms)).cpu().tolist()
+            self._check_version()
+            sc = self._scope(q.tenant_id, q.workspace_id, v.shape[0])
+            n = len(sc.rows)
+            if n == 0:
+                return []
+            mask = sc.alive & sc.public
+            users, groups = set(q.allowed_users), set(q.allowed_groups)
+            for i in np.flatnonzero(sc.alive & ~sc.public):
+                a = sc.acls[i]
+                mask[i] = _allowed(users, groups, a.allow_users, a.allow_groups) and \
+                    not _denied(users, groups, a.deny_users, a.deny_groups)
+            if q.source_ids:
+                mask &= np.isin(np.asarray(sc.sources, dtype=object), list(q.source_ids))
+            cand = np.flatnonzero(mask)
+            if len(cand) == 0:
+                return []
+            vn = float(np.linalg.norm(v))
+            if sc.hnsw is not None and len(cand) > self.exact_below and vn > 0:
+                k = q.top_k
+                while True:  # widen the beam until k rows pass the filter (or no more can)
+                    s, lab = sc.hnsw.search(v, k, max(self.ef_search, k), mask.view(np.uint8))
+                    if len(lab) >= q.top_k or k >= len(cand):
+                        break
+                    k *= 4
+                idx, scores = lab[:q.top_k], s[:q.top_k].astype(np.float64).tolist()
+            else:
+                sims = sc.tensor(self.device) @ torch.from_numpy(v).to(self.device)
+                sims = sims / vn if vn > 0 else torch.zeros_like(sims)
+                sims = sims.masked_fill(~torch.from_numpy(mask).to(self.device), float("-inf"))
+                kth = torch.topk(sims, min(q.top_k, len(cand))).values[-1]
+                keep = torch.nonzero(sims >= kth).flatten()  # the k best and every row tied with the k-th
+                sims, cand = sims[keep], keep.cpu().numpy()
+                idx, scores = cand, sims.cpu().tolist()
+            rows = [(sc.rows[i], sc.acls[i], sc.raw[i]) for i in idx]
         out = []
-        for (r, acl), s, e in zip(keep, scores, embs):
+        for (r, acl, e), s in zip(rows, scores):
             if s < q.min_score:
                 continue
-            meta = json.loads(r[8]) if r[8] else {}
-            out.append(VectorSearchResult(EmbeddedChunk(r[0], r[1], r[2], r[3], r[4], r[5], r[6], e.tolist(), meta,
-                                                        acl), float(s)))
+            e = e.tolist()
+            meta = json.loads(r[7]) if r[7] else {}
+            out.append(VectorSearchResult(EmbeddedChunk(r[0], r[1], r[2], r[3], r[4], r[5], r[6], e, meta, acl),
+                                          float(s)))
         out.sort(key=lambda x: (-x.score, x.chunk.id))
         return out[:q.top_k]

@@ -11,7 +11,7 @@ import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 SRC = os.path.join(ROOT, "csrc", "native")
-FILES = ["selftest.cpp", "shm.cpp", "wire.cpp", "block_alloc.cpp", "cpu_kernels.cpp", "wasm.cpp", "text_index.cpp"]
+FILES = ["selftest.cpp", "shm.cpp", "wire.cpp", "block_alloc.cpp", "cpu_kernels.cpp", "wasm.cpp", "text_index.cpp", "hnsw.cpp"]
 
 
 def _build(tmp_path, flags):

@@ -7,6 +7,7 @@ import os
 import sys
 import textwrap
 
+import numpy as np
 import pytest
 
 from kapsl_sdk_b200 import rag
@@ -131,3 +132,71 @@ def test_chunker():
     cs = rag.SimpleChunker(4, 1).chunk(doc)
     assert [c.text for c in cs] == ["0 1 2 3", "3 4 5 6", "6 7 8 9"] and cs[1].id == "d:1"
     assert cs[2].metadata["chunk_index"] == "2"
+
+
+def _clustered(n, dim, seed):
+    rng = np.random.default_rng(seed)
+    centers = rng.standard_normal((40, dim)).astype(np.float32)
+    return (centers[rng.integers(0, 40, n)] + 0.6 * rng.standard_normal((n, dim))).astype(np.float32), centers
+
+
+def test_hnsw_recall_filter_and_removal():
+    from kapsl_sdk_b200 import _native
+
+    X, centers = _clustered(6000, 48, 0)
+    h = _native.rag.Hnsw(48, M=16, ef_construction=200, seed=7)
+    assert list(h.add(X[:10])) == list(range(10)) and len(h.add(X[10:])) == 5990 and len(h) == 6000
+    Xn = X / np.linalg.norm(X, axis=1, keepdims=True)
+    rng = np.random.default_rng(1)
+    hits = 0
+    for _ in range(100):
+        q = centers[rng.integers(0, 40)] + 0.6 * rng.standard_normal(48).astype(np.float32)
+        s, lab = h.search(q, 10, 96)
+        sims = Xn @ (q / np.linalg.norm(q))
+        hits += len(set(lab.tolist()) & set(np.argsort(-sims)[:10].tolist()))
+        assert np.allclose(s, sims[lab], atol=1e-5) and np.all(np.diff(s) <= 1e-6)
+    assert hits / 1000 >= 0.95
+    mask = np.zeros(6000, np.uint8)
+    mask[::7] = 1  # filter: only every 7th label may be returned
+    s, lab = h.search(X[3], 10, 400, mask)
+    assert len(lab) == 10 and all(int(x) % 7 == 0 for x in lab)
+    best = int(h.search(X[5], 1, 64)[1][0])
+    h.remove(best)
+    assert best not in h.search(X[5], 10, 64)[1].tolist()
+
+
+@pytest.mark.parametrize("index", ["flat", "hnsw"])
+def test_resident_store_matches_exact_scores_and_sees_other_writers(tmp_path, index):
+    X, _ = _clustered(3000, 32, 2)
+    db = str(tmp_path / "v.db")
+    store = rag.SqliteVectorStore(db, index=index, exact_below=100)
+    acl_eng = rag.AccessControl(allow_groups=["eng"])
+    chunks = [rag.EmbeddedChunk(f"c{i}", "t", "ws", "src" + str(i % 3), f"d{i // 10}", i % 10, f"text {i}",
+                                X[i].tolist(), {"i": i}, acl_eng if i % 5 == 0 else rag.AccessControl())
+              for i in range(len(X))]
+    store.upsert(chunks[:2000])
+    q = X[17] + 0.1
+    Xn = X / np.linalg.norm(X, axis=1, keepdims=True)
+
+    def exact(n, allow_eng, sources=None):
+        sims = Xn[:n] @ (q / np.linalg.norm(q))
+        ok = [i for i in range(n) if (allow_eng or i % 5) and (sources is None or f"src{i % 3}" in sources)]
+        return [f"c{i}" for i in sorted(ok, key=lambda i: -sims[i])[:10]]
+
+    got = store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws"))
+    assert [r.chunk.id for r in got] == exact(2000, False)
+    assert got[0].chunk.embedding == pytest.approx(X[int(got[0].chunk.id[1:])].tolist())
+    got = store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws", allowed_groups=["eng"], source_ids=["src1"]))
+    assert [r.chunk.id for r in got] == exact(2000, True, {"src1"})
+    # writes through this object update the resident rows
+    store.upsert(chunks[2000:])
+    assert [r.chunk.id for r in store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws"))] == exact(3000, False)
+    top = store.query(rag.VectorQuery(q.tolist(), 1, "t", "ws"))[0].chunk
+    store.delete_by_doc("t", "ws", top.source_id, top.doc_id)
+    after = [r.chunk.id for r in store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws"))]
+    assert all(cid not in after for cid in [c.id for c in chunks if c.doc_id == top.doc_id])
+    # another connection's commit drops the resident copy
+    other = rag.SqliteVectorStore(db)
+    moved = rag.EmbeddedChunk("new", "t", "ws", "src0", "dn", 0, "new", (q * 3).tolist())
+    other.upsert([moved])
+    assert store.query(rag.VectorQuery(q.tolist(), 1, "t", "ws"))[0].chunk.id == "new"
