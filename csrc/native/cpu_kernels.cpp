@@ -23,6 +23,10 @@
 #include <omp.h>
 #endif
 
+#ifdef __AVX2__
+#include <immintrin.h>
+#endif
+
 namespace kapsl {
 namespace cpu {
 
@@ -298,6 +302,103 @@ inline void q4k_block(const uint8_t* b, float* out) {
 }
 
 }  // namespace
+
+namespace {
+
+// 6-bit scale and min of sub-block j (0..7) of a Q4_K block's 12 scale bytes
+inline void q4k_scale_min(const uint8_t* sc, int j, int* s, int* m) {
+  if (j < 4) {
+    *s = sc[j] & 63;
+    *m = sc[j + 4] & 63;
+  } else {
+    *s = (sc[j + 4] & 0xF) | ((sc[j - 4] >> 6) << 4);
+    *m = (sc[j + 4] >> 4) | ((sc[j] >> 6) << 4);
+  }
+}
+
+// sum_j s[j] * (q_j . xq_j) over the 8 sub-blocks of one block; q_j are the low
+// (even j) or high (odd j) nibbles of qs[(j / 2) * 32 .. + 32]
+inline int32_t q4k_dot_q8(const uint8_t* qs, const int8_t* xq, const int* s) {
+#ifdef __AVX2__
+  const __m256i lo4 = _mm256_set1_epi8(0x0F);
+  __m256i acc = _mm256_setzero_si256();
+  for (int p = 0; p < 4; ++p) {
+    const __m256i q = _mm256_loadu_si256((const __m256i*)(qs + p * 32));
+    const __m256i ql = _mm256_and_si256(q, lo4), qh = _mm256_and_si256(_mm256_srli_epi16(q, 4), lo4);
+    const __m256i xl = _mm256_loadu_si256((const __m256i*)(xq + p * 64));
+    const __m256i xh = _mm256_loadu_si256((const __m256i*)(xq + p * 64 + 32));
+    // u8 x s8 -> pairwise s16 (|.| <= 2 * 15 * 127), then x scale with pairwise s32 sums
+    acc = _mm256_add_epi32(acc, _mm256_madd_epi16(_mm256_maddubs_epi16(ql, xl), _mm256_set1_epi16((short)s[2 * p])));
+    acc = _mm256_add_epi32(acc,
+                           _mm256_madd_epi16(_mm256_maddubs_epi16(qh, xh), _mm256_set1_epi16((short)s[2 * p + 1])));
+  }
+  const __m128i h = _mm_add_epi32(_mm256_castsi256_si128(acc), _mm256_extracti128_si256(acc, 1));
+  const __m128i h2 = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0x4E));
+  return _mm_cvtsi128_si32(_mm_add_epi32(h2, _mm_shuffle_epi32(h2, 0xB1)));
+#else
+  int32_t total = 0;
+  for (int j = 0; j < 8; ++j) {
+    const uint8_t* q = qs + (j / 2) * 32;
+    const int shift = (j & 1) * 4;
+    int32_t d = 0;
+    for (int i = 0; i < 32; ++i) d += ((q[i] >> shift) & 0xF) * xq[j * 32 + i];
+    total += s[j] * d;
+  }
+  return total;
+#endif
+}
+
+}  // namespace
+
+void q4k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K) {
+  const int64_t nb = K / kQK;
+  // activations: int8 blocks of 256, their scales and 32-value sums
+  std::vector<int8_t> xq((size_t)(T * K));
+  std::vector<float> dx((size_t)(T * nb));
+  std::vector<int32_t> bsum((size_t)(T * nb * 8));
+  parallel_for(T * nb, 4, [&](int64_t tb) {
+    const float* xr = x + tb * kQK;
+    float amax = 0.f;
+    for (int i = 0; i < kQK; ++i) amax = std::max(amax, std::fabs(xr[i]));
+    const float scale = amax / 127.f, inv = amax > 0.f ? 127.f / amax : 0.f;
+    dx[tb] = scale;
+    int8_t* q = xq.data() + tb * kQK;
+    for (int j = 0; j < 8; ++j) {
+      int32_t sum = 0;
+      for (int i = 0; i < 32; ++i) {
+        const int v = (int)std::nearbyint(xr[j * 32 + i] * inv);
+        q[j * 32 + i] = (int8_t)std::max(-127, std::min(127, v));
+        sum += q[j * 32 + i];
+      }
+      bsum[tb * 8 + j] = sum;
+    }
+  });
+  parallel_for(N, 16, [&](int64_t n) {
+    const uint8_t* row = w + n * nb * kQ4KBytes;
+    float acc[16];
+    for (int64_t t0 = 0; t0 < T; t0 += 16) {
+      const int64_t tn = std::min<int64_t>(16, T - t0);
+      for (int64_t t = 0; t < tn; ++t) acc[t] = 0.f;
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + b * kQ4KBytes;
+        uint16_t dh, mh;
+        std::memcpy(&dh, blk, 2);
+        std::memcpy(&mh, blk + 2, 2);
+        const float d = half_to_float(dh), dmin = half_to_float(mh);
+        int s[8], m[8];
+        for (int j = 0; j < 8; ++j) q4k_scale_min(blk + 4, j, &s[j], &m[j]);
+        for (int64_t t = 0; t < tn; ++t) {
+          const int64_t tb = (t0 + t) * nb + b;
+          const int32_t dot = q4k_dot_q8(blk + 16, xq.data() + tb * kQK, s);
+          int32_t msum = 0;
+          for (int j = 0; j < 8; ++j) msum += m[j] * bsum[tb * 8 + j];
+          acc[t] += dx[tb] * (d * (float)dot - dmin * (float)msum);
+        }
+      }
+      for (int64_t t = 0; t < tn; ++t) y[(t0 + t) * N + n] = acc[t];
+    }
+  });
+}
 
 void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K) {
   const int64_t nb = K / kQK;

@@ -35,6 +35,14 @@ void silu_mul(const float* x, float* out, int64_t T, int64_t F);
 // 4-bit quants; v = d * sc * q - dmin * m).
 // y[t, n] = sum_k x[t, k] * w[n, k]            (x [T, K], y [T, N] fp32)
 void q4k_matmul(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K);
+// The same product with the activations quantized to int8 per 256-value
+// block (scale = max|x| / 127, round to nearest) and integer dot products of
+// the 4-bit quants with them (AVX2 u8 x s8 multiply-adds), scaled per 32-value
+// sub-block:  y = dx * (d * sum_j sc_j * sum(q * xq) - dmin * sum_j m_j * sum(xq)).
+// This is the arithmetic llama.cpp's CPU path uses for Q4_K (8-bit
+// activation blocks); the error against q4k_matmul is that of rounding x to
+// 8 bits.
+void q4k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K);
 // out[(n - n0), k] = w[n, k] for rows n0 <= n < n1 (fp32)
 void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K);
 

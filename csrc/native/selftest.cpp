@@ -304,6 +304,27 @@ static void test_cpu_pool() {
       }
     });
   for (auto& t : ts) t.join();
+  // Q4_K: the int8-activation kernel against the fp32 one on random blocks
+  // (d and dmin kept small and finite: f16 0x1400 = 2^-10, 0x1000 = 2^-11)
+  const int64_t N = 33, K = 512, T = 5;
+  std::mt19937 rng(11);
+  std::vector<uint8_t> wq(N * (K / 256) * 144);
+  for (auto& b : wq) b = (uint8_t)rng();
+  for (int64_t blk = 0; blk < N * (K / 256); ++blk) {
+    wq[blk * 144 + 0] = 0x00, wq[blk * 144 + 1] = 0x14;
+    wq[blk * 144 + 2] = 0x00, wq[blk * 144 + 3] = 0x10;
+  }
+  std::uniform_real_distribution<float> U(-1, 1);
+  std::vector<float> x(T * K), y0(T * N), y1(T * N);
+  for (auto& v : x) v = U(rng);
+  cpu::q4k_matmul(x.data(), wq.data(), y0.data(), T, N, K);
+  cpu::q4k_matmul_q8(x.data(), wq.data(), y1.data(), T, N, K);
+  float amax = 0.f, err = 0.f;
+  for (int64_t i = 0; i < T * N; ++i) {
+    amax = std::max(amax, std::fabs(y0[i]));
+    err = std::max(err, std::fabs(y0[i] - y1[i]));
+  }
+  CHECK(err <= 0.02f * amax, "q4k int8 kernel: error %g of %g", err, amax);
 }
 
 // A module with recursion, br_table, bulk memory, a mutable global, memory.grow

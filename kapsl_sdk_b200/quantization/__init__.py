@@ -17,7 +17,9 @@ llama.cpp (crates/kapsl-llm/src/gguf_backend.rs:110-118).
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
+from typing import Optional
 
 import torch
 
@@ -139,15 +141,25 @@ class Q4KRows:
         native().cpu.q4k_dequant_rows(self.raw, 0, self.n, out.numpy())
         return out
 
-    def matmul(self, x: torch.Tensor, row_block: int = 2048) -> torch.Tensor:
-        """x [T, K] fp32 -> x @ W.T [T, N]."""
+    def matmul(self, x: torch.Tensor, row_block: int = 2048, int8: Optional[bool] = None) -> torch.Tensor:
+        """x [T, K] fp32 -> x @ W.T [T, N].
+
+        Up to 16 rows (decode) run the native kernels on the packed blocks:
+        with ``int8`` (default unless ``KAPSL_CPU_Q4K_INT8=0``) the activations
+        are rounded to int8 per 256-value block and multiplied with the 4-bit
+        quants in integer arithmetic (llama.cpp's Q4_K x Q8_K scheme; ~0.7% of
+        the output range), otherwise each block is dequantized to fp32 first.
+        More rows dequantize ``row_block`` weight rows at a time into one fp32
+        buffer and use BLAS."""
         from .._ext import native
 
         cpu = native().cpu
         x = x.float().contiguous()
         y = torch.empty(x.shape[0], self.n, dtype=torch.float32)
         if x.shape[0] <= 16:
-            cpu.q4k_matmul(x.numpy(), self.raw, y.numpy())
+            if int8 is None:
+                int8 = os.environ.get("KAPSL_CPU_Q4K_INT8", "1") != "0"
+            (cpu.q4k_matmul_q8 if int8 else cpu.q4k_matmul)(x.numpy(), self.raw, y.numpy())
             return y
         buf = torch.empty(min(row_block, self.n), self.k, dtype=torch.float32)
         for n0 in range(0, self.n, row_block):

@@ -1,6 +1,7 @@
 """GGUF Q4_K weights kept quantized on the CPU backend: the C++ kernel and the
 row-block path match a dense matmul with the dequantized weights, and an
-engine on a Q4_K GGUF serves the same tokens quantized as dequantized."""
+engine on a Q4_K GGUF serves the same tokens quantized as dequantized; the
+int8-activation decode kernel matches its integer statement."""
 import os
 
 import numpy as np
@@ -21,7 +22,16 @@ def test_q4k_rows_matmul_matches_dequantized(T):
     dense = torch.from_numpy(dequant_q4_k(raw.reshape(-1)).reshape(N, K))
     assert torch.equal(q.dequantize(), dense)
     x = torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32))
-    torch.testing.assert_close(q.matmul(x, row_block=32), x @ dense.T, rtol=1e-4, atol=1e-4)
+    ref = x @ dense.T
+    torch.testing.assert_close(q.matmul(x, row_block=32, int8=False), ref, rtol=1e-4, atol=1e-4)
+    # int8 activations (decode sizes): within the rounding of x to 8 bits per 256-value block
+    got = q.matmul(x, row_block=32, int8=True)
+    assert (got - ref).abs().max() <= 0.02 * ref.abs().max()
+    if T <= 16:  # and exactly the integer statement of the same arithmetic
+        xb = x.reshape(T, K // 256, 256)
+        dx = xb.abs().amax(-1, keepdim=True) / 127
+        xq = torch.where(dx > 0, torch.round(xb / dx).clamp(-127, 127), torch.zeros_like(xb))
+        torch.testing.assert_close(got, (xq * dx).reshape(T, K) @ dense.T, rtol=2e-4, atol=2e-4)
     sub = q.take(np.array([5, 1, 7])).rows(1, 3)
     assert torch.equal(sub.dequantize(), dense[[1, 7]])
 
@@ -45,6 +55,7 @@ def test_engine_on_q4k_gguf_keeps_weights_quantized(tmp_path, monkeypatch):
     assert isinstance(m_d.layers[0]["qkv"], torch.Tensor)
     torch.testing.assert_close(m_q.layers[0]["qkv"].dequantize(), m_d.layers[0]["qkv"])
     prompt = list(range(11, 60))
+    monkeypatch.setenv("KAPSL_CPU_Q4K_INT8", "0")  # the fp32-activation kernel: same tokens as dense fp32
     outs = []
     for c, m in ((c_q, m_q), (c_d, m_d)):
         eng = LLMEngine(c, weights=m, device="cpu", engine_cfg=EngineConfig(
