@@ -350,29 +350,110 @@ inline int32_t q4k_dot_q8(const uint8_t* qs, const int8_t* xq, const int* s) {
 
 }  // namespace
 
-void q4k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K) {
-  const int64_t nb = K / kQK;
-  // activations: int8 blocks of 256, their scales and 32-value sums
-  std::vector<int8_t> xq((size_t)(T * K));
-  std::vector<float> dx((size_t)(T * nb));
-  std::vector<int32_t> bsum((size_t)(T * nb * 8));
+namespace {
+
+constexpr int64_t kQ6KBytes = 210;
+
+// the 6-bit quants of one Q6_K block in value order (0..63)
+inline void q6k_unpack(const uint8_t* b, uint8_t* q) {
+  for (int h = 0; h < 2; ++h) {
+    const uint8_t* L = b + h * 64;
+    const uint8_t* H = b + 128 + h * 32;
+    uint8_t* o = q + h * 128;
+    for (int i = 0; i < 32; ++i) {
+      o[i] = (uint8_t)((L[i] & 0xF) | ((H[i] & 3) << 4));
+      o[32 + i] = (uint8_t)((L[32 + i] & 0xF) | (((H[i] >> 2) & 3) << 4));
+      o[64 + i] = (uint8_t)((L[i] >> 4) | (((H[i] >> 4) & 3) << 4));
+      o[96 + i] = (uint8_t)((L[32 + i] >> 4) | (((H[i] >> 6) & 3) << 4));
+    }
+  }
+}
+
+// sum_g scale_g * (q_g . xq_g) over the 16 groups of 16 values of one block
+// (blk: the packed block; q: its unpacked quants, used without AVX2)
+inline int32_t q6k_dot_q8(const uint8_t* blk, const uint8_t* q, const int8_t* xq, const int8_t* sc) {
+#ifdef __AVX2__
+  (void)q;
+  const __m256i m4 = _mm256_set1_epi8(0x0F), m2 = _mm256_set1_epi8(0x03);
+  __m256i acc = _mm256_setzero_si256();
+  for (int h = 0; h < 2; ++h) {
+    const __m256i L0 = _mm256_loadu_si256((const __m256i*)(blk + h * 64));
+    const __m256i L1 = _mm256_loadu_si256((const __m256i*)(blk + h * 64 + 32));
+    const __m256i H = _mm256_loadu_si256((const __m256i*)(blk + 128 + h * 32));
+    // the four 32-value chunks of this half, in value order
+    const __m256i qv[4] = {
+        _mm256_or_si256(_mm256_and_si256(L0, m4), _mm256_slli_epi16(_mm256_and_si256(H, m2), 4)),
+        _mm256_or_si256(_mm256_and_si256(L1, m4),
+                        _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(H, 2), m2), 4)),
+        _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(L0, 4), m4),
+                        _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(H, 4), m2), 4)),
+        _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(L1, 4), m4),
+                        _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(H, 6), m2), 4))};
+    for (int j = 0; j < 4; ++j) {
+      const int c = h * 4 + j;  // values 32c .. 32c + 31 = groups 2c, 2c + 1
+      const __m256i xv = _mm256_loadu_si256((const __m256i*)(xq + c * 32));
+      // pairwise u8 x s8 (|.| <= 2 * 63 * 127); lanes 0-7 hold group 2c, 8-15 group 2c + 1
+      const __m256i p = _mm256_maddubs_epi16(qv[j], xv);
+      const __m256i s = _mm256_set_m128i(_mm_set1_epi16(sc[2 * c + 1]), _mm_set1_epi16(sc[2 * c]));
+      acc = _mm256_add_epi32(acc, _mm256_madd_epi16(p, s));
+    }
+  }
+  const __m128i hs = _mm_add_epi32(_mm256_castsi256_si128(acc), _mm256_extracti128_si256(acc, 1));
+  const __m128i h2 = _mm_add_epi32(hs, _mm_shuffle_epi32(hs, 0x4E));
+  return _mm_cvtsi128_si32(_mm_add_epi32(h2, _mm_shuffle_epi32(h2, 0xB1)));
+#else
+  (void)blk;
+  int32_t total = 0;
+  for (int g = 0; g < 16; ++g) {
+    int32_t d = 0;
+    for (int i = 0; i < 16; ++i) d += q[g * 16 + i] * xq[g * 16 + i];
+    total += sc[g] * d;
+  }
+  return total;
+#endif
+}
+
+#ifdef __AVX2__
+constexpr bool kUnpackForDot = false;
+#else
+constexpr bool kUnpackForDot = true;
+#endif
+
+// int8 activation blocks of 256 values: scale = max|x| / 127 and per-group sums
+// (group = `group` values)
+void quantize_rows_q8(const float* x, int64_t T, int64_t K, int group, std::vector<int8_t>& xq,
+                      std::vector<float>& dx, std::vector<int32_t>& gsum) {
+  const int64_t nb = K / kQK, ng = kQK / group;
+  xq.resize((size_t)(T * K));
+  dx.resize((size_t)(T * nb));
+  gsum.resize((size_t)(T * nb * ng));
   parallel_for(T * nb, 4, [&](int64_t tb) {
     const float* xr = x + tb * kQK;
     float amax = 0.f;
     for (int i = 0; i < kQK; ++i) amax = std::max(amax, std::fabs(xr[i]));
-    const float scale = amax / 127.f, inv = amax > 0.f ? 127.f / amax : 0.f;
-    dx[tb] = scale;
+    const float inv = amax > 0.f ? 127.f / amax : 0.f;
+    dx[tb] = amax / 127.f;
     int8_t* q = xq.data() + tb * kQK;
-    for (int j = 0; j < 8; ++j) {
+    for (int64_t g = 0; g < ng; ++g) {
       int32_t sum = 0;
-      for (int i = 0; i < 32; ++i) {
-        const int v = (int)std::nearbyint(xr[j * 32 + i] * inv);
-        q[j * 32 + i] = (int8_t)std::max(-127, std::min(127, v));
-        sum += q[j * 32 + i];
+      for (int i = 0; i < group; ++i) {
+        const int v = (int)std::nearbyint(xr[g * group + i] * inv);
+        q[g * group + i] = (int8_t)std::max(-127, std::min(127, v));
+        sum += q[g * group + i];
       }
-      bsum[tb * 8 + j] = sum;
+      gsum[tb * ng + g] = sum;
     }
   });
+}
+
+}  // namespace
+
+void q4k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K) {
+  const int64_t nb = K / kQK;
+  std::vector<int8_t> xq;
+  std::vector<float> dx;
+  std::vector<int32_t> bsum;  // per 32 values
+  quantize_rows_q8(x, T, K, 32, xq, dx, bsum);
   parallel_for(N, 16, [&](int64_t n) {
     const uint8_t* row = w + n * nb * kQ4KBytes;
     float acc[16];
@@ -396,6 +477,57 @@ void q4k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_
         }
       }
       for (int64_t t = 0; t < tn; ++t) y[(t0 + t) * N + n] = acc[t];
+    }
+  });
+}
+
+void q6k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K) {
+  const int64_t nb = K / kQK;
+  std::vector<int8_t> xq;
+  std::vector<float> dx;
+  std::vector<int32_t> gsum;  // per 16 values
+  quantize_rows_q8(x, T, K, 16, xq, dx, gsum);
+  parallel_for(N, 16, [&](int64_t n) {
+    const uint8_t* row = w + n * nb * kQ6KBytes;
+    alignas(32) uint8_t q[kQK];
+    float acc[16];
+    for (int64_t t0 = 0; t0 < T; t0 += 16) {
+      const int64_t tn = std::min<int64_t>(16, T - t0);
+      for (int64_t t = 0; t < tn; ++t) acc[t] = 0.f;
+      for (int64_t b = 0; b < nb; ++b) {
+        const uint8_t* blk = row + b * kQ6KBytes;
+        if (kUnpackForDot) q6k_unpack(blk, q);
+        const int8_t* sc = (const int8_t*)(blk + 192);
+        uint16_t dh;
+        std::memcpy(&dh, blk + 208, 2);
+        const float d = half_to_float(dh);
+        for (int64_t t = 0; t < tn; ++t) {
+          const int64_t tb = (t0 + t) * nb + b;
+          const int32_t dot = q6k_dot_q8(blk, q, xq.data() + tb * kQK, sc);
+          int32_t off = 0;
+          for (int g = 0; g < 16; ++g) off += sc[g] * gsum[tb * 16 + g];
+          acc[t] += dx[tb] * d * (float)(dot - 32 * off);
+        }
+      }
+      for (int64_t t = 0; t < tn; ++t) y[(t0 + t) * N + n] = acc[t];
+    }
+  });
+}
+
+void q6k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K) {
+  const int64_t nb = K / kQK;
+  parallel_for(n1 - n0, 8, [&](int64_t r) {
+    const uint8_t* row = w + (n0 + r) * nb * kQ6KBytes;
+    uint8_t q[kQK];
+    for (int64_t b = 0; b < nb; ++b) {
+      const uint8_t* blk = row + b * kQ6KBytes;
+      q6k_unpack(blk, q);
+      const int8_t* sc = (const int8_t*)(blk + 192);
+      uint16_t dh;
+      std::memcpy(&dh, blk + 208, 2);
+      const float d = half_to_float(dh);
+      float* o = out + r * K + b * kQK;
+      for (int v = 0; v < kQK; ++v) o[v] = d * (float)sc[v / 16] * (float)((int)q[v] - 32);
     }
   });
 }

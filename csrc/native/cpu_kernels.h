@@ -46,5 +46,12 @@ void q4k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_
 // out[(n - n0), k] = w[n, k] for rows n0 <= n < n1 (fp32)
 void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K);
 
+// GGUF Q6_K rows (210-byte blocks of 256: 128 bytes of low 4 bits, 64 bytes of
+// high 2 bits, 16 int8 scales, f16 d; v = d * scale[v / 16] * (q - 32)).
+// The product with int8 activation blocks, as for Q4_K:
+//   y = dx * d * (sum_g scale_g * sum(q * xq) - 32 * sum_g scale_g * sum_g(xq)).
+void q6k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K);
+void q6k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K);
+
 }  // namespace cpu
 }  // namespace kapsl

@@ -325,6 +325,22 @@ static void test_cpu_pool() {
     err = std::max(err, std::fabs(y0[i] - y1[i]));
   }
   CHECK(err <= 0.02f * amax, "q4k int8 kernel: error %g of %g", err, amax);
+  // Q6_K: the int8 kernel against dequantized rows (d = f16 0x1000 = 2^-11)
+  std::vector<uint8_t> w6(N * (K / 256) * 210);
+  for (auto& b : w6) b = (uint8_t)rng();
+  for (int64_t blk = 0; blk < N * (K / 256); ++blk) w6[blk * 210 + 208] = 0x00, w6[blk * 210 + 209] = 0x10;
+  std::vector<float> deq(N * K);
+  cpu::q6k_dequant_rows(w6.data(), deq.data(), 0, N, K);
+  cpu::q6k_matmul_q8(x.data(), w6.data(), y1.data(), T, N, K);
+  amax = err = 0.f;
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t n = 0; n < N; ++n) {
+      float ref = 0.f;
+      for (int64_t k = 0; k < K; ++k) ref += x[t * K + k] * deq[n * K + k];
+      amax = std::max(amax, std::fabs(ref));
+      err = std::max(err, std::fabs(ref - y1[t * N + n]));
+    }
+  CHECK(err <= 0.02f * amax, "q6k int8 kernel: error %g of %g", err, amax);
 }
 
 // A module with recursion, br_table, bulk memory, a mutable global, memory.grow

@@ -122,6 +122,34 @@ def quantize_q4_k(x: np.ndarray) -> np.ndarray:
     return out.reshape(-1)
 
 
+def quantize_q6_k(x: np.ndarray) -> np.ndarray:
+    """fp32 [n * 256] -> Q6_K bytes.  Per 16-value group: scale = max|x| / 32
+    (signed by the value of largest magnitude, so it maps to -32); the 16 scales
+    are coded as int8 multiples of ``d = max|scale| / 127``; quants are
+    round(x / (d * sc)) + 32 clipped to 0..63."""
+    x = np.asarray(x, np.float32).reshape(-1, 16, 16)
+    nb = x.shape[0]
+    idx = np.abs(x).argmax(-1)
+    vmax = np.take_along_axis(x, idx[..., None], -1)[..., 0]
+    scales = -vmax / 32.0
+    d = np.abs(scales).max(-1) / 127.0
+    d16 = d.astype(np.float16)
+    dq = np.where(d16 > 0, d16.astype(np.float32), 1.0)
+    sc = np.clip(np.rint(scales / dq[:, None]), -127, 127).astype(np.int8)
+    eff = d16.astype(np.float32)[:, None] * sc
+    q = np.where(eff[:, :, None] != 0, np.rint(x / np.where(eff != 0, eff, 1)[:, :, None]), 0) + 32
+    q = np.clip(q, 0, 63).astype(np.uint8).reshape(nb, 2, 4, 32)  # [block, half, quarter, 32]
+    out = np.zeros((nb, Q6_K_BYTES), np.uint8)
+    lo, hi = q & 0xF, q >> 4
+    for h in range(2):
+        out[:, h * 64:h * 64 + 32] = lo[:, h, 0] | (lo[:, h, 2] << 4)
+        out[:, h * 64 + 32:h * 64 + 64] = lo[:, h, 1] | (lo[:, h, 3] << 4)
+        out[:, 128 + h * 32:128 + h * 32 + 32] = hi[:, h, 0] | (hi[:, h, 1] << 2) | (hi[:, h, 2] << 4) | (hi[:, h, 3] << 6)
+    out[:, 192:208] = sc.view(np.uint8)
+    out[:, 208:210] = d16.reshape(-1, 1).view(np.uint8).reshape(nb, 2)
+    return out.reshape(-1)
+
+
 # ------------------------------------------------------------------ reading
 def _permute_back(w: np.ndarray, n_head: int) -> np.ndarray:
     """Undo the interleaved-rotary permutation of llama q/k rows."""
@@ -236,15 +264,16 @@ def _gguf_rope_scaling(reader, arch: str) -> Optional[dict]:
 
 
 def _q4k_rows(t):
-    """A 2-D Q4_K tensor as kept-quantized rows (None for other types)."""
+    """A 2-D Q4_K or Q6_K tensor as kept-packed rows (None for other types)."""
     from gguf import GGMLQuantizationType as Q
 
-    from ..quantization import Q4KRows
+    from ..quantization import Q4KRows, Q6KRows
 
-    if t.tensor_type != Q.Q4_K or len(t.shape) != 2:
+    cls = {Q.Q4_K: Q4KRows, Q.Q6_K: Q6KRows}.get(t.tensor_type)
+    if cls is None or len(t.shape) != 2:
         return None
     n, k = int(t.shape[1]), int(t.shape[0])
-    return Q4KRows(np.asarray(t.data).view(np.uint8).reshape(n, k // QK_K * Q4_K_BYTES), k)
+    return cls(np.asarray(t.data).view(np.uint8).reshape(n, k // QK_K * cls.BLOCK), k)
 
 
 def _row_perm(rows: int, n_head: int) -> np.ndarray:
@@ -254,7 +283,7 @@ def _row_perm(rows: int, n_head: int) -> np.ndarray:
 
 def iter_gguf_full(path: str, cfg: Optional[ModelConfig] = None, keep_q4k: bool = False):
     """Yields the runtime's full-tensor stream (see models.llama.random_full_weights).
-    ``keep_q4k``: 2-D Q4_K projection weights stay quantized (``Q4KRows``) for the CPU backend."""
+    ``keep_q4k``: 2-D Q4_K and Q6_K weights stay packed (``Q4KRows`` / ``Q6KRows``) for the CPU backend."""
     from gguf import GGUFReader
 
     r = GGUFReader(path)
@@ -370,7 +399,9 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
     """Serialize a full-tensor stream as a GGUF file of architecture ``arch``
     ("llama": q/k rows permuted as llama.cpp stores them; "phi3": fused
     attn_qkv and [gate; up] in ffn_up, no permutation).
-    ``quant``: "f32", "f16" or "q4_k" (2-D weights quantized, norms kept f32)."""
+    ``quant``: "f32", "f16", "q4_k" (2-D weights quantized, norms kept f32) or
+    "q4_k_m" (Q4_K with Q6_K for output, attn_v and ffn_down, the mix of
+    llama.cpp's Q4_K_M preset applied to every layer)."""
     from gguf import GGMLQuantizationType as Q
     from gguf import GGUFWriter
 
@@ -397,7 +428,10 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
 
     def put(name, t: torch.Tensor, is_weight: bool):
         a = t.detach().float().cpu().numpy()
-        if quant == "q4_k" and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
+        six = quant == "q4_k_m" and (name == "output.weight" or name.endswith((".attn_v.weight", ".ffn_down.weight")))
+        if six and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
+            w.add_tensor(name, quantize_q6_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q6_K)
+        elif quant in ("q4_k", "q4_k_m") and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
             # quantized tensors are handed over as [rows, bytes per row]
             w.add_tensor(name, quantize_q4_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q4_K)
         elif quant == "f16" and a.ndim == 2:

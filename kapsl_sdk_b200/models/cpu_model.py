@@ -20,27 +20,30 @@ import numpy as np
 import torch
 
 from ..ops import reference as ref
-from ..quantization import Q4KRows
+from ..quantization import PackedRows, RowStack
 from .config import ModelConfig
 
 
 def _mm(x: torch.Tensor, w) -> torch.Tensor:
-    """x @ w.T for an fp32 weight or kept-quantized Q4_K rows."""
-    return w.matmul(x) if isinstance(w, Q4KRows) else x @ w.T
+    """x @ w.T for an fp32 weight or kept-packed GGUF rows."""
+    return x @ w.T if isinstance(w, torch.Tensor) else w.matmul(x)
 
 
 def _cat_rows(parts: list):
-    """Row-concatenation of weights (quantized rows stay quantized when all parts are)."""
-    if all(isinstance(p, Q4KRows) for p in parts):
-        return Q4KRows.cat(parts)
-    return torch.cat([p.dequantize() if isinstance(p, Q4KRows) else p for p in parts], 0)
+    """Row-concatenation of weights: packed rows of one format stay one packed
+    matrix, mixed formats (Q4_K_M's Q4_K q/k with a Q6_K v) a RowStack."""
+    if all(isinstance(p, torch.Tensor) for p in parts):
+        return torch.cat(parts, 0)
+    if all(isinstance(p, PackedRows) for p in parts) and len({type(p) for p in parts}) == 1:
+        return type(parts[0]).cat(parts)
+    return RowStack(parts)
 
 
 class CPUCausalLM:
     def __init__(self, cfg: ModelConfig, embed: torch.Tensor, lm_head: torch.Tensor, final_norm: torch.Tensor,
                  layers: list):
         def f(t):
-            if t is None or isinstance(t, Q4KRows):
+            if t is None or isinstance(t, (PackedRows, RowStack)):
                 return t
             return t.detach().to("cpu", torch.float32).contiguous()
         self.cfg = cfg

@@ -98,13 +98,15 @@ def dequantize_q4_k(raw: torch.Tensor, n: int, k: int) -> torch.Tensor:
     return out
 
 
-class Q4KRows:
-    """GGUF Q4_K weight rows kept quantized for the CPU backend: ``raw`` is
-    uint8 [N, K / 256 * 144] (one row per output feature), multiplied by the C++
-    kernel (``_native.cpu.q4k_matmul``) for short activations and by row
-    blocks dequantized into a BLAS matmul for long ones."""
+class PackedRows:
+    """GGUF k-quant weight rows kept packed for the CPU backend: ``raw`` is
+    uint8 [N, K / 256 * BLOCK] (one row per output feature).  Short activations
+    (decode) go through the native kernels on the packed blocks; long ones
+    dequantize row blocks into a BLAS matmul.  Subclasses name the format."""
 
-    BLOCK = 144
+    FMT = ""
+    BLOCK = 0
+    INT8_KERNEL = FP32_KERNEL = DEQUANT = ""
 
     def __init__(self, raw, k: int):
         import numpy as np
@@ -112,7 +114,7 @@ class Q4KRows:
         self.raw = np.ascontiguousarray(raw, dtype=np.uint8)
         self.k = int(k)
         if self.raw.ndim != 2 or self.k % 256 or self.raw.shape[1] != self.k // 256 * self.BLOCK:
-            raise ValueError("Q4_K rows: raw must be [N, K / 256 * 144] with K a multiple of 256")
+            raise ValueError(f"{self.FMT} rows: raw must be [N, K / 256 * {self.BLOCK}] with K a multiple of 256")
 
     @property
     def n(self) -> int:
@@ -122,23 +124,23 @@ class Q4KRows:
     def shape(self) -> tuple:
         return (self.n, self.k)
 
-    def rows(self, a: int, b: int) -> "Q4KRows":
-        return Q4KRows(self.raw[a:b], self.k)
+    def rows(self, a: int, b: int) -> "PackedRows":
+        return type(self)(self.raw[a:b], self.k)
 
-    def take(self, idx) -> "Q4KRows":
-        return Q4KRows(self.raw[idx], self.k)
+    def take(self, idx) -> "PackedRows":
+        return type(self)(self.raw[idx], self.k)
 
     @staticmethod
-    def cat(parts: list) -> "Q4KRows":
+    def cat(parts: list) -> "PackedRows":
         import numpy as np
 
-        return Q4KRows(np.concatenate([p.raw for p in parts], 0), parts[0].k)
+        return type(parts[0])(np.concatenate([p.raw for p in parts], 0), parts[0].k)
 
     def dequantize(self) -> torch.Tensor:
         from .._ext import native
 
         out = torch.empty(self.n, self.k, dtype=torch.float32)
-        native().cpu.q4k_dequant_rows(self.raw, 0, self.n, out.numpy())
+        getattr(native().cpu, self.DEQUANT)(self.raw, 0, self.n, out.numpy())
         return out
 
     def matmul(self, x: torch.Tensor, row_block: int = 2048, int8: Optional[bool] = None) -> torch.Tensor:
@@ -146,8 +148,8 @@ class Q4KRows:
 
         Up to 16 rows (decode) run the native kernels on the packed blocks:
         with ``int8`` (default unless ``KAPSL_CPU_Q4K_INT8=0``) the activations
-        are rounded to int8 per 256-value block and multiplied with the 4-bit
-        quants in integer arithmetic (llama.cpp's Q4_K x Q8_K scheme; ~0.7% of
+        are rounded to int8 per 256-value block and multiplied with the quants
+        in integer arithmetic (llama.cpp's k-quant x Q8_K scheme; under 1% of
         the output range), otherwise each block is dequantized to fp32 first.
         More rows dequantize ``row_block`` weight rows at a time into one fp32
         buffer and use BLAS."""
@@ -159,12 +161,50 @@ class Q4KRows:
         if x.shape[0] <= 16:
             if int8 is None:
                 int8 = os.environ.get("KAPSL_CPU_Q4K_INT8", "1") != "0"
-            (cpu.q4k_matmul_q8 if int8 else cpu.q4k_matmul)(x.numpy(), self.raw, y.numpy())
+            kernel = self.INT8_KERNEL if int8 or not self.FP32_KERNEL else self.FP32_KERNEL
+            getattr(cpu, kernel)(x.numpy(), self.raw, y.numpy())
             return y
         buf = torch.empty(min(row_block, self.n), self.k, dtype=torch.float32)
+        deq = getattr(cpu, self.DEQUANT)
         for n0 in range(0, self.n, row_block):
             n1 = min(self.n, n0 + row_block)
             w = buf[:n1 - n0]
-            cpu.q4k_dequant_rows(self.raw, n0, n1, w.numpy())
+            deq(self.raw, n0, n1, w.numpy())
             y[:, n0:n1] = x @ w.T
         return y
+
+
+class Q4KRows(PackedRows):
+    """Q4_K rows (144-byte blocks): int8-activation and fp32-activation decode kernels."""
+
+    FMT, BLOCK = "Q4_K", 144
+    INT8_KERNEL, FP32_KERNEL, DEQUANT = "q4k_matmul_q8", "q4k_matmul", "q4k_dequant_rows"
+
+
+class Q6KRows(PackedRows):
+    """Q6_K rows (210-byte blocks; the output and some FFN-down / V weights of
+    Q4_K_M files): int8-activation decode kernel."""
+
+    FMT, BLOCK = "Q6_K", 210
+    INT8_KERNEL, FP32_KERNEL, DEQUANT = "q6k_matmul_q8", "", "q6k_dequant_rows"
+
+
+class RowStack:
+    """Row-concatenation of weights of different formats (packed rows of two
+    k-quant types, or packed and fp32 rows): each part multiplies on its own
+    and the outputs are joined."""
+
+    def __init__(self, parts: list):
+        self.parts = list(parts)
+        self.k = int(self.parts[0].shape[1])
+        self.n = sum(int(p.shape[0]) for p in self.parts)
+
+    @property
+    def shape(self) -> tuple:
+        return (self.n, self.k)
+
+    def matmul(self, x: torch.Tensor) -> torch.Tensor:
+        return torch.cat([p.matmul(x) if isinstance(p, PackedRows) else x @ p.T for p in self.parts], 1)
+
+    def dequantize(self) -> torch.Tensor:
+        return torch.cat([p.dequantize() if isinstance(p, PackedRows) else p for p in self.parts], 0)

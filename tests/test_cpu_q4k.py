@@ -62,3 +62,57 @@ def test_engine_on_q4k_gguf_keeps_weights_quantized(tmp_path, monkeypatch):
             max_num_seqs=2, max_num_batched_tokens=32, max_model_len=128, num_blocks=32), seed=0)
         outs.append(eng.generate([prompt], SamplingParams.greedy(8, ignore_eos=True))[0])
     assert outs[0] == outs[1]
+
+
+def test_q6k_rows_and_mixed_stack_match_dequantized():
+    from gguf import GGMLQuantizationType as Q
+    from gguf import quants
+
+    from kapsl_sdk_b200.loaders.gguf import quantize_q6_k
+    from kapsl_sdk_b200.models.cpu_model import _cat_rows
+    from kapsl_sdk_b200.quantization import Q6KRows, RowStack
+
+    rng = np.random.default_rng(3)
+    N, K = 80, 512
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.05
+    raw = quantize_q6_k(w.reshape(-1)).reshape(N, -1)
+    dense = torch.from_numpy(quants.dequantize(raw.reshape(-1, 210), Q.Q6_K).reshape(N, K).copy())
+    assert (dense - torch.from_numpy(w)).abs().max() <= 0.02 * abs(w).max()  # 6-bit codes of the input
+    q6 = Q6KRows(raw, K)
+    assert torch.equal(q6.dequantize(), dense)
+    q4 = Q4KRows(quantize_q4_k(w.reshape(-1)).reshape(N, -1), K)
+    both = _cat_rows([q4, q6, torch.from_numpy(w[:8])])  # Q4_K + Q6_K + fp32 rows
+    assert isinstance(both, RowStack) and both.shape == (2 * N + 8, K)
+    full = torch.cat([q4.dequantize(), dense, torch.from_numpy(w[:8])])
+    torch.testing.assert_close(both.dequantize(), full)
+    for T in (1, 9, 16, 40):
+        x = torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32))
+        ref = x @ full.T
+        assert (both.matmul(x) - ref).abs().max() <= 0.02 * ref.abs().max()
+        if T <= 16:  # Q6_K int8 kernel = its integer statement
+            xb = x.reshape(T, K // 256, 256)
+            dx = xb.abs().amax(-1, keepdim=True) / 127
+            xq = torch.where(dx > 0, torch.round(xb / dx).clamp(-127, 127), torch.zeros_like(xb))
+            torch.testing.assert_close(q6.matmul(x), (xq * dx).reshape(T, K) @ dense.T, rtol=2e-4, atol=2e-4)
+
+
+def test_engine_on_q4_k_m_mix(tmp_path):
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.loaders.gguf import load_gguf_model, write_gguf_model
+    from kapsl_sdk_b200.models.config import ModelConfig
+    from kapsl_sdk_b200.models.llama import random_full_weights
+    from kapsl_sdk_b200.quantization import Q6KRows, RowStack
+
+    cfg = ModelConfig(name="q", arch="llama", vocab_size=256, hidden_size=256, intermediate_size=512, num_layers=2,
+                      num_heads=4, num_kv_heads=2, head_dim=64, max_position=256, bos_token_id=None,
+                      eos_token_id=None)
+    p = str(tmp_path / "m.gguf")
+    write_gguf_model(p, cfg, random_full_weights(cfg, torch.device("cpu"), seed=2, std=0.05), quant="q4_k_m")
+    c, m, _ = load_gguf_model(p, "cpu")
+    assert isinstance(m.layers[0]["qkv"], RowStack) and isinstance(m.layers[0]["down"], Q6KRows)
+    assert isinstance(m.lm_head, Q6KRows)
+    eng = LLMEngine(c, weights=m, device="cpu", engine_cfg=EngineConfig(max_num_seqs=2, max_num_batched_tokens=32,
+                                                                       max_model_len=128, num_blocks=32), seed=0)
+    out = eng.generate([list(range(11, 50))], SamplingParams.greedy(6, ignore_eos=True))[0]
+    assert len(out) == 6
