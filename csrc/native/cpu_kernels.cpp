@@ -532,6 +532,77 @@ void q6k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int6
   });
 }
 
+namespace {
+
+// q_b . xq_b for one 32-value Q8_0 block: s8 x s8 as |q| (u8, 128 for -128)
+// times sign(xq, q) (xq is never -128, so negating it cannot overflow)
+inline int32_t q80_dot_q8(const int8_t* q, const int8_t* xq) {
+#ifdef __AVX2__
+  const __m256i qv = _mm256_loadu_si256((const __m256i*)q);
+  const __m256i xv = _mm256_loadu_si256((const __m256i*)xq);
+  const __m256i p = _mm256_maddubs_epi16(_mm256_abs_epi8(qv), _mm256_sign_epi8(xv, qv));  // |.| <= 2 * 128 * 127
+  const __m256i s = _mm256_madd_epi16(p, _mm256_set1_epi16(1));
+  const __m128i h = _mm_add_epi32(_mm256_castsi256_si128(s), _mm256_extracti128_si256(s, 1));
+  const __m128i h2 = _mm_add_epi32(h, _mm_shuffle_epi32(h, 0x4E));
+  return _mm_cvtsi128_si32(_mm_add_epi32(h2, _mm_shuffle_epi32(h2, 0xB1)));
+#else
+  int32_t d = 0;
+  for (int i = 0; i < 32; ++i) d += q[i] * xq[i];
+  return d;
+#endif
+}
+
+constexpr int64_t kQ80Bytes = 34;
+
+}  // namespace
+
+void q80_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K) {
+  const int64_t nb = K / 32;
+  std::vector<int8_t> xq;
+  std::vector<float> dx;
+  std::vector<int32_t> gsum;
+  quantize_rows_q8(x, T, K, 32, xq, dx, gsum);
+  parallel_for(N, 16, [&](int64_t n) {
+    const uint8_t* row = w + n * nb * kQ80Bytes;
+    float acc[16];
+    for (int64_t t0 = 0; t0 < T; t0 += 16) {
+      const int64_t tn = std::min<int64_t>(16, T - t0);
+      for (int64_t t = 0; t < tn; ++t) acc[t] = 0.f;
+      for (int64_t b8 = 0; b8 < nb / 8; ++b8) {  // one 256-value activation block = 8 weight blocks
+        float d[8];
+        for (int j = 0; j < 8; ++j) {
+          uint16_t dh;
+          std::memcpy(&dh, row + (b8 * 8 + j) * kQ80Bytes, 2);
+          d[j] = half_to_float(dh);
+        }
+        for (int64_t t = 0; t < tn; ++t) {
+          const int64_t tb = (t0 + t) * (K / kQK) + b8;
+          const int8_t* xb = xq.data() + tb * kQK;
+          float s = 0.f;
+          for (int j = 0; j < 8; ++j)
+            s += d[j] * (float)q80_dot_q8((const int8_t*)(row + (b8 * 8 + j) * kQ80Bytes + 2), xb + j * 32);
+          acc[t] += dx[tb] * s;
+        }
+      }
+      for (int64_t t = 0; t < tn; ++t) y[(t0 + t) * N + n] = acc[t];
+    }
+  });
+}
+
+void q80_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K) {
+  const int64_t nb = K / 32;
+  parallel_for(n1 - n0, 8, [&](int64_t r) {
+    const uint8_t* row = w + (n0 + r) * nb * kQ80Bytes;
+    for (int64_t b = 0; b < nb; ++b) {
+      uint16_t dh;
+      std::memcpy(&dh, row + b * kQ80Bytes, 2);
+      const float d = half_to_float(dh);
+      const int8_t* q = (const int8_t*)(row + b * kQ80Bytes + 2);
+      for (int i = 0; i < 32; ++i) out[r * K + b * 32 + i] = d * (float)q[i];
+    }
+  });
+}
+
 void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K) {
   const int64_t nb = K / kQK;
   parallel_for(n1 - n0, 8, [&](int64_t r) {

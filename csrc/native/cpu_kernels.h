@@ -53,5 +53,11 @@ void q4k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int6
 void q6k_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K);
 void q6k_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K);
 
+// GGUF Q8_0 rows (34-byte blocks of 32: f16 d, 32 int8; v = d * q), K a
+// multiple of 256: y = dx * sum_b d_b * sum(q_b * xq_b) with int8 activation
+// blocks of 256 as above (every int8 code, -128 included, is handled).
+void q80_matmul_q8(const float* x, const uint8_t* w, float* y, int64_t T, int64_t N, int64_t K);
+void q80_dequant_rows(const uint8_t* w, float* out, int64_t n0, int64_t n1, int64_t K);
+
 }  // namespace cpu
 }  // namespace kapsl

@@ -142,6 +142,21 @@ void cpu_module(py::module_& m) {
     py::gil_scoped_release nogil;
     kapsl::cpu::q6k_dequant_rows(w.data(), out.mutable_data(), n0, n1, K);
   });
+  c.def("q80_matmul_q8", [](F32 x, U8 w, F32 y) {
+    need(x.ndim() == 2 && w.ndim() == 2 && y.ndim() == 2, "q80_matmul_q8: x [T, K], w [N, K/32*34], y [T, N]");
+    const int64_t T = x.shape(0), K = x.shape(1), N = w.shape(0);
+    need(K % 256 == 0 && w.shape(1) == K / 32 * 34 && y.shape(0) == T && y.shape(1) == N, "q80_matmul_q8: shapes");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::q80_matmul_q8(x.data(), w.data(), y.mutable_data(), T, N, K);
+  });
+  c.def("q80_dequant_rows", [](U8 w, int64_t n0, int64_t n1, F32 out) {
+    need(w.ndim() == 2 && 0 <= n0 && n0 <= n1 && n1 <= w.shape(0), "q80_dequant_rows: rows");
+    const int64_t K = w.shape(1) / 34 * 32;
+    need(w.shape(1) % 34 == 0 && out.ndim() == 2 && out.shape(0) == n1 - n0 && out.shape(1) == K,
+         "q80_dequant_rows: out [n1 - n0, K]");
+    py::gil_scoped_release nogil;
+    kapsl::cpu::q80_dequant_rows(w.data(), out.mutable_data(), n0, n1, K);
+  });
   c.def("q4k_dequant_rows", [](U8 w, int64_t n0, int64_t n1, F32 out) {
     need(w.ndim() == 2 && 0 <= n0 && n0 <= n1 && n1 <= w.shape(0), "q4k_dequant_rows: rows");
     const int64_t K = w.shape(1) / 144 * 256;

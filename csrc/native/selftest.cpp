@@ -341,6 +341,21 @@ static void test_cpu_pool() {
       err = std::max(err, std::fabs(ref - y1[t * N + n]));
     }
   CHECK(err <= 0.02f * amax, "q6k int8 kernel: error %g of %g", err, amax);
+  // Q8_0: the int8 kernel against dequantized rows (d = 2^-11)
+  std::vector<uint8_t> w8(N * (K / 32) * 34);
+  for (auto& b : w8) b = (uint8_t)rng();
+  for (int64_t blk = 0; blk < N * (K / 32); ++blk) w8[blk * 34] = 0x00, w8[blk * 34 + 1] = 0x10;
+  cpu::q80_dequant_rows(w8.data(), deq.data(), 0, N, K);
+  cpu::q80_matmul_q8(x.data(), w8.data(), y1.data(), T, N, K);
+  amax = err = 0.f;
+  for (int64_t t = 0; t < T; ++t)
+    for (int64_t n = 0; n < N; ++n) {
+      float ref = 0.f;
+      for (int64_t k = 0; k < K; ++k) ref += x[t * K + k] * deq[n * K + k];
+      amax = std::max(amax, std::fabs(ref));
+      err = std::max(err, std::fabs(ref - y1[t * N + n]));
+    }
+  CHECK(err <= 0.02f * amax, "q8_0 int8 kernel: error %g of %g", err, amax);
 }
 
 // A module with recursion, br_table, bulk memory, a mutable global, memory.grow

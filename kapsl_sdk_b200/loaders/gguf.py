@@ -264,13 +264,14 @@ def _gguf_rope_scaling(reader, arch: str) -> Optional[dict]:
 
 
 def _q4k_rows(t):
-    """A 2-D Q4_K or Q6_K tensor as kept-packed rows (None for other types)."""
+    """A 2-D Q4_K, Q6_K or Q8_0 tensor as kept-packed rows (None for other
+    types, and for Q8_0 rows whose length is not a multiple of 256)."""
     from gguf import GGMLQuantizationType as Q
 
-    from ..quantization import Q4KRows, Q6KRows
+    from ..quantization import Q4KRows, Q6KRows, Q80Rows
 
-    cls = {Q.Q4_K: Q4KRows, Q.Q6_K: Q6KRows}.get(t.tensor_type)
-    if cls is None or len(t.shape) != 2:
+    cls = {Q.Q4_K: Q4KRows, Q.Q6_K: Q6KRows, Q.Q8_0: Q80Rows}.get(t.tensor_type)
+    if cls is None or len(t.shape) != 2 or int(t.shape[0]) % QK_K:
         return None
     n, k = int(t.shape[1]), int(t.shape[0])
     return cls(np.asarray(t.data).view(np.uint8).reshape(n, k // QK_K * cls.BLOCK), k)
@@ -401,7 +402,7 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
     attn_qkv and [gate; up] in ffn_up, no permutation).
     ``quant``: "f32", "f16", "q4_k" (2-D weights quantized, norms kept f32) or
     "q4_k_m" (Q4_K with Q6_K for output, attn_v and ffn_down, the mix of
-    llama.cpp's Q4_K_M preset applied to every layer)."""
+    llama.cpp's Q4_K_M preset applied to every layer) or "q8_0"."""
     from gguf import GGMLQuantizationType as Q
     from gguf import GGUFWriter
 
@@ -431,6 +432,10 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
         six = quant == "q4_k_m" and (name == "output.weight" or name.endswith((".attn_v.weight", ".ffn_down.weight")))
         if six and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
             w.add_tensor(name, quantize_q6_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q6_K)
+        elif quant == "q8_0" and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
+            from gguf import quants
+
+            w.add_tensor(name, quants.quantize(np.ascontiguousarray(a), Q.Q8_0), raw_dtype=Q.Q8_0)
         elif quant in ("q4_k", "q4_k_m") and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
             # quantized tensors are handed over as [rows, bytes per row]
             w.add_tensor(name, quantize_q4_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q4_K)

@@ -189,6 +189,13 @@ class Q6KRows(PackedRows):
     INT8_KERNEL, FP32_KERNEL, DEQUANT = "q6k_matmul_q8", "", "q6k_dequant_rows"
 
 
+class Q80Rows(PackedRows):
+    """Q8_0 rows (34-byte blocks of 32 values; K a multiple of 256): int8-activation decode kernel."""
+
+    FMT, BLOCK = "Q8_0", 272  # bytes per 256 values (8 blocks of 34)
+    INT8_KERNEL, FP32_KERNEL, DEQUANT = "q80_matmul_q8", "", "q80_dequant_rows"
+
+
 class RowStack:
     """Row-concatenation of weights of different formats (packed rows of two
     k-quant types, or packed and fp32 rows): each part multiplies on its own

@@ -116,3 +116,48 @@ def test_engine_on_q4_k_m_mix(tmp_path):
                                                                        max_model_len=128, num_blocks=32), seed=0)
     out = eng.generate([list(range(11, 50))], SamplingParams.greedy(6, ignore_eos=True))[0]
     assert len(out) == 6
+
+
+def test_q80_rows_match_gguf_and_integer_statement(tmp_path):
+    from gguf import GGMLQuantizationType as Q
+    from gguf import quants
+
+    from kapsl_sdk_b200.quantization import Q80Rows
+
+    rng = np.random.default_rng(4)
+    N, K = 40, 768
+    w = rng.standard_normal((N, K)).astype(np.float32) * 0.05
+    raw = quants.quantize(w, Q.Q8_0)
+    dense = torch.from_numpy(quants.dequantize(raw, Q.Q8_0).reshape(N, K).copy())
+    q8 = Q80Rows(raw, K)
+    assert torch.equal(q8.dequantize(), dense)
+    for T in (1, 16, 30):
+        x = torch.from_numpy(rng.standard_normal((T, K)).astype(np.float32))
+        ref = x @ dense.T
+        got = q8.matmul(x)
+        assert (got - ref).abs().max() <= 0.02 * ref.abs().max()
+        if T <= 16:
+            xb = x.reshape(T, K // 256, 256)
+            dx = xb.abs().amax(-1, keepdim=True) / 127
+            xq = torch.where(dx > 0, torch.round(xb / dx).clamp(-127, 127), torch.zeros_like(xb))
+            torch.testing.assert_close(got, (xq * dx).reshape(T, K) @ dense.T, rtol=2e-4, atol=2e-4)
+
+
+def test_engine_on_q8_0_gguf(tmp_path):
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.loaders.gguf import load_gguf_model, write_gguf_model
+    from kapsl_sdk_b200.models.config import ModelConfig
+    from kapsl_sdk_b200.models.llama import random_full_weights
+    from kapsl_sdk_b200.quantization import Q80Rows
+
+    cfg = ModelConfig(name="q", arch="llama", vocab_size=256, hidden_size=256, intermediate_size=512, num_layers=2,
+                      num_heads=4, num_kv_heads=2, head_dim=64, max_position=256, bos_token_id=None,
+                      eos_token_id=None)
+    p = str(tmp_path / "m.gguf")
+    write_gguf_model(p, cfg, random_full_weights(cfg, torch.device("cpu"), seed=2, std=0.05), quant="q8_0")
+    c, m, _ = load_gguf_model(p, "cpu")
+    assert isinstance(m.layers[0]["qkv"], Q80Rows) and isinstance(m.layers[1]["gate_up"], Q80Rows)
+    eng = LLMEngine(c, weights=m, device="cpu", engine_cfg=EngineConfig(max_num_seqs=2, max_num_batched_tokens=32,
+                                                                       max_model_len=128, num_blocks=32), seed=0)
+    assert len(eng.generate([list(range(11, 50))], SamplingParams.greedy(6, ignore_eos=True))[0]) == 6
