@@ -122,6 +122,8 @@ def _denied(users: set, groups: set, deny_users: list, deny_groups: list) -> boo
 
 
 def _json_list(s: Optional[str]) -> list:
+    if not s or s == "[]":
+        return []
     try:
         v = json.loads(s) if s else []
     except ValueError:
@@ -153,7 +155,9 @@ class _Scope:
             self._dev = (device, torch.from_numpy(self.emb).to(device))
         return self._dev[1]
 
-    def add(self, row: tuple, acl: AccessControl, emb: np.ndarray) -> None:
+    def add(self, row: tuple, acl: AccessControl, emb: np.ndarray, pending: bool = True) -> None:
+        """One row; with ``pending=False`` the caller queues its embedding as
+        part of a matrix (``add_matrix``)."""
         old = self.pos.get(row[0])
         if old is not None:
             self.kill(old)
@@ -163,18 +167,27 @@ class _Scope:
         self.acls.append(acl)
         self.sources.append(row[3])
         self.raw.append(emb)
-        norm = float(np.linalg.norm(emb))
-        self._pending.append((emb / norm if norm > 0 else emb, not (acl.allow_users or acl.allow_groups or
-                                                                     acl.deny_users or acl.deny_groups)))
+        if pending:
+            self.add_matrix(emb[None], np.array([self._public(acl)]))
+
+    @staticmethod
+    def _public(acl: AccessControl) -> bool:
+        return not (acl.allow_users or acl.allow_groups or acl.deny_users or acl.deny_groups)
+
+    def add_matrix(self, emb: np.ndarray, public: np.ndarray) -> None:
+        self._pending.append((emb, public))
 
     def flush(self) -> None:
         if not self._pending:
             return
-        e = np.stack([x for x, _ in self._pending]).astype(np.float32)
+        e = np.concatenate([m for m, _ in self._pending]).astype(np.float32)
+        pub = np.concatenate([p for _, p in self._pending])
+        norm = np.linalg.norm(e, axis=1, keepdims=True)
+        e = np.divide(e, norm, out=np.zeros_like(e), where=norm > 0)  # zero rows stay zero (score 0)
         self.emb = np.concatenate([self.emb, e])
         self._dev = None
         self.alive = np.concatenate([self.alive, np.ones(len(e), bool)])
-        self.public = np.concatenate([self.public, np.array([p for _, p in self._pending], bool)])
+        self.public = np.concatenate([self.public, pub.astype(bool)])
         if self.hnsw is not None:
             self.hnsw.add(e)
         self._pending = []
@@ -264,11 +277,14 @@ class SqliteVectorStore:
                 "SELECT id, tenant_id, workspace_id, source_id, doc_id, chunk_index, text, embedding, metadata_json, "
                 "acl_allow_users, acl_allow_groups, acl_deny_users, acl_deny_groups FROM rag_chunks "
                 "WHERE tenant_id = ? AND workspace_id = ?", (tenant_id, workspace_id)).fetchall()
-            for r in rows:
-                e = np.frombuffer(r[7], dtype="<f4")
-                if e.shape[0] == dim:
-                    sc.add(r[:7] + r[8:9], AccessControl(_json_list(r[9]), _json_list(r[10]), _json_list(r[11]),
-                                                         _json_list(r[12])), e)
+            rows = [r for r in rows if len(r[7]) == 4 * dim]
+            emb = np.frombuffer(b"".join(r[7] for r in rows), dtype="<f4").reshape(len(rows), dim)
+            pub = np.zeros(len(rows), bool)
+            for i, (r, e) in enumerate(zip(rows, emb)):
+                acl = AccessControl(_json_list(r[9]), _json_list(r[10]), _json_list(r[11]), _json_list(r[12]))
+                sc.add(r[:7] + r[8:9], acl, e, pending=False)
+                pub[i] = sc._public(acl)
+            sc.add_matrix(emb, pub)
             self._scopes[key] = sc
         sc.flush()
         return sc
