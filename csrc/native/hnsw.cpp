@@ -1,10 +1,12 @@
 #include "hnsw.h"
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <mutex>
 #include <queue>
 #include <stdexcept>
+#include <thread>
 
 #ifdef __AVX2__
 #include <immintrin.h>
@@ -64,11 +66,22 @@ float Hnsw::dist(const float* a, int32_t b) const {
   return 1.f - s;
 }
 
+void Hnsw::neighbours(int32_t n, int level, std::vector<int32_t>& out) const {
+  if (concurrent_) {
+    std::lock_guard<std::mutex> g(node_mu_[n]);
+    out = links_[n][level];
+  } else {
+    out = links_[n][level];
+  }
+}
+
 int32_t Hnsw::greedy(const float* q, int32_t ep, int level) const {
   float d = dist(q, ep);
+  std::vector<int32_t> nb;
   for (bool moved = true; moved;) {
     moved = false;
-    for (int32_t n : links_[ep][level]) {
+    neighbours(ep, level, nb);
+    for (int32_t n : nb) {
       const float dn = dist(q, n);
       if (dn < d) {
         d = dn;
@@ -89,11 +102,13 @@ std::vector<Hnsw::Cand> Hnsw::beam(const float* q, int32_t ep, int ef, int level
   vis.test_and_set(ep);
   frontier.push({d0, ep});
   best.push({d0, ep});
+  std::vector<int32_t> nb;
   while (!frontier.empty()) {
     const Cand c = frontier.top();
     if (c.first > best.top().first && (int)best.size() >= ef) break;
     frontier.pop();
-    for (int32_t n : links_[c.second][level]) {
+    neighbours(c.second, level, nb);
+    for (int32_t n : nb) {
       if (vis.test_and_set(n)) continue;
       const float dn = dist(q, n);
       if ((int)best.size() < ef || dn < best.top().first) {
@@ -132,31 +147,46 @@ std::vector<int32_t> Hnsw::select(std::vector<Cand> cand, int m) const {
   return kept;
 }
 
-int64_t Hnsw::add(const float* in) {
-  std::lock_guard<std::mutex> turn(turn_);
-  std::unique_lock<std::shared_mutex> lock(mu_);
+int64_t Hnsw::append(const float* in, int level) {
   const int32_t id = (int32_t)links_.size();
   double norm = 0.0;
   for (int i = 0; i < dim_; ++i) norm += (double)in[i] * in[i];
   const float inv = norm > 0.0 ? (float)(1.0 / std::sqrt(norm)) : 0.f;
   for (int i = 0; i < dim_; ++i) data_.push_back(in[i] * inv);
-  std::uniform_real_distribution<double> u(std::nextafter(0.0, 1.0), 1.0);
-  const int level = (int)std::floor(-std::log(u(rng_)) * ml_);
   links_.emplace_back(level + 1);
   removed_.push_back(0);
+  node_mu_.emplace_back();
+  return id;
+}
+
+void Hnsw::link(int32_t id) {
   const float* q = vec(id);
-  if (entry_ < 0) {
-    entry_ = id;
-    top_ = level;
-    return id;
+  const int level = (int)links_[id].size() - 1;
+  int32_t ep;
+  int top;
+  {
+    std::lock_guard<std::mutex> g(entry_mu_);
+    if (entry_ < 0) {
+      entry_ = id;
+      top_ = level;
+      return;
+    }
+    ep = entry_;
+    top = top_;
   }
-  int32_t ep = entry_;
-  for (int l = top_; l > level; --l) ep = greedy(q, ep, l);
-  for (int l = std::min(level, top_); l >= 0; --l) {
+  for (int l = top; l > level; --l) ep = greedy(q, ep, l);
+  for (int l = std::min(level, top); l >= 0; --l) {
     std::vector<Cand> w = beam(q, ep, efc_, l);
     const int mmax = l == 0 ? M0_ : M_;
-    links(id, l) = select(w, M_);
-    for (int32_t n : links_[id][l]) {
+    const std::vector<int32_t> mine = select(w, M_);
+    {
+      std::unique_lock<std::mutex> g(node_mu_[id], std::defer_lock);
+      if (concurrent_) g.lock();
+      links(id, l) = mine;
+    }
+    for (int32_t n : mine) {
+      std::unique_lock<std::mutex> g(node_mu_[n], std::defer_lock);
+      if (concurrent_) g.lock();
       std::vector<int32_t>& nl = links(n, l);
       nl.push_back(id);
       if ((int)nl.size() > mmax) {
@@ -168,11 +198,48 @@ int64_t Hnsw::add(const float* in) {
     }
     ep = w.front().second;
   }
+  std::lock_guard<std::mutex> g(entry_mu_);
   if (level > top_) {
     top_ = level;
     entry_ = id;
   }
+}
+
+int64_t Hnsw::add(const float* in) {
+  std::lock_guard<std::mutex> turn(turn_);
+  std::unique_lock<std::shared_mutex> lock(mu_);
+  std::uniform_real_distribution<double> u(std::nextafter(0.0, 1.0), 1.0);
+  const int64_t id = append(in, (int)std::floor(-std::log(u(rng_)) * ml_));
+  link((int32_t)id);
   return id;
+}
+
+int64_t Hnsw::add_batch(const float* vecs, int64_t n, int threads) {
+  std::lock_guard<std::mutex> turn(turn_);
+  std::unique_lock<std::shared_mutex> lock(mu_);
+  const int64_t first = (int64_t)links_.size();
+  if (n <= 0) return first;
+  std::uniform_real_distribution<double> u(std::nextafter(0.0, 1.0), 1.0);
+  data_.reserve(data_.size() + (size_t)n * dim_);
+  for (int64_t i = 0; i < n; ++i) append(vecs + i * dim_, (int)std::floor(-std::log(u(rng_)) * ml_));
+  int64_t start = first;
+  for (; start < first + n && (entry_ < 0 || start - first < 64); ++start) link((int32_t)start);  // seed serially
+  if (threads <= 0) threads = (int)std::max(1u, std::thread::hardware_concurrency());
+  threads = (int)std::min<int64_t>(threads, first + n - start);
+  if (threads <= 1) {
+    for (int64_t i = start; i < first + n; ++i) link((int32_t)i);
+    return first;
+  }
+  concurrent_ = true;
+  std::atomic<int64_t> next{start};
+  std::vector<std::thread> pool;
+  for (int t = 0; t < threads; ++t)
+    pool.emplace_back([&] {
+      for (int64_t i; (i = next.fetch_add(1)) < first + n;) link((int32_t)i);
+    });
+  for (auto& t : pool) t.join();
+  concurrent_ = false;
+  return first;
 }
 
 void Hnsw::remove(int64_t label) {

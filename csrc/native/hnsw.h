@@ -14,7 +14,8 @@
 //   (one byte per label, optional) filters what is returned, not what is
 //   traversed, so the graph stays connected under any filter; removed labels
 //   are traversed and never returned.
-// Readers share a lock; insert and remove take it exclusively.  A writer first
+// Readers share a lock; insert and remove take it exclusively.  A batch insert
+// links nodes from several threads under per-node locks.  A writer first
 // takes a turnstile mutex that arriving readers also pass through, so a steady
 // stream of searches cannot starve inserts (glibc's reader-writer lock prefers
 // readers).
@@ -25,6 +26,7 @@
 
 #include <stdint.h>
 
+#include <deque>
 #include <mutex>
 #include <random>
 #include <shared_mutex>
@@ -39,6 +41,10 @@ class Hnsw {
   Hnsw(int dim, int M = 16, int ef_construction = 200, uint64_t seed = 42);
   // Labels are dense: label i is the i-th inserted vector.  Returns it.
   int64_t add(const float* vec);
+  // Inserts n vectors (row-major [n, dim]) with `threads` workers (0 = one per
+  // core); returns the first label.  Levels are drawn in label order, so only
+  // the links depend on the workers' interleaving.
+  int64_t add_batch(const float* vecs, int64_t n, int threads = 0);
   void remove(int64_t label);
   // (similarity, label) best first; at most k.
   std::vector<std::pair<float, int64_t>> search(const float* q, int k, int ef, const uint8_t* allowed,
@@ -54,6 +60,11 @@ class Hnsw {
   std::vector<Cand> beam(const float* q, int32_t ep, int ef, int level) const;  // nearest first
   std::vector<int32_t> select(std::vector<Cand> cand, int m) const;  // the paper's heuristic
   std::vector<int32_t>& links(int32_t n, int level) { return links_[n][level]; }
+  // list of node n at `level`, copied under the node's lock while a batch
+  // insert runs (workers update lists concurrently)
+  void neighbours(int32_t n, int level, std::vector<int32_t>& out) const;
+  int64_t append(const float* vec, int level);  // storage for one node, not linked
+  void link(int32_t id);                        // connect a stored node into the graph
 
   int dim_, M_, M0_, efc_;
   double ml_;
@@ -65,6 +76,9 @@ class Hnsw {
   int top_ = -1;
   mutable std::shared_mutex mu_;
   mutable std::mutex turn_;
+  mutable std::deque<std::mutex> node_mu_;  // per-node list locks (batch insert)
+  std::mutex entry_mu_;                     // entry_ / top_ during a batch insert
+  bool concurrent_ = false;
 };
 
 }  // namespace rag

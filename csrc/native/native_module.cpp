@@ -255,17 +255,22 @@ PYBIND11_MODULE(_native, m) {
   py::class_<rag::Hnsw>(rg, "Hnsw")
       .def(py::init<int, int, int, uint64_t>(), py::arg("dim"), py::arg("M") = 16, py::arg("ef_construction") = 200,
            py::arg("seed") = 42)
-      .def("add", [](rag::Hnsw& h, py::array_t<float, py::array::c_style | py::array::forcecast> x) {
+      .def("add", [](rag::Hnsw& h, py::array_t<float, py::array::c_style | py::array::forcecast> x, int threads) {
         if (x.ndim() < 1 || x.ndim() > 2 || x.shape(x.ndim() - 1) != h.dim())
           throw std::invalid_argument("hnsw.add: expected [dim] or [n, dim] float32");
         const int64_t n = x.ndim() == 1 ? 1 : x.shape(0);
         py::array_t<int64_t> labels(n);
         auto L = labels.mutable_unchecked<1>();
         const float* p = x.data();
-        py::gil_scoped_release nogil;
-        for (int64_t i = 0; i < n; ++i) L(i) = h.add(p + i * h.dim());
+        {
+          py::gil_scoped_release nogil;
+          const int64_t first = n == 1 ? h.add(p) : h.add_batch(p, n, threads);
+          for (int64_t i = 0; i < n; ++i) L(i) = first + i;
+        }
         return labels;
-      }, "Insert vectors; returns their labels (0, 1, 2, ... in insertion order)")
+      }, py::arg("vectors"), py::arg("threads") = 0,
+         "Insert vectors (several at once: `threads` workers, 0 = one per core); returns their labels "
+         "(0, 1, 2, ... in insertion order)")
       .def("remove", &rag::Hnsw::remove)
       .def("search", [](const rag::Hnsw& h, py::array_t<float, py::array::c_style | py::array::forcecast> q, int k,
                         int ef, py::object allowed) {

@@ -480,15 +480,16 @@ static void test_text_index() {
   }
 }
 
-// HNSW: one writer inserting while readers search (the index's lock), then
-// the nearest neighbour of an inserted vector is itself.
+// HNSW: a batch insert linked by 4 threads (per-node locks), then one writer
+// inserting while readers search (the index's lock); the nearest neighbour of
+// an inserted vector is itself.
 static void test_hnsw() {
   rag::Hnsw h(16, 8, 64, 3);
   std::mt19937 gen(5);
   std::normal_distribution<float> nd;
   std::vector<float> data(2000 * 16);
   for (auto& v : data) v = nd(gen);
-  h.add(data.data());
+  CHECK(h.add_batch(data.data(), 1000, 4) == 0, "hnsw: first label of a batch");  // 4 linking threads
   std::atomic<bool> done{false};
   std::vector<std::thread> readers;
   for (int t = 0; t < 3; ++t)
@@ -497,7 +498,7 @@ static void test_hnsw() {
       while (!done.load())
         for (int i = 0; i < 50; ++i) (void)h.search(data.data() + 16 * ((i * 37 + t) % 2000), 5, 32, allow.data(), 2000);
     });
-  for (int i = 1; i < 2000; ++i) h.add(data.data() + 16 * i);
+  for (int i = 1000; i < 2000; ++i) h.add(data.data() + 16 * i);
   done = true;
   for (auto& t : readers) t.join();
   int self = 0;

@@ -183,14 +183,18 @@ def test_resident_store_matches_exact_scores_and_sees_other_writers(tmp_path, in
         ok = [i for i in range(n) if (allow_eng or i % 5) and (sources is None or f"src{i % 3}" in sources)]
         return [f"c{i}" for i in sorted(ok, key=lambda i: -sims[i])[:10]]
 
+    def same(got, want):  # exact search gives the exact list; HNSW at least 9 of the 10
+        ids = [r.chunk.id for r in got]
+        return ids == want if index == "flat" else len(set(ids) & set(want)) >= 9
+
     got = store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws"))
-    assert [r.chunk.id for r in got] == exact(2000, False)
+    assert same(got, exact(2000, False))
     assert got[0].chunk.embedding == pytest.approx(X[int(got[0].chunk.id[1:])].tolist())
     got = store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws", allowed_groups=["eng"], source_ids=["src1"]))
-    assert [r.chunk.id for r in got] == exact(2000, True, {"src1"})
+    assert same(got, exact(2000, True, {"src1"}))
     # writes through this object update the resident rows
     store.upsert(chunks[2000:])
-    assert [r.chunk.id for r in store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws"))] == exact(3000, False)
+    assert same(store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws")), exact(3000, False))
     top = store.query(rag.VectorQuery(q.tolist(), 1, "t", "ws"))[0].chunk
     store.delete_by_doc("t", "ws", top.source_id, top.doc_id)
     after = [r.chunk.id for r in store.query(rag.VectorQuery(q.tolist(), 10, "t", "ws"))]
