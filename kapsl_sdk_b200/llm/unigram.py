@@ -249,3 +249,31 @@ def train_unigram(sentences: Iterable[str], vocab_size: int, *, max_piece_len: i
     all_scores = [0.0] * 3 + [floor - 1.0] * (len(meta) - 3) + [scores[i] for i in order]
     return UnigramTokenizer(all_pieces, all_scores, unk_id=0, bos_id=1, eos_id=2,
                             add_dummy_prefix=add_dummy_prefix, byte_fallback=byte_fallback)
+
+
+def main(argv: Optional[list] = None) -> int:
+    """``python -m kapsl_sdk_b200.llm.unigram corpus.txt [more.txt ...] --vocab-size 8000 -o tokenizer.json``:
+    train on the lines of the given files and write an HF ``tokenizer.json``."""
+    import argparse
+
+    p = argparse.ArgumentParser(prog="python -m kapsl_sdk_b200.llm.unigram", description=main.__doc__)
+    p.add_argument("files", nargs="+")
+    p.add_argument("--vocab-size", type=int, default=8000)
+    p.add_argument("--max-piece-len", type=int, default=16)
+    p.add_argument("--byte-fallback", action="store_true")
+    p.add_argument("-o", "--output", default="tokenizer.json")
+    a = p.parse_args(argv)
+    lines = []
+    for f in a.files:
+        with open(f, encoding="utf-8", errors="replace") as fh:
+            lines.extend(line.rstrip("\n") for line in fh if line.strip())
+    tok = train_unigram(lines, a.vocab_size, max_piece_len=a.max_piece_len, byte_fallback=a.byte_fallback)
+    tok.save(a.output)
+    n_tok = sum(len(tok.encode(s)) for s in lines[:10000])
+    n_chr = sum(len(s) for s in lines[:10000])
+    print(f"{a.output}: {tok.vocab_size} pieces, {n_chr / max(n_tok, 1):.2f} characters per token")
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -148,3 +148,12 @@ def test_byte_fallback_and_persistence(tmp_path):
     assert plain.unk_id in plain.encode("¿") and plain.decode(plain.encode("a ¿")) .endswith("⁇ ")
     with pytest.raises(ValueError):
         U.train_unigram(["abcdefghij"], 5)
+
+
+def test_command_line_trainer(tmp_path):
+    src = tmp_path / "corpus.txt"
+    src.write_text("\n".join(corpus(300)), encoding="utf-8")
+    out = tmp_path / "tok.json"
+    assert U.main([str(src), "--vocab-size", "150", "-o", str(out)]) == 0
+    tok = U.UnigramTokenizer.load(str(out))
+    assert tok.vocab_size <= 150 and tok.decode(tok.encode("the lazy fox")) == "the lazy fox"
