@@ -3,6 +3,8 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <queue>
 #include <stdexcept>
@@ -246,6 +248,99 @@ void Hnsw::remove(int64_t label) {
   std::lock_guard<std::mutex> turn(turn_);
   std::unique_lock<std::shared_mutex> lock(mu_);
   if (label >= 0 && label < (int64_t)removed_.size()) removed_[label] = 1;
+}
+
+Hnsw::Hnsw(Hnsw&& o) noexcept
+    : dim_(o.dim_), M_(o.M_), M0_(o.M0_), efc_(o.efc_), ml_(o.ml_), rng_(o.rng_), data_(std::move(o.data_)),
+      links_(std::move(o.links_)), removed_(std::move(o.removed_)), entry_(o.entry_), top_(o.top_) {
+  for (size_t i = 0; i < links_.size(); ++i) node_mu_.emplace_back();
+}
+
+void Hnsw::save(const std::string& path) const {
+  std::shared_lock<std::shared_mutex> lock(mu_);
+  std::FILE* f = std::fopen(path.c_str(), "wb");
+  if (!f) throw std::runtime_error("hnsw.save: cannot open " + path);
+  bool ok = true;
+  auto put = [&](const void* p, size_t n) { ok = ok && (n == 0 || std::fwrite(p, 1, n, f) == n); };  // empty lists may have no buffer
+  const int32_t head[5] = {dim_, M_, efc_, entry_, top_};
+  const int64_t n = (int64_t)links_.size();
+  put("KHNSW001", 8);
+  put(head, sizeof(head));
+  put(&n, 8);
+  put(data_.data(), data_.size() * sizeof(float));
+  put(removed_.data(), removed_.size());
+  for (const auto& levels : links_) {
+    const int32_t nl = (int32_t)levels.size();
+    put(&nl, 4);
+    for (const auto& l : levels) {
+      const int32_t c = (int32_t)l.size();
+      put(&c, 4);
+      put(l.data(), l.size() * 4);
+    }
+  }
+  ok = (std::fclose(f) == 0) && ok;
+  if (!ok) throw std::runtime_error("hnsw.save: write failed for " + path);
+}
+
+Hnsw Hnsw::load(const std::string& path) {
+  std::FILE* f = std::fopen(path.c_str(), "rb");
+  if (!f) throw std::runtime_error("hnsw.load: cannot open " + path);
+  auto fail = [&](const char* what) {
+    std::fclose(f);
+    throw std::runtime_error(std::string("hnsw.load: ") + what + " in " + path);
+  };
+  auto get = [&](void* p, size_t n) {
+    if (n != 0 && std::fread(p, 1, n, f) != n) fail("truncated file");
+  };
+  char magic[8];
+  int32_t head[5];
+  int64_t n;
+  get(magic, 8);
+  get(head, sizeof(head));
+  get(&n, 8);
+  if (std::memcmp(magic, "KHNSW001", 8) != 0 || head[0] <= 0 || head[0] > (1 << 16) || head[1] < 2 ||
+      head[1] > 1024 || head[2] < 1 || n < 0 || n > ((int64_t)1 << 31) - 1 || head[3] < -1 || head[3] >= n ||
+      head[4] < -1 || head[4] > 64)
+    fail("bad header");
+  Hnsw h(head[0], head[1], head[2]);
+  h.entry_ = head[3];
+  h.top_ = head[4];
+  // read the payload in bounded pieces so a forged count cannot demand a huge buffer up front
+  std::vector<float> vecs;
+  std::vector<uint8_t> removed;
+  for (int64_t i = 0; i < n; ++i) {
+    const size_t at = vecs.size();
+    vecs.resize(at + (size_t)h.dim_);
+    get(vecs.data() + at, (size_t)h.dim_ * sizeof(float));
+  }
+  removed.resize((size_t)n);
+  get(removed.data(), removed.size());
+  h.data_ = std::move(vecs);
+  h.removed_ = std::move(removed);
+  h.links_.resize((size_t)n);
+  for (int64_t i = 0; i < n; ++i) {
+    int32_t nl;
+    get(&nl, 4);
+    if (nl < 1 || nl > 65) fail("bad level count");
+    h.links_[i].resize(nl);
+    for (auto& l : h.links_[i]) {
+      int32_t c;
+      get(&c, 4);
+      if (c < 0 || c > 2 * h.M0_) fail("bad neighbour count");
+      l.resize(c);
+      get(l.data(), (size_t)c * 4);
+    }
+  }
+  std::fclose(f);
+  for (int64_t i = 0; i < n; ++i)  // every id must name a node that has the level it is linked at
+    for (size_t lv = 0; lv < h.links_[i].size(); ++lv)
+      for (int32_t x : h.links_[i][lv])
+        if (x < 0 || x >= n || h.links_[x].size() <= lv) throw std::runtime_error("hnsw.load: bad link in " + path);
+  if (n > 0 && (h.entry_ < 0 || (int)h.links_[h.entry_].size() != h.top_ + 1))
+    throw std::runtime_error("hnsw.load: bad entry point in " + path);
+  if (n == 0 && (h.entry_ != -1 || h.top_ != -1)) throw std::runtime_error("hnsw.load: bad entry point in " + path);
+  for (int64_t i = 0; i < n; ++i) h.node_mu_.emplace_back();
+  return h;
 }
 
 int64_t Hnsw::size() const {

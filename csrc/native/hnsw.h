@@ -30,6 +30,7 @@
 #include <mutex>
 #include <random>
 #include <shared_mutex>
+#include <string>
 #include <utility>
 #include <vector>
 
@@ -39,6 +40,7 @@ namespace rag {
 class Hnsw {
  public:
   Hnsw(int dim, int M = 16, int ef_construction = 200, uint64_t seed = 42);
+  Hnsw(Hnsw&& o) noexcept;
   // Labels are dense: label i is the i-th inserted vector.  Returns it.
   int64_t add(const float* vec);
   // Inserts n vectors (row-major [n, dim]) with `threads` workers (0 = one per
@@ -51,6 +53,12 @@ class Hnsw {
                                                 int64_t allowed_len) const;
   int64_t size() const;
   int dim() const { return dim_; }
+  // Binary file: "KHNSW001", dim, M, ef_construction, entry, top level, node
+  // count, unit vectors, removed flags, then per node its level count and per
+  // level its neighbour count and ids.  load() checks every count and id
+  // against the file and throws on anything out of range.
+  void save(const std::string& path) const;
+  static Hnsw load(const std::string& path);
 
  private:
   using Cand = std::pair<float, int32_t>;  // (distance, node)

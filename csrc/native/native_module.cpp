@@ -298,7 +298,9 @@ PYBIND11_MODULE(_native, m) {
       }, py::arg("query"), py::arg("k"), py::arg("ef") = 64, py::arg("allowed") = py::none(),
          "(cosine similarities, labels), best first; `allowed` is a uint8 mask over labels")
       .def("__len__", &rag::Hnsw::size)
-      .def_property_readonly("dim", &rag::Hnsw::dim);
+      .def_property_readonly("dim", &rag::Hnsw::dim)
+      .def("save", &rag::Hnsw::save, py::call_guard<py::gil_scoped_release>())
+      .def_static("load", &rag::Hnsw::load, py::call_guard<py::gil_scoped_release>());
 
   // ---- WebAssembly connectors (WASI preview1)
   m.def("wasm_run",

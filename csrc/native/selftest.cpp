@@ -507,6 +507,32 @@ static void test_hnsw() {
     self += !r.empty() && r[0].second == i;
   }
   CHECK(self >= 95, "hnsw: only %d of 100 vectors find themselves", self);
+  // saved graphs: random byte flips and truncations must make load() throw or
+  // give a graph that searches without touching memory out of range
+  const std::string path = "/tmp/kapsl-selftest-hnsw-" + std::to_string(getpid());
+  h.save(path);
+  std::string bytes;
+  {
+    std::FILE* f = std::fopen(path.c_str(), "rb");
+    char buf[4096];
+    for (size_t r; (r = std::fread(buf, 1, sizeof buf, f)) > 0;) bytes.append(buf, r);
+    std::fclose(f);
+  }
+  CHECK(rag::Hnsw::load(path).size() == 2000, "hnsw: reloaded graph size");
+  for (int trial = 0; trial < 40; ++trial) {
+    std::string b = bytes;
+    for (int k = 0; k < 4; ++k) b[gen() % b.size()] ^= (char)(1 + gen() % 255);
+    if (trial % 5 == 0) b.resize(gen() % b.size());
+    std::FILE* f = std::fopen(path.c_str(), "wb");
+    std::fwrite(b.data(), 1, b.size(), f);
+    std::fclose(f);
+    try {
+      rag::Hnsw g = rag::Hnsw::load(path);
+      (void)g.search(data.data(), 5, 32, nullptr, 0);
+    } catch (const std::exception&) {
+    }
+  }
+  std::remove(path.c_str());
 }
 
 int main(int argc, char** argv) {

@@ -188,8 +188,10 @@ class _Scope:
         self._dev = None
         self.alive = np.concatenate([self.alive, np.ones(len(e), bool)])
         self.public = np.concatenate([self.public, pub.astype(bool)])
-        if self.hnsw is not None:
-            self.hnsw.add(e)
+        if self.hnsw is not None:  # rows a loaded graph already holds are not inserted again
+            skip = max(0, len(self.hnsw) - (len(self.alive) - len(e)))
+            if skip < len(e):
+                self.hnsw.add(e[skip:])
         self._pending = []
 
     def kill(self, n: int) -> None:
@@ -208,9 +210,13 @@ class SqliteVectorStore:
     commit by another connection (SQLite's ``data_version``) drops it."""
 
     def __init__(self, path: str, device: str = "cpu", index: str = "flat", ef_search: int = 96,
-                 exact_below: int = 4096):
+                 exact_below: int = 4096, index_dir: Optional[str] = None):
+        """``index_dir``: with ``index="hnsw"``, graphs are saved there and loaded
+        again by a later store whose scope holds the same rows (same ids and
+        update times in rowid order), instead of being rebuilt."""
         if index not in ("flat", "hnsw"):
             raise ValueError(f"unknown vector index {index!r}")
+        self.index_dir = index_dir
         self._conn = sqlite3.connect(path, check_same_thread=False)
         self._lock = threading.Lock()
         self.device, self.index, self.ef_search, self.exact_below = device, index, ef_search, exact_below
@@ -275,9 +281,19 @@ class SqliteVectorStore:
             sc = _Scope(dim, self.index == "hnsw")
             rows = self._conn.execute(
                 "SELECT id, tenant_id, workspace_id, source_id, doc_id, chunk_index, text, embedding, metadata_json, "
-                "acl_allow_users, acl_allow_groups, acl_deny_users, acl_deny_groups FROM rag_chunks "
-                "WHERE tenant_id = ? AND workspace_id = ?", (tenant_id, workspace_id)).fetchall()
+                "acl_allow_users, acl_allow_groups, acl_deny_users, acl_deny_groups, updated_at FROM rag_chunks "
+                "WHERE tenant_id = ? AND workspace_id = ? ORDER BY rowid", (tenant_id, workspace_id)).fetchall()
             rows = [r for r in rows if len(r[7]) == 4 * dim]
+            cache = self._graph_path(tenant_id, workspace_id, dim, rows) if sc.hnsw is not None else None
+            if cache is not None and os.path.exists(cache):
+                from .. import _native
+
+                try:
+                    g = _native.rag.Hnsw.load(cache)
+                    if len(g) == len(rows) and g.dim == dim:
+                        sc.hnsw = g
+                except (RuntimeError, ValueError):
+                    pass  # unreadable: rebuilt and saved again below
             emb = np.frombuffer(b"".join(r[7] for r in rows), dtype="<f4").reshape(len(rows), dim)
             pub = np.zeros(len(rows), bool)
             for i, (r, e) in enumerate(zip(rows, emb)):
@@ -286,8 +302,39 @@ class SqliteVectorStore:
                 pub[i] = sc._public(acl)
             sc.add_matrix(emb, pub)
             self._scopes[key] = sc
+            if cache is not None:
+                rebuilt = len(sc.hnsw) < len(rows)
+                sc.flush()
+                if rebuilt:
+                    self._save_graph(sc.hnsw, cache)
         sc.flush()
         return sc
+
+    def _graph_path(self, tenant_id: str, workspace_id: str, dim: int, rows: list) -> Optional[str]:
+        if not self.index_dir:
+            return None
+        import hashlib
+
+        scope = hashlib.sha1(f"{tenant_id}\0{workspace_id}\0{dim}".encode()).hexdigest()[:16]
+        h = hashlib.sha1()
+        for r in rows:
+            h.update(f"{r[0]}\0{r[13]}\n".encode())
+        return os.path.join(self.index_dir, f"{scope}-{h.hexdigest()[:24]}.hnsw")
+
+    @staticmethod
+    def _save_graph(g, path: str) -> None:
+        d = os.path.dirname(path)
+        os.makedirs(d, exist_ok=True)
+        tmp = f"{path}.{os.getpid()}.tmp"
+        g.save(tmp)
+        os.replace(tmp, path)
+        prefix = os.path.basename(path).split("-")[0] + "-"
+        for f in os.listdir(d):  # older graphs of the same scope
+            if f.startswith(prefix) and f.endswith(".hnsw") and os.path.join(d, f) != path:
+                try:
+                    os.remove(os.path.join(d, f))
+                except OSError:
+                    pass
 
     def query(self, q: VectorQuery) -> list:
         import torch

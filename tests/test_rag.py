@@ -204,3 +204,40 @@ def test_resident_store_matches_exact_scores_and_sees_other_writers(tmp_path, in
     moved = rag.EmbeddedChunk("new", "t", "ws", "src0", "dn", 0, "new", (q * 3).tolist())
     other.upsert([moved])
     assert store.query(rag.VectorQuery(q.tolist(), 1, "t", "ws"))[0].chunk.id == "new"
+
+
+def test_hnsw_graph_is_saved_and_reloaded(tmp_path):
+    from kapsl_sdk_b200 import _native
+
+    X, _ = _clustered(3000, 32, 5)
+    h = _native.rag.Hnsw(32)
+    h.add(X)
+    h.remove(7)
+    p = str(tmp_path / "g.hnsw")
+    h.save(p)
+    g = _native.rag.Hnsw.load(p)
+    for q in X[:20]:
+        a, b = h.search(q, 10, 64), g.search(q, 10, 64)
+        assert np.array_equal(a[1], b[1]) and np.allclose(a[0], b[0])
+    bad = tmp_path / "bad.hnsw"
+    data = bytearray(open(p, "rb").read())
+    data[-4:] = (10 ** 6).to_bytes(4, "little", signed=True)  # a link to a node that does not exist
+    bad.write_bytes(bytes(data))
+    with pytest.raises(RuntimeError):
+        _native.rag.Hnsw.load(str(bad))
+    bad.write_bytes(bytes(data[:100]))
+    with pytest.raises(RuntimeError):
+        _native.rag.Hnsw.load(str(bad))
+    # the store saves a scope's graph and a later store loads it instead of rebuilding
+    db, idx = str(tmp_path / "v.db"), str(tmp_path / "graphs")
+    s1 = rag.SqliteVectorStore(db, index="hnsw", exact_below=10, index_dir=idx)
+    s1.upsert([rag.EmbeddedChunk(f"c{i}", "t", "ws", "s", "d", i, "x", X[i].tolist()) for i in range(3000)])
+    r1 = [r.chunk.id for r in s1.query(rag.VectorQuery(X[3].tolist(), 5, "t", "ws"))]
+    files = os.listdir(idx)
+    assert len(files) == 1
+    mtime = os.path.getmtime(os.path.join(idx, files[0]))
+    s2 = rag.SqliteVectorStore(db, index="hnsw", exact_below=10, index_dir=idx)
+    assert [r.chunk.id for r in s2.query(rag.VectorQuery(X[3].tolist(), 5, "t", "ws"))] == r1
+    assert os.listdir(idx) == files and os.path.getmtime(os.path.join(idx, files[0])) == mtime  # loaded
+    s2.upsert([rag.EmbeddedChunk("new", "t", "ws", "s", "d", 0, "x", X[3].tolist())])
+    assert s2.query(rag.VectorQuery(X[3].tolist(), 2, "t", "ws"))[0].chunk.id in ("new", "c3")
