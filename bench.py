@@ -85,9 +85,13 @@ def parse_args():
     p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
                    help="row-parallel reduction: fused NVLink kernels or the NCCL baseline")
     p.add_argument("--no-graph", action="store_true")
+    p.add_argument("--no-overlap", action="store_true",
+                   help="one engine step at a time (the host waits for each step's tokens before the next launch)")
     p.add_argument("--num-layers", type=int, default=0, help="override (testing only; invalid for the metric)")
     p.add_argument("--warmup-scale", type=float, default=1.0,
                    help="fraction of requests served by each warm-up step")
+    p.add_argument("--profile", action="store_true",
+                   help="per-step host/device breakdown of the timed region (stderr, one JSON line per rank)")
     a = p.parse_args()
     for k, v in WORKLOADS[a.workload].items():
         if getattr(a, k) is None:
@@ -201,6 +205,8 @@ def main():
     from kapsl_sdk_b200.models.config import get_preset
 
     cuda_ops()
+    if args.profile:
+        os.environ["KAPSL_LLM_PROFILE"] = "1"
     if args.parallel == "pd":
         return run_pd(args, dev, world, rank, local)
     cfg = get_preset(args.model)
@@ -212,7 +218,8 @@ def main():
 
         tp_comm = TPComm.from_world(mode=args.tp_mode)
     ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
-                        max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph)
+                        max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph,
+                        overlap_steps=not args.no_overlap)
     engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0)
     weight_gb = (torch.cuda.memory_allocated(dev) - engine.pool.storage.numel() * engine.pool.storage.element_size()) / 1e9
     # data-parallel replicas serve their own copy of the workload (weak scaling);
@@ -247,6 +254,12 @@ def main():
     barrier()
 
     # ---------------- device-timed region
+    if engine.profile is not None:
+        for k in list(engine.profile):
+            engine.profile[k] = 0
+        if tp_comm is not None and hasattr(tp_comm, "phase_times"):
+            tp_comm.phase_times(reset=True)
+    wall0 = time.perf_counter()
     launches0 = engine.runner.launches
     h2d0, d2h0 = engine.runner.stats["h2d_bytes"], engine.runner.stats["d2h_bytes"]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -262,6 +275,12 @@ def main():
         torch.cuda.synchronize()
         barrier()
     ms = start.elapsed_time(end)
+    if engine.profile is not None:
+        prof = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in engine.profile.items()}
+        prof.update(rank=rank, wall_s=round(time.perf_counter() - wall0, 3), device_ms=round(ms, 1))
+        if tp_comm is not None and hasattr(tp_comm, "phase_times"):
+            prof["tp_reduce"] = {k: round(v, 2) for k, v in tp_comm.phase_times().items()}
+        print(json.dumps({"profile": prof}), file=sys.stderr, flush=True)
     launches = engine.runner.launches - launches0
     h2d = (engine.runner.stats["h2d_bytes"] - h2d0) / args.steps
     d2h = (engine.runner.stats["d2h_bytes"] - d2h0) / args.steps

@@ -302,11 +302,8 @@ void launch_decode_attention(const CUtensorMap& tk, const CUtensorMap& tv, const
     throw std::runtime_error("decode attention: split-KV needs scratch buffers");
   auto kern = decode_attn_kernel<kDecWarps, kDecStages>;
   const size_t smem = decode_attn_smem_bytes();
-  static bool attr_set = false;
-  if (!attr_set) {
-    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  ensure_smem_attr(attr_devs, kern, smem);
   dim3 grid(nsplit, Hkv, B);
   kern<<<grid, kDecWarps * 32, smem, st>>>(tk, tv, q, q_stride, block_tables, max_blocks, ctx_lens, out,
                                            out_stride, part_o, part_lse, Hq, Hkv, scale * kLog2e, err);
@@ -531,11 +528,8 @@ void launch_prefill_attention(const CUtensorMap& tk, const CUtensorMap& tv, cons
   if (Hq % Hkv != 0) throw std::runtime_error("prefill attention: Hq must be a multiple of Hkv");
   auto kern = prefill_attn_kernel<kPreStages>;
   const size_t smem = prefill_attn_smem_bytes();
-  static bool attr_set = false;
-  if (!attr_set) {
-    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_set = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  ensure_smem_attr(attr_devs, kern, smem);
   kern<<<dim3(num_work, Hq), 128, smem, st>>>(tk, tv, q, q_stride, work, seq_info, block_tables, max_blocks, out,
                                               out_stride, Hq, Hkv, scale * kLog2e, err);
   KAPSL_LAUNCH_CHECK();

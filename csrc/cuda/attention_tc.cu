@@ -309,12 +309,8 @@ void launch_prefill_attention_tc(const CUtensorMap& q_map, const CUtensorMap& k_
   if (Hq % Hkv != 0 || Hq / Hkv > kRows) throw std::runtime_error("prefill attention (tc): bad head grouping");
   if (nwork <= 0) return;
   const size_t smem = prefill_attn_tc_smem_bytes();
-  static bool attr = false;
-  if (!attr) {
-    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
-    attr = true;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  ensure_smem_attr(attr_devs, prefill_attn_tc_kernel, smem);
   const float scale_log2 = scale * 1.4426950408889634f;
   prefill_attn_tc_kernel<<<dim3(nwork, Hkv), kThreads, smem, st>>>(q_map, k_map, v_map, work, seq_info,
                                                                    block_tables, max_blocks, Hq, Hkv, scale_log2,

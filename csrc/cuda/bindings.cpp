@@ -71,14 +71,27 @@ void silu_mul(Tensor out, Tensor x) {
   kapsl::launch_silu_mul(bf(out), bf(x), (int)x.size(0), (int)out.size(1), cur_stream());
 }
 
-void embedding(Tensor out, Tensor table, Tensor ids, int64_t vocab_start) {
+void embedding(Tensor out, Tensor table, Tensor ids, int64_t vocab_start, c10::optional<Tensor> src_rows,
+               c10::optional<Tensor> prev_tokens) {
   CHECK_DT(table, at::kBFloat16, "table");
   CHECK_DT(ids, at::kInt, "ids");
   TORCH_CHECK(table.is_contiguous() && out.is_contiguous() && out.size(1) == table.size(1), "embedding: layout");
   TORCH_CHECK(out.size(0) <= ids.numel(), "embedding: ids too short");
+  TORCH_CHECK(src_rows.has_value() == prev_tokens.has_value(), "embedding: src_rows and prev_tokens go together");
+  const int32_t* src = nullptr;
+  const int32_t* prev = nullptr;
+  int n_src = 0;
+  if (src_rows.has_value()) {
+    CHECK_DT((*src_rows), at::kInt, "src_rows");
+    CHECK_DT((*prev_tokens), at::kInt, "prev_tokens");
+    TORCH_CHECK(src_rows->is_contiguous() && prev_tokens->is_contiguous(), "embedding: src/prev layout");
+    src = src_rows->data_ptr<int32_t>();
+    prev = prev_tokens->data_ptr<int32_t>();
+    n_src = (int)src_rows->numel();
+  }
   const c10::cuda::CUDAGuard g(table.device());
   kapsl::launch_embedding(bf(out), bf(table), ids.data_ptr<int32_t>(), (int)out.size(0), (int)table.size(1),
-                          vocab_start, table.size(0), cur_stream());
+                          vocab_start, table.size(0), src, prev, n_src, cur_stream());
 }
 
 CUtensorMap cache_map(const Tensor& cache) {
@@ -490,7 +503,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("weight"), py::arg("eps"), py::arg("residual") = py::none());
   m.def("rope_kv_write", &rope_kv_write, "RoPE on q/k in place + paged KV write");
   m.def("silu_mul", &silu_mul, "SwiGLU: out = silu(x[:, :F]) * x[:, F:]");
-  m.def("embedding", &embedding, "embedding gather (rows outside the shard are zero)");
+  m.def("embedding", &embedding, "embedding gather (rows outside the shard are zero)", py::arg("out"),
+        py::arg("table"), py::arg("ids"), py::arg("vocab_start"), py::arg("src_rows") = py::none(),
+        py::arg("prev_tokens") = py::none());
   m.def("decode_num_splits", &decode_num_splits);
   m.def("decode_attention", &decode_attention, "paged split-KV decode attention");
   m.def("prefill_attention", &prefill_attention, "paged chunked-prefill attention");

@@ -10,6 +10,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <stdexcept>
 #include <string>
 
@@ -29,6 +30,22 @@ void note_launch(uint64_t n = 1);
   } while (0)
 
 #define KAPSL_LAUNCH_CHECK() KAPSL_CHECK_CUDA(cudaGetLastError())
+
+// Raises the dynamic shared-memory limit of `kern` to `smem` bytes on the
+// CURRENT device the first time a launch there needs it.  The attribute is
+// per device, so `done` (a static owned by the launch site) keeps one bit per
+// device ordinal: a process that drives several GPUs sets it on each of them.
+// Two threads racing on the same device both call cudaFuncSetAttribute, which
+// is idempotent; the bit is published with release order.
+template <typename Kernel>
+inline void ensure_smem_attr(std::atomic<uint64_t>& done, Kernel* kern, size_t smem) {
+  int dev = 0;
+  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = dev < 64 ? (1ull << dev) : 0ull;
+  if (bit != 0 && (done.load(std::memory_order_acquire) & bit)) return;
+  KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  if (bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
+}
 
 // 2-D bf16 tensor map (row-major, `rows` x `cols`, row pitch `pitch_elems`),
 // box = box_rows x box_cols, 128-byte swizzle.  Encoded through the driver

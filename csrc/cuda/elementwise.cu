@@ -7,6 +7,8 @@
 // attention in crates/kapsl-kernels/src/attention/mod.rs; RMSNorm/RoPE/KV
 // writes happen inside ONNX Runtime graphs (crates/kapsl-llm/src/engine.rs:3567)
 // and host KV packing (crates/kapsl-llm/src/kv_cache.rs:1423-1499).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -204,11 +206,20 @@ void launch_silu_mul(bf16* out, const bf16* x, int T, int F, cudaStream_t st) {
 }
 
 // --------------------------------------------------------------- embedding
+// Rows t < n_src whose src_rows[t] >= 0 take their token from prev_tokens
+// (the previous step's sampler output, still on the device) instead of ids[t]:
+// the host schedules and launches step k+1 before it has read step k's tokens.
 __global__ void embedding_kernel(bf16* __restrict__ out, const bf16* __restrict__ table,
                                  const int32_t* __restrict__ ids, int H, int64_t vocab_start,
-                                 int64_t vocab_rows) {
+                                 int64_t vocab_rows, const int32_t* __restrict__ src_rows,
+                                 const int32_t* __restrict__ prev_tokens, int n_src) {
   const int t = blockIdx.x;
-  const int64_t id = (int64_t)ids[t] - vocab_start;
+  int32_t tok = ids[t];
+  if (t < n_src) {
+    const int32_t r = src_rows[t];
+    if (r >= 0) tok = prev_tokens[r];
+  }
+  const int64_t id = (int64_t)tok - vocab_start;
   Vec8* o = reinterpret_cast<Vec8*>(out + (int64_t)t * H);
   const bool in_range = id >= 0 && id < vocab_rows;
   const Vec8* src = reinterpret_cast<const Vec8*>(table + (in_range ? id : 0) * H);
@@ -225,10 +236,14 @@ __global__ void embedding_kernel(bf16* __restrict__ out, const bf16* __restrict_
 }
 
 void launch_embedding(bf16* out, const bf16* table, const int32_t* ids, int T, int H, int64_t vocab_start,
-                      int64_t vocab_rows, cudaStream_t st) {
+                      int64_t vocab_rows, const int32_t* src_rows, const int32_t* prev_tokens, int n_src,
+                      cudaStream_t st) {
   if (T == 0) return;
   if (H % 8 != 0) throw std::runtime_error("embedding: hidden size must be a multiple of 8");
-  embedding_kernel<<<T, 256, 0, st>>>(out, table, ids, H, vocab_start, vocab_rows);
+  if (n_src > 0 && (src_rows == nullptr || prev_tokens == nullptr))
+    throw std::runtime_error("embedding: src_rows and prev_tokens are needed together");
+  embedding_kernel<<<T, 256, 0, st>>>(out, table, ids, H, vocab_start, vocab_rows, src_rows, prev_tokens,
+                                      std::min(n_src, T));
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

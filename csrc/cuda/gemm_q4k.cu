@@ -486,13 +486,8 @@ template <int TT, int EPI>
 void launch_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const Q4Args& a, int grid, int* err, cudaStream_t st) {
   auto kern = gemm_q4k_kernel<TT, EPI>;
   constexpr size_t smem = Cfg<TT>::SMEM;
-  static int attr_dev = -1;
-  int dev;
-  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  ensure_smem_attr(attr_devs, kern, smem);
   kern<<<grid, kThreads, smem, st>>>(tw, tx, a, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();

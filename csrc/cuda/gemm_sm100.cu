@@ -592,13 +592,8 @@ void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
                 int* err, cudaStream_t st) {
   auto kern = gemm2sm_kernel<STAGES, EPI, F32>;
   constexpr size_t smem = (size_t)STAGES * 2 * 128 * BK * 2 + 1024;
-  static int attr_dev = -1;
-  int dev;
-  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  ensure_smem_attr(attr_devs, kern, smem);
   kern<<<grid, kThreads, smem, st>>>(ta, tb, M, N, K, ep, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();
@@ -671,13 +666,8 @@ void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
                 int grid, int* err, cudaStream_t st) {
   auto kern = gemm_kernel<BN, STAGES, EPI, F32, GROUPED>;
   constexpr size_t smem = smem_bytes<BN, STAGES>();
-  static int attr_dev = -1;
-  int dev;
-  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
-  if (attr_dev != dev) {
-    KAPSL_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    attr_dev = dev;
-  }
+  static std::atomic<uint64_t> attr_devs{0};
+  ensure_smem_attr(attr_devs, kern, smem);
   kern<<<grid, kThreads, smem, st>>>(ta, tb, M, N, K, splits, ep, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();

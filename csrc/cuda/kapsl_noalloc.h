@@ -26,7 +26,8 @@
 //     partial rows before the combine pass reads them.  The `err` word, when
 //     given, must start at zero; the kernel sets it to 1 if a KV page load does
 //     not arrive within its bounded wait.  With err == NULL a static per-device
-//     word (zero when the module loads, never reset) is used instead.
+//     word (zero when the module loads) is used instead; read it, and reset it
+//     to zero, with kapsl_noalloc_read_and_clear_error() on the current device.
 //
 // Layouts match the tensor API: q [B, >= Hq*128] bf16 (row stride q_stride
 // elements), k/v cache [num_blocks, Hkv, 16, 128] bf16 contiguous,
@@ -64,6 +65,13 @@ int kapsl_decode_attention_noalloc(const void* q, int64_t q_stride, const void* 
 
 // Human-readable text of the last error on the calling thread ("" if none).
 const char* kapsl_noalloc_last_error(void);
+
+// Stores the current device's fallback error word (the one launches with
+// err == NULL write) into *out and resets it to zero.  The copies are
+// synchronous and use no device allocation; synchronise the stream of the
+// launches it should cover first (a non-blocking stream is not ordered with
+// these copies).  Returns a KAPSL_NOALLOC_* code.
+int kapsl_noalloc_read_and_clear_error(int* out);
 
 #ifdef __cplusplus
 }

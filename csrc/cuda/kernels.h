@@ -21,8 +21,10 @@ void launch_rope_kv_write(__nv_bfloat16* qkv, int64_t qkv_stride, const int32_t*
 
 void launch_silu_mul(__nv_bfloat16* out, const __nv_bfloat16* x, int T, int F, cudaStream_t st);
 
+// rows t < n_src with src_rows[t] >= 0 read their token id from prev_tokens[src_rows[t]]
 void launch_embedding(__nv_bfloat16* out, const __nv_bfloat16* table, const int32_t* ids, int T, int H,
-                      int64_t vocab_start, int64_t vocab_rows, cudaStream_t st);
+                      int64_t vocab_start, int64_t vocab_rows, const int32_t* src_rows, const int32_t* prev_tokens,
+                      int n_src, cudaStream_t st);
 
 size_t decode_attn_smem_bytes();
 int decode_attn_num_splits(int B, int Hkv, int max_ctx, int num_sms);

@@ -75,6 +75,27 @@ extern "C" int kapsl_decode_attention_noalloc_setup(void) {
 
 extern "C" const char* kapsl_noalloc_last_error(void) { return g_last_error; }
 
+extern "C" int kapsl_noalloc_read_and_clear_error(int* out) {
+  if (out == nullptr) return fail(KAPSL_NOALLOC_ERR_ARGS, "noalloc_read_and_clear_error: out is NULL");
+  DeviceSlots* s = nullptr;
+  int rc = setup_current(&s);
+  if (rc != KAPSL_NOALLOC_OK) return rc;
+  // Synchronous symbol copies on the legacy default stream; the caller has
+  // synchronised the stream of the launches this read covers.
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_noalloc_err, sizeof(int));
+  if (e == cudaSuccess) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_noalloc_err, &zero, sizeof(int));
+  }
+  if (e != cudaSuccess) {
+    std::snprintf(g_last_error, sizeof(g_last_error), "noalloc_read_and_clear_error: %s", cudaGetErrorString(e));
+    return KAPSL_NOALLOC_ERR_LAUNCH;
+  }
+  *out = v;
+  return KAPSL_NOALLOC_OK;
+}
+
 extern "C" int kapsl_decode_attention_noalloc(const void* q, int64_t q_stride, const void* k_cache,
                                               const void* v_cache, int64_t num_blocks, const int32_t* block_tables,
                                               int max_blocks, const int32_t* ctx_lens, void* out,

@@ -202,6 +202,12 @@ __global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
       for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch);
       if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, 5000000000ull)) atomicExch(a.err, 33);
       a.epoch_ctr[5] = (int64_t)globaltimer_ns();
+      // running sums over calls: barrier-1 wait (CTA 0), data phase (until the
+      // last CTA retires), barrier-2 wait, number of calls
+      a.epoch_ctr[8] += a.epoch_ctr[3] - a.epoch_ctr[2];
+      a.epoch_ctr[9] += a.epoch_ctr[4] - a.epoch_ctr[3];
+      a.epoch_ctr[10] += a.epoch_ctr[5] - a.epoch_ctr[4];
+      a.epoch_ctr[11] += 1;
       a.epoch_ctr[1] = 0;
       a.epoch_ctr[0] = epoch;
       __threadfence();

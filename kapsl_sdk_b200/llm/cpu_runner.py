@@ -1,7 +1,10 @@
 """Model runner for the CPU backend: same contract as
 :class:`~kapsl_sdk_b200.llm.model_runner.ModelRunner` (``admit``,
-``execute``, ``logits``) with host-side sampling that reproduces the reference
-sampler bit for bit (per-sequence LCG state kept on the sequence)."""
+``execute``, ``launch`` / ``collect``, ``logits``) with host-side sampling
+that reproduces the reference sampler bit for bit (per-sequence LCG state
+kept on the sequence).  ``launch`` computes the step at once; ``collect``
+hands its tokens over.  A decode input token that the engine has not applied
+yet (``Sequence.pending``) is taken from the previous launch's tokens."""
 from __future__ import annotations
 
 import time
@@ -21,6 +24,26 @@ class CPUModelRunner:
         self.launches = 0
         self.last_prepare_s = 0.0
         self.stats = {"steps": 0, "graph_steps": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+        self.prof = None
+        self._step_id = 0
+        self._prev = (0, np.zeros(0, dtype=np.int64))  # (step id, tokens) of the last launch
+
+    def launch(self, batch: ScheduledBatch):
+        from .model_runner import Inflight
+
+        sid, toks = self._prev
+        for s in batch.decode:  # its last output token is the previous launch's sample
+            if s.pending is not None:
+                if s.pending[0] != sid:
+                    raise RuntimeError("pending token from a step other than the previous one")
+                s.output_ids[-1] = int(toks[s.pending[1]])
+        seqs, toks = self.execute(batch)
+        self._step_id += 1
+        self._prev = (self._step_id, toks)
+        return Inflight(self._step_id, seqs, len(seqs), toks, None, None, "cpu", batch.num_tokens)
+
+    def collect(self, inf):
+        return inf.seqs, np.asarray(inf.h_out).copy()
 
     def admit(self, seqs: list) -> None:
         return None

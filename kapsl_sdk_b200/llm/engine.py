@@ -26,7 +26,7 @@ from .block_manager import make_allocator
 from .kv_cache import KVLayout, KVPool
 from .model_runner import ModelRunner
 from .scheduler import Scheduler
-from .sequence import SamplingParams, Sequence, SequenceStatus
+from .sequence import PENDING_TOKEN, SamplingParams, Sequence, SequenceStatus
 
 
 @dataclass
@@ -55,6 +55,9 @@ class EngineConfig:
     shareable_kv: bool = False          # pool mappable by another process (disaggregated decode side)
     preemption: str = "recompute"       # or "swap": preempted KV pages go to host memory
     swap_space_bytes: int = 4 << 30     # host memory for swapped pages
+    # launch step k+1 before reading step k's tokens: None = on for GPU engines (the CPU
+    # backend computes inside launch, so overlapping would only delay its tokens), True / False force
+    overlap_steps: Optional[bool] = None
 
 
 class LLMEngine:
@@ -119,6 +122,7 @@ class LLMEngine:
                                    e.max_model_len, e.preemption,
                                    e.swap_space_bytes // self.pool.layout.bytes_per_block())
         self._swapped_kv: dict = {}  # seq_id -> host copy of its computed pages
+        self._inflight = None  # launched step whose tokens the host has not applied yet
         self._seq_ids = itertools.count(1)
         self.sessions: dict[str, Sequence] = {}
         self.finished: list[Sequence] = []
@@ -137,6 +141,8 @@ class LLMEngine:
         if os.environ.get("KAPSL_LLM_PROFILE", os.environ.get("KAPSL_LLM_PROFILE_DECODE", "0")) == "1":
             self.profile = {"steps": 0, "decode_steps": 0, "tokens": 0, "schedule_s": 0.0, "prepare_s": 0.0,
                             "gpu_wait_s": 0.0, "postprocess_s": 0.0}
+            if hasattr(self.runner, "prof"):
+                self.runner.prof = self.profile  # the GPU runner adds launch / sync / device times
 
     # ------------------------------------------------------------ requests
     def _reserved_bytes(self) -> int:
@@ -210,6 +216,7 @@ class LLMEngine:
         return seq
 
     def abort(self, request_id: str) -> None:
+        self._drain()
         for s in self.scheduler.abort(request_id):
             s.finish_time = time.perf_counter()
             s.finish_reason = "aborted"
@@ -219,6 +226,7 @@ class LLMEngine:
         """Truncate the live request ``request_id`` to its first ``length`` tokens
         (prompt + output); generation then continues from there.  Returns the
         number of sequences changed."""
+        self._drain()
         table = getattr(self.runner, "rng_table", None)
         hit = [s for s in list(self.scheduler.running) + list(self.scheduler.waiting) + list(self.scheduler.swapped)
                if s.request_id == request_id]
@@ -249,7 +257,7 @@ class LLMEngine:
             self.rollback(s.request_id, length)
 
     def has_unfinished(self) -> bool:
-        return self.scheduler.has_work()
+        return self.scheduler.has_work() or self._inflight is not None
 
     # ---------------------------------------------------------------- step
     def _stop(self, s: Sequence, tok: int) -> Optional[str]:
@@ -262,7 +270,151 @@ class LLMEngine:
             return "length"
         return None
 
+    # ------------------------------------------------------------------
+    # Overlapped stepping (GPU runner): step() schedules and launches the next
+    # step BEFORE it waits for the one in flight, so the host's scheduling,
+    # input staging and kernel launches run while the GPU executes.  Sampled
+    # tokens a launched step has not returned yet are PENDING_TOKEN in
+    # ``output_ids``; the next step's decode rows take them from the device.
+    # While a step is in flight the scheduler does not preempt (a victim could
+    # hold such a token); a step that needs preemption waits for the in-flight
+    # one first.  Pipeline stages and the disaggregated prefill side
+    # (``kv_export``) keep the step-at-a-time path.
+    def _overlap_ok(self) -> bool:
+        on = self.ecfg.overlap_steps
+        if on is None:
+            on = self.device.type == "cuda"
+        return bool(on) and self.pp is None and self.kv_export is None
+
     def step(self) -> list[StepOutput]:
+        if self.pp is not None or self.kv_export is not None:
+            outs = self._drain()
+            return outs + self._step_serial()
+        prof = self.profile is not None
+        t0 = time.perf_counter() if prof else 0.0
+        overlap = self._overlap_ok()
+        if self._inflight is None or not overlap or self.scheduler.blocked:
+            outs = self._drain()
+            batch = self._schedule(True)
+            if batch.empty:
+                return outs
+            t1 = time.perf_counter() if prof else 0.0
+            inf = self._launch(batch)
+            if prof:
+                self._prof_step(batch, t1 - t0)
+            if overlap:
+                self._inflight = inf
+                return outs
+            return outs + self._complete(inf)
+        batch = self._schedule(False)
+        t1 = time.perf_counter() if prof else 0.0
+        new = self._launch(batch) if not batch.empty else None
+        if prof and new is not None:
+            self._prof_step(batch, t1 - t0)
+        old, self._inflight = self._inflight, new
+        return self._complete(old)
+
+    def _drain(self) -> list[StepOutput]:
+        """Wait for the step in flight (if any) and apply its tokens."""
+        if self._inflight is None:
+            return []
+        inf, self._inflight = self._inflight, None
+        return self._complete(inf)
+
+    def _schedule(self, allow_preempt: bool):
+        nv = self._nvtx
+        if nv:
+            torch.cuda.nvtx.range_push("schedule")
+        batch = self.scheduler.schedule(allow_preempt=allow_preempt)
+        if batch.preempted or batch.swap_in or batch.swap_out:
+            self._apply_preemptions(batch)
+        if nv:
+            torch.cuda.nvtx.range_pop()
+        return batch
+
+    def _prof_step(self, batch, schedule_s: float) -> None:
+        p = self.profile
+        p["steps"] += 1
+        p["schedule_s"] += schedule_s
+        p["prepare_s"] += self.runner.last_prepare_s
+        p["tokens"] += batch.num_tokens
+        if not batch.prefill:
+            p["decode_steps"] += 1
+
+    def _launch(self, batch):
+        """Launch ``batch`` and advance the host state as of its completion: computed
+        token counts, and a PENDING_TOKEN per sampling sequence."""
+        nv = self._nvtx
+        if nv:
+            torch.cuda.nvtx.range_push(f"launch T={batch.num_tokens} decode={len(batch.decode)}")
+        if batch.admitted:
+            self.runner.admit(batch.admitted)
+        inf = self.runner.launch(batch)
+        if nv:
+            torch.cuda.nvtx.range_pop()
+        for s in batch.decode:
+            s.num_computed += 1
+        for s, n in batch.prefill:
+            s.num_computed += n
+        max_len = self.ecfg.max_model_len
+        for r, s in enumerate(inf.seqs):
+            s.output_ids.append(PENDING_TOKEN)
+            s.pending = (inf.step_id, r)
+            inf.out_idx.append(len(s.output_ids) - 1)
+            if len(s.output_ids) >= s.params.max_new_tokens or s.length >= max_len:
+                s.pending_finish = True  # this token is its last whatever its value
+        return inf
+
+    def _complete(self, inf) -> list[StepOutput]:
+        """Wait for launched step ``inf``, put its tokens in place and retire the
+        sequences that stopped.  A sequence that stopped here while a later step
+        is already in flight drops that step's placeholder (its token is ignored
+        when that step completes: the sequence is finished by then)."""
+        prof = self.profile is not None
+        seqs, toks = self.runner.collect(inf)
+        now = time.perf_counter()
+        outs = []
+        for s, idx, tok in zip(seqs, inf.out_idx, toks.tolist()):
+            if s.status.finished:
+                continue
+            s.output_ids[idx] = tok
+            if s.pending is not None and s.pending[0] == inf.step_id:
+                s.pending = None
+            if s.first_token_time is None:
+                s.first_token_time = now
+            s.token_times.append(now)
+            reason = self._stop_at(s, tok, idx + 1)
+            if reason is not None:
+                del s.output_ids[idx + 1:]
+                s.num_computed = min(s.num_computed, s.length)
+                s.pending = None
+                s.pending_finish = False
+                s.finish_time = now
+                s.finish_reason = reason
+                self.scheduler.finish(s, SequenceStatus.FINISHED_STOPPED if reason == "stop"
+                                      else SequenceStatus.FINISHED_LENGTH, keep_blocks=False)
+                self.finished.append(s)
+            if s.on_token is not None:
+                s.on_token(s, tok, reason is not None)
+            outs.append(StepOutput(s.request_id, s, tok, reason is not None))
+        if prof:
+            self.profile["postprocess_s"] += time.perf_counter() - now
+        return outs
+
+    def _stop_at(self, s: Sequence, tok: int, n_out: int) -> Optional[str]:
+        """Stop reason after output token ``n_out`` (1-based) of ``s`` is ``tok``."""
+        p = s.params
+        if not p.ignore_eos and (tok in self.stop_ids or tok in p.stop_token_ids):
+            return "stop"
+        if n_out >= p.max_new_tokens:
+            return "length"
+        if len(s.prompt_ids) + n_out >= self.ecfg.max_model_len:
+            return "length"
+        return None
+
+    def _step_serial(self) -> list[StepOutput]:
+        """One step at a time: pipeline stages, the disaggregated prefill side and
+        the CPU runner."""
         prof = self.profile is not None
         t0 = time.perf_counter() if prof else 0.0
         nv = self._nvtx
@@ -387,6 +539,7 @@ class LLMEngine:
         }
 
     def shutdown(self) -> None:
+        self._drain()
         self.runner.release_graphs()
         if hasattr(self.pool, "close"):
             self.pool.close()

@@ -1,10 +1,18 @@
 """Builds device inputs for a scheduled batch, runs the model, samples.
 
-Host work per step is a handful of numpy writes into ONE pinned int32 staging
-buffer and ONE pinned int64 buffer, copied to the device with two async
-copies; every kernel input is a fixed view of the device copies.  Decode-only
-steps replay a CUDA graph captured per batch-size bucket (model forward +
-sampler + penalty-count update), so a decode step costs one graph launch.
+Host work per step is a handful of numpy writes into a pinned int32 staging
+buffer and a pinned int64 buffer, copied to the device with two async copies;
+every kernel input is a fixed view of the device copies.  Decode-only steps
+replay a CUDA graph captured per batch-size bucket (model forward + sampler +
+penalty-count update), so a decode step costs one graph launch.
+
+A step is split into :meth:`ModelRunner.launch` (fill, copy, launch, start
+the token read-back; returns at once) and :meth:`ModelRunner.collect` (wait
+for that step's tokens).  The engine launches step k+1 before it collects
+step k, so host scheduling overlaps the GPU: the staging and read-back
+buffers are double-buffered, and a decode row whose input token step k has
+sampled but the host has not read yet names that token's sampler row
+(``src`` region); the embedding kernel reads it from the device.
 
 Reference counterpart: the per-step input preparation, KV gather/pack and
 sampling of crates/kapsl-llm/src/engine.rs:3170-3914 (batched decode) and
@@ -46,12 +54,24 @@ class _Layout:
         self.topp = o; o += max_seqs
         self.pen = o; o += max_seqs
         self.adm_slot = o; o += max_seqs
+        self.src = o; o += max_seqs  # decode rows: previous step's sampler row of the input token, or -1
         self.n32 = o
         o = 0
         self.slots = o; o += max_tokens
         self.lidx = o; o += max_seqs
         self.adm_rng = o; o += max_seqs
         self.n64 = o
+
+
+class Inflight:
+    """A launched step: its sampling sequences (row order of ``out_tokens``), the
+    pinned buffer its tokens are read back into, and the event after that copy."""
+    __slots__ = ("step_id", "seqs", "R", "h_out", "done", "start", "kind", "num_tokens", "out_idx")
+
+    def __init__(self, step_id, seqs, R, h_out, done, start, kind, num_tokens):
+        self.step_id, self.seqs, self.R, self.h_out = step_id, seqs, R, h_out
+        self.done, self.start, self.kind, self.num_tokens = done, start, kind, num_tokens
+        self.out_idx: list = []
 
 
 class ModelRunner:
@@ -69,18 +89,21 @@ class ModelRunner:
         self.pad_slot = max_num_seqs
         W = (max_num_batched_tokens + 63) // 64 + max_num_seqs
         self.L = _Layout(self.max_tokens, S, self.max_blocks, W)
-        self.h32 = torch.zeros(self.L.n32, dtype=torch.int32, pin_memory=True)
-        self.h64 = torch.zeros(self.L.n64, dtype=torch.int64, pin_memory=True)
-        self.n32 = self.h32.numpy()
-        self.n64 = self.h64.numpy()
-        self.f32view = self.n32.view(np.float32)
+        # two pinned staging sets, used by alternate steps: while step k's copies may still
+        # be queued, step k+1 is filled into the other set
+        self._h32s = [torch.zeros(self.L.n32, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._h64s = [torch.zeros(self.L.n64, dtype=torch.int64, pin_memory=True) for _ in range(2)]
+        self._houts = [torch.zeros(S, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        self._buf = 1
+        self._select(0)
         self.d32 = torch.zeros(self.L.n32, dtype=torch.int32, device=self.device)
         self.d64 = torch.zeros(self.L.n64, dtype=torch.int64, device=self.device)
         # per-sequence device tables
         self.rng_table = torch.zeros(S, dtype=torch.int64, device=self.device)
         self.counts = torch.zeros(S, self.vocab, dtype=torch.int32, device=self.device)
         self.out_tokens = torch.zeros(S, dtype=torch.int32, device=self.device)
-        self.h_out = torch.zeros(S, dtype=torch.int32, pin_memory=True)
+        self._admit_seqs: list = []
+        self._step_id = 0
         self.use_graph = use_cuda_graph
         self.graph_sizes = sorted(graph_sizes or self._default_graph_sizes(max_num_seqs))
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
@@ -88,7 +111,19 @@ class ModelRunner:
         self.graph_pool = None
         self.launches = 0  # kernels launched by steps (eager count + graph replays x graph size)
         self.last_prepare_s = 0.0
+        # per-step host/device breakdown (a dict shared with the engine's profile, or None):
+        # launch_s host time issuing kernels, sync_s host wait for the step, device_s the
+        # step's span on the stream (CUDA events), split by graph / eager steps
+        self.prof: Optional[dict] = None
         self.stats = {"steps": 0, "graph_steps": 0, "h2d_bytes": 0, "d2h_bytes": 0}
+
+    def _select(self, buf: int) -> None:
+        """Make staging set ``buf`` the one _fill writes and _h2d copies."""
+        self._buf = buf
+        self.h32, self.h64, self.h_out = self._h32s[buf], self._h64s[buf], self._houts[buf]
+        self.n32 = self.h32.numpy()
+        self.n64 = self.h64.numpy()
+        self.f32view = self.n32.view(np.float32)
 
     @staticmethod
     def _default_graph_sizes(max_seqs: int) -> list[int]:
@@ -110,9 +145,11 @@ class ModelRunner:
     def _bt(self, nrows: int) -> torch.Tensor:
         return self.d32[self.L.bt:self.L.bt + nrows * self.max_blocks].view(nrows, self.max_blocks)
 
-    def _forward_batch(self, T: int, S: int, R: int, Bd: int, max_ctx: int, nwork: int, nsplit: int) -> ForwardBatch:
+    def _forward_batch(self, T: int, S: int, R: int, Bd: int, max_ctx: int, nwork: int, nsplit: int,
+                       nsrc: int = 0) -> ForwardBatch:
         L = self.L
         return ForwardBatch(
+            src_rows=self._v32(L.src, nsrc) if nsrc else None, prev_tokens=self.out_tokens if nsrc else None,
             input_ids=self._v32(L.ids, T), positions=self._v32(L.pos, T), slots=self.d64[L.slots:L.slots + T],
             block_tables=self._bt(max(S, 1)), ctx_lens=self._v32(L.ctx, max(S, 1)),
             logits_idx=self.d64[L.lidx:L.lidx + R], num_tokens=T, num_decode=Bd, max_decode_ctx=max_ctx,
@@ -144,7 +181,12 @@ class ModelRunner:
             nbs = np.array([len(b) for b in bts], dtype=np.int64)
             flat = np.concatenate(bts)
             starts = np.cumsum(nbs) - nbs
-            n32[L.ids:L.ids + Bd] = [s.output_ids[-1] if s.output_ids else s.prompt_ids[-1] for s in dec]
+            # an input token that the previous step sampled and the host has not read yet
+            # (``pending``) is taken on the device from that step's sampler row
+            pend = [s.pending[1] if s.pending is not None else -1 for s in dec]
+            n32[L.src:L.src + Bd] = pend
+            n32[L.ids:L.ids + Bd] = [0 if p >= 0 else (s.output_ids[-1] if s.output_ids else s.prompt_ids[-1])
+                                     for s, p in zip(dec, pend)]
             n32[L.pos:L.pos + Bd] = pos
             n64[L.slots:L.slots + Bd] = flat[starts + pos // bs].astype(np.int64) * bs + pos % bs
             n32[L.ctx:L.ctx + Bd] = lens
@@ -153,6 +195,7 @@ class ModelRunner:
         Bpad = max(Bd, pad_to)
         if Bpad > Bd:  # CUDA-graph padding rows: no KV write, 1-token context on block 0
             n32[L.ids + Bd:L.ids + Bpad] = 0
+            n32[L.src + Bd:L.src + Bpad] = -1
             n32[L.pos + Bd:L.pos + Bpad] = 0
             n64[L.slots + Bd:L.slots + Bpad] = -1
             n32[L.ctx + Bd:L.ctx + Bpad] = 1
@@ -209,7 +252,12 @@ class ModelRunner:
         self.stats["h2d_bytes"] += self.h32.numel() * 4 + self.h64.numel() * 8
 
     def admit(self, seqs: list) -> None:
-        """Initialise per-slot device state (LCG seed, penalty counts) for new sequences."""
+        """Initialise per-slot device state (LCG seed, penalty counts) for new
+        sequences; applied on the stream by the next :meth:`launch`, before its kernels."""
+        self._admit_seqs.extend(seqs)
+
+    def _write_admissions(self) -> None:
+        seqs, self._admit_seqs = self._admit_seqs, []
         if not seqs:
             return
         L = self.L
@@ -217,9 +265,8 @@ class ModelRunner:
             self.n32[L.adm_slot + i] = s.slot
             st = s.rng_state
             self.n64[L.adm_rng + i] = st - (1 << 64) if st >= (1 << 63) else st
-        n = len(seqs)
-        # (H2D of the staging buffers happens in execute(); admission runs after it on the stream)
-        self._pending_admit = n
+        # (the H2D copy of the staging set happens next; admission runs after it on the stream)
+        self._pending_admit = len(seqs)
         self._admit_prompts = [(s.slot, s.prompt_ids + s.output_ids) for s in seqs]
 
     def reset_slots(self, seqs: list) -> None:
@@ -255,7 +302,12 @@ class ModelRunner:
 
     # ------------------------------------------------------------ execute
     def execute(self, batch: ScheduledBatch) -> tuple[list, np.ndarray]:
-        """Run one step; returns (sequences that sampled, their new tokens)."""
+        """Run one step to completion; returns (sequences that sampled, their new tokens)."""
+        return self.collect(self.launch(batch))
+
+    def launch(self, batch: ScheduledBatch) -> "Inflight":
+        """Fill and copy the step's inputs, launch its kernels and the read-back of
+        its sampled tokens; returns without waiting for the GPU."""
         decode_only = not batch.prefill and len(batch.decode) > 0
         pad_to = 0
         gsize = 0
@@ -268,10 +320,18 @@ class ModelRunner:
                     gsize = pad_to = bucket
         tp0 = time.perf_counter()
         c0 = launch_count()
+        self._select(self._buf ^ 1)  # the set used two steps ago: its copies have completed
         T, S, R, Rpad, Bd, Bpad, nwork, sample_seqs = self._fill(batch, pad_to)
+        self._write_admissions()
         self._h2d()
         self._apply_admissions()
-        self.last_prepare_s = time.perf_counter() - tp0
+        tl0 = time.perf_counter()
+        self.last_prepare_s = tl0 - tp0
+        prof = self.prof
+        ev0 = None
+        if prof is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
         if gsize:
             g = self.graphs.get(gsize)
             if g is None:
@@ -284,16 +344,35 @@ class ModelRunner:
             nsplit = 0
             if bucket:  # same split-KV policy as the captured graphs, so both paths agree bitwise
                 nsplit = self._graph_splits(bucket)
-            fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, nsplit)
+            fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, nsplit, nsrc=Bpad)
             logits = self.model.forward(fb, self.pool.k, self.pool.v)
             if logits is not None:  # None: an earlier pipeline stage (the last stage samples)
                 self._sample(logits, R)
             self.launches += launch_count() - c0
         self.h_out[:R].copy_(self.out_tokens[:R], non_blocking=True)
-        torch.cuda.current_stream(self.device).synchronize()
+        done = torch.cuda.Event(enable_timing=prof is not None)
+        done.record()
+        self._step_id += 1
         self.stats["d2h_bytes"] += R * 4
         self.stats["steps"] += 1
-        return sample_seqs, self.h_out[:R].numpy().copy()
+        inf = Inflight(self._step_id, sample_seqs, R, self.h_out, done, ev0, "graph" if gsize else "eager", T)
+        if prof is not None:
+            self._tally(f"{inf.kind}_launch_s", time.perf_counter() - tl0)
+        return inf
+
+    def collect(self, inf: "Inflight") -> tuple[list, np.ndarray]:
+        """Wait for step ``inf`` and return (its sampling sequences, their tokens)."""
+        t0 = time.perf_counter()
+        inf.done.synchronize()
+        if self.prof is not None:
+            self._tally("sync_s", time.perf_counter() - t0)
+            self._tally(f"{inf.kind}_steps", 1)
+            self._tally(f"{inf.kind}_tokens", inf.num_tokens)
+            self._tally(f"{inf.kind}_device_s", inf.start.elapsed_time(inf.done) / 1e3)
+        return inf.seqs, inf.h_out[:inf.R].numpy().copy()
+
+    def _tally(self, key: str, v) -> None:
+        self.prof[key] = self.prof.get(key, 0) + v
 
     def logits(self, batch: ScheduledBatch) -> torch.Tensor:
         """Eager forward of ``batch`` returning the fp32 logits of its sampling
@@ -301,7 +380,7 @@ class ModelRunner:
         T, S, R, Rpad, Bd, Bpad, nwork, _ = self._fill(batch, 0)
         self._h2d()
         max_ctx = int(self.n32[self.L.ctx:self.L.ctx + Bd].max()) if Bd else 0
-        fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, 0)
+        fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, 0, nsrc=Bpad)
         out = self.model.forward(fb, self.pool.k, self.pool.v)
         torch.cuda.current_stream(self.device).synchronize()
         return out
@@ -314,7 +393,7 @@ class ModelRunner:
         staging views, already filled for this step)."""
         max_ctx = self.max_blocks * self.bs
         nsplit = self._graph_splits(B)
-        fb = self._forward_batch(B, B, B, B, max_ctx, 0, nsplit)
+        fb = self._forward_batch(B, B, B, B, max_ctx, 0, nsplit, nsrc=B)
         # warm up once outside capture (allocator, function attributes)
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))

@@ -66,6 +66,8 @@ class Scheduler:
         self.swap_capacity = swap_blocks if preemption == "swap" else 0
         self.swap_used = 0
         self.swapped: deque[Sequence] = deque()
+        self._allow_preempt = True
+        self.blocked = False
         self.num_swap_out = 0
         self.num_swap_in = 0
 
@@ -104,6 +106,8 @@ class Scheduler:
         return (seq.num_computed + self.bs - 1) // self.bs
 
     def _preempt_one(self, protect: Sequence, scheduled: set, out: ScheduledBatch) -> bool:
+        if not self._allow_preempt:
+            return False
         victims = [s for s in self.running if s is not protect and id(s) not in scheduled]
         if not victims:
             return False
@@ -147,7 +151,12 @@ class Scheduler:
             self.num_swap_in += 1
 
     # ------------------------------------------------------------- schedule
-    def schedule(self) -> ScheduledBatch:
+    def schedule(self, allow_preempt: bool = True) -> ScheduledBatch:
+        """Build the next step.  ``allow_preempt=False`` (a step is still in flight,
+        so running sequences may hold tokens the host has not seen): a sequence
+        that cannot grow is skipped for this step instead of preempting another."""
+        self._allow_preempt = allow_preempt
+        self.blocked = False  # a running sequence could not grow and preemption was not allowed
         out = ScheduledBatch()
         budget = self.max_tokens
         scheduled: set = set()
@@ -161,6 +170,8 @@ class Scheduler:
                 continue  # preempted while making room for an earlier one
             if budget <= 0:
                 break
+            if seq.pending_finish:
+                continue  # its last token is in flight; it finishes when the token lands
             if not seq.in_prefill:
                 ok = True
                 while not self._grow(seq, seq.length):
@@ -168,8 +179,9 @@ class Scheduler:
                         ok = False
                         break
                 if not ok:
-                    if not scheduled:
+                    if not scheduled and allow_preempt:
                         raise OutOfBlocks("KV pool too small for a single sequence")
+                    self.blocked = not allow_preempt
                     continue
                 out.decode.append(seq)
                 scheduled.add(id(seq))
@@ -184,8 +196,9 @@ class Scheduler:
                         ok = False
                         break
                 if not ok:
-                    if not scheduled:
+                    if not scheduled and allow_preempt:
                         raise OutOfBlocks("KV pool too small for a single sequence")
+                    self.blocked = not allow_preempt
                     continue
                 out.prefill.append((seq, n))
                 scheduled.add(id(seq))

@@ -33,6 +33,9 @@ class SamplingParams:
         return cls(max_new_tokens=max_new_tokens, temperature=0.0, top_p=1.0, top_k=0, repetition_penalty=1.0, **kw)
 
 
+PENDING_TOKEN = -1  # placeholder in output_ids for a token sampled by a step still in flight
+
+
 class SequenceStatus(enum.Enum):
     WAITING = "waiting"
     RUNNING = "running"
@@ -66,6 +69,10 @@ class Sequence:
     session_id: Optional[str] = None
     on_token: Optional[Callable] = None
     finish_reason: Optional[str] = None
+    # the last output token is still on the device: (step id, sampler row) of the launched
+    # step that samples it; output_ids holds PENDING_TOKEN there until the step completes
+    pending: Optional[tuple] = None
+    pending_finish: bool = False   # the in-flight token is its last (length limit): not scheduled again
     _bt: Optional[tuple] = field(default=None, repr=False)  # (block_ids list, its length, int32 copy)
 
     def block_table(self) -> np.ndarray:

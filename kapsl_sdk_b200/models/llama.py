@@ -284,6 +284,10 @@ class ForwardBatch:
     pf_work: Optional[torch.Tensor] = None      # int32 [n, 2]
     pf_seq_info: Optional[torch.Tensor] = None  # int32 [S_pf, 4]
     decode_splits: int = 0
+    # tokens still on the device: row t < len(src_rows) with src_rows[t] >= 0
+    # embeds prev_tokens[src_rows[t]] (the previous step's sample) instead of input_ids[t]
+    src_rows: Optional[torch.Tensor] = None     # int32 [n]
+    prev_tokens: Optional[torch.Tensor] = None  # int32 [R_prev]
 
 
 class CausalLM:
@@ -328,7 +332,8 @@ class CausalLM:
             hin = st.recv_hidden(T, cfg.hidden_size, torch.bfloat16, self.device)
             h = hin if h is None else h.copy_(hin)
         else:
-            h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start, out=h)
+            h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start, out=h, src_rows=fb.src_rows,
+                              prev_tokens=fb.prev_tokens)
         attn = torch.empty(T, self.hq * self.D, dtype=torch.bfloat16, device=self.device)
         x = torch.empty_like(h)
         for li, L in enumerate(self.w.layers):

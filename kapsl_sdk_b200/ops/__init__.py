@@ -65,10 +65,14 @@ def silu_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tenso
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
-              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+              out: Optional[torch.Tensor] = None, src_rows: Optional[torch.Tensor] = None,
+              prev_tokens: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Rows of ``table`` for ``ids``.  With ``src_rows``: row ``t < len(src_rows)``
+    whose ``src_rows[t] >= 0`` looks up ``prev_tokens[src_rows[t]]`` instead of
+    ``ids[t]`` (a token the previous step sampled and the host has not read yet)."""
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
-    cuda_ops().embedding(out, table, ids, int(vocab_start))
+    cuda_ops().embedding(out, table, ids, int(vocab_start), src_rows, prev_tokens)
     return out
 
 

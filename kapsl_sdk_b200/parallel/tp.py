@@ -108,8 +108,10 @@ class TPComm:
                        if self.ep_rows else None)
         self.hidden_buf = c.tensor_from_ptr(base + off_h, [rows_pad, hidden], "bfloat16", dev)
         self.partial_buf = c.tensor_from_ptr(base, [rows_pad, hidden], "bfloat16", dev)  # pull mode: own partial
-        # [0] barrier epoch, [1] finished-CTA count, [2..5] %globaltimer phase stamps of the last call
-        self.epoch = torch.zeros(8, dtype=torch.int64, device=self.device)
+        # [0] barrier epoch, [1] finished-CTA count, [2..5] %globaltimer phase stamps of the last
+        # call, [8..11] running sums (ns) of the barrier-1 wait, the data phase, the barrier-2
+        # wait, and the number of calls of the pull reduction (see :meth:`phase_times`)
+        self.epoch = torch.zeros(16, dtype=torch.int64, device=self.device)
         torch.cuda.synchronize(self.device)
         self.dist.barrier(group=self.group)
 
@@ -124,6 +126,20 @@ class TPComm:
                 c.symm_close(b)
         c.symm_free(self.bufs["base"])
         self.bufs = None
+
+    def phase_times(self, reset: bool = False) -> dict:
+        """Accumulated device-side phase times of the fused pull reduction
+        (read from the kernel's %globaltimer stamps): mean microseconds per
+        call of the first barrier, the data phase and the second barrier."""
+        if self.bufs is None:
+            return {}
+        v = self.epoch[8:12].tolist()
+        n = max(int(v[3]), 1)
+        out = {"calls": int(v[3]), "barrier1_us": v[0] / n / 1e3, "data_us": v[1] / n / 1e3,
+               "barrier2_us": v[2] / n / 1e3}
+        if reset:
+            self.epoch[8:12].zero_()
+        return out
 
     # -------------------------------------------------------------- helpers
     def min_int(self, v: int) -> int:

@@ -316,9 +316,13 @@ class SqliteVectorStore:
         import hashlib
 
         scope = hashlib.sha1(f"{tenant_id}\0{workspace_id}\0{dim}".encode()).hexdigest()[:16]
+        # the key covers each row's id, update time AND embedding bytes: an
+        # upsert within the same second keeps id, time and row order, so only
+        # the vector itself tells a stale graph from a current one
         h = hashlib.sha1()
         for r in rows:
             h.update(f"{r[0]}\0{r[13]}\n".encode())
+            h.update(r[7])
         return os.path.join(self.index_dir, f"{scope}-{h.hexdigest()[:24]}.hnsw")
 
     @staticmethod

@@ -83,6 +83,30 @@ def test_generate_graph_matches_eager():
     assert outs[0] == outs[1]
 
 
+def test_overlapped_steps_match_serial_steps():
+    """Launching step k+1 before step k's tokens reach the host (decode inputs
+    taken from the previous step's sampler output on the device) gives the same
+    tokens as one step at a time: same batches (all requests admitted at once,
+    equal lengths), seeded top-k/top-p sampling with repetition penalty."""
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+
+    cfg = small_cfg()
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (40, 300, 17, 129, 3, 64)]
+    outs = []
+    for overlap in (False, True):
+        eng = make_engine(cfg, overlap_steps=overlap)
+        seqs = [eng.add_request(f"r{i}", p, SamplingParams(max_new_tokens=20, temperature=0.8, top_k=40, top_p=0.9,
+                                                             repetition_penalty=1.1, seed=11 + i, ignore_eos=True))
+                for i, p in enumerate(prompts)]
+        while eng.has_unfinished():
+            eng.step()
+        assert all(len(s.output_ids) == 20 and s.pending is None for s in seqs)
+        outs.append([s.output_ids for s in seqs])
+        eng.shutdown()
+    assert outs[0] == outs[1]
+
+
 def test_prefix_cache_reuse_and_preemption():
     from kapsl_sdk_b200.llm.sequence import SamplingParams
 

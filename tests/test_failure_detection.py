@@ -31,7 +31,7 @@ HB_WORKER = textwrap.dedent("""
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     dist.init_process_group("gloo", timeout=timedelta(seconds=20))
     store = dist.distributed_c10d._get_default_store()
-    hb = HeartbeatMonitor(store, rank, world, interval_s=0.2, timeout_s=2.0).start()
+    hb = HeartbeatMonitor(store, rank, world, interval_s=0.2, timeout_s=3.0).start()
     dist.barrier()
     if rank == 2:
         os._exit(17)  # crash between steps, no cleanup

@@ -241,3 +241,17 @@ def test_hnsw_graph_is_saved_and_reloaded(tmp_path):
     assert os.listdir(idx) == files and os.path.getmtime(os.path.join(idx, files[0])) == mtime  # loaded
     s2.upsert([rag.EmbeddedChunk("new", "t", "ws", "s", "d", 0, "x", X[3].tolist())])
     assert s2.query(rag.VectorQuery(X[3].tolist(), 2, "t", "ws"))[0].chunk.id in ("new", "c3")
+
+
+def test_hnsw_saved_graph_rebuilt_after_same_second_reupsert(tmp_path):
+    """Re-upserting the last chunk with a new vector keeps its id, row order and
+    (within one second) its update time; the saved graph must still be rebuilt."""
+    X, _ = _clustered(600, 16, 4)
+    db, idx = str(tmp_path / "v.db"), str(tmp_path / "graphs")
+    s1 = rag.SqliteVectorStore(db, index="hnsw", exact_below=10, index_dir=idx)
+    s1.upsert([rag.EmbeddedChunk(f"c{i}", "t", "ws", "s", "d", i, "x", X[i].tolist()) for i in range(600)])
+    s1.query(rag.VectorQuery(X[0].tolist(), 3, "t", "ws"))  # builds and saves the graph
+    far = -X[0] * 5.0
+    s1.upsert([rag.EmbeddedChunk("c599", "t", "ws", "s", "d", 599, "x", far.tolist())])
+    s2 = rag.SqliteVectorStore(db, index="hnsw", exact_below=10, index_dir=idx)
+    assert s2.query(rag.VectorQuery(far.tolist(), 1, "t", "ws"))[0].chunk.id == "c599"

@@ -37,7 +37,12 @@ def reference_fill(self, batch, pad_to=0):
     Bd = len(dec)
     for i, s in enumerate(dec):
         pos = s.length - 1
-        n32[L.ids + i] = s.output_ids[-1] if s.output_ids else s.prompt_ids[-1]
+        if s.pending is not None:  # input token still on the device: its sampler row
+            n32[L.src + i] = s.pending[1]
+            n32[L.ids + i] = 0
+        else:
+            n32[L.src + i] = -1
+            n32[L.ids + i] = s.output_ids[-1] if s.output_ids else s.prompt_ids[-1]
         n32[L.pos + i] = pos
         n64[L.slots + i] = s.block_ids[pos // self.bs] * self.bs + pos % self.bs
         n32[L.ctx + i] = s.length
@@ -46,6 +51,7 @@ def reference_fill(self, batch, pad_to=0):
     Bpad = max(Bd, pad_to)
     for i in range(Bd, Bpad):
         n32[L.ids + i] = 0
+        n32[L.src + i] = -1
         n32[L.pos + i] = 0
         n64[L.slots + i] = -1
         n32[L.ctx + i] = 1
@@ -114,9 +120,12 @@ def _seq(rnd, i, bs=16):
 def _batch(rnd, seqs):
     b = ScheduledBatch()
     for s in seqs:
+        s.pending = None
         if s.output_ids and rnd.random() < 0.6:
             s.num_computed = s.length - 1
             b.decode.append(s)
+            if rnd.random() < 0.5:  # last token sampled by the step still in flight
+                s.pending = (7, rnd.randrange(16))
         else:
             s.num_computed = rnd.randint(0, s.length - 1)
             b.prefill.append((s, rnd.randint(1, s.length - s.num_computed)))

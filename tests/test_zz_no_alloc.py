@@ -2,11 +2,12 @@
 
 Calls the exported ``kapsl_decode_attention_noalloc`` symbol of the CUDA
 extension through ctypes and compares its output with the tensor API
-(``ops.decode_attention``, which takes caller-allocated split scratch) on two
-consecutive calls.  The file name sorts last so the test also runs after the
-rest of the GPU suite in one process.
+(``ops.decode_attention``, which takes caller-allocated split scratch) and with
+the plain fp32 attention oracle on two consecutive calls.  The file name sorts
+last so the test also runs after the rest of the GPU suite in one process.
 """
 import ctypes
+import math
 import random
 
 import pytest
@@ -29,7 +30,15 @@ def _lib():
                    ctypes.c_void_p]
     lib.kapsl_decode_attention_noalloc_setup.restype = ctypes.c_int
     lib.kapsl_noalloc_last_error.restype = ctypes.c_char_p
+    lib.kapsl_noalloc_read_and_clear_error.restype = ctypes.c_int
+    lib.kapsl_noalloc_read_and_clear_error.argtypes = [ctypes.POINTER(ctypes.c_int)]
     return lib
+
+
+def _fallback_err(lib) -> int:
+    v = ctypes.c_int(-1)
+    assert lib.kapsl_noalloc_read_and_clear_error(ctypes.byref(v)) == 0, lib.kapsl_noalloc_last_error()
+    return v.value
 
 
 def _case(dev, lens, seed):
@@ -52,6 +61,20 @@ def _case(dev, lens, seed):
     return q, kc, vc, bt.to(dev), ctx
 
 
+def _oracle(q, kc, vc, bt, lens):
+    """fp32 attention of each row over its gathered pages: [B, HQ, D]."""
+    from kapsl_sdk_b200.ops import reference as ref
+
+    out = []
+    kcc, vcc, btc = kc.cpu(), vc.cpu(), bt.cpu()
+    for i, L in enumerate(lens):
+        blocks = btc[i, :(L + 15) // 16].tolist()
+        k = ref.gather_paged(kcc, blocks, L)
+        v = ref.gather_paged(vcc, blocks, L)
+        out.append(ref.attention(q[i].view(1, HQ, D).cpu(), k, v, 1 / math.sqrt(D), L - 1)[0])
+    return torch.stack(out)
+
+
 def _call(lib, q, kc, vc, bt, ctx, out, nsplit, err):
     st = torch.cuda.current_stream(q.device).cuda_stream
     return lib.kapsl_decode_attention_noalloc(
@@ -72,12 +95,14 @@ def test_noalloc_matches_tensor_api():
     for lens, nsplit, seed in cases:
         q, kc, vc, bt, ctx = _case(dev, lens, seed)
         want = ops.decode_attention(q, kc, vc, bt, ctx, HQ, HKV, num_splits=nsplit)
+        exact = _oracle(q, kc, vc, bt, lens)
         for _ in range(2):  # two consecutive calls reuse the same static scratch
             out = torch.full_like(want, float("nan"))
             rc = _call(lib, q, kc, vc, bt, ctx, out, nsplit, err)
             assert rc == 0, lib.kapsl_noalloc_last_error()
             torch.cuda.synchronize()
             torch.testing.assert_close(out.float(), want.float(), atol=2e-2, rtol=2e-2)
+            torch.testing.assert_close(out.float().cpu().view(len(lens), HQ, D), exact, atol=2e-2, rtol=2e-2)
         assert int(err.item()) == 0
 
 
@@ -88,8 +113,16 @@ def test_noalloc_rejects_oversize():
     q, kc, vc, bt, ctx = _case(dev, [40, 50], 2)
     out = torch.zeros(2, HQ * D, device=dev, dtype=torch.bfloat16)
     # 2 rows * 28 heads * 64 splits is within the limit; a huge batch is not
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    assert _call(lib, q, kc, vc, bt, ctx, out, 64, err) == 0
+    torch.cuda.synchronize()
+    assert int(err.item()) == 0
+    torch.testing.assert_close(out.float().cpu().view(2, HQ, D), _oracle(q, kc, vc, bt, [40, 50]), atol=2e-2,
+                               rtol=2e-2)
+    # without an err pointer the static per-device word is used; it reads back zero and is cleared
     assert _call(lib, q, kc, vc, bt, ctx, out, 64, None) == 0
     torch.cuda.synchronize()
+    assert _fallback_err(lib) == 0
     big = 100000
     rc = lib.kapsl_decode_attention_noalloc(
         q.data_ptr(), q.stride(0), kc.data_ptr(), vc.data_ptr(), kc.shape[0], bt.data_ptr(), bt.shape[1],
@@ -97,3 +130,21 @@ def test_noalloc_rejects_oversize():
         torch.cuda.current_stream(dev).cuda_stream)
     assert rc == 1
     assert b"exceed the static scratch limit" in lib.kapsl_noalloc_last_error()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_noalloc_second_device():
+    """A call on cuda:1 after calls on cuda:0: the scratch address and the
+    shared-memory attribute are per device."""
+    lib = _lib()
+    for idx in (0, 1):
+        dev = torch.device("cuda", idx)
+        with torch.cuda.device(dev):
+            q, kc, vc, bt, ctx = _case(dev, [300, 17, 1025], 3)
+            out = torch.full((3, HQ * D), float("nan"), device=dev, dtype=torch.bfloat16)
+            err = torch.zeros(1, dtype=torch.int32, device=dev)
+            assert _call(lib, q, kc, vc, bt, ctx, out, 8, err) == 0, lib.kapsl_noalloc_last_error()
+            torch.cuda.synchronize(dev)
+            assert int(err.item()) == 0
+            torch.testing.assert_close(out.float().cpu().view(3, HQ, D), _oracle(q, kc, vc, bt, [300, 17, 1025]),
+                                       atol=2e-2, rtol=2e-2)
