@@ -185,39 +185,125 @@ int64_t prefill_attn_tc_tokens(int64_t Hq, int64_t Hkv) {
 }
 
 // rng and counts are per-sequence tables indexed by slots[row] (row itself when slots is None).
-void sample(Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, c10::optional<Tensor> rep_penalty,
-            c10::optional<Tensor> counts, c10::optional<Tensor> slots, Tensor rng, Tensor out) {
+kapsl::SampleLaunch sample_args(Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p,
+                                c10::optional<Tensor> rep_penalty, c10::optional<Tensor> counts,
+                                c10::optional<Tensor> slots, Tensor rng, Tensor out, c10::optional<Tensor> occ,
+                                c10::optional<Tensor> occ_n, int64_t vocab_start, int64_t vocab_size,
+                                const std::vector<int64_t>& cand_ptrs, const std::vector<int64_t>& flag_ptrs,
+                                int64_t rank, int64_t b_cap, c10::optional<Tensor> ctr, int64_t timeout_ns,
+                                Tensor err) {
   CHECK_DT(logits, at::kFloat, "logits");
   TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "sample: logits [B, V]");
   CHECK_DT(rng, at::kLong, "rng");
   CHECK_DT(out, at::kInt, "out");
+  CHECK_DT(err, at::kInt, "err");
   const int B = (int)logits.size(0);
   TORCH_CHECK(temperature.numel() >= B && top_k.numel() >= B && top_p.numel() >= B && out.numel() >= B,
               "sample: per-row parameter arrays too short");
   TORCH_CHECK(slots.has_value() || rng.numel() >= B, "sample: rng table too short");
-  const float* rp = rep_penalty.has_value() ? rep_penalty->data_ptr<float>() : nullptr;
-  const int32_t* cn = counts.has_value() ? counts->data_ptr<int32_t>() : nullptr;
-  const int32_t* cr = nullptr;
+  kapsl::SampleLaunch l;
+  l.logits = logits.data_ptr<float>();
+  l.stride = logits.stride(0);
+  l.B = B;
+  l.Vl = (int)logits.size(1);
+  l.v0 = (int)vocab_start;
+  l.Vtot = vocab_size > 0 ? (int)vocab_size : (int)logits.size(1);
+  TORCH_CHECK(l.v0 >= 0 && l.v0 < l.Vtot, "sample: vocab_start outside the vocabulary");
+  l.temperature = temperature.data_ptr<float>();
+  l.top_k = top_k.data_ptr<int32_t>();
+  l.top_p = top_p.data_ptr<float>();
+  l.rep_penalty = rep_penalty.has_value() ? rep_penalty->data_ptr<float>() : nullptr;
+  if (counts.has_value()) {
+    CHECK_DT(*counts, at::kInt, "counts");
+    TORCH_CHECK(counts->size(-1) == l.Vtot, "sample: counts width must equal the vocabulary");
+    l.counts = counts->data_ptr<int32_t>();
+  }
+  if (occ.has_value()) {
+    TORCH_CHECK(occ_n.has_value(), "sample: occ needs occ_n");
+    CHECK_DT(*occ, at::kInt, "occ");
+    CHECK_DT(*occ_n, at::kInt, "occ_n");
+    l.occ = occ->data_ptr<int32_t>();
+    l.occ_n = occ_n->data_ptr<int32_t>();
+    l.occ_cap = (int)occ->size(-1);
+  }
   if (slots.has_value()) {
     CHECK_DT(*slots, at::kInt, "slots");
     TORCH_CHECK(slots->numel() >= B, "sample: slots too short");
-    cr = slots->data_ptr<int32_t>();
+    l.slots = slots->data_ptr<int32_t>();
   }
-  if (cn) TORCH_CHECK(counts->size(-1) == logits.size(1), "sample: counts width must equal vocab");
-  const c10::cuda::CUDAGuard g(logits.device());
-  kapsl::launch_sample(logits.data_ptr<float>(), logits.stride(0), B, (int)logits.size(1),
-                       temperature.data_ptr<float>(), top_k.data_ptr<int32_t>(), top_p.data_ptr<float>(), rp, cn, cr,
-                       reinterpret_cast<uint64_t*>(rng.data_ptr<int64_t>()), out.data_ptr<int32_t>(), cur_stream());
+  l.rng = reinterpret_cast<uint64_t*>(rng.data_ptr<int64_t>());
+  l.out = out.data_ptr<int32_t>();
+  l.err = err.data_ptr<int>();
+  l.world = cand_ptrs.empty() ? 1 : (int)cand_ptrs.size();
+  TORCH_CHECK(l.world <= 8, "sample: at most 8 ranks");
+  TORCH_CHECK(flag_ptrs.empty() || flag_ptrs.size() == cand_ptrs.size(), "sample: one flag word set per rank");
+  l.rank = (int)rank;
+  l.b_cap = (int)b_cap;
+  for (int i = 0; i < l.world && !cand_ptrs.empty(); ++i) {
+    l.cand[i] = reinterpret_cast<void*>(cand_ptrs[i]);
+    l.flags[i] = flag_ptrs.empty() ? nullptr : reinterpret_cast<int64_t*>(flag_ptrs[i]);
+  }
+  if (l.world > 1) {
+    TORCH_CHECK(ctr.has_value(), "sample: vocab-parallel sampling needs its counter tensor");
+    CHECK_DT(*ctr, at::kLong, "ctr");
+    l.ctr = ctr->data_ptr<int64_t>();
+  }
+  l.timeout_ns = timeout_ns;
+  return l;
 }
 
-void count_tokens(Tensor counts, Tensor rows, Tensor ids) {
+void sample(Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, c10::optional<Tensor> rep_penalty,
+            c10::optional<Tensor> counts, c10::optional<Tensor> slots, Tensor rng, Tensor out,
+            c10::optional<Tensor> occ, c10::optional<Tensor> occ_n, int64_t vocab_start, int64_t vocab_size,
+            c10::optional<Tensor> full_scratch, int64_t full_ctas, std::vector<int64_t> cand_ptrs,
+            std::vector<int64_t> flag_ptrs, int64_t rank, int64_t b_cap, c10::optional<Tensor> ctr,
+            int64_t timeout_ns, Tensor err) {
+  kapsl::SampleLaunch l = sample_args(logits, temperature, top_k, top_p, rep_penalty, counts, slots, rng, out, occ,
+                                      occ_n, vocab_start, vocab_size, cand_ptrs, flag_ptrs, rank, b_cap, ctr,
+                                      timeout_ns, err);
+  if (full_scratch.has_value() && full_ctas > 0) {
+    TORCH_CHECK((size_t)full_scratch->nbytes() >= kapsl::sample_full_scratch_bytes(l.Vl, (int)full_ctas),
+                "sample: whole-vocabulary scratch too small");
+    l.full_scratch = full_scratch->data_ptr();
+    l.full_ctas = (int)full_ctas;
+  }
+  const c10::cuda::CUDAGuard g(logits.device());
+  kapsl::launch_sample(l, cur_stream());
+}
+
+void sample_merge(Tensor logits, Tensor temperature, Tensor top_k, Tensor top_p, c10::optional<Tensor> slots,
+                  Tensor rng, Tensor out, int64_t vocab_size, std::vector<int64_t> cand_ptrs, int64_t rank,
+                  int64_t b_cap, Tensor ctr, Tensor err) {
+  kapsl::SampleLaunch l = sample_args(logits, temperature, top_k, top_p, c10::nullopt, c10::nullopt, slots, rng,
+                                      out, c10::nullopt, c10::nullopt, 0, vocab_size, cand_ptrs, {}, rank, b_cap,
+                                      ctr, 0, err);
+  const c10::cuda::CUDAGuard g(logits.device());
+  kapsl::launch_sample_merge(l, cur_stream());
+}
+
+int64_t sample_full_scratch_bytes(int64_t V, int64_t ctas) {
+  return (int64_t)kapsl::sample_full_scratch_bytes((int)V, (int)ctas);
+}
+
+void count_tokens(Tensor counts, Tensor rows, Tensor ids, c10::optional<Tensor> occ, c10::optional<Tensor> occ_n) {
   CHECK_DT(counts, at::kInt, "counts");
   CHECK_DT(rows, at::kInt, "rows");
   CHECK_DT(ids, at::kInt, "ids");
   TORCH_CHECK(rows.numel() == ids.numel(), "count_tokens: rows/ids length");
+  TORCH_CHECK(occ.has_value() == occ_n.has_value(), "count_tokens: occ and occ_n go together");
+  int32_t* o = nullptr;
+  int32_t* on = nullptr;
+  int cap = 0;
+  if (occ.has_value()) {
+    CHECK_DT(*occ, at::kInt, "occ");
+    CHECK_DT(*occ_n, at::kInt, "occ_n");
+    o = occ->data_ptr<int32_t>();
+    on = occ_n->data_ptr<int32_t>();
+    cap = (int)occ->size(-1);
+  }
   const c10::cuda::CUDAGuard g(counts.device());
   kapsl::launch_count_tokens(counts.data_ptr<int32_t>(), (int)counts.size(-1), rows.data_ptr<int32_t>(),
-                             ids.data_ptr<int32_t>(), (int)ids.numel(), cur_stream());
+                             ids.data_ptr<int32_t>(), (int)ids.numel(), o, on, cap, cur_stream());
 }
 
 void gemm(Tensor A, Tensor B, Tensor C, int64_t epi, c10::optional<Tensor> bias, c10::optional<Tensor> res,
@@ -281,7 +367,9 @@ void gemm_scatter(Tensor A, Tensor B, std::vector<int64_t> peers, int64_t my_ran
 }
 
 void tp_reduce_ag(std::vector<int64_t> recv, std::vector<int64_t> hidden, std::vector<int64_t> flags, int64_t rank,
-                  int64_t rows_per_rank, int64_t rows_total, int64_t cols, int64_t ld, Tensor epoch_ctr, Tensor err) {
+                  int64_t rows_per_rank, int64_t rows_total, int64_t cols, int64_t ld, Tensor epoch_ctr, Tensor err,
+                  int64_t timeout_ns) {
+  TORCH_CHECK(timeout_ns > 0, "tp_reduce_ag: timeout_ns must be positive");
   TORCH_CHECK(recv.size() == hidden.size() && recv.size() == flags.size(), "tp_reduce_ag: pointer tables differ");
   CHECK_DT(epoch_ctr, at::kLong, "epoch_ctr");
   const c10::cuda::CUDAGuard g(epoch_ctr.device());
@@ -290,12 +378,13 @@ void tp_reduce_ag(std::vector<int64_t> recv, std::vector<int64_t> hidden, std::v
   auto f = as_ptrs<int64_t>(flags);
   kapsl::launch_tp_reduce_ag(r.data(), h.data(), f.data(), (int)r.size(), (int)rank, (int)rows_per_rank,
                              (int)rows_total, (int)cols, ld, epoch_ctr.data_ptr<int64_t>(), err.data_ptr<int>(),
-                             kapsl::gemm_num_sms(), cur_stream());
+                             kapsl::gemm_num_sms(), (uint64_t)timeout_ns, cur_stream());
 }
 
 void tp_pull_reduce_ag(std::vector<int64_t> partial, std::vector<int64_t> hidden, std::vector<int64_t> flags,
                        int64_t rank, int64_t rows_per_rank, int64_t rows_total, int64_t cols, int64_t ld,
-                       Tensor epoch_ctr, Tensor err) {
+                       Tensor epoch_ctr, Tensor err, int64_t timeout_ns) {
+  TORCH_CHECK(timeout_ns > 0, "tp_pull_reduce_ag: timeout_ns must be positive");
   TORCH_CHECK(partial.size() == hidden.size() && partial.size() == flags.size(), "tp_pull_reduce_ag: tables differ");
   CHECK_DT(epoch_ctr, at::kLong, "epoch_ctr");
   const c10::cuda::CUDAGuard g(epoch_ctr.device());
@@ -304,7 +393,7 @@ void tp_pull_reduce_ag(std::vector<int64_t> partial, std::vector<int64_t> hidden
   auto f = as_ptrs<int64_t>(flags);
   kapsl::launch_tp_pull_reduce_ag(r.data(), h.data(), f.data(), (int)r.size(), (int)rank, (int)rows_per_rank,
                                   (int)rows_total, (int)cols, ld, epoch_ctr.data_ptr<int64_t>(), err.data_ptr<int>(),
-                                  kapsl::gemm_num_sms(), cur_stream());
+                                  kapsl::gemm_num_sms(), (uint64_t)timeout_ns, cur_stream());
 }
 
 void p2p_copy(int64_t dst, int64_t src, int64_t bytes, int64_t ctas_per_sm) {
@@ -427,7 +516,8 @@ void moe_gather(Tensor x, Tensor src, Tensor mtiles, Tensor xs) {
 // y / hidden / flags: per-rank device addresses (world = len(y)); flags empty when world == 1.
 void moe_combine(std::vector<int64_t> y, std::vector<int64_t> hidden, std::vector<int64_t> flags, int64_t rank,
                  Tensor ids, Tensor wts, Tensor pos, Tensor seg, int64_t T, int64_t K, int64_t el, int64_t cols,
-                 int64_t ld_y, int64_t ld_h, int64_t rows_per_rank, c10::optional<Tensor> epoch_ctr, Tensor err) {
+                 int64_t ld_y, int64_t ld_h, int64_t rows_per_rank, c10::optional<Tensor> epoch_ctr, Tensor err,
+                 int64_t timeout_ns) {
   const int world = (int)y.size();
   TORCH_CHECK(hidden.size() == y.size() && (world == 1 || flags.size() == y.size()), "moe_combine: tables differ");
   TORCH_CHECK(world == 1 || epoch_ctr.has_value(), "moe_combine: epoch counter needed for world > 1");
@@ -439,7 +529,7 @@ void moe_combine(std::vector<int64_t> y, std::vector<int64_t> hidden, std::vecto
                             ids.data_ptr<int32_t>(), wts.data_ptr<float>(), pos.data_ptr<int32_t>(),
                             seg.data_ptr<int32_t>(), (int)T, (int)K, (int)el, (int)cols, ld_y, ld_h,
                             (int)rows_per_rank, epoch_ctr.has_value() ? epoch_ctr->data_ptr<int64_t>() : nullptr,
-                            err.data_ptr<int>(), kapsl::gemm_num_sms(), cur_stream());
+                            err.data_ptr<int>(), kapsl::gemm_num_sms(), (uint64_t)timeout_ns, cur_stream());
 }
 
 // Copy blocks src_ids[i] -> dst_ids[i] of every plane (layer x K/V) from the local
@@ -509,8 +599,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_num_splits", &decode_num_splits);
   m.def("decode_attention", &decode_attention, "paged split-KV decode attention");
   m.def("prefill_attention", &prefill_attention, "paged chunked-prefill attention");
-  m.def("sample", &sample, "top-k/top-p/temperature/penalty sampler with per-row LCG");
-  m.def("count_tokens", &count_tokens, "counts[rows[i], ids[i]] += 1");
+  m.def("sample", &sample, "top-k/top-p/temperature/penalty sampler with per-row LCG (vocab-parallel capable)");
+  m.def("sample_merge", &sample_merge, "vocab-parallel sampler: merge all-gathered candidates, top-p, draw");
+  m.def("sample_full_scratch_bytes", &sample_full_scratch_bytes);
+  m.def("count_tokens", &count_tokens, "counts[rows[i], ids[i]] += 1 (+ first-occurrence lists)",
+        py::arg("counts"), py::arg("rows"), py::arg("ids"), py::arg("occ") = py::none(),
+        py::arg("occ_n") = py::none());
   m.def("gemm", &gemm, "tcgen05 GEMM C = epi(A @ B^T)");
   m.def("gemm_scatter", &gemm_scatter, "row-parallel GEMM storing rows into owner ranks' receive buffers");
   m.def("tp_reduce_ag", &tp_reduce_ag, "barrier + reduce own rows + residual + all-gather push + barrier");

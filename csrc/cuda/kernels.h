@@ -49,10 +49,45 @@ void launch_prefill_attention_tc(const CUtensorMap& q_map, const CUtensorMap& k_
 CUtensorMap make_tmap_3d_bf16(const void* base, const uint64_t (&dims)[3], const uint64_t (&strides_bytes)[2],
                               const uint32_t (&box)[3], bool swizzle128);
 
-void launch_sample(float* logits, int64_t stride, int B, int V, const float* temperature, const int32_t* top_k,
-                   const float* top_p, const float* rep_penalty, const int32_t* counts, const int32_t* slots,
-                   uint64_t* rng, int32_t* out, cudaStream_t st);
-void launch_count_tokens(int32_t* counts, int V, const int32_t* rows, const int32_t* ids, int n, cudaStream_t st);
+// Sampler launch (sampling.cu).  world > 1: vocabulary-parallel (this rank's
+// logits are columns [v0, v0 + Vl) of the vocabulary); cand / flags are the
+// ranks' symmetric candidate buffers and flag words (cand[p] == null for
+// p != rank when an NCCL all-gather moves the candidates instead).
+struct SampleLaunch {
+  float* logits = nullptr;
+  int64_t stride = 0;
+  int B = 0;
+  int Vl = 0;
+  int v0 = 0;
+  int Vtot = 0;
+  const float* temperature = nullptr;
+  const int32_t* top_k = nullptr;
+  const float* top_p = nullptr;
+  const float* rep_penalty = nullptr;
+  const int32_t* counts = nullptr;
+  const int32_t* occ = nullptr;
+  const int32_t* occ_n = nullptr;
+  int occ_cap = 0;
+  const int32_t* slots = nullptr;
+  uint64_t* rng = nullptr;
+  int32_t* out = nullptr;
+  int world = 1;
+  int rank = 0;
+  int b_cap = 0;
+  void* cand[8] = {nullptr};
+  int64_t* flags[8] = {nullptr};
+  int64_t* ctr = nullptr;
+  int64_t timeout_ns = 0;
+  int* err = nullptr;
+  void* full_scratch = nullptr;  // whole-vocabulary rows: sample_full_scratch_bytes(Vl, full_ctas)
+  int full_ctas = 0;
+};
+void launch_sample(const SampleLaunch& l, cudaStream_t st);
+size_t sample_full_scratch_bytes(int V, int ctas);
+// the vocabulary-parallel merge step alone (after an NCCL all-gather of the candidates)
+void launch_sample_merge(const SampleLaunch& l, cudaStream_t st);
+void launch_count_tokens(int32_t* counts, int V, const int32_t* rows, const int32_t* ids, int n, int32_t* occ,
+                         int32_t* occ_n, int occ_cap, cudaStream_t st);
 
 int gemm_num_sms();
 // epi: 0 plain, 1 +bias, 2 +residual, 3 SwiGLU over interleaved gate/up (N % 256 == 0, C is [M, N/2]).
@@ -84,7 +119,7 @@ void launch_moe_gather(const __nv_bfloat16* x, int64_t x_stride, const int32_t* 
 void launch_moe_combine(const __nv_bfloat16* const* y, __nv_bfloat16* const* hidden, int64_t* const* flags, int world,
                         int rank, const int32_t* ids, const float* wts, const int32_t* pos, const int32_t* seg, int T,
                         int K, int el, int cols, int64_t ld_y, int64_t ld_h, int rows_per_rank, int64_t* epoch_ctr,
-                        int* err, int num_sms, cudaStream_t st);
+                        int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
 
 // disaggregated prefill/decode: push KV blocks into a peer pool (kv_connector.cu)
 void launch_kv_push(const void* src_pool, void* dst_pool, const int32_t* src_ids, const int32_t* dst_ids, int nblocks,
@@ -97,10 +132,10 @@ void launch_gemm_scatter(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat1
                          int M, int N, int K, int* err, cudaStream_t st);
 void launch_tp_reduce_ag(__nv_bfloat16* const* recv, __nv_bfloat16* const* hidden, int64_t* const* flags, int world,
                          int rank, int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr,
-                         int* err, int num_sms, cudaStream_t st);
+                         int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
 void launch_tp_pull_reduce_ag(__nv_bfloat16* const* partial, __nv_bfloat16* const* hidden, int64_t* const* flags,
                               int world, int rank, int rows_per_rank, int rows_total, int cols, int64_t ld,
-                              int64_t* epoch_ctr, int* err, int num_sms, cudaStream_t st);
+                              int64_t* epoch_ctr, int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
 void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st);
 void* symm_alloc(size_t bytes);
 void symm_free(void* p);

@@ -231,6 +231,7 @@ struct MoECombineArgs {
   int64_t ld_y, ld_h;
   int world, rank, rows_per_rank;
   int64_t* epoch_ctr;
+  uint64_t timeout_ns;  // limit of the peer-flag waits
   int* err;
 };
 
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoECombineArgs a) {
         __threadfence_system();
         for (int p = 0; p < WORLD; ++p) st_release_sys(a.flags[p] + 0 * 8 + a.rank, epoch_sh);
       }
-      if (!wait_flags(a.flags[a.rank] + 0 * 8, WORLD, epoch_sh, 5000000000ull)) {
+      if (!wait_flags(a.flags[a.rank] + 0 * 8, WORLD, epoch_sh, a.timeout_ns)) {
         ok_sh = 0;
         atomicExch(a.err, 41);
       }
@@ -311,7 +312,7 @@ __global__ void __launch_bounds__(256) moe_combine_kernel(MoECombineArgs a) {
       const int64_t done = atomicAdd(reinterpret_cast<unsigned long long*>(&a.epoch_ctr[1]), 1ull);
       if (done == gridDim.x - 1) {
         for (int p = 0; p < WORLD; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch_sh);
-        if (!wait_flags(a.flags[a.rank] + 1 * 8, WORLD, epoch_sh, 5000000000ull)) atomicExch(a.err, 42);
+        if (!wait_flags(a.flags[a.rank] + 1 * 8, WORLD, epoch_sh, a.timeout_ns)) atomicExch(a.err, 42);
         a.epoch_ctr[1] = 0;
         a.epoch_ctr[0] = epoch_sh;
         __threadfence();
@@ -354,7 +355,7 @@ void launch_moe_gather(const bf16* x, int64_t x_stride, const int32_t* src, cons
 void launch_moe_combine(const bf16* const* y, bf16* const* hidden, int64_t* const* flags, int world, int rank,
                         const int32_t* ids, const float* wts, const int32_t* pos, const int32_t* seg, int T, int K,
                         int el, int cols, int64_t ld_y, int64_t ld_h, int rows_per_rank, int64_t* epoch_ctr,
-                        int* err, int num_sms, cudaStream_t st) {
+                        int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st) {
   if (T == 0) return;
   if (cols % 8 != 0 || ld_y % 8 != 0 || ld_h % 8 != 0) throw std::runtime_error("moe_combine: cols % 8 != 0");
   MoECombineArgs a{};
@@ -377,6 +378,7 @@ void launch_moe_combine(const bf16* const* y, bf16* const* hidden, int64_t* cons
   a.rank = rank;
   a.rows_per_rank = rows_per_rank;
   a.epoch_ctr = epoch_ctr;
+  a.timeout_ns = timeout_ns;
   a.err = err;
   const int rows = world > 1 ? rows_per_rank : T;
   const int64_t work = (int64_t)rows * (cols / 8);

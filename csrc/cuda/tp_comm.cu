@@ -37,6 +37,7 @@ struct TPArgs {
   int cols;
   int64_t ld;
   int64_t* epoch_ctr;  // local: [0] epoch, [1] finished-CTA counter
+  uint64_t timeout_ns; // limit of every wait on a peer flag; past it the kernel records an error and returns
   int* err;
 };
 
@@ -50,7 +51,7 @@ __global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
       __threadfence_system();  // the previous kernel's peer stores are performed
       for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 0 * 8 + a.rank, epoch_sh);
     }
-    if (!wait_flags(a.flags[a.rank] + 0 * 8, a.world, epoch_sh, 5000000000ull)) {
+    if (!wait_flags(a.flags[a.rank] + 0 * 8, a.world, epoch_sh, a.timeout_ns)) {
       ok_sh = 0;
       atomicExch(a.err, 30);
     }
@@ -103,7 +104,7 @@ __global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
     const int64_t done = atomicAdd(reinterpret_cast<unsigned long long*>(&a.epoch_ctr[1]), 1ull);
     if (done == gridDim.x - 1) {
       for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch);
-      if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, 5000000000ull)) atomicExch(a.err, 31);
+      if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, a.timeout_ns)) atomicExch(a.err, 31);
       a.epoch_ctr[1] = 0;
       a.epoch_ctr[0] = epoch;
       __threadfence();
@@ -128,7 +129,7 @@ __global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
       __threadfence_system();
       for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 0 * 8 + a.rank, epoch_sh);
     }
-    if (!wait_flags(a.flags[a.rank] + 0 * 8, a.world, epoch_sh, 5000000000ull)) {
+    if (!wait_flags(a.flags[a.rank] + 0 * 8, a.world, epoch_sh, a.timeout_ns)) {
       ok_sh = 0;
       atomicExch(a.err, 32);
     }
@@ -200,7 +201,7 @@ __global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
     if (done == gridDim.x - 1) {
       a.epoch_ctr[4] = (int64_t)globaltimer_ns();
       for (int p = 0; p < a.world; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch);
-      if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, 5000000000ull)) atomicExch(a.err, 33);
+      if (!wait_flags(a.flags[a.rank] + 1 * 8, a.world, epoch, a.timeout_ns)) atomicExch(a.err, 33);
       a.epoch_ctr[5] = (int64_t)globaltimer_ns();
       // running sums over calls: barrier-1 wait (CTA 0), data phase (until the
       // last CTA retires), barrier-2 wait, number of calls
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
 
 void launch_tp_pull_reduce_ag(bf16* const* partial, bf16* const* hidden, int64_t* const* flags, int world, int rank,
                               int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr, int* err,
-                              int num_sms, cudaStream_t st) {
+                              int num_sms, uint64_t timeout_ns, cudaStream_t st) {
   if (world > 8) throw std::runtime_error("tp: at most 8 ranks");
   if (cols % 8 != 0 || ld % 8 != 0) throw std::runtime_error("tp: columns must be a multiple of 8");
   TPArgs a{};
@@ -233,6 +234,7 @@ void launch_tp_pull_reduce_ag(bf16* const* partial, bf16* const* hidden, int64_t
   a.cols = cols;
   a.ld = ld;
   a.epoch_ctr = epoch_ctr;
+  a.timeout_ns = timeout_ns;
   a.err = err;
   const int64_t work = (int64_t)rows_per_rank * (cols / 8);
   // at most 4 CTAs of 256 threads per SM: every CTA is resident, so the barrier cannot deadlock
@@ -251,7 +253,7 @@ void launch_tp_pull_reduce_ag(bf16* const* partial, bf16* const* hidden, int64_t
 
 void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const* flags, int world, int rank,
                          int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr, int* err,
-                         int num_sms, cudaStream_t st) {
+                         int num_sms, uint64_t timeout_ns, cudaStream_t st) {
   if (world > 8) throw std::runtime_error("tp: at most 8 ranks");
   if (cols % 8 != 0 || ld % 8 != 0) throw std::runtime_error("tp: columns must be a multiple of 8");
   TPArgs a{};
@@ -267,6 +269,7 @@ void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const*
   a.cols = cols;
   a.ld = ld;
   a.epoch_ctr = epoch_ctr;
+  a.timeout_ns = timeout_ns;
   a.err = err;
   const int64_t work = (int64_t)rows_per_rank * (cols / 8);
   int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms);  // all CTAs co-resident

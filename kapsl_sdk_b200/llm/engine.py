@@ -100,7 +100,7 @@ class LLMEngine:
 
             moe = MoE(cfg, self.device, tp_comm)
         self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe, stage=pp_stage)
-        self.model.configure_tp(e.max_num_batched_tokens + e.max_num_seqs)
+        self.model.configure_tp(e.max_num_batched_tokens + e.max_num_seqs, sample_rows=e.max_num_seqs + 1)
         if pp_stage is not None:
             e.use_cuda_graph = False  # stages exchange hidden states inside the step
         layout = KVLayout(nlayers, self.model.hkv, cfg.head_dim, e.block_size)

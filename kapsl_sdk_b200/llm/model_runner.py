@@ -66,12 +66,13 @@ class _Layout:
 class Inflight:
     """A launched step: its sampling sequences (row order of ``out_tokens``), the
     pinned buffer its tokens are read back into, and the event after that copy."""
-    __slots__ = ("step_id", "seqs", "R", "h_out", "done", "start", "kind", "num_tokens", "out_idx")
+    __slots__ = ("step_id", "seqs", "R", "h_out", "done", "start", "kind", "num_tokens", "out_idx", "launch_s")
 
     def __init__(self, step_id, seqs, R, h_out, done, start, kind, num_tokens):
         self.step_id, self.seqs, self.R, self.h_out = step_id, seqs, R, h_out
         self.done, self.start, self.kind, self.num_tokens = done, start, kind, num_tokens
         self.out_idx: list = []
+        self.launch_s = 0.0
 
 
 class ModelRunner:
@@ -101,6 +102,11 @@ class ModelRunner:
         # per-sequence device tables
         self.rng_table = torch.zeros(S, dtype=torch.int64, device=self.device)
         self.counts = torch.zeros(S, self.vocab, dtype=torch.int32, device=self.device)
+        # per slot: the ids that occurred (first-seen order), so the sampler's
+        # repetition penalty touches only those logits
+        self.occ = torch.zeros(S, max(self.max_blocks * self.bs, 1), dtype=torch.int32, device=self.device)
+        self.occ_n = torch.zeros(S, dtype=torch.int32, device=self.device)
+        self.full_scratch: Optional[torch.Tensor] = None  # whole-vocabulary sampling rows
         self.out_tokens = torch.zeros(S, dtype=torch.int32, device=self.device)
         self._admit_seqs: list = []
         self._step_id = 0
@@ -157,12 +163,28 @@ class ModelRunner:
             pf_seq_info=self._v32(L.sinfo, (S - Bd) * 4).view(S - Bd, 4) if S > Bd else None,
             decode_splits=nsplit)
 
-    def _sample(self, logits: torch.Tensor, R: int) -> None:
+    FULL_CTAS = 32  # rows sampled over the whole vocabulary at once
+
+    @staticmethod
+    def _needs_full(seqs) -> bool:
+        """A row samples over the whole vocabulary (T > 0 with top_k 0 or > 1024)."""
+        return any(s.params.temperature > 0 and not 0 < s.params.top_k <= ops.SAMPLE_MAX_TOP_K for s in seqs)
+
+    def _sample(self, logits: torch.Tensor, R: int, full: bool = False) -> None:
         L = self.L
-        ops.sample(logits, self._f32(L.temp, R), self._v32(L.topk, R), self._f32(L.topp, R), self.rng_table,
-                   self.out_tokens[:R], rep_penalty=self._f32(L.pen, R), counts=self.counts,
-                   slots=self._v32(L.sslot, R))
-        ops.count_tokens(self.counts, self._v32(L.sslot, R), self.out_tokens[:R])
+        args = (self._f32(L.temp, R), self._v32(L.topk, R), self._f32(L.topp, R))
+        tp = self.model.tp
+        if self.model.tp_size > 1 and not full:  # logits hold this rank's vocabulary slice
+            tp.vocab_sample(logits, self.model.vocab_start, self.vocab, *args, self.rng_table, self.out_tokens[:R],
+                            rep_penalty=self._f32(L.pen, R), counts=self.counts, slots=self._v32(L.sslot, R),
+                            occ=self.occ, occ_n=self.occ_n)
+        else:
+            if full and self.full_scratch is None:
+                self.full_scratch = ops.sample_full_scratch(self.vocab, self.device, self.FULL_CTAS)
+            ops.sample(logits, *args, self.rng_table, self.out_tokens[:R], rep_penalty=self._f32(L.pen, R),
+                       counts=self.counts, slots=self._v32(L.sslot, R), occ=self.occ, occ_n=self.occ_n,
+                       full_scratch=self.full_scratch if full else None, full_ctas=self.FULL_CTAS if full else 0)
+        ops.count_tokens(self.counts, self._v32(L.sslot, R), self.out_tokens[:R], self.occ, self.occ_n)
 
     # ------------------------------------------------------- host inputs
     def _fill(self, batch: ScheduledBatch, pad_to: int = 0):
@@ -279,9 +301,11 @@ class ModelRunner:
                               dtype=torch.int64).to(self.device)
         self.rng_table.index_copy_(0, slots, rng)
         self.counts.index_fill_(0, slots, 0)
+        self.occ_n.index_fill_(0, slots, 0)
         rows = np.concatenate([np.full(len(s.all_ids), s.slot, dtype=np.int32) for s in seqs])
         ids = np.concatenate([np.asarray(s.all_ids, dtype=np.int32) for s in seqs])
-        ops.count_tokens(self.counts, torch.from_numpy(rows).to(self.device), torch.from_numpy(ids).to(self.device))
+        ops.count_tokens(self.counts, torch.from_numpy(rows).to(self.device), torch.from_numpy(ids).to(self.device),
+                         self.occ, self.occ_n)
 
     def _apply_admissions(self) -> None:
         n = getattr(self, "_pending_admit", 0)
@@ -291,12 +315,13 @@ class ModelRunner:
         slots_d = self._v32(L.adm_slot, n).long()
         self.rng_table.index_copy_(0, slots_d, self.d64[L.adm_rng:L.adm_rng + n])
         self.counts.index_fill_(0, slots_d, 0)
+        self.occ_n.index_fill_(0, slots_d, 0)
         rows = np.concatenate([np.full(len(p), sl, dtype=np.int32) for sl, p in self._admit_prompts])
         ids = np.concatenate([np.asarray(p, dtype=np.int32) for _, p in self._admit_prompts])
         rows_t = torch.from_numpy(rows).pin_memory().to(self.device, non_blocking=True)
         ids_t = torch.from_numpy(ids).pin_memory().to(self.device, non_blocking=True)
         self.stats["h2d_bytes"] += rows.nbytes + ids.nbytes
-        ops.count_tokens(self.counts, rows_t, ids_t)
+        ops.count_tokens(self.counts, rows_t, ids_t, self.occ, self.occ_n)
         self._pending_admit = 0
         self._admit_prompts = []
 
@@ -318,6 +343,8 @@ class ModelRunner:
                 bucket = self.graph_sizes[k]
                 if self.use_graph:
                     gsize = pad_to = bucket
+        full = self._needs_full(batch.decode) or self._needs_full(
+            s for s, n in batch.prefill if s.num_computed + n >= s.length)
         tp0 = time.perf_counter()
         c0 = launch_count()
         self._select(self._buf ^ 1)  # the set used two steps ago: its copies have completed
@@ -333,11 +360,12 @@ class ModelRunner:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev0.record()
         if gsize:
-            g = self.graphs.get(gsize)
+            key = (gsize, full)
+            g = self.graphs.get(key)
             if g is None:
-                g = self._capture(gsize)
+                g = self._capture(gsize, full)
             g.replay()
-            self.launches += launch_count() - c0 + self.graph_launches[gsize]
+            self.launches += launch_count() - c0 + self.graph_launches[key]
             self.stats["graph_steps"] += 1
         else:
             max_ctx = int(self.n32[self.L.ctx:self.L.ctx + Bd].max()) if Bd else 0
@@ -345,9 +373,9 @@ class ModelRunner:
             if bucket:  # same split-KV policy as the captured graphs, so both paths agree bitwise
                 nsplit = self._graph_splits(bucket)
             fb = self._forward_batch(T, S, R, Bd, max_ctx, nwork, nsplit, nsrc=Bpad)
-            logits = self.model.forward(fb, self.pool.k, self.pool.v)
+            logits = self.model.forward(fb, self.pool.k, self.pool.v, full_vocab=full)
             if logits is not None:  # None: an earlier pipeline stage (the last stage samples)
-                self._sample(logits, R)
+                self._sample(logits, R, full)
             self.launches += launch_count() - c0
         self.h_out[:R].copy_(self.out_tokens[:R], non_blocking=True)
         done = torch.cuda.Event(enable_timing=prof is not None)
@@ -357,7 +385,8 @@ class ModelRunner:
         self.stats["steps"] += 1
         inf = Inflight(self._step_id, sample_seqs, R, self.h_out, done, ev0, "graph" if gsize else "eager", T)
         if prof is not None:
-            self._tally(f"{inf.kind}_launch_s", time.perf_counter() - tl0)
+            inf.launch_s = time.perf_counter() - tl0
+            self._tally(f"{inf.kind}_launch_s", inf.launch_s)
         return inf
 
     def collect(self, inf: "Inflight") -> tuple[list, np.ndarray]:
@@ -365,10 +394,14 @@ class ModelRunner:
         t0 = time.perf_counter()
         inf.done.synchronize()
         if self.prof is not None:
+            dev_s = inf.start.elapsed_time(inf.done) / 1e3
             self._tally("sync_s", time.perf_counter() - t0)
             self._tally(f"{inf.kind}_steps", 1)
             self._tally(f"{inf.kind}_tokens", inf.num_tokens)
-            self._tally(f"{inf.kind}_device_s", inf.start.elapsed_time(inf.done) / 1e3)
+            self._tally(f"{inf.kind}_device_s", dev_s)
+            trace = self.prof.get("trace")
+            if trace is not None:  # per step: kind, tokens, sampling rows, host launch s, device s
+                trace.append((inf.kind, inf.num_tokens, inf.R, round(inf.launch_s, 6), round(dev_s, 6)))
         return inf.seqs, inf.h_out[:inf.R].numpy().copy()
 
     def _tally(self, key: str, v) -> None:
@@ -388,29 +421,33 @@ class ModelRunner:
     def _graph_splits(self, B: int) -> int:
         return int(ops.cuda_ops().decode_num_splits(B, self.model.hkv, self.max_blocks * self.bs))
 
-    def _capture(self, B: int) -> torch.cuda.CUDAGraph:
+    def _capture(self, B: int, full: bool = False) -> torch.cuda.CUDAGraph:
         """Capture forward+sample for a decode batch of ``B`` rows (inputs are the
-        staging views, already filled for this step)."""
+        staging views, already filled for this step); ``full``: the variant whose
+        rows may sample over the whole vocabulary."""
         max_ctx = self.max_blocks * self.bs
         nsplit = self._graph_splits(B)
         fb = self._forward_batch(B, B, B, B, max_ctx, 0, nsplit, nsrc=B)
+        if full and self.full_scratch is None:
+            self.full_scratch = ops.sample_full_scratch(self.vocab, self.device, self.FULL_CTAS)
         # warm up once outside capture (allocator, function attributes)
         s = torch.cuda.Stream(self.device)
         s.wait_stream(torch.cuda.current_stream(self.device))
         with torch.cuda.stream(s):
-            logits = self.model.forward(fb, self.pool.k, self.pool.v)
+            logits = self.model.forward(fb, self.pool.k, self.pool.v, full_vocab=full)
         torch.cuda.current_stream(self.device).wait_stream(s)
         torch.cuda.synchronize(self.device)
         # the warm-up wrote KV for real rows at their slots (same values as the replay will); fine.
         g = torch.cuda.CUDAGraph()
         c0 = launch_count()
         with torch.cuda.graph(g, pool=self.graph_pool):
-            logits = self.model.forward(fb, self.pool.k, self.pool.v)
-            self._sample(logits, B)
-        self.graph_launches[B] = launch_count() - c0
+            logits = self.model.forward(fb, self.pool.k, self.pool.v, full_vocab=full)
+            self._sample(logits, B, full)
+        key = (B, full)
+        self.graph_launches[key] = launch_count() - c0
         if self.graph_pool is None:
             self.graph_pool = g.pool()
-        self.graphs[B] = g
+        self.graphs[key] = g
         return g
 
     def release_graphs(self) -> None:

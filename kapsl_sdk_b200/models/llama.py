@@ -110,6 +110,12 @@ def ffn_shard_size(cfg: ModelConfig, tp: int) -> int:
     return -(-cfg.intermediate_size // (tp * align)) * align
 
 
+def vocab_slice(vocab: int, tp: int) -> int:
+    """Vocabulary columns per rank of the vocab-parallel lm_head: ceil(V / tp)
+    rounded up to the GEMM's 128-row tile (Qwen2.5-7B over 8 ranks: 19072)."""
+    return -(-vocab // (tp * 128)) * 128 if tp > 1 else vocab
+
+
 def _pad_rows(w: torch.Tensor, n: int) -> torch.Tensor:
     return w if w.shape[0] == n else torch.cat([w, w.new_zeros(n - w.shape[0], *w.shape[1:])], 0)
 
@@ -240,9 +246,12 @@ def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: in
     ``layers`` keeps only a pipeline stage's layer range."""
     plan = ShardPlan.make(cfg, tp, rank)
     V, d = cfg.vocab_size, cfg.hidden_size
-    # embedding and lm_head are replicated on every rank: each rank computes the
-    # same logits and samples the same token, so no gather of logits is needed
+    # the embedding is replicated (a lookup of T rows); the lm_head is held whole on
+    # every rank, padded with zero rows to tp equal vocabulary slices: a step
+    # multiplies only this rank's slice and the sampler merges the ranks'
+    # candidates (the whole matrix serves steps that sample over every id)
     vl, v0 = V, 0
+    vpad = vocab_slice(V, tp) * tp
     w = ModelWeights(embed=None, lm_head=None, final_norm=torch.ones(d, device=device, dtype=torch.bfloat16),
                      vocab_start=v0, heads_local=plan.heads_local, kv_heads_local=plan.kv_heads_local,
                      ffn_local=ffn_shard_size(cfg, tp) if not cfg.is_moe else cfg.intermediate_size)
@@ -251,7 +260,7 @@ def weights_from_full(cfg: ModelConfig, full_iter, device, tp: int = 1, rank: in
         if kind == "embed":
             w.embed = t[v0:v0 + vl].to(device, torch.bfloat16).contiguous()
         elif kind == "lm_head":
-            w.lm_head = t[v0:v0 + vl].to(device, torch.bfloat16).contiguous()
+            w.lm_head = _pad_rows(t[v0:v0 + vl].to(device, torch.bfloat16), vpad).contiguous()
         elif kind == "final_norm":
             w.final_norm = t.to(device, torch.bfloat16).contiguous()
         else:
@@ -310,10 +319,13 @@ class CausalLM:
         self.cos_sin = ref.rope_cos_sin(cfg.max_position, cfg.head_dim, cfg.rope_theta, device=self.device,
                                          scaling=cfg.rope_scaling)
         self.qkv_width = (self.hq + 2 * self.hkv) * self.D
+        W = self.tp_size
+        self.vocab_slice = vocab_slice(cfg.vocab_size, W)
+        self.vocab_start = (tp_comm.rank if W > 1 else 0) * self.vocab_slice
 
-    def configure_tp(self, max_tokens: int) -> None:
+    def configure_tp(self, max_tokens: int, sample_rows: int = 0) -> None:
         if self.tp is not None and self.tp.world_size > 1:
-            self.tp.configure(max_tokens, self.cfg.hidden_size)
+            self.tp.configure(max_tokens, self.cfg.hidden_size, sample_rows=sample_rows)
         if self.moe is not None:
             self.moe.configure(max_tokens)
 
@@ -321,7 +333,10 @@ class CausalLM:
     def tp_size(self) -> int:
         return 1 if self.tp is None else self.tp.world_size
 
-    def forward(self, fb: ForwardBatch, k_caches: list, v_caches: list) -> torch.Tensor:
+    def forward(self, fb: ForwardBatch, k_caches: list, v_caches: list, full_vocab: bool = True) -> torch.Tensor:
+        """Logits (fp32) of the rows ``fb.logits_idx``: every vocabulary column, or
+        with tensor parallelism and ``full_vocab=False`` only this rank's slice
+        (columns [vocab_start, vocab_start + vocab_slice))."""
         cfg = self.cfg
         T = fb.num_tokens
         Bd = fb.num_decode
@@ -366,7 +381,11 @@ class CausalLM:
             return None
         xs = h.index_select(0, fb.logits_idx)
         xs = ops.rmsnorm(xs, self.w.final_norm, cfg.rms_eps)
-        return ops.linear(xs, self.w.lm_head, out_dtype=torch.float32)
+        if self.tp_size > 1 and not full_vocab:
+            head = self.w.lm_head[self.vocab_start:self.vocab_start + self.vocab_slice]
+        else:
+            head = self.w.lm_head[:cfg.vocab_size]
+        return ops.linear(xs, head, out_dtype=torch.float32)
 
 
 def reference_forward(cfg: ModelConfig, full_layers: list, embed: torch.Tensor, lm_head: torch.Tensor,

@@ -117,7 +117,7 @@ class MoE:
             b = self.tp.bufs
             rpr = _ceil(T, self.world)
             ops.moe_combine(b["ep"], b["hidden"], b["flags"], self.rank, ids, wts, pos, self.seg, self.el, d, d, d,
-                            rpr, self.tp.epoch)
+                            rpr, self.tp.epoch, self.tp.timeout_ns)
         else:
             part = self.partial[:T]
             part.zero_()

@@ -220,20 +220,39 @@ def prefill_tc_tile(num_heads: int, num_kv_heads: int) -> int:
     return 128 // (num_heads // num_kv_heads)
 
 
+SAMPLE_MAX_TOP_K = 1024  # top_k above this (or 0, with T > 0) takes the whole-vocabulary path
+
+
 def sample(logits: torch.Tensor, temperature: torch.Tensor, top_k: torch.Tensor, top_p: torch.Tensor,
            rng_state: torch.Tensor, out: torch.Tensor, rep_penalty: Optional[torch.Tensor] = None,
-           counts: Optional[torch.Tensor] = None, slots: Optional[torch.Tensor] = None) -> torch.Tensor:
+           counts: Optional[torch.Tensor] = None, slots: Optional[torch.Tensor] = None,
+           occ: Optional[torch.Tensor] = None, occ_n: Optional[torch.Tensor] = None,
+           full_scratch: Optional[torch.Tensor] = None, full_ctas: int = 0) -> torch.Tensor:
     """Sample one token per row of fp32 ``logits`` (modified in place).
 
-    ``rng_state`` (int64 LCG states) and ``counts`` (per-id occurrence counts
-    for the repetition penalty) are per-sequence tables indexed by
-    ``slots[row]`` (or by the row itself when ``slots`` is None)."""
-    cuda_ops().sample(logits, temperature, top_k, top_p, rep_penalty, counts, slots, rng_state, out)
+    ``rng_state`` (int64 LCG states), ``counts`` (per-id occurrence counts for
+    the repetition penalty) and ``occ`` / ``occ_n`` (each slot's list of ids
+    that occurred, so the penalty touches only those logits) are per-sequence
+    tables indexed by ``slots[row]`` (or by the row itself when ``slots`` is
+    None).  Rows with T > 0 and top_k 0 or > 1024 are sampled over the whole
+    vocabulary when ``full_scratch`` (:func:`sample_full_scratch`) is given."""
+    cuda_ops().sample(logits, temperature, top_k, top_p, rep_penalty, counts, slots, rng_state, out, occ, occ_n, 0,
+                      logits.shape[1], full_scratch, int(full_ctas), [], [], 0, 0, None, 0,
+                      error_buffer(logits.device))
     return out
 
 
-def count_tokens(counts: torch.Tensor, rows: torch.Tensor, ids: torch.Tensor) -> None:
-    cuda_ops().count_tokens(counts, rows, ids)
+def sample_full_scratch(vocab: int, device, ctas: int = 32) -> torch.Tensor:
+    """Scratch for ``ctas`` rows sampled over the whole vocabulary at once."""
+    n = int(cuda_ops().sample_full_scratch_bytes(vocab, ctas))
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def count_tokens(counts: torch.Tensor, rows: torch.Tensor, ids: torch.Tensor, occ: Optional[torch.Tensor] = None,
+                 occ_n: Optional[torch.Tensor] = None) -> None:
+    """``counts[rows[i], ids[i]] += 1``; a first occurrence also appends the id to
+    ``occ[rows[i]]`` (length ``occ_n[rows[i]]``)."""
+    cuda_ops().count_tokens(counts, rows, ids, occ, occ_n)
 
 
 # ------------------------------------------------------------ mixture of experts
@@ -276,7 +295,10 @@ def grouped_linear(xs: torch.Tensor, w: torch.Tensor, n_per_group: int, mtiles: 
 
 def moe_combine(y_ptrs: list[int], hidden_ptrs: list[int], flag_ptrs: list[int], rank: int, ids: torch.Tensor,
                 weights: torch.Tensor, pos: torch.Tensor, seg: torch.Tensor, e_local: int, cols: int, ld_y: int,
-                ld_h: int, rows_per_rank: int, epoch: Optional[torch.Tensor] = None) -> None:
+                ld_h: int, rows_per_rank: int, epoch: Optional[torch.Tensor] = None,
+                timeout_ns: int = 5_000_000_000) -> None:
+    """Weighted top-k combine + residual; with peers (len(y_ptrs) > 1) each wait on
+    a peer's flag gives up after ``timeout_ns`` and records error 41 / 42."""
     T, k = ids.shape
     cuda_ops().moe_combine(y_ptrs, hidden_ptrs, flag_ptrs, rank, ids, weights, pos, seg, T, k, e_local, cols, ld_y,
-                           ld_h, rows_per_rank, epoch, error_buffer(ids.device))
+                           ld_h, rows_per_rank, epoch, error_buffer(ids.device), int(timeout_ns))

@@ -2,11 +2,13 @@
 
 Layout (Megatron style): QKV and gate/up are column-parallel (each rank holds
 its heads / FFN slice), o_proj and down_proj are row-parallel (each rank holds
-the matching input slice and produces a partial sum).  The embedding and
-lm_head are replicated, so every rank ends each layer with the same residual
-stream, computes the same logits and samples the same token with the same
-per-sequence RNG state: the ranks stay in lock step without gathering logits
-or broadcasting tokens.
+the matching input slice and produces a partial sum).  The embedding is
+replicated and every rank ends each layer with the same residual stream.  The
+lm_head is vocabulary-parallel: each rank multiplies its slice of the
+vocabulary, selects that slice's top-k candidates, and the candidates (not
+the logits) are exchanged (:meth:`TPComm.vocab_sample`); every rank then
+draws the same token with the same per-sequence RNG state, so the ranks stay
+in lock step without broadcasting tokens.
 
 Two reduction modes for the row-parallel layers:
 
@@ -39,11 +41,21 @@ from .._ext import cuda_ops
 
 
 class TPComm:
+    # candidates per row in the vocabulary-parallel sampler's exchange buffers
+    SAMPLE_K = 1024
+
     def __init__(self, world_size: int, rank: int, device, mode: str = "fused", group=None,
-                 max_tokens: int = 4096, hidden: int = 4096, ep_rows: int = 0):
+                 max_tokens: int = 4096, hidden: int = 4096, ep_rows: int = 0, timeout_s: float = 5.0):
+        """``timeout_s`` bounds every device-side wait on a peer (flag barriers of the
+        fused reduction, the MoE combine and the sampler's candidate exchange): a
+        wait that runs out records an error code (see ``ops.check_errors``) and
+        the kernel returns instead of hanging."""
         import torch.distributed as dist
 
         assert mode in ("fused", "scatter", "nccl")
+        self.timeout_ns = int(timeout_s * 1e9)
+        self.sample_rows = 0
+        self.cand_local = None
         self.dist = dist
         self.world_size = world_size
         self.rank = rank
@@ -66,10 +78,20 @@ class TPComm:
         return cls(dist.get_world_size(), dist.get_rank(), torch.device("cuda", torch.cuda.current_device()), mode,
                    max_tokens=max_tokens, hidden=hidden)
 
-    def configure(self, max_tokens: int, hidden: int, ep_rows: int = 0) -> None:
+    def configure(self, max_tokens: int, hidden: int, ep_rows: int = 0, sample_rows: int = 0) -> None:
         """(Re)size the symmetric buffers once the model geometry is known.
         ``ep_rows``: rows of the expert-output buffer that peers read in the
-        fused MoE combine (0 for dense models)."""
+        fused MoE combine (0 for dense models); ``sample_rows``: rows the
+        vocabulary-parallel sampler exchanges candidates for."""
+        if self.world_size > 1 and sample_rows > self.sample_rows:
+            self.sample_rows = sample_rows
+            self.samp_ctr = torch.zeros(2, dtype=torch.int64, device=self.device)
+            if self.mode == "nccl":
+                self.cand_local = torch.zeros(2, self.world_size, sample_rows, self.SAMPLE_K, 2, dtype=torch.float32,
+                                              device=self.device)
+            elif self.bufs is not None:
+                self.close()
+                self.bufs = None
         if self.mode != "nccl" and self.world_size > 1 and (max_tokens > self.max_tokens or hidden != self.hidden
                                                               or ep_rows > self.ep_rows or self.bufs is None):
             self.close()
@@ -84,10 +106,11 @@ class TPComm:
         rows_pad = rpr * W
         recv_bytes = W * rpr * hidden * 2
         hid_bytes = rows_pad * hidden * 2
-        flag_bytes = 2 * 8 * 8
+        flag_bytes = 4 * 8 * 8  # sites: 0/1 reduction barriers, 2 sampler candidates, 3 spare
         ep_bytes = self.ep_rows * hidden * 2
+        cand_bytes = 2 * W * self.sample_rows * self.SAMPLE_K * 8
         align = lambda n: (n + 255) // 256 * 256
-        total = align(recv_bytes) + align(hid_bytes) + align(flag_bytes) + align(ep_bytes)
+        total = align(recv_bytes) + align(hid_bytes) + align(flag_bytes) + align(ep_bytes) + align(cand_bytes)
         base = c.symm_alloc(total)
         handle = c.symm_handle(base)
         handles = [None] * W
@@ -98,10 +121,11 @@ class TPComm:
         off_h = align(recv_bytes)
         off_f = off_h + align(hid_bytes)
         off_e = off_f + align(flag_bytes)
+        off_c = off_e + align(ep_bytes)
         self.bufs = {
             "base": base, "bases": bases, "rpr": rpr, "rows_pad": rows_pad,
             "recv": [b for b in bases], "hidden": [b + off_h for b in bases], "flags": [b + off_f for b in bases],
-            "ep": [b + off_e for b in bases],
+            "ep": [b + off_e for b in bases], "cand": [b + off_c for b in bases],
         }
         dev = self.device.index
         self.ep_buf = (c.tensor_from_ptr(base + off_e, [self.ep_rows, hidden], "bfloat16", dev)
@@ -140,6 +164,36 @@ class TPComm:
         if reset:
             self.epoch[8:12].zero_()
         return out
+
+    # ------------------------------------------------------ vocab-parallel sampling
+    def vocab_sample(self, logits: torch.Tensor, vocab_start: int, vocab_size: int, temperature, top_k, top_p,
+                     rng, out, rep_penalty=None, counts=None, slots=None, occ=None, occ_n=None) -> None:
+        """Sample from logits split over the ranks by vocabulary (``logits`` holds
+        columns [vocab_start, vocab_start + logits.shape[1]) of every row).  Each
+        rank selects its slice's top-k candidates; in fused mode the select
+        kernel stores them into every peer's candidate buffer and a merge kernel
+        (after a bounded wait on the peers' flags) finishes every row; in NCCL
+        mode an all-gather moves them.  All ranks draw the same tokens."""
+        c = cuda_ops()
+        err = ops.error_buffer(logits.device)
+        B = logits.shape[0]
+        if B > self.sample_rows:
+            raise ValueError(f"{B} sampling rows exceed the sampler exchange buffers ({self.sample_rows})")
+        W, r = self.world_size, self.rank
+        if self.bufs is not None:
+            c.sample(logits, temperature, top_k, top_p, rep_penalty, counts, slots, rng, out, occ, occ_n,
+                     int(vocab_start), int(vocab_size), None, 0, list(self.bufs["cand"]), list(self.bufs["flags"]),
+                     r, self.sample_rows, self.samp_ctr, self.timeout_ns, err)
+            return
+        local = self.cand_local.data_ptr()
+        ptrs = [0] * W
+        ptrs[r] = local
+        c.sample(logits, temperature, top_k, top_p, rep_penalty, counts, slots, rng, out, occ, occ_n,
+                 int(vocab_start), int(vocab_size), None, 0, ptrs, [], r, self.sample_rows, self.samp_ctr, 0, err)
+        blk = self.cand_local[0]
+        self.dist.all_gather_into_tensor(blk.view(-1), blk[r].reshape(-1), group=self.group)
+        c.sample_merge(logits, temperature, top_k, top_p, slots, rng, out, int(vocab_size), [local] * W, r,
+                       self.sample_rows, self.samp_ctr, err)
 
     # -------------------------------------------------------------- helpers
     def min_int(self, v: int) -> int:
@@ -181,8 +235,8 @@ class TPComm:
         if self.mode == "scatter" and isinstance(w, torch.Tensor):  # quantized weights take the pull path
             c.gemm_scatter(x, w, b["recv"], self.rank, rpr, self.hidden, err)
             c.tp_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden,
-                           self.epoch, err)
+                           self.epoch, err, self.timeout_ns)
         else:
             ops.linear(x, w, out=self.partial_buf[:T])
             c.tp_pull_reduce_ag(b["recv"], b["hidden"], b["flags"], self.rank, rpr, T, self.hidden, self.hidden,
-                                self.epoch, err)
+                                self.epoch, err, self.timeout_ns)

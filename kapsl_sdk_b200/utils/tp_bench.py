@@ -102,7 +102,7 @@ def main():
             fn = lambda: c.gemm_scatter(x, w, tp.bufs["recv"], rank, rpr, NO, err)
         elif mode == "reduce_only":
             fn = lambda: c.tp_reduce_ag(tp.bufs["recv"], tp.bufs["hidden"], tp.bufs["flags"], rank, rpr, M, NO, NO,
-                                        tp.epoch, err)
+                                        tp.epoch, err, tp.timeout_ns)
         else:
             fn = lambda: tp.row_parallel_residual(x, w, h)
         for _ in range(3):

@@ -265,12 +265,101 @@ def test_sampler_matches_reference(dev):
     topp = torch.tensor([p[2] for p in params], dtype=torch.float32, device=dev)
     rng = torch.tensor([s - (1 << 64) if s >= 1 << 63 else s for s in states], dtype=torch.int64, device=dev)
     out = torch.zeros(B, dtype=torch.int32, device=dev)
-    # row 5 has top_k 0 (whole vocab): the kernel keeps the best 1024 candidates; with T=0.8, top_p 0.8
-    # over 152k random logits the nucleus is far larger, so only rows 0-4 are compared exactly.
-    ops.sample(logits.to(dev).clone(), temp, topk, topp, rng, out)
-    for i in range(5):
-        tok, _ = ref.sample_next_token(logits[i].numpy(), *params[i], states[i])
+    # row 5 has top_k 0: the whole vocabulary in the reference's order (T=0.8, top_p 0.8 over 152k
+    # random logits keeps a nucleus of ~100k ids)
+    ops.sample(logits.to(dev).clone(), temp, topk, topp, rng, out, full_scratch=ops.sample_full_scratch(V, dev, 4),
+               full_ctas=4)
+    for i in range(B):
+        tok, st = ref.sample_next_token(logits[i].numpy(), *params[i], states[i])
         assert int(out[i]) == tok, (i, int(out[i]), tok)
+        assert int(rng[i]) & ((1 << 64) - 1) == st, i  # the LCG advanced exactly as the reference's
+
+
+def test_sampler_sparse_penalty_matches_dense(dev):
+    """The occurrence lists (ids that occurred, per slot) give the same penalised
+    draws as scanning the dense counts, over many rows and parameter mixes."""
+    from kapsl_sdk_b200 import ops
+    from kapsl_sdk_b200.ops import reference as ref
+
+    V, B = 32000, 64
+    g = torch.Generator().manual_seed(9)
+    logits = torch.randn(B, V, generator=g) * 2
+    hist = [torch.randint(0, V, (int(n),), generator=g).tolist() for n in torch.randint(0, 300, (B,), generator=g)]
+    for i in range(B):  # make some penalised ids the top candidates
+        for t in hist[i][:3]:
+            logits[i, t] = 8.0
+    counts = torch.zeros(B, V, dtype=torch.int32, device=dev)
+    occ = torch.zeros(B, 512, dtype=torch.int32, device=dev)
+    occ_n = torch.zeros(B, dtype=torch.int32, device=dev)
+    rows = torch.tensor([i for i in range(B) for _ in hist[i]], dtype=torch.int32, device=dev)
+    ids = torch.tensor([t for i in range(B) for t in hist[i]], dtype=torch.int32, device=dev)
+    ops.count_tokens(counts, rows, ids, occ, occ_n)
+    assert occ_n.tolist() == [len(set(h)) for h in hist]
+    temp = torch.tensor([[0.0, 0.7, 1.2][i % 3] for i in range(B)], device=dev)
+    topk = torch.tensor([[1, 40, 7, 1024][i % 4] for i in range(B)], dtype=torch.int32, device=dev)
+    topp = torch.tensor([[1.0, 0.9, 0.5][i % 3] for i in range(B)], device=dev)
+    pen = torch.tensor([[1.15, 1.0, 2.0, 0.8][i % 4] for i in range(B)], device=dev)
+    states = [ref.seed_state(None, f"p-{i}", i + 1) for i in range(B)]
+    outs = []
+    for sparse in (True, False):
+        rng = torch.tensor([s - (1 << 64) if s >= 1 << 63 else s for s in states], dtype=torch.int64, device=dev)
+        out = torch.zeros(B, dtype=torch.int32, device=dev)
+        ops.sample(logits.to(dev), temp, topk, topp, rng, out, rep_penalty=pen, counts=counts,
+                   occ=occ if sparse else None, occ_n=occ_n if sparse else None)
+        outs.append(out.tolist())
+    assert outs[0] == outs[1]
+    for i in range(B):
+        pl = ref.apply_repetition_penalty(logits[i].numpy(), hist[i], float(pen[i]))
+        tok, _ = ref.sample_next_token(pl, float(temp[i]), int(topk[i]), float(topp[i]), states[i])
+        assert outs[0][i] == tok, (i, outs[0][i], tok)
+
+
+@pytest.mark.parametrize("W", [2, 8])
+def test_vocab_parallel_sampler_emulated(dev, W):
+    """The vocabulary-parallel path on one GPU: W 'ranks' each select over their
+    slice of the logits and store their candidates into the exchange buffer
+    (one buffer stands for every peer's; no flags, as after an all-gather); the
+    merge kernel then draws every row.  Tokens and LCG states equal the
+    reference sampler's over the whole vocabulary."""
+    from kapsl_sdk_b200 import _cuda, ops
+    from kapsl_sdk_b200.models.llama import vocab_slice
+    from kapsl_sdk_b200.ops import reference as ref
+
+    V, B = 152064, 33
+    Vs = vocab_slice(V, W)
+    g = torch.Generator().manual_seed(5)
+    logits = torch.randn(B, V, generator=g) * 3
+    params = [[(0.0, 0, 1.0), (0.7, 40, 0.9), (1.0, 5, 1.0), (0.5, 1, 0.5), (1.3, 1024, 0.95)][i % 5]
+              for i in range(B)]
+    temp = torch.tensor([p[0] for p in params], device=dev)
+    topk = torch.tensor([p[1] for p in params], dtype=torch.int32, device=dev)
+    topp = torch.tensor([p[2] for p in params], device=dev)
+    states = [ref.seed_state(7, f"vp-{i}", i + 1) for i in range(B)]
+    padded = torch.zeros(B, Vs * W)
+    padded[:, :V] = logits
+    cand = torch.zeros(2, W, B, 1024, 2, dtype=torch.float32, device=dev)
+    err = ops.error_buffer(dev)
+    err.zero_()
+    rng = torch.tensor([s - (1 << 64) if s >= 1 << 63 else s for s in states], dtype=torch.int64, device=dev)
+    out = torch.full((B,), -1, dtype=torch.int32, device=dev)
+    ctr = torch.zeros(2, dtype=torch.int64, device=dev)
+    c = _cuda
+    for r in range(W):  # select on each slice; candidates land in block [0][r]
+        sl = padded[:, r * Vs:(r + 1) * Vs].contiguous().to(dev)
+        c.sample(sl, temp, topk, topp, None, None, None, rng, out, None, None, r * Vs, V, None, 0,
+                 [cand.data_ptr()] * W, [], r, B, ctr, 0, err)
+    rng2 = rng.clone()
+    out2 = torch.full((B,), -1, dtype=torch.int32, device=dev)
+    c.sample_merge(padded[:, :Vs].contiguous().to(dev), temp, topk, topp, None, rng2, out2, V,
+                   [cand.data_ptr()] * W, W - 1, B, ctr, err)
+    torch.cuda.synchronize()
+    assert int(err.max()) == 0
+    assert int(out.min()) == -1  # select alone draws nothing
+    for i in range(B):
+        tok, st = ref.sample_next_token(logits[i].numpy(), *params[i], states[i])
+        assert int(out2[i]) == tok, (i, int(out2[i]), tok)
+        if params[i][0] > 0:
+            assert int(rng2[i]) & ((1 << 64) - 1) == st, i
 
 
 def test_sampler_penalty_counts(dev):
