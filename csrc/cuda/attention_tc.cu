@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int h = 0; h < 2; ++h) tma_load_3d(s.q + h * kHalfBytes, &q_map, &s.q_full, h * 64, kvh * g, row0 + t0);
       for (int j = 0; j < ntiles && !s.abort_flag; ++j) {
         const int st = j & 1;
-        if (j >= 2 && !wait_or_abort(s, &s.kv_empty[st], ((j >> 1) - 1) & 1, err, 61)) break;
+        if (j >= 2 && !wait_or_abort(s, &s.kv_empty[st], ((j >> 1) - 1) & 1, err, 71)) break;
         mbar_arrive_expect_tx(&s.kv_full[st], 2u * kTileBytes);
         for (int pg = 0; pg < kKeys / kPage; ++pg) {
           const int page = j * (kKeys / kPage) + pg;
@@ -157,8 +157,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t q_addr = smem_u32(s.q), p_addr = smem_u32(s.p);
       auto issue_s = [&](int j) -> bool {
         const int st = j & 1;
-        if (!wait_or_abort(s, &s.kv_full[st], (j >> 1) & 1, err, 62)) return false;
-        if (j >= 2 && !wait_or_abort(s, &s.s_free[st], ((j >> 1) - 1) & 1, err, 63)) return false;
+        if (!wait_or_abort(s, &s.kv_full[st], (j >> 1) & 1, err, 72)) return false;
+        if (j >= 2 && !wait_or_abort(s, &s.s_free[st], ((j >> 1) - 1) & 1, err, 73)) return false;
         tc_fence_after();
         const uint32_t k_addr = smem_u32(s.k[st]);
         for (int kk = 0; kk < kD / 16; ++kk) {
@@ -169,10 +169,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         mma_commit(&s.s_full[st]);
         return true;
       };
-      bool ok = wait_or_abort(s, &s.q_full, 0, err, 64) && issue_s(0);
+      bool ok = wait_or_abort(s, &s.q_full, 0, err, 74) && issue_s(0);
       for (int j = 0; ok && j < ntiles; ++j) {
         if (j + 1 < ntiles && !issue_s(j + 1)) break;
-        if (!wait_or_abort(s, &s.p_full, j & 1, err, 65)) break;
+        if (!wait_or_abort(s, &s.p_full, j & 1, err, 75)) break;
         tc_fence_after();
         const uint32_t v_addr = smem_u32(s.v[j & 1]);
         for (int kk = 0; kk < kKeys / 16; ++kk) {
@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
       const int st = j & 1;
-      if (!wait_or_abort(s, &s.s_full[st], (j >> 1) & 1, err, 66)) { ok = false; break; }
+      if (!wait_or_abort(s, &s.s_full[st], (j >> 1) & 1, err, 76)) { ok = false; break; }
       tc_fence_after();
       const uint32_t s_tmem = tmem + lane_off + st * kKeys;
       // pass 1: row max of the scaled, masked scores
@@ -219,7 +219,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float corr = exp2f(m - m_new);  // 0 on the first tile (m = -inf)
       // the previous tile's P.V is done: fold it into o (it also frees P)
       if (j > 0) {
-        if (!wait_or_abort(s, &s.o_full, (j - 1) & 1, err, 67)) { ok = false; break; }
+        if (!wait_or_abort(s, &s.o_full, (j - 1) & 1, err, 77)) { ok = false; break; }
         tc_fence_after();
         const uint32_t o_tmem = tmem + lane_off + 2 * kKeys + half * 64;
         float ov[32];
@@ -264,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(&s.p_full);
       mbar_arrive(&s.s_free[st]);
     }
-    if (ok && ntiles > 0 && wait_or_abort(s, &s.o_full, (ntiles - 1) & 1, err, 68)) {
+    if (ok && ntiles > 0 && wait_or_abort(s, &s.o_full, (ntiles - 1) & 1, err, 78)) {
       tc_fence_after();
       const uint32_t o_tmem = tmem + lane_off + 2 * kKeys + half * 64;
       float ov[32];

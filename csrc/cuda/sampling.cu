@@ -475,7 +475,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_merge_kernel(SampleArgs a
     ok_sh = 1;
     if (a.flags[a.rank] != nullptr && !wait_flags(a.flags[a.rank] + 2 * 8, a.world, epoch, (uint64_t)a.timeout_ns)) {
       ok_sh = 0;
-      atomicExch(a.err, 40);
+      atomicExch(a.err, 50);
     }
   }
   __syncthreads();
@@ -710,7 +710,7 @@ void launch_sample_merge(const SampleLaunch& l, cudaStream_t st) {
   fill_args(a, l);
   const size_t smem = (size_t)l.world * kMaxTopK * 8;
   static std::atomic<uint64_t> attr_devs{0};
-  ensure_smem_attr(attr_devs, sample_merge_kernel, smem);
+  ensure_smem_attr(attr_devs, sample_merge_kernel, (size_t)8 * kMaxTopK * 8);  // the largest group's need
   sample_merge_kernel<<<l.B, kSampThreads, smem, st>>>(a);
   KAPSL_LAUNCH_CHECK();
   note_launch();

@@ -432,4 +432,6 @@ class LLMBackend(Engine):
                                framework="llm", peak_concurrency=max(1, self._peak))
 
     def health_check(self) -> bool:
-        return self.engine is not None and self._thread is not None and self._thread.is_alive()
+        eng = self.engine
+        return (eng is not None and self._thread is not None and self._thread.is_alive()
+                and getattr(eng, "failed", None) is None)

@@ -58,6 +58,7 @@ class EngineConfig:
     # launch step k+1 before reading step k's tokens: None = on for GPU engines (the CPU
     # backend computes inside launch, so overlapping would only delay its tokens), True / False force
     overlap_steps: Optional[bool] = None
+    capture_graphs_at_start: bool = True  # capture every decode bucket when the engine is built
 
 
 class LLMEngine:
@@ -115,6 +116,8 @@ class LLMEngine:
         self.runner = ModelRunner(self.model, self.pool, e.max_num_seqs, e.max_num_batched_tokens, e.max_model_len,
                                   e.use_cuda_graph)
         self._finish_init(cfg, e, nblocks, tp_comm)
+        if e.use_cuda_graph and e.capture_graphs_at_start:
+            self.runner.capture_all()
 
     def _finish_init(self, cfg: ModelConfig, e: EngineConfig, nblocks: int, tp_comm) -> None:
         self.allocator = make_allocator(nblocks, e.block_size, e.enable_prefix_cache, e.eviction)
@@ -123,6 +126,7 @@ class LLMEngine:
                                    e.swap_space_bytes // self.pool.layout.bytes_per_block())
         self._swapped_kv: dict = {}  # seq_id -> host copy of its computed pages
         self._inflight = None  # launched step whose tokens the host has not applied yet
+        self.failed: Optional[EngineError] = None  # set when a step failed on the device
         self._seq_ids = itertools.count(1)
         self.sessions: dict[str, Sequence] = {}
         self.finished: list[Sequence] = []
@@ -180,11 +184,19 @@ class LLMEngine:
             if len(history) + len(prompt_ids) + params.max_new_tokens <= max_sess:
                 prompt_ids = history + prompt_ids
         rng = ref.seed_state(params.seed, request_id, seq_id)
-        seq = Sequence(seq_id=seq_id, request_id=request_id, prompt_ids=prompt_ids, params=params, rng_state=rng,
-                       session_id=session_id, on_token=on_token)
         if len(prompt_ids) + 1 > self.ecfg.max_model_len:
             raise EngineError.invalid_input(
                 f"prompt of {len(prompt_ids)} tokens exceeds max_model_len {self.ecfg.max_model_len}")
+        return self.adopt_request(request_id, prompt_ids, params, seq_id, rng, session_id, on_token)
+
+    def adopt_request(self, request_id: str, prompt_ids: list, params: SamplingParams, seq_id: int,
+                      rng_state: int, session_id: Optional[str] = None, on_token: Optional[Callable] = None
+                      ) -> Sequence:
+        """Queue a request whose checks, session history and sampler seed another
+        engine already resolved (the leader of a tensor-parallel serving group
+        publishes exactly these fields, so every rank queues identical sequences)."""
+        seq = Sequence(seq_id=seq_id, request_id=request_id, prompt_ids=list(prompt_ids), params=params,
+                       rng_state=rng_state, session_id=session_id, on_token=on_token)
         self.scheduler.add(seq)
         if session_id is not None:
             self.sessions[session_id] = seq
@@ -286,7 +298,13 @@ class LLMEngine:
             on = self.device.type == "cuda"
         return bool(on) and self.pp is None and self.kv_export is None
 
+    def health_check(self) -> bool:
+        """False once a step failed on the device (see :class:`DeviceError`)."""
+        return self.failed is None
+
     def step(self) -> list[StepOutput]:
+        if self.failed is not None:
+            raise self.failed
         if self.pp is not None or self.kv_export is not None:
             outs = self._drain()
             return outs + self._step_serial()
@@ -371,7 +389,15 @@ class LLMEngine:
         is already in flight drops that step's placeholder (its token is ignored
         when that step completes: the sequence is finished by then)."""
         prof = self.profile is not None
-        seqs, toks = self.runner.collect(inf)
+        try:
+            seqs, toks = self.runner.collect(inf)
+        except EngineError as e:
+            # a kernel's bounded wait ran out (lost peer, stalled copy): the step's
+            # tokens are invalid and the engine stops serving; health_check turns
+            # false so a replica pool routes around it
+            self.failed = e
+            self._inflight = None
+            raise
         now = time.perf_counter()
         outs = []
         for s, idx, tok in zip(seqs, inf.out_idx, toks.tolist()):

@@ -29,6 +29,7 @@ import torch
 
 from .. import ops
 from .._ext import launch_count
+from ..engine_api import EngineError, ErrorKind
 from ..models.llama import CausalLM, ForwardBatch
 from ..ops import reference as ref
 from .kv_cache import KVPool
@@ -66,13 +67,25 @@ class _Layout:
 class Inflight:
     """A launched step: its sampling sequences (row order of ``out_tokens``), the
     pinned buffer its tokens are read back into, and the event after that copy."""
-    __slots__ = ("step_id", "seqs", "R", "h_out", "done", "start", "kind", "num_tokens", "out_idx", "launch_s")
+    __slots__ = ("step_id", "seqs", "R", "h_out", "done", "start", "kind", "num_tokens", "out_idx", "launch_s",
+                 "h_err")
 
     def __init__(self, step_id, seqs, R, h_out, done, start, kind, num_tokens):
         self.step_id, self.seqs, self.R, self.h_out = step_id, seqs, R, h_out
         self.done, self.start, self.kind, self.num_tokens = done, start, kind, num_tokens
         self.out_idx: list = []
         self.launch_s = 0.0
+        self.h_err = None
+
+
+class DeviceError(EngineError):
+    """A kernel of the step recorded a status code: a bounded wait on a peer or a
+    pipeline stage ran out (a lost tensor-parallel rank, a stalled copy).  The
+    step's results are not valid and the engine stops serving."""
+
+    def __init__(self, code: int):
+        super().__init__(ErrorKind.BACKEND, ops.describe_error(code))
+        self.code = code
 
 
 class ModelRunner:
@@ -95,6 +108,8 @@ class ModelRunner:
         self._h32s = [torch.zeros(self.L.n32, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self._h64s = [torch.zeros(self.L.n64, dtype=torch.int64, pin_memory=True) for _ in range(2)]
         self._houts = [torch.zeros(S, dtype=torch.int32, pin_memory=True) for _ in range(2)]
+        # the kernels' status words, read back with every step's tokens (no extra sync)
+        self._herrs = [torch.zeros(16, dtype=torch.int32, pin_memory=True) for _ in range(2)]
         self._buf = 1
         self._select(0)
         self.d32 = torch.zeros(self.L.n32, dtype=torch.int32, device=self.device)
@@ -127,6 +142,7 @@ class ModelRunner:
         """Make staging set ``buf`` the one _fill writes and _h2d copies."""
         self._buf = buf
         self.h32, self.h64, self.h_out = self._h32s[buf], self._h64s[buf], self._houts[buf]
+        self.h_err = self._herrs[buf]
         self.n32 = self.h32.numpy()
         self.n64 = self.h64.numpy()
         self.f32view = self.n32.view(np.float32)
@@ -378,12 +394,14 @@ class ModelRunner:
                 self._sample(logits, R, full)
             self.launches += launch_count() - c0
         self.h_out[:R].copy_(self.out_tokens[:R], non_blocking=True)
+        self.h_err.copy_(ops.error_buffer(self.device), non_blocking=True)
         done = torch.cuda.Event(enable_timing=prof is not None)
         done.record()
         self._step_id += 1
         self.stats["d2h_bytes"] += R * 4
         self.stats["steps"] += 1
         inf = Inflight(self._step_id, sample_seqs, R, self.h_out, done, ev0, "graph" if gsize else "eager", T)
+        inf.h_err = self.h_err
         if prof is not None:
             inf.launch_s = time.perf_counter() - tl0
             self._tally(f"{inf.kind}_launch_s", inf.launch_s)
@@ -402,6 +420,12 @@ class ModelRunner:
             trace = self.prof.get("trace")
             if trace is not None:  # per step: kind, tokens, sampling rows, host launch s, device s
                 trace.append((inf.kind, inf.num_tokens, inf.R, round(inf.launch_s, 6), round(dev_s, 6)))
+        if inf.h_err is not None:
+            codes = inf.h_err.numpy()
+            if codes.any():
+                code = int(codes[codes != 0][0])
+                ops.error_buffer(self.device).zero_()
+                raise DeviceError(code)
         return inf.seqs, inf.h_out[:inf.R].numpy().copy()
 
     def _tally(self, key: str, v) -> None:
@@ -417,6 +441,38 @@ class ModelRunner:
         out = self.model.forward(fb, self.pool.k, self.pool.v)
         torch.cuda.current_stream(self.device).synchronize()
         return out
+
+    def capture_all(self) -> int:
+        """Capture the decode graph of every batch bucket now (engine start-up), so
+        no capture (a synchronize, a warm-up pass and a graph build, ~0.1 s each)
+        lands in the middle of serving.  Inputs are padding rows (no KV write,
+        a 1-token context on block 0).  Every rank of a tensor-parallel group
+        runs this at the same point (the warm-up passes hold collectives)."""
+        if not self.use_graph:
+            return 0
+        L, n32, n64, f32 = self.L, self.n32, self.n64, self.f32view
+        MB = self.max_blocks
+        n = 0
+        for B in self.graph_sizes:
+            if (B, False) in self.graphs:
+                continue
+            n32[L.ids:L.ids + B] = 0
+            n32[L.src:L.src + B] = -1
+            n32[L.pos:L.pos + B] = 0
+            n64[L.slots:L.slots + B] = -1
+            n32[L.ctx:L.ctx + B] = 1
+            n32[L.bt + np.arange(B, dtype=np.int64) * MB] = 0
+            n64[L.lidx:L.lidx + B] = np.arange(B, dtype=np.int64)
+            n32[L.sslot:L.sslot + B] = self.pad_slot
+            f32[L.temp:L.temp + B] = 0.0
+            n32[L.topk:L.topk + B] = 0
+            f32[L.topp:L.topp + B] = 1.0
+            f32[L.pen:L.pen + B] = 1.0
+            self._h2d()
+            self._capture(B, False)
+            n += 1
+        torch.cuda.synchronize(self.device)
+        return n
 
     def _graph_splits(self, B: int) -> int:
         return int(ops.cuda_ops().decode_num_splits(B, self.model.hkv, self.max_blocks * self.bs))

@@ -30,6 +30,30 @@ def error_buffer(device: torch.device) -> torch.Tensor:
     return buf
 
 
+# Status codes the kernels record in the error buffer when a bounded wait runs out
+# (or a size check fails); 0 = ok.
+DEVICE_ERRORS = {
+    1: "decode attention: a KV page load did not arrive within its wait limit",
+    2: "prefill attention: a KV page load did not arrive within its wait limit",
+    **{c: "GEMM pipeline wait ran out (1-SM kernel)" for c in range(10, 14)},
+    **{c: "GEMM pipeline wait ran out (2-SM kernel)" for c in range(20, 24)},
+    30: "tensor-parallel reduction (push): a peer missed barrier 1",
+    31: "tensor-parallel reduction (push): a peer missed barrier 2",
+    32: "tensor-parallel reduction (pull): a peer missed barrier 1",
+    33: "tensor-parallel reduction (pull): a peer missed barrier 2",
+    40: "MoE permute: expert rows exceed the sorted buffer",
+    41: "MoE combine: a peer missed barrier 1",
+    42: "MoE combine: a peer missed barrier 2",
+    50: "vocab-parallel sampler: a peer's candidates did not arrive",
+    **{c: "Q4_K GEMM pipeline wait ran out" for c in range(60, 67)},
+    **{c: "tcgen05 prefill attention pipeline wait ran out" for c in range(71, 79)},
+}
+
+
+def describe_error(code: int) -> str:
+    return f"device error {code}: {DEVICE_ERRORS.get(code, 'unknown status')}"
+
+
 def check_errors(device: torch.device) -> int:
     """Return (and clear) the first non-zero kernel status word on ``device``."""
     buf = error_buffer(device)

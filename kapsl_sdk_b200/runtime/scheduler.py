@@ -243,8 +243,16 @@ class Scheduler:
         return sum(q.depth() for q in self.high), sum(q.depth() for q in self.low)
 
     def is_healthy(self) -> bool:
+        """Every queue below 80% of its capacity (reference scheduler.rs:284-304),
+        and no engine reporting itself unhealthy (e.g. a device fault)."""
         lim = 0.8 * self.queue_size
-        return all(q.depth() < lim for q in self.high + self.low)
+        if not all(q.depth() < lim for q in self.high + self.low):
+            return False
+        for e in self.engines:
+            hc = getattr(e, "health_check", None)
+            if hc is not None and not hc():
+                return False
+        return True
 
     def get_metrics(self) -> EngineMetrics:
         m = self.engines[0].metrics()

@@ -167,3 +167,59 @@ def test_kv_admission_limits():
     eng.add_request("a", list(range(3, 50)), SamplingParams(max_new_tokens=40), admission_control=True)
     with pytest.raises(EngineError, match="soft limit"):
         eng.add_request("b", list(range(3, 40)), SamplingParams(max_new_tokens=10), admission_control=True)
+
+
+@pytest.mark.gpu
+def test_peer_wait_runs_out_and_engine_reports_failure():
+    """(1) The fused tensor-parallel reduction on one GPU with world 2, the 'peer'
+    a second local allocation whose flags nothing posts, and a 1 ms wait limit:
+    the kernel returns within milliseconds and records status 32/33 instead of
+    hanging.  (2) An engine whose step reads back such a status raises an
+    EngineError naming it and reports itself unhealthy from then on."""
+    import torch
+
+    from kapsl_sdk_b200 import ops
+    from kapsl_sdk_b200._ext import cuda_ops
+    from kapsl_sdk_b200.engine_api import EngineError
+    from kapsl_sdk_b200.llm.engine import EngineConfig, LLMEngine
+    from kapsl_sdk_b200.llm.sequence import SamplingParams
+    from kapsl_sdk_b200.models.config import ModelConfig
+
+    c = cuda_ops()
+    dev = torch.device("cuda", 0)
+    rows, cols, W = 64, 256, 2
+    part = [torch.zeros(rows, cols, dtype=torch.bfloat16, device=dev) for _ in range(W)]
+    hid = [torch.zeros(rows, cols, dtype=torch.bfloat16, device=dev) for _ in range(W)]
+    flags = [torch.zeros(32, dtype=torch.int64, device=dev) for _ in range(W)]
+    epoch = torch.zeros(16, dtype=torch.int64, device=dev)
+    err = ops.error_buffer(dev)
+    err.zero_()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    c.tp_pull_reduce_ag([p.data_ptr() for p in part], [h.data_ptr() for h in hid], [f.data_ptr() for f in flags],
+                        0, rows // W, rows, cols, cols, epoch, err, 1_000_000)
+    torch.cuda.synchronize()
+    assert time.perf_counter() - t0 < 2.0
+    code = int(err.max())
+    assert code in (32, 33), code
+    err.zero_()
+    torch.cuda.synchronize()
+
+    cfg = ModelConfig(name="small", arch="qwen2", vocab_size=2048, hidden_size=512, intermediate_size=1024,
+                      num_layers=2, num_heads=4, num_kv_heads=2, head_dim=128, rope_theta=1e6, rms_eps=1e-6,
+                      max_position=4096, bos_token_id=None, eos_token_id=None)
+    eng = LLMEngine(cfg, device=dev, engine_cfg=EngineConfig(max_num_seqs=4, max_num_batched_tokens=128,
+                                                             max_model_len=512, num_blocks=64), seed=0)
+    eng.add_request("a", list(range(10, 50)), SamplingParams.greedy(32, ignore_eos=True))
+    eng.step()
+    assert eng.health_check()
+    err.fill_(32)  # stands in for a peer wait that ran out during the next step
+    with pytest.raises(EngineError, match="missed barrier 1"):
+        for _ in range(3):
+            eng.step()
+    assert not eng.health_check()
+    with pytest.raises(EngineError):
+        eng.step()
+    assert int(err.max()) == 0  # the status was consumed
+    eng.failed = None
+    eng.shutdown()

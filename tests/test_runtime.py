@@ -339,3 +339,32 @@ def test_metrics_http_exporter():
         assert 'kapsl_output_tokens_total{model="llm"} 7.0' in body and "kapsl_ttft_seconds_bucket" in body
     finally:
         srv.shutdown()
+
+
+def test_replica_with_failed_engine_is_routed_around():
+    """An engine whose device step failed reports health_check() False: its
+    scheduler turns unhealthy and the pool routes every request to the other
+    replica, without first trying the failed one."""
+    from kapsl_sdk_b200.runtime.replica_pool import PoolStrategy, ReplicaPool
+
+    class Failed(Echo):
+        failed = True
+
+        def health_check(self):
+            return False
+
+        def infer(self, req):
+            raise AssertionError("a failed replica must not be tried")
+
+    bad, good = Scheduler([Failed()]), Scheduler([Echo()])
+    pool = ReplicaPool(PoolStrategy.ROUND_ROBIN)
+    pool.add_replica(0, bad)
+    pool.add_replica(1, good)
+    try:
+        assert not bad.is_healthy() and good.is_healthy()
+        assert pool.healthy_count() == 1
+        for i in range(4):
+            assert pool.infer(InferenceRequest(pkt(bytes([i])))).data == bytes([i])
+    finally:
+        for x in (bad, good):
+            x.shutdown()
