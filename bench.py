@@ -13,12 +13,14 @@ penalty 1.15).  One benchmark "step" serves the whole workload to completion.
     python bench.py --impl reference ...                      reference arm
 
 The device-timed value brackets the K steps with CUDA events (barrier +
-synchronize on both sides, max over ranks).  The ``e2e`` value runs the same
-workload through ``LLMEngine.generate`` (the public API) and times it with the
-host clock; every engine step copies its inputs host->device from pinned
-memory and reads its sampled tokens back device->host.  Weights (15 GB) and
-the KV working set are far larger than the 126 MB L2, so no explicit L2
-flush is needed between steps.
+synchronize on both sides, max over ranks).  The ``e2e`` value serves one more
+copy of the workload through the wire API: rank 0 runs the socket server and
+LLMBackend (the other ranks follow its steps), and client processes stream
+every request with ``KapslClient.infer_stream``; it is timed with the host
+clock from the first request sent to the last token received.  Every engine
+step copies its inputs host->device from pinned memory and reads its sampled
+tokens back device->host.  Weights (15 GB) and the KV working set are far
+larger than the 126 MB L2, so no explicit L2 flush is needed between steps.
 """
 from __future__ import annotations
 
@@ -257,6 +259,8 @@ def main():
     if engine.profile is not None:
         for k in list(engine.profile):
             engine.profile[k] = 0
+        if os.environ.get("KAPSL_TRACE_DIR"):
+            engine.profile["trace"] = []
         if tp_comm is not None and hasattr(tp_comm, "phase_times"):
             tp_comm.phase_times(reset=True)
     wall0 = time.perf_counter()
@@ -276,6 +280,10 @@ def main():
         barrier()
     ms = start.elapsed_time(end)
     if engine.profile is not None:
+        trace = engine.profile.pop("trace", None)
+        if trace is not None:
+            with open(os.path.join(os.environ["KAPSL_TRACE_DIR"], f"trace_n{world}_r{rank}.json"), "w") as f:
+                json.dump(trace, f)
         prof = {k: (round(v, 4) if isinstance(v, float) else v) for k, v in engine.profile.items()}
         prof.update(rank=rank, wall_s=round(time.perf_counter() - wall0, 3), device_ms=round(ms, 1))
         if tp_comm is not None and hasattr(tp_comm, "phase_times"):
@@ -288,14 +296,14 @@ def main():
     ttft = statistics.median([s.ttft() for s in all_seqs if s.ttft() is not None])
     tpot = statistics.median([s.tpot() for s in all_seqs if s.tpot() is not None])
 
-    # ---------------- end to end through the public API (host clock)
+    # ---------------- end to end through the serving API (host clock)
     barrier()
     e2e_prompts = prompts_for(npass + args.steps)
-    t0 = time.perf_counter()
-    outs = engine.generate(e2e_prompts, params)
-    torch.cuda.synchronize()
-    e2e_s = time.perf_counter() - t0
-    e2e_tokens = sum(len(o) for o in outs)
+    h2d1, d2h1 = engine.runner.stats["h2d_bytes"], engine.runner.stats["d2h_bytes"]
+    group = tp_comm is not None and world > 1  # data-parallel replicas each serve their own copy
+    e2e_tokens, e2e_s = serve_e2e(engine, world if group else 1, rank if group else 0, params, e2e_prompts)
+    e2e_h2d = engine.runner.stats["h2d_bytes"] - h2d1
+    e2e_d2h = engine.runner.stats["d2h_bytes"] - d2h1
     barrier()
 
     vals = torch.tensor([ms, out_tokens, e2e_s, e2e_tokens, ttft, tpot], dtype=torch.float64, device=dev)
@@ -310,7 +318,8 @@ def main():
             tot_e2e_tokens = float(g[:, 3].sum())
         else:
             tot_tokens = float(g[0, 1])
-            tot_e2e_tokens = float(g[0, 3])
+            tot_e2e_tokens = float(g[0, 3])  # served by rank 0
+        e2e_max = float(g[0, 2]) if tp_comm is not None else e2e_max
         ttft_all = float(g[:, 4].max())
         tpot_all = float(g[:, 5].max())
     else:
@@ -332,8 +341,10 @@ def main():
             "p50_ttft_ms": round(ttft_all * 1000, 2), "p50_tpot_ms": round(tpot_all * 1000, 3),
             "clocks": clocks.summary(),
             "e2e": {"value": round(tot_e2e_tokens / e2e_max, 2), "unit": "output tokens/s",
-                    "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h),
-                    "api": "LLMEngine.generate"},
+                    "h2d_bytes_per_step": int(e2e_h2d), "d2h_bytes_per_step": int(e2e_d2h),
+                    "api": "KapslClient.infer_stream over a Unix socket (token-id prompts; rank 0 serves, "
+                           "other ranks follow its steps)",
+                    "timing": "host clock, first request sent to last token received, client processes"},
             "gpu_launches": int(launches),
         }
         print(json.dumps(line))
@@ -342,6 +353,95 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def _e2e_client(sock: str, prompts: list, go, q) -> None:
+    """One client process: a thread per prompt streams it through KapslClient;
+    reports (tokens received, time of the first send, time of the last token)."""
+    import threading
+
+    import numpy as np
+
+    from kapsl_sdk import KapslClient
+
+    got = [0] * len(prompts)
+
+    def run(i):
+        c = KapslClient(sock)
+        data = np.asarray(prompts[i], dtype=np.int32).tobytes()
+        n = 0
+        for _ in c.infer_stream(0, [1, len(prompts[i])], "int32", data):
+            n += 1
+        got[i] = n
+
+    th = [threading.Thread(target=run, args=(i,)) for i in range(len(prompts))]
+    go.wait()
+    t0 = time.monotonic()
+    for t in th:
+        t.start()
+    for t in th:
+        t.join()
+    q.put((sum(got), t0, time.monotonic()))
+
+
+def serve_e2e(engine, world: int, rank: int, params, prompts: list, nclients: int = 4):
+    """Serve ``prompts`` through the wire API: rank 0 runs KapslServer + LLMBackend
+    (over a GroupLeader when world > 1, the other ranks follow its steps) on a
+    Unix socket, and ``nclients`` client processes stream every prompt
+    concurrently with KapslClient.infer_stream.  Returns (tokens, seconds) on
+    rank 0, (0, 0) elsewhere."""
+    import multiprocessing as mp
+    import threading
+
+    from kapsl_sdk_b200.llm.backend import LLMBackend, RuntimeConfig
+    from kapsl_sdk_b200.parallel.group import GroupLeader, StepChannel, follow
+    from kapsl_sdk_b200.server import KapslServer
+
+    chan = None
+    if world > 1:
+        import torch.distributed as dist
+
+        name = [f"kapsl-bench-{os.getpid()}-{os.urandom(3).hex()}" if rank == 0 else None]
+        dist.broadcast_object_list(name, src=0)
+        chan = StepChannel(name[0], world, rank)
+        dist.barrier()
+        if rank != 0:
+            follow(engine, chan)
+            chan.close()
+            return 0, 0.0
+    eng = GroupLeader(engine, chan) if chan is not None else engine
+    backend = LLMBackend(eng, runtime_config=RuntimeConfig(sampling=params), own_thread=False)
+    tmp = tempfile.mkdtemp(prefix="kapsl-e2e-")
+    sock = os.path.join(tmp, "kapsl.sock")
+    srv = KapslServer({0: backend}).listen_unix(sock).start()
+    ctx = mp.get_context("spawn")
+    go, q = ctx.Event(), ctx.Queue()
+    procs = [ctx.Process(target=_e2e_client, args=(sock, prompts[i::nclients], go, q), daemon=True)
+             for i in range(nclients)]
+    for p in procs:
+        p.start()
+    results = []
+
+    def watch():
+        for _ in procs:
+            results.append(q.get())
+        backend._stop.set()
+
+    threading.Thread(target=watch, daemon=True).start()
+    time.sleep(3.0)  # client processes import and connect before the start signal
+    go.set()
+    try:
+        backend.run()
+    finally:
+        srv.stop()
+        for p in procs:
+            p.join(30)
+        if chan is not None:
+            eng.stop_followers()
+            chan.close()
+    tokens = sum(r[0] for r in results)
+    secs = max(r[2] for r in results) - min(r[1] for r in results)
+    return tokens, secs
 
 
 def _cpu_server(gguf: str, sock: str, num_requests: int, chunk: int, max_len: int, output_len: int) -> None:
