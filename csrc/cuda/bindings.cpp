@@ -396,6 +396,26 @@ void tp_pull_reduce_ag(std::vector<int64_t> partial, std::vector<int64_t> hidden
                                   kapsl::gemm_num_sms(), (uint64_t)timeout_ns, cur_stream());
 }
 
+void tp_reduce_norm_ag(std::vector<int64_t> partial, std::vector<int64_t> xout, std::vector<int64_t> flags, Tensor h,
+                       Tensor w, double eps, int64_t rank, int64_t rows_per_rank, int64_t rows_total, int64_t ld,
+                       Tensor epoch_ctr, Tensor err, int64_t timeout_ns) {
+  TORCH_CHECK(partial.size() == xout.size() && partial.size() == flags.size(), "tp_reduce_norm_ag: tables differ");
+  TORCH_CHECK(timeout_ns > 0, "tp_reduce_norm_ag: timeout_ns must be positive");
+  CHECK_DT(h, at::kBFloat16, "h");
+  CHECK_DT(w, at::kBFloat16, "w");
+  CHECK_DT(epoch_ctr, at::kLong, "epoch_ctr");
+  TORCH_CHECK(h.dim() == 2 && h.stride(1) == 1 && h.stride(0) == ld && w.numel() == h.size(1) && w.is_contiguous(),
+              "tp_reduce_norm_ag: h [rows, cols] with row stride ld, w [cols]");
+  const c10::cuda::CUDAGuard g(h.device());
+  auto pp = as_ptrs<const __nv_bfloat16>(partial);
+  auto xp = as_ptrs<__nv_bfloat16>(xout);
+  auto fp = as_ptrs<int64_t>(flags);
+  kapsl::launch_tp_reduce_norm_ag(pp.data(), xp.data(), fp.data(), bf(h), reinterpret_cast<const __nv_bfloat16*>(
+                                      w.data_ptr()), (float)eps, (int)pp.size(), (int)rank, (int)rows_per_rank,
+                                  (int)rows_total, (int)h.size(1), ld, epoch_ctr.data_ptr<int64_t>(),
+                                  err.data_ptr<int>(), kapsl::gemm_num_sms(), (uint64_t)timeout_ns, cur_stream());
+}
+
 void p2p_copy(int64_t dst, int64_t src, int64_t bytes, int64_t ctas_per_sm) {
   TORCH_CHECK(bytes % 16 == 0 && dst % 16 == 0 && src % 16 == 0, "p2p_copy: 16-byte aligned sizes and addresses");
   kapsl::launch_p2p_copy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, (int)ctas_per_sm,
@@ -623,6 +643,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_copy_blocks", &kv_copy_blocks, "KV block gather/scatter between device-accessible pools (host swap)");
   m.def("copy_async", &copy_async, "cudaMemcpyAsync on the current stream (copy-engine baseline)");
   m.def("tp_pull_reduce_ag", &tp_pull_reduce_ag, "barrier + pull peers' partial rows + residual + all-gather push");
+  m.def("tp_reduce_norm_ag", &tp_reduce_norm_ag,
+        "barrier + pull peers' partial rows + residual (own rows) + RMSNorm + all-gather of the normed rows");
   m.def("p2p_copy", &p2p_copy, "16-byte vector copy between (possibly peer-mapped) device addresses");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", &symm_free);

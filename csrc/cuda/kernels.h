@@ -136,6 +136,11 @@ void launch_tp_reduce_ag(__nv_bfloat16* const* recv, __nv_bfloat16* const* hidde
 void launch_tp_pull_reduce_ag(__nv_bfloat16* const* partial, __nv_bfloat16* const* hidden, int64_t* const* flags,
                               int world, int rank, int rows_per_rank, int rows_total, int cols, int64_t ld,
                               int64_t* epoch_ctr, int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
+// row-parallel reduction + residual (rows owned by this rank) + RMSNorm + all-gather of the normed rows
+void launch_tp_reduce_norm_ag(const __nv_bfloat16* const* partial, __nv_bfloat16* const* xout,
+                              int64_t* const* flags, __nv_bfloat16* h, const __nv_bfloat16* w, float eps, int world,
+                              int rank, int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr,
+                              int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
 void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st);
 void* symm_alloc(size_t bytes);
 void symm_free(void* p);

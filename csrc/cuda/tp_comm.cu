@@ -216,6 +216,196 @@ __global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
   }
 }
 
+// Pull reduction fused with the residual add, the next RMSNorm and the
+// all-gather of the normed rows.  The residual stream is sharded by rows: this
+// rank keeps (and updates) only the rows it owns; what every rank needs in
+// full is the next GEMM's input x = rmsnorm(h) * w.  One CTA per owned row:
+//   pass 1  h_row += sum over ranks of their partial rows (P2P loads), rounded
+//           to bf16 and stored back; sum of squares of the rounded values
+//   pass 2  x_row = h_row * rsqrt(mean + eps) * w, stored into every rank's x
+// between the usual two flag barriers (partials out / x rows out).
+struct TPNormArgs {
+  const bf16* partial[8];  // peers' partial sums [rows_pad][ld] (their GEMM outputs)
+  bf16* xout[8];           // peers' normed-input buffers [rows_pad][ld]
+  int64_t* flags[8];
+  bf16* h;                 // local residual stream (rows owned by this rank are kept current)
+  const bf16* w;           // RMSNorm weight [cols]
+  float eps;
+  int world, rank, rows_per_rank, rows_total, cols;
+  int64_t ld;
+  int64_t* epoch_ctr;
+  uint64_t timeout_ns;
+  int* err;
+};
+
+static constexpr int kNormThreads = 256;
+static constexpr int kNormMaxChunks = 4;  // 16-byte chunks per thread: cols <= 8 * 256 * 4 = 8192
+
+template <int WORLD>
+__global__ void __launch_bounds__(kNormThreads) tp_reduce_norm_ag_kernel(TPNormArgs a) {
+  __shared__ int64_t epoch_sh;
+  __shared__ int ok_sh;
+  __shared__ float red[kNormThreads / 32];
+  if (threadIdx.x == 0) {
+    epoch_sh = a.epoch_ctr[0] + 1;
+    ok_sh = 1;
+    if (blockIdx.x == 0) {
+      a.epoch_ctr[2] = (int64_t)globaltimer_ns();
+      __threadfence_system();
+      for (int p = 0; p < WORLD; ++p) st_release_sys(a.flags[p] + 0 * 8 + a.rank, epoch_sh);
+    }
+    if (!wait_flags(a.flags[a.rank] + 0 * 8, WORLD, epoch_sh, a.timeout_ns)) {
+      ok_sh = 0;
+      atomicExch(a.err, 34);
+    }
+    if (blockIdx.x == 0) a.epoch_ctr[3] = (int64_t)globaltimer_ns();
+  }
+  __syncthreads();
+  const int64_t epoch = epoch_sh;
+  if (ok_sh) {
+    const int r0 = a.rank * a.rows_per_rank;
+    const int nrows = max(0, min(a.rows_per_rank, a.rows_total - r0));
+    const int chunks = a.cols / 8;
+    const int tid = threadIdx.x;
+    for (int lr = blockIdx.x; lr < nrows; lr += gridDim.x) {
+      const int64_t base = (int64_t)(r0 + lr) * a.ld;
+      uint4 hb[kNormMaxChunks];
+      float ss = 0.f;
+#pragma unroll
+      for (int j0 = 0; j0 < kNormMaxChunks; j0 += 2) {
+        uint4 v[2][WORLD];
+        uint4 hr[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {  // every load of two chunks in flight before any use
+          const int c = tid + (j0 + u) * kNormThreads;
+          if (c < chunks) {
+            hr[u] = *reinterpret_cast<const uint4*>(a.h + base + c * 8);
+#pragma unroll
+            for (int p = 0; p < WORLD; ++p) v[u][p] = *reinterpret_cast<const uint4*>(a.partial[p] + base + c * 8);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int c = tid + (j0 + u) * kNormThreads;
+          if (c >= chunks) continue;
+          float acc[8];
+          const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&hr[u]);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(hp[j]);
+            acc[2 * j] = f.x;
+            acc[2 * j + 1] = f.y;
+          }
+#pragma unroll
+          for (int p = 0; p < WORLD; ++p) {
+            const __nv_bfloat162* vp = reinterpret_cast<const __nv_bfloat162*>(&v[u][p]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 f = __bfloat1622float2(vp[j]);
+              acc[2 * j] += f.x;
+              acc[2 * j + 1] += f.y;
+            }
+          }
+          uint4 o;
+          o.x = pack_bf16(acc[0], acc[1]);
+          o.y = pack_bf16(acc[2], acc[3]);
+          o.z = pack_bf16(acc[4], acc[5]);
+          o.w = pack_bf16(acc[6], acc[7]);
+          *reinterpret_cast<uint4*>(a.h + base + c * 8) = o;
+          hb[j0 + u] = o;
+          const __nv_bfloat162* op = reinterpret_cast<const __nv_bfloat162*>(&o);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // the norm sees the rounded residual, as a separate pass would
+            const float2 f = __bfloat1622float2(op[j]);
+            ss += f.x * f.x + f.y * f.y;
+          }
+        }
+      }
+      ss = warp_sum(ss);
+      if ((tid & 31) == 0) red[tid >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < kNormThreads / 32; ++i) tot += red[i];
+      const float inv = rsqrtf(tot / (float)a.cols + a.eps);
+#pragma unroll
+      for (int j = 0; j < kNormMaxChunks; ++j) {
+        const int c = tid + j * kNormThreads;
+        if (c >= chunks) continue;
+        const uint4 wv = *reinterpret_cast<const uint4*>(a.w + c * 8);
+        const __nv_bfloat162* wp = reinterpret_cast<const __nv_bfloat162*>(&wv);
+        const __nv_bfloat162* hp = reinterpret_cast<const __nv_bfloat162*>(&hb[j]);
+        uint4 o;
+        uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 hv = __bfloat1622float2(hp[q]);
+          const float2 fw = __bfloat1622float2(wp[q]);
+          ow[q] = pack_bf16(hv.x * inv * fw.x, hv.y * inv * fw.y);
+        }
+#pragma unroll
+        for (int p = 0; p < WORLD; ++p) *reinterpret_cast<uint4*>(a.xout[p] + base + c * 8) = o;
+      }
+      __syncthreads();  // red[] is reused by the next row
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const int64_t done = atomicAdd(reinterpret_cast<unsigned long long*>(&a.epoch_ctr[1]), 1ull);
+    if (done == gridDim.x - 1) {
+      a.epoch_ctr[4] = (int64_t)globaltimer_ns();
+      for (int p = 0; p < WORLD; ++p) st_release_sys(a.flags[p] + 1 * 8 + a.rank, epoch);
+      if (!wait_flags(a.flags[a.rank] + 1 * 8, WORLD, epoch, a.timeout_ns)) atomicExch(a.err, 35);
+      a.epoch_ctr[5] = (int64_t)globaltimer_ns();
+      a.epoch_ctr[8] += a.epoch_ctr[3] - a.epoch_ctr[2];
+      a.epoch_ctr[9] += a.epoch_ctr[4] - a.epoch_ctr[3];
+      a.epoch_ctr[10] += a.epoch_ctr[5] - a.epoch_ctr[4];
+      a.epoch_ctr[11] += 1;
+      a.epoch_ctr[1] = 0;
+      a.epoch_ctr[0] = epoch;
+      __threadfence();
+    }
+  }
+}
+
+void launch_tp_reduce_norm_ag(const bf16* const* partial, bf16* const* xout, int64_t* const* flags, bf16* h,
+                              const bf16* w, float eps, int world, int rank, int rows_per_rank, int rows_total,
+                              int cols, int64_t ld, int64_t* epoch_ctr, int* err, int num_sms, uint64_t timeout_ns,
+                              cudaStream_t st) {
+  if (world > 8) throw std::runtime_error("tp: at most 8 ranks");
+  if (cols % 8 != 0 || ld % 8 != 0) throw std::runtime_error("tp: columns must be a multiple of 8");
+  if (cols / 8 > kNormThreads * kNormMaxChunks) throw std::runtime_error("tp: hidden size above 8192");
+  TPNormArgs a{};
+  for (int i = 0; i < world; ++i) {
+    a.partial[i] = partial[i];
+    a.xout[i] = xout[i];
+    a.flags[i] = flags[i];
+  }
+  a.h = h;
+  a.w = w;
+  a.eps = eps;
+  a.world = world;
+  a.rank = rank;
+  a.rows_per_rank = rows_per_rank;
+  a.rows_total = rows_total;
+  a.cols = cols;
+  a.ld = ld;
+  a.epoch_ctr = epoch_ctr;
+  a.timeout_ns = timeout_ns;
+  a.err = err;
+  int grid = std::min(rows_per_rank, num_sms * 4);
+  if (grid < 1) grid = 1;
+  switch (world) {
+    case 2: tp_reduce_norm_ag_kernel<2><<<grid, kNormThreads, 0, st>>>(a); break;
+    case 4: tp_reduce_norm_ag_kernel<4><<<grid, kNormThreads, 0, st>>>(a); break;
+    case 8: tp_reduce_norm_ag_kernel<8><<<grid, kNormThreads, 0, st>>>(a); break;
+    default: throw std::runtime_error("tp: fused norm reduction needs world size 2, 4 or 8");
+  }
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
 void launch_tp_pull_reduce_ag(bf16* const* partial, bf16* const* hidden, int64_t* const* flags, int world, int rank,
                               int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr, int* err,
                               int num_sms, uint64_t timeout_ns, cudaStream_t st) {

@@ -89,9 +89,12 @@ class DeviceError(EngineError):
 
 
 class ModelRunner:
+    pf_tile = 64  # query tokens per prefill-attention work item (the model's kernel decides)
+
     def __init__(self, model: CausalLM, pool: KVPool, max_num_seqs: int = 256, max_num_batched_tokens: int = 2048,
                  max_model_len: int = 4096, use_cuda_graph: bool = True, graph_sizes: Optional[list] = None):
         self.model = model
+        self.pf_tile = getattr(model, "prefill_tile", 64)
         self.pool = pool
         self.device = model.device
         self.bs = pool.layout.block_size
@@ -101,7 +104,7 @@ class ModelRunner:
         self.vocab = model.cfg.vocab_size
         S = max_num_seqs + 1  # one spare slot for graph padding rows
         self.pad_slot = max_num_seqs
-        W = (max_num_batched_tokens + 63) // 64 + max_num_seqs
+        W = (max_num_batched_tokens + self.pf_tile - 1) // self.pf_tile + max_num_seqs
         self.L = _Layout(self.max_tokens, S, self.max_blocks, W)
         # two pinned staging sets, used by alternate steps: while step k's copies may still
         # be queued, step k+1 is filled into the other set
@@ -257,9 +260,10 @@ class ModelRunner:
             n32[L.bt + row * MB:L.bt + row * MB + len(blk)] = blk
             si = L.sinfo + j * 4
             n32[si:si + 4] = (t, n, p0 + n, row)
-            k = (n + 63) // 64  # 64-token work items of this chunk
+            tile = self.pf_tile
+            k = (n + tile - 1) // tile  # work items of this chunk
             n32[L.work + 2 * nwork:L.work + 2 * (nwork + k):2] = j
-            n32[L.work + 2 * nwork + 1:L.work + 2 * (nwork + k):2] = np.arange(0, n, 64, dtype=np.int32)
+            n32[L.work + 2 * nwork + 1:L.work + 2 * (nwork + k):2] = np.arange(0, n, tile, dtype=np.int32)
             nwork += k
             if p0 + n >= s.length:  # chunk completes the prompt: sample from its last token
                 sample_seqs.append(s)

@@ -13,6 +13,7 @@ model code of its own.
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 from typing import Optional
 
@@ -21,6 +22,14 @@ import torch
 from .. import ops
 from ..ops import reference as ref
 from .config import ModelConfig
+
+
+PREFILL_TC_DEFAULT = False
+
+
+def _prefill(model, qkv, k_cache, v_cache, fb, attn) -> None:
+    fn = ops.prefill_attention_tc if model.prefill_tc else ops.prefill_attention
+    fn(qkv, k_cache, v_cache, fb.pf_work, fb.pf_seq_info, fb.block_tables, model.hq, model.hkv, attn, model.scale)
 
 
 @dataclass
@@ -320,6 +329,13 @@ class CausalLM:
                                          scaling=cfg.rope_scaling)
         self.qkv_width = (self.hq + 2 * self.hkv) * self.D
         W = self.tp_size
+        # chunked-prefill attention: the tcgen05 kernel (head group packed into the 128
+        # MMA rows, floor(128 / g) query tokens per work item) or the mma.sync kernel
+        # (64-token work items); KAPSL_PREFILL_TC=0/1 overrides the default
+        env = os.environ.get("KAPSL_PREFILL_TC")
+        self.prefill_tc = (env == "1") if env is not None else PREFILL_TC_DEFAULT
+        g = self.hq // max(self.hkv, 1)
+        self.prefill_tile = (128 // g) if self.prefill_tc and 0 < g <= 128 else 64
         self.vocab_slice = vocab_slice(cfg.vocab_size, W)
         self.vocab_start = (tp_comm.rank if W > 1 else 0) * self.vocab_slice
 
@@ -350,6 +366,8 @@ class CausalLM:
             h = ops.embedding(fb.input_ids[:T], self.w.embed, self.w.vocab_start, out=h, src_rows=fb.src_rows,
                               prev_tokens=fb.prev_tokens)
         attn = torch.empty(T, self.hq * self.D, dtype=torch.bfloat16, device=self.device)
+        if tp and self.moe is None and st is None and self.tp.fused_norm:
+            return self._forward_sharded(fb, k_caches, v_caches, h, attn, full_vocab)
         x = torch.empty_like(h)
         for li, L in enumerate(self.w.layers):
             ops.rmsnorm(h, L.in_norm, cfg.rms_eps, out=x)
@@ -361,8 +379,7 @@ class CausalLM:
                                      self.hq, self.hkv, self.scale, out=attn[:Bd], num_splits=fb.decode_splits,
                                      max_ctx=fb.max_decode_ctx)
             if T > Bd:
-                ops.prefill_attention(qkv, k_caches[li], v_caches[li], fb.pf_work, fb.pf_seq_info, fb.block_tables,
-                                      self.hq, self.hkv, attn, self.scale)
+                _prefill(self, qkv, k_caches[li], v_caches[li], fb, attn)
             if not tp:
                 ops.linear(attn, L.w_o, residual=h, out=h)
             else:
@@ -381,11 +398,43 @@ class CausalLM:
             return None
         xs = h.index_select(0, fb.logits_idx)
         xs = ops.rmsnorm(xs, self.w.final_norm, cfg.rms_eps)
+        return self._lm_head(xs, full_vocab)
+
+    def _lm_head(self, xs: torch.Tensor, full_vocab: bool) -> torch.Tensor:
         if self.tp_size > 1 and not full_vocab:
             head = self.w.lm_head[self.vocab_start:self.vocab_start + self.vocab_slice]
         else:
-            head = self.w.lm_head[:cfg.vocab_size]
+            head = self.w.lm_head[:self.cfg.vocab_size]
         return ops.linear(xs, head, out_dtype=torch.float32)
+
+    def _forward_sharded(self, fb: ForwardBatch, k_caches: list, v_caches: list, h: torch.Tensor,
+                         attn: torch.Tensor, full_vocab: bool) -> torch.Tensor:
+        """Fused tensor-parallel layer loop: every row-parallel GEMM is followed by
+        one kernel that reduces the rows this rank owns, adds them to its shard
+        of the residual stream, applies the next RMSNorm (the next layer's input
+        norm, or the final norm after the last layer) and stores the normed rows
+        into every rank's input buffer.  No separate norm launches and no full
+        residual copies."""
+        cfg = self.cfg
+        T, Bd = fb.num_tokens, fb.num_decode
+        layers = self.w.layers
+        x = self.tp.norm_input(T)
+        ops.rmsnorm(h, layers[0].in_norm, cfg.rms_eps, out=x)  # embedding rows are on every rank
+        for li, L in enumerate(layers):
+            qkv = ops.linear(x, L.w_qkv, bias=L.b_qkv)
+            ops.rope_kv_write(qkv, fb.positions, fb.slots, self.cos_sin, k_caches[li], v_caches[li], self.hq,
+                              self.hkv, self.D)
+            if Bd > 0:
+                ops.decode_attention(qkv[:Bd], k_caches[li], v_caches[li], fb.block_tables[:Bd], fb.ctx_lens[:Bd],
+                                     self.hq, self.hkv, self.scale, out=attn[:Bd], num_splits=fb.decode_splits,
+                                     max_ctx=fb.max_decode_ctx)
+            if T > Bd:
+                _prefill(self, qkv, k_caches[li], v_caches[li], fb, attn)
+            x = self.tp.row_parallel_norm(attn, L.w_o, h, L.post_norm, cfg.rms_eps)
+            g = ops.linear(x, L.w_gu, swiglu=True)
+            nxt = layers[li + 1].in_norm if li + 1 < len(layers) else self.w.final_norm
+            x = self.tp.row_parallel_norm(g, L.w_down, h, nxt, cfg.rms_eps)
+        return self._lm_head(x.index_select(0, fb.logits_idx), full_vocab)
 
 
 def reference_forward(cfg: ModelConfig, full_layers: list, embed: torch.Tensor, lm_head: torch.Tensor,

@@ -109,8 +109,10 @@ class TPComm:
         flag_bytes = 4 * 8 * 8  # sites: 0/1 reduction barriers, 2 sampler candidates, 3 spare
         ep_bytes = self.ep_rows * hidden * 2
         cand_bytes = 2 * W * self.sample_rows * self.SAMPLE_K * 8
+        xn_bytes = rows_pad * hidden * 2
         align = lambda n: (n + 255) // 256 * 256
-        total = align(recv_bytes) + align(hid_bytes) + align(flag_bytes) + align(ep_bytes) + align(cand_bytes)
+        total = (align(recv_bytes) + align(hid_bytes) + align(flag_bytes) + align(ep_bytes) + align(cand_bytes)
+                 + align(xn_bytes))
         base = c.symm_alloc(total)
         handle = c.symm_handle(base)
         handles = [None] * W
@@ -122,11 +124,13 @@ class TPComm:
         off_f = off_h + align(hid_bytes)
         off_e = off_f + align(flag_bytes)
         off_c = off_e + align(ep_bytes)
+        off_x = off_c + align(cand_bytes)
         self.bufs = {
             "base": base, "bases": bases, "rpr": rpr, "rows_pad": rows_pad,
             "recv": [b for b in bases], "hidden": [b + off_h for b in bases], "flags": [b + off_f for b in bases],
-            "ep": [b + off_e for b in bases], "cand": [b + off_c for b in bases],
+            "ep": [b + off_e for b in bases], "cand": [b + off_c for b in bases], "xnorm": [b + off_x for b in bases],
         }
+        self.xnorm_buf = c.tensor_from_ptr(base + off_x, [rows_pad, hidden], "bfloat16", self.device.index)
         dev = self.device.index
         self.ep_buf = (c.tensor_from_ptr(base + off_e, [self.ep_rows, hidden], "bfloat16", dev)
                        if self.ep_rows else None)
@@ -212,6 +216,31 @@ class TPComm:
         if T > self.bufs["rows_pad"]:
             raise ValueError(f"{T} tokens exceed the tensor-parallel buffers ({self.bufs['rows_pad']})")
         return self.hidden_buf[:T]
+
+    @property
+    def fused_norm(self) -> bool:
+        """The fused pull reduction can also apply the next RMSNorm (sharded residual)."""
+        return self.bufs is not None and self.mode == "fused" and self.world_size in (2, 4, 8)
+
+    def norm_input(self, T: int) -> torch.Tensor:
+        """The symmetric buffer the fused reduction writes the next GEMM's input into."""
+        return self.xnorm_buf[:T]
+
+    def row_parallel_norm(self, x: torch.Tensor, w, h: torch.Tensor, norm_w: torch.Tensor,
+                          eps: float) -> torch.Tensor:
+        """``h += all_reduce(x @ w.T)`` for the rows this rank owns (the residual
+        stream is sharded by rows), then returns ``rmsnorm(h) * norm_w`` for every
+        row (every rank's copy written by its owner).  One GEMM into the local
+        partial buffer, then one kernel: barrier, pull of the owned rows'
+        partials from every peer, residual add, RMSNorm, P2P stores of the
+        normed rows, barrier."""
+        T = x.shape[0]
+        b = self.bufs
+        rpr = (T + self.world_size - 1) // self.world_size
+        ops.linear(x, w, out=self.partial_buf[:T])
+        cuda_ops().tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,
+                                     self.hidden, self.epoch, ops.error_buffer(x.device), self.timeout_ns)
+        return self.xnorm_buf[:T]
 
     def row_parallel_linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """NCCL baseline: partial GEMM then all-reduce."""
