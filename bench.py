@@ -69,7 +69,10 @@ def parse_args():
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=1)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", default="kapsl", choices=["kapsl", "reference"])
+    p.add_argument("--impl", default="kapsl", choices=["kapsl", "reference", "b1"],
+                   help="kapsl: this framework; reference: the reference's own build; b1: the in-repo library "
+                        "baseline (cuBLAS via torch, NCCL all-reduce, vLLM flash-attention, torch sampling) on the "
+                        "same engine")
     p.add_argument("--workload", default="qwen2.5-7b", choices=sorted(WORKLOADS),
                    help="named serving workload (model + request shape); the flags below override it")
     p.add_argument("--model", default=None)
@@ -218,11 +221,14 @@ def main():
     if args.parallel == "tp" and world > 1:
         from kapsl_sdk_b200.parallel.tp import TPComm
 
-        tp_comm = TPComm.from_world(mode=args.tp_mode)
+        tp_comm = TPComm.from_world(mode="nccl" if args.impl == "b1" else args.tp_mode)
+    model_cls = None
+    if args.impl == "b1":
+        from kapsl_sdk_b200.models.baseline import BaselineCausalLM as model_cls
     ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
                         max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph,
                         overlap_steps=not args.no_overlap)
-    engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0)
+    engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0, model_cls=model_cls)
     weight_gb = (torch.cuda.memory_allocated(dev) - engine.pool.storage.numel() * engine.pool.storage.element_size()) / 1e9
     # data-parallel replicas serve their own copy of the workload (weak scaling);
     # tensor parallel shares one workload across the ranks (strong scaling).
@@ -326,6 +332,8 @@ def main():
         ms_max, e2e_max, tot_tokens, tot_e2e_tokens, ttft_all, tpot_all = ms, e2e_s, out_tokens, e2e_tokens, ttft, tpot
     value = tot_tokens / (ms_max / 1000.0)
     par = (f"tp{world}" + ("" if world == 1 else f"-{args.tp_mode}")) if args.parallel == "tp" else f"dp{world}"
+    if args.impl == "b1":
+        par += " (library baseline: cuBLAS + NCCL + vLLM flash-attention)"
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
@@ -347,6 +355,8 @@ def main():
                     "timing": "host clock, first request sent to last token received, client processes"},
             "gpu_launches": int(launches),
         }
+        if args.impl == "b1":
+            line["impl"] = "b1-library-baseline"
         print(json.dumps(line))
     engine.shutdown()
     if world > 1:

@@ -48,6 +48,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
                        int max_blocks, const int32_t* __restrict__ ctx_lens, bf16* __restrict__ out,
                        int64_t out_stride, float* __restrict__ part_o, float* __restrict__ part_lse, int Hq,
                        int Hkv, float scale_log2, int* __restrict__ err) {
+  griddep_entry();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte align the dynamic smem base (required by the 128B swizzle).
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(NWARPS * 32)
 
 __global__ void combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_lse,
                                bf16* __restrict__ out, int64_t out_stride, int Hq, int nsplit) {
+  griddep_entry();
   const int head = blockIdx.x, b = blockIdx.y, d = threadIdx.x;
   const int64_t base = ((int64_t)b * Hq + head) * nsplit;
   float M = -INFINITY;
@@ -305,12 +307,12 @@ void launch_decode_attention(const CUtensorMap& tk, const CUtensorMap& tv, const
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
   dim3 grid(nsplit, Hkv, B);
-  kern<<<grid, kDecWarps * 32, smem, st>>>(tk, tv, q, q_stride, block_tables, max_blocks, ctx_lens, out,
+  launch_k(kern, grid, kDecWarps * 32, smem, st, tk, tv, q, q_stride, block_tables, max_blocks, ctx_lens, out,
                                            out_stride, part_o, part_lse, Hq, Hkv, scale * kLog2e, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();
   if (nsplit > 1) {
-    combine_kernel<<<dim3(Hq, B), kD, 0, st>>>(part_o, part_lse, out, out_stride, Hq, nsplit);
+    launch_k(combine_kernel, dim3(Hq, B), kD, 0, st, part_o, part_lse, out, out_stride, Hq, nsplit);
     KAPSL_LAUNCH_CHECK();
     note_launch();
   }
@@ -326,6 +328,7 @@ __global__ void __launch_bounds__(128)
                         const int32_t* __restrict__ seq_info, const int32_t* __restrict__ block_tables,
                         int max_blocks, bf16* __restrict__ out, int64_t out_stride, int Hq, int Hkv,
                         float scale_log2, int* __restrict__ err) {
+  griddep_entry();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES];
@@ -530,7 +533,7 @@ void launch_prefill_attention(const CUtensorMap& tk, const CUtensorMap& tv, cons
   const size_t smem = prefill_attn_smem_bytes();
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
-  kern<<<dim3(num_work, Hq), 128, smem, st>>>(tk, tv, q, q_stride, work, seq_info, block_tables, max_blocks, out,
+  launch_k(kern, dim3(num_work, Hq), 128, smem, st, tk, tv, q, q_stride, work, seq_info, block_tables, max_blocks, out,
                                               out_stride, Hq, Hkv, scale * kLog2e, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();

@@ -89,6 +89,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            const int32_t* __restrict__ seq_info, const int32_t* __restrict__ block_tables,
                            int max_blocks, int Hq, int Hkv, float scale_log2, __nv_bfloat16* __restrict__ out,
                            int64_t out_stride, int* err) {
+  griddep_entry();
   extern __shared__ uint8_t smem_raw[];
   TcSmem& s = *reinterpret_cast<TcSmem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -312,7 +313,7 @@ void launch_prefill_attention_tc(const CUtensorMap& q_map, const CUtensorMap& k_
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, prefill_attn_tc_kernel, smem);
   const float scale_log2 = scale * 1.4426950408889634f;
-  prefill_attn_tc_kernel<<<dim3(nwork, Hkv), kThreads, smem, st>>>(q_map, k_map, v_map, work, seq_info,
+  launch_k(prefill_attn_tc_kernel, dim3(nwork, Hkv), kThreads, smem, st, q_map, k_map, v_map, work, seq_info,
                                                                    block_tables, max_blocks, Hq, Hkv, scale_log2,
                                                                    out, out_stride, err);
   KAPSL_LAUNCH_CHECK();

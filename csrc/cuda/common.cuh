@@ -13,6 +13,7 @@
 #include <atomic>
 #include <stdexcept>
 #include <string>
+#include <utility>
 
 namespace kapsl {
 
@@ -47,6 +48,31 @@ inline void ensure_smem_attr(std::atomic<uint64_t>& done, Kernel* kern, size_t s
   if (bit != 0) done.fetch_or(bit, std::memory_order_acq_rel);
 }
 
+// Programmatic dependent launch.  Every kernel of this library starts with
+// griddep_entry(): it lets the next kernel in the stream begin launching (its
+// CTAs get scheduled and reach their own entry while this grid runs) and then
+// waits until the previous grid has completed and its memory is visible.
+// Because every kernel waits first, a grid never completes before its
+// predecessor, so "previous grid done" implies "every earlier grid done".
+// launch_k() issues a kernel with the attribute that allows the early launch
+// (KAPSL_PDL=0 turns it off: plain stream order).
+bool pdl_enabled();
+
+template <typename... KArgs, typename... Args>
+inline void launch_k(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  KAPSL_CHECK_CUDA(cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...));
+}
+
 // 2-D bf16 tensor map (row-major, `rows` x `cols`, row pitch `pitch_elems`),
 // box = box_rows x box_cols, 128-byte swizzle.  Encoded through the driver
 // entry point so the extension does not link libcuda directly.
@@ -59,6 +85,11 @@ CUtensorMap make_tmap_2d_u8(const void* base, uint64_t rows, uint64_t cols_bytes
 
 // --------------------------------------------------------------- device side
 #ifdef __CUDACC__
+__device__ __forceinline__ void griddep_entry() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(bf16* __restrict__ out, i
                                                        const bf16* __restrict__ x, int64_t x_stride,
                                                        bf16* __restrict__ residual, int64_t res_stride,
                                                        const bf16* __restrict__ w, int H, float eps) {
+  griddep_entry();
   const int row = blockIdx.x;
   const int chunks = H >> 3;
   const Vec8* xr = reinterpret_cast<const Vec8*>(x + row * x_stride);
@@ -102,9 +103,9 @@ void launch_rmsnorm(bf16* out, int64_t out_stride, const bf16* x, int64_t x_stri
     threads = (((chunks + npt - 1) / npt + 31) / 32) * 32;
   }
   switch (npt) {
-    case 1: rmsnorm_kernel<1><<<rows, threads, 0, st>>>(out, out_stride, x, x_stride, residual, res_stride, w, H, eps); break;
-    case 2: rmsnorm_kernel<2><<<rows, threads, 0, st>>>(out, out_stride, x, x_stride, residual, res_stride, w, H, eps); break;
-    case 4: rmsnorm_kernel<4><<<rows, threads, 0, st>>>(out, out_stride, x, x_stride, residual, res_stride, w, H, eps); break;
+    case 1: launch_k(rmsnorm_kernel<1>, rows, threads, 0, st, out, out_stride, x, x_stride, residual, res_stride, w, H, eps); break;
+    case 2: launch_k(rmsnorm_kernel<2>, rows, threads, 0, st, out, out_stride, x, x_stride, residual, res_stride, w, H, eps); break;
+    case 4: launch_k(rmsnorm_kernel<4>, rows, threads, 0, st, out, out_stride, x, x_stride, residual, res_stride, w, H, eps); break;
     default: throw std::runtime_error("rmsnorm: hidden size too large");
   }
   KAPSL_LAUNCH_CHECK();
@@ -122,6 +123,7 @@ __global__ void rope_kv_write_kernel(bf16* __restrict__ qkv, int64_t qkv_stride,
                                      const float* __restrict__ cos_sin,  // [max_pos, D]
                                      bf16* __restrict__ k_cache, bf16* __restrict__ v_cache, int Hq,
                                      int Hkv, int D, int block_size) {
+  griddep_entry();
   const int t = blockIdx.x;
   const int half = D >> 1;
   const int pos = positions[t];
@@ -170,7 +172,7 @@ void launch_rope_kv_write(bf16* qkv, int64_t qkv_stride, const int32_t* position
                           int block_size, cudaStream_t st) {
   if (T == 0) return;
   if (D % 8 != 0) throw std::runtime_error("rope: head_dim must be a multiple of 8");
-  rope_kv_write_kernel<<<T, 256, 0, st>>>(qkv, qkv_stride, positions, slots, cos_sin, k_cache, v_cache, Hq,
+  launch_k(rope_kv_write_kernel, T, 256, 0, st, qkv, qkv_stride, positions, slots, cos_sin, k_cache, v_cache, Hq,
                                           Hkv, D, block_size);
   KAPSL_LAUNCH_CHECK();
   note_launch();
@@ -179,6 +181,7 @@ void launch_rope_kv_write(bf16* qkv, int64_t qkv_stride, const int32_t* position
 // ------------------------------------------------------------------ SwiGLU
 // x: [T, 2F] = [gate | up]; out: [T, F] = silu(gate) * up.
 __global__ void silu_mul_kernel(bf16* __restrict__ out, const bf16* __restrict__ x, int F) {
+  griddep_entry();
   const int t = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c * 8 >= F) return;
@@ -200,7 +203,7 @@ void launch_silu_mul(bf16* out, const bf16* x, int T, int F, cudaStream_t st) {
   if (T == 0) return;
   if (F % 8 != 0) throw std::runtime_error("silu_mul: width must be a multiple of 8");
   dim3 grid((F / 8 + 127) / 128, T);
-  silu_mul_kernel<<<grid, 128, 0, st>>>(out, x, F);
+  launch_k(silu_mul_kernel, grid, 128, 0, st, out, x, F);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -213,6 +216,7 @@ __global__ void embedding_kernel(bf16* __restrict__ out, const bf16* __restrict_
                                  const int32_t* __restrict__ ids, int H, int64_t vocab_start,
                                  int64_t vocab_rows, const int32_t* __restrict__ src_rows,
                                  const int32_t* __restrict__ prev_tokens, int n_src) {
+  griddep_entry();
   const int t = blockIdx.x;
   int32_t tok = ids[t];
   if (t < n_src) {
@@ -242,7 +246,7 @@ void launch_embedding(bf16* out, const bf16* table, const int32_t* ids, int T, i
   if (H % 8 != 0) throw std::runtime_error("embedding: hidden size must be a multiple of 8");
   if (n_src > 0 && (src_rows == nullptr || prev_tokens == nullptr))
     throw std::runtime_error("embedding: src_rows and prev_tokens are needed together");
-  embedding_kernel<<<T, 256, 0, st>>>(out, table, ids, H, vocab_start, vocab_rows, src_rows, prev_tokens,
+  launch_k(embedding_kernel, T, 256, 0, st, out, table, ids, H, vocab_start, vocab_rows, src_rows, prev_tokens,
                                       std::min(n_src, T));
   KAPSL_LAUNCH_CHECK();
   note_launch();

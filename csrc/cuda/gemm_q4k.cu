@@ -124,6 +124,7 @@ template <int TT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_q4k_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x, Q4Args a,
                     int* __restrict__ err) {
+  griddep_entry();
   using C = Cfg<TT>;
   constexpr uint32_t IDESC = idesc_bf16<WT, TT>();
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -401,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // Sum split-K partials [splits, M, N] -> bf16 Y (+ residual).
 __global__ void q4k_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, bf16* __restrict__ out,
                                   int64_t ldc, const bf16* __restrict__ res, int64_t ldr) {
+  griddep_entry();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (int64_t)M * N) return;
   float acc = 0.f;
@@ -414,6 +416,7 @@ __global__ void q4k_reduce_kernel(const float* __restrict__ partial, int splits,
 // One warp per super-block, lane = position inside each 32-weight sub-block.
 // Same rounding steps as the Python reference quantizer (loaders.gguf.quantize_q4_k).
 __global__ void q4k_quantize_kernel(const bf16* __restrict__ x, int64_t nblocks, uint8_t* __restrict__ out) {
+  griddep_entry();
   const int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (b >= nblocks) return;
@@ -464,6 +467,7 @@ __global__ void q4k_quantize_kernel(const bf16* __restrict__ x, int64_t nblocks,
 
 // Dequantize to bf16 (fp32 math), one thread per 32-weight sub-block row segment.
 __global__ void q4k_dequant_kernel(const uint8_t* __restrict__ raw, int64_t nblocks, bf16* __restrict__ out) {
+  griddep_entry();
   const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // one per (block, sub-block)
   if (g >= nblocks * 8) return;
   const int64_t b = g >> 3;
@@ -488,7 +492,7 @@ void launch_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const Q4Args& a, i
   constexpr size_t smem = Cfg<TT>::SMEM;
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
-  kern<<<grid, kThreads, smem, st>>>(tw, tx, a, err);
+  launch_k(kern, grid, kThreads, smem, st, tw, tx, a, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -540,7 +544,7 @@ void launch_gemm_q4k(const __nv_bfloat16* X, int64_t ldx, const uint8_t* Wq, int
 #undef KAPSL_Q4_DISPATCH
   if (splits > 1) {
     const int64_t total = (int64_t)M * N;
-    q4k_reduce_kernel<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(workspace, splits, M, N, Y, ldy, res, ldr);
+    launch_k(q4k_reduce_kernel, (unsigned)((total + 255) / 256), 256, 0, st, workspace, splits, M, N, Y, ldy, res, ldr);
     KAPSL_LAUNCH_CHECK();
     note_launch();
   }
@@ -550,7 +554,7 @@ void launch_q4k_quantize(const __nv_bfloat16* x, int64_t n, uint8_t* out, cudaSt
   if (n % q4k::QK != 0) throw std::runtime_error("q4k_quantize: size must be a multiple of 256");
   const int64_t nb = n / q4k::QK;
   if (nb == 0) return;
-  q4k::q4k_quantize_kernel<<<(unsigned)((nb * 32 + 255) / 256), 256, 0, st>>>(x, nb, out);
+  launch_k(q4k::q4k_quantize_kernel, (unsigned)((nb * 32 + 255) / 256), 256, 0, st, x, nb, out);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -559,7 +563,7 @@ void launch_q4k_dequant(const uint8_t* raw, int64_t n, __nv_bfloat16* out, cudaS
   if (n % q4k::QK != 0) throw std::runtime_error("q4k_dequant: size must be a multiple of 256");
   const int64_t nb = n / q4k::QK;
   if (nb == 0) return;
-  q4k::q4k_dequant_kernel<<<(unsigned)((nb * 8 + 255) / 256), 256, 0, st>>>(raw, nb, out);
+  launch_k(q4k::q4k_dequant_kernel, (unsigned)((nb * 8 + 255) / 256), 256, 0, st, raw, nb, out);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

@@ -122,6 +122,7 @@ template <int BN, int STAGES, int EPI, bool OUT_F32, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
                 int N, int K, int splits, EpiArgs ep, int* __restrict__ err) {
+  griddep_entry();
   constexpr int A_BYTES = BM * BK * 2;
   constexpr int B_BYTES = BN * BK * 2;
   constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
@@ -393,6 +394,7 @@ template <int STAGES, int EPI, bool OUT_F32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
                    int N, int K, EpiArgs ep, int* __restrict__ err) {
+  griddep_entry();
   constexpr int BN = 256;
   constexpr int HALF_BYTES = 128 * BK * 2;  // 16 KiB: A half or B half
   constexpr int STAGE_BYTES = 2 * HALF_BYTES;
@@ -594,7 +596,7 @@ void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
   constexpr size_t smem = (size_t)STAGES * 2 * 128 * BK * 2 + 1024;
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, M, N, K, ep, err);
+  launch_k(kern, grid, kThreads, smem, st, ta, tb, M, N, K, ep, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -602,6 +604,7 @@ void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
 // Sum split-K partials and apply the epilogue.
 template <int EPI, bool OUT_F32>
 __global__ void splitk_reduce_kernel(const float* __restrict__ partial, int splits, int M, int N, EpiArgs ep) {
+  griddep_entry();
   const int64_t idx = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   const int64_t total = (int64_t)M * N;
   if (idx >= total) return;
@@ -668,7 +671,7 @@ void launch_cfg(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int 
   constexpr size_t smem = smem_bytes<BN, STAGES>();
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
-  kern<<<grid, kThreads, smem, st>>>(ta, tb, M, N, K, splits, ep, err);
+  launch_k(kern, grid, kThreads, smem, st, ta, tb, M, N, K, splits, ep, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -810,11 +813,11 @@ void launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C
     const int64_t total = (int64_t)M * N / 4;
     const int blocks = (int)((total + 255) / 256);
     switch (epi) {
-      case 0: out_f32 ? splitk_reduce_kernel<0, true><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep)
-                      : splitk_reduce_kernel<0, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
-      case 1: splitk_reduce_kernel<1, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
-      case 2: splitk_reduce_kernel<2, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
-      case 3: splitk_reduce_kernel<3, false><<<blocks, 256, 0, st>>>(workspace, splits, M, N, ep); break;
+      case 0: out_f32 ? launch_k(splitk_reduce_kernel<0, true>, blocks, 256, 0, st, workspace, splits, M, N, ep)
+                      : launch_k(splitk_reduce_kernel<0, false>, blocks, 256, 0, st, workspace, splits, M, N, ep); break;
+      case 1: launch_k(splitk_reduce_kernel<1, false>, blocks, 256, 0, st, workspace, splits, M, N, ep); break;
+      case 2: launch_k(splitk_reduce_kernel<2, false>, blocks, 256, 0, st, workspace, splits, M, N, ep); break;
+      case 3: launch_k(splitk_reduce_kernel<3, false>, blocks, 256, 0, st, workspace, splits, M, N, ep); break;
     }
     KAPSL_LAUNCH_CHECK();
     note_launch();
@@ -875,9 +878,9 @@ void launch_grouped_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb,
     const int64_t total = (int64_t)rows * N / 4;
     const int blocks = (int)((total + 255) / 256);
     if (epi == 3)
-      splitk_reduce_kernel<3, false><<<blocks, 256, 0, st>>>(workspace, splits, rows, N, ep);
+      launch_k(splitk_reduce_kernel<3, false>, blocks, 256, 0, st, workspace, splits, rows, N, ep);
     else
-      splitk_reduce_kernel<0, false><<<blocks, 256, 0, st>>>(workspace, splits, rows, N, ep);
+      launch_k(splitk_reduce_kernel<0, false>, blocks, 256, 0, st, workspace, splits, rows, N, ep);
     KAPSL_LAUNCH_CHECK();
     note_launch();
   }

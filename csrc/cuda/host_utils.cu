@@ -1,7 +1,9 @@
 // Host-side helpers shared by all kernels: launch accounting and TMA
 // descriptor encoding.
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
+#include <string>
 
 #include "common.cuh"
 
@@ -11,6 +13,14 @@ static std::atomic<uint64_t> g_launches{0};
 
 uint64_t launch_count() { return g_launches.load(std::memory_order_relaxed); }
 void note_launch(uint64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("KAPSL_PDL");
+    return v == nullptr || std::string(v) != "0";
+  }();
+  return on;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,

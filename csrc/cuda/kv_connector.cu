@@ -19,6 +19,7 @@ __global__ void __launch_bounds__(256) kv_push_kernel(const uint4* __restrict__ 
                                                       const int32_t* __restrict__ dst_ids, int nblocks, int planes,
                                                       int64_t src_plane_vecs, int64_t dst_plane_vecs,
                                                       int block_vecs) {
+  griddep_entry();
   const int64_t total = (int64_t)planes * nblocks * block_vecs;
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i0 < total; i0 += 4 * stride) {
@@ -53,7 +54,7 @@ void launch_kv_push(const void* src_pool, void* dst_pool, const int32_t* src_ids
   const int block_vecs = (int)(block_bytes / 16);
   const int64_t total = (int64_t)planes * nblocks * block_vecs;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((total + 1023) / 1024, 4LL * num_sms));
-  kv_push_kernel<<<grid, 256, 0, st>>>(static_cast<const uint4*>(src_pool), static_cast<uint4*>(dst_pool), src_ids,
+  launch_k(kv_push_kernel, grid, 256, 0, st, static_cast<const uint4*>(src_pool), static_cast<uint4*>(dst_pool), src_ids,
                                        dst_ids, nblocks, planes, src_blocks_per_plane * block_vecs,
                                        dst_blocks_per_plane * block_vecs, block_vecs);
   KAPSL_LAUNCH_CHECK();

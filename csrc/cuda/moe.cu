@@ -33,6 +33,7 @@ __global__ void __launch_bounds__(kRouteWarps * 32) moe_route_kernel(const bf16*
                                                                      const bf16* __restrict__ wr, int T, int d, int E,
                                                                      int K, int renorm, int32_t* __restrict__ ids,
                                                                      float* __restrict__ wts) {
+  griddep_entry();
   __shared__ float logit_sh[64];
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -136,6 +137,7 @@ __global__ void __launch_bounds__(kPermThreads) moe_permute_kernel(const int32_t
                                                                    int32_t* __restrict__ seg, int32_t* __restrict__ pos,
                                                                    int32_t* __restrict__ mtiles,
                                                                    int32_t* __restrict__ src, int* __restrict__ err) {
+  griddep_entry();
   __shared__ int warp_cnt[kPermThreads / 32][kMaxExperts];
   __shared__ int run_cnt[kMaxExperts];
   __shared__ int seg_sh[kMaxExperts + 1];
@@ -206,6 +208,7 @@ __global__ void __launch_bounds__(256) moe_gather_kernel(const bf16* __restrict_
                                                          const int32_t* __restrict__ src,
                                                          const int32_t* __restrict__ mtiles, bf16* __restrict__ xs,
                                                          int64_t xs_stride, int d) {
+  griddep_entry();
   const int rows = mtiles[0] * 128;
   const int chunks = d / 8;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)rows * chunks;
@@ -237,6 +240,7 @@ struct MoECombineArgs {
 
 template <int WORLD>
 __global__ void __launch_bounds__(256) moe_combine_kernel(MoECombineArgs a) {
+  griddep_entry();
   __shared__ int64_t epoch_sh;
   __shared__ int ok_sh;
   if (WORLD > 1) {
@@ -327,7 +331,7 @@ void launch_moe_route(const bf16* x, int64_t x_stride, const bf16* wr, int T, in
   if (T == 0) return;
   if (E > kMaxExperts || K > 8 || K > E) throw std::runtime_error("moe_route: need E <= 64 and K <= min(8, E)");
   if (d % 8 != 0 || x_stride % 8 != 0) throw std::runtime_error("moe_route: d and stride must be multiples of 8");
-  moe_route_kernel<<<T, kRouteWarps * 32, 0, st>>>(x, x_stride, wr, T, d, E, K, renorm ? 1 : 0, ids, wts);
+  launch_k(moe_route_kernel, T, kRouteWarps * 32, 0, st, x, x_stride, wr, T, d, E, K, renorm ? 1 : 0, ids, wts);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -336,7 +340,7 @@ void launch_moe_permute(const int32_t* ids, int T, int K, int E, int e_lo, int e
                         int32_t* pos, int32_t* mtiles, int32_t* src, int* err, cudaStream_t st) {
   if (E > kMaxExperts) throw std::runtime_error("moe_permute: at most 64 experts");
   if (e_lo < 0 || el < 1 || e_lo + el > E) throw std::runtime_error("moe_permute: bad local expert range");
-  moe_permute_kernel<<<1, kPermThreads, 0, st>>>(ids, T * K, K, E, e_lo, el, max_rows, seg, pos, mtiles, src, err);
+  launch_k(moe_permute_kernel, 1, kPermThreads, 0, st, ids, T * K, K, E, e_lo, el, max_rows, seg, pos, mtiles, src, err);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -347,7 +351,7 @@ void launch_moe_gather(const bf16* x, int64_t x_stride, const int32_t* src, cons
     throw std::runtime_error("moe_gather: d and strides must be multiples of 8");
   const int64_t work = (int64_t)max_rows * (d / 8);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 4LL * num_sms));
-  moe_gather_kernel<<<grid, 256, 0, st>>>(x, x_stride, src, mtiles, xs, xs_stride, d);
+  launch_k(moe_gather_kernel, grid, 256, 0, st, x, x_stride, src, mtiles, xs, xs_stride, d);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -384,10 +388,10 @@ void launch_moe_combine(const bf16* const* y, bf16* const* hidden, int64_t* cons
   const int64_t work = (int64_t)rows * (cols / 8);
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>((work + 255) / 256, 4LL * num_sms));
   switch (world) {
-    case 1: moe_combine_kernel<1><<<grid, 256, 0, st>>>(a); break;
-    case 2: moe_combine_kernel<2><<<grid, 256, 0, st>>>(a); break;
-    case 4: moe_combine_kernel<4><<<grid, 256, 0, st>>>(a); break;
-    case 8: moe_combine_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    case 1: launch_k(moe_combine_kernel<1>, grid, 256, 0, st, a); break;
+    case 2: launch_k(moe_combine_kernel<2>, grid, 256, 0, st, a); break;
+    case 4: launch_k(moe_combine_kernel<4>, grid, 256, 0, st, a); break;
+    case 8: launch_k(moe_combine_kernel<8>, grid, 256, 0, st, a); break;
     default: throw std::runtime_error("moe_combine: world size must be 1, 2, 4 or 8");
   }
   KAPSL_LAUNCH_CHECK();

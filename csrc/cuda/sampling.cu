@@ -405,6 +405,7 @@ __device__ int slice_topk(const SampleArgs& a, const float* lg, int k, SelectSme
 
 template <bool FINISH>
 __global__ void __launch_bounds__(kSampThreads) sample_select_kernel(SampleArgs a) {
+  griddep_entry();
   __shared__ SelectSmem sm;
   __shared__ int64_t epoch_sh;
   const int row = blockIdx.x;
@@ -464,6 +465,7 @@ __global__ void __launch_bounds__(kSampThreads) sample_select_kernel(SampleArgs 
 // Vocabulary-parallel merge: every rank's sorted slice candidates of a row ->
 // the global top-k -> top-p -> draw.  Candidate buffers and flags as above.
 __global__ void __launch_bounds__(kSampThreads) sample_merge_kernel(SampleArgs a) {
+  griddep_entry();
   extern __shared__ __align__(16) unsigned char dyn[];
   float* val = reinterpret_cast<float*>(dyn);
   int* idx = reinterpret_cast<int*>(val + a.world * kMaxTopK);
@@ -546,6 +548,7 @@ __device__ __forceinline__ void cas_u64(unsigned long long* k, int i, int j, boo
 
 __global__ void __launch_bounds__(kSampThreads) sample_full_kernel(SampleArgs a, unsigned long long* scratch,
                                                                    int npow) {
+  griddep_entry();
   __shared__ unsigned long long tile[kFullTile];
   __shared__ float s_red[32];
   __shared__ int s_i[4];
@@ -711,7 +714,7 @@ void launch_sample_merge(const SampleLaunch& l, cudaStream_t st) {
   const size_t smem = (size_t)l.world * kMaxTopK * 8;
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, sample_merge_kernel, (size_t)8 * kMaxTopK * 8);  // the largest group's need
-  sample_merge_kernel<<<l.B, kSampThreads, smem, st>>>(a);
+  launch_k(sample_merge_kernel, l.B, kSampThreads, smem, st, a);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -725,13 +728,13 @@ void launch_sample(const SampleLaunch& l, cudaStream_t st) {
   SampleArgs a{};
   fill_args(a, l);
   if (l.world <= 1) {
-    sample_select_kernel<true><<<l.B, kSampThreads, 0, st>>>(a);
+    launch_k(sample_select_kernel<true>, l.B, kSampThreads, 0, st, a);
     KAPSL_LAUNCH_CHECK();
     note_launch();
   } else {
     if (l.world > 8 || l.B > l.b_cap || l.ctr == nullptr || l.cand[l.rank] == nullptr)
       throw std::runtime_error("sample: vocab-parallel buffers missing or too small");
-    sample_select_kernel<false><<<l.B, kSampThreads, 0, st>>>(a);
+    launch_k(sample_select_kernel<false>, l.B, kSampThreads, 0, st, a);
     KAPSL_LAUNCH_CHECK();
     note_launch();
     if (l.flags[l.rank] != nullptr) launch_sample_merge(l, st);
@@ -740,7 +743,7 @@ void launch_sample(const SampleLaunch& l, cudaStream_t st) {
     if (l.world > 1) throw std::runtime_error("sample: whole-vocabulary rows need the full logits");
     int npow = 1;
     while (npow < l.Vl) npow <<= 1;
-    sample_full_kernel<<<l.full_ctas, kSampThreads, 0, st>>>(a, reinterpret_cast<unsigned long long*>(l.full_scratch),
+    launch_k(sample_full_kernel, l.full_ctas, kSampThreads, 0, st, a, reinterpret_cast<unsigned long long*>(l.full_scratch),
                                                              npow);
     KAPSL_LAUNCH_CHECK();
     note_launch();
@@ -753,6 +756,7 @@ void launch_sample(const SampleLaunch& l, cudaStream_t st) {
 __global__ void count_tokens_kernel(int32_t* __restrict__ counts, int V, const int32_t* __restrict__ rows,
                                     const int32_t* __restrict__ ids, int n, int32_t* __restrict__ occ,
                                     int32_t* __restrict__ occ_n, int occ_cap) {
+  griddep_entry();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int r = rows[i];
@@ -769,7 +773,7 @@ __global__ void count_tokens_kernel(int32_t* __restrict__ counts, int V, const i
 void launch_count_tokens(int32_t* counts, int V, const int32_t* rows, const int32_t* ids, int n, int32_t* occ,
                          int32_t* occ_n, int occ_cap, cudaStream_t st) {
   if (n == 0) return;
-  count_tokens_kernel<<<(n + 255) / 256, 256, 0, st>>>(counts, V, rows, ids, n, occ, occ_n, occ_cap);
+  launch_k(count_tokens_kernel, (n + 255) / 256, 256, 0, st, counts, V, rows, ids, n, occ, occ_n, occ_cap);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

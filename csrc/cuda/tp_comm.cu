@@ -42,6 +42,7 @@ struct TPArgs {
 };
 
 __global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
+  griddep_entry();
   __shared__ int64_t epoch_sh;
   __shared__ int ok_sh;
   if (threadIdx.x == 0) {
@@ -119,6 +120,7 @@ __global__ void __launch_bounds__(256) tp_reduce_ag_kernel(TPArgs a) {
 // reduced rows to every peer; barrier 2 as above.
 template <int WORLD>
 __global__ void __launch_bounds__(256) tp_pull_reduce_ag_kernel(TPArgs a) {
+  griddep_entry();
   __shared__ int64_t epoch_sh;
   __shared__ int ok_sh;
   if (threadIdx.x == 0) {
@@ -243,6 +245,7 @@ static constexpr int kNormMaxChunks = 4;  // 16-byte chunks per thread: cols <= 
 
 template <int WORLD>
 __global__ void __launch_bounds__(kNormThreads) tp_reduce_norm_ag_kernel(TPNormArgs a) {
+  griddep_entry();
   __shared__ int64_t epoch_sh;
   __shared__ int ok_sh;
   __shared__ float red[kNormThreads / 32];
@@ -397,9 +400,9 @@ void launch_tp_reduce_norm_ag(const bf16* const* partial, bf16* const* xout, int
   int grid = std::min(rows_per_rank, num_sms * 4);
   if (grid < 1) grid = 1;
   switch (world) {
-    case 2: tp_reduce_norm_ag_kernel<2><<<grid, kNormThreads, 0, st>>>(a); break;
-    case 4: tp_reduce_norm_ag_kernel<4><<<grid, kNormThreads, 0, st>>>(a); break;
-    case 8: tp_reduce_norm_ag_kernel<8><<<grid, kNormThreads, 0, st>>>(a); break;
+    case 2: launch_k(tp_reduce_norm_ag_kernel<2>, grid, kNormThreads, 0, st, a); break;
+    case 4: launch_k(tp_reduce_norm_ag_kernel<4>, grid, kNormThreads, 0, st, a); break;
+    case 8: launch_k(tp_reduce_norm_ag_kernel<8>, grid, kNormThreads, 0, st, a); break;
     default: throw std::runtime_error("tp: fused norm reduction needs world size 2, 4 or 8");
   }
   KAPSL_LAUNCH_CHECK();
@@ -431,10 +434,10 @@ void launch_tp_pull_reduce_ag(bf16* const* partial, bf16* const* hidden, int64_t
   int grid = (int)std::min<int64_t>((work + 511) / 512, (int64_t)num_sms * 4);
   if (grid < 1) grid = 1;
   switch (world) {
-    case 1: tp_pull_reduce_ag_kernel<1><<<grid, 256, 0, st>>>(a); break;
-    case 2: tp_pull_reduce_ag_kernel<2><<<grid, 256, 0, st>>>(a); break;
-    case 4: tp_pull_reduce_ag_kernel<4><<<grid, 256, 0, st>>>(a); break;
-    case 8: tp_pull_reduce_ag_kernel<8><<<grid, 256, 0, st>>>(a); break;
+    case 1: launch_k(tp_pull_reduce_ag_kernel<1>, grid, 256, 0, st, a); break;
+    case 2: launch_k(tp_pull_reduce_ag_kernel<2>, grid, 256, 0, st, a); break;
+    case 4: launch_k(tp_pull_reduce_ag_kernel<4>, grid, 256, 0, st, a); break;
+    case 8: launch_k(tp_pull_reduce_ag_kernel<8>, grid, 256, 0, st, a); break;
     default: throw std::runtime_error("tp: world size must be 1, 2, 4 or 8");
   }
   KAPSL_LAUNCH_CHECK();
@@ -464,7 +467,7 @@ void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const*
   const int64_t work = (int64_t)rows_per_rank * (cols / 8);
   int grid = (int)std::min<int64_t>((work + 255) / 256, (int64_t)num_sms);  // all CTAs co-resident
   if (grid < 1) grid = 1;
-  tp_reduce_ag_kernel<<<grid, 256, 0, st>>>(a);
+  launch_k(tp_reduce_ag_kernel, grid, 256, 0, st, a);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }
@@ -475,6 +478,7 @@ void launch_tp_reduce_ag(bf16* const* recv, bf16* const* hidden, int64_t* const*
 template <int UNROLL>
 __global__ void __launch_bounds__(256) p2p_copy_kernel(uint4* __restrict__ dst, const uint4* __restrict__ src,
                                                       int64_t n) {
+  griddep_entry();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride * UNROLL) {
     uint4 v[UNROLL];
@@ -490,7 +494,7 @@ __global__ void __launch_bounds__(256) p2p_copy_kernel(uint4* __restrict__ dst, 
 void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st) {
   const int64_t n = bytes / 16;
   const int grid = gemm_num_sms() * ctas_per_sm;
-  p2p_copy_kernel<4><<<grid, 256, 0, st>>>(reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n);
+  launch_k(p2p_copy_kernel<4>, grid, 256, 0, st, reinterpret_cast<uint4*>(dst), reinterpret_cast<const uint4*>(src), n);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

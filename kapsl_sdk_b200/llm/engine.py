@@ -63,9 +63,12 @@ class EngineConfig:
 
 class LLMEngine:
     def __init__(self, cfg: ModelConfig, weights: Optional[ModelWeights] = None, device="cuda",
-                 engine_cfg: Optional[EngineConfig] = None, tp_comm=None, moe=None, seed: int = 0, pp_stage=None):
+                 engine_cfg: Optional[EngineConfig] = None, tp_comm=None, moe=None, seed: int = 0, pp_stage=None,
+                 model_cls=None):
         """``pp_stage``: a :class:`~kapsl_sdk_b200.parallel.pp.PipelineStage`; the engine then
-        holds that stage's layers (and their KV pages) and steps in micro-batches."""
+        holds that stage's layers (and their KV pages) and steps in micro-batches.
+        ``model_cls``: the GPU model class (default :class:`CausalLM`; the library
+        baseline passes :class:`~kapsl_sdk_b200.models.baseline.BaselineCausalLM`)."""
         self.cfg = cfg
         self.ecfg = engine_cfg or EngineConfig()
         self.device = torch.device(device)
@@ -100,7 +103,7 @@ class LLMEngine:
             from ..models.moe import MoE
 
             moe = MoE(cfg, self.device, tp_comm)
-        self.model = CausalLM(cfg, weights, self.device, tp_comm=tp_comm, moe=moe, stage=pp_stage)
+        self.model = (model_cls or CausalLM)(cfg, weights, self.device, tp_comm=tp_comm, moe=moe, stage=pp_stage)
         self.model.configure_tp(e.max_num_batched_tokens + e.max_num_seqs, sample_rows=e.max_num_seqs + 1)
         if pp_stage is not None:
             e.use_cuda_graph = False  # stages exchange hidden states inside the step

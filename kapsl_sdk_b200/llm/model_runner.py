@@ -192,6 +192,11 @@ class ModelRunner:
     def _sample(self, logits: torch.Tensor, R: int, full: bool = False) -> None:
         L = self.L
         args = (self._f32(L.temp, R), self._v32(L.topk, R), self._f32(L.topp, R))
+        if getattr(self.model, "library_sampler", False):  # the library baseline samples with torch ops
+            slots = self._v32(L.sslot, R)
+            self.model.sample(logits, *args, self.out_tokens, self._f32(L.pen, R), self.counts, slots)
+            self._count(slots, self.out_tokens[:R])
+            return
         tp = self.model.tp
         if self.model.tp_size > 1 and not full:  # logits hold this rank's vocabulary slice
             tp.vocab_sample(logits, self.model.vocab_start, self.vocab, *args, self.rng_table, self.out_tokens[:R],
@@ -203,7 +208,14 @@ class ModelRunner:
             ops.sample(logits, *args, self.rng_table, self.out_tokens[:R], rep_penalty=self._f32(L.pen, R),
                        counts=self.counts, slots=self._v32(L.sslot, R), occ=self.occ, occ_n=self.occ_n,
                        full_scratch=self.full_scratch if full else None, full_ctas=self.FULL_CTAS if full else 0)
-        ops.count_tokens(self.counts, self._v32(L.sslot, R), self.out_tokens[:R], self.occ, self.occ_n)
+        self._count(self._v32(L.sslot, R), self.out_tokens[:R])
+
+    def _count(self, rows: torch.Tensor, ids: torch.Tensor) -> None:
+        """counts[rows[i], ids[i]] += 1 (and first occurrences appended to the slot lists)."""
+        if getattr(self.model, "library_sampler", False):
+            self.counts.index_put_((rows.long(), ids.long()), torch.ones_like(ids), accumulate=True)
+        else:
+            ops.count_tokens(self.counts, rows, ids, self.occ, self.occ_n)
 
     # ------------------------------------------------------- host inputs
     def _fill(self, batch: ScheduledBatch, pad_to: int = 0):
@@ -324,8 +336,7 @@ class ModelRunner:
         self.occ_n.index_fill_(0, slots, 0)
         rows = np.concatenate([np.full(len(s.all_ids), s.slot, dtype=np.int32) for s in seqs])
         ids = np.concatenate([np.asarray(s.all_ids, dtype=np.int32) for s in seqs])
-        ops.count_tokens(self.counts, torch.from_numpy(rows).to(self.device), torch.from_numpy(ids).to(self.device),
-                         self.occ, self.occ_n)
+        self._count(torch.from_numpy(rows).to(self.device), torch.from_numpy(ids).to(self.device))
 
     def _apply_admissions(self) -> None:
         n = getattr(self, "_pending_admit", 0)
@@ -341,7 +352,7 @@ class ModelRunner:
         rows_t = torch.from_numpy(rows).pin_memory().to(self.device, non_blocking=True)
         ids_t = torch.from_numpy(ids).pin_memory().to(self.device, non_blocking=True)
         self.stats["h2d_bytes"] += rows.nbytes + ids.nbytes
-        ops.count_tokens(self.counts, rows_t, ids_t, self.occ, self.occ_n)
+        self._count(rows_t, ids_t)
         self._pending_admit = 0
         self._admit_prompts = []
 
