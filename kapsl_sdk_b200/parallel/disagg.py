@@ -170,6 +170,7 @@ class _Job:
     params: SamplingParams
     seq: Optional[object] = None
     t_submit: float = field(default_factory=time.perf_counter)
+    pushed: int = 0  # prefill side: leading blocks already pushed to the decode pool
 
 
 class _Worker:
@@ -198,12 +199,30 @@ class PrefillWorker(_Worker):
         engine.kv_export = self._export
 
     def _export(self, seqs) -> None:
+        """A prompt finished: push the blocks not streamed yet (the last, partial one
+        at least); its completion post waits for that copy (same stream, so every
+        earlier chunk's copy of the prompt has completed too)."""
         bs = self.engine.pool.layout.block_size
         for s in seqs:
             job = self.jobs.pop(s.request_id)
             nblk = (len(s.prompt_ids) + bs - 1) // bs
-            ev = self.conn.push(s.block_ids[:nblk], job.blocks[:nblk], job.k)
+            ev = self.conn.push(s.block_ids[job.pushed:nblk], job.blocks[job.pushed:nblk], job.k)
+            job.pushed = nblk
             self.pending.append((ev, job, s.output_ids[-1], _advance_rng(s.rng_state, s.params)))
+
+    def _stream_chunks(self) -> None:
+        """After a step: push every prompt's blocks that this step completed (full
+        16-token blocks of every layer), so long prompts move to the decode pool
+        chunk by chunk while their later chunks still prefill."""
+        bs = self.engine.pool.layout.block_size
+        for job in self.jobs.values():
+            s = job.seq
+            if s is None or s.status.finished:
+                continue
+            full = min(s.num_computed, len(s.prompt_ids)) // bs
+            if full > job.pushed:
+                self.conn.push(s.block_ids[job.pushed:full], job.blocks[job.pushed:full], job.k)
+                job.pushed = full
 
     def progress(self) -> str:
         return (f"jobs seen {self.next_job}/{self.total}, prefilling {len(self.jobs)}, pushes in flight "
@@ -225,18 +244,26 @@ class PrefillWorker(_Worker):
             self.next_job += 1
             self.jobs[j.request_id] = j
             p = SamplingParams(**{**j.params.__dict__, "max_new_tokens": 1})
-            self.engine.add_request(j.request_id, j.prompt, p)
+            j.seq = self.engine.add_request(j.request_id, j.prompt, p)
         if self.engine.has_unfinished():
             self.engine.step()
+            if self.conn.mode != "host":
+                self._stream_chunks()
+        more = (self.total < 0 or self.next_job < self.total or bool(self.jobs) or self.engine.has_unfinished())
+        # The decision to go on must be the same on every rank of the group (each
+        # poll holds a broadcast), so it never depends on this rank's copies in
+        # flight: when the group is done, every rank waits for its own copies and
+        # posts their completions before leaving the loop.
         still = []
         for ev, job, tok, rng in self.pending:
+            if ev is not None and not ev.query() and not more:
+                ev.synchronize()
             if ev is None or ev.query():
                 self.store.set(f"{self.ns}/done/{job.k}/{self.rank}", pickle.dumps((tok, rng)))
             else:
                 still.append((ev, job, tok, rng))
         self.pending = still
-        return (self.total < 0 or self.next_job < self.total or bool(self.jobs) or bool(self.pending)
-                or self.engine.has_unfinished())
+        return more
 
 
 class DecodeWorker(_Worker):
