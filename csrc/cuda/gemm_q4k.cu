@@ -27,6 +27,7 @@
 // The raw weights cross HBM once at 4.5 bits per weight; for small M the
 // kernel streams them at memory speed, for large M the MMAs (N = TT = 256)
 // amortise the dequant over 256 tokens.
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -74,7 +75,13 @@ struct Q4Args {
   // tiled + (nt * nsb + sb) * RAW_BYTES, one bulk copy per super-block.
   const uint8_t* tiled;
   int M, N, K, splits;
+  int spin;           // 1: waits spin on try_wait; 0: waits suspend in try_wait (KAPSL_Q4K_SPIN)
 };
+
+// Bounded mbarrier wait: spinning, or suspended in try_wait between polls.
+__device__ __forceinline__ bool q4_wait(int spin, uint64_t* bar, uint32_t parity) {
+  return spin ? mbar_wait_bounded(bar, parity) : mbar_wait_sleep(bar, parity);
+}
 
 __device__ __forceinline__ float half_bits_to_float(uint32_t h) {
   return __half2float(__ushort_as_half((unsigned short)h));
@@ -200,7 +207,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode_unit(u, tt, nt, sp);
         const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
         for (int sb = sb0; sb < sb1; ++sb) {
-          if (!mbar_wait_sleep(&raw_empty[rs], rph ^ 1)) { fail(60); break; }
+          if (!q4_wait(a.spin, &raw_empty[rs], rph ^ 1)) { fail(60); break; }
           mbar_arrive_expect_tx(&raw_full[rs], RAW_BYTES);
           const int sbr = rot_sb(u, sb0, sb1, sb);
           if (a.tiled)
@@ -224,7 +231,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         decode_unit(u, tt, nt, sp);
         const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
         for (int kb = sb0 * 4; kb < sb1 * 4; ++kb) {
-          if (!mbar_wait_sleep(&x_empty[xs], xph ^ 1)) { fail(61); break; }
+          if (!q4_wait(a.spin, &x_empty[xs], xph ^ 1)) { fail(61); break; }
           mbar_arrive_expect_tx(&x_full[xs], C::X_BYTES);
           tma_load_2d(xring + (size_t)xs * C::X_BYTES, &tmap_x, &x_full[xs],
                       (rot_sb(u, sb0, sb1, kb >> 2) * 4 + (kb & 3)) * BK, tt * TT);
@@ -245,15 +252,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
         const int acc = C::NACC == 2 ? (it & 1) : 0;
         const uint32_t acc_ph = C::NACC == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
-        if (!mbar_wait_sleep(&acc_empty[acc], acc_ph ^ 1)) { fail(62); break; }
+        if (!q4_wait(a.spin, &acc_empty[acc], acc_ph ^ 1)) { fail(62); break; }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TT);
         bool first = true, ok = true;
         for (int sb = sb0; sb < sb1 && ok; ++sb) {
-          if (!mbar_wait_sleep(&a_full[as], aph)) { fail(63); ok = false; break; }
+          if (!q4_wait(a.spin, &a_full[as], aph)) { fail(63); ok = false; break; }
           const uint32_t a_tmem = tmem_base + (uint32_t)(C::A_COL0 + as * 128);
           for (int i = 0; i < QK / BK; ++i) {
-            if (!mbar_wait_sleep(&x_full[xs], xph)) { fail(63); ok = false; break; }
+            if (!q4_wait(a.spin, &x_full[xs], xph)) { fail(63); ok = false; break; }
             tc_fence_after();
             const uint32_t xa = smem_u32(xring + (size_t)xs * C::X_BYTES);
 #pragma unroll
@@ -291,7 +298,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int sb0 = sp * sb_per_split, sb1 = min(nsb, sb0 + sb_per_split);
         bool stop = false;
         for (int sb = sb0; sb < sb1; ++sb) {
-          const bool got = mbar_wait_sleep(&raw_full[rs], rph);
+          const bool got = q4_wait(a.spin, &raw_full[rs], rph);
           if (!__all_sync(0xffffffffu, got)) {
             if (lane == 0) fail(64);
             stop = true;
@@ -311,7 +318,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive(&raw_empty[rs]);  // the stage's bytes are in registers
           if (++rs == C::NRAW) { rs = 0; rph ^= 1; }
-          const bool free_slot = mbar_wait_sleep(&a_empty[as], aph ^ 1);
+          const bool free_slot = q4_wait(a.spin, &a_empty[as], aph ^ 1);
           if (!__all_sync(0xffffffffu, free_slot)) {
             if (lane == 0) fail(65);
             stop = true;
@@ -360,7 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       decode_unit(u, tt, nt, sp);
       const int acc = C::NACC == 2 ? (it & 1) : 0;
       const uint32_t acc_ph = C::NACC == 2 ? (uint32_t)((it >> 1) & 1) : (uint32_t)(it & 1);
-      const bool got = mbar_wait_sleep(&acc_full[acc], acc_ph);
+      const bool got = q4_wait(a.spin, &acc_full[acc], acc_ph);
       if (!__all_sync(0xffffffffu, got)) {
         if (lane == 0) fail(66);
         break;
@@ -525,7 +532,11 @@ void launch_gemm_q4k(const __nv_bfloat16* X, int64_t ldx, const uint8_t* Wq, int
     throw std::runtime_error("gemm_q4k: tile-contiguous weights need N % 128 == 0 and a 16-byte aligned base");
   CUtensorMap tw = make_tmap_2d_u8(Wq, N, (uint64_t)w_pitch, (uint64_t)w_pitch, WT, QB);
   CUtensorMap tx = make_tmap_2d_bf16(X, M, K, ldx, TT, BK);
-  Q4Args a{Y, ldy, res, ldr, workspace, tiled ? Wq : nullptr, M, N, K, splits};
+  static const int spin = [] {
+    const char* v = std::getenv("KAPSL_Q4K_SPIN");
+    return (v != nullptr && v[0] == '1') ? 1 : 0;
+  }();
+  Q4Args a{Y, ldy, res, ldr, workspace, tiled ? Wq : nullptr, M, N, K, splits, spin};
   const int grid = std::min(tiles * splits, sms);
   const int epi = splits > 1 ? 4 : (res ? 2 : 0);
 #define KAPSL_Q4_DISPATCH(TTV)                                            \

@@ -203,6 +203,14 @@ def tiny_llama() -> ModelConfig:
                        max_position=4096)
 
 
+def tiny_qwen2() -> ModelConfig:
+    """2 layers, d 512, 8q/2kv heads of 128, FFN 1024, vocab 4096, QKV bias: the smallest
+    Qwen2-style decoder the GPU kernels take (head dim 128), for smoke runs and tests."""
+    return ModelConfig(name="tiny-qwen2", arch="qwen2", vocab_size=4096, hidden_size=512, intermediate_size=1024,
+                       num_layers=2, num_heads=8, num_kv_heads=2, head_dim=128, rope_theta=1e6, rms_eps=1e-6,
+                       qkv_bias=True, max_position=4096)
+
+
 def qwen2_5_7b() -> ModelConfig:
     """Qwen2.5-7B: 28 layers, d 3584, 28q/4kv heads of 128, FFN 18944, vocab 152064, theta 1e6, QKV bias."""
     return ModelConfig(name="qwen2.5-7b", arch="qwen2", vocab_size=152064, hidden_size=3584, intermediate_size=18944,
@@ -241,6 +249,7 @@ def llama3_70b_q4k() -> ModelConfig:
 
 PRESETS = {
     "tiny-llama": tiny_llama,
+    "tiny-qwen2": tiny_qwen2,
     "qwen2.5-7b": qwen2_5_7b,
     "llama-3-70b": llama3_70b,
     "llama-3-70b-q4k": llama3_70b_q4k,

@@ -192,13 +192,23 @@ class GroupLeader:
         self.engine.shutdown()
 
 
-def follow(engine, channel: StepChannel, idle_timeout_s: float = 3600.0) -> int:
+def follow(engine, channel: StepChannel, idle_timeout_s: float = 3600.0, should_exit=None) -> int:
     """Follower loop: apply each published event batch to ``engine`` and step it,
     until the leader publishes a stop (the engine is left running for the
-    caller).  Returns the number of steps taken."""
+    caller).  ``should_exit()`` is polled while no message arrives (e.g. the
+    leader was lost after a termination signal); a true value ends the loop.
+    Returns the number of steps taken."""
     steps = 0
+    idle_since = time.monotonic()
     while True:
-        events = pickle.loads(channel.receive(timeout_s=idle_timeout_s))
+        try:
+            raw = channel.receive(timeout_s=1.0)
+        except TimeoutError:
+            if (should_exit is not None and should_exit()) or time.monotonic() - idle_since > idle_timeout_s:
+                return steps
+            continue
+        idle_since = time.monotonic()
+        events = pickle.loads(raw)
         stop = False
         for ev in events:
             kind = ev[0]

@@ -26,6 +26,7 @@ import argparse
 import os
 import signal
 import sys
+import time
 from typing import Optional
 
 from ..server import DEFAULT_SHM_NAME, DEFAULT_SOCKET, DEFAULT_TCP_PORT
@@ -141,9 +142,14 @@ def main(argv: Optional[list] = None) -> int:
         dist.broadcast_object_list(name, src=0)
         if rank != 0:
             chan = StepChannel(name[0], world, rank)
+            # a termination signal reaches every rank at once: keep following until the
+            # leader publishes its stop, and give up only if it has not after 30 s
+            term = []
+            signal.signal(signal.SIGTERM, lambda *_: term.append(time.monotonic()))
+            signal.signal(signal.SIGINT, lambda *_: term.append(time.monotonic()))
             dist.barrier()
             try:
-                steps = follow(built[0][0], chan)
+                steps = follow(built[0][0], chan, should_exit=lambda: bool(term) and time.monotonic() - term[0] > 30)
                 print(f"kapsl-runtime rank {rank}: followed {steps} steps, outputs {output_digest(built[0][0])}",
                       flush=True)
                 built[0][0].shutdown()

@@ -17,6 +17,7 @@ from __future__ import annotations
 import argparse
 import json
 import math
+import os
 import random
 
 import torch
@@ -96,16 +97,20 @@ def bench_prefill(S, chunk, hq, hkv, timed):
     q = torch.randn(S * chunk, hq * 128, device=dev, dtype=torch.bfloat16)
     out = torch.empty_like(q)
     info = torch.tensor([(s * chunk, chunk, chunk, s) for s in range(S)], dtype=torch.int32, device=dev)
-    work = torch.tensor(ops.prefill_work([chunk] * S), dtype=torch.int32, device=dev)
-    fn = lambda: ops.prefill_attention(q, kc, vc, work, info, bt, hq, hkv, out)
+    tc = os.environ.get("KAPSL_PREFILL_TC") == "1"  # the tcgen05 kernel instead of the mma.sync one
+    tile = ops.prefill_tc_tile(hq, hkv) if tc else 64
+    work = torch.tensor(ops.prefill_work([chunk] * S, tile=tile), dtype=torch.int32, device=dev)
+    kern = ops.prefill_attention_tc if tc else ops.prefill_attention
+    fn = lambda: kern(q, kc, vc, work, info, bt, hq, hkv, out)
+    name = "prefill_attention_tc" if tc else "prefill_attention"
     if not timed:
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
-        return {"kernel": "prefill_attention", "S": S, "chunk": chunk}
+        return {"kernel": name, "S": S, "chunk": chunk}
     ms = _time(fn)
     flops = S * hq * 128 * 4 * chunk * chunk / 2
-    return {"kernel": "prefill_attention", "S": S, "chunk": chunk, "ms": ms, "tflops": flops / ms / 1e9}
+    return {"kernel": name, "S": S, "chunk": chunk, "ms": ms, "tflops": flops / ms / 1e9}
 
 
 def bench_sample(B, V, timed):
@@ -118,7 +123,15 @@ def bench_sample(B, V, timed):
     topp = torch.full((B,), 0.9, device=dev)
     rng = torch.arange(B, dtype=torch.int64, device=dev)
     out = torch.empty(B, dtype=torch.int32, device=dev)
-    fn = lambda: ops.sample(logits, temp, topk, topp, rng, out)
+    # serving-like repetition penalty: 1500 earlier ids per row (prompt + output), kept as
+    # per-slot counts and occurrence lists
+    pen = torch.full((B,), 1.15, device=dev)
+    counts = torch.zeros(B, V, dtype=torch.int32, device=dev)
+    occ = torch.zeros(B, 4096, dtype=torch.int32, device=dev)
+    occ_n = torch.zeros(B, dtype=torch.int32, device=dev)
+    rows = torch.arange(B, dtype=torch.int32, device=dev).repeat_interleave(1500)
+    ops.count_tokens(counts, rows, torch.randint(0, V, (B * 1500,), dtype=torch.int32, device=dev), occ, occ_n)
+    fn = lambda: ops.sample(logits, temp, topk, topp, rng, out, rep_penalty=pen, counts=counts, occ=occ, occ_n=occ_n)
     if not timed:
         for _ in range(3):
             fn()
