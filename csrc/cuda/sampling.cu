@@ -231,6 +231,60 @@ __device__ void slice_argmax(const SampleArgs& a, const float* lg, SelectSmem& s
   __syncthreads();
 }
 
+static constexpr int kSample = 2048;  // strided sample that places the one-pass threshold
+
+// One-pass top-k candidates: a sorted strided sample of the slice gives a
+// threshold t expected to let ~max(4k, 512) elements through; one pass then
+// gathers every element >= t (a ballot and one shared atomic per warp, no
+// histogram).  Returns the number gathered when it holds the top k (k <= count
+// <= kCandCap), otherwise -1 and the caller takes the exact radix path.
+__device__ int slice_gather_sampled(const SampleArgs& a, const float* lg, int k, int vend, SelectSmem& sm) {
+  const int tid = threadIdx.x, lane = tid & 31;
+  if (vend < 8 * kSample || k > 256) return -1;
+  const int stride = vend / kSample;
+  for (int i = tid; i < kSample; i += blockDim.x) {
+    sm.val[i] = lg[(int64_t)i * stride];
+    sm.idx[i] = i;
+  }
+  __syncthreads();
+  bitonic_desc(sm.val, sm.idx, kSample);
+  const int want = max(4 * k, 512);
+  int r = (int)(((int64_t)want * kSample) / vend);
+  r = min(max(r, 2), kSample - 1);
+  const float t = sm.val[r - 1];
+  if (tid == 0) sm.misc[3] = 0;
+  __syncthreads();
+  for (int base = 0; base < vend; base += blockDim.x) {
+    const int v = base + tid;
+    float l = -INFINITY;
+    if (v < vend) l = lg[v];
+    const bool take = v < vend && l >= t;
+    const unsigned m = __ballot_sync(0xffffffffu, take);
+    if (m) {
+      int wbase = 0;
+      if (lane == 0) wbase = atomicAdd(&sm.misc[3], __popc(m));
+      wbase = __shfl_sync(0xffffffffu, wbase, 0);
+      const int p = wbase + __popc(m & ((1u << lane) - 1u));
+      if (take && p < kCandCap) {
+        sm.val[p] = l;
+        sm.idx[p] = a.v0 + v;
+      }
+    }
+  }
+  __syncthreads();
+  const int n = sm.misc[3];
+  if (n < k || n > kCandCap) return -1;
+  int npow = 1;
+  while (npow < n) npow <<= 1;
+  for (int i = n + tid; i < npow; i += blockDim.x) {
+    sm.val[i] = -INFINITY;
+    sm.idx[i] = 0x7fffffff;
+  }
+  __syncthreads();
+  bitonic_desc(sm.val, sm.idx, npow);
+  return n;
+}
+
 // Finds the top-k (k <= kMaxTopK) of the slice: on return sm.val/sm.idx[0..k)
 // hold them sorted (raw value desc, global id asc) and the function returns k
 // (fewer when the slice is shorter).
@@ -239,6 +293,8 @@ __device__ int slice_topk(const SampleArgs& a, const float* lg, int k, SelectSme
   const int vend = min(a.Vl, a.Vtot - a.v0);
   if (k > vend) k = vend;
   if (k <= 0) return 0;
+  if (slice_gather_sampled(a, lg, k, vend, sm) >= 0) return k;
+  __syncthreads();
   uint32_t prefix = 0, mask = 0;
   int need = k;   // rank of the boundary element inside the current prefix group
   int shift = 20, bits = 12;
@@ -404,7 +460,7 @@ __device__ int slice_topk(const SampleArgs& a, const float* lg, int k, SelectSme
 }
 
 template <bool FINISH>
-__global__ void __launch_bounds__(kSampThreads) sample_select_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kSampThreads, 2) sample_select_kernel(SampleArgs a) {
   griddep_entry();
   __shared__ SelectSmem sm;
   __shared__ int64_t epoch_sh;

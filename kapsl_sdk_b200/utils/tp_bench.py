@@ -90,13 +90,24 @@ def main():
     from .._ext import cuda_ops
 
     c = cuda_ops()
-    for mode in ("fused", "scatter", "nccl", "gemm_only", "scatter_only", "reduce_only"):
-        fusedbuf = mode in ("fused", "scatter", "scatter_only", "reduce_only")
+    nw = torch.ones(NO, device=dev, dtype=torch.bfloat16)
+    for mode in ("fused", "norm", "norm_only", "scatter", "nccl", "nccl_norm", "gemm_only", "scatter_only",
+                 "reduce_only"):
+        fusedbuf = mode in ("fused", "norm", "norm_only", "scatter", "scatter_only", "reduce_only")
         tp = TPComm(world, rank, dev, ("scatter" if mode == "scatter" else "fused") if fusedbuf else "nccl", max_tokens=M, hidden=NO)
         h = tp.residual_stream(M) if fusedbuf else torch.zeros(M, NO, device=dev, dtype=torch.bfloat16)
         rpr = (M + world - 1) // world
         err = ops.error_buffer(dev)
-        if mode == "gemm_only":
+        b = tp.bufs
+        if mode == "norm":  # the layer boundary of the fused path: GEMM + reduce + residual + RMSNorm + all-gather
+            fn = lambda: tp.row_parallel_norm(x, w, h, nw, 1e-6)
+        elif mode == "norm_only":
+            fn = lambda: c.tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, nw, 1e-6, rank, rpr, M, NO,
+                                             tp.epoch, err, tp.timeout_ns)
+        elif mode == "nccl_norm":  # the NCCL path's layer boundary: GEMM, all-reduce, residual add, RMSNorm
+            xo = torch.empty_like(h)
+            fn = lambda: (tp.row_parallel_residual(x, w, h), ops.rmsnorm(h, nw, 1e-6, out=xo))
+        elif mode == "gemm_only":
             fn = lambda: ops.linear(x, w)
         elif mode == "scatter_only":
             fn = lambda: c.gemm_scatter(x, w, tp.bufs["recv"], rank, rpr, NO, err)
@@ -119,10 +130,10 @@ def main():
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         res[mode + "_ms"] = round(float(ms), 4)
         res[mode + "_err"] = ops.check_errors(dev)
-        if mode == "fused":
+        if mode in ("fused", "norm"):
             st = tp.epoch.tolist()  # start, after barrier 1, last CTA done, after barrier 2 (ns)
-            res["fused_phase_us"] = {"barrier1": (st[3] - st[2]) / 1e3, "work": (st[4] - st[3]) / 1e3,
-                                     "barrier2": (st[5] - st[4]) / 1e3}
+            res[mode + "_phase_us"] = {"barrier1": (st[3] - st[2]) / 1e3, "work": (st[4] - st[3]) / 1e3,
+                                       "barrier2": (st[5] - st[4]) / 1e3}
         tp.close()
     flops = 2 * M * NO * K
     nvl = 2 * (world - 1) / world * M * NO * 2
