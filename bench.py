@@ -60,6 +60,11 @@ WORKLOADS["tiny-llama-cpu"] = dict(model="tiny-llama", num_requests=4, min_promp
 # disaggregated prefill/decode (``--parallel pd``): 32 requests, 8192-token prompts, 128 output tokens
 WORKLOADS["llama-3-8b-pd"] = dict(model="llama-3-8b", num_requests=32, min_prompt=8192, max_prompt=8192,
                                   output_len=128)
+# The in-repo library baseline (B1: cuBLAS + NCCL + vLLM flash-attention on the same engine,
+# `bench.py --impl b1`) for the headline workload, output tok/s by GPU count, as recorded in
+# BASELINE.md; vs_baseline = value / this (null where B1 has no number for that count).
+B1_TOK_S = {("qwen2.5-7b", 1): 4351.21}
+
 MODEL_LABEL = {"qwen2.5-7b": "Qwen2.5-7B-arch", "mixtral-8x7b": "Mixtral-8x7B-arch",
                "llama-3-70b-q4k": "Llama-3-70B-arch Q4_K", "llama-3-8b": "Llama-3-8B-arch"}
 
@@ -338,7 +343,10 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
-            "higher_is_better": True, "scaling": "strong" if args.parallel == "tp" else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if args.parallel == "tp" else "weak",
+            "vs_baseline": (round(value / B1_TOK_S[(args.model, world)], 3)
+                            if args.impl == "kapsl" and args.parallel == "tp" and (args.model, world) in B1_TOK_S
+                            and args.num_requests == WORKLOADS["qwen2.5-7b"]["num_requests"] else None),
             "dtype": "bf16", "data": "synthetic token ids, random-init weights N(0,0.02) seed 0",
             "config": {"model": MODEL_LABEL.get(args.model, args.model),
                        "global_batch": args.num_requests * (world if tp_comm is None else 1),
