@@ -416,6 +416,46 @@ void tp_reduce_norm_ag(std::vector<int64_t> partial, std::vector<int64_t> xout, 
                                   err.data_ptr<int>(), kapsl::gemm_num_sms(), (uint64_t)timeout_ns, cur_stream());
 }
 
+void flag_pingpong(int64_t my_flag, int64_t peer_flag, int64_t peer_data, int64_t payload_bytes, int64_t rank,
+                   int64_t iters, int64_t mode, int64_t base, int64_t timeout_ns, Tensor out_ns, Tensor err) {
+  TORCH_CHECK(my_flag % 8 == 0 && peer_flag % 8 == 0 && peer_data % 16 == 0 && payload_bytes % 16 == 0,
+              "flag_pingpong: aligned flags and payload");
+  CHECK_DT(out_ns, at::kLong, "out_ns");
+  kapsl::launch_flag_pingpong(reinterpret_cast<int64_t*>(my_flag), reinterpret_cast<int64_t*>(peer_flag),
+                              reinterpret_cast<void*>(peer_data), (int)payload_bytes, (int)rank, (int)iters,
+                              (int)mode, base, (uint64_t)timeout_ns, out_ns.data_ptr<int64_t>(), err.data_ptr<int>(),
+                              cur_stream());
+}
+
+void tp_ll_norm(Tensor own, std::vector<int64_t> slot, std::vector<int64_t> gslot, Tensor h, Tensor xout, Tensor w,
+                double eps, int64_t rank, int64_t rows_per_rank, int64_t rows_total, int64_t cap, bool two,
+                Tensor epoch_ctr, Tensor err, int64_t timeout_ns) {
+  TORCH_CHECK(timeout_ns > 0, "tp_ll_norm: timeout_ns must be positive");
+  TORCH_CHECK(!two || gslot.size() == slot.size(), "tp_ll_norm: gather slot table");
+  CHECK_DT(own, at::kBFloat16, "own");
+  CHECK_DT(h, at::kBFloat16, "h");
+  CHECK_DT(xout, at::kBFloat16, "xout");
+  CHECK_DT(w, at::kBFloat16, "w");
+  CHECK_DT(epoch_ctr, at::kLong, "epoch_ctr");
+  CHECK_DT(err, at::kInt, "err");
+  const int64_t ld = h.stride(0);
+  TORCH_CHECK(h.dim() == 2 && h.stride(1) == 1 && w.numel() == h.size(1) && w.is_contiguous() &&
+                  own.stride(0) == ld && xout.stride(0) == ld && own.stride(1) == 1 && xout.stride(1) == 1 &&
+                  own.size(0) >= rows_total && xout.size(0) >= rows_total && h.size(0) >= rows_total,
+              "tp_ll_norm: own / h / xout [rows, cols] with one row stride, w [cols]");
+  for (auto p : slot) TORCH_CHECK(p % 16 == 0, "tp_ll_norm: slots must be 16-byte aligned");
+  for (auto p : gslot) TORCH_CHECK(p % 16 == 0, "tp_ll_norm: slots must be 16-byte aligned");
+  const c10::cuda::CUDAGuard g(h.device());
+  std::vector<void*> sp, gp;
+  for (auto p : slot) sp.push_back(reinterpret_cast<void*>(p));
+  for (auto p : gslot) gp.push_back(reinterpret_cast<void*>(p));
+  kapsl::launch_tp_ll_norm(bf(own), sp.data(), two ? gp.data() : nullptr, bf(h), bf(xout),
+                           reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (float)eps, (int)sp.size(), (int)rank,
+                           (int)rows_per_rank, (int)rows_total, (int)h.size(1), ld, (int)cap, two,
+                           epoch_ctr.data_ptr<int64_t>(), err.data_ptr<int>(), kapsl::gemm_num_sms(),
+                           (uint64_t)timeout_ns, cur_stream());
+}
+
 void p2p_copy(int64_t dst, int64_t src, int64_t bytes, int64_t ctas_per_sm) {
   TORCH_CHECK(bytes % 16 == 0 && dst % 16 == 0 && src % 16 == 0, "p2p_copy: 16-byte aligned sizes and addresses");
   kapsl::launch_p2p_copy(reinterpret_cast<void*>(dst), reinterpret_cast<const void*>(src), bytes, (int)ctas_per_sm,
@@ -645,6 +685,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_pull_reduce_ag", &tp_pull_reduce_ag, "barrier + pull peers' partial rows + residual + all-gather push");
   m.def("tp_reduce_norm_ag", &tp_reduce_norm_ag,
         "barrier + pull peers' partial rows + residual (own rows) + RMSNorm + all-gather of the normed rows");
+  m.def("flag_pingpong", &flag_pingpong, "NVLink flag round-trip latency probe (two ranks)");
+  m.def("tp_ll_norm", &tp_ll_norm,
+        "one-shot row reduction + residual + RMSNorm with flag-carrying 8-byte lines (few rows)");
+  m.def("tp_ll_slot_bytes", &kapsl::tp_ll_slot_bytes);
   m.def("p2p_copy", &p2p_copy, "16-byte vector copy between (possibly peer-mapped) device addresses");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_free", &symm_free);

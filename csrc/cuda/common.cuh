@@ -168,15 +168,24 @@ __device__ __forceinline__ int64_t ld_acquire_sys(const int64_t* p) {
   asm volatile("ld.acquire.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
+__device__ __forceinline__ int64_t ld_relaxed_sys(const int64_t* p) {
+  int64_t v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
 // Waits until flags_site[p] >= epoch for every p < world; false after timeout_ns.
+// The flags are polled with relaxed loads and one acquire fence follows the last
+// one (fence-based acquire: later loads see what the peers released before their
+// flag stores), which measured half the round trip of polling with ld.acquire.
 __device__ __forceinline__ bool wait_flags(const int64_t* flags_site, int world, int64_t epoch,
                                            uint64_t timeout_ns) {
   const uint64_t t0 = globaltimer_ns();
   for (int p = 0; p < world; ++p) {
-    while (ld_acquire_sys(flags_site + p) < epoch) {
+    while (ld_relaxed_sys(flags_site + p) < epoch) {
       if (globaltimer_ns() - t0 > timeout_ns) return false;
     }
   }
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
   return true;
 }
 

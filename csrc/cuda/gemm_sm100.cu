@@ -390,16 +390,19 @@ __device__ __forceinline__ void mma_commit_2sm_mc(uint64_t* bar) {
       : "memory");
 }
 
-template <int STAGES, int EPI, bool OUT_F32>
+template <int BN, int STAGES, int EPI, bool OUT_F32>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm2sm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
                    int N, int K, EpiArgs ep, int* __restrict__ err) {
   griddep_entry();
-  constexpr int BN = 256;
-  constexpr int HALF_BYTES = 128 * BK * 2;  // 16 KiB: A half or B half
-  constexpr int STAGE_BYTES = 2 * HALF_BYTES;
-  constexpr uint32_t TMEM_COLS = 512;
-  constexpr uint32_t IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+  static_assert(BN % 32 == 0 && BN >= 64 && BN <= 256, "2-SM tile width");
+  constexpr int A_HALF = 128 * BK * 2;       // 16 KiB: this CTA's 128 rows of the A tile
+  constexpr int B_HALF = (BN / 2) * BK * 2;  // this CTA's BN/2 rows of the B tile
+  constexpr int HALF_BYTES = A_HALF;
+  constexpr int STAGE_BYTES = A_HALF + B_HALF;
+  static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1 KiB aligned (128-byte swizzle atoms)");
+  constexpr uint32_t TMEM_COLS = 512;        // two accumulators at columns 0 and 256
+  constexpr uint32_t IDESC = idesc_bf16<256, BN>();
 
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -467,7 +470,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           uint8_t* sb = sa + HALF_BYTES;
           if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
           tma_load_2d_2sm(sa, &tmap_a, &full_bar[stage], kb * BK, mt * 256 + (int)rank * 128);
-          tma_load_2d_2sm(sb, &tmap_b, &full_bar[stage], kb * BK, nt * BN + (int)rank * 128);
+          tma_load_2d_2sm(sb, &tmap_b, &full_bar[stage], kb * BK, nt * BN + (int)rank * (BN / 2));
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -490,7 +493,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * 256);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase)) {
             abort_sh = 1;
@@ -535,7 +538,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       }
       tc_fence_after();
       const int row = mt * 256 + (int)rank * 128 + quad * 32 + lane;
-      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * BN);
+      const uint32_t tbase = tmem_base + ((uint32_t)(quad * 32) << 16) + (uint32_t)(acc * 256);
       if (EPI == 3) {
         constexpr int HALF = BN / 2;
         const int out_c0 = nt * HALF;
@@ -589,11 +592,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
 }
 
-template <int STAGES, int EPI, bool F32>
+template <int BN, int STAGES, int EPI, bool F32>
 void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& ep, int grid,
                 int* err, cudaStream_t st) {
-  auto kern = gemm2sm_kernel<STAGES, EPI, F32>;
-  constexpr size_t smem = (size_t)STAGES * 2 * 128 * BK * 2 + 1024;
+  auto kern = gemm2sm_kernel<BN, STAGES, EPI, F32>;
+  constexpr size_t smem = (size_t)STAGES * (128 + BN / 2) * BK * 2 + 1024;
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
   launch_k(kern, grid, kThreads, smem, st, ta, tb, M, N, K, ep, err);
@@ -706,7 +709,7 @@ void launch_gemm_scatter(const bf16* A, int64_t lda, const bf16* B, int64_t ldb,
   if (M >= 256 && units2 * 4 >= (sms / 2) * 3) {
     CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, 128, BK);
     CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, BK);
-    launch_2sm<6, 5, false>(ta, tb, M, N, K, ep, 2 * std::min(units2, sms / 2), err, st);
+    launch_2sm<256, 6, 5, false>(ta, tb, M, N, K, ep, 2 * std::min(units2, sms / 2), err, st);
     return;
   }
   const int m_tiles = (M + BM - 1) / BM;
@@ -732,25 +735,58 @@ void launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C
   if (epi == 3 && N % 256 != 0) throw std::runtime_error("gemm: SwiGLU epilogue needs N % 256 == 0");
   const int sms = gemm_num_sms();
   {
-    // 2-SM 256x256 tiles when they fill at least 3/4 of the CTA pairs (force_bn == 512 forces them)
+    // 2-SM tiles (256 rows x BN) when 256x256 tiles fill at least 3/4 of the CTA pairs.
+    // force_bn > 256 forces them with BN = force_bn - 256 (512: 256-wide tiles).
+    // BN is picked by a wave model: time ~ waves x (BN + 16), where a wave is one
+    // tile per CTA pair and +16 charges the per-k-block fixed cost of a narrower
+    // tile; e.g. N = 4608 at M = 2304 takes 192-wide tiles (216 tiles = 2.9 waves
+    // of 74 pairs) over 256-wide ones (162 tiles = 2.2 -> 3 waves).
     const int nclusters = sms / 2;
-    const int units2 = ((M + 255) / 256) * ((N + 255) / 256);
-    const bool use2 = force_bn == 512 || (force_bn == 0 && force_splits == 0 && M >= 256 && units2 * 4 >= nclusters * 3);
+    const int m2 = (M + 255) / 256;
+    const int units256 = m2 * ((N + 255) / 256);
+    const bool use2 = force_bn > 256 || (force_bn == 0 && force_splits == 0 && M >= 256 && units256 * 4 >= nclusters * 3);
     if (use2) {
-      if (epi == 3 && N % 256 != 0) throw std::runtime_error("gemm: SwiGLU epilogue needs N % 256 == 0");
+      int bn2 = force_bn > 256 ? force_bn - 256 : 256;
+      if (force_bn == 0 && epi != 3) {
+        long best = -1;
+        for (int cand : {256, 224, 192, 128}) {
+          const int units = m2 * ((N + cand - 1) / cand);
+          const long cost = (long)((units + nclusters - 1) / nclusters) * (cand + 16);
+          if (best < 0 || cost < best) {
+            best = cost;
+            bn2 = cand;
+          }
+        }
+      }
+      if (bn2 != 256 && bn2 != 224 && bn2 != 192 && bn2 != 128) throw std::runtime_error("gemm: 2-SM tile width");
+      if (epi == 3 && (bn2 != 256 || N % 256 != 0)) throw std::runtime_error("gemm: SwiGLU epilogue needs 256-wide tiles");
       CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, 128, BK);
-      CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, BK);
+      CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, bn2 / 2, BK);
       EpiArgs ep{C, ldc, bias, res, ldr, workspace};
+      const int units2 = m2 * ((N + bn2 - 1) / bn2);
       const int grid = 2 * std::min(units2, nclusters);
       constexpr int ST = 6;
-      switch (epi) {
-        case 0: out_f32 ? launch_2sm<ST, 0, true>(ta, tb, M, N, K, ep, grid, err, st)
-                        : launch_2sm<ST, 0, false>(ta, tb, M, N, K, ep, grid, err, st); break;
-        case 1: launch_2sm<ST, 1, false>(ta, tb, M, N, K, ep, grid, err, st); break;
-        case 2: launch_2sm<ST, 2, false>(ta, tb, M, N, K, ep, grid, err, st); break;
-        case 3: launch_2sm<ST, 3, false>(ta, tb, M, N, K, ep, grid, err, st); break;
-        default: throw std::runtime_error("gemm: bad epilogue");
+#define KAPSL_GEMM2_DISPATCH(BNV)                                                                        \
+  switch (epi) {                                                                                        \
+    case 0: out_f32 ? launch_2sm<BNV, ST, 0, true>(ta, tb, M, N, K, ep, grid, err, st)                   \
+                    : launch_2sm<BNV, ST, 0, false>(ta, tb, M, N, K, ep, grid, err, st); break;          \
+    case 1: launch_2sm<BNV, ST, 1, false>(ta, tb, M, N, K, ep, grid, err, st); break;                     \
+    case 2: launch_2sm<BNV, ST, 2, false>(ta, tb, M, N, K, ep, grid, err, st); break;                     \
+    default: throw std::runtime_error("gemm: bad epilogue");                                            \
+  }
+      switch (bn2) {
+        case 256:
+          if (epi == 3) {
+            launch_2sm<256, ST, 3, false>(ta, tb, M, N, K, ep, grid, err, st);
+          } else {
+            KAPSL_GEMM2_DISPATCH(256)
+          }
+          break;
+        case 224: KAPSL_GEMM2_DISPATCH(224) break;
+        case 192: KAPSL_GEMM2_DISPATCH(192) break;
+        default: KAPSL_GEMM2_DISPATCH(128) break;
       }
+#undef KAPSL_GEMM2_DISPATCH
       return;
     }
   }

@@ -141,6 +141,15 @@ void launch_tp_reduce_norm_ag(const __nv_bfloat16* const* partial, __nv_bfloat16
                               int64_t* const* flags, __nv_bfloat16* h, const __nv_bfloat16* w, float eps, int world,
                               int rank, int rows_per_rank, int rows_total, int cols, int64_t ld, int64_t* epoch_ctr,
                               int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
+void launch_flag_pingpong(int64_t* my_flag, int64_t* peer_flag, void* peer_data, int payload_bytes, int rank,
+                          int iters, int mode, int64_t base, uint64_t timeout_ns, int64_t* out_ns, int* err,
+                          cudaStream_t st);
+// row-parallel reduction + residual + RMSNorm with flag-carrying 8-byte lines (one-shot / two-shot)
+size_t tp_ll_slot_bytes(int world, int cap, int cols, bool two);
+void launch_tp_ll_norm(const __nv_bfloat16* own, void* const* slot, void* const* gslot, __nv_bfloat16* h,
+                       __nv_bfloat16* xout, const __nv_bfloat16* w, float eps, int world, int rank, int rows_per_rank,
+                       int rows_total, int cols, int64_t ld, int cap, bool two, int64_t* epoch_ctr, int* err,
+                       int num_sms, uint64_t timeout_ns, cudaStream_t st);
 void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st);
 void* symm_alloc(size_t bytes);
 void symm_free(void* p);

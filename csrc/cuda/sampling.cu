@@ -196,9 +196,33 @@ __device__ void slice_argmax(const SampleArgs& a, const float* lg, SelectSmem& s
   float best = -INFINITY;
   int bi = -1;
   const int vend = min(a.Vl, a.Vtot - a.v0);
-  for (int v = tid; v < vend; v += blockDim.x) {
+  // float4 loads, four in flight per thread; a thread visits its elements in
+  // increasing index order, so ">=" keeps the last of equal maxima
+  const int vend4 = (reinterpret_cast<uintptr_t>(lg) & 15) == 0 ? (vend & ~3) : 0;
+  const int step = (int)blockDim.x * 16;
+  for (int base = 0; base < vend4; base += step) {
+    float4 q[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = base + (u * (int)blockDim.x + tid) * 4;
+      if (v < vend4) q[u] = *reinterpret_cast<const float4*>(lg + v);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int v = base + (u * (int)blockDim.x + tid) * 4;
+      if (v >= vend4) continue;
+      const float e[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        if (bi < 0 || e[j] >= best) {
+          best = e[j];
+          bi = v + j;
+        }
+    }
+  }
+  for (int v = vend4 + tid; v < vend; v += blockDim.x) {
     const float l = lg[v];
-    if (bi < 0 || l > best || (l == best && v > bi)) {
+    if (bi < 0 || l >= best) {
       best = l;
       bi = v;
     }
@@ -231,41 +255,91 @@ __device__ void slice_argmax(const SampleArgs& a, const float* lg, SelectSmem& s
   __syncthreads();
 }
 
-static constexpr int kSample = 2048;  // strided sample that places the one-pass threshold
+static constexpr int kSample = 4096;  // strided sample that places the one-pass threshold (4 per thread)
+static constexpr int kGatherVec = 4;  // float4 loads per thread in flight in the one-pass gather
 
-// One-pass top-k candidates: a sorted strided sample of the slice gives a
-// threshold t expected to let ~max(4k, 512) elements through; one pass then
-// gathers every element >= t (a ballot and one shared atomic per warp, no
-// histogram).  Returns the number gathered when it holds the top k (k <= count
-// <= kCandCap), otherwise -1 and the caller takes the exact radix path.
+__device__ __forceinline__ float key_float(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
+}
+
+// One-pass top-k candidates: a strided sample of the slice places a threshold t
+// expected to let ~3k + 64 elements through (the largest 16-bit key prefix that
+// at least r sample values reach, found by a bisection of block-wide counts; no
+// sort); one pass then gathers every element >= t.  Returns the number gathered
+// when it holds the top k (k <= count <= kCandCap), otherwise -1 and the caller
+// takes the exact radix path.
 __device__ int slice_gather_sampled(const SampleArgs& a, const float* lg, int k, int vend, SelectSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31;
-  if (vend < 8 * kSample || k > 256) return -1;
+  if (vend < 2 * kSample || k > 256 || blockDim.x * 4 != kSample) return -1;
   const int stride = vend / kSample;
-  for (int i = tid; i < kSample; i += blockDim.x) {
-    sm.val[i] = lg[(int64_t)i * stride];
-    sm.idx[i] = i;
+  uint32_t sk[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) sk[j] = float_key(lg[(int64_t)(tid + j * blockDim.x) * stride]);
+  const int want = 3 * k + 64;
+  int r = (int)(((int64_t)want * kSample + vend - 1) / vend);
+  r = min(max(r, 2), kSample);
+  uint32_t t = 0;
+#pragma unroll 1
+  for (int bit = 31; bit >= 16; --bit) {
+    const uint32_t c = t | (1u << bit);
+    const int n = __syncthreads_count(sk[0] >= c) + __syncthreads_count(sk[1] >= c) +
+                  __syncthreads_count(sk[2] >= c) + __syncthreads_count(sk[3] >= c);
+    if (n >= r) t = c;
   }
-  __syncthreads();
-  bitonic_desc(sm.val, sm.idx, kSample);
-  const int want = max(4 * k, 512);
-  int r = (int)(((int64_t)want * kSample) / vend);
-  r = min(max(r, 2), kSample - 1);
-  const float t = sm.val[r - 1];
+  const float t_thr = (t == 0) ? -INFINITY : key_float(t);
   if (tid == 0) sm.misc[3] = 0;
   __syncthreads();
-  for (int base = 0; base < vend; base += blockDim.x) {
-    const int v = base + tid;
-    float l = -INFINITY;
-    if (v < vend) l = lg[v];
-    const bool take = v < vend && l >= t;
-    const unsigned m = __ballot_sync(0xffffffffu, take);
-    if (m) {
-      int wbase = 0;
-      if (lane == 0) wbase = atomicAdd(&sm.misc[3], __popc(m));
-      wbase = __shfl_sync(0xffffffffu, wbase, 0);
-      const int p = wbase + __popc(m & ((1u << lane) - 1u));
-      if (take && p < kCandCap) {
+  // One pass, kGatherVec float4 loads per thread in flight: each thread counts its
+  // elements >= t, a warp scan places them, one shared atomic per warp reserves room.
+  const bool vec_ok = (reinterpret_cast<uintptr_t>(lg) & 15) == 0;
+  const int vend4 = vec_ok ? (vend & ~3) : 0;
+  const int step = (int)blockDim.x * 4 * kGatherVec;
+  for (int base = 0; base < vend4; base += step) {
+    float4 q[kGatherVec];
+#pragma unroll
+    for (int u = 0; u < kGatherVec; ++u) {
+      const int v = base + (u * (int)blockDim.x + tid) * 4;
+      q[u] = v < vend4 ? *reinterpret_cast<const float4*>(lg + v) : make_float4(-INFINITY, -INFINITY, -INFINITY,
+                                                                                  -INFINITY);
+    }
+    int cnt = 0;
+#pragma unroll
+    for (int u = 0; u < kGatherVec; ++u)
+      if (base + (u * (int)blockDim.x + tid) * 4 < vend4)
+        cnt += (q[u].x >= t_thr) + (q[u].y >= t_thr) + (q[u].z >= t_thr) + (q[u].w >= t_thr);
+    int incl = cnt;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int wbase = 0;
+    if (lane == 31 && incl > 0) wbase = atomicAdd(&sm.misc[3], incl);
+    wbase = __shfl_sync(0xffffffffu, wbase, 31);
+    int p = wbase + incl - cnt;
+    if (cnt > 0) {
+#pragma unroll
+      for (int u = 0; u < kGatherVec; ++u) {
+        const int v = base + (u * (int)blockDim.x + tid) * 4;
+        if (v >= vend4) continue;
+        const float e[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (e[j] >= t_thr) {
+            if (p < kCandCap) {
+              sm.val[p] = e[j];
+              sm.idx[p] = a.v0 + v + j;
+            }
+            ++p;
+          }
+      }
+    }
+  }
+  for (int v = vend4 + tid; v < vend; v += blockDim.x) {  // tail (or an unaligned slice)
+    const float l = lg[v];
+    if (l >= t_thr) {
+      const int p = atomicAdd(&sm.misc[3], 1);
+      if (p < kCandCap) {
         sm.val[p] = l;
         sm.idx[p] = a.v0 + v;
       }

@@ -24,7 +24,9 @@ from ..ops import reference as ref
 from .config import ModelConfig
 
 
-PREFILL_TC_DEFAULT = False
+# Chunked-prefill attention on tcgen05 (attention_tc.cu) by default: checked against the fp32
+# oracle and 3-10% faster than the mma.sync kernel on 2048- and 8192-token chunks.
+PREFILL_TC_DEFAULT = True
 
 
 def _prefill(model, qkv, k_cache, v_cache, fb, attn) -> None:

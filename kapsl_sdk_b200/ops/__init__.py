@@ -41,6 +41,12 @@ DEVICE_ERRORS = {
     31: "tensor-parallel reduction (push): a peer missed barrier 2",
     32: "tensor-parallel reduction (pull): a peer missed barrier 1",
     33: "tensor-parallel reduction (pull): a peer missed barrier 2",
+    34: "tensor-parallel reduction + norm (pull): a peer missed barrier 1",
+    35: "tensor-parallel reduction + norm (pull): a peer missed barrier 2",
+    36: "tensor-parallel row reduction: a peer's partial rows did not arrive",
+    37: "tensor-parallel row reduction: an owner's normed rows did not arrive",
+    38: "tensor-parallel row reduction (LL): a peer's partial rows did not arrive",
+    39: "NVLink flag probe: the peer's flag did not arrive",
     40: "MoE permute: expert rows exceed the sorted buffer",
     41: "MoE combine: a peer missed barrier 1",
     42: "MoE combine: a peer missed barrier 2",

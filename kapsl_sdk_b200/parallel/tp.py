@@ -65,6 +65,15 @@ class TPComm:
         self.hidden = hidden
         self.max_tokens = max_tokens
         self.ep_rows = ep_rows
+        # Row counts up to which the fused layer boundary uses the flag-carrying-line
+        # kernels: one-shot (every rank reduces every row: one one-way NVLink latency,
+        # 2 x (W-1) x rows of traffic), then two-shot (owned rows + all-gather of the
+        # normed rows: two one-way latencies, ~4 x rows of traffic); above both, the
+        # barrier + pull kernel (half the bytes of two-shot lines, two flag barriers).
+        self.ll1_rows = int(os.environ.get("KAPSL_TP_LL1_ROWS", {2: 64, 4: 32, 8: 16}.get(world_size, 0)))
+        self.ll2_rows = int(os.environ.get("KAPSL_TP_LL2_ROWS", {2: 512, 4: 512, 8: 512}.get(world_size, 0)))
+        # "ll": flag-carrying lines for few rows, pull above (default); "pull": barrier + pull kernel only
+        self.norm_kernel = os.environ.get("KAPSL_TP_NORM", "ll")
         self.bufs = None
         self.ep_buf = None
         if mode != "nccl" and world_size > 1:
@@ -110,9 +119,12 @@ class TPComm:
         ep_bytes = self.ep_rows * hidden * 2
         cand_bytes = 2 * W * self.sample_rows * self.SAMPLE_K * 8
         xn_bytes = rows_pad * hidden * 2
+        # flag-carrying-line slots (reduce slots, then gather slots): rows of one source per parity
+        self.ll_cap = max(min(self.ll1_rows, rows_pad), -(-min(self.ll2_rows, rows_pad) // W), 1)
+        ll_bytes = c.tp_ll_slot_bytes(W, self.ll_cap, hidden, True)
         align = lambda n: (n + 255) // 256 * 256
         total = (align(recv_bytes) + align(hid_bytes) + align(flag_bytes) + align(ep_bytes) + align(cand_bytes)
-                 + align(xn_bytes))
+                 + align(xn_bytes) + align(ll_bytes))
         base = c.symm_alloc(total)
         handle = c.symm_handle(base)
         handles = [None] * W
@@ -125,11 +137,16 @@ class TPComm:
         off_e = off_f + align(flag_bytes)
         off_c = off_e + align(ep_bytes)
         off_x = off_c + align(cand_bytes)
+        off_ll = off_x + align(xn_bytes)
+        ll_half = ll_bytes // 2
         self.bufs = {
             "base": base, "bases": bases, "rpr": rpr, "rows_pad": rows_pad,
             "recv": [b for b in bases], "hidden": [b + off_h for b in bases], "flags": [b + off_f for b in bases],
             "ep": [b + off_e for b in bases], "cand": [b + off_c for b in bases], "xnorm": [b + off_x for b in bases],
+            "ll": [b + off_ll for b in bases], "llg": [b + off_ll + ll_half for b in bases],
         }
+        # this rank's own partial for the line kernels (the row-parallel GEMM output; read locally)
+        self.own_buf = torch.empty(rows_pad, hidden, dtype=torch.bfloat16, device=self.device)
         self.xnorm_buf = c.tensor_from_ptr(base + off_x, [rows_pad, hidden], "bfloat16", self.device.index)
         dev = self.device.index
         self.ep_buf = (c.tensor_from_ptr(base + off_e, [self.ep_rows, hidden], "bfloat16", dev)
@@ -228,19 +245,42 @@ class TPComm:
 
     def row_parallel_norm(self, x: torch.Tensor, w, h: torch.Tensor, norm_w: torch.Tensor,
                           eps: float) -> torch.Tensor:
-        """``h += all_reduce(x @ w.T)`` for the rows this rank owns (the residual
-        stream is sharded by rows), then returns ``rmsnorm(h) * norm_w`` for every
-        row (every rank's copy written by its owner).  One GEMM into the local
-        partial buffer, then one kernel: barrier, pull of the owned rows'
+        """``h += all_reduce(x @ w.T)`` then returns ``rmsnorm(h) * norm_w`` for every
+        row: one GEMM into a local partial buffer, then one kernel chosen by the
+        row count T.  T <= ll1_rows: one-shot flag-carrying lines (every rank
+        reduces every row, h stays replicated); T <= ll2_rows: two-shot lines
+        (the owner of a row reduces it, h is sharded by rows, the normed rows are
+        pushed to every rank); larger T: flag barrier, pull of the owned rows'
         partials from every peer, residual add, RMSNorm, P2P stores of the
-        normed rows, barrier."""
+        normed rows, barrier.  Every variant sums h + partial_0 + ... +
+        partial_{W-1} in rank order, so they agree bit for bit."""
         T = x.shape[0]
         b = self.bufs
         rpr = (T + self.world_size - 1) // self.world_size
-        ops.linear(x, w, out=self.partial_buf[:T])
-        cuda_ops().tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,
-                                     self.hidden, self.epoch, ops.error_buffer(x.device), self.timeout_ns)
-        return self.xnorm_buf[:T]
+        err = ops.error_buffer(x.device)
+        if self.norm_kernel == "pull":
+            ops.linear(x, w, out=self.partial_buf[:T])
+            cuda_ops().tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,
+                                         self.hidden, self.epoch, err, self.timeout_ns)
+            return self.xnorm_buf[:T]
+        own = self.own_buf[:T]
+        if self.norm_kernel == "ll":
+            ll1 = T <= min(self.ll1_rows, self.ll_cap)
+            if ll1 or (T <= self.ll2_rows and rpr <= self.ll_cap):
+                ops.linear(x, w, out=own)
+                cuda_ops().tp_ll_norm(own, b["ll"], b["llg"], h, self.xnorm_buf[:T], norm_w, float(eps), self.rank,
+                                      rpr, T, self.ll_cap, not ll1, self.epoch, err, self.timeout_ns)
+                return self.xnorm_buf[:T]
+            ops.linear(x, w, out=self.partial_buf[:T])
+            cuda_ops().tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,
+                                         self.hidden, self.epoch, err, self.timeout_ns)
+            return self.xnorm_buf[:T]
+        raise ValueError(f"unknown tensor-parallel norm kernel {self.norm_kernel!r}")
+
+    def replicated_residual(self, T: int) -> bool:
+        """Whether the fused row reduction of a ``T``-row batch keeps every row of the
+        residual stream current on every rank (one-shot) or only the owned rows."""
+        return self.norm_kernel == "ll" and T <= min(self.ll1_rows, self.ll_cap)
 
     def row_parallel_linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         """NCCL baseline: partial GEMM then all-reduce."""

@@ -2,6 +2,14 @@
 
     torchrun --nproc-per-node N --master-addr 127.0.0.1 -m kapsl_sdk_b200.utils.tp_bench M N_OUT K_TOTAL
 
+Modes (``TP_BENCH_MODES``, comma-separated): ``ll`` the model's layer boundary
+(GEMM + reduction + residual + RMSNorm, the kernel picked by row count),
+``ll1`` / ``ll2`` forced flag-carrying-line one-shot / two-shot, ``ll_only1``
+/ ``ll_only2`` those kernels alone, ``norm`` / ``norm_only`` the barrier + pull kernel,
+``fused`` the pull reduction without the norm, ``nccl`` / ``nccl_norm`` GEMM +
+NCCL all-reduce (+ add + RMSNorm), ``gemm_only``.  ``tp_bench ping`` measures
+the NVLink flag round trip between ranks 0 and 1.
+
 Each rank holds a [M, K_TOTAL/N] slice of the input and a [N_OUT, K_TOTAL/N]
 slice of the weight; one call computes h += all_reduce(x @ w.T).  Times are
 CUDA-event device times, 20 calls after 3 warm-ups, max over ranks.  The
@@ -61,14 +69,55 @@ def p2p_probe(dev, rank, world):
     c.symm_free(base)
 
 
+def ping_probe(dev, rank, world):
+    """NVLink flag round trip between ranks 0 and 1 (one thread per GPU bouncing a
+    counter): release/acquire, relaxed, and data-then-fence-then-flag."""
+    from .. import ops
+    from .._ext import cuda_ops
+
+    c = cuda_ops()
+    nbytes = 4 << 20
+    base = c.symm_alloc(nbytes + 4096)
+    handles = [None] * world
+    dist.all_gather_object(handles, c.symm_handle(base))
+    res = {}
+    if rank < 2:
+        peer = c.symm_open(handles[1 - rank])
+        out = torch.zeros(1, dtype=torch.int64, device=dev)
+        err = ops.error_buffer(dev)
+        nxt = 0
+        for mode, payload in ((0, 0), (1, 0), (2, 0), (2, 65536), (2, 1 << 20)):
+            for it in (1, 200):
+                torch.cuda.synchronize()
+                dist.barrier(group=None)
+                c.flag_pingpong(base, peer, peer + 4096, payload, rank, it, mode, nxt, int(2e9), out, err)
+                torch.cuda.synchronize()
+                nxt += it
+                if it > 1:
+                    res[f"mode{mode}_payload{payload}_rt_us"] = round(int(out.item()) / 1e3, 2)
+        res["err"] = ops.check_errors(dev)
+        torch.cuda.synchronize()
+        dist.barrier()
+        c.symm_close(peer)
+    else:
+        for _ in range(10):
+            dist.barrier()
+        dist.barrier()
+    if rank == 0:
+        print(json.dumps({"ping": res}), flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    c.symm_free(base)
+
+
 def main():
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
-    if sys.argv[1] == "p2p":
-        p2p_probe(dev, rank, world)
+    if sys.argv[1] in ("p2p", "ping"):
+        (p2p_probe if sys.argv[1] == "p2p" else ping_probe)(dev, rank, world)
         dist.destroy_process_group()
         return
     M, NO, KT = (int(x) for x in sys.argv[1:4])
@@ -91,16 +140,36 @@ def main():
 
     c = cuda_ops()
     nw = torch.ones(NO, device=dev, dtype=torch.bfloat16)
-    for mode in ("fused", "norm", "norm_only", "scatter", "nccl", "nccl_norm", "gemm_only", "scatter_only",
-                 "reduce_only"):
-        fusedbuf = mode in ("fused", "norm", "norm_only", "scatter", "scatter_only", "reduce_only")
-        tp = TPComm(world, rank, dev, ("scatter" if mode == "scatter" else "fused") if fusedbuf else "nccl", max_tokens=M, hidden=NO)
+    modes = os.environ.get("TP_BENCH_MODES", "ll,ll1,ll2,ll_only1,ll_only2,norm,norm_only,nccl,"
+                                             "nccl_norm,gemm_only").split(",")
+    for mode in modes:
+        fusedbuf = mode not in ("nccl", "nccl_norm", "gemm_only")
+        tp = TPComm(world, rank, dev, "fused" if fusedbuf else "nccl", max_tokens=M, hidden=NO)
+        if mode in ("rows1", "rows_only1"):
+            tp.oneshot_rows = 1 << 30
+        elif mode in ("rows2", "rows_only2"):
+            tp.oneshot_rows = 0
+        if mode in ("ll1", "ll_only1"):
+            tp.ll1_rows, tp.ll2_rows = M, 0
+        elif mode in ("ll2", "ll_only2"):
+            tp.ll1_rows, tp.ll2_rows = 0, M
+        if mode in ("ll1", "ll_only1", "ll2", "ll_only2"):
+            tp.close()  # re-size the slots
+            tp._setup_symmetric(M, NO)
+        if mode in ("norm", "norm_only"):
+            tp.norm_kernel = "pull"
         h = tp.residual_stream(M) if fusedbuf else torch.zeros(M, NO, device=dev, dtype=torch.bfloat16)
         rpr = (M + world - 1) // world
         err = ops.error_buffer(dev)
         b = tp.bufs
-        if mode == "norm":  # the layer boundary of the fused path: GEMM + reduce + residual + RMSNorm + all-gather
+        if mode in ("norm", "ll", "ll1", "ll2"):  # GEMM + reduce + residual + norm
             fn = lambda: tp.row_parallel_norm(x, w, h, nw, 1e-6)
+        elif mode in ("ll_only1", "ll_only2"):
+            two = mode == "ll_only2"
+            own = tp.own_buf[:M]
+            own.copy_(ops.linear(x, w))
+            fn = lambda: c.tp_ll_norm(own, b["ll"], b["llg"], h, tp.xnorm_buf[:M], nw, 1e-6, rank, rpr, M, tp.ll_cap,
+                                      two, tp.epoch, err, tp.timeout_ns)
         elif mode == "norm_only":
             fn = lambda: c.tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, nw, 1e-6, rank, rpr, M, NO,
                                              tp.epoch, err, tp.timeout_ns)
@@ -109,17 +178,14 @@ def main():
             fn = lambda: (tp.row_parallel_residual(x, w, h), ops.rmsnorm(h, nw, 1e-6, out=xo))
         elif mode == "gemm_only":
             fn = lambda: ops.linear(x, w)
-        elif mode == "scatter_only":
-            fn = lambda: c.gemm_scatter(x, w, tp.bufs["recv"], rank, rpr, NO, err)
-        elif mode == "reduce_only":
-            fn = lambda: c.tp_reduce_ag(tp.bufs["recv"], tp.bufs["hidden"], tp.bufs["flags"], rank, rpr, M, NO, NO,
-                                        tp.epoch, err, tp.timeout_ns)
         else:
             fn = lambda: tp.row_parallel_residual(x, w, h)
         for _ in range(3):
             fn()
         torch.cuda.synchronize()
         dist.barrier()
+        if fusedbuf:
+            tp.phase_times(reset=True)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record()
         for _ in range(20):
@@ -130,17 +196,16 @@ def main():
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         res[mode + "_ms"] = round(float(ms), 4)
         res[mode + "_err"] = ops.check_errors(dev)
-        if mode in ("fused", "norm"):
-            st = tp.epoch.tolist()  # start, after barrier 1, last CTA done, after barrier 2 (ns)
-            res[mode + "_phase_us"] = {"barrier1": (st[3] - st[2]) / 1e3, "work": (st[4] - st[3]) / 1e3,
-                                       "barrier2": (st[5] - st[4]) / 1e3}
+        if fusedbuf:  # rank 0's mean phase times (us): first wait, data, second wait
+            res[mode + "_phase_us"] = {k: round(v, 2) for k, v in tp.phase_times().items() if k != "calls"}
         tp.close()
     flops = 2 * M * NO * K
     nvl = 2 * (world - 1) / world * M * NO * 2
     roof = max(flops / peak, nvl / 770e9) * 1e3
     res["roofline_ms"] = round(roof, 4)
-    res["fused_frac_of_roofline"] = round(roof / res["fused_ms"], 3)
-    res["nccl_frac_of_roofline"] = round(roof / res["nccl_ms"], 3)
+    for k in ("ll", "norm", "nccl"):
+        if k + "_ms" in res:
+            res[k + "_frac_of_roofline"] = round(roof / res[k + "_ms"], 3)
     if rank == 0:
         print(json.dumps(res), flush=True)
     dist.barrier()
