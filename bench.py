@@ -100,6 +100,9 @@ def parse_args():
     p.add_argument("--num-layers", type=int, default=0, help="override (testing only; invalid for the metric)")
     p.add_argument("--warmup-scale", type=float, default=1.0,
                    help="fraction of requests served by each warm-up step")
+    p.add_argument("--no-e2e", action="store_true",
+                   help="skip the end-to-end pass through the serving API (secondary workloads; the headline "
+                        "line always carries it)")
     p.add_argument("--profile", action="store_true",
                    help="per-step host/device breakdown of the timed region (stderr, one JSON line per rank)")
     a = p.parse_args()
@@ -312,7 +315,10 @@ def main():
     e2e_prompts = prompts_for(npass + args.steps)
     h2d1, d2h1 = engine.runner.stats["h2d_bytes"], engine.runner.stats["d2h_bytes"]
     group = tp_comm is not None and world > 1  # data-parallel replicas each serve their own copy
-    e2e_tokens, e2e_s = serve_e2e(engine, world if group else 1, rank if group else 0, params, e2e_prompts)
+    if args.no_e2e:
+        e2e_tokens, e2e_s = 0, 1.0
+    else:
+        e2e_tokens, e2e_s = serve_e2e(engine, world if group else 1, rank if group else 0, params, e2e_prompts)
     e2e_h2d = engine.runner.stats["h2d_bytes"] - h2d1
     e2e_d2h = engine.runner.stats["d2h_bytes"] - d2h1
     barrier()
@@ -356,7 +362,7 @@ def main():
                        "num_layers": cfg.num_layers},
             "p50_ttft_ms": round(ttft_all * 1000, 2), "p50_tpot_ms": round(tpot_all * 1000, 3),
             "clocks": clocks.summary(),
-            "e2e": {"value": round(tot_e2e_tokens / e2e_max, 2), "unit": "output tokens/s",
+            "e2e": None if args.no_e2e else {"value": round(tot_e2e_tokens / e2e_max, 2), "unit": "output tokens/s",
                     "h2d_bytes_per_step": int(e2e_h2d), "d2h_bytes_per_step": int(e2e_d2h),
                     "api": "KapslClient.infer_stream over a Unix socket (token-id prompts; rank 0 serves, "
                            "other ranks follow its steps)",
