@@ -38,6 +38,9 @@
 namespace kapsl {
 
 static constexpr int kSampThreads = 1024;
+// The select kernel runs 512 threads with two CTAs per SM (64 registers a thread, no
+// spills), so one wave holds 296 rows.
+static constexpr int kSelectThreads = 512;
 static constexpr int kMaxTopK = 1024;   // largest top_k of the fast path
 static constexpr int kCandCap = 2048;   // candidates gathered into shared memory
 static constexpr int kHistBins = 4096;  // 12-bit digits
@@ -255,7 +258,8 @@ __device__ void slice_argmax(const SampleArgs& a, const float* lg, SelectSmem& s
   __syncthreads();
 }
 
-static constexpr int kSample = 4096;  // strided sample that places the one-pass threshold (4 per thread)
+static constexpr int kSample = 4096;  // strided sample that places the one-pass threshold
+static constexpr int kSamplePer = kSample / kSelectThreads;
 static constexpr int kGatherVec = 4;  // float4 loads per thread in flight in the one-pass gather
 
 __device__ __forceinline__ float key_float(uint32_t k) {
@@ -270,11 +274,12 @@ __device__ __forceinline__ float key_float(uint32_t k) {
 // takes the exact radix path.
 __device__ int slice_gather_sampled(const SampleArgs& a, const float* lg, int k, int vend, SelectSmem& sm) {
   const int tid = threadIdx.x, lane = tid & 31;
-  if (vend < 2 * kSample || k > 256 || blockDim.x * 4 != kSample) return -1;
+  if (vend < 2 * kSample || k > 256 || blockDim.x != kSelectThreads) return -1;
   const int stride = vend / kSample;
-  uint32_t sk[4];
+  const int warp = tid >> 5, nwarps = kSelectThreads / 32;
+  uint32_t sk[kSamplePer];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) sk[j] = float_key(lg[(int64_t)(tid + j * blockDim.x) * stride]);
+  for (int j = 0; j < kSamplePer; ++j) sk[j] = float_key(lg[(int64_t)(tid + j * kSelectThreads) * stride]);
   const int want = 3 * k + 64;
   int r = (int)(((int64_t)want * kSample + vend - 1) / vend);
   r = min(max(r, 2), kSample);
@@ -282,8 +287,16 @@ __device__ int slice_gather_sampled(const SampleArgs& a, const float* lg, int k,
 #pragma unroll 1
   for (int bit = 31; bit >= 16; --bit) {
     const uint32_t c = t | (1u << bit);
-    const int n = __syncthreads_count(sk[0] >= c) + __syncthreads_count(sk[1] >= c) +
-                  __syncthreads_count(sk[2] >= c) + __syncthreads_count(sk[3] >= c);
+    int mine = 0;
+#pragma unroll
+    for (int j = 0; j < kSamplePer; ++j) mine += sk[j] >= c;
+    mine = __reduce_add_sync(0xffffffffu, mine);
+    if (lane == 0) sm.wsum[warp] = (uint32_t)mine;
+    __syncthreads();
+    int n = 0;
+#pragma unroll
+    for (int w = 0; w < nwarps; ++w) n += (int)sm.wsum[w];
+    __syncthreads();
     if (n >= r) t = c;
   }
   const float t_thr = (t == 0) ? -INFINITY : key_float(t);
@@ -534,7 +547,7 @@ __device__ int slice_topk(const SampleArgs& a, const float* lg, int k, SelectSme
 }
 
 template <bool FINISH>
-__global__ void __launch_bounds__(kSampThreads, 2) sample_select_kernel(SampleArgs a) {
+__global__ void __launch_bounds__(kSelectThreads, 2) sample_select_kernel(SampleArgs a) {
   griddep_entry();
   __shared__ SelectSmem sm;
   __shared__ int64_t epoch_sh;
@@ -858,13 +871,13 @@ void launch_sample(const SampleLaunch& l, cudaStream_t st) {
   SampleArgs a{};
   fill_args(a, l);
   if (l.world <= 1) {
-    launch_k(sample_select_kernel<true>, l.B, kSampThreads, 0, st, a);
+    launch_k(sample_select_kernel<true>, l.B, kSelectThreads, 0, st, a);
     KAPSL_LAUNCH_CHECK();
     note_launch();
   } else {
     if (l.world > 8 || l.B > l.b_cap || l.ctr == nullptr || l.cand[l.rank] == nullptr)
       throw std::runtime_error("sample: vocab-parallel buffers missing or too small");
-    launch_k(sample_select_kernel<false>, l.B, kSampThreads, 0, st, a);
+    launch_k(sample_select_kernel<false>, l.B, kSelectThreads, 0, st, a);
     KAPSL_LAUNCH_CHECK();
     note_launch();
     if (l.flags[l.rank] != nullptr) launch_sample_merge(l, st);
