@@ -86,10 +86,12 @@ def parse_args():
     p.add_argument("--max-prompt", type=int, default=None)
     p.add_argument("--output-len", type=int, default=None)
     p.add_argument("--chunk", type=int, default=2048)
-    p.add_argument("--parallel", default="tp", choices=["dp", "tp", "pd"],
+    p.add_argument("--parallel", default="tp", choices=["dp", "tp", "pd", "pp"],
                    help="tp: one model over all N GPUs (the named TP=N config, strong scaling); "
                         "dp: N independent replicas, each serving its own copy of the workload; "
-                        "pd: disaggregated, prefill on GPUs [0, N/2) and decode on [N/2, N), TP N/2 each")
+                        "pd: disaggregated, prefill on GPUs [0, N/2) and decode on [N/2, N), TP N/2 each; "
+                        "pp: N pipeline stages (layers split over the GPUs, hidden states over NCCL "
+                        "point-to-point, two micro-batches per step)")
     p.add_argument("--kv-mode", default="p2p", choices=["p2p", "copy"],
                    help="pd: KV transfer by the P2P push kernel or the copy-engine baseline")
     p.add_argument("--tp-mode", default="fused", choices=["fused", "nccl"],
@@ -230,19 +232,27 @@ def main():
         from kapsl_sdk_b200.parallel.tp import TPComm
 
         tp_comm = TPComm.from_world(mode="nccl" if args.impl == "b1" else args.tp_mode)
+    pp_stage = None
+    if args.parallel == "pp" and world > 1:
+        from kapsl_sdk_b200.parallel.pp import PipelineStage
+
+        pp_stage = PipelineStage(rank, world, cfg.num_layers, micro_batches=2)
+        args.no_e2e = True  # the serving front end drives tensor-parallel groups, not pipeline stages
     model_cls = None
     if args.impl == "b1":
         from kapsl_sdk_b200.models.baseline import BaselineCausalLM as model_cls
     ecfg = EngineConfig(max_num_seqs=args.num_requests, max_num_batched_tokens=args.chunk,
                         max_model_len=args.max_prompt + args.output_len + 16, use_cuda_graph=not args.no_graph,
                         overlap_steps=not args.no_overlap)
-    engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0, model_cls=model_cls)
+    engine = LLMEngine(cfg, device=dev, engine_cfg=ecfg, tp_comm=tp_comm, seed=0, model_cls=model_cls,
+                       pp_stage=pp_stage)
+    shared = tp_comm is not None or pp_stage is not None  # one workload over all ranks
     weight_gb = (torch.cuda.memory_allocated(dev) - engine.pool.storage.numel() * engine.pool.storage.element_size()) / 1e9
     # data-parallel replicas serve their own copy of the workload (weak scaling);
     # tensor parallel shares one workload across the ranks (strong scaling).
     # A fresh prompt set for every pass (warm-up, timed, end-to-end), so no pass
     # can reuse KV blocks that an earlier pass left in the prefix cache.
-    rank_seed = 1000 * (rank if tp_comm is None else 0)
+    rank_seed = 1000 * (0 if shared else rank)
 
     def prompts_for(pass_idx: int):
         return make_workload(args, cfg.vocab_size, seed=1 + rank_seed + pass_idx)
@@ -330,32 +340,33 @@ def main():
         g = torch.stack(gathered)
         ms_max = float(g[:, 0].max())
         e2e_max = float(g[:, 2].max())
-        if tp_comm is None:
+        if not shared:
             tot_tokens = float(g[:, 1].sum())
             tot_e2e_tokens = float(g[:, 3].sum())
         else:
             tot_tokens = float(g[0, 1])
             tot_e2e_tokens = float(g[0, 3])  # served by rank 0
-        e2e_max = float(g[0, 2]) if tp_comm is not None else e2e_max
+        e2e_max = float(g[0, 2]) if shared else e2e_max
         ttft_all = float(g[:, 4].max())
         tpot_all = float(g[:, 5].max())
     else:
         ms_max, e2e_max, tot_tokens, tot_e2e_tokens, ttft_all, tpot_all = ms, e2e_s, out_tokens, e2e_tokens, ttft, tpot
     value = tot_tokens / (ms_max / 1000.0)
-    par = (f"tp{world}" + ("" if world == 1 else f"-{args.tp_mode}")) if args.parallel == "tp" else f"dp{world}"
+    par = ((f"tp{world}" + ("" if world == 1 else f"-{args.tp_mode}")) if args.parallel == "tp"
+           else f"{args.parallel}{world}")
     if args.impl == "b1":
         par += " (library baseline: cuBLAS + NCCL + vLLM flash-attention)"
     if rank == 0:
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "output tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
-            "higher_is_better": True, "scaling": "strong" if args.parallel == "tp" else "weak",
+            "higher_is_better": True, "scaling": "strong" if shared or args.parallel == "tp" else "weak",
             "vs_baseline": (round(value / B1_TOK_S[(args.model, world)], 3)
                             if args.impl == "kapsl" and args.parallel == "tp" and (args.model, world) in B1_TOK_S
                             and args.num_requests == WORKLOADS["qwen2.5-7b"]["num_requests"] else None),
             "dtype": "bf16", "data": "synthetic token ids, random-init weights N(0,0.02) seed 0",
             "config": {"model": MODEL_LABEL.get(args.model, args.model),
-                       "global_batch": args.num_requests * (world if tp_comm is None else 1),
+                       "global_batch": args.num_requests * (1 if shared else world),
                        "seq_len": f"prompt U[{args.min_prompt},{args.max_prompt}] + {args.output_len} out",
                        "parallelism": par, "chunked_prefill": args.chunk, "kv_block": 16,
                        "l2": f"inputs larger than L2 ({weight_gb:.0f} GB weights, GB-scale KV), no flush",

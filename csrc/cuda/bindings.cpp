@@ -344,6 +344,22 @@ void gemm(Tensor A, Tensor B, Tensor C, int64_t epi, c10::optional<Tensor> bias,
                      (int)force_splits);
 }
 
+// Plain bf16 GEMM whose split-K partials (if it splits K) stay in the workspace for the
+// consumer; returns the number of splits (1: C was written).
+int64_t gemm_deferred(Tensor A, Tensor B, Tensor C, Tensor workspace, Tensor err) {
+  CHECK_DT(A, at::kBFloat16, "A");
+  CHECK_DT(B, at::kBFloat16, "B");
+  CHECK_DT(C, at::kBFloat16, "C");
+  CHECK_DT(workspace, at::kFloat, "workspace");
+  TORCH_CHECK(A.dim() == 2 && B.dim() == 2 && C.dim() == 2 && A.stride(1) == 1 && B.stride(1) == 1 &&
+                  C.stride(1) == 1 && B.size(1) == A.size(1) && C.size(0) == A.size(0) && C.size(1) == B.size(0),
+              "gemm_deferred: A [M, K], B [N, K], C [M, N]");
+  const c10::cuda::CUDAGuard g(A.device());
+  return kapsl::launch_gemm(bf(A), A.stride(0), bf(B), B.stride(0), C.data_ptr(), C.stride(0), false, (int)A.size(0),
+                            (int)B.size(0), (int)A.size(1), 0, nullptr, nullptr, 0, workspace.data_ptr<float>(),
+                            workspace.numel() * sizeof(float), err.data_ptr<int>(), cur_stream(), 0, 0, true);
+}
+
 // ---- tensor parallel over NVLink peer memory
 template <class T>
 std::vector<T*> as_ptrs(const std::vector<int64_t>& v) {
@@ -429,7 +445,14 @@ void flag_pingpong(int64_t my_flag, int64_t peer_flag, int64_t peer_data, int64_
 
 void tp_ll_norm(Tensor own, std::vector<int64_t> slot, std::vector<int64_t> gslot, Tensor h, Tensor xout, Tensor w,
                 double eps, int64_t rank, int64_t rows_per_rank, int64_t rows_total, int64_t cap, bool two,
-                Tensor epoch_ctr, Tensor err, int64_t timeout_ns) {
+                Tensor epoch_ctr, Tensor err, int64_t timeout_ns, c10::optional<Tensor> ws, int64_t splits) {
+  const float* wsp = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(ws.has_value() && ws->scalar_type() == at::kFloat &&
+                    ws->numel() >= splits * rows_total * h.size(1),
+                "tp_ll_norm: split-K partials need the fp32 workspace [splits, rows, cols]");
+    wsp = ws->data_ptr<float>();
+  }
   TORCH_CHECK(timeout_ns > 0, "tp_ll_norm: timeout_ns must be positive");
   TORCH_CHECK(!two || gslot.size() == slot.size(), "tp_ll_norm: gather slot table");
   CHECK_DT(own, at::kBFloat16, "own");
@@ -449,7 +472,7 @@ void tp_ll_norm(Tensor own, std::vector<int64_t> slot, std::vector<int64_t> gslo
   std::vector<void*> sp, gp;
   for (auto p : slot) sp.push_back(reinterpret_cast<void*>(p));
   for (auto p : gslot) gp.push_back(reinterpret_cast<void*>(p));
-  kapsl::launch_tp_ll_norm(bf(own), sp.data(), two ? gp.data() : nullptr, bf(h), bf(xout),
+  kapsl::launch_tp_ll_norm(bf(own), wsp, (int)splits, sp.data(), two ? gp.data() : nullptr, bf(h), bf(xout),
                            reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (float)eps, (int)sp.size(), (int)rank,
                            (int)rows_per_rank, (int)rows_total, (int)h.size(1), ld, (int)cap, two,
                            epoch_ctr.data_ptr<int64_t>(), err.data_ptr<int>(), kapsl::gemm_num_sms(),
@@ -686,6 +709,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("tp_reduce_norm_ag", &tp_reduce_norm_ag,
         "barrier + pull peers' partial rows + residual (own rows) + RMSNorm + all-gather of the normed rows");
   m.def("flag_pingpong", &flag_pingpong, "NVLink flag round-trip latency probe (two ranks)");
+  m.def("gemm_deferred", &gemm_deferred, "plain GEMM leaving split-K partials in the workspace; returns splits");
   m.def("tp_ll_norm", &tp_ll_norm,
         "one-shot row reduction + residual + RMSNorm with flag-carrying 8-byte lines (few rows)");
   m.def("tp_ll_slot_bytes", &kapsl::tp_ll_slot_bytes);

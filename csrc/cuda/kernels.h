@@ -91,10 +91,13 @@ void launch_count_tokens(int32_t* counts, int V, const int32_t* rows, const int3
 
 int gemm_num_sms();
 // epi: 0 plain, 1 +bias, 2 +residual, 3 SwiGLU over interleaved gate/up (N % 256 == 0, C is [M, N/2]).
-void launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, void* C, int64_t ldc,
-                 bool out_f32, int M, int N, int K, int epi, const __nv_bfloat16* bias, const __nv_bfloat16* res,
-                 int64_t ldr, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st, int force_bn,
-                 int force_splits);
+// Returns the number of K splits used.  defer_splitk (plain epilogue only): when the GEMM splits K,
+// the fp32 partials stay in the workspace ([splits][M][N]) for the consumer to sum, and no reduce
+// kernel runs (C is not written); with one split C is written as usual.
+int launch_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, void* C, int64_t ldc,
+                bool out_f32, int M, int N, int K, int epi, const __nv_bfloat16* bias, const __nv_bfloat16* res,
+                int64_t ldr, float* workspace, size_t workspace_bytes, int* err, cudaStream_t st, int force_bn,
+                int force_splits, bool defer_splitk = false);
 
 // grouped (MoE expert) GEMM; mtiles = [valid 128-row tiles, expert of tile 0, ...] on the device
 void launch_grouped_gemm(const __nv_bfloat16* A, int64_t lda, const __nv_bfloat16* B, int64_t ldb, __nv_bfloat16* C,
@@ -146,10 +149,10 @@ void launch_flag_pingpong(int64_t* my_flag, int64_t* peer_flag, void* peer_data,
                           cudaStream_t st);
 // row-parallel reduction + residual + RMSNorm with flag-carrying 8-byte lines (one-shot / two-shot)
 size_t tp_ll_slot_bytes(int world, int cap, int cols, bool two);
-void launch_tp_ll_norm(const __nv_bfloat16* own, void* const* slot, void* const* gslot, __nv_bfloat16* h,
-                       __nv_bfloat16* xout, const __nv_bfloat16* w, float eps, int world, int rank, int rows_per_rank,
-                       int rows_total, int cols, int64_t ld, int cap, bool two, int64_t* epoch_ctr, int* err,
-                       int num_sms, uint64_t timeout_ns, cudaStream_t st);
+void launch_tp_ll_norm(const __nv_bfloat16* own, const float* ws, int splits, void* const* slot, void* const* gslot,
+                       __nv_bfloat16* h, __nv_bfloat16* xout, const __nv_bfloat16* w, float eps, int world, int rank,
+                       int rows_per_rank, int rows_total, int cols, int64_t ld, int cap, bool two, int64_t* epoch_ctr,
+                       int* err, int num_sms, uint64_t timeout_ns, cudaStream_t st);
 void launch_p2p_copy(void* dst, const void* src, int64_t bytes, int ctas_per_sm, cudaStream_t st);
 void* symm_alloc(size_t bytes);
 void symm_free(void* p);

@@ -438,7 +438,9 @@ __device__ __forceinline__ void add_bf16x8(float (&acc)[8], const uint4& v) {
 //    local gather slot.  Reuse: a rank reaches call e+2 after receiving every
 //    owner's normed rows of call e+1, produced after those owners read call e.
 struct TPLLArgs {
-  const bf16* own;      // this rank's partial [rows][ld]
+  const bf16* own;      // this rank's partial [rows][ld] (when splits == 0)
+  const float* ws;      // or the GEMM's fp32 split-K partials [splits][rows][cols], summed here
+  int splits;
   uint4* slot[8];       // peers' reduce slots [2][W][cap][cols / 4] (16 B = two lines = 4 values)
   uint4* gslot[8];      // two-shot: peers' gather slots [2][W * cap][cols / 4]
   bf16* h;              // residual stream (one-shot: every row; two-shot: owned rows kept current)
@@ -489,6 +491,23 @@ __device__ __forceinline__ bool ll_load(const uint4* src, uint32_t fl, uint64_t 
   return ok;
 }
 
+// 16-byte chunk c (8 columns) of this rank's partial row r: the bf16 GEMM output, or
+// the sum of the split-K partials in split order rounded to bf16 (the arithmetic of
+// the split-K reduce kernel, so every reduction variant sees the same values).
+__device__ __forceinline__ uint4 own_chunk(const TPLLArgs& a, int r, int c) {
+  if (a.splits == 0) return *reinterpret_cast<const uint4*>(a.own + (int64_t)r * a.ld + c * 8);
+  const int64_t sstride = (int64_t)a.rows_total * a.cols;
+  const float* p = a.ws + (int64_t)r * a.cols + c * 8;
+  float4 lo = reinterpret_cast<const float4*>(p)[0], hi = reinterpret_cast<const float4*>(p)[1];
+  for (int sp = 1; sp < a.splits; ++sp) {
+    const float4 l2 = reinterpret_cast<const float4*>(p + sp * sstride)[0];
+    const float4 h2 = reinterpret_cast<const float4*>(p + sp * sstride)[1];
+    lo.x += l2.x; lo.y += l2.y; lo.z += l2.z; lo.w += l2.w;
+    hi.x += h2.x; hi.y += h2.y; hi.z += h2.z; hi.w += h2.w;
+  }
+  return make_uint4(pack_bf16(lo.x, lo.y), pack_bf16(lo.z, lo.w), pack_bf16(hi.x, hi.y), pack_bf16(hi.z, hi.w));
+}
+
 template <int WORLD, bool TWO>
 __global__ void __launch_bounds__(kNormThreads) tp_ll_norm_kernel(TPLLArgs a) {
   griddep_entry();
@@ -510,9 +529,8 @@ __global__ void __launch_bounds__(kNormThreads) tp_ll_norm_kernel(TPLLArgs a) {
   for (int r = b; r < a.rows_total; r += G) {
     const int owner = TWO ? r / rpr : -1;
     if (TWO && owner == a.rank) continue;
-    const bf16* src = a.own + (int64_t)r * a.ld;
     for (int c = tid; c < chunks; c += kNormThreads) {
-      const uint4 v = *reinterpret_cast<const uint4*>(src + c * 8);
+      const uint4 v = own_chunk(a, r, c);
       if (TWO) {
         ll_store(a.slot[owner] + (((int64_t)par * WORLD + a.rank) * a.cap + (r - owner * rpr)) * lines + 2 * c, v, fl);
       } else {
@@ -547,7 +565,7 @@ __global__ void __launch_bounds__(kNormThreads) tp_ll_norm_kernel(TPLLArgs a) {
 #pragma unroll
       for (int p = 0; p < WORLD; ++p) {
         if (p == a.rank) {
-          v[p] = *reinterpret_cast<const uint4*>(a.own + base + c * 8);
+          v[p] = own_chunk(a, r, c);
         } else {
           const uint4* src = a.slot[a.rank] + (((int64_t)par * WORLD + p) * a.cap + lr) * lines + 2 * c;
           ok = ll_load(src, fl, t0, a.timeout_ns, ok, a.err, v[p]);
@@ -649,10 +667,10 @@ size_t tp_ll_slot_bytes(int world, int cap, int cols, bool two) {
   return two ? 2 * red : red;
 }
 
-void launch_tp_ll_norm(const bf16* own, void* const* slot, void* const* gslot, bf16* h, bf16* xout, const bf16* w,
-                       float eps, int world, int rank, int rows_per_rank, int rows_total, int cols, int64_t ld,
-                       int cap, bool two, int64_t* epoch_ctr, int* err, int num_sms, uint64_t timeout_ns,
-                       cudaStream_t st) {
+void launch_tp_ll_norm(const bf16* own, const float* ws, int splits, void* const* slot, void* const* gslot, bf16* h,
+                       bf16* xout, const bf16* w, float eps, int world, int rank, int rows_per_rank, int rows_total,
+                       int cols, int64_t ld, int cap, bool two, int64_t* epoch_ctr, int* err, int num_sms,
+                       uint64_t timeout_ns, cudaStream_t st) {
   if (world != 2 && world != 4 && world != 8) throw std::runtime_error("tp: LL reduction needs world size 2, 4 or 8");
   if (cols % 8 != 0 || ld % 8 != 0) throw std::runtime_error("tp: columns must be a multiple of 8");
   if (cols / 8 > kNormThreads * kNormMaxChunks) throw std::runtime_error("tp: hidden size above 8192");
@@ -660,8 +678,11 @@ void launch_tp_ll_norm(const bf16* own, void* const* slot, void* const* gslot, b
   if (two && (rows_per_rank > cap || (int64_t)rows_per_rank * world < rows_total))
     throw std::runtime_error("tp: LL two-shot rows per rank exceed the slot capacity");
   if (rows_total <= 0) return;
+  if (splits > 1 && ws == nullptr) throw std::runtime_error("tp: split-K partials without a workspace");
   TPLLArgs a{};
   a.own = own;
+  a.ws = ws;
+  a.splits = splits > 1 ? splits : 0;
   for (int i = 0; i < world; ++i) {
     a.slot[i] = reinterpret_cast<uint4*>(slot[i]);
     a.gslot[i] = two ? reinterpret_cast<uint4*>(gslot[i]) : nullptr;

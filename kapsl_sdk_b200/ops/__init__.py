@@ -173,6 +173,11 @@ def _workspace(device: torch.device, nbytes: int = 64 << 20) -> torch.Tensor:
     return w
 
 
+def workspace(device: torch.device) -> torch.Tensor:
+    """The per-device fp32 GEMM workspace (split-K partials)."""
+    return _workspace(device)
+
+
 def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, block: int = 128) -> torch.Tensor:
     """[F, d] gate and up -> [2F, d] with alternating 128-row blocks
     (gate_0, up_0, gate_1, up_1, ...), the layout the SwiGLU epilogue reads."""

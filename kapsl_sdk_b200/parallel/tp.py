@@ -267,9 +267,14 @@ class TPComm:
         if self.norm_kernel == "ll":
             ll1 = T <= min(self.ll1_rows, self.ll_cap)
             if ll1 or (T <= self.ll2_rows and rpr <= self.ll_cap):
-                ops.linear(x, w, out=own)
+                if isinstance(w, torch.Tensor):  # split-K partials are summed inside the line kernel
+                    ws = ops.workspace(x.device)
+                    splits = cuda_ops().gemm_deferred(x, w, own, ws, err)
+                else:
+                    ws, splits = None, 1
+                    ops.linear(x, w, out=own)
                 cuda_ops().tp_ll_norm(own, b["ll"], b["llg"], h, self.xnorm_buf[:T], norm_w, float(eps), self.rank,
-                                      rpr, T, self.ll_cap, not ll1, self.epoch, err, self.timeout_ns)
+                                      rpr, T, self.ll_cap, not ll1, self.epoch, err, self.timeout_ns, ws, int(splits))
                 return self.xnorm_buf[:T]
             ops.linear(x, w, out=self.partial_buf[:T])
             cuda_ops().tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,

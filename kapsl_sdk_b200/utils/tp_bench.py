@@ -169,7 +169,7 @@ def main():
             own = tp.own_buf[:M]
             own.copy_(ops.linear(x, w))
             fn = lambda: c.tp_ll_norm(own, b["ll"], b["llg"], h, tp.xnorm_buf[:M], nw, 1e-6, rank, rpr, M, tp.ll_cap,
-                                      two, tp.epoch, err, tp.timeout_ns)
+                                      two, tp.epoch, err, tp.timeout_ns, None, 1)
         elif mode == "norm_only":
             fn = lambda: c.tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, nw, 1e-6, rank, rpr, M, NO,
                                              tp.epoch, err, tp.timeout_ns)
