@@ -506,7 +506,8 @@ PYBIND11_MODULE(_native, m) {
         return responses ? shm::Ring<shm::ShmResponse>(r.base() + shm::RESP_RING_OFFSET, shm::RING_CAPACITY_ARG, false).len()
                          : shm::Ring<shm::ShmRequest>(r.base() + shm::REQ_RING_OFFSET, shm::RING_CAPACITY_ARG, false).len();
       })
-      .def("read_error", [](const shm::Region& r, uint64_t off) { return shm::read_error(r, off); });
+      .def("read_error", [](const shm::Region& r, uint64_t off) { return shm::read_error(r, off); })
+      .def("mark_result_read", [](shm::Region& r, uint64_t off) { shm::mark_result_read(r, off); });
 
   py::class_<shm::TieredAllocator>(m, "TieredAllocator")
       .def(py::init<uint64_t, uint64_t, std::vector<uint64_t>, std::vector<uint32_t>, double>(), py::arg("base"),

@@ -162,6 +162,7 @@ void WireServer::attach_shm(const std::string& shm_name) {
   // results go to the upper half of the tensor pool; clients write inputs into the lower half
   const uint64_t half = h.max_tensor_size / 2;
   hybrid_alloc_ = std::make_unique<shm::TieredAllocator>(h.tensor_pool_offset + half, h.max_tensor_size - half);
+  hybrid_alloc_->set_guard(hybrid_region_->base());  // a result slot is reused only once its client read it
 }
 
 void WireServer::start() {
@@ -377,8 +378,9 @@ bool WireServer::handle_frame(int fd, uint32_t model_id, uint32_t op, const std:
     }
     if (!err.empty()) return send_frame(fd, STATUS_ERR, err);
     const uint64_t need = shm::tensor_bytes(out);
-    auto slot = hybrid_alloc_->try_allocate(need, /*force=*/true);
+    auto slot = hybrid_alloc_->try_allocate(need + shm::kResultGuard, /*force=*/true);
     if (!slot) return send_frame(fd, STATUS_ERR, "SHM result pool exhausted (" + std::to_string(need) + " bytes)");
+    *slot += shm::kResultGuard;  // the guard word sits in front of the tensor
     shm::write_tensor(*hybrid_region_, *slot, out);
     HybridResponse resp;
     resp.meta.request_id = hr.meta.request_id;
@@ -409,6 +411,7 @@ ShmServer::ShmServer(py::object handler, const std::string& name, size_t size, i
   for (auto& [id, b] : shm::ModelPools::plan(bytes, {model_weights.begin(), model_weights.end()}))
     specs.push_back(shm::ModelPoolSpec{id, b, {}, {}});
   alloc_ = std::make_unique<shm::ModelPools>(result_base_, bytes, specs);
+  alloc_->set_guard(region_->base());  // a result slot is reused only once its client read it
 }
 
 ShmServer::~ShmServer() {
@@ -487,22 +490,22 @@ void ShmServer::process(const shm::ShmRequest& req) {
   }
   if (err.empty()) {
     const uint64_t need = shm::tensor_bytes(out);
-    auto slot = alloc_->try_allocate(req.meta.model_id, need, /*force=*/true);
+    auto slot = alloc_->try_allocate(req.meta.model_id, need + shm::kResultGuard, /*force=*/true);
     if (!slot) {
       exhausted_.fetch_add(1);
       err = "SHM tensor pool exhausted (required=" + std::to_string(need) + " bytes)";
     } else {
-      shm::write_tensor(*region_, *slot, out);
-      resp.result_offset = *slot;
+      shm::write_tensor(*region_, *slot + shm::kResultGuard, out);
+      resp.result_offset = *slot + shm::kResultGuard;
       resp.result_size = need;
     }
   }
   if (!err.empty()) {
     resp.meta.status = 1;
-    auto slot = alloc_->try_allocate(req.meta.model_id, 8 + err.size(), /*force=*/true);
+    auto slot = alloc_->try_allocate(req.meta.model_id, 8 + err.size() + shm::kResultGuard, /*force=*/true);
     if (slot) {
-      shm::write_error(*region_, *slot, err);
-      resp.error_offset = *slot;
+      shm::write_error(*region_, *slot + shm::kResultGuard, err);
+      resp.error_offset = *slot + shm::kResultGuard;
     }
   }
   resp.meta.latency_ns =

@@ -119,15 +119,18 @@ std::optional<uint64_t> SlotAllocator::try_allocate(uint64_t size, bool force) {
   for (uint64_t i = 0; i < n_; ++i) {
     const uint64_t s = (next_ + i) % n_;
     auto& l = leases_[s];
-    if (l.has_value() && std::chrono::duration<double>(now - *l).count() < ttl_s_) {
-      if (oldest == n_ || *l < *leases_[oldest]) oldest = s;
+    const bool live = l.has_value() && std::chrono::duration<double>(now - *l).count() < ttl_s_;
+    // a live lease on a guarded slot ends as soon as its reader has marked it read
+    if (live && !(guard_ && unread_word(s).load(std::memory_order_acquire) == 0)) {
+      if (!guard_ && (oldest == n_ || *l < *leases_[oldest])) oldest = s;
       continue;
     }
     l = now;
     next_ = (s + 1) % n_;
+    if (guard_) unread_word(s).store(1, std::memory_order_release);
     return base_ + s * slot_;
   }
-  if (force && oldest < n_) {
+  if (force && oldest < n_) {  // never with a guard: an unread result is not overwritten
     leases_[oldest] = now;
     next_ = (oldest + 1) % n_;
     return base_ + oldest * slot_;
@@ -382,6 +385,11 @@ bool SharedLeases::release(uint64_t offset) {
 
 // ----------------------------------------------------------------- tensors
 uint64_t tensor_bytes(const wire::Packet& p) { return sizeof(TensorHeader) + p.data.size(); }
+
+void mark_result_read(Region& r, uint64_t off) {
+  if (off < kResultGuard || (off - kResultGuard) % 8 != 0 || !r.in_bounds(off - kResultGuard, 8)) return;
+  reinterpret_cast<std::atomic<uint64_t>*>(r.base() + off - kResultGuard)->store(0, std::memory_order_release);
+}
 
 void write_tensor(Region& r, uint64_t off, const wire::Packet& p) {
   if (p.shape.size() > 8) throw std::invalid_argument("at most 8 dimensions fit a TensorHeader");

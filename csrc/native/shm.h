@@ -211,12 +211,20 @@ class Ring {
   size_t cap_;
 };
 
+// Result slots handed to clients start with a kResultGuard-byte header whose first
+// 64-bit word is 1 while the result is unread; the client stores 0 after copying
+// it out (mark_result_read), and the tensor itself starts kResultGuard bytes in.
+constexpr uint64_t kResultGuard = 64;
+
 // Round-robin slot allocator with TTL leases (expired leases are reclaimed).
 class SlotAllocator {
  public:
   SlotAllocator(uint64_t base, uint64_t slot_size, uint64_t num_slots, double ttl_s = 30.0);
-  // force: when every slot is leased, take over the one leased longest ago
+  // force: when every slot is leased, take over the one leased longest ago.  With a
+  // guard set, a slot whose unread word is 0 is free again before its lease expires,
+  // taking a slot sets the word to 1, and force never takes over an unread result.
   std::optional<uint64_t> try_allocate(uint64_t size, bool force = false);
+  void set_guard(uint8_t* region_base) { guard_ = region_base; }
   bool release(uint64_t offset);
   size_t in_use() const;
   double oldest_lease_ms() const;
@@ -231,6 +239,10 @@ class SlotAllocator {
   mutable std::mutex mu_;
   std::vector<std::optional<clock::time_point>> leases_;
   uint64_t next_ = 0;
+  uint8_t* guard_ = nullptr;
+  std::atomic<uint64_t>& unread_word(uint64_t s) const {
+    return *reinterpret_cast<std::atomic<uint64_t>*>(guard_ + base_ + s * slot_);
+  }
 };
 
 // Size classes 256 KiB, 1 MiB, 4 MiB, 16 MiB, 64 MiB (smallest fitting class
@@ -247,6 +259,9 @@ class TieredAllocator {
   uint64_t largest_slot() const;
   std::string layout_summary() const;
   const std::vector<std::unique_ptr<SlotAllocator>>& classes() const { return classes_; }
+  void set_guard(uint8_t* region_base) {
+    for (auto& c : classes_) c->set_guard(region_base);
+  }
 
  private:
   std::vector<std::unique_ptr<SlotAllocator>> classes_;
@@ -284,6 +299,10 @@ class ModelPools {
   // (base, end) of a model's pool, or of the shared pool for model_id == UINT32_MAX
   std::pair<uint64_t, uint64_t> range(uint32_t model_id) const;
   std::string layout_summary() const;
+  void set_guard(uint8_t* region_base) {
+    for (auto& [id, p] : pools_) p.alloc->set_guard(region_base);
+    shared_.alloc->set_guard(region_base);
+  }
 
   // Pool sizes for models weighted by expected concurrency: a reserve of
   // reserve_pct percent (at least min_pool bytes) stays shared, the rest is
@@ -327,6 +346,8 @@ class SharedLeases {
 void write_tensor(Region& r, uint64_t off, const wire::Packet& p);
 wire::Packet read_tensor(const Region& r, uint64_t off);
 void write_error(Region& r, uint64_t off, const std::string& msg);
+// Client side of the result guard: the result (or error) at `off` has been copied out.
+void mark_result_read(Region& r, uint64_t off);
 std::string read_error(const Region& r, uint64_t off);
 uint64_t tensor_bytes(const wire::Packet& p);
 

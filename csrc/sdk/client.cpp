@@ -462,9 +462,11 @@ class KapslShmClient {
             } else {
               if (r->meta.status != 0) {
                 err = r->error_offset ? shm::read_error(*region_, r->error_offset) : "Unknown error";
+                if (r->error_offset) shm::mark_result_read(*region_, r->error_offset);
               } else {
                 wire::Packet out = shm::read_tensor(*region_, r->result_offset);
                 result = std::move(out.data);
+                shm::mark_result_read(*region_, r->result_offset);  // the server may reuse the slot now
               }
               break;
             }
@@ -542,7 +544,9 @@ class KapslHybridClient {
     wire::HybridResponse r;
     try {
       r = wire::decode_hybrid_response(f.payload);
-      return py::bytes(shm::read_tensor(*region_, r.shm_offset).data);
+      std::string data = shm::read_tensor(*region_, r.shm_offset).data;
+      shm::mark_result_read(*region_, r.shm_offset);  // the server may reuse the slot now
+      return py::bytes(data);
     } catch (const std::exception& e) {
       raise_py(PyExc_RuntimeError, e.what());
     }

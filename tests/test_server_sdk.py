@@ -226,6 +226,59 @@ def test_shm_rejects_out_of_bounds_offsets():
         srv.stop()
 
 
+def test_shm_unread_results_are_not_overwritten():
+    """More responses than result slots while no client reads: every result the
+    server did write keeps its own bytes (an unread slot is never taken over; the
+    surplus requests get errors), and marking results read frees their slots."""
+    from kapsl_sdk_b200._ext import native
+
+    nat = native()
+    name = f"kapsl-guard-{uuid.uuid4().hex[:8]}"
+    srv = nat.ShmServer(__import__("kapsl_sdk_b200.server.dispatch", fromlist=["x"]).Dispatcher(
+        lambda i: EchoTarget()), name, 16 << 20, 1)
+    srv.start()
+    try:
+        region = nat.ShmRegion.open(name)
+        base = region.header()["tensor_pool_offset"]
+        slots = sum(int(c.split("x")[1]) for c in srv.pool_layout().split(": ")[1].split(","))
+        n = slots + 6
+
+        def send(i):
+            payload = struct.pack("<4i", i, 2 * i, 3 * i, 4 * i)
+            region.write_tensor(base + i * 4096, [4], "int32", payload)
+            assert region.push_request(i + 1, 0, 0, base + i * 4096, 80 + 16)
+            return payload
+
+        payloads = {}
+        got = {}
+        for i in range(n):
+            payloads[i + 1] = send(i)
+            t0 = time.time()
+            while i + 1 not in got and time.time() - t0 < 5:  # one at a time, in order
+                r = region.pop_response()
+                if r is None:
+                    time.sleep(0.001)
+                    continue
+                got[r[0]] = r
+        assert len(got) == n
+        ok = {rid: r for rid, r in got.items() if r[1] == 0}
+        assert len(ok) == slots and sorted(ok) == list(range(1, slots + 1))
+        assert all(got[rid][1] != 0 for rid in range(slots + 1, n + 1))  # pool exhausted, nothing overwritten
+        for rid, r in ok.items():
+            assert region.read_tensor(r[2])[2] == payloads[rid]
+            region.mark_result_read(r[2])
+        payloads[n + 1] = send(n)
+        t0 = time.time()
+        r = None
+        while r is None and time.time() - t0 < 5:
+            r = region.pop_response()
+            time.sleep(0.001)
+        assert r is not None and r[0] == n + 1 and r[1] == 0
+        assert region.read_tensor(r[2])[2] == payloads[n + 1]
+    finally:
+        srv.stop()
+
+
 def test_model_pools_allocator():
     """Per-model sub-pools with a shared overflow pool: model pool first, spill
     to the shared pool, unknown ids to the shared pool, release by offset range."""
