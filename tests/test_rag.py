@@ -251,7 +251,13 @@ def test_hnsw_saved_graph_rebuilt_after_same_second_reupsert(tmp_path):
     s1 = rag.SqliteVectorStore(db, index="hnsw", exact_below=10, index_dir=idx)
     s1.upsert([rag.EmbeddedChunk(f"c{i}", "t", "ws", "s", "d", i, "x", X[i].tolist()) for i in range(600)])
     s1.query(rag.VectorQuery(X[0].tolist(), 3, "t", "ws"))  # builds and saves the graph
+    saved1 = [f for f in os.listdir(idx) if f.endswith(".hnsw")]
+    assert len(saved1) == 1
     far = -X[0] * 5.0
     s1.upsert([rag.EmbeddedChunk("c599", "t", "ws", "s", "d", 599, "x", far.tolist())])
     s2 = rag.SqliteVectorStore(db, index="hnsw", exact_below=10, index_dir=idx)
-    assert s2.query(rag.VectorQuery(far.tolist(), 1, "t", "ws"))[0].chunk.id == "c599"
+    assert s2.query(rag.VectorQuery(X[5].tolist(), 3, "t", "ws"))[0].chunk.id == "c5"
+    # the stale graph was not loaded: a graph under the new key replaced it (the
+    # search itself is approximate, so the file name is the deterministic check)
+    saved2 = [f for f in os.listdir(idx) if f.endswith(".hnsw")]
+    assert len(saved2) == 1 and saved2 != saved1
