@@ -35,6 +35,10 @@ namespace gemm {
 constexpr int BM = 128;
 constexpr int BK = 64;
 constexpr int kThreads = 192;
+// scatter-epilogue staging per epilogue warp: 32 rows x 64 bf16 columns, rows padded
+// to 144 bytes so the per-lane row writes and the row-piece reads spread over banks
+constexpr int kScatterRow = 144;
+constexpr int kScatterStage = 32 * kScatterRow;
 
 using namespace tc;
 
@@ -664,6 +668,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             if (nvalid > 0) store_row32<OUT_F32>(ep.out, ep.ldc, row, out_c0 + c, nvalid, v);
           }
         }
+      } else if (EPI == 5) {
+        // Tensor-parallel scatter: each 64-column slab of this warp's 32 rows goes
+        // through shared memory (one 128-byte row per lane), then 8 rounds of 4 rows
+        // x 8 lanes store 128-byte contiguous row pieces into the owner rank's
+        // receive slot over NVLink (a lane-per-row store would send 16-byte pieces).
+        uint8_t* stg = smem + (size_t)STAGES * STAGE_BYTES + (size_t)quad * kScatterStage;
+        const int row0 = mt * 256 + (int)rank * 128 + quad * 32;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 64) {
+          float v0[32], v1[32];
+          tmem_ld32(tbase + c, v0);
+          tmem_ld32(tbase + c + 32, v1);
+          uint4* mine = reinterpret_cast<uint4*>(stg + lane * kScatterRow);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            mine[q] = make_uint4(pack_bf16(v0[8 * q], v0[8 * q + 1]), pack_bf16(v0[8 * q + 2], v0[8 * q + 3]),
+                                 pack_bf16(v0[8 * q + 4], v0[8 * q + 5]), pack_bf16(v0[8 * q + 6], v0[8 * q + 7]));
+            mine[4 + q] = make_uint4(pack_bf16(v1[8 * q], v1[8 * q + 1]), pack_bf16(v1[8 * q + 2], v1[8 * q + 3]),
+                                     pack_bf16(v1[8 * q + 4], v1[8 * q + 5]), pack_bf16(v1[8 * q + 6], v1[8 * q + 7]));
+          }
+          __syncwarp();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const int rr = 4 * k + (lane >> 3), seg = lane & 7;
+            const int grow = row0 + rr, gcol = nt * BN + c + seg * 8;
+            if (grow < M && gcol < N)
+              *reinterpret_cast<uint4*>(scatter_dst(ep, grow, gcol)) =
+                  *reinterpret_cast<const uint4*>(stg + rr * kScatterRow + seg * 16);
+          }
+          __syncwarp();
+        }
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 32) {
@@ -683,10 +718,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
               for (int i = 0; i < 32; ++i) v[i] += rr[i];
             }
-            if (EPI == 5)
-              store_row32<false>(scatter_dst(ep, row, col), 0, 0, 0, nvalid, v);
-            else
-              store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
+            store_row32<OUT_F32>(ep.out, ep.ldc, row, col, nvalid, v);
           }
         }
       }
@@ -695,6 +727,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_remote(acc ? leader_tempty1 : leader_tempty0);
     }
   }
+  if (EPI == 5) __threadfence_system();  // remote rows are performed before the grid completes
   tc_fence_before();
   __syncthreads();
   cluster_sync_all();  // no CTA leaves while its peer may still signal it
@@ -703,14 +736,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 }
 
 // Stages of the 2-SM kernel for a tile width: the most that fit next to the 1 KiB
-// alignment pad under the 227 KiB dynamic shared-memory limit.
-constexpr int gemm2_stages(int bn) { return (232448 - 1024 - 512) / ((128 + bn / 2) * BK * 2); }
+// alignment pad (and, for the scatter epilogue, its staging) under the 227 KiB
+// dynamic shared-memory limit.
+constexpr int gemm2_stages(int bn, int epi = 0) {
+  return (232448 - 1024 - 512 - (epi == 5 ? 4 * kScatterStage : 0)) / ((128 + bn / 2) * BK * 2);
+}
 
 template <int BN, int STAGES, int EPI, bool F32>
 void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& ep, int grid,
                 int* err, cudaStream_t st) {
   auto kern = gemm2sm_kernel<BN, STAGES, EPI, F32>;
-  constexpr size_t smem = (size_t)STAGES * (128 + BN / 2) * BK * 2 + 1024;
+  constexpr size_t smem = (size_t)STAGES * (128 + BN / 2) * BK * 2 + 1024 + (EPI == 5 ? 4 * kScatterStage : 0);
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
   launch_k(kern, grid, kThreads, smem, st, ta, tb, M, N, K, ep, err);
@@ -823,7 +859,7 @@ void launch_gemm_scatter(const bf16* A, int64_t lda, const bf16* B, int64_t ldb,
   if (M >= 256 && units2 * 4 >= (sms / 2) * 3) {
     CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, 128, BK);
     CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, 128, BK);
-    launch_2sm<256, gemm2_stages(256), 5, false>(ta, tb, M, N, K, ep, 2 * std::min(units2, sms / 2), err, st);
+    launch_2sm<256, gemm2_stages(256, 5), 5, false>(ta, tb, M, N, K, ep, 2 * std::min(units2, sms / 2), err, st);
     return;
   }
   const int m_tiles = (M + BM - 1) / BM;

@@ -74,6 +74,12 @@ class TPComm:
         self.ll2_rows = int(os.environ.get("KAPSL_TP_LL2_ROWS", {2: 512, 4: 512, 8: 512}.get(world_size, 0)))
         # "ll": flag-carrying lines for few rows, pull above (default); "pull": barrier + pull kernel only
         self.norm_kernel = os.environ.get("KAPSL_TP_NORM", "ll")
+        # above the line-kernel sizes: "scatter" (the GEMM epilogue stores each row into its
+        # owner's receive slot over NVLink while the GEMM runs; the reduction then reads local
+        # memory) or "pull" (the reduction pulls the partial rows from the peers)
+        self.large_kernel = os.environ.get("KAPSL_TP_LARGE", "scatter")
+        self._sms = torch.cuda.get_device_properties(self.device).multi_processor_count if \
+            self.device.type == "cuda" else 148
         self.bufs = None
         self.ep_buf = None
         if mode != "nccl" and world_size > 1:
@@ -276,11 +282,28 @@ class TPComm:
                 cuda_ops().tp_ll_norm(own, b["ll"], b["llg"], h, self.xnorm_buf[:T], norm_w, float(eps), self.rank,
                                       rpr, T, self.ll_cap, not ll1, self.epoch, err, self.timeout_ns, ws, int(splits))
                 return self.xnorm_buf[:T]
-            ops.linear(x, w, out=self.partial_buf[:T])
-            cuda_ops().tp_reduce_norm_ag(b["recv"], b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,
+            if self._scatter_ok(x, w):
+                # the epilogue pushed every row into its owner's slot [my rank]; the reduction
+                # reads slot p of this rank where the pull variant would read peer p's partial
+                cuda_ops().gemm_scatter(x, w, b["recv"], self.rank, rpr, self.hidden, err)
+                my, r0, row_bytes = b["recv"][self.rank], self.rank * rpr, self.hidden * 2
+                parts = [my + (p * rpr - r0) * row_bytes for p in range(self.world_size)]
+            else:
+                ops.linear(x, w, out=self.partial_buf[:T])
+                parts = b["recv"]
+            cuda_ops().tp_reduce_norm_ag(parts, b["xnorm"], b["flags"], h, norm_w, float(eps), self.rank, rpr, T,
                                          self.hidden, self.epoch, err, self.timeout_ns)
             return self.xnorm_buf[:T]
         raise ValueError(f"unknown tensor-parallel norm kernel {self.norm_kernel!r}")
+
+    def _scatter_ok(self, x: torch.Tensor, w) -> bool:
+        """The scatter GEMM runs its coalesced epilogue in the 2-SM kernel, chosen when
+        256 x 256 tiles fill at least 3/4 of the CTA pairs (the GEMM's own rule)."""
+        if self.large_kernel != "scatter" or not isinstance(w, torch.Tensor) or self.hidden % 8:
+            return False
+        T, N = x.shape[0], w.shape[0]
+        units = -(-T // 256) * -(-N // 256)
+        return T >= 256 and units * 4 >= (self._sms // 2) * 3
 
     def replicated_residual(self, T: int) -> bool:
         """Whether the fused row reduction of a ``T``-row batch keeps every row of the

@@ -6,7 +6,8 @@ Modes (``TP_BENCH_MODES``, comma-separated): ``ll`` the model's layer boundary
 (GEMM + reduction + residual + RMSNorm, the kernel picked by row count),
 ``ll1`` / ``ll2`` forced flag-carrying-line one-shot / two-shot, ``ll_only1``
 / ``ll_only2`` those kernels alone, ``norm`` / ``norm_only`` the barrier + pull kernel,
-``fused`` the pull reduction without the norm, ``nccl`` / ``nccl_norm`` GEMM +
+``pull_large`` the default selection but with the pull kernel instead of
+the scatter GEMM above the line-kernel sizes, ``fused`` the pull reduction without the norm, ``nccl`` / ``nccl_norm`` GEMM +
 NCCL all-reduce (+ add + RMSNorm), ``gemm_only``.  ``tp_bench ping`` measures
 the NVLink flag round trip between ranks 0 and 1.
 
@@ -140,7 +141,7 @@ def main():
 
     c = cuda_ops()
     nw = torch.ones(NO, device=dev, dtype=torch.bfloat16)
-    modes = os.environ.get("TP_BENCH_MODES", "ll,ll1,ll2,ll_only1,ll_only2,norm,norm_only,nccl,"
+    modes = os.environ.get("TP_BENCH_MODES", "ll,ll1,ll2,ll_only1,ll_only2,pull_large,norm,norm_only,nccl,"
                                              "nccl_norm,gemm_only").split(",")
     for mode in modes:
         fusedbuf = mode not in ("nccl", "nccl_norm", "gemm_only")
@@ -158,11 +159,13 @@ def main():
             tp._setup_symmetric(M, NO)
         if mode in ("norm", "norm_only"):
             tp.norm_kernel = "pull"
+        if mode == "pull_large":  # the layer boundary with the pull kernel above the line-kernel sizes
+            tp.large_kernel = "pull"
         h = tp.residual_stream(M) if fusedbuf else torch.zeros(M, NO, device=dev, dtype=torch.bfloat16)
         rpr = (M + world - 1) // world
         err = ops.error_buffer(dev)
         b = tp.bufs
-        if mode in ("norm", "ll", "ll1", "ll2"):  # GEMM + reduce + residual + norm
+        if mode in ("norm", "ll", "ll1", "ll2", "pull_large"):  # GEMM + reduce + residual + norm
             fn = lambda: tp.row_parallel_norm(x, w, h, nw, 1e-6)
         elif mode in ("ll_only1", "ll_only2"):
             two = mode == "ll_only2"

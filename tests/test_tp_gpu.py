@@ -77,6 +77,32 @@ for mode in ("fused", "nccl"):
             xs_by[var] = xn.clone()
             tp.close()
         out["norm_bitwise"] = all(torch.equal(xs_by["pull"], xs_by[v]) for v in ("ll1", "ll2"))
+        # large batches: the scatter GEMM (rows pushed to their owners from the epilogue,
+        # local reduction) against the pull reduction, bit for bit, and against fp32
+        T2, K2, N2 = 2048, 512, 2048
+        x2 = torch.randn(T2, K2 * world, device=dev, dtype=torch.bfloat16)
+        w2 = torch.randn(N2, K2 * world, device=dev, dtype=torch.bfloat16) / 40
+        h2 = torch.randn(T2, N2, device=dev, dtype=torch.bfloat16)
+        nw2 = (torch.rand(N2, device=dev) + 0.5).to(torch.bfloat16)
+        ref2 = (h2.float() + x2.float() @ w2.float().T).to(torch.bfloat16).float()
+        xref2 = ref2 * torch.rsqrt(ref2.pow(2).mean(-1, keepdim=True) + 1e-6) * nw2.float()
+        xs2 = x2[:, rank * K2:(rank + 1) * K2].contiguous()
+        ws2 = w2[:, rank * K2:(rank + 1) * K2].contiguous()
+        big = {}
+        for var in ("pull", "scatter"):
+            tp = TPComm(world, rank, dev, "fused", max_tokens=T2, hidden=N2)
+            tp.large_kernel = var
+            hh = tp.residual_stream(T2)
+            for _ in range(2):
+                hh.copy_(h2)
+                xn = tp.row_parallel_norm(xs2, ws2, hh, nw2, 1e-6)
+            torch.cuda.synchronize()
+            out["large_used_" + var] = tp._scatter_ok(xs2, ws2)
+            out["large_x_" + var] = float((xn.float() - xref2).abs().max())
+            out["large_err_" + var] = ops.check_errors(dev)
+            big[var] = xn.clone()
+            tp.close()
+        out["large_bitwise"] = bool(torch.equal(big["pull"], big["scatter"]))
 # 2) a small model: TP=world greedy tokens vs TP=1 on rank 0
 # 12 query heads over 2 KV heads: at 8 ranks each KV group of 6 is padded to 8 query heads
 cfg = ModelConfig(name="s", arch="qwen2", vocab_size=1024, hidden_size=512, intermediate_size=1024, num_layers=2,
@@ -157,6 +183,9 @@ def test_tensor_and_expert_parallel():
                if not (r["norm_err_" + v] == 0 and r["norm_h_" + v] < 0.05 and r["norm_x_" + v] < 0.05)]
         assert not bad, (bad, r)
         assert r["norm_bitwise"], r
+        assert r["large_used_scatter"] and not r["large_used_pull"], r
+        assert r["large_err_pull"] == 0 and r["large_err_scatter"] == 0, r
+        assert r["large_x_pull"] < 0.05 and r["large_x_scatter"] < 0.05 and r["large_bitwise"], r
     for key in ("tp_tokens", "ep_tokens", "nccl_tokens"):
         assert all(r[key] == res[0][key] for r in res)  # ranks stay in lock step
     # greedy tokens: the reductions round differently (NCCL sums bf16 partials in its own
