@@ -19,9 +19,6 @@
 //
 // Operand tiles are loaded per CTA (each CTA reads its own tiles from local
 // HBM); EPI 5 stores rows into peer GPUs' receive buffers (tensor parallel).
-#include <cstdlib>
-#include <mutex>
-
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -64,53 +61,12 @@ struct EpiArgs {
   // Grouped (MoE) mode: [0] = number of valid 128-row M tiles, [1 + i] = the
   // expert (row block of B, N rows each) that M tile i multiplies with.
   const int* group_mtiles;
-  // Split-K finished in the kernel (EPI 4 with tile_ctr set): per (tile, 32-row
-  // quarter) arrival counters; the last split to store its partial sums all of
-  // them in split order and applies epilogue fix_epi (0-3) into out / ldc.
-  int* tile_ctr;
-  int fix_epi;
-  int fix_f32;
 };
 
 __device__ __forceinline__ __nv_bfloat16* scatter_dst(const EpiArgs& ep, int row, int col) {
   const int owner = row / ep.rows_per_rank;
   const int local = row - owner * ep.rows_per_rank;
   return ep.peers[owner] + ((int64_t)ep.my_rank * ep.rows_per_rank + local) * ep.ldc + col;
-}
-
-// 32 consecutive fp32 values at off of every split's partial, summed in split order
-// (split 0 first, as the separate reduce kernel does); L2 reads, since the other
-// splits' partials were written by other SMs during this kernel.
-__device__ __forceinline__ void sum_splits32(const float* partial, int64_t sstride, int splits, int64_t off,
-                                             int nvalid, float (&v)[32]) {
-  if (nvalid >= 32) {
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float4 q = __ldcg(reinterpret_cast<const float4*>(partial + off) + i);
-      v[4 * i] = q.x;
-      v[4 * i + 1] = q.y;
-      v[4 * i + 2] = q.z;
-      v[4 * i + 3] = q.w;
-    }
-    for (int sp = 1; sp < splits; ++sp) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float4 q = __ldcg(reinterpret_cast<const float4*>(partial + sp * sstride + off) + i);
-        v[4 * i] += q.x;
-        v[4 * i + 1] += q.y;
-        v[4 * i + 2] += q.z;
-        v[4 * i + 3] += q.w;
-      }
-    }
-  } else {
-#pragma unroll
-    for (int i = 0; i < 32; ++i) v[i] = i < nvalid ? __ldcg(partial + off + i) : 0.f;
-    for (int sp = 1; sp < splits; ++sp) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i)
-        if (i < nvalid) v[i] += __ldcg(partial + sp * sstride + off + i);
-    }
-  }
 }
 
 // Store 32 consecutive columns (c0..c0+31) of one row.
@@ -166,55 +122,6 @@ __device__ __forceinline__ void load_bf16x32(const bf16* src, int nvalid, float 
 // EPI: 0 plain, 1 bias, 2 residual, 3 swiglu (interleaved), 4 split-K partial (fp32, raw)
 // GROUPED: A rows are expert-sorted segments padded to BM; M tile i uses the B
 // rows of expert ep.group_mtiles[1 + i] (B holds the experts stacked, N rows each).
-// The last split of a (tile, 32-row quarter) finishes row `row`: sum of the split
-// partials + the real epilogue, stored like the separate reduce kernel would.
-template <int BN>
-__device__ void splitk_fixup_row(const EpiArgs& ep, int splits, int M, int N, int row, int nt) {
-  const int64_t sstride = (int64_t)M * N;
-  if (ep.fix_epi == 3) {
-    constexpr int HALF = BN / 2;
-#pragma unroll 1
-    for (int c = 0; c < HALF; c += 32) {
-      const int out_c0 = nt * HALF + c;
-      const int nvalid = min(32, N / 2 - out_c0);
-      if (nvalid <= 0) break;
-      float g[32], u[32];
-      sum_splits32(ep.partial, sstride, splits, (int64_t)row * N + nt * BN + c, nvalid, g);
-      sum_splits32(ep.partial, sstride, splits, (int64_t)row * N + nt * BN + HALF + c, nvalid, u);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) u[i] = silu(g[i]) * u[i];
-      if (ep.fix_f32)
-        store_row32<true>(ep.out, ep.ldc, row, out_c0, nvalid, u);
-      else
-        store_row32<false>(ep.out, ep.ldc, row, out_c0, nvalid, u);
-    }
-    return;
-  }
-#pragma unroll 1
-  for (int c = 0; c < BN; c += 32) {
-    const int col = nt * BN + c;
-    const int nvalid = min(32, N - col);
-    if (nvalid <= 0) break;
-    float v[32];
-    sum_splits32(ep.partial, sstride, splits, (int64_t)row * N + col, nvalid, v);
-    if (ep.fix_epi == 1) {
-      float bb[32];
-      load_bf16x32(ep.bias + col, nvalid, bb);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += bb[i];
-    } else if (ep.fix_epi == 2) {
-      float rr[32];
-      load_bf16x32(ep.res + (int64_t)row * ep.ldr + col, nvalid, rr);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] += rr[i];
-    }
-    if (ep.fix_f32)
-      store_row32<true>(ep.out, ep.ldc, row, col, nvalid, v);
-    else
-      store_row32<false>(ep.out, ep.ldc, row, col, nvalid, v);
-  }
-}
-
 template <int BN, int STAGES, int EPI, bool OUT_F32, bool GROUPED = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, int M,
@@ -423,23 +330,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
-      if (EPI == 4 && !GROUPED && ep.tile_ctr != nullptr) {
-        // split-K in the kernel: this warp's 32 partial rows are out; the last split
-        // of this (tile, quarter) to arrive sums every split and applies the epilogue
-        __threadfence();
-        __syncwarp();
-        int last = 0;
-        if (lane == 0) {
-          int* ctr = ep.tile_ctr + ((int64_t)(mt * n_tiles + nt) * 4 + quad);
-          last = atomicAdd(ctr, 1) == splits - 1;
-          if (last) *ctr = 0;  // ready for the next launch: every split of this quarter has arrived
-        }
-        last = __shfl_sync(0xffffffffu, last, 0);
-        if (last) {
-          __threadfence();
-          if (row < M) splitk_fixup_row<BN>(ep, splits, M, N, row, nt);
-        }
-      }
     }
   }
   tc_fence_before();
@@ -735,12 +625,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
 }
 
-// Stages of the 2-SM kernel for a tile width: the most that fit next to the 1 KiB
-// alignment pad (and, for the scatter epilogue, its staging) under the 227 KiB
-// dynamic shared-memory limit.
-constexpr int gemm2_stages(int bn, int epi = 0) {
+// Stages of the 2-SM kernel for a tile width: six, or fewer when six do not fit next
+// to the 1 KiB alignment pad (and the scatter epilogue's staging) under the 227 KiB
+// dynamic shared-memory limit.  The deepest rings that fit (7-9 stages) measured no
+// faster: the mainloop is not bound by operand bytes in flight.
+constexpr int gemm2_fit(int bn, int epi) {
   return (232448 - 1024 - 512 - (epi == 5 ? 4 * kScatterStage : 0)) / ((128 + bn / 2) * BK * 2);
 }
+constexpr int gemm2_stages(int bn, int epi = 0) { return gemm2_fit(bn, epi) < 6 ? gemm2_fit(bn, epi) : 6; }
 
 template <int BN, int STAGES, int EPI, bool F32>
 void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& ep, int grid,
@@ -875,29 +767,6 @@ void launch_gemm_scatter(const bf16* A, int64_t lda, const bf16* B, int64_t ldb,
 }
 
 // Chooses tile width and split-K so that the grid covers the SMs.
-// Per-device arrival counters for split-K finished in the GEMM kernel (zeroed once;
-// every launch leaves them zero).  Not allocated while the stream is being
-// captured: that launch falls back to the separate reduce kernel.
-static constexpr int kSplitCounters = 1 << 16;
-static int* splitk_counters(cudaStream_t st) {
-  static int* ctr[64] = {nullptr};
-  static std::mutex mu;
-  int dev;
-  KAPSL_CHECK_CUDA(cudaGetDevice(&dev));
-  if (dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(mu);
-  if (ctr[dev] == nullptr) {
-    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
-    KAPSL_CHECK_CUDA(cudaStreamIsCapturing(st, &cs));
-    if (cs != cudaStreamCaptureStatusNone) return nullptr;
-    int* p = nullptr;
-    KAPSL_CHECK_CUDA(cudaMalloc(&p, kSplitCounters * sizeof(int)));
-    KAPSL_CHECK_CUDA(cudaMemset(p, 0, kSplitCounters * sizeof(int)));
-    ctr[dev] = p;
-  }
-  return ctr[dev];
-}
-
 int launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C, int64_t ldc, bool out_f32, int M,
                 int N, int K, int epi, const bf16* bias, const bf16* res, int64_t ldr, float* workspace,
                 size_t workspace_bytes, int* err, cudaStream_t st, int force_bn, int force_splits, bool defer_splitk) {
@@ -939,9 +808,6 @@ int launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C,
       EpiArgs ep{C, ldc, bias, res, ldr, workspace};
       const int units2 = m2 * ((N + bn2 - 1) / bn2);
       const int grid = 2 * std::min(units2, nclusters);
-      // As many stages as fit in 227 KiB: the mainloop is bound by how many operand
-      // bytes are in flight from L2 (a k-block took the same time with 192- and
-      // 256-wide tiles at 6 stages), so the ring is as deep as shared memory allows.
 #define KAPSL_GEMM2_DISPATCH(BNV)                                                                        \
   {                                                                                                     \
     constexpr int ST = gemm2_stages(BNV);                                                               \
@@ -1005,14 +871,6 @@ int launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C,
   CUtensorMap ta = make_tmap_2d_bf16(A, M, K, lda, BM, BK);
   CUtensorMap tb = make_tmap_2d_bf16(B, N, K, ldb, bn, BK);
   EpiArgs ep{C, ldc, bias, res, ldr, workspace};
-  bool fixup = false;
-  if (splits > 1 && !defer_splitk && m_tiles * n_tiles * 4 <= kSplitCounters &&
-      std::getenv("KAPSL_SPLITK_KERNEL") == nullptr) {
-    ep.tile_ctr = splitk_counters(st);
-    fixup = ep.tile_ctr != nullptr;
-    ep.fix_epi = epi;
-    ep.fix_f32 = out_f32 ? 1 : 0;
-  }
   const int units = m_tiles * n_tiles * splits;
   const int grid = std::min(units, sms);
   const int kepi = splits > 1 ? 4 : epi;
@@ -1029,10 +887,10 @@ int launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C,
   if (bn == 256) {
     KAPSL_GEMM_DISPATCH(256, 4)
   } else {
-    KAPSL_GEMM_DISPATCH(128, 7)
+    KAPSL_GEMM_DISPATCH(128, 6)
   }
 #undef KAPSL_GEMM_DISPATCH
-  if (splits > 1 && (defer_splitk || fixup)) return splits;  // summed by the consumer / inside the kernel
+  if (splits > 1 && defer_splitk) return splits;  // the consumer sums the partials
   if (splits > 1) {
     const int64_t total = (int64_t)M * N / 4;
     const int blocks = (int)((total + 255) / 256);
