@@ -177,8 +177,9 @@ def test_tensor_and_expert_parallel():
         res.append(json.loads(line[0][7:]))
     for r in res:
         assert r["fused_err"] == 0 and r["nccl_err"] == 0 and r["engine_err"] == 0 and r["ep_err"] == 0
-        # outputs of magnitude ~3: bf16 rounding of each partial and of the sum is ~0.01 each
-        assert r["fused"] < 0.05 and r["nccl"] < 0.05, r
+        # outputs of magnitude ~3: bf16 rounding of each partial and of the sum is ~0.01 each;
+        # NCCL's bf16 ring rounds once per hop, so its error grows with the rank count
+        assert r["fused"] < 0.05 and r["nccl"] < 0.025 * world, r
         bad = [v for v in ("pull", "ll1", "ll2")
                if not (r["norm_err_" + v] == 0 and r["norm_h_" + v] < 0.05 and r["norm_x_" + v] < 0.05)]
         assert not bad, (bad, r)
