@@ -307,56 +307,46 @@ __device__ int slice_gather_sampled(const SampleArgs& a, const float* lg, int k,
   const bool vec_ok = (reinterpret_cast<uintptr_t>(lg) & 15) == 0;
   const int vend4 = vec_ok ? (vend & ~3) : 0;
   const int step = (int)blockDim.x * 4 * kGatherVec;
-  // the next slab's loads are issued before this slab is scanned (software pipelining),
-  // and a warp with nothing at or above t skips the scan and the shared atomic
-  auto load_slab = [&](int base, float4 (&dst)[kGatherVec]) {
+  for (int base = 0; base < vend4; base += step) {
+    float4 q[kGatherVec];
 #pragma unroll
     for (int u = 0; u < kGatherVec; ++u) {
       const int v = base + (u * (int)blockDim.x + tid) * 4;
-      dst[u] = v < vend4 ? *reinterpret_cast<const float4*>(lg + v)
-                         : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+      q[u] = v < vend4 ? *reinterpret_cast<const float4*>(lg + v) : make_float4(-INFINITY, -INFINITY, -INFINITY,
+                                                                                  -INFINITY);
     }
-  };
-  float4 q[kGatherVec], nq[kGatherVec];
-  if (vend4 > 0) load_slab(0, q);
-  for (int base = 0; base < vend4; base += step) {
-    if (base + step < vend4) load_slab(base + step, nq);
     int cnt = 0;
 #pragma unroll
     for (int u = 0; u < kGatherVec; ++u)
       if (base + (u * (int)blockDim.x + tid) * 4 < vend4)
         cnt += (q[u].x >= t_thr) + (q[u].y >= t_thr) + (q[u].z >= t_thr) + (q[u].w >= t_thr);
-    if (__any_sync(0xffffffffu, cnt > 0)) {
-      int incl = cnt;
+    int incl = cnt;
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
-      }
-      int wbase = 0;
-      if (lane == 31) wbase = atomicAdd(&sm.misc[3], incl);
-      wbase = __shfl_sync(0xffffffffu, wbase, 31);
-      int p = wbase + incl - cnt;
-      if (cnt > 0) {
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += y;
+    }
+    int wbase = 0;
+    if (lane == 31 && incl > 0) wbase = atomicAdd(&sm.misc[3], incl);
+    wbase = __shfl_sync(0xffffffffu, wbase, 31);
+    int p = wbase + incl - cnt;
+    if (cnt > 0) {
 #pragma unroll
-        for (int u = 0; u < kGatherVec; ++u) {
-          const int v = base + (u * (int)blockDim.x + tid) * 4;
-          if (v >= vend4) continue;
-          const float e[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+      for (int u = 0; u < kGatherVec; ++u) {
+        const int v = base + (u * (int)blockDim.x + tid) * 4;
+        if (v >= vend4) continue;
+        const float e[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            if (e[j] >= t_thr) {
-              if (p < kCandCap) {
-                sm.val[p] = e[j];
-                sm.idx[p] = a.v0 + v + j;
-              }
-              ++p;
+        for (int j = 0; j < 4; ++j)
+          if (e[j] >= t_thr) {
+            if (p < kCandCap) {
+              sm.val[p] = e[j];
+              sm.idx[p] = a.v0 + v + j;
             }
-        }
+            ++p;
+          }
       }
     }
-#pragma unroll
-    for (int u = 0; u < kGatherVec; ++u) q[u] = nq[u];
   }
   for (int v = vend4 + tid; v < vend; v += blockDim.x) {  // tail (or an unaligned slice)
     const float l = lg[v];

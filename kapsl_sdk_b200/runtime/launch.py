@@ -52,7 +52,9 @@ def parse_args(argv: Optional[list] = None) -> argparse.Namespace:
     p.add_argument("--ignore-eos", action="store_true", help="default sampling ignores EOS (benchmarks)")
     p.add_argument("--greedy", action="store_true", help="default sampling is greedy (temperature 0)")
     p.add_argument("--max-new-tokens", type=int, default=0, help="default max_new_tokens of requests")
-    p.add_argument("--ready-file", default=None, help="written by rank 0 once the servers accept connections")
+    p.add_argument("--ready-file", default=None,
+                   help="written by rank 0 once the servers accept connections: socket, TCP port and its pid, "
+                        "one per line (SIGTERM to that pid stops the whole group)")
     a = p.parse_args(argv)
     if not a.models and not a.preset:
         p.error("give at least one model package / path or --preset")
@@ -183,7 +185,7 @@ def main(argv: Optional[list] = None) -> int:
     signal.signal(signal.SIGINT, _stop)
     if a.ready_file:
         with open(a.ready_file + ".tmp", "w") as f:
-            f.write(f"{a.socket or ''}\n{srv.tcp_port or ''}\n")
+            f.write(f"{a.socket or ''}\n{srv.tcp_port or ''}\n{os.getpid()}\n")  # socket, TCP port, rank 0 pid
         os.replace(a.ready_file + ".tmp", a.ready_file)
     print(f"kapsl-runtime: serving {len(backends)} model(s) on "
           f"{', '.join(x for x in (a.socket, f'tcp {srv.tcp_port}' if srv.tcp_port else '', a.shm_name) if x)}"
