@@ -396,6 +396,34 @@ PYBIND11_MODULE(_native, m) {
   m.attr("STATUS_ERR") = wire::STATUS_ERR;
   m.attr("STATUS_STREAM_CHUNK") = wire::STATUS_STREAM_CHUNK;
   m.attr("STATUS_STREAM_END") = wire::STATUS_STREAM_END;
+  py::class_<TokenChannel, std::shared_ptr<TokenChannel>>(m, "TokenChannel",
+                                                          "token ids from the engine loop to a streaming connection")
+      .def(py::init<>())
+      .def("push", &TokenChannel::push)
+      .def("finish", &TokenChannel::finish)
+      .def("fail", &TokenChannel::fail)
+      .def("cancel", &TokenChannel::cancel)
+      .def("cancelled", &TokenChannel::cancelled)
+      .def("pop", [](TokenChannel& c, int timeout_ms) {
+        std::vector<int32_t> v;
+        std::string e;
+        int st;
+        {
+          py::gil_scoped_release nogil;
+          st = c.pop(v, e, timeout_ms);
+        }
+        return py::make_tuple(st, v, e);
+      }, "(status, tokens, error): status 0 tokens, 1 end, 2 error, 3 timeout");
+  // One call per engine step: push tok[i] into chans[i], then close those with fin[i].
+  m.def("push_tokens", [](const std::vector<std::shared_ptr<TokenChannel>>& chans, const std::vector<int32_t>& toks,
+                          const std::vector<bool>& fin) {
+    if (chans.size() != toks.size() || chans.size() != fin.size()) throw std::invalid_argument("push_tokens: lengths");
+    py::gil_scoped_release nogil;
+    for (size_t i = 0; i < chans.size(); ++i) {
+      chans[i]->push(toks[i]);
+      if (fin[i]) chans[i]->finish();
+    }
+  });
   m.def("encode_packet", [](py::object shape, std::string dtype, py::bytes data) {
     return py::bytes(wire::encode_packet(packet_from_py(py::make_tuple(shape, dtype, data))));
   });

@@ -217,6 +217,44 @@ void WireServer::accept_loop(int lfd) {
   }
 }
 
+// Streams a token channel: every token queued since the last wake-up becomes an
+// int32 [1, 1] chunk frame, written together in one call; then END (or ERR, END).
+// A failed write (the client went away) cancels the channel, and the producer
+// aborts the request.
+bool WireServer::stream_channel(int fd, TokenChannel& ch) {
+  std::vector<int32_t> toks;
+  std::string cerr, out;
+  for (;;) {
+    const int st = ch.pop(toks, cerr, 200);
+    if (st == TokenChannel::kTimeout) {
+      if (!running_.load()) {
+        ch.cancel();
+        return false;
+      }
+      continue;
+    }
+    if (st == TokenChannel::kTokens) {
+      out.clear();
+      wire::Packet pk;
+      pk.shape = {1, 1};
+      pk.dtype = "int32";
+      for (const int32_t t : toks) {
+        pk.data.assign(reinterpret_cast<const char*>(&t), 4);
+        const std::string pl = wire::encode_packet(pk);
+        out += wire::response_header(wire::STATUS_STREAM_CHUNK, (uint32_t)pl.size());
+        out += pl;
+      }
+      if (!net::write_all(fd, out.data(), out.size())) {
+        ch.cancel();
+        return false;
+      }
+      continue;
+    }
+    if (st == TokenChannel::kError) return send_frame(fd, wire::STATUS_ERR, cerr) && send_frame(fd, wire::STATUS_STREAM_END, "");
+    return send_frame(fd, wire::STATUS_STREAM_END, "");
+  }
+}
+
 bool WireServer::send_frame(int fd, uint32_t status, const std::string& payload) {
   std::string out = wire::response_header(status, (uint32_t)payload.size());
   out += payload;
@@ -290,11 +328,16 @@ bool WireServer::handle_frame(int fd, uint32_t model_id, uint32_t op, const std:
     }
     if (auto err = check_auth(req)) return send_frame(fd, STATUS_ERR, *err);
     py::object it;
+    std::shared_ptr<TokenChannel> ch;
     std::string err;
     {
       py::gil_scoped_acquire gil;
       try {
-        it = py::iter(handler_.attr("infer_stream")(model_id, request_to_py(req)));
+        py::object res = handler_.attr("infer_stream")(model_id, request_to_py(req));
+        if (py::isinstance<TokenChannel>(res))
+          ch = res.cast<std::shared_ptr<TokenChannel>>();  // token ids streamed without the GIL
+        else
+          it = py::iter(res);
       } catch (py::error_already_set& e) {
         err = py_error_message(e);
       } catch (const std::exception& e) {
@@ -302,6 +345,7 @@ bool WireServer::handle_frame(int fd, uint32_t model_id, uint32_t op, const std:
       }
     }
     if (!err.empty()) return send_frame(fd, STATUS_ERR, err);  // initial failure: ERR only
+    if (ch) return stream_channel(fd, *ch);
     bool ok = true;
     for (;;) {
       Packet chunk;

@@ -19,6 +19,7 @@
 // the call itself.  Every SHM offset/size from a client is bounds-checked.
 #pragma once
 
+#include "token_channel.h"
 #include <pybind11/pybind11.h>
 
 #include <atomic>
@@ -59,6 +60,7 @@ class WireServer {
   void serve_connection(int fd);
   bool handle_frame(int fd, uint32_t model_id, uint32_t op, const std::string& payload);
   bool send_frame(int fd, uint32_t status, const std::string& payload);
+  bool stream_channel(int fd, TokenChannel& ch);
   std::optional<std::string> check_auth(const wire::Request& r) const;
 
   py::object handler_;

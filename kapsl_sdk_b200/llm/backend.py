@@ -142,10 +142,19 @@ def _find_tag(template: str, label: str) -> Optional[str]:
         i = b + 1
 
 
-class _Pending:
-    __slots__ = ("request_id", "prompt_ids", "params", "session_id", "out", "cancel", "seq")
+def _native_mod():
+    try:
+        from .._ext import native
 
-    def __init__(self, request_id, prompt_ids, params, session_id, cancel):
+        return native()
+    except Exception:  # pragma: no cover - the native module is part of the build
+        return None
+
+
+class _Pending:
+    __slots__ = ("request_id", "prompt_ids", "params", "session_id", "out", "cancel", "seq", "channel")
+
+    def __init__(self, request_id, prompt_ids, params, session_id, cancel, channel=None):
         self.request_id = request_id
         self.prompt_ids = prompt_ids
         self.params = params
@@ -153,6 +162,18 @@ class _Pending:
         self.out: "queue.Queue" = queue.Queue()
         self.cancel = cancel
         self.seq = None
+        # native TokenChannel of a token-id stream served by the native server, else None
+        self.channel = channel
+
+    def fail(self, err) -> None:
+        if self.channel is not None:
+            self.channel.fail(str(err))
+        else:
+            self.out.put(err)
+
+    def cancelled(self) -> bool:
+        return (self.cancel is not None and self.cancel.is_cancelled()) or \
+            (self.channel is not None and self.channel.cancelled())
 
 
 class LLMBackend(Engine):
@@ -264,13 +285,13 @@ class LLMBackend(Engine):
                                             admission_control=self.admission_control)
                     self._live[p.request_id] = p
                 except EngineError as e:
-                    p.out.put(e)
+                    p.fail(e)
                 except Exception as e:  # pragma: no cover - defensive
-                    p.out.put(EngineError.backend(str(e)))
+                    p.fail(EngineError.backend(str(e)))
             for rid, p in list(self._live.items()):
-                if p.cancel is not None and p.cancel.is_cancelled():
+                if p.cancelled():
                     eng.abort(rid)
-                    p.out.put(EngineError.cancelled("Request cancelled"))
+                    p.fail(EngineError.cancelled("Request cancelled"))
                     del self._live[rid]
             if not eng.has_unfinished():
                 if not drained:
@@ -284,19 +305,27 @@ class LLMBackend(Engine):
                 err = e if isinstance(e, EngineError) else EngineError.inference(f"LLM execution error: {e}")
                 for rid, p in list(self._live.items()):
                     eng.abort(rid)
-                    p.out.put(err)
+                    p.fail(err)
                     del self._live[rid]
                 continue
             self._stats["busy_s"] += time.perf_counter() - t0
             self._peak = max(self._peak, len(self._live))
+            chans, ctoks, cfins = [], [], []
             for o in outs:
                 p = self._live.get(o.request_id)
                 if p is None:
                     continue
-                p.out.put((o.new_token, o.finished, o.seq.finish_reason))
+                if p.channel is not None:
+                    chans.append(p.channel)
+                    ctoks.append(int(o.new_token))
+                    cfins.append(bool(o.finished))
+                else:
+                    p.out.put((o.new_token, o.finished, o.seq.finish_reason))
                 self._stats["tokens"] += 1
                 if o.finished:
                     del self._live[o.request_id]
+            if chans:  # one native call for every channel-streamed token of the step
+                _native_mod().push_tokens(chans, ctoks, cfins)
 
     # ------------------------------------------------------------- serving
     def _params_for(self, request: InferenceRequest) -> SamplingParams:
@@ -321,6 +350,30 @@ class LLMBackend(Engine):
             if m.priority is not None:
                 s.priority = int(m.priority)
         return s
+
+    def infer_stream_native(self, request: InferenceRequest):
+        """A token-id request (int32 / int64 input) as a native ``TokenChannel`` the
+        native server streams from without the GIL (the same frames as
+        :meth:`infer_stream`: one int32 [1, 1] chunk per token, then END, or ERR
+        and END); ``None`` for text requests or without the native module."""
+        if request.input.dtype not in (TensorDtype.INT32, TensorDtype.INT64):
+            return None
+        nat = _native_mod()
+        if nat is None or not hasattr(nat, "TokenChannel"):
+            return None
+        if self.engine is None:
+            raise EngineError.model_not_loaded()
+        ids = np.frombuffer(request.input.data, dtype=np.int32 if request.input.dtype is TensorDtype.INT32
+                            else np.int64).astype(np.int64).tolist()
+        if not ids:
+            raise EngineError.invalid_input("empty prompt")
+        rid = (request.metadata.request_id if request.metadata and request.metadata.request_id else None) \
+            or request.session_id or str(uuid.uuid4())
+        ch = nat.TokenChannel()
+        p = _Pending(rid, ids, self._params_for(request), request.session_id, request.cancellation, channel=ch)
+        self._stats["requests"] += 1
+        self._inbox.put(p)
+        return ch
 
     def infer_stream(self, request: InferenceRequest) -> Iterator[BinaryTensorPacket]:
         """Utf8 input -> streamed text deltas (the reference's behaviour).  An int32 or

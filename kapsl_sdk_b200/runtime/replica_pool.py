@@ -133,11 +133,26 @@ class ReplicaPool:
     execute = infer
 
     def infer_stream(self, request: InferenceRequest):
+        return self._stream(request, native=False)
+
+    def infer_stream_native(self, request: InferenceRequest):
+        """:meth:`infer_stream` as a native token channel when the chosen replica
+        offers one, else None; same ordering and failover."""
+        return self._stream(request, native=True)
+
+    def _stream(self, request: InferenceRequest, native: bool):
         order = self._ordered(request)
         last = None
         for r in order:
+            if native and getattr(r.scheduler, "infer_stream_native", None) is None:
+                return None
             r.requests_total += 1
             try:
+                if native:
+                    ch = r.scheduler.infer_stream_native(request)
+                    if ch is None:
+                        r.requests_total -= 1  # not applicable: the packet stream serves it
+                    return ch
                 return r.scheduler.infer_stream(request)
             except EngineError as e:
                 if e.kind.name in ("INVALID_INPUT", "CANCELLED"):

@@ -239,6 +239,15 @@ class Scheduler:
         eng = self.engines[self._route(request) % len(self.engines)]
         return eng.infer_stream(request)
 
+    def infer_stream_native(self, request: InferenceRequest):
+        """:meth:`infer_stream` as a native token channel when the routed engine
+        offers one (token-id requests to an LLM backend), else None."""
+        if not self.is_healthy():
+            raise EngineError.overloaded("scheduler unhealthy")
+        eng = self.engines[self._route(request) % len(self.engines)]
+        native = getattr(eng, "infer_stream_native", None)
+        return native(request) if native is not None else None
+
     def get_queue_depth(self) -> tuple:
         return sum(q.depth() for q in self.high), sum(q.depth() for q in self.low)
 

@@ -59,6 +59,13 @@ class Dispatcher:
     def infer_stream(self, model_id: int, req: dict) -> Iterator[tuple]:
         target = self._target(model_id)
         request = request_from_dict(req)
+        native = getattr(target, "infer_stream_native", None)
+        if native is not None:
+            # a token-id stream the native server writes without the GIL (None: not
+            # applicable to this request, take the packet iterator)
+            ch = native(request)
+            if ch is not None:
+                return ch
         stream = target.infer_stream(request)  # errors here are "initial" failures
 
         def gen():
@@ -84,3 +91,7 @@ class EngineTarget:
 
     def infer_stream(self, request: InferenceRequest):
         return self.engine.infer_stream(request)
+
+    def infer_stream_native(self, request: InferenceRequest):
+        native = getattr(self.engine, "infer_stream_native", None)
+        return native(request) if native is not None else None

@@ -85,7 +85,7 @@ NOJOIN_WORKER = textwrap.dedent("""
     rank = int(os.environ["RANK"])
     dist.init_process_group("gloo", timeout=timedelta(seconds=3))
     if rank == 1:
-        time.sleep(8)  # never joins the collective in time
+        time.sleep(20)  # never joins the collective in time
         os._exit(0)
     t0 = time.time()
     try:
@@ -100,7 +100,8 @@ NOJOIN_WORKER = textwrap.dedent("""
 def test_collective_with_missing_rank_raises_instead_of_hanging():
     outs = _spawn(NOJOIN_WORKER, 2)
     assert "RAISED" in outs[0][1], outs[0][1][-2000:]
-    assert float(outs[0][1].split("RAISED")[1].split()[1]) < 8
+    # the 3 s process-group timeout ends the collective long before the peer would exit
+    assert float(outs[0][1].split("RAISED")[1].split()[1]) < 15
 
 
 def test_server_survives_corrupted_truncated_and_dropped_requests():

@@ -162,6 +162,54 @@ def test_backend_stream_over_unix_socket():
         backend.unload()
 
 
+def test_token_id_streams_use_the_native_channel():
+    """Token-id prompts are streamed by the native server from a TokenChannel (no
+    Python generator per token): the same greedy tokens as the Python packet path,
+    errors as ERR frames, and a client that hangs up mid-stream cancels its request."""
+    import socket
+    import time
+
+    from kapsl_sdk import KapslClient
+    from kapsl_sdk_b200._ext import native
+    from kapsl_sdk_b200.llm.backend import LLMBackend
+    from kapsl_sdk_b200.server import KapslServer
+    from kapsl_sdk_b200.server import wire
+
+    cfg = tiny_cfg(vocab_size=259 + 3)
+    backend = LLMBackend(cpu_engine(cfg))
+    backend.rc.sampling = SamplingParams.greedy(12, ignore_eos=True)
+    d = tempfile.mkdtemp(prefix="kapsl-llm-")
+    path = os.path.join(d, "s.sock")
+    srv = KapslServer(models={0: backend}).listen_unix(path).start()
+    try:
+        ids = np.array([5, 9, 13, 40, 7], dtype=np.int32)
+        req = InferenceRequest(BinaryTensorPacket([1, 5], TensorDtype.INT32, ids.tobytes()))
+        assert isinstance(srv.dispatcher._target(0).infer_stream_native(req), native().TokenChannel)
+        time.sleep(0.5)  # let that probe request finish on the engine loop
+        want = [int(np.frombuffer(p.data, np.int32)[0]) for p in backend.infer_stream(req)]  # Python packets
+        c = KapslClient(path)
+        got = [int(np.frombuffer(b, np.int32)[0]) for b in c.infer_stream(0, [1, 5], "int32", ids.tobytes())]
+        assert got == want and len(got) == 12
+        with pytest.raises(RuntimeError, match="empty prompt"):
+            list(c.infer_stream(0, [1, 0], "int32", b""))
+        # hang up after the first chunk: the request is aborted, not run to its end
+        backend.rc.sampling = SamplingParams.greedy(200, ignore_eos=True)
+        s = socket.socket(socket.AF_UNIX)
+        s.connect(path)
+        body = wire.encode_request(([1, 5], "int32", ids.tobytes()))
+        s.sendall(wire.request_header(0, wire.OP_INFER_STREAM, len(body)) + body)
+        assert len(s.recv(8)) == 8
+        s.close()
+        t0 = time.time()
+        while (backend._live or backend._inbox.qsize()) and time.time() - t0 < 20:
+            time.sleep(0.05)
+        assert not backend._live
+        assert backend.engine.has_unfinished() is False
+    finally:
+        srv.stop()
+        backend.unload()
+
+
 def test_backend_serves_on_the_callers_thread():
     """own_thread=False: the engine loop runs in run() on the calling thread
     (the thread that built the model keeps the only OpenMP team), and unload()
