@@ -548,7 +548,7 @@ __device__ int slice_topk(const SampleArgs& a, const float* lg, int k, SelectSme
 
 template <bool FINISH>
 __global__ void __launch_bounds__(kSelectThreads, 2) sample_select_kernel(SampleArgs a) {
-  griddep_entry();
+  griddep_wait_only();
   __shared__ SelectSmem sm;
   __shared__ int64_t epoch_sh;
   const int row = blockIdx.x;
