@@ -333,7 +333,12 @@ def main():
     e2e_d2h = engine.runner.stats["d2h_bytes"] - d2h1
     barrier()
 
+    # correctness of the timed pass: ranks that share one workload (tensor / pipeline
+    # parallel) must have produced the same tokens; every token id lies in the vocabulary
+    digest = outputs_digest(all_seqs)
+    in_vocab = all(0 <= t < cfg.vocab_size for s in all_seqs for t in s.output_ids)
     vals = torch.tensor([ms, out_tokens, e2e_s, e2e_tokens, ttft, tpot], dtype=torch.float64, device=dev)
+    checks = torch.tensor([digest, int(in_vocab)], dtype=torch.int64, device=dev)
     if world > 1:
         gathered = [torch.zeros_like(vals) for _ in range(world)]
         dist.all_gather(gathered, vals)
@@ -349,7 +354,13 @@ def main():
         e2e_max = float(g[0, 2]) if shared else e2e_max
         ttft_all = float(g[:, 4].max())
         tpot_all = float(g[:, 5].max())
+        gc = [torch.zeros_like(checks) for _ in range(world)]
+        dist.all_gather(gc, checks)
+        gc = torch.stack(gc)
+        ranks_agree = bool((gc[:, 0] == gc[0, 0]).all()) if shared else None
+        in_vocab = bool(gc[:, 1].all())
     else:
+        ranks_agree = None
         ms_max, e2e_max, tot_tokens, tot_e2e_tokens, ttft_all, tpot_all = ms, e2e_s, out_tokens, e2e_tokens, ttft, tpot
     value = tot_tokens / (ms_max / 1000.0)
     par = ((f"tp{world}" + ("" if world == 1 else f"-{args.tp_mode}")) if args.parallel == "tp"
@@ -379,6 +390,9 @@ def main():
                            "other ranks follow its steps)",
                     "timing": "host clock, first request sent to last token received, client processes"},
             "gpu_launches": int(launches),
+            "check": {"tokens_in_vocab": in_vocab, "ranks_agree": ranks_agree,
+                      "what": "timed pass: every output id inside the vocabulary; ranks sharing one workload "
+                              "produced identical outputs (digest over all sequences)"},
         }
         if args.impl == "b1":
             line["impl"] = "b1-library-baseline"
@@ -388,6 +402,18 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+def outputs_digest(seqs) -> int:
+    """63-bit digest of every sequence's output ids, in request order."""
+    import hashlib
+
+    h = hashlib.sha1()
+    for s in seqs:
+        h.update(len(s.output_ids).to_bytes(4, "little"))
+        for t in s.output_ids:
+            h.update(int(t).to_bytes(4, "little", signed=True))
+    return int.from_bytes(h.digest()[:8], "little") & ((1 << 63) - 1)
 
 
 def _e2e_client(sock: str, prompts: list, go, q) -> None:
