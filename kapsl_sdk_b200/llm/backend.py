@@ -271,6 +271,22 @@ class LLMBackend(Engine):
 
     # ------------------------------------------------------------ engine loop
     def _loop(self) -> None:
+        try:
+            self._serve_loop()
+        finally:
+            # the loop ended (unload): a request still waiting for tokens gets an error
+            # instead of a stream that never ends
+            gone = EngineError.model_not_loaded()
+            for p in list(self._live.values()):
+                p.fail(gone)
+            self._live.clear()
+            while True:
+                try:
+                    self._inbox.get_nowait().fail(gone)
+                except queue.Empty:
+                    break
+
+    def _serve_loop(self) -> None:
         eng = self.engine
         while not self._stop.is_set():
             drained = False

@@ -3,6 +3,7 @@ paged KV, reference sampler) behind LLMBackend, served by the C++ socket
 server and consumed with the C++ client SDK."""
 import os
 import tempfile
+import time
 
 import numpy as np
 import pytest
@@ -208,6 +209,45 @@ def test_token_id_streams_use_the_native_channel():
     finally:
         srv.stop()
         backend.unload()
+
+
+def test_unload_ends_open_streams_with_an_error():
+    """Unloading while requests stream: the Python stream raises and the native
+    channel reports an error, instead of either waiting forever."""
+    import threading
+
+    from kapsl_sdk_b200.engine_api import EngineError
+    from kapsl_sdk_b200.llm.backend import LLMBackend
+
+    cfg = tiny_cfg(vocab_size=259 + 3)
+    backend = LLMBackend(cpu_engine(cfg))
+    backend.rc.sampling = SamplingParams.greedy(240, ignore_eos=True)
+    ids = np.array([5, 9, 13, 40], np.int32).tobytes()
+    req = InferenceRequest(BinaryTensorPacket([1, 4], TensorDtype.INT32, ids))
+    ch = backend.infer_stream_native(req)
+    got, err = [], []
+
+    def consume():
+        try:
+            for pkt in backend.infer_stream(req):
+                got.append(pkt)
+        except EngineError as e:
+            err.append(e)
+
+    t = threading.Thread(target=consume)
+    t.start()
+    t0 = time.time()
+    while not got and time.time() - t0 < 30:
+        time.sleep(0.01)
+    backend.unload()
+    t.join(30)
+    assert not t.is_alive() and err and got
+    status = None
+    for _ in range(200):
+        status, toks, msg = ch.pop(100)
+        if status in (1, 2):
+            break
+    assert status == 2 and msg
 
 
 def test_backend_serves_on_the_callers_thread():
