@@ -255,7 +255,12 @@ class OnnxGraph:
                  # reductions / selection
                  "ReduceSum", "ReduceMax", "ReduceMin", "ReduceProd", "ReduceL2", "ArgMax", "ArgMin", "TopK",
                  # layers
-                 "InstanceNormalization", "ConvTranspose", "Einsum", "GlobalMaxPool"}
+                 "InstanceNormalization", "ConvTranspose", "Einsum", "GlobalMaxPool",
+                 # indexing, quantization, normalization
+                 "GatherElements", "ScatterElements", "ScatterND", "GatherND", "OneHot", "NonZero",
+                 "DepthToSpace", "SpaceToDepth", "QuantizeLinear", "DequantizeLinear", "GroupNormalization",
+                 "LpNormalization", "ReduceLogSumExp", "ReduceSumSquare", "ReduceL1", "Mish", "Celu",
+                 "ThresholdedRelu", "Shrink", "Compress", "BitShift"}
 
     def __init__(self, model: OnnxModel, device="cpu"):
         bad = sorted({n.op for n in model.nodes} - self.SUPPORTED)
@@ -549,6 +554,132 @@ class OnnxGraph:
         if op == "Einsum":
             eq = a["equation"]
             return torch.einsum(eq.decode() if isinstance(eq, bytes) else eq, *x)
+        return self._op_extra(n, x)
+
+    def _op_extra(self, n: Node, x: list):
+        """Indexing, quantization and normalization operators (opset 13+ semantics)."""
+        a, op = n.attrs, n.op
+        F = torch.nn.functional
+        if op == "GatherElements":
+            ax = a.get("axis", 0)
+            idx = x[1].long()
+            idx = torch.where(idx < 0, idx + x[0].shape[ax], idx)
+            return torch.gather(x[0], ax, idx)
+        if op == "ScatterElements":
+            ax, red = a.get("axis", 0), a.get("reduction", b"none")
+            red = red.decode() if isinstance(red, bytes) else red
+            idx = x[1].long()
+            idx = torch.where(idx < 0, idx + x[0].shape[ax], idx)
+            if red == "none":
+                return x[0].scatter(ax, idx, x[2])
+            return x[0].scatter_reduce(ax, idx, x[2], {"add": "sum", "mul": "prod", "max": "amax",
+                                                        "min": "amin"}[red], include_self=True)
+        if op == "ScatterND":
+            y = x[0].clone()
+            idx = x[1].long()
+            k = idx.shape[-1]
+            flat_idx = idx.reshape(-1, k)
+            upd = x[2].reshape(flat_idx.shape[0], *x[0].shape[k:])
+            for i in range(flat_idx.shape[0]):
+                y[tuple(flat_idx[i].tolist())] = upd[i]
+            return y
+        if op == "GatherND":
+            b = a.get("batch_dims", 0)
+            if b:
+                raise ValueError("GatherND with batch_dims is not supported")
+            idx = x[1].long()
+            k = idx.shape[-1]
+            flat = idx.reshape(-1, k)
+            out = torch.stack([x[0][tuple(r.tolist())] for r in flat]) if flat.shape[0] else \
+                x[0].new_zeros((0, *x[0].shape[k:]))
+            return out.reshape(*idx.shape[:-1], *x[0].shape[k:])
+        if op == "OneHot":
+            depth = int(x[1].reshape(-1)[0].item())
+            vals = x[2].reshape(-1)
+            idx = x[0].long()
+            idx = torch.where(idx < 0, idx + depth, idx)
+            valid = ((idx >= 0) & (idx < depth)).unsqueeze(-1)
+            oh = (F.one_hot(idx.clamp(0, depth - 1), depth) * valid).to(vals.dtype)
+            y = vals[0] + oh * (vals[1] - vals[0])
+            ax = a.get("axis", -1)
+            return y if ax in (-1, y.dim() - 1) else torch.movedim(y, -1, ax)
+        if op == "NonZero":
+            return torch.nonzero(x[0]).T.contiguous()
+        if op in ("DepthToSpace", "SpaceToDepth"):
+            bs = a["blocksize"]
+            N, C, H, W = x[0].shape
+            if op == "SpaceToDepth":
+                y = x[0].reshape(N, C, H // bs, bs, W // bs, bs).permute(0, 3, 5, 1, 2, 4)
+                return y.reshape(N, C * bs * bs, H // bs, W // bs)
+            mode = a.get("mode", b"DCR")
+            mode = mode.decode() if isinstance(mode, bytes) else mode
+            if mode == "DCR":
+                y = x[0].reshape(N, bs, bs, C // (bs * bs), H, W).permute(0, 3, 4, 1, 5, 2)
+            else:
+                y = x[0].reshape(N, C // (bs * bs), bs, bs, H, W).permute(0, 1, 4, 2, 5, 3)
+            return y.reshape(N, C // (bs * bs), H * bs, W * bs)
+        if op == "QuantizeLinear":
+            scale = x[1]
+            zp = x[2] if len(x) > 2 and x[2] is not None else torch.zeros((), dtype=torch.uint8)
+            ax = a.get("axis", 1)
+            if scale.dim() == 1 and x[0].dim() > 1:
+                shape = [1] * x[0].dim()
+                shape[ax] = -1
+                scale, zp = scale.reshape(shape), zp.reshape(shape)
+            lo, hi = (0, 255) if zp.dtype == torch.uint8 else (-128, 127)
+            q = torch.round(x[0] / scale) + zp.to(torch.float32)  # round half to even, as ONNX specifies
+            return q.clamp(lo, hi).to(zp.dtype)
+        if op == "DequantizeLinear":
+            scale = x[1]
+            zp = x[2] if len(x) > 2 and x[2] is not None else torch.zeros((), dtype=x[0].dtype)
+            ax = a.get("axis", 1)
+            if scale.dim() == 1 and x[0].dim() > 1:
+                shape = [1] * x[0].dim()
+                shape[ax] = -1
+                scale, zp = scale.reshape(shape), zp.reshape(shape)
+            return (x[0].to(torch.float32) - zp.to(torch.float32)) * scale
+        if op == "GroupNormalization":
+            g = a["num_groups"]
+            y = F.group_norm(x[0], g, eps=a.get("epsilon", 1e-5))
+            C = x[0].shape[1]
+            if x[1].numel() == C:  # opset 21: per-channel scale and bias
+                shape = [1, C] + [1] * (x[0].dim() - 2)
+                return y * x[1].reshape(shape) + x[2].reshape(shape)
+            rep = C // g  # opset 18: per-group scale and bias
+            shape = [1, C] + [1] * (x[0].dim() - 2)
+            return y * x[1].repeat_interleave(rep).reshape(shape) + x[2].repeat_interleave(rep).reshape(shape)
+        if op == "LpNormalization":
+            return F.normalize(x[0], p=a.get("p", 2), dim=a.get("axis", -1))
+        if op in ("ReduceLogSumExp", "ReduceSumSquare", "ReduceL1"):
+            axes = a.get("axes") if "axes" in a else (x[1].tolist() if len(x) > 1 and x[1] is not None else None)
+            keep = bool(a.get("keepdims", 1))
+            dims = tuple(axes) if axes else tuple(range(x[0].dim()))
+            if op == "ReduceLogSumExp":
+                return torch.logsumexp(x[0], dim=dims, keepdim=keep)
+            if op == "ReduceSumSquare":
+                return (x[0] * x[0]).sum(dim=dims, keepdim=keep)
+            return x[0].abs().sum(dim=dims, keepdim=keep)
+        if op == "Mish":
+            return x[0] * torch.tanh(F.softplus(x[0]))
+        if op == "Celu":
+            al = a.get("alpha", 1.0)
+            return torch.clamp(x[0], min=0) + torch.clamp(al * (torch.exp(x[0] / al) - 1), max=0)
+        if op == "ThresholdedRelu":
+            return torch.where(x[0] > a.get("alpha", 1.0), x[0], torch.zeros_like(x[0]))
+        if op == "Shrink":
+            lam, bias = a.get("lambd", 0.5), a.get("bias", 0.0)
+            return torch.where(x[0] < -lam, x[0] + bias, torch.where(x[0] > lam, x[0] - bias, torch.zeros_like(x[0])))
+        if op == "Compress":
+            cond = x[1].bool()
+            if "axis" not in a:
+                return x[0].flatten()[cond[: x[0].numel()].nonzero().flatten()]
+            ax = a["axis"]
+            keep = cond[: x[0].shape[ax]].nonzero().flatten()
+            return torch.index_select(x[0], ax, keep)
+        if op == "BitShift":
+            d = a["direction"]
+            d = d.decode() if isinstance(d, bytes) else d
+            return x[0] << x[1] if d == "LEFT" else x[0] >> x[1]
         raise ValueError(f"unsupported ONNX op {op}")
 
 
@@ -616,7 +747,8 @@ def _ld(f: int, b: bytes) -> bytes:
 
 
 def encode_tensor(name: str, a: np.ndarray) -> bytes:
-    dt = {np.dtype(np.float32): 1, np.dtype(np.int64): 7, np.dtype(np.int32): 6, np.dtype(np.float16): 10}[a.dtype]
+    dt = {np.dtype(np.float32): 1, np.dtype(np.uint8): 2, np.dtype(np.int8): 3, np.dtype(np.int32): 6,
+          np.dtype(np.int64): 7, np.dtype(np.bool_): 9, np.dtype(np.float16): 10}[a.dtype]
     b = b"".join(_key(1, 0) + _enc_varint(d) for d in a.shape)
     b += _key(2, 0) + _enc_varint(dt) + _ld(8, name.encode()) + _ld(9, np.ascontiguousarray(a).tobytes())
     return b

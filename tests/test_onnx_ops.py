@@ -1,143 +1,127 @@
-"""ONNX interpreter operators beyond the core set, each run through an
-encoded ModelProto (encode_model -> read_model -> OnnxGraph) and compared
-with a numpy / torch statement of the operator."""
+"""ONNX interpreter operators beyond the core set, each a one-node graph encoded,
+decoded and run by ``OnnxGraph`` against a NumPy statement of the ONNX spec."""
 import os
 import tempfile
 
 import numpy as np
 import pytest
-import torch
 
 from kapsl_sdk_b200.loaders.onnx import Node, OnnxGraph, encode_model, read_model
 
-rng = np.random.default_rng(0)
+rng = np.random.default_rng(4)
 
 
-def run(nodes, feeds: dict, outputs, inits=None):
+def run1(op, feeds: dict, attrs=None, inits=None, n_out=1):
+    ins = list(feeds) + list(inits or {})
+    outs = [f"y{i}" for i in range(n_out)]
+    blob = encode_model([Node(op, ins, outs, attrs=attrs or {})], list(feeds), outs, inits or {})
     p = os.path.join(tempfile.mkdtemp(), "m.onnx")
-    with open(p, "wb") as f:
-        f.write(encode_model(nodes, list(feeds), outputs, inits or {}))
-    out = OnnxGraph(read_model(p)).run(feeds)
-    return [out[o].numpy() for o in outputs]
+    open(p, "wb").write(blob)
+    res = OnnxGraph(read_model(p)).run(feeds)
+    return [res[o].numpy() for o in outs] if n_out > 1 else res[outs[0]].numpy()
 
 
-X = rng.standard_normal((2, 3, 4)).astype(np.float32)
+def test_gather_scatter_elements():
+    x = rng.standard_normal((3, 4)).astype(np.float32)
+    idx = np.array([[0, -1, 2, 1], [3, 0, 0, 2]], np.int64)
+    want = np.take_along_axis(x[:2], np.where(idx < 0, idx + 4, idx), axis=1)
+    assert np.allclose(run1("GatherElements", {"x": x}, {"axis": 1}, {"i": idx}), want)
+    data = np.zeros((3, 3), np.float32)
+    ind = np.array([[1, 0, 2], [0, 2, 1]], np.int64)
+    upd = np.array([[1.0, 1.1, 1.2], [2.0, 2.1, 2.2]], np.float32)
+    want = data.copy()
+    for i in range(2):
+        for j in range(3):
+            want[ind[i, j], j] = upd[i, j]
+    assert np.allclose(run1("ScatterElements", {"d": data}, {"axis": 0}, {"i": ind, "u": upd}), want)
+    want_add = np.ones((3, 3), np.float32)
+    for i in range(2):
+        for j in range(3):
+            want_add[ind[i, j], j] += upd[i, j]
+    got = run1("ScatterElements", {"d": np.ones((3, 3), np.float32)}, {"axis": 0, "reduction": "add"},
+               {"i": ind, "u": upd})
+    assert np.allclose(got, want_add)
 
 
-@pytest.mark.parametrize("op,ref", [
-    ("Exp", np.exp), ("Neg", np.negative), ("Abs", np.abs), ("Floor", np.floor), ("Ceil", np.ceil),
-    ("Sign", np.sign), ("Sin", np.sin), ("Cos", np.cos), ("Round", np.round),
-    ("Softplus", lambda x: np.log1p(np.exp(x))), ("Softsign", lambda x: x / (1 + np.abs(x))),
-    ("HardSwish", lambda x: x * np.clip(x / 6 + 0.5, 0, 1)),
-])
-def test_unary(op, ref):
-    (y,) = run([Node(op, ["x"], ["y"])], {"x": X}, ["y"])
-    assert np.allclose(y, ref(X), atol=1e-5)
+def test_scatter_nd_gather_nd():
+    data = np.arange(24, dtype=np.float32).reshape(2, 3, 4)
+    idx = np.array([[0, 1], [1, 2]], np.int64)
+    upd = -np.ones((2, 4), np.float32)
+    want = data.copy()
+    want[0, 1] = -1
+    want[1, 2] = -1
+    assert np.allclose(run1("ScatterND", {"d": data}, {}, {"i": idx, "u": upd}), want)
+    assert np.allclose(run1("GatherND", {"d": data}, {}, {"i": idx}), np.stack([data[0, 1], data[1, 2]]))
 
 
-def test_parameterised_activations():
-    (y,) = run([Node("LeakyRelu", ["x"], ["y"], attrs={"alpha": 0.1})], {"x": X}, ["y"])
-    assert np.allclose(y, np.where(X > 0, X, 0.1 * X))
-    (y,) = run([Node("Elu", ["x"], ["y"], attrs={"alpha": 0.5})], {"x": X}, ["y"])
-    assert np.allclose(y, np.where(X > 0, X, 0.5 * (np.exp(X) - 1)), atol=1e-6)
-    (y,) = run([Node("HardSigmoid", ["x"], ["y"], attrs={"alpha": 0.3, "beta": 0.4})], {"x": X}, ["y"])
-    assert np.allclose(y, np.clip(0.3 * X + 0.4, 0, 1))
-    (y,) = run([Node("Gelu", ["x"], ["y"], attrs={"approximate": "tanh"})], {"x": X}, ["y"])
-    assert np.allclose(y, torch.nn.functional.gelu(torch.from_numpy(X), approximate="tanh").numpy(), atol=1e-6)
-    lo, hi = np.array(-0.5, np.float32), np.array(0.25, np.float32)
-    (y,) = run([Node("Clip", ["x", "lo", "hi"], ["y"])], {"x": X}, ["y"], {"lo": lo, "hi": hi})
-    assert np.allclose(y, np.clip(X, -0.5, 0.25))
-    slope = np.array([0.1, 0.2, 0.3, 0.4], np.float32)
-    (y,) = run([Node("PRelu", ["x", "s"], ["y"])], {"x": X}, ["y"], {"s": slope})
-    assert np.allclose(y, np.where(X >= 0, X, X * slope))
+def test_one_hot_and_nonzero():
+    ind = np.array([0, 2, -1, 5], np.int64)
+    got = run1("OneHot", {"i": ind}, {}, {"d": np.array([3], np.int64), "v": np.array([-1.0, 4.0], np.float32)})
+    want = np.full((4, 3), -1.0, np.float32)
+    want[0, 0] = want[1, 2] = want[2, 2] = 4.0  # -1 counts from the end; 5 is out of range
+    assert np.allclose(got, want)
+    x = np.array([[1, 0], [0, 3]], np.float32)
+    assert np.array_equal(run1("NonZero", {"x": x}), np.array(np.nonzero(x)))
 
 
-def test_variadic_compare_logic_and_where():
-    a, b, c = (rng.standard_normal((3, 4)).astype(np.float32) for _ in range(3))
-    ys = run([Node("Max", ["a", "b", "c"], ["mx"]), Node("Min", ["a", "b"], ["mn"]), Node("Sum", ["a", "b", "c"], ["s"]),
-              Node("Mean", ["a", "b"], ["m"]), Node("Less", ["a", "b"], ["lt"]), Node("GreaterOrEqual", ["a", "b"], ["ge"]),
-              Node("Where", ["lt", "a", "b"], ["w"]), Node("And", ["lt", "ge"], ["nd"]), Node("Not", ["lt"], ["nt"])],
-             {"a": a, "b": b, "c": c}, ["mx", "mn", "s", "m", "w", "nd", "nt"])
-    assert np.allclose(ys[0], np.maximum(np.maximum(a, b), c)) and np.allclose(ys[1], np.minimum(a, b))
-    assert np.allclose(ys[2], a + b + c, atol=1e-6) and np.allclose(ys[3], (a + b) / 2)
-    assert np.allclose(ys[4], np.where(a < b, a, b)) and not ys[5].any() and (ys[6] == (a >= b)).all()
-    ia, ib = np.array([7, -7, 7], np.int64), np.array([3, 3, -3], np.int64)
-    (m0, m1) = run([Node("Mod", ["a", "b"], ["m0"]), Node("Mod", ["a", "b"], ["m1"], attrs={"fmod": 1})],
-                   {"a": ia, "b": ib}, ["m0", "m1"])
-    assert m0.tolist() == [1, 2, -2] and m1.tolist() == [1, -1, 1]
+@pytest.mark.parametrize("mode", ["DCR", "CRD"])
+def test_depth_space(mode):
+    x = rng.standard_normal((1, 8, 2, 3)).astype(np.float32)
+    b = 2
+    N, C, H, W = x.shape
+    if mode == "DCR":
+        want = x.reshape(N, b, b, C // 4, H, W).transpose(0, 3, 4, 1, 5, 2).reshape(N, C // 4, H * b, W * b)
+    else:
+        want = x.reshape(N, C // 4, b, b, H, W).transpose(0, 1, 4, 2, 5, 3).reshape(N, C // 4, H * b, W * b)
+    got = run1("DepthToSpace", {"x": x}, {"blocksize": 2, "mode": mode})
+    assert np.allclose(got, want)
+    if mode == "DCR":  # SpaceToDepth inverts the DCR layout
+        assert np.allclose(run1("SpaceToDepth", {"x": got}, {"blocksize": 2}), x)
 
 
-def test_shape_ops():
-    x = rng.standard_normal((2, 1, 3)).astype(np.float32)
-    shp = np.array([2, 4, 3], np.int64)
-    (y,) = run([Node("Expand", ["x", "s"], ["y"])], {"x": x}, ["y"], {"s": shp})
-    assert np.allclose(y, np.broadcast_to(x, (2, 4, 3)))
-    (y,) = run([Node("Tile", ["x", "r"], ["y"])], {"x": x}, ["y"], {"r": np.array([1, 2, 2], np.int64)})
-    assert np.allclose(y, np.tile(x, (1, 2, 2)))
-    z = rng.standard_normal((6, 5)).astype(np.float32)
-    a, b = run([Node("Split", ["z", "sp"], ["a", "b"], attrs={"axis": 0})], {"z": z}, ["a", "b"],
-               {"sp": np.array([2, 4], np.int64)})
-    assert np.allclose(a, z[:2]) and np.allclose(b, z[2:])
-    a, b, c = run([Node("Split", ["z"], ["a", "b", "c"], attrs={"axis": 1})], {"z": z}, ["a", "b", "c"])
-    assert [t.shape[1] for t in (a, b, c)] == [2, 2, 1]
-    pads = np.array([0, 1, 2, 0], np.int64)  # begin (axis0, axis1), end (axis0, axis1)
-    (y,) = run([Node("Pad", ["z", "p", "v"], ["y"])], {"z": z}, ["y"], {"p": pads, "v": np.array(9.0, np.float32)})
-    assert np.allclose(y, np.pad(z, ((0, 2), (1, 0)), constant_values=9.0))
-    for mode in ("reflect", "edge"):
-        (y,) = run([Node("Pad", ["z", "p"], ["y"], attrs={"mode": mode})], {"z": z}, ["y"], {"p": pads})
-        assert np.allclose(y, np.pad(z, ((0, 2), (1, 0)), mode=mode))
-    (y,) = run([Node("ConstantOfShape", ["s"], ["y"], attrs={"value": np.array([2.5], np.float32)})],
-               {"s": np.array([2, 3], np.int64)}, ["y"])
-    assert y.shape == (2, 3) and (y == 2.5).all()
-    (y,) = run([Node("Range", ["a", "b", "d"], ["y"])],
-               {"a": np.array(1, np.int64), "b": np.array(10, np.int64), "d": np.array(3, np.int64)}, ["y"])
-    assert y.tolist() == [1, 4, 7]
-    (y,) = run([Node("Trilu", ["z", "k"], ["y"], attrs={"upper": 0})], {"z": z}, ["y"], {"k": np.array(1, np.int64)})
-    assert np.allclose(y, np.tril(z, 1))
-    (y,) = run([Node("CumSum", ["z", "ax"], ["y"], attrs={"exclusive": 1, "reverse": 1})], {"z": z}, ["y"],
-               {"ax": np.array(1, np.int64)})
-    ref = np.flip(np.cumsum(np.flip(z, 1), 1), 1) - z
-    assert np.allclose(y, ref, atol=1e-5)
-    img = rng.standard_normal((1, 2, 3, 4)).astype(np.float32)
-    (y,) = run([Node("Resize", ["x", "", "sc"], ["y"], attrs={"mode": "nearest"})], {"x": img}, ["y"],
-               {"sc": np.array([1, 1, 2, 2], np.float32)})
-    assert np.allclose(y, img.repeat(2, 2).repeat(2, 3))
+def test_quantize_dequantize():
+    x = np.array([-1.0, 0.0, 0.25, 1.5, 300.0], np.float32)
+    s, z = np.array(0.5, np.float32), np.array(10, np.uint8)
+    q = run1("QuantizeLinear", {"x": x}, {}, {"s": s, "z": z})
+    assert q.dtype == np.uint8 and q.tolist() == [8, 10, 10, 13, 255]  # 0.25 / 0.5 = 0.5 rounds to even
+    assert np.allclose(run1("DequantizeLinear", {"q": q}, {}, {"s": s, "z": z}), (q.astype(np.float32) - 10) * 0.5)
+    x2 = rng.standard_normal((2, 3)).astype(np.float32)
+    sc = np.array([0.1, 0.2, 0.05], np.float32)
+    zp = np.array([0, -3, 5], np.int8)
+    q2 = run1("QuantizeLinear", {"x": x2}, {"axis": 1}, {"s": sc, "z": zp})
+    assert q2.dtype == np.int8
+    assert np.array_equal(q2, np.clip(np.round(x2 / sc) + zp, -128, 127).astype(np.int8))
 
 
-def test_reductions_and_selection():
+def test_norms_and_reductions():
+    x = rng.standard_normal((2, 6, 4)).astype(np.float32)
+    g = 3
+    xr = x.reshape(2, g, -1)
+    norm = ((xr - xr.mean(-1, keepdims=True)) / np.sqrt(xr.var(-1, keepdims=True) + 1e-5)).reshape(x.shape)
+    sc, bi = rng.standard_normal(6).astype(np.float32), rng.standard_normal(6).astype(np.float32)
+    got = run1("GroupNormalization", {"x": x}, {"num_groups": g}, {"s": sc, "b": bi})
+    assert np.allclose(got, norm * sc[None, :, None] + bi[None, :, None], atol=1e-4)
+    assert np.allclose(run1("LpNormalization", {"x": x}, {"axis": -1, "p": 2}),
+                       x / np.linalg.norm(x, axis=-1, keepdims=True), atol=1e-5)
     axes = np.array([1], np.int64)
-    ys = run([Node("ReduceSum", ["x", "ax"], ["s"], attrs={"keepdims": 0}), Node("ReduceMax", ["x"], ["mx"],
-              attrs={"axes": [0, 2]}), Node("ReduceProd", ["x"], ["p"], attrs={"axes": [2], "keepdims": 0}),
-              Node("ReduceL2", ["x"], ["l2"], attrs={"axes": [-1]}), Node("ArgMax", ["x"], ["am"], attrs={"axis": 2}),
-              Node("ArgMin", ["x"], ["an"], attrs={"axis": 1, "keepdims": 0})],
-             {"x": X}, ["s", "mx", "p", "l2", "am", "an"], {"ax": axes})
-    assert np.allclose(ys[0], X.sum(1), atol=1e-6) and np.allclose(ys[1], X.max((0, 2), keepdims=True))
-    assert np.allclose(ys[2], X.prod(2), atol=1e-6)
-    assert np.allclose(ys[3], np.sqrt((X ** 2).sum(-1, keepdims=True)), atol=1e-6)
-    assert (ys[4] == X.argmax(2)[..., None]).all() and (ys[5] == X.argmin(1)).all()
-    v, i = run([Node("TopK", ["x", "k"], ["v", "i"], attrs={"axis": -1})], {"x": X}, ["v", "i"],
-               {"k": np.array([2], np.int64)})
-    assert np.allclose(v, -np.sort(-X, -1)[..., :2]) and (np.take_along_axis(X, i, -1) == v).all()
-    (y,) = run([Node("LogSoftmax", ["x"], ["y"], attrs={"axis": 1})], {"x": X}, ["y"])
-    assert np.allclose(y, torch.log_softmax(torch.from_numpy(X), 1).numpy(), atol=1e-6)
+    assert np.allclose(run1("ReduceLogSumExp", {"x": x}, {"keepdims": 0}, {"a": axes}),
+                       np.log(np.exp(x).sum(1)), atol=1e-5)
+    assert np.allclose(run1("ReduceSumSquare", {"x": x}, {}, {"a": axes}), (x * x).sum(1, keepdims=True), atol=1e-5)
+    assert np.allclose(run1("ReduceL1", {"x": x}, {}, {"a": axes}), np.abs(x).sum(1, keepdims=True), atol=1e-5)
 
 
-def test_layers():
-    img = rng.standard_normal((2, 3, 5, 5)).astype(np.float32)
-    g, b = rng.standard_normal(3).astype(np.float32), rng.standard_normal(3).astype(np.float32)
-    (y,) = run([Node("InstanceNormalization", ["x", "g", "b"], ["y"], attrs={"epsilon": 1e-5})], {"x": img}, ["y"],
-               {"g": g, "b": b})
-    mu, var = img.mean((2, 3), keepdims=True), img.var((2, 3), keepdims=True)
-    assert np.allclose(y, (img - mu) / np.sqrt(var + 1e-5) * g[:, None, None] + b[:, None, None], atol=1e-4)
-    w = rng.standard_normal((3, 4, 3, 3)).astype(np.float32)
-    (y,) = run([Node("ConvTranspose", ["x", "w"], ["y"], attrs={"strides": [2, 2], "pads": [1, 1, 1, 1],
-                                                                "output_padding": [1, 1]})],
-               {"x": img}, ["y"], {"w": w})
-    ref = torch.nn.functional.conv_transpose2d(torch.from_numpy(img), torch.from_numpy(w), stride=2, padding=1,
-                                               output_padding=1).numpy()
-    assert y.shape == ref.shape and np.allclose(y, ref, atol=1e-5)
-    (y,) = run([Node("GlobalMaxPool", ["x"], ["y"])], {"x": img}, ["y"])
-    assert np.allclose(y, img.max((2, 3), keepdims=True))
-    a, c = rng.standard_normal((2, 3, 4)).astype(np.float32), rng.standard_normal((2, 4, 5)).astype(np.float32)
-    (y,) = run([Node("Einsum", ["a", "c"], ["y"], attrs={"equation": "bij,bjk->bik"})], {"a": a, "c": c}, ["y"])
-    assert np.allclose(y, a @ c, atol=1e-5)
+def test_activations_and_selection():
+    x = np.linspace(-3, 3, 13, dtype=np.float32)
+    assert np.allclose(run1("Mish", {"x": x}), x * np.tanh(np.log1p(np.exp(x))), atol=1e-6)
+    assert np.allclose(run1("Celu", {"x": x}, {"alpha": 2.0}),
+                       np.maximum(0, x) + np.minimum(0, 2.0 * (np.exp(x / 2.0) - 1)), atol=1e-6)
+    assert np.allclose(run1("ThresholdedRelu", {"x": x}, {"alpha": 1.0}), np.where(x > 1.0, x, 0))
+    assert np.allclose(run1("Shrink", {"x": x}, {"lambd": 1.0, "bias": 0.5}),
+                       np.where(x < -1, x + 0.5, np.where(x > 1, x - 0.5, 0)))
+    m = np.arange(12, dtype=np.float32).reshape(3, 4)
+    cond = np.array([True, False, True])
+    assert np.array_equal(run1("Compress", {"m": m}, {"axis": 0}, {"c": cond}), m[[0, 2]])
+    assert np.array_equal(run1("Compress", {"m": m}, {}, {"c": np.array([0, 1, 1], bool)}), np.array([1.0, 2.0]))
+    v = np.array([1, 4, 7], np.int64)
+    assert run1("BitShift", {"v": v}, {"direction": "LEFT"}, {"s": np.array([1, 2, 0], np.int64)}).tolist() == \
+        [2, 16, 7]
