@@ -11,6 +11,9 @@ the GGML ones (they have to match to read real files):
   Quants of sub-blocks 2c and 2c+1 share bytes 32c..32c+31 (low / high nibble).
 * Q6_K: 256 values; 128 bytes of low 4 bits, 64 bytes of high 2 bits, 16 int8
   sub-block scales, f16 ``d``; v = d * sc * (q - 32).
+* Q4_0 / Q4_1 / Q5_0 / Q5_1 (32 values), Q2_K / Q3_K / Q5_K (256 values): dequantized
+  at load by the functions below (checked against the gguf package's dequantizers);
+  any other GGML type goes through the gguf package's NumPy dequantizer.
 
 Llama-architecture files store q/k projections permuted for interleaved rotary
 pairs; they are permuted back to the rotate-half layout the RoPE kernel uses.
@@ -84,6 +87,115 @@ def dequant_q8_0(raw: np.ndarray) -> np.ndarray:
     d = b[:, 0:2].copy().view(np.float16).astype(np.float32)
     q = b[:, 2:].view(np.int8).astype(np.float32)
     return (d * q).reshape(-1)
+
+
+def _f16(b: np.ndarray, at: int) -> np.ndarray:
+    """[nb, 1] float32 from the f16 at byte offset `at` of each block."""
+    return b[:, at:at + 2].copy().view(np.float16).astype(np.float32)
+
+
+def _nibbles32(qs: np.ndarray) -> np.ndarray:
+    """[nb, 16] bytes -> [nb, 32] quants: value j < 16 is the low nibble of byte j,
+    value 16 + j its high nibble (the legacy 32-value block order)."""
+    return np.concatenate([qs & 0xF, qs >> 4], axis=1).astype(np.float32)
+
+
+def _high_bits32(qh: np.ndarray) -> np.ndarray:
+    """[nb, 4] bytes (a little-endian u32) -> [nb, 32] bits, bit j for value j."""
+    return np.unpackbits(qh, axis=1, bitorder="little").astype(np.float32)
+
+
+def dequant_q4_0(raw: np.ndarray) -> np.ndarray:
+    """32 values: f16 d, 16 bytes of 4-bit quants; v = d * (q - 8)."""
+    b = raw.reshape(-1, 18)
+    return (_f16(b, 0) * (_nibbles32(b[:, 2:18]) - 8)).reshape(-1)
+
+
+def dequant_q4_1(raw: np.ndarray) -> np.ndarray:
+    """32 values: f16 d, f16 m, 16 bytes of 4-bit quants; v = d * q + m."""
+    b = raw.reshape(-1, 20)
+    return (_f16(b, 0) * _nibbles32(b[:, 4:20]) + _f16(b, 2)).reshape(-1)
+
+
+def dequant_q5_0(raw: np.ndarray) -> np.ndarray:
+    """32 values: f16 d, 4 bytes of fifth bits, 16 bytes of low nibbles; v = d * (q - 16)."""
+    b = raw.reshape(-1, 22)
+    q = _nibbles32(b[:, 6:22]) + 16 * _high_bits32(b[:, 2:6])
+    return (_f16(b, 0) * (q - 16)).reshape(-1)
+
+
+def dequant_q5_1(raw: np.ndarray) -> np.ndarray:
+    """32 values: f16 d, f16 m, 4 bytes of fifth bits, 16 bytes of low nibbles; v = d * q + m."""
+    b = raw.reshape(-1, 24)
+    q = _nibbles32(b[:, 8:24]) + 16 * _high_bits32(b[:, 4:8])
+    return (_f16(b, 0) * q + _f16(b, 2)).reshape(-1)
+
+
+def dequant_q5_k(raw: np.ndarray) -> np.ndarray:
+    """256 values in 8 sub-blocks of 32: f16 d, f16 dmin, 12 bytes of 6-bit (scale,
+    min) pairs packed as in Q4_K, 32 bytes of fifth bits, 128 bytes of low nibbles.
+    Sub-blocks 2c and 2c+1 share nibble bytes 32c..32c+31 (low / high nibble); the
+    fifth bit of value l of sub-block s is bit s of high byte l."""
+    b = raw.reshape(-1, 176)
+    d, dmin = _f16(b, 0), _f16(b, 2)
+    sc, mn = _q4k_scale_min(b[:, 4:16])
+    qh = b[:, 16:48]
+    qs = b[:, 48:176].reshape(-1, 4, 32)
+    q = np.empty((b.shape[0], 8, 32), np.int32)
+    q[:, 0::2] = qs & 0xF
+    q[:, 1::2] = qs >> 4
+    q |= ((qh[:, None, :] >> np.arange(8, dtype=np.uint8)[None, :, None]) & 1).astype(np.int32) << 4
+    out = (d[:, :, None] * sc[:, :, None].astype(np.float32)) * q.astype(np.float32) - \
+        dmin[:, :, None] * mn[:, :, None].astype(np.float32)
+    return out.reshape(-1)
+
+
+def dequant_q2_k(raw: np.ndarray) -> np.ndarray:
+    """256 values in 16 groups of 16: 16 bytes of (4-bit scale | 4-bit min << 4), 64
+    bytes of 2-bit quants, f16 d, f16 dmin; v = d * scale * q - dmin * min.  Each half
+    of 128 values reads 32 quant bytes four times (shifts 0, 2, 4, 6); group g of a
+    half takes bytes 16 * (g % 2) .. + 15 at shift 2 * (g // 2)."""
+    b = raw.reshape(-1, 84)
+    scale, mn = (b[:, 0:16] & 0xF).astype(np.float32), (b[:, 0:16] >> 4).astype(np.float32)
+    d, dmin = _f16(b, 80), _f16(b, 82)
+    qs = b[:, 16:80].reshape(-1, 2, 2, 16)  # [nb, half, byte group, 16]
+    q = np.empty((b.shape[0], 2, 8, 16), np.float32)
+    for g in range(8):
+        q[:, :, g] = (qs[:, :, g % 2] >> (2 * (g // 2))) & 3
+    q = q.reshape(-1, 16, 16)
+    return (d[:, :, None] * scale[:, :, None] * q - dmin[:, :, None] * mn[:, :, None]).reshape(-1)
+
+
+def _q3k_scales(sc: np.ndarray) -> np.ndarray:
+    """[nb, 12] bytes -> [nb, 16] signed scales (6 bits each, biased by 32): the low
+    4 bits of scales 0-7 / 8-15 are the low / high nibbles of bytes 0-7, the top 2
+    bits come from bytes 8-11 (2 bits per scale, shifts 0, 2, 4, 6 for scale groups
+    of four)."""
+    lo = np.concatenate([sc[:, 0:8] & 0xF, sc[:, 0:8] >> 4], axis=1).astype(np.int32)
+    hi = np.empty((sc.shape[0], 16), np.int32)
+    for k in range(4):
+        hi[:, 4 * k:4 * k + 4] = (sc[:, 8:12] >> (2 * k)) & 3
+    return ((hi << 4) | lo) - 32
+
+
+def dequant_q3_k(raw: np.ndarray) -> np.ndarray:
+    """256 values in 16 groups of 16: 32 bytes of high-bit masks, 64 bytes of 2-bit
+    quants, 12 bytes of 6-bit scales, f16 d; v = d * scale * (q - 4 * (1 - h)) where q
+    is the 2-bit quant and h its mask bit.  Quant bytes are laid out as in Q2_K; the
+    mask bit of value l (0-31) in the j-th 32-value run of the block is bit j of mask
+    byte l."""
+    b = raw.reshape(-1, 110)
+    hm = b[:, 0:32]
+    qs = b[:, 32:96].reshape(-1, 2, 2, 16)
+    scale = _q3k_scales(b[:, 96:108]).astype(np.float32)
+    d = _f16(b, 108)
+    q = np.empty((b.shape[0], 2, 8, 16), np.int32)
+    for g in range(8):
+        q[:, :, g] = (qs[:, :, g % 2] >> (2 * (g // 2))) & 3
+    q = q.reshape(-1, 8, 32)  # 32-value runs: run r covers groups 2r, 2r+1
+    h = ((hm[:, None, :] >> np.arange(8, dtype=np.uint8)[None, :, None]) & 1).astype(np.int32)
+    q = (q - 4 * (1 - h)).reshape(-1, 16, 16).astype(np.float32)
+    return (d[:, :, None] * scale[:, :, None] * q).reshape(-1)
 
 
 # -------------------------------------------------------------- quantization
@@ -183,8 +295,17 @@ def tensor_to_numpy(t) -> np.ndarray:
         a = dequant_q4_k(raw.view(np.uint8))
     elif tt == Q.Q6_K:
         a = dequant_q6_k(raw.view(np.uint8))
+    elif tt in (Q.Q4_0, Q.Q4_1, Q.Q5_0, Q.Q5_1, Q.Q2_K, Q.Q3_K, Q.Q5_K):
+        a = {Q.Q4_0: dequant_q4_0, Q.Q4_1: dequant_q4_1, Q.Q5_0: dequant_q5_0, Q.Q5_1: dequant_q5_1,
+             Q.Q2_K: dequant_q2_k, Q.Q3_K: dequant_q3_k, Q.Q5_K: dequant_q5_k}[tt](raw.view(np.uint8))
     else:
-        raise ValueError(f"unsupported GGUF tensor type {tt.name} for {t.name}")
+        # remaining GGML formats (IQ*, TQ*, ...) through the gguf package's NumPy dequantizers
+        from gguf import quants
+
+        try:
+            a = quants.dequantize(raw, tt)
+        except NotImplementedError:
+            raise ValueError(f"unsupported GGUF tensor type {tt.name} for {t.name}") from None
     return a.reshape(shape)
 
 
@@ -402,7 +523,8 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
     attn_qkv and [gate; up] in ffn_up, no permutation).
     ``quant``: "f32", "f16", "q4_k" (2-D weights quantized, norms kept f32) or
     "q4_k_m" (Q4_K with Q6_K for output, attn_v and ffn_down, the mix of
-    llama.cpp's Q4_K_M preset applied to every layer) or "q8_0"."""
+    llama.cpp's Q4_K_M preset applied to every layer), "q8_0", or the legacy
+    32-value formats "q4_0" / "q5_1" (written with the gguf package's quantizer)."""
     from gguf import GGMLQuantizationType as Q
     from gguf import GGUFWriter
 
@@ -432,10 +554,11 @@ def write_gguf_model(path: str, cfg: ModelConfig, full_stream, quant: str = "f32
         six = quant == "q4_k_m" and (name == "output.weight" or name.endswith((".attn_v.weight", ".ffn_down.weight")))
         if six and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
             w.add_tensor(name, quantize_q6_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q6_K)
-        elif quant == "q8_0" and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
+        elif quant in ("q8_0", "q4_0", "q5_1") and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
             from gguf import quants
 
-            w.add_tensor(name, quants.quantize(np.ascontiguousarray(a), Q.Q8_0), raw_dtype=Q.Q8_0)
+            qt = {"q8_0": Q.Q8_0, "q4_0": Q.Q4_0, "q5_1": Q.Q5_1}[quant]
+            w.add_tensor(name, quants.quantize(np.ascontiguousarray(a), qt), raw_dtype=qt)
         elif quant in ("q4_k", "q4_k_m") and is_weight and a.ndim == 2 and a.shape[1] % QK_K == 0:
             # quantized tensors are handed over as [rows, bytes per row]
             w.add_tensor(name, quantize_q4_k(a.reshape(-1)).reshape(a.shape[0], -1), raw_dtype=Q.Q4_K)
