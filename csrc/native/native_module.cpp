@@ -12,6 +12,7 @@
 #include "shm.h"
 #include "text_index.h"
 #include "wasm.h"
+#include "work_queue.h"
 #include "wire.h"
 
 namespace py = pybind11;
@@ -396,6 +397,58 @@ PYBIND11_MODULE(_native, m) {
   m.attr("STATUS_ERR") = wire::STATUS_ERR;
   m.attr("STATUS_STREAM_CHUNK") = wire::STATUS_STREAM_CHUNK;
   m.attr("STATUS_STREAM_END") = wire::STATUS_STREAM_END;
+  py::class_<WorkQueue>(m, "WorkQueue", "bounded scheduler queue: overflow policy, micro-batch take, depth")
+      .def(py::init<size_t>(), py::arg("capacity"))
+      .def("put", [](WorkQueue& q, py::object job, int policy, bool block) {
+        PyObject* j = job.inc_ref().ptr();  // owned by the queue once accepted
+        PyObject* dropped = nullptr;
+        int r;
+        {
+          py::gil_scoped_release nogil;
+          r = q.put(j, policy, block, &dropped);
+        }
+        if (r != WorkQueue::kAccepted) Py_DECREF(j);
+        py::object d = dropped ? py::reinterpret_steal<py::object>(dropped) : py::object(py::none());
+        return py::make_tuple(r == WorkQueue::kAccepted, d);
+      }, py::arg("job"), py::arg("policy"), py::arg("block") = true,
+         "policy 0 block, 1 drop newest, 2 drop oldest -> (accepted, evicted job or None)")
+      .def("take", [](WorkQueue& q, size_t max_items, double delay_s) {
+        std::vector<PyObject*> v;
+        {
+          py::gil_scoped_release nogil;
+          v = q.take(max_items, delay_s);
+        }
+        py::list out;
+        for (PyObject* p : v) out.append(py::reinterpret_steal<py::object>(p));
+        return out;
+      })
+      .def("done", [](WorkQueue& q, size_t n) {
+        py::gil_scoped_release nogil;
+        q.done(n);
+      })
+      .def("close", [](WorkQueue& q) {
+        py::gil_scoped_release nogil;
+        q.close();
+      })
+      .def("depth", [](WorkQueue& q) {
+        py::gil_scoped_release nogil;
+        return q.depth();
+      })
+      .def_property_readonly("closed", [](WorkQueue& q) {
+        py::gil_scoped_release nogil;
+        return q.closed();
+      })
+      .def_property_readonly("capacity", &WorkQueue::capacity)
+      .def("drain", [](WorkQueue& q) {
+        std::vector<PyObject*> v;
+        {
+          py::gil_scoped_release nogil;
+          v = q.drain();
+        }
+        py::list out;
+        for (PyObject* p : v) out.append(py::reinterpret_steal<py::object>(p));
+        return out;
+      });
   py::class_<TokenChannel, std::shared_ptr<TokenChannel>>(m, "TokenChannel",
                                                           "token ids from the engine loop to a streaming connection")
       .def(py::init<>())

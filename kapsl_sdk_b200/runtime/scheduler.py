@@ -4,7 +4,7 @@
   (crates/kapsl-scheduler/src/request_metadata.rs:5-102): explicit priority 0,
   SLA < 250 ms, light work (input <= 500 KB, <= 1 GFLOP, or size x batch <= 2 MB)
   or batch <= 4 are latency critical.
-* ``WorkQueue`` / ``Executor`` — a bounded queue per worker; high-priority
+* ``WorkQueue`` / ``Executor`` — a bounded native queue per worker; high-priority
   requests run one at a time, low-priority ones are micro-batched up to
   ``max_micro_batch`` within ``queue_delay`` and sent to ``engine.infer_batch``
   (gpu_executor.rs:11-329).  Cancellation is checked before execution.
@@ -16,7 +16,6 @@
 """
 from __future__ import annotations
 
-import collections
 import concurrent.futures as cf
 import enum
 import threading
@@ -80,62 +79,40 @@ class _Job:
 
 
 class WorkQueue:
+    """Bounded queue of one executor worker.  The queueing itself (overflow policy,
+    micro-batch take, depth, close) is the native ``WorkQueue``
+    (csrc/native/work_queue.h), which waits with the GIL released; this wrapper
+    fails the futures of jobs the DROP_OLDEST policy evicts."""
+
+    _POLICY = {OverflowPolicy.BLOCK: 0, OverflowPolicy.DROP_NEWEST: 1, OverflowPolicy.DROP_OLDEST: 2}
+
     def __init__(self, capacity: int):
+        from .._ext import native
+
         self.capacity = capacity
-        self.items: "collections.deque[_Job]" = collections.deque()
-        self.cv = threading.Condition()
-        self.in_flight = 0
-        self.closed = False
+        self._q = native().WorkQueue(capacity)
+
+    @property
+    def closed(self) -> bool:
+        return self._q.closed
 
     def depth(self) -> int:
-        with self.cv:
-            return len(self.items) + self.in_flight
+        return self._q.depth()
 
     def put(self, job: _Job, policy: OverflowPolicy, block: bool = True) -> bool:
-        with self.cv:
-            while len(self.items) >= self.capacity:
-                if policy is OverflowPolicy.DROP_NEWEST or not block:
-                    return False
-                if policy is OverflowPolicy.DROP_OLDEST:
-                    old = self.items.popleft()
-                    old.future.set_exception(EngineError.overloaded("request dropped: queue overflow"))
-                    break
-                self.cv.wait(timeout=0.05)
-                if self.closed:
-                    return False
-            self.items.append(job)
-            self.cv.notify_all()
-            return True
+        ok, evicted = self._q.put(job, self._POLICY[policy], block)
+        if evicted is not None:
+            evicted.future.set_exception(EngineError.overloaded("request dropped: queue overflow"))
+        return ok
 
     def take(self, max_items: int, delay_s: float) -> list:
-        with self.cv:
-            while not self.items and not self.closed:
-                self.cv.wait(timeout=0.05)
-            if self.closed and not self.items:
-                return []
-            batch = [self.items.popleft()]
-            deadline = time.perf_counter() + delay_s
-            while len(batch) < max_items:
-                if self.items:
-                    batch.append(self.items.popleft())
-                    continue
-                left = deadline - time.perf_counter()
-                if left <= 0:
-                    break
-                self.cv.wait(timeout=left)
-            self.in_flight += len(batch)
-            self.cv.notify_all()
-            return batch
+        return self._q.take(max_items, delay_s)
 
     def done(self, n: int) -> None:
-        with self.cv:
-            self.in_flight -= n
-            self.cv.notify_all()
+        self._q.done(n)
 
     def close(self) -> None:
-        with self.cv:
-            self.closed = True
-            self.cv.notify_all()
+        self._q.close()  # the executor still runs what is queued, then stops
 
 
 class Executor:

@@ -368,3 +368,50 @@ def test_replica_with_failed_engine_is_routed_around():
     finally:
         for x in (bad, good):
             x.shutdown()
+
+
+def test_native_work_queue_under_concurrent_producers_and_consumers():
+    """The scheduler's native queue: 4 producers block on a capacity-8 queue while
+    2 consumers take micro-batches; every job comes out exactly once, batches never
+    exceed their size, and the depth returns to zero once the work is done."""
+    import threading
+
+    from kapsl_sdk_b200._ext import native
+
+    q = native().WorkQueue(8)
+    seen, sizes, lock = [], [], threading.Lock()
+
+    def produce(p):
+        for i in range(500):
+            ok, evicted = q.put((p, i), 0, True)
+            assert ok and evicted is None
+
+    def consume():
+        while True:
+            batch = q.take(4, 0.001)
+            if not batch:
+                if q.closed:
+                    return
+                continue
+            with lock:
+                seen.extend(batch)
+                sizes.append(len(batch))
+            q.done(len(batch))
+
+    cons = [threading.Thread(target=consume) for _ in range(2)]
+    prods = [threading.Thread(target=produce, args=(p,)) for p in range(4)]
+    [t.start() for t in cons + prods]
+    [t.join(60) for t in prods]
+    while q.depth():
+        time.sleep(0.01)
+    q.close()
+    [t.join(60) for t in cons]
+    assert sorted(seen) == [(p, i) for p in range(4) for i in range(500)]
+    assert max(sizes) <= 4 and q.depth() == 0
+    # overflow policies
+    q2 = native().WorkQueue(1)
+    assert q2.put("a", 0, True) == (True, None)
+    assert q2.put("b", 1, True) == (False, None)      # drop newest: rejected
+    assert q2.put("c", 0, False) == (False, None)     # non-blocking put on a full queue
+    assert q2.put("d", 2, True) == (True, "a")        # drop oldest: "a" evicted
+    assert q2.take(4, 0.0) == ["d"]
