@@ -36,6 +36,12 @@ constexpr int kThreads = 192;
 // to 144 bytes so the per-lane row writes and the row-piece reads spread over banks
 constexpr int kScatterRow = 144;
 constexpr int kScatterStage = 32 * kScatterRow;
+// 64-wide k slices per ring stage of the 2-SM kernel.  The MMA thread pays about
+// 100 cycles per stage for its full-barrier wait that the tensor pipe does not hide
+// (measured: 256 x 256 x 64 per pair takes ~620 cycles with one slice per stage and
+// ~525 with two, against 512 of MMA issue), so a stage carries two slices and the
+// wait is paid once per 8 MMAs.
+constexpr int KSUB2 = 2;
 
 using namespace tc;
 
@@ -403,8 +409,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   constexpr int A_HALF = 128 * BK * 2;       // 16 KiB: this CTA's 128 rows of the A tile
   constexpr int B_HALF = (BN / 2) * BK * 2;  // this CTA's BN/2 rows of the B tile
   constexpr int HALF_BYTES = A_HALF;
-  constexpr int STAGE_BYTES = A_HALF + B_HALF;
-  static_assert(STAGE_BYTES % 1024 == 0, "stages stay 1 KiB aligned (128-byte swizzle atoms)");
+  constexpr int ATOM_BYTES = A_HALF + B_HALF;  // one 64-wide k slice of both operands
+  constexpr int STAGE_BYTES = KSUB2 * ATOM_BYTES;
+  static_assert(ATOM_BYTES % 1024 == 0, "k slices stay 1 KiB aligned (128-byte swizzle atoms)");
   constexpr uint32_t TMEM_COLS = 512;        // two accumulators at columns 0 and 256
   constexpr uint32_t IDESC = idesc_bf16<256, BN>();
 
@@ -424,7 +431,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   const int nclusters = gridDim.x >> 1;
   const int m_tiles = (M + 255) / 256;
   const int n_tiles = (N + BN - 1) / BN;
-  const int kblocks = (K + BK - 1) / BK;
+  const int kslices = (K + BK - 1) / BK;
+  const int kblocks = (kslices + KSUB2 - 1) / KSUB2;  // stages per tile; the last may hold one slice
   const int units = m_tiles * n_tiles;
 
   if (threadIdx.x == 0) {
@@ -471,10 +479,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           uint8_t* sa = smem + (size_t)stage * STAGE_BYTES;
-          uint8_t* sb = sa + HALF_BYTES;
-          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * STAGE_BYTES);
-          tma_load_2d_2sm(sa, &tmap_a, &full_bar[stage], kb * BK, mt * 256 + (int)rank * 128);
-          tma_load_2d_2sm(sb, &tmap_b, &full_bar[stage], kb * BK, nt * BN + (int)rank * (BN / 2));
+          const int nsl = min(KSUB2, kslices - kb * KSUB2);
+          if (leader) mbar_arrive_expect_tx(&full_bar[stage], 2 * nsl * ATOM_BYTES);
+          for (int j = 0; j < nsl; ++j) {
+            const int kx = (kb * KSUB2 + j) * BK;
+            tma_load_2d_2sm(sa + j * ATOM_BYTES, &tmap_a, &full_bar[stage], kx, mt * 256 + (int)rank * 128);
+            tma_load_2d_2sm(sa + j * ATOM_BYTES + HALF_BYTES, &tmap_b, &full_bar[stage], kx,
+                            nt * BN + (int)rank * (BN / 2));
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -505,12 +517,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES);
-          const uint32_t sb = sa + HALF_BYTES;
+          const int nsl = min(KSUB2, kslices - kb * KSUB2);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            mma_bf16_2sm(d_tmem, smem_desc_sw128(sa + k * 32), smem_desc_sw128(sb + k * 32), IDESC,
-                         (kb > 0 || k > 0) ? 1u : 0u);
+          for (int j = 0; j < KSUB2; ++j) {
+            if (j < nsl) {
+              const uint32_t sa = smem_u32(smem + (size_t)stage * STAGE_BYTES + j * ATOM_BYTES);
+              const uint32_t sb = sa + HALF_BYTES;
+#pragma unroll
+              for (int k = 0; k < BK / 16; ++k)
+                mma_bf16_2sm(d_tmem, smem_desc_sw128(sa + k * 32), smem_desc_sw128(sb + k * 32), IDESC,
+                             (kb > 0 || j > 0 || k > 0) ? 1u : 0u);
+            }
+          }
           mma_commit_2sm_mc(&empty_bar[stage]);
           if (++stage == STAGES) {
             stage = 0;
@@ -625,20 +643,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   if (warp == 1) asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
 }
 
-// Stages of the 2-SM kernel for a tile width: six, or fewer when six do not fit next
+// Stages of the 2-SM kernel for a tile width: as many KSUB2-slice stages as fit next
 // to the 1 KiB alignment pad (and the scatter epilogue's staging) under the 227 KiB
-// dynamic shared-memory limit.  The deepest rings that fit (7-9 stages) measured no
-// faster: the mainloop is not bound by operand bytes in flight.
+// dynamic shared-memory limit, at most four (three for 256-wide tiles).
 constexpr int gemm2_fit(int bn, int epi) {
-  return (232448 - 1024 - 512 - (epi == 5 ? 4 * kScatterStage : 0)) / ((128 + bn / 2) * BK * 2);
+  return (232448 - 1024 - 512 - (epi == 5 ? 4 * kScatterStage : 0)) / (KSUB2 * (128 + bn / 2) * BK * 2);
 }
-constexpr int gemm2_stages(int bn, int epi = 0) { return gemm2_fit(bn, epi) < 6 ? gemm2_fit(bn, epi) : 6; }
+constexpr int gemm2_stages(int bn, int epi = 0) { return gemm2_fit(bn, epi) < 4 ? gemm2_fit(bn, epi) : 4; }
 
 template <int BN, int STAGES, int EPI, bool F32>
 void launch_2sm(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, const EpiArgs& ep, int grid,
                 int* err, cudaStream_t st) {
   auto kern = gemm2sm_kernel<BN, STAGES, EPI, F32>;
-  constexpr size_t smem = (size_t)STAGES * (128 + BN / 2) * BK * 2 + 1024 + (EPI == 5 ? 4 * kScatterStage : 0);
+  constexpr size_t smem = (size_t)STAGES * KSUB2 * (128 + BN / 2) * BK * 2 + 1024 + (EPI == 5 ? 4 * kScatterStage : 0);
   static std::atomic<uint64_t> attr_devs{0};
   ensure_smem_attr(attr_devs, kern, smem);
   launch_k(kern, grid, kThreads, smem, st, ta, tb, M, N, K, ep, err);
@@ -780,10 +797,10 @@ int launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C,
   {
     // 2-SM tiles (256 rows x BN) when 256x256 tiles fill at least 3/4 of the CTA pairs.
     // force_bn > 256 forces them with BN = force_bn - 256 (512: 256-wide tiles).
-    // BN is picked by a wave model: time ~ waves x (BN + 16), where a wave is one
-    // tile per CTA pair and +16 charges the per-k-block fixed cost of a narrower
-    // tile; e.g. N = 4608 at M = 2304 takes 192-wide tiles (216 tiles = 2.9 waves
-    // of 74 pairs) over 256-wide ones (162 tiles = 2.2 -> 3 waves).
+    // BN is picked by a wave model: time ~ waves, where a wave is one tile per CTA
+    // pair.  A tile's time does not depend on its width: a cta_group::2 MMA of
+    // M = 256, K = 16 measured ~128 cycles for N = 128, 192 and 256 alike, so the
+    // widest tile wins every tie and a narrower one only when it saves a wave.
     const int nclusters = sms / 2;
     const int m2 = (M + 255) / 256;
     const int units256 = m2 * ((N + 255) / 256);
@@ -794,7 +811,7 @@ int launch_gemm(const bf16* A, int64_t lda, const bf16* B, int64_t ldb, void* C,
         long best = -1;
         for (int cand : {256, 224, 192, 128}) {
           const int units = m2 * ((N + cand - 1) / cand);
-          const long cost = (long)((units + nclusters - 1) / nclusters) * (cand + 16);
+          const long cost = (long)((units + nclusters - 1) / nclusters);
           if (best < 0 || cost < best) {
             best = cost;
             bn2 = cand;

@@ -36,7 +36,7 @@ def _time(fn, iters: int = 20) -> float:
     return s.elapsed_time(e) / iters
 
 
-def bench_gemm(M, N, K, epi, timed):
+def bench_gemm(M, N, K, epi, timed, cublas=False):
     from .. import ops
 
     dev = torch.device("cuda", 0)
@@ -57,7 +57,11 @@ def bench_gemm(M, N, K, epi, timed):
         torch.cuda.synchronize()
         return {"kernel": "gemm", "M": M, "N": N, "K": K}
     ms = _time(fn)
-    return {"kernel": "gemm", "M": M, "N": N, "K": K, "epi": epi, "ms": ms, "tflops": 2 * M * N * K / ms / 1e9}
+    r = {"kernel": "gemm", "M": M, "N": N, "K": K, "epi": epi, "ms": ms, "tflops": 2 * M * N * K / ms / 1e9}
+    if cublas:  # the library GEMM of the same plain product, timed the same way
+        ms_lib = _time(lambda: torch.nn.functional.linear(a, b))
+        r.update(cublas_ms=ms_lib, cublas_tflops=2 * M * N * K / ms_lib / 1e9, ratio=ms_lib / ms)
+    return r
 
 
 def bench_decode(B, ctx, hq, hkv, timed):
@@ -203,9 +207,10 @@ def main(argv=None):
     p.add_argument("dims", nargs="+", type=int)
     p.add_argument("--epi", default="plain", choices=["plain", "bias", "residual", "swiglu"])
     p.add_argument("--time", action="store_true")
+    p.add_argument("--cublas", action="store_true", help="gemm: also time torch.nn.functional.linear")
     a = p.parse_args(argv)
     if a.what == "gemm":
-        r = bench_gemm(*a.dims[:3], a.epi, a.time)
+        r = bench_gemm(*a.dims[:3], a.epi, a.time, a.cublas)
     elif a.what == "gemm_q4k":
         r = bench_gemm_q4k(*a.dims[:3], a.time)
     elif a.what == "moe":

@@ -1,6 +1,5 @@
 """Numerics of every sm_100a kernel against plain fp32 PyTorch restatements."""
 import math
-import os
 import random
 
 import numpy as np
@@ -217,8 +216,6 @@ def test_prefill_attention(dev, Hq, Hkv):
         close(out[q0:q0 + n].view(n, Hq, D), exp, 0.02)
 
 
-@pytest.mark.skipif(os.environ.get("KAPSL_TEST_TC_PREFILL") != "1",
-                    reason="tcgen05 prefill attention has not run on a GPU yet; enable with KAPSL_TEST_TC_PREFILL=1")
 @pytest.mark.parametrize("Hq,Hkv", [(32, 8), (28, 4), (8, 8)])
 def test_prefill_attention_tc(dev, Hq, Hkv):
     """The tcgen05 prefill kernel against the fp32 statement (same cases as the mma.sync kernel)."""
