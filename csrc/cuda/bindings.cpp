@@ -563,6 +563,16 @@ void q4k_dequant(Tensor raw, Tensor out) {
   kapsl::launch_q4k_dequant(raw.data_ptr<uint8_t>(), out.numel(), bf(out), cur_stream());
 }
 
+void q4k_dequant_rows(Tensor raw, int64_t n, int64_t k, bool tiled, int64_t half, Tensor out) {
+  CHECK_DT(out, at::kBFloat16, "out");
+  TORCH_CHECK(raw.is_contiguous() && raw.scalar_type() == at::kByte && raw.numel() * 256 == n * k * 144,
+              "q4k_dequant_rows: raw must hold n * k / 256 blocks");
+  TORCH_CHECK(out.dim() == 2 && out.stride(1) == 1 && out.size(0) >= n && out.size(1) >= k, "q4k_dequant_rows: out");
+  const c10::cuda::CUDAGuard g(raw.device());
+  kapsl::launch_q4k_dequant_rows(raw.data_ptr<uint8_t>(), (int)n, (int)k, tiled, (int)half, bf(out), out.stride(0),
+                                 cur_stream());
+}
+
 void moe_route(Tensor x, Tensor wr, int64_t K, bool renorm, Tensor ids, Tensor wts) {
   CHECK_DT(x, at::kBFloat16, "x");
   CHECK_DT(wr, at::kBFloat16, "w_router");
@@ -694,6 +704,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_q4k", &gemm_q4k, "GEMM with GGUF Q4_K weights dequantized into TMEM inside the mainloop");
   m.def("q4k_quantize", &q4k_quantize, "bf16 -> GGUF Q4_K blocks");
   m.def("q4k_dequant", &q4k_dequant, "GGUF Q4_K blocks -> bf16");
+  m.def("q4k_dequant_rows", &q4k_dequant_rows, "GGUF Q4_K weight matrix -> bf16 rows (tile-major input, SwiGLU layout)");
   m.def("grouped_gemm", &grouped_gemm, "grouped (per-expert) tcgen05 GEMM driven by a device tile table");
   m.def("moe_route", &moe_route, "router logits + top-k + softmax weights");
   m.def("moe_permute", &moe_permute, "stable expert sort of the top-k assignments (padded segments)");

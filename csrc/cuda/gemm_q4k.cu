@@ -493,6 +493,51 @@ __global__ void q4k_dequant_kernel(const uint8_t* __restrict__ raw, int64_t nblo
   }
 }
 
+// Whole-matrix dequant for large-M products (the bf16 tcgen05 GEMM then runs at
+// its full rate; the fused kernel re-dequantizes every weight tile once per
+// 256-token tile).  One warp per (weight row, super-block): lane l makes weights
+// 8l..8l+7 from 8 consecutive quant bytes (low nibbles for the first 32 of each
+// 64-weight group, high for the next 32) and stores them as one 16-byte piece, so a
+// warp writes the 512-byte row segment in one coalesced store.  Same arithmetic
+// as q4k_dequant_kernel (d*sc and dmin*m rounded to fp32, then q*ds - dm, no
+// contraction), so both produce the same bf16 bits.  `tiled`: blocks in the GEMM's
+// tile-major order [n/128][k/256][128][144].  `half` > 0 writes gate/up rows
+// interleaved in 128-row blocks for the SwiGLU epilogue (row r of the first half
+// to 256*(r/128) + r%128, row half + r to 256*(r/128) + 128 + r%128).
+__global__ void q4k_dequant_rows_kernel(const uint8_t* __restrict__ raw, int n, int k, int tiled, int half,
+                                        bf16* __restrict__ out, int64_t ldo) {
+  griddep_entry();
+  const int nsb = k / QK;
+  const int64_t wid = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (wid >= (int64_t)n * nsb) return;
+  const int row = (int)(wid / nsb), sb = (int)(wid % nsb);
+  const uint8_t* blk = tiled ? raw + (((int64_t)(row >> 7) * nsb + sb) * 128 + (row & 127)) * QB
+                             : raw + ((int64_t)row * nsb + sb) * QB;
+  const int j = lane >> 2;  // sub-block of weights 8l..8l+7
+  const float d = half_bits_to_float(blk[0] | (blk[1] << 8));
+  const float dmin = half_bits_to_float(blk[2] | (blk[3] << 8));
+  int sc, mn;
+  scale_min(blk + 4, j, sc, mn);
+  const float ds = __fmul_rn(d, (float)sc), dm = __fmul_rn(dmin, (float)mn);
+  const int g = lane >> 3, m8 = lane & 7;
+  const uint2 q = *reinterpret_cast<const uint2*>(blk + 16 + 32 * g + 8 * (m8 & 3));
+  const int shift = (m8 & 4) ? 4 : 0;
+  uint32_t w[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t word = i < 2 ? q.x : q.y;
+    const int b0 = (2 * i) & 3;
+    const int q0 = (word >> (8 * b0 + shift)) & 0xF, q1 = (word >> (8 * (b0 + 1) + shift)) & 0xF;
+    const bf16 v0 = __float2bfloat16(__fsub_rn(__fmul_rn(ds, (float)q0), dm));
+    const bf16 v1 = __float2bfloat16(__fsub_rn(__fmul_rn(ds, (float)q1), dm));
+    w[i] = (uint32_t)__bfloat16_as_ushort(v0) | ((uint32_t)__bfloat16_as_ushort(v1) << 16);
+  }
+  int orow = row;
+  if (half > 0) orow = row < half ? 256 * (row >> 7) + (row & 127) : 256 * ((row - half) >> 7) + 128 + ((row - half) & 127);
+  *reinterpret_cast<uint4*>(out + (int64_t)orow * ldo + (int64_t)sb * QK + 8 * lane) = make_uint4(w[0], w[1], w[2], w[3]);
+}
+
 template <int TT, int EPI>
 void launch_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const Q4Args& a, int grid, int* err, cudaStream_t st) {
   auto kern = gemm_q4k_kernel<TT, EPI>;
@@ -566,6 +611,19 @@ void launch_q4k_quantize(const __nv_bfloat16* x, int64_t n, uint8_t* out, cudaSt
   const int64_t nb = n / q4k::QK;
   if (nb == 0) return;
   launch_k(q4k::q4k_quantize_kernel, (unsigned)((nb * 32 + 255) / 256), 256, 0, st, x, nb, out);
+  KAPSL_LAUNCH_CHECK();
+  note_launch();
+}
+
+void launch_q4k_dequant_rows(const uint8_t* raw, int n, int k, bool tiled, int half, __nv_bfloat16* out, int64_t ldo,
+                             cudaStream_t st) {
+  if (k % q4k::QK != 0 || (tiled && n % 128 != 0) || ldo % 8 != 0)
+    throw std::runtime_error("q4k_dequant_rows: k % 256, n % 128 (tiled) and ldo % 8 must be 0");
+  if (half > 0 && (half % 128 != 0 || 2 * half != n)) throw std::runtime_error("q4k_dequant_rows: bad gate/up split");
+  const int64_t warps = (int64_t)n * (k / q4k::QK);
+  if (warps == 0) return;
+  launch_k(q4k::q4k_dequant_rows_kernel, (unsigned)((warps + 7) / 8), 256, 0, st, raw, n, k, tiled ? 1 : 0, half, out,
+           ldo);
   KAPSL_LAUNCH_CHECK();
   note_launch();
 }

@@ -111,6 +111,10 @@ void launch_gemm_q4k(const __nv_bfloat16* X, int64_t ldx, const uint8_t* Wq, int
                      size_t workspace_bytes, int force_splits, bool tiled, int* err, cudaStream_t st);
 void launch_q4k_quantize(const __nv_bfloat16* x, int64_t n, uint8_t* out, cudaStream_t st);
 void launch_q4k_dequant(const uint8_t* raw, int64_t n, __nv_bfloat16* out, cudaStream_t st);
+// Q4_K weight matrix [n, k] (row-major or tile-major blocks) -> bf16 rows of pitch
+// ldo; half > 0 interleaves the two row halves in 128-row blocks (SwiGLU layout).
+void launch_q4k_dequant_rows(const uint8_t* raw, int n, int k, bool tiled, int half, __nv_bfloat16* out, int64_t ldo,
+                             cudaStream_t st);
 
 // mixture of experts (moe.cu)
 void launch_moe_route(const __nv_bfloat16* x, int64_t x_stride, const __nv_bfloat16* wr, int T, int d, int E, int K,

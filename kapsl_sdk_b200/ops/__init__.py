@@ -136,10 +136,39 @@ def linear(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor] =
     return out
 
 
+# Token count and weight rows from which a Q4_K product dequantizes the whole weight
+# matrix to bf16 (one memory-bound pass, ~20.5 bits moved per weight) and runs the
+# bf16 tcgen05 GEMM, instead of the fused kernel that dequantizes each weight tile
+# again for every 256-token tile.  Measured on B200 (ms, fused -> dequant + bf16):
+# 2048 x 8192 x 3584 0.135 -> 0.112, 2048 x 57344 x 8192 1.99 -> 1.69, 2048 x 7168 x 8192
+# 0.242 -> 0.231; the fused kernel stays ahead at 1024 tokens (0.126 vs 0.143) and on
+# narrow products (2048 x 1280 x 8192: 0.067 vs 0.100).
+Q4K_DEQUANT_MIN_M = 2048
+Q4K_DEQUANT_MIN_N = 4096
+
+_q4k_scratch: dict[int, torch.Tensor] = {}
+
+
+def _q4k_weight_scratch(device: torch.device, numel: int) -> Optional[torch.Tensor]:
+    """Per-device bf16 buffer for a dequantized weight matrix, grown on demand;
+    None when it would have to grow while a CUDA graph is being captured."""
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    buf = _q4k_scratch.get(idx)
+    if buf is None or buf.numel() < numel:
+        if torch.cuda.is_current_stream_capturing():
+            return None
+        buf = torch.empty(numel, dtype=torch.bfloat16, device=device)
+        _q4k_scratch[idx] = buf
+    return buf
+
+
 def _quant_linear(x, weight, bias, residual, swiglu, out, out_dtype, workspace) -> torch.Tensor:
     """``linear`` for a :class:`~kapsl_sdk_b200.quantization.QuantWeight` (Q4_K):
     the fused dequant GEMM, with residual fused; SwiGLU expects the gate and up
-    rows concatenated ([gate; up], not interleaved)."""
+    rows concatenated ([gate; up], not interleaved).  From ``Q4K_DEQUANT_MIN_M``
+    tokens and ``Q4K_DEQUANT_MIN_N`` weight rows the weight is dequantized into a scratch matrix (gate/up rows written
+    in the interleaved SwiGLU layout) and the bf16 GEMM runs with the same
+    epilogue."""
     if weight.fmt != "q4_k":
         raise ValueError(f"no fused kernel for weight format {weight.fmt!r}")
     if out_dtype != torch.bfloat16:
@@ -149,6 +178,20 @@ def _quant_linear(x, weight, bias, residual, swiglu, out, out_dtype, workspace) 
         workspace = _workspace(x.device)
     c = cuda_ops()
     err = error_buffer(x.device)
+    if M >= Q4K_DEQUANT_MIN_M and N >= Q4K_DEQUANT_MIN_N and (not weight.tiled or N % 128 == 0):
+        buf = _q4k_weight_scratch(x.device, N * weight.k)
+        if buf is not None:
+            w = buf[:N * weight.k].view(N, weight.k)
+            half = N // 2 if swiglu and N % 256 == 0 else 0
+            c.q4k_dequant_rows(weight.raw, N, weight.k, weight.tiled, half, w)
+            if swiglu and half:
+                return linear(x, w, swiglu=True, out=out, workspace=workspace)
+            if swiglu:
+                return silu_mul(linear(x, w, workspace=workspace), out)
+            y = linear(x, w, residual=residual, out=out, workspace=workspace)
+            if bias is not None:
+                y.add_(bias)
+            return y
     if swiglu:
         y = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
         c.gemm_q4k(x, weight.raw, y, weight.k, None, workspace, 0, weight.tiled, err)

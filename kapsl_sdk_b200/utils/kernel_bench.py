@@ -197,8 +197,17 @@ def bench_gemm_q4k(M, N, K, timed):
         return {"kernel": "gemm_q4k", "M": M, "N": N, "K": K}
     ms = _time(fn)
     ms_bf16 = _time(lambda: ops.linear(x, w, out=out))
+    saved = ops.Q4K_DEQUANT_MIN_M, ops.Q4K_DEQUANT_MIN_N
+    try:  # each path forced: fused dequant-in-mainloop kernel, and dequant pass + bf16 GEMM
+        ops.Q4K_DEQUANT_MIN_M = 1 << 30
+        ms_fused = _time(fn)
+        ops.Q4K_DEQUANT_MIN_M = ops.Q4K_DEQUANT_MIN_N = 0
+        ms_deq = _time(fn)
+    finally:
+        ops.Q4K_DEQUANT_MIN_M, ops.Q4K_DEQUANT_MIN_N = saved
     return {"kernel": "gemm_q4k", "M": M, "N": N, "K": K, "ms": ms, "q4k_GBps": qw.nbytes() / ms / 1e6,
-            "tflops": 2 * M * N * K / ms / 1e9, "bf16_weights_ms": ms_bf16}
+            "tflops": 2 * M * N * K / ms / 1e9, "bf16_weights_ms": ms_bf16, "fused_ms": ms_fused,
+            "dequant_then_bf16_ms": ms_deq}
 
 
 def main(argv=None):

@@ -110,3 +110,56 @@ def test_q4k_model_generates():
         prompts, SamplingParams.greedy(8, ignore_eos=True))
     agree = sum(int(a == b) for o1, o2 in zip(outs_q, outs_b) for a, b in zip(o1, o2))
     assert agree >= 14, (outs_q, outs_b)
+
+
+@pytest.mark.parametrize("tiled", [True, False])
+def test_dequant_rows_matches_dequantizer(tiled):
+    """The whole-matrix dequant of the large-token path gives the dequantizer's
+    bf16 bits, in row order and in the interleaved gate/up (SwiGLU) order."""
+    from kapsl_sdk_b200 import ops
+    from kapsl_sdk_b200._ext import cuda_ops
+    from kapsl_sdk_b200.quantization import quantize_q4_k
+
+    dev = torch.device("cuda", 0)
+    N, K = 512, 1536
+    qw = quantize_q4_k(_w(N, K, 11).to(dev), tiled=tiled)
+    ref = qw.dequantize()
+    got = torch.empty(N, K + 64, device=dev, dtype=torch.bfloat16)  # padded pitch
+    cuda_ops().q4k_dequant_rows(qw.raw, N, K, qw.tiled, 0, got)
+    assert torch.equal(got[:, :K], ref)
+    inter = torch.empty(N, K, device=dev, dtype=torch.bfloat16)
+    cuda_ops().q4k_dequant_rows(qw.raw, N, K, qw.tiled, N // 2, inter)
+    assert torch.equal(inter, ops.interleave_gate_up(ref[:N // 2], ref[N // 2:]))
+
+
+@pytest.mark.parametrize("M", [600, 1100])
+def test_gemm_q4k_large_token_path(M, monkeypatch):
+    """From Q4K_DEQUANT_MIN_M tokens the product runs as dequant + bf16 GEMM: plain,
+    residual and SwiGLU results agree with the fp32 reference and with the fused kernel."""
+    from kapsl_sdk_b200 import ops
+    from kapsl_sdk_b200.quantization import quantize_q4_k
+
+    dev = torch.device("cuda", 0)
+    N, K = 1024, 2048
+    qw = quantize_q4_k(_w(N, K, 5).to(dev))
+    x = (torch.randn(M, K, generator=torch.Generator().manual_seed(3)) * 0.5).to(dev, torch.bfloat16)
+    res = torch.randn(M, N, device=dev).to(torch.bfloat16)
+    wf = qw.dequantize().float()
+    ref = x.float() @ wf.T
+    gate, up = ref[:, :N // 2], ref[:, N // 2:]
+    ref_sw = gate * torch.sigmoid(gate) * up
+    outs = {}
+    monkeypatch.setattr(ops, "Q4K_DEQUANT_MIN_N", 0)
+    for thr in (M, 1 << 30):  # dequant path, then the fused kernel
+        monkeypatch.setattr(ops, "Q4K_DEQUANT_MIN_M", thr)
+        y = ops.linear(x, qw)
+        yr = ops.linear(x, qw, residual=res)
+        ys = ops.linear(x, qw, swiglu=True)
+        tol = 0.02 * ref.abs().max().item() + 1e-3
+        assert (y.float() - ref).abs().max().item() <= tol
+        assert (yr.float() - ref - res.float()).abs().max().item() <= tol + 1e-2
+        assert (ys.float() - ref_sw).abs().max().item() <= 0.02 * ref_sw.abs().max().item() + 1e-3
+        outs[thr] = y
+    # both paths multiply the same dequantized weights; they differ only in rounding
+    assert (outs[M].float() - outs[1 << 30].float()).abs().max().item() <= 0.02 * ref.abs().max().item()
+    assert ops.check_errors(dev) == 0
