@@ -563,6 +563,27 @@ void q4k_dequant(Tensor raw, Tensor out) {
   kapsl::launch_q4k_dequant(raw.data_ptr<uint8_t>(), out.numel(), bf(out), cur_stream());
 }
 
+void gemm_issue_probe(Tensor A, Tensor B, int64_t mode, int64_t ksub, int64_t stages, int64_t units, int64_t width,
+                      Tensor cycles, Tensor err) {
+  CHECK_DT(A, at::kBFloat16, "A");
+  CHECK_DT(B, at::kBFloat16, "B");
+  TORCH_CHECK(A.is_contiguous() && B.is_contiguous() && A.size(1) == B.size(1), "gemm_issue_probe: A [M, K], B [N, K]");
+  TORCH_CHECK(cycles.scalar_type() == at::kLong && err.scalar_type() == at::kInt, "gemm_issue_probe: int64 cycles, int32 err");
+  const c10::cuda::CUDAGuard g(A.device());
+  kapsl::launch_gemm_issue_probe(bf(A), bf(B), (int)A.size(0), (int)B.size(0), (int)A.size(1), (int)mode, (int)ksub,
+                                 (int)stages, (int)units, (int)width,
+                                 reinterpret_cast<long long*>(cycles.data_ptr<int64_t>()),
+                                 err.data_ptr<int>(), cur_stream());
+}
+
+void mma_rate_probe(int64_t n, int64_t iters, Tensor cycles, Tensor err) {
+  TORCH_CHECK(cycles.scalar_type() == at::kLong && err.scalar_type() == at::kInt && cycles.is_cuda(),
+              "mma_rate_probe: int64 cycles, int32 err");
+  const c10::cuda::CUDAGuard g(cycles.device());
+  kapsl::launch_mma_rate_probe((int)n, (int)iters, reinterpret_cast<long long*>(cycles.data_ptr<int64_t>()),
+                               err.data_ptr<int>(), cur_stream());
+}
+
 void q4k_dequant_rows(Tensor raw, int64_t n, int64_t k, bool tiled, int64_t half, Tensor out) {
   CHECK_DT(out, at::kBFloat16, "out");
   TORCH_CHECK(raw.is_contiguous() && raw.scalar_type() == at::kByte && raw.numel() * 256 == n * k * 144,
@@ -704,6 +725,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_q4k", &gemm_q4k, "GEMM with GGUF Q4_K weights dequantized into TMEM inside the mainloop");
   m.def("q4k_quantize", &q4k_quantize, "bf16 -> GGUF Q4_K blocks");
   m.def("q4k_dequant", &q4k_dequant, "GGUF Q4_K blocks -> bf16");
+  m.def("gemm_issue_probe", &gemm_issue_probe, "cycles per k slice of the 2-SM MMA thread (diagnostic)");
+  m.def("mma_rate_probe", &mma_rate_probe, "cycles per cta_group::1 MMA of width n (diagnostic)");
   m.def("q4k_dequant_rows", &q4k_dequant_rows, "GGUF Q4_K weight matrix -> bf16 rows (tile-major input, SwiGLU layout)");
   m.def("grouped_gemm", &grouped_gemm, "grouped (per-expert) tcgen05 GEMM driven by a device tile table");
   m.def("moe_route", &moe_route, "router logits + top-k + softmax weights");

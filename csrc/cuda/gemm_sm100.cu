@@ -458,9 +458,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_sh;
 
+  // Tile order: groups of G m-tiles, m fastest inside a group.  Up to 16 m-tiles
+  // (4096 rows) one group holds them all, so each weight tile is streamed from HBM
+  // once with every m-tile of a wave reusing it from L2; above that, groups of 8
+  // keep a wave's operand footprint near-square (8192^3: ~69 MB of A and B per
+  // wave instead of all of A, 128 MB, per wave).
+  const int group_m = m_tiles > 16 ? 8 : m_tiles;
   auto decode = [&](int u, int& mt, int& nt) {
-    mt = u % m_tiles;
-    nt = u / m_tiles;
+    const int g = u / (group_m * n_tiles), r = u % (group_m * n_tiles);
+    const int m0 = g * group_m;
+    const int gm = min(group_m, m_tiles - m0);
+    mt = m0 + r % gm;
+    nt = r / gm;
   };
 
   if (warp == 0) {

@@ -90,6 +90,11 @@ void launch_count_tokens(int32_t* counts, int V, const int32_t* rows, const int3
                          int32_t* occ_n, int occ_cap, cudaStream_t st);
 
 int gemm_num_sms();
+// Mainloop issue-cost probes (diagnostics): cycles per 64-wide k slice of the 2-SM
+// MMA thread under protocol mode 0..4, and cycles per cta_group::1 MMA of width n.
+void launch_gemm_issue_probe(const __nv_bfloat16* A, const __nv_bfloat16* B, int M, int N, int K, int mode, int ksub,
+                             int stages, int units, int width, long long* cycles, int* err, cudaStream_t st);
+void launch_mma_rate_probe(int n, int iters, long long* cycles, int* err, cudaStream_t st);
 // epi: 0 plain, 1 +bias, 2 +residual, 3 SwiGLU over interleaved gate/up (N % 256 == 0, C is [M, N/2]).
 // Returns the number of K splits used.  defer_splitk (plain epilogue only): when the GEMM splits K,
 // the fp32 partials stay in the workspace ([splits][M][N]) for the consumer to sum, and no reduce

@@ -36,7 +36,7 @@ def _time(fn, iters: int = 20) -> float:
     return s.elapsed_time(e) / iters
 
 
-def bench_gemm(M, N, K, epi, timed, cublas=False):
+def bench_gemm(M, N, K, epi, timed, cublas=False, iters=20):
     from .. import ops
 
     dev = torch.device("cuda", 0)
@@ -56,10 +56,11 @@ def bench_gemm(M, N, K, epi, timed, cublas=False):
             fn()
         torch.cuda.synchronize()
         return {"kernel": "gemm", "M": M, "N": N, "K": K}
-    ms = _time(fn)
-    r = {"kernel": "gemm", "M": M, "N": N, "K": K, "epi": epi, "ms": ms, "tflops": 2 * M * N * K / ms / 1e9}
+    ms = _time(fn, iters)
+    r = {"kernel": "gemm", "M": M, "N": N, "K": K, "epi": epi, "iters": iters, "ms": ms,
+         "tflops": 2 * M * N * K / ms / 1e9}
     if cublas:  # the library GEMM of the same plain product, timed the same way
-        ms_lib = _time(lambda: torch.nn.functional.linear(a, b))
+        ms_lib = _time(lambda: torch.nn.functional.linear(a, b), iters)
         r.update(cublas_ms=ms_lib, cublas_tflops=2 * M * N * K / ms_lib / 1e9, ratio=ms_lib / ms)
     return r
 
@@ -210,16 +211,49 @@ def bench_gemm_q4k(M, N, K, timed):
             "dequant_then_bf16_ms": ms_deq}
 
 
+def bench_gemm_issue(M, N, K, units=3):
+    """Cycles per 64-wide k slice spent by the 2-SM GEMM's MMA thread under each
+    piece of the pipeline protocol (MMA alone is 512), and cycles per
+    cta_group::1 MMA by width; read with clock64 on the issuing thread."""
+    from .._ext import cuda_ops
+    from .. import ops
+
+    dev = torch.device("cuda", 0)
+    a = torch.zeros(M, K, device=dev, dtype=torch.bfloat16)
+    b = torch.zeros(N, K, device=dev, dtype=torch.bfloat16)
+    cyc = torch.zeros(1, dtype=torch.int64, device=dev)
+    err = ops.error_buffer(dev)
+    rows = []
+    for name, mode, ksub, stages, width in [
+            ("mma only", 0, 1, 6, 256), ("mma only, N=192", 0, 1, 6, 192), ("mma only, N=128", 0, 1, 6, 128),
+            ("+ commit per slice", 1, 1, 6, 256), ("+ completed-barrier wait per slice", 2, 1, 6, 256),
+            ("ring, no loads", 3, 1, 6, 256), ("ring + TMA, 1 slice x 6 stages", 4, 1, 6, 256),
+            ("ring + TMA, 2 slices x 3 stages", 4, 2, 3, 256), ("ring + TMA, 2 slices x 2 stages", 4, 2, 2, 256)]:
+        for _ in range(2):  # the second run is the one read
+            cuda_ops().gemm_issue_probe(a, b, mode, ksub, stages, units, width, cyc, err)
+        torch.cuda.synchronize()
+        rows.append({"variant": name, "cycles_per_slice": int(cyc.item())})
+    for n in (64, 128, 256):
+        for _ in range(2):
+            cuda_ops().mma_rate_probe(n, 2000, cyc, err)
+        torch.cuda.synchronize()
+        rows.append({"variant": f"cta_group::1 M=128 N={n} K=16", "cycles_per_mma": int(cyc.item())})
+    return {"kernel": "gemm_issue", "M": M, "N": N, "K": K, "rows": rows, "errors": ops.check_errors(dev)}
+
+
 def main(argv=None):
     p = argparse.ArgumentParser()
-    p.add_argument("what", choices=["gemm", "gemm_q4k", "moe", "decode", "prefill", "sample"])
+    p.add_argument("what", choices=["gemm", "gemm_q4k", "gemm_issue", "moe", "decode", "prefill", "sample"])
     p.add_argument("dims", nargs="+", type=int)
     p.add_argument("--epi", default="plain", choices=["plain", "bias", "residual", "swiglu"])
     p.add_argument("--time", action="store_true")
     p.add_argument("--cublas", action="store_true", help="gemm: also time torch.nn.functional.linear")
+    p.add_argument("--iters", type=int, default=20, help="gemm: timed launches (200 reach the power cap)")
     a = p.parse_args(argv)
     if a.what == "gemm":
-        r = bench_gemm(*a.dims[:3], a.epi, a.time, a.cublas)
+        r = bench_gemm(*a.dims[:3], a.epi, a.time, a.cublas, a.iters)
+    elif a.what == "gemm_issue":
+        r = bench_gemm_issue(*a.dims[:4])
     elif a.what == "gemm_q4k":
         r = bench_gemm_q4k(*a.dims[:3], a.time)
     elif a.what == "moe":
