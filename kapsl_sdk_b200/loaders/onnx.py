@@ -6,12 +6,13 @@ fields; field numbers from the public onnx.proto) and provides:
 
 * ``read_model`` -> graph nodes, inputs/outputs, initializers as numpy arrays
   (raw_data or typed repeated fields; external data files next to the model);
-* ``OnnxGraph`` -> a PyTorch interpreter for an explicitly scoped op subset
-  (MatMul, Gemm, Add, Sub, Mul, Div, Relu, Sigmoid, Tanh, Softmax, Reshape,
-  Flatten, Transpose, Identity, Constant, Conv, MaxPool, AveragePool,
-  GlobalAveragePool, Concat, Gather, Unsqueeze, Squeeze, Cast, Erf, Sqrt, Pow,
-  ReduceMean, LayerNormalization, Shape, Slice).  Graphs using other ops are
-  rejected at load time with the op names listed;
+* ``OnnxGraph`` -> a PyTorch interpreter for the operators listed in
+  ``OnnxGraph.SUPPORTED`` (tensor math, convolution and pooling, shapes and
+  indexing, reductions, normalizations, quantize / dequantize and the
+  integer / QLinear products, Resize per the spec's coordinate modes,
+  NonMaxSuppression, control flow with subgraphs (If, Loop, Scan) and the
+  recurrent layers RNN / GRU / LSTM).  Graphs using other ops (checked through
+  every subgraph) are rejected at load time with the op names listed;
 * ``load_onnx_llm`` -> LLM weights from initializers named like a HF
   checkpoint (``model.layers.{i}.self_attn.q_proj.weight`` ...), the way an
   ONNX export of a decoder keeps them.
@@ -33,6 +34,14 @@ import torch
 _NP = {1: np.float32, 2: np.uint8, 3: np.int8, 4: np.uint16, 5: np.int16, 6: np.int32, 7: np.int64, 9: np.bool_,
        10: np.float16, 11: np.float64, 12: np.uint32, 13: np.uint64}
 BFLOAT16 = 16
+_TORCH_DT = {1: torch.float32, 2: torch.uint8, 3: torch.int8, 5: torch.int16, 6: torch.int32, 7: torch.int64,
+             9: torch.bool, 10: torch.float16, 11: torch.float64, 16: torch.bfloat16}
+
+
+def _saturate(v: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """Round-to-nearest-even values already rounded, clamped to an integer dtype's range."""
+    info = torch.iinfo(dtype)
+    return v.clamp(info.min, info.max).to(dtype)
 
 
 def _varint(b: bytes, i: int):
@@ -173,6 +182,8 @@ def _attr(b: bytes, base_dir):
             ints += [_signed64(x) for x in _packed_varints(v, wt)]
         elif f == 9:
             strs.append(v.decode(errors="replace"))
+        elif f == 6:  # GraphProto (If / Loop / Scan bodies)
+            val = _graph(v, base_dir)
         elif f == 20:
             kind = v
     if ints:
@@ -191,21 +202,10 @@ def _value_info_name(b: bytes) -> str:
     return ""
 
 
-def read_model(path: str) -> OnnxModel:
-    with open(path, "rb") as fh:
-        data = fh.read()
-    base = os.path.dirname(os.path.abspath(path))
-    graph = None
-    opset = 13
-    for f, _, v in _fields(data):
-        if f == 7:
-            graph = v
-        elif f == 8:
-            for ff, _, vv in _fields(v):
-                if ff == 2:
-                    opset = vv
-    if graph is None:
-        raise ValueError("ONNX file has no graph")
+def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
+    """GraphProto -> OnnxModel (nodes, declared inputs and outputs, initializers).
+    Subgraphs keep their initializer-backed inputs out of ``inputs`` like the
+    main graph; names they use without defining come from the enclosing scope."""
     nodes, inputs, outputs, inits = [], [], [], {}
     for f, _, v in _fields(graph):
         if f == 1:
@@ -234,6 +234,24 @@ def read_model(path: str) -> OnnxModel:
     return OnnxModel(nodes, inputs, outputs, inits, opset)
 
 
+def read_model(path: str) -> OnnxModel:
+    with open(path, "rb") as fh:
+        data = fh.read()
+    base = os.path.dirname(os.path.abspath(path))
+    graph = None
+    opset = 13
+    for f, _, v in _fields(data):
+        if f == 7:
+            graph = v
+        elif f == 8:
+            for ff, _, vv in _fields(v):
+                if ff == 2:
+                    opset = vv
+    if graph is None:
+        raise ValueError("ONNX file has no graph")
+    return _graph(graph, base, opset)
+
+
 # ---------------------------------------------------------- interpreter
 def _conv_pads(a, nd):
     p = a.get("pads") or [0] * (2 * nd)
@@ -260,29 +278,128 @@ class OnnxGraph:
                  "GatherElements", "ScatterElements", "ScatterND", "GatherND", "OneHot", "NonZero",
                  "DepthToSpace", "SpaceToDepth", "QuantizeLinear", "DequantizeLinear", "GroupNormalization",
                  "LpNormalization", "ReduceLogSumExp", "ReduceSumSquare", "ReduceL1", "Mish", "Celu",
-                 "ThresholdedRelu", "Shrink", "Compress", "BitShift"}
+                 "ThresholdedRelu", "Shrink", "Compress", "BitShift",
+                 # control flow, recurrent layers
+                 "If", "Loop", "Scan", "RNN", "GRU", "LSTM",
+                 # trigonometric, quantized, detection, sampling, normalization, sequences
+                 "Tan", "Asin", "Acos", "Atan", "Sinh", "Cosh", "Asinh", "Acosh", "Atanh", "IsInf", "CastLike",
+                 "EyeLike", "Hardmax", "LRN", "MeanVarianceNormalization", "RMSNormalization", "ReverseSequence",
+                 "Unique", "Det", "LpPool", "GlobalLpPool", "MatMulInteger", "QLinearMatMul", "ConvInteger",
+                 "QLinearConv", "NonMaxSuppression", "GridSample", "RandomNormal", "RandomUniform",
+                 "RandomNormalLike", "RandomUniformLike", "Bernoulli", "Upsample"}
+
+    CONTROL = {"If", "Loop", "Scan"}
+    # a Loop whose trip count and condition are both absent runs until this many
+    # iterations, then fails (the spec's unbounded loop)
+    MAX_LOOP_ITERS = 1 << 24
 
     def __init__(self, model: OnnxModel, device="cpu"):
-        bad = sorted({n.op for n in model.nodes} - self.SUPPORTED)
+        bad = sorted(self.ops_used(model) - self.SUPPORTED)
         if bad:
             raise ValueError(f"unsupported ONNX ops: {', '.join(bad)}")
         self.m = model
         self.device = torch.device(device)
         self.consts = {k: torch.from_numpy(np.ascontiguousarray(v)).to(self.device) for k, v in model.initializers.items()}
+        self._sub_consts: dict[int, dict] = {}
+
+    @staticmethod
+    def ops_used(model: OnnxModel) -> set:
+        """Operator types of a graph and of every subgraph it holds."""
+        ops = set()
+        for n in model.nodes:
+            ops.add(n.op)
+            for v in n.attrs.values():
+                if isinstance(v, OnnxModel):
+                    ops |= OnnxGraph.ops_used(v)
+        return ops
 
     def run(self, feeds: dict) -> dict:
         env = dict(self.consts)
         for k, v in feeds.items():
             env[k] = v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v))
             env[k] = env[k].to(self.device)
-        for n in self.m.nodes:
+        self._exec(self.m, env)
+        return {o: env[o] for o in self.m.outputs}
+
+    def _exec(self, m: OnnxModel, env: dict) -> None:
+        for n in m.nodes:
             args = [env[i] if i else None for i in n.inputs]
-            outs = self._op(n, args)
+            outs = self._control(n, args, env) if n.op in self.CONTROL else self._op(n, args)
             if not isinstance(outs, (list, tuple)):
                 outs = [outs]
             for name, val in zip(n.outputs, outs):
-                env[name] = val
-        return {o: env[o] for o in self.m.outputs}
+                if name:
+                    env[name] = val
+
+    def _sub(self, g: OnnxModel, env: dict, bind: dict) -> list:
+        """Runs subgraph ``g`` in a child scope of ``env`` (outer names stay visible,
+        the subgraph's own initializers and bound inputs shadow them)."""
+        consts = self._sub_consts.get(id(g))
+        if consts is None:
+            consts = {k: torch.from_numpy(np.ascontiguousarray(v)).to(self.device) for k, v in g.initializers.items()}
+            self._sub_consts[id(g)] = consts
+        scope = dict(env)
+        scope.update(consts)
+        scope.update(bind)
+        self._exec(g, scope)
+        return [scope[o] for o in g.outputs]
+
+    def _control(self, n: Node, x: list, env: dict):
+        """If / Loop / Scan (ONNX control flow, opset 11+ / 13+ / 9+ semantics)."""
+        a, op = n.attrs, n.op
+        if op == "If":
+            branch = a["then_branch"] if bool(x[0].reshape(-1)[0]) else a["else_branch"]
+            return self._sub(branch, env, {})
+        body = a["body"]
+        if op == "Loop":
+            trip = int(x[0].reshape(-1)[0]) if len(x) > 0 and x[0] is not None else None
+            keep = bool(x[1].reshape(-1)[0]) if len(x) > 1 and x[1] is not None else True
+            vs = list(x[2:])
+            nv = len(vs)
+            scans: list = []
+            i = 0
+            while (trip is None or i < trip) and keep:
+                if trip is None and (len(x) < 2 or x[1] is None) and i >= self.MAX_LOOP_ITERS:
+                    raise ValueError("Loop without trip count or condition did not end")
+                bind = {body.inputs[0]: torch.tensor(i, dtype=torch.int64, device=self.device),
+                        body.inputs[1]: torch.tensor(keep, device=self.device)}
+                bind.update({name: v for name, v in zip(body.inputs[2:], vs)})
+                out = self._sub(body, env, bind)
+                keep = bool(out[0].reshape(-1)[0])
+                vs = out[1:1 + nv]
+                if not scans:
+                    scans = [[] for _ in out[1 + nv:]]
+                for acc, v in zip(scans, out[1 + nv:]):
+                    acc.append(v)
+                i += 1
+            n_scan = len(body.outputs) - 1 - nv
+            stacked = [torch.stack(acc) for acc in scans] if scans else \
+                [torch.empty(0, device=self.device) for _ in range(n_scan)]
+            return vs + stacked
+        # Scan
+        m = a["num_scan_inputs"]
+        ns = len(x) - m
+        states, ins = list(x[:ns]), list(x[ns:])
+        in_axes = [ax % t.dim() for ax, t in zip(a.get("scan_input_axes") or [0] * m, ins)]
+        in_dirs = a.get("scan_input_directions") or [0] * m
+        T = ins[0].shape[in_axes[0]]
+        k = len(body.outputs) - ns
+        acc = [[] for _ in range(k)]
+        for t in range(T):
+            slices = [v.select(ax, T - 1 - t if d else t) for v, ax, d in zip(ins, in_axes, in_dirs)]
+            out = self._sub(body, env, {name: v for name, v in zip(body.inputs, states + slices)})
+            states = out[:ns]
+            for lst, v in zip(acc, out[ns:]):
+                lst.append(v)
+        out_axes = a.get("scan_output_axes") or [0] * k
+        out_dirs = a.get("scan_output_directions") or [0] * k
+        res = []
+        for lst, ax, d in zip(acc, out_axes, out_dirs):
+            if d:
+                lst = lst[::-1]
+            r = lst[0].dim() + 1
+            res.append(torch.stack(lst, dim=ax % r))
+        return states + res
 
     def _op(self, n: Node, x: list):
         a, op = n.attrs, n.op
@@ -484,21 +601,18 @@ class OnnxGraph:
         if op == "Size":
             return torch.tensor(x[0].numel(), dtype=torch.int64, device=self.device)
         if op == "Resize":
-            mode = a.get("mode", "nearest")
-            mode = mode.decode() if isinstance(mode, bytes) else mode
-            sizes = x[3] if len(x) > 3 and x[3] is not None and x[3].numel() else None
-            scales = x[2] if len(x) > 2 and x[2] is not None and x[2].numel() else None
-            if sizes is not None:
-                out = [int(v) for v in sizes.tolist()][2:]
-                kw = {"size": out}
-            else:
-                kw = {"scale_factor": [float(v) for v in scales.tolist()][2:]}
-            if mode == "nearest":
-                return F.interpolate(x[0], mode="nearest", **kw)
-            ctm = a.get("coordinate_transformation_mode", "half_pixel")
-            ctm = ctm.decode() if isinstance(ctm, bytes) else ctm
-            lin = {3: "linear", 4: "bilinear", 5: "trilinear"}[x[0].dim()]
-            return F.interpolate(x[0], mode=lin, align_corners=ctm == "align_corners", **kw)
+            def sa(k, d):
+                v = a.get(k, d)
+                return v.decode() if isinstance(v, bytes) else v
+
+            def opt(i):
+                return x[i] if len(x) > i and x[i] is not None and x[i].numel() else None
+
+            return self._resize(x[0], opt(1), opt(2), opt(3), sa("mode", "nearest"),
+                                sa("coordinate_transformation_mode", "half_pixel"),
+                                sa("nearest_mode", "round_prefer_floor"), a.get("cubic_coeff_a", -0.75),
+                                a.get("exclude_outside", 0), a.get("extrapolation_value", 0.0), a.get("axes"),
+                                sa("keep_aspect_ratio_policy", "stretch"), a.get("antialias", 0))
         if op == "Trilu":
             k = int(x[1].item()) if len(x) > 1 and x[1] is not None else 0
             return torch.triu(x[0], k) if a.get("upper", 1) else torch.tril(x[0], k)
@@ -680,7 +794,443 @@ class OnnxGraph:
             d = a["direction"]
             d = d.decode() if isinstance(d, bytes) else d
             return x[0] << x[1] if d == "LEFT" else x[0] >> x[1]
+        if op in ("RNN", "GRU", "LSTM"):
+            return self._recurrent(op, x, a)
+        return self._op_late(n, x)
+
+    @staticmethod
+    def _rnn_act(name: str, alpha, beta):
+        """ONNX recurrent-layer activation by name (alpha / beta as the spec defines them)."""
+        name = name.decode() if isinstance(name, bytes) else name
+        F = torch.nn.functional
+        k = name.lower()
+        if k == "sigmoid":
+            return torch.sigmoid
+        if k == "tanh":
+            return torch.tanh
+        if k == "relu":
+            return torch.relu
+        if k == "affine":
+            return lambda v: (1.0 if alpha is None else alpha) * v + (0.0 if beta is None else beta)
+        if k == "leakyrelu":
+            return lambda v: F.leaky_relu(v, 0.01 if alpha is None else alpha)
+        if k == "thresholdedrelu":
+            return lambda v: torch.where(v > (1.0 if alpha is None else alpha), v, torch.zeros_like(v))
+        if k == "scaledtanh":
+            return lambda v: (1.0 if alpha is None else alpha) * torch.tanh((1.0 if beta is None else beta) * v)
+        if k == "hardsigmoid":
+            return lambda v: torch.clamp((0.2 if alpha is None else alpha) * v + (0.5 if beta is None else beta), 0, 1)
+        if k == "elu":
+            return lambda v: F.elu(v, 1.0 if alpha is None else alpha)
+        if k == "softsign":
+            return F.softsign
+        if k == "softplus":
+            return F.softplus
+        raise ValueError(f"unsupported recurrent activation {name}")
+
+    def _recurrent(self, op: str, x: list, a: dict):
+        """RNN / GRU / LSTM over [seq, batch, input] (layout 0) or [batch, seq, input]
+        (layout 1): gate orders i, o, f, c (LSTM) and z, r, h (GRU), optional
+        biases, per-batch sequence lengths (steps past a length leave Y zero and
+        Y_h at the last valid state; the reverse direction walks each sequence's
+        valid part backwards), initial states, LSTM peepholes and input_forget,
+        GRU linear_before_reset, clip, forward / reverse / bidirectional."""
+        def arg(i):
+            return x[i] if len(x) > i and x[i] is not None else None
+
+        layout = a.get("layout", 0)
+        X, W, R, B, lens, h0 = x[0], x[1], x[2], arg(3), arg(4), arg(5)
+        c0, P = (arg(6), arg(7)) if op == "LSTM" else (None, None)
+        if layout:
+            X = X.transpose(0, 1)
+            h0 = h0.transpose(0, 1) if h0 is not None else None
+            c0 = c0.transpose(0, 1) if c0 is not None else None
+        direction = a.get("direction", "forward")
+        direction = direction.decode() if isinstance(direction, bytes) else direction
+        nd = 2 if direction == "bidirectional" else 1
+        H = a["hidden_size"]
+        G = {"RNN": 1, "GRU": 3, "LSTM": 4}[op]
+        seq, batch = X.shape[0], X.shape[1]
+        default_acts = {"RNN": ["Tanh"], "GRU": ["Sigmoid", "Tanh"], "LSTM": ["Sigmoid", "Tanh", "Tanh"]}[op]
+        names = a.get("activations") or default_acts * nd
+        if len(names) == len(default_acts) and nd == 2:
+            names = list(names) * 2
+        alphas, betas = a.get("activation_alpha") or [], a.get("activation_beta") or []
+        acts = [self._rnn_act(nm, alphas[i] if i < len(alphas) else None, betas[i] if i < len(betas) else None)
+                for i, nm in enumerate(names)]
+        clip = a.get("clip")
+        lens = lens.long() if lens is not None else torch.full((batch,), seq, dtype=torch.long, device=X.device)
+        Y = X.new_zeros(seq, nd, batch, H)
+        Yh = X.new_zeros(nd, batch, H)
+        Yc = X.new_zeros(nd, batch, H)
+        bidx = torch.arange(batch, device=X.device)
+        for d in range(nd):
+            rev = direction == "reverse" or d == 1
+            f_, g_, h_ = (acts[d * len(default_acts) + j] for j in range(len(default_acts))) if op == "LSTM" else \
+                ((acts[d * len(default_acts)], acts[d * len(default_acts) + 1], None) if op == "GRU" else
+                 (acts[d], None, None))
+            Wd, Rd = W[d], R[d]
+            Bd = B[d] if B is not None else X.new_zeros(2 * G * H)
+            Wb, Rb = Bd[:G * H], Bd[G * H:]
+            h = h0[d] if h0 is not None else X.new_zeros(batch, H)
+            c = c0[d] if c0 is not None else X.new_zeros(batch, H)
+
+            def cl(v):
+                return v.clamp(-clip, clip) if clip is not None else v
+
+            for step in range(seq):
+                valid = step < lens
+                t = (lens - 1 - step).clamp(min=0) if rev else torch.full_like(lens, step)
+                xt = X[t, bidx]
+                if op == "RNN":
+                    hn = f_(cl(xt @ Wd.T + Wb + h @ Rd.T + Rb))
+                elif op == "GRU":
+                    gx = xt @ Wd.T + Wb
+                    Rz, Rr, Rh = Rd[:H], Rd[H:2 * H], Rd[2 * H:]
+                    z = f_(cl(gx[:, :H] + h @ Rz.T + Rb[:H]))
+                    r = f_(cl(gx[:, H:2 * H] + h @ Rr.T + Rb[H:2 * H]))
+                    if a.get("linear_before_reset", 0):
+                        hh = g_(cl(gx[:, 2 * H:] + r * (h @ Rh.T + Rb[2 * H:])))
+                    else:
+                        hh = g_(cl(gx[:, 2 * H:] + (r * h) @ Rh.T + Rb[2 * H:]))
+                    hn = (1 - z) * hh + z * h
+                else:
+                    gs = xt @ Wd.T + Wb + h @ Rd.T + Rb
+                    gi, go, gf, gc = gs[:, :H], gs[:, H:2 * H], gs[:, 2 * H:3 * H], gs[:, 3 * H:]
+                    if P is not None:
+                        gi = gi + P[d][:H] * c
+                        gf = gf + P[d][2 * H:] * c
+                    i_ = f_(cl(gi))
+                    fg = 1 - i_ if a.get("input_forget", 0) else f_(cl(gf))
+                    cn = fg * c + i_ * g_(cl(gc))
+                    if P is not None:
+                        go = go + P[d][H:2 * H] * cn
+                    hn = f_(cl(go)) * h_(cn)
+                    c = torch.where(valid[:, None], cn, c)
+                h = torch.where(valid[:, None], hn, h)
+                Y[t[valid], d, bidx[valid]] = hn[valid]
+            Yh[d] = h
+            Yc[d] = c
+        if layout:
+            outs = [Y.permute(2, 0, 1, 3), Yh.transpose(0, 1), Yc.transpose(0, 1)]
+        else:
+            outs = [Y, Yh, Yc]
+        return outs if op == "LSTM" else outs[:2]
+
+    def _op_late(self, n: Node, x: list):
+        """Trigonometric / hyperbolic functions, integer and quantized-linear
+        products and convolutions, detection (NonMaxSuppression), sampling
+        (GridSample), normalizations and sequence utilities (opset 13-23 semantics)."""
+        a, op = n.attrs, n.op
+        F = torch.nn.functional
+
+        def sattr(k, d):
+            v = a.get(k, d)
+            return v.decode() if isinstance(v, bytes) else v
+
+        trig = {"Tan": torch.tan, "Asin": torch.asin, "Acos": torch.acos, "Atan": torch.atan, "Sinh": torch.sinh,
+                "Cosh": torch.cosh, "Asinh": torch.asinh, "Acosh": torch.acosh, "Atanh": torch.atanh}
+        if op in trig:
+            return trig[op](x[0])
+        if op == "IsInf":
+            v = x[0]
+            pos = torch.isposinf(v) if a.get("detect_positive", 1) else torch.zeros_like(v, dtype=torch.bool)
+            neg = torch.isneginf(v) if a.get("detect_negative", 1) else torch.zeros_like(v, dtype=torch.bool)
+            return pos | neg
+        if op == "CastLike":
+            return x[0].to(x[1].dtype)
+        if op == "EyeLike":
+            dt = _TORCH_DT.get(a["dtype"], x[0].dtype) if "dtype" in a else x[0].dtype
+            r, c = x[0].shape
+            rows = torch.arange(r, device=x[0].device)
+            cols = rows + a.get("k", 0)
+            ok = (cols >= 0) & (cols < c)
+            y = torch.zeros(r, c, dtype=torch.float64, device=x[0].device)
+            y[rows[ok], cols[ok]] = 1
+            return y.to(dt)
+        if op == "Hardmax":
+            ax = a.get("axis", -1)
+            idx = x[0].argmax(dim=ax, keepdim=True)
+            return torch.zeros_like(x[0]).scatter(ax, idx, 1.0)
+        if op == "LRN":
+            size = a["size"]
+            al, be, bias = a.get("alpha", 1e-4), a.get("beta", 0.75), a.get("bias", 1.0)
+            lo, hi = (size - 1) // 2, size - 1 - (size - 1) // 2
+            sq = F.pad(x[0] * x[0], [0, 0] * (x[0].dim() - 2) + [lo, hi])
+            C = x[0].shape[1]
+            acc = sum(sq[:, i:i + C] for i in range(size))
+            return x[0] / (bias + al / size * acc) ** be
+        if op == "MeanVarianceNormalization":
+            axes = tuple(a.get("axes") or [0, 2, 3])
+            mean = x[0].mean(dim=axes, keepdim=True)
+            var = (x[0] * x[0]).mean(dim=axes, keepdim=True) - mean * mean
+            return (x[0] - mean) / (torch.sqrt(var) + 1e-9)
+        if op == "RMSNormalization":
+            ax = a.get("axis", -1) % x[0].dim()
+            xf = x[0].float()
+            ms = (xf * xf).mean(dim=tuple(range(ax, x[0].dim())), keepdim=True)
+            return (xf * torch.rsqrt(ms + a.get("epsilon", 1e-5)) * x[1].float()).to(x[0].dtype)
+        if op == "ReverseSequence":
+            bax, tax = a.get("batch_axis", 1), a.get("time_axis", 0)
+            y = x[0].clone()
+            for b, L in enumerate(x[1].tolist()):
+                src = x[0].select(bax, b)
+                t_ax = tax if tax < bax else tax - 1
+                y.select(bax, b).narrow(t_ax, 0, L).copy_(src.narrow(t_ax, 0, L).flip(t_ax))
+            return y
+        if op == "Unique":
+            v = x[0].cpu().numpy()
+            ax = a.get("axis")
+            vals, first, inv, cnt = np.unique(v if ax is not None else v.reshape(-1), return_index=True,
+                                               return_inverse=True, return_counts=True, axis=ax)
+            inv = inv.reshape(-1)
+            if not a.get("sorted", 1):  # order of first occurrence
+                order = np.argsort(first, kind="stable")
+                rank = np.empty_like(order)
+                rank[order] = np.arange(len(order))
+                vals = np.take(vals, order, axis=ax if ax is not None else 0)
+                first, cnt, inv = first[order], cnt[order], rank[inv]
+            dev = x[0].device
+            return [torch.from_numpy(np.ascontiguousarray(vals)).to(dev),
+                    torch.from_numpy(first.astype(np.int64)).to(dev), torch.from_numpy(inv.astype(np.int64)).to(dev),
+                    torch.from_numpy(cnt.astype(np.int64)).to(dev)]
+        if op == "Det":
+            return torch.linalg.det(x[0])
+        if op in ("LpPool", "GlobalLpPool"):
+            p = a.get("p", 2)
+            v = x[0].abs() ** p
+            nd = x[0].dim() - 2
+            if op == "GlobalLpPool":
+                return v.sum(dim=tuple(range(2, x[0].dim())), keepdim=True) ** (1.0 / p)
+            k = a["kernel_shape"]
+            lo, hi = _conv_pads(a, nd)
+            if any(lo + hi):
+                v = F.pad(v, [q for pair in zip(reversed(lo), reversed(hi)) for q in pair])
+            s = a.get("strides") or [1] * nd
+            pooled = getattr(F, f"avg_pool{nd}d")(v, k, s) * float(np.prod(k))
+            return pooled ** (1.0 / p)
+        if op == "MatMulInteger":
+            A = x[0].to(torch.int64)
+            B = x[1].to(torch.int64)
+            if len(x) > 2 and x[2] is not None:
+                az = x[2].to(torch.int64)
+                A = A - (az.reshape(-1, 1) if az.dim() == 1 and az.numel() > 1 else az)
+            if len(x) > 3 and x[3] is not None:
+                B = B - x[3].to(torch.int64)
+            return torch.matmul(A.double(), B.double()).round().to(torch.int32)
+        if op == "QLinearMatMul":
+            A = x[0].double() - x[2].double()
+            B = x[3].double() - x[5].double()
+            real = torch.matmul(A * x[1].double(), B * x[4].double())
+            return _saturate(torch.round(real / x[6].double()) + x[7].double(), x[7].dtype)
+        if op in ("ConvInteger", "QLinearConv"):
+            if op == "ConvInteger":
+                xi, w = x[0].double(), x[1].double()
+                xz = x[2].double() if len(x) > 2 and x[2] is not None else 0.0
+                wz = x[3].double() if len(x) > 3 and x[3] is not None else None
+            else:
+                xi, w = x[0].double(), x[3].double()
+                xz, wz = x[2].double(), x[5].double()
+            nd = w.dim() - 2
+            if wz is not None:
+                w = w - (wz.reshape(-1, *([1] * (nd + 1))) if wz.dim() == 1 and wz.numel() > 1 else wz)
+            xi = xi - xz
+            lo, hi = _conv_pads(a, nd)
+            if any(lo + hi):  # zero-point padding: padded input equals the zero point, i.e. 0 after the shift
+                xi = F.pad(xi, [q for pair in zip(reversed(lo), reversed(hi)) for q in pair])
+            fn = {1: F.conv1d, 2: F.conv2d, 3: F.conv3d}[nd]
+            acc = fn(xi, w, None, stride=a.get("strides") or 1, dilation=a.get("dilations") or 1,
+                     groups=a.get("group", 1))
+            if op == "ConvInteger":
+                return acc.round().to(torch.int32)
+            if len(x) > 8 and x[8] is not None:
+                acc = acc + x[8].double().reshape(1, -1, *([1] * nd))
+            ws = x[4].double()
+            scale = x[1].double() * (ws.reshape(1, -1, *([1] * nd)) if ws.numel() > 1 else ws)
+            return _saturate(torch.round(acc * scale / x[6].double()) + x[7].double(), x[7].dtype)
+        if op == "NonMaxSuppression":
+            return self._nms(x, a)
+        if op == "GridSample":
+            mode = sattr("mode", "bilinear")
+            mode = {"linear": "bilinear", "cubic": "bicubic"}.get(mode, mode)
+            return F.grid_sample(x[0], x[1], mode=mode, padding_mode=sattr("padding_mode", "zeros"),
+                                 align_corners=bool(a.get("align_corners", 0)))
+        if op in ("RandomNormal", "RandomUniform", "RandomNormalLike", "RandomUniformLike", "Bernoulli"):
+            g = torch.Generator(device="cpu")
+            if "seed" in a:
+                g.manual_seed(int(a["seed"]))
+            else:
+                g.seed()
+            if op == "Bernoulli":
+                y = torch.bernoulli(x[0].detach().cpu().double(), generator=g)
+                return y.to(_TORCH_DT.get(a.get("dtype"), x[0].dtype)).to(x[0].device)
+            shape = list(x[0].shape) if op.endswith("Like") else a["shape"]
+            dt = _TORCH_DT.get(a.get("dtype"), x[0].dtype if op.endswith("Like") else torch.float32)
+            if "Normal" in op:
+                y = torch.randn(shape, generator=g, dtype=torch.float64) * a.get("scale", 1.0) + a.get("mean", 0.0)
+            else:
+                lo, hi = a.get("low", 0.0), a.get("high", 1.0)
+                y = torch.rand(shape, generator=g, dtype=torch.float64) * (hi - lo) + lo
+            return y.to(dt).to(self.device)
+        if op == "Upsample":
+            return self._resize(x[0], None, x[1], None, sattr("mode", "nearest"), "asymmetric", "floor", -0.75, 0, 0.0)
         raise ValueError(f"unsupported ONNX op {op}")
+
+    @staticmethod
+    def _resize_weights(n_in: int, n_out: int, scale: float, mode: str, ctm: str, nearest_mode: str, cubic_a: float,
+                        exclude_outside: int, roi: tuple) -> tuple:
+        """[n_out, n_in] interpolation matrix of one axis (ONNX Resize): output index
+        -> input coordinate by the coordinate transformation mode, then nearest
+        (rounded by nearest_mode), linear (2 taps) or cubic (4 taps, Keys kernel with
+        coefficient a) weights on clamped neighbour indices (edge values beyond the
+        border; exclude_outside zeroes and renormalises the outside taps).  Returns
+        the matrix and a mask of rows outside a tf_crop_and_resize window."""
+        Wm = np.zeros((n_out, n_in), np.float64)
+        outside = np.zeros(n_out, bool)
+        for o in range(n_out):
+            if ctm == "half_pixel":
+                xo = (o + 0.5) / scale - 0.5
+            elif ctm == "pytorch_half_pixel":
+                xo = (o + 0.5) / scale - 0.5 if n_out > 1 else 0.0
+            elif ctm == "align_corners":
+                xo = 0.0 if n_out == 1 else o * (n_in - 1) / (n_out - 1)
+            elif ctm == "asymmetric":
+                xo = o / scale
+            elif ctm == "half_pixel_symmetric":
+                adj = n_out / (scale * n_in)
+                xo = n_in / 2 * (1 - adj) + (o + 0.5) / scale - 0.5
+            elif ctm == "tf_crop_and_resize":
+                st, en = roi
+                xo = st * (n_in - 1) + o * (en - st) * (n_in - 1) / (n_out - 1) if n_out > 1 else \
+                    0.5 * (st + en) * (n_in - 1)
+                if xo < 0 or xo > n_in - 1:
+                    outside[o] = True
+                    continue
+            else:
+                raise ValueError(f"unsupported coordinate_transformation_mode {ctm}")
+            base = int(np.floor(xo))
+            r = xo - base
+            if mode == "nearest":
+                if nearest_mode == "round_prefer_floor":
+                    pick = base if r <= 0.5 else base + 1
+                elif nearest_mode == "round_prefer_ceil":
+                    pick = base if r < 0.5 else base + 1
+                elif nearest_mode == "floor":
+                    pick = base
+                elif nearest_mode == "ceil":
+                    pick = base if r == 0 else base + 1
+                else:
+                    raise ValueError(f"unsupported nearest_mode {nearest_mode}")
+                Wm[o, min(max(pick, 0), n_in - 1)] = 1.0
+                continue
+            if mode == "linear":
+                taps, coef = [base, base + 1], [1 - r, r]
+            elif mode == "cubic":
+                A = cubic_a
+
+                def k(t):  # Keys (1981) cubic convolution kernel
+                    t = abs(t)
+                    if t <= 1:
+                        return ((A + 2) * t - (A + 3)) * t * t + 1
+                    if t < 2:
+                        return ((A * t - 5 * A) * t + 8 * A) * t - 4 * A
+                    return 0.0
+                taps = [base - 1, base, base + 1, base + 2]
+                coef = [k(r + 1), k(r), k(1 - r), k(2 - r)]
+            else:
+                raise ValueError(f"unsupported Resize mode {mode}")
+            if exclude_outside:
+                coef = [c if 0 <= t < n_in else 0.0 for t, c in zip(taps, coef)]
+                tot = sum(coef)
+                coef = [c / tot for c in coef] if tot else coef
+            for t, c in zip(taps, coef):
+                Wm[o, min(max(t, 0), n_in - 1)] += c
+        return Wm, outside
+
+    def _resize(self, X, roi, scales, sizes, mode, ctm, nearest_mode, cubic_a, exclude_outside, extrapolation,
+                axes=None, keep_aspect="stretch", antialias=0):
+        """ONNX Resize (and Upsample) as one interpolation matrix per resized axis."""
+        nd = X.dim()
+        axes = [ax % nd for ax in axes] if axes else list(range(nd))
+        ins = [X.shape[ax] for ax in axes]
+        if sizes is not None:
+            want = [int(v) for v in sizes.tolist()]
+            sc = [w / i for w, i in zip(want, ins)]
+            if keep_aspect != "stretch":
+                pick = min(sc) if keep_aspect == "not_larger" else max(sc)
+                sc = [pick] * len(sc)
+                want = [int(np.floor(pick * i + 0.5)) for i in ins]
+        else:
+            sc = [float(v) for v in scales.tolist()]
+            want = None
+        rois = [(0.0, 1.0)] * len(axes)
+        if roi is not None:
+            rv = [float(v) for v in roi.tolist()]
+            h = len(rv) // 2
+            rois = list(zip(rv[:h], rv[h:]))
+            if h == nd and len(axes) != nd:
+                rois = [rois[ax] for ax in axes]
+        if want is None:
+            want = [int(np.floor(i * s * ((en - st) if ctm == "tf_crop_and_resize" else 1.0)))
+                    for i, s, (st, en) in zip(ins, sc, rois)]
+        y = X
+        for ax, n_in, n_out, s, r in zip(axes, ins, want, sc, rois):
+            if n_in == n_out and s == 1.0 and ctm != "tf_crop_and_resize":
+                continue
+            if antialias and s < 1 and mode != "nearest":
+                raise ValueError("Resize with antialias on a downscaled axis is not supported")
+            Wm, outside = self._resize_weights(n_in, n_out, s, mode, ctm, nearest_mode, cubic_a, exclude_outside, r)
+            moved = y.movedim(ax, -1)
+            if mode == "nearest" and not outside.any():
+                idx = torch.from_numpy(Wm.argmax(1)).to(y.device)
+                out = moved.index_select(-1, idx)
+            else:
+                out = (moved.double() @ torch.from_numpy(Wm.T).to(y.device)).to(y.dtype)
+                if outside.any():
+                    out[..., torch.from_numpy(outside).to(y.device)] = extrapolation
+            y = out.movedim(-1, ax)
+        return y
+
+    def _nms(self, x: list, a: dict) -> torch.Tensor:
+        """NonMaxSuppression: per batch and class, boxes above score_threshold in
+        descending score order, each kept unless its IoU with a kept box exceeds
+        iou_threshold, at most max_output_boxes_per_class; rows (batch, class, box)."""
+        boxes, scores = x[0].double().cpu(), x[1].double().cpu()
+        mx = int(x[2].reshape(-1)[0]) if len(x) > 2 and x[2] is not None and x[2].numel() else 0
+        iou_t = float(x[3].reshape(-1)[0]) if len(x) > 3 and x[3] is not None and x[3].numel() else 0.0
+        sc_t = float(x[4].reshape(-1)[0]) if len(x) > 4 and x[4] is not None and x[4].numel() else None
+        if a.get("center_point_box", 0):
+            cx, cy, w, h = boxes.unbind(-1)
+            y1, x1, y2, x2 = cy - h / 2, cx - w / 2, cy + h / 2, cx + w / 2
+        else:
+            ya, xa, yb, xb = boxes.unbind(-1)
+            y1, y2 = torch.minimum(ya, yb), torch.maximum(ya, yb)
+            x1, x2 = torch.minimum(xa, xb), torch.maximum(xa, xb)
+        area = (y2 - y1) * (x2 - x1)
+        out = []
+        for b in range(scores.shape[0]):
+            for c in range(scores.shape[1]):
+                sc = scores[b, c]
+                order = sorted(range(sc.numel()), key=lambda i: -float(sc[i]))
+                kept: list = []
+                for i in order:
+                    if len(kept) >= mx:
+                        break
+                    if sc_t is not None and not float(sc[i]) > sc_t:
+                        break
+                    ok = True
+                    for j in kept:
+                        ih = min(float(y2[b, i]), float(y2[b, j])) - max(float(y1[b, i]), float(y1[b, j]))
+                        iw = min(float(x2[b, i]), float(x2[b, j])) - max(float(x1[b, i]), float(x1[b, j]))
+                        inter = max(ih, 0.0) * max(iw, 0.0)
+                        union = float(area[b, i]) + float(area[b, j]) - inter
+                        if union > 0 and inter / union > iou_t:
+                            ok = False
+                            break
+                    if ok:
+                        kept.append(i)
+                out += [[b, c, i] for i in kept]
+        return torch.tensor(out, dtype=torch.int64, device=x[0].device).reshape(-1, 3)
 
 
 # ------------------------------------------------------------------ LLMs
@@ -755,7 +1305,13 @@ def encode_tensor(name: str, a: np.ndarray) -> bytes:
 
 
 def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, opset: int = 13) -> bytes:
-    """Minimal ModelProto writer (for tests and synthetic exports)."""
+    """Minimal ModelProto writer (for tests and synthetic exports).  A node
+    attribute given as an :class:`OnnxModel` is written as a subgraph."""
+    g = _encode_graph(nodes, inputs, outputs, initializers)
+    return _key(1, 0) + _enc_varint(8) + _ld(2, b"kapsl") + _ld(7, g) + _ld(8, _key(2, 0) + _enc_varint(opset))
+
+
+def _encode_graph(nodes: list, inputs: list, outputs: list, initializers: dict) -> bytes:
     g = b""
     for n in nodes:
         nb = b"".join(_ld(1, i.encode()) for i in n.inputs) + b"".join(_ld(2, o.encode()) for o in n.outputs)
@@ -772,6 +1328,8 @@ def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, o
                 ab += _ld(4, v.encode()) + _key(20, 0) + _enc_varint(3)
             elif isinstance(v, np.ndarray):
                 ab += _ld(5, encode_tensor(k, v)) + _key(20, 0) + _enc_varint(4)
+            elif isinstance(v, OnnxModel):
+                ab += _ld(6, _encode_graph(v.nodes, v.inputs, v.outputs, v.initializers)) + _key(20, 0) + _enc_varint(5)
             nb += _ld(5, ab)
         g += _ld(1, nb)
     g += _ld(2, b"graph")
@@ -781,5 +1339,4 @@ def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, o
         g += _ld(11, _ld(1, i.encode()))
     for o in outputs:
         g += _ld(12, _ld(1, o.encode()))
-    m = _key(1, 0) + _enc_varint(8) + _ld(2, b"kapsl") + _ld(7, g) + _ld(8, _key(2, 0) + _enc_varint(opset))
-    return m
+    return g
