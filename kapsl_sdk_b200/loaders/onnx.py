@@ -286,7 +286,11 @@ class OnnxGraph:
                  "EyeLike", "Hardmax", "LRN", "MeanVarianceNormalization", "RMSNormalization", "ReverseSequence",
                  "Unique", "Det", "LpPool", "GlobalLpPool", "MatMulInteger", "QLinearMatMul", "ConvInteger",
                  "QLinearConv", "NonMaxSuppression", "GridSample", "RandomNormal", "RandomUniform",
-                 "RandomNormalLike", "RandomUniformLike", "Bernoulli", "Upsample"}
+                 "RandomNormalLike", "RandomUniformLike", "Bernoulli", "Upsample",
+                 # transformer graphs (standard opset 23 and the com.microsoft fused ops)
+                 "Attention", "RotaryEmbedding", "SkipLayerNormalization", "SimplifiedLayerNormalization",
+                 "SkipSimplifiedLayerNormalization", "FastGelu", "BiasGelu", "QuickGelu", "BiasAdd",
+                 "MultiHeadAttention", "MatMulNBits"}
 
     CONTROL = {"If", "Loop", "Scan"}
     # a Loop whose trip count and condition are both absent runs until this many
@@ -1074,7 +1078,201 @@ class OnnxGraph:
             return y.to(dt).to(self.device)
         if op == "Upsample":
             return self._resize(x[0], None, x[1], None, sattr("mode", "nearest"), "asymmetric", "floor", -0.75, 0, 0.0)
+        return self._op_transformer(n, x)
+
+    def _op_transformer(self, n: Node, x: list):
+        """Operators of exported transformer graphs: the standard Attention and
+        RotaryEmbedding (opset 23) and the com.microsoft fused ops that ONNX Runtime's
+        transformer optimizer writes (SkipLayerNormalization, SimplifiedLayerNormalization,
+        SkipSimplifiedLayerNormalization, FastGelu, BiasGelu, QuickGelu, BiasAdd,
+        MultiHeadAttention, MatMulNBits block-quantized weights)."""
+        a, op = n.attrs, n.op
+        F = torch.nn.functional
+
+        def opt(i):
+            return x[i] if len(x) > i and x[i] is not None else None
+
+        if op == "Attention":
+            return self._attention(x, a)
+        if op == "RotaryEmbedding":
+            X, cos, sin, pos = x[0], x[1], x[2], opt(3)
+            three = X.dim() == 3
+            if three:  # [B, S, hidden] -> [B, H, S, D]
+                B_, S_, hid = X.shape
+                H_ = a["num_heads"]
+                X = X.reshape(B_, S_, H_, hid // H_).transpose(1, 2)
+            if pos is not None:
+                cos, sin = cos[pos.long()], sin[pos.long()]
+            cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)  # [B, 1, S, rot/2]
+            rot = a.get("rotary_embedding_dim", 0) or X.shape[-1]
+            xr, rest = X[..., :rot], X[..., rot:]
+            if a.get("interleaved", 0):
+                x1, x2 = xr[..., 0::2], xr[..., 1::2]
+                o1, o2 = x1 * cos - x2 * sin, x2 * cos + x1 * sin
+                y = torch.stack([o1, o2], -1).reshape(xr.shape)
+            else:
+                x1, x2 = xr[..., :rot // 2], xr[..., rot // 2:]
+                y = torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
+            y = torch.cat([y, rest], -1)
+            return y.transpose(1, 2).reshape(x[0].shape) if three else y
+        if op in ("SkipLayerNormalization", "SkipSimplifiedLayerNormalization"):
+            s_ = x[0] + x[1]
+            bias = opt(4) if op == "SkipLayerNormalization" else opt(3)
+            if bias is not None:
+                s_ = s_ + bias
+            eps = a.get("epsilon", 1e-12)
+            sf = s_.float()
+            if op == "SkipLayerNormalization":
+                mean = sf.mean(-1, keepdim=True)
+                var = ((sf - mean) ** 2).mean(-1, keepdim=True)
+                inv = torch.rsqrt(var + eps)
+                y = (sf - mean) * inv * x[2].float()
+                if opt(3) is not None:
+                    y = y + x[3].float()
+            else:
+                mean = torch.zeros_like(sf[..., :1])
+                inv = torch.rsqrt((sf * sf).mean(-1, keepdim=True) + eps)
+                y = sf * inv * x[2].float()
+            return [y.to(x[0].dtype), mean, inv, s_]
+        if op == "SimplifiedLayerNormalization":
+            ax = a.get("axis", -1) % x[0].dim()
+            xf = x[0].float()
+            inv = torch.rsqrt((xf * xf).mean(dim=tuple(range(ax, x[0].dim())), keepdim=True) + a.get("epsilon", 1e-5))
+            return [(xf * inv * x[1].float()).to(x[0].dtype), inv]
+        if op == "FastGelu":
+            v = x[0] + x[1] if opt(1) is not None else x[0]
+            return F.gelu(v, approximate="tanh")
+        if op == "BiasGelu":
+            return F.gelu(x[0] + x[1])
+        if op == "QuickGelu":
+            return x[0] * torch.sigmoid(a.get("alpha", 1.702) * x[0])
+        if op == "BiasAdd":
+            return x[0] + x[1] + x[2]
+        if op == "MultiHeadAttention":
+            return self._mha(x, a)
+        if op == "MatMulNBits":
+            w = self._nbits_weight(x, a)
+            y = torch.matmul(x[0], w.to(x[0].dtype).T)
+            return y + x[5] if opt(5) is not None else y
         raise ValueError(f"unsupported ONNX op {op}")
+
+    @staticmethod
+    def _nbits_weight(x: list, a: dict) -> torch.Tensor:
+        """MatMulNBits weights [N, K]: `bits`-bit codes packed low bits first in each
+        byte, blocks of `block_size` along K with one scale each, zero point per
+        block (packed codes or the scales' type; 2^(bits-1) when absent)."""
+        K, N, bits, bs = a["K"], a["N"], a.get("bits", 4), a["block_size"]
+        if bits not in (2, 4, 8):
+            raise ValueError(f"MatMulNBits with {bits}-bit codes is not supported")
+        nb = (K + bs - 1) // bs
+        raw = x[1].reshape(N, nb, -1).to(torch.int64)
+        per = 8 // bits
+        shifts = torch.arange(per, device=raw.device) * bits
+        q = ((raw.unsqueeze(-1) >> shifts) & ((1 << bits) - 1)).reshape(N, nb, -1)[:, :, :bs]
+        scales = x[2].reshape(N, nb).float()
+        zp = x[3] if len(x) > 3 and x[3] is not None else None
+        if zp is None:
+            z = torch.full((N, nb), float(1 << (bits - 1)), device=raw.device)
+        elif zp.dtype == torch.uint8:
+            zb = zp.reshape(N, -1).to(torch.int64)
+            z = ((zb.unsqueeze(-1) >> shifts) & ((1 << bits) - 1)).reshape(N, -1)[:, :nb].float()
+        else:
+            z = zp.reshape(N, nb).float()
+        w = (q.float() - z.unsqueeze(-1)) * scales.unsqueeze(-1)
+        return w.reshape(N, nb * bs)[:, :K]
+
+    def _attention(self, x: list, a: dict):
+        """Attention (opset 23): 3-D [B, S, heads * D] or 4-D [B, heads, S, D] Q/K/V,
+        grouped KV heads, past key / value concatenated (present outputs), boolean
+        (True attends) or additive mask, is_causal (upper-left aligned lower
+        triangle), scale (default 1/sqrt(D)), softcap; qk_matmul_output_mode picks
+        the 4th output (0 scores, 1 + mask, 2 + softcap, 3 softmax)."""
+        Q, K, V = x[0], x[1], x[2]
+        mask = x[3] if len(x) > 3 and x[3] is not None else None
+        pk = x[4] if len(x) > 4 and x[4] is not None else None
+        pv = x[5] if len(x) > 5 and x[5] is not None else None
+        three = Q.dim() == 3
+        if three:
+            hq, hk = a["q_num_heads"], a["kv_num_heads"]
+            B_ = Q.shape[0]
+            Q = Q.reshape(B_, Q.shape[1], hq, -1).transpose(1, 2)
+            K = K.reshape(B_, K.shape[1], hk, -1).transpose(1, 2)
+            V = V.reshape(B_, V.shape[1], hk, -1).transpose(1, 2)
+        if pk is not None:
+            K = torch.cat([pk, K], 2)
+        if pv is not None:
+            V = torch.cat([pv, V], 2)
+        present_k, present_v = K, V
+        hq, hk = Q.shape[1], K.shape[1]
+        if hq != hk:
+            K = K.repeat_interleave(hq // hk, 1)
+            V = V.repeat_interleave(hq // hk, 1)
+        scale = a.get("scale", 1.0 / np.sqrt(Q.shape[-1]))
+        qf, kf, vf = Q.float(), K.float(), V.float()
+        scores = qf @ kf.transpose(-1, -2) * scale
+        L, S = scores.shape[-2], scores.shape[-1]
+        bias = torch.zeros(L, S, device=scores.device)
+        if a.get("is_causal", 0):
+            bias = bias.masked_fill(~torch.ones(L, S, dtype=torch.bool, device=scores.device).tril(), float("-inf"))
+        if mask is not None:
+            bias = bias + (torch.zeros(mask.shape, device=scores.device).masked_fill(~mask, float("-inf"))
+                           if mask.dtype == torch.bool else mask.float())
+        masked = scores + bias
+        sc = a.get("softcap", 0.0)
+        capped = sc * torch.tanh(masked / sc) if sc and sc > 0 else masked
+        probs = torch.softmax(capped, -1)
+        y = (probs @ vf).to(x[0].dtype)
+        if three:
+            y = y.transpose(1, 2).reshape(y.shape[0], L, -1)
+        mode = a.get("qk_matmul_output_mode", 0)
+        qk = [scores, masked, capped, probs][mode]
+        return [y, present_k, present_v, qk]
+
+    def _mha(self, x: list, a: dict):
+        """com.microsoft MultiHeadAttention over [B, S, heads * D] query / key / value:
+        optional packed bias (q, k, v), key_padding_mask ([B] valid lengths or [B, L]
+        0 / 1), additive attention_bias, past key / value ([B, heads, P, D]),
+        unidirectional (causal with the past offset), scale (default 1/sqrt(D));
+        masked positions get mask_filter_value."""
+        def opt(i):
+            return x[i] if len(x) > i and x[i] is not None else None
+
+        H = a["num_heads"]
+        q, k, v = x[0], opt(1), opt(2)
+        bias, kpm, ab, pk, pv = opt(3), opt(4), opt(5), opt(6), opt(7)
+        B_, S_, hq = q.shape
+        if bias is not None:
+            dq = hq
+            dk = k.shape[-1]
+            q, k, v = q + bias[:dq], k + bias[dq:dq + dk], v + bias[dq + dk:]
+        D = hq // H
+
+        def heads(t):
+            return t.reshape(B_, t.shape[1], H, -1).transpose(1, 2)
+
+        qh, kh, vh = heads(q), heads(k), heads(v)
+        if pk is not None:
+            kh = torch.cat([pk, kh], 2)
+            vh = torch.cat([pv, vh], 2)
+        Lk = kh.shape[2]
+        scale = a.get("scale", 0.0) or 1.0 / np.sqrt(D)
+        scores = qh.float() @ kh.float().transpose(-1, -2) * scale
+        fill = a.get("mask_filter_value", -10000.0)
+        keep = torch.ones(B_, 1, S_, Lk, dtype=torch.bool, device=q.device)
+        if kpm is not None:
+            if kpm.dim() == 1:
+                keep = keep & (torch.arange(Lk, device=q.device)[None, :] < kpm.long()[:, None])[:, None, None, :]
+            else:
+                keep = keep & (kpm != 0)[:, None, None, :]
+        if a.get("unidirectional", 0):
+            past = Lk - S_
+            keep = keep & (torch.arange(Lk, device=q.device)[None, :] <=
+                           torch.arange(S_, device=q.device)[:, None] + past)
+        scores = torch.where(keep, scores, torch.full_like(scores, fill))
+        if ab is not None:
+            scores = scores + ab.float()
+        y = torch.softmax(scores, -1) @ vh.float()
+        return [y.transpose(1, 2).reshape(B_, S_, -1).to(q.dtype), kh, vh]
 
     @staticmethod
     def _resize_weights(n_in: int, n_out: int, scale: float, mode: str, ctm: str, nearest_mode: str, cubic_a: float,
