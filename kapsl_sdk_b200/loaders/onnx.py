@@ -22,6 +22,7 @@ Reference: the reference serves any ONNX graph through ONNX Runtime
 """
 from __future__ import annotations
 
+import collections
 import os
 import struct
 from dataclasses import dataclass, field
@@ -36,6 +37,12 @@ _NP = {1: np.float32, 2: np.uint8, 3: np.int8, 4: np.uint16, 5: np.int16, 6: np.
 BFLOAT16 = 16
 _TORCH_DT = {1: torch.float32, 2: torch.uint8, 3: torch.int8, 5: torch.int16, 6: torch.int32, 7: torch.int64,
              9: torch.bool, 10: torch.float16, 11: torch.float64, 16: torch.bfloat16}
+
+
+def _contig(v: np.ndarray) -> np.ndarray:
+    """C-contiguous view or copy that keeps 0-d arrays 0-d (np.ascontiguousarray makes them 1-d)."""
+    v = np.asarray(v)
+    return v if v.flags.c_contiguous else np.ascontiguousarray(v)
 
 
 def _saturate(v: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
@@ -297,14 +304,60 @@ class OnnxGraph:
     # iterations, then fails (the spec's unbounded loop)
     MAX_LOOP_ITERS = 1 << 24
 
-    def __init__(self, model: OnnxModel, device="cpu"):
+    # ops whose inputs after the first are read on the host (shapes, axes, counts):
+    # those inputs stay where they are, so shape arithmetic never syncs the device
+    HOST_ARG_OPS = {"Reshape", "Expand", "Tile", "Slice", "Range", "ConstantOfShape", "Resize", "Upsample", "Pad",
+                    "OneHot", "Split", "Unsqueeze", "Squeeze", "ReduceMean", "ReduceSum", "ReduceMax", "ReduceMin",
+                    "ReduceProd", "ReduceL2", "ReduceL1", "ReduceLogSumExp", "ReduceSumSquare", "TopK", "Trilu",
+                    "CumSum", "Shape", "Size"}
+    # ops whose output shape depends on input values
+    DATA_SHAPED_OPS = {"NonZero", "Unique", "NonMaxSuppression", "Compress", "If", "Loop", "Scan"}
+    RANDOM_OPS = {"RandomNormal", "RandomUniform", "RandomNormalLike", "RandomUniformLike", "Bernoulli"}
+    STATIC_CACHE_MAX_NUMEL = 1 << 24
+    SMALL_INT_NUMEL = 64
+
+    def __init__(self, model: OnnxModel, device="cpu", plan_cache: int = 4):
         bad = sorted(self.ops_used(model) - self.SUPPORTED)
         if bad:
             raise ValueError(f"unsupported ONNX ops: {', '.join(bad)}")
         self.m = model
         self.device = torch.device(device)
-        self.consts = {k: torch.from_numpy(np.ascontiguousarray(v)).to(self.device) for k, v in model.initializers.items()}
+        self.consts = {k: self._place(torch.from_numpy(_contig(v))) for k, v in model.initializers.items()}
         self._sub_consts: dict[int, dict] = {}
+        self._static = self._static_values(model)
+        self.plan_cache = max(0, plan_cache)
+        self._plans: "collections.OrderedDict" = collections.OrderedDict()
+        self.stats = {"plans_built": 0, "plan_hits": 0, "nodes_skipped": 0}
+
+    def _place(self, t: torch.Tensor) -> torch.Tensor:
+        """Small integer tensors (shapes, axes, indices of shape arithmetic) live on
+        the host; everything else on the interpreter's device."""
+        if not t.is_floating_point() and t.dtype != torch.bool and t.numel() <= self.SMALL_INT_NUMEL:
+            return t.cpu()
+        return t.to(self.device)
+
+    def _static_values(self, model: OnnxModel) -> set:
+        """Names whose values depend only on the initializers and the input shapes
+        (Shape / Size of a value whose shape is fixed by the input shapes, and
+        deterministic ops over such values).  For one set of input shapes they are
+        computed once and reused (the per-shape plan)."""
+        static = set(model.initializers)
+        stable = set(model.initializers) | set(model.inputs)
+        for n in model.nodes:
+            ins = [i for i in n.inputs if i]
+            if n.op in ("Shape", "Size"):
+                is_static = all(i in stable for i in ins[:1])
+            else:
+                is_static = n.op not in self.RANDOM_OPS and n.op not in self.CONTROL and all(i in static for i in ins)
+            value_args = ins if n.op in ("ConstantOfShape", "Range") else ins[1:]
+            is_stable = is_static or (all(i in stable for i in ins) and n.op not in self.DATA_SHAPED_OPS and
+                                      (n.op not in self.HOST_ARG_OPS or all(i in static for i in value_args)))
+            for o in n.outputs:
+                if o and is_static:
+                    static.add(o)
+                if o and is_stable:
+                    stable.add(o)
+        return static - set(model.initializers)
 
     @staticmethod
     def ops_used(model: OnnxModel) -> set:
@@ -320,27 +373,59 @@ class OnnxGraph:
     def run(self, feeds: dict) -> dict:
         env = dict(self.consts)
         for k, v in feeds.items():
-            env[k] = v if isinstance(v, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(v))
+            env[k] = v if isinstance(v, torch.Tensor) else torch.from_numpy(_contig(v))
             env[k] = env[k].to(self.device)
-        self._exec(self.m, env)
+        key = tuple((k, tuple(v.shape), str(v.dtype)) for k, v in sorted(env.items()) if k in feeds)
+        plan = self._plans.get(key) if self.plan_cache else None
+        if plan is not None:
+            self._plans.move_to_end(key)
+            env.update(plan)
+            self.stats["plan_hits"] += 1
+            self._exec(self.m, env, skip=plan)
+        else:
+            self._exec(self.m, env)
+            if self.plan_cache and self._static:
+                self._plans[key] = {k: env[k] for k in self._static
+                                    if k in env and isinstance(env[k], torch.Tensor)
+                                    and env[k].numel() <= self.STATIC_CACHE_MAX_NUMEL}
+                self.stats["plans_built"] += 1
+                while len(self._plans) > self.plan_cache:
+                    self._plans.popitem(last=False)
         return {o: env[o] for o in self.m.outputs}
 
-    def _exec(self, m: OnnxModel, env: dict) -> None:
+    def _exec(self, m: OnnxModel, env: dict, skip: Optional[dict] = None) -> None:
         for n in m.nodes:
+            if skip and n.outputs and all((not o) or o in skip for o in n.outputs):
+                self.stats["nodes_skipped"] += 1
+                continue
             args = [env[i] if i else None for i in n.inputs]
-            outs = self._control(n, args, env) if n.op in self.CONTROL else self._op(n, args)
+            if n.op in self.CONTROL:
+                outs = self._control(n, args, env)
+            else:
+                outs = self._op(n, self._harmonize(n.op, args))
             if not isinstance(outs, (list, tuple)):
                 outs = [outs]
             for name, val in zip(n.outputs, outs):
                 if name:
                     env[name] = val
 
+    def _harmonize(self, op: str, args: list) -> list:
+        """Host-resident small tensors join a device operand's device, except the
+        host-read arguments of shape operators."""
+        devs = {t.device for t in args if isinstance(t, torch.Tensor) and t.device.type != "cpu"}
+        if not devs:
+            return args
+        dev = next(iter(devs))
+        first_only = op in self.HOST_ARG_OPS
+        return [t.to(dev) if isinstance(t, torch.Tensor) and t.device.type == "cpu" and (i == 0 or not first_only)
+                else t for i, t in enumerate(args)]
+
     def _sub(self, g: OnnxModel, env: dict, bind: dict) -> list:
         """Runs subgraph ``g`` in a child scope of ``env`` (outer names stay visible,
         the subgraph's own initializers and bound inputs shadow them)."""
         consts = self._sub_consts.get(id(g))
         if consts is None:
-            consts = {k: torch.from_numpy(np.ascontiguousarray(v)).to(self.device) for k, v in g.initializers.items()}
+            consts = {k: self._place(torch.from_numpy(_contig(v))) for k, v in g.initializers.items()}
             self._sub_consts[id(g)] = consts
         scope = dict(env)
         scope.update(consts)
@@ -436,7 +521,7 @@ class OnnxGraph:
             return x[0]
         if op == "Constant":
             v = a.get("value")
-            return torch.from_numpy(np.ascontiguousarray(v)).to(self.device)
+            return self._place(torch.from_numpy(_contig(v)))
         if op == "Reshape":
             shape = [int(s) for s in x[1].tolist()]
             shape = [x[0].shape[i] if s == 0 else s for i, s in enumerate(shape)]
@@ -470,8 +555,11 @@ class OnnxGraph:
         if op == "Concat":
             return torch.cat(x, dim=a.get("axis", 0))
         if op == "Gather":
-            return torch.index_select(x[0], a.get("axis", 0), x[1].long().flatten()).reshape(
-                *x[0].shape[:a.get("axis", 0)], *x[1].shape, *x[0].shape[a.get("axis", 0) + 1:])
+            ax = a.get("axis", 0) % x[0].dim()
+            idx = x[1].long()
+            idx = torch.where(idx < 0, idx + x[0].shape[ax], idx)  # negative indices count from the end
+            return torch.index_select(x[0], ax, idx.flatten()).reshape(
+                [*x[0].shape[:ax], *x[1].shape, *x[0].shape[ax + 1:]])
         if op in ("Unsqueeze", "Squeeze"):
             axes = a.get("axes") if "axes" in a else (x[1].tolist() if len(x) > 1 and x[1] is not None else None)
             y = x[0]
@@ -492,7 +580,7 @@ class OnnxGraph:
             shape = x[0].shape[ax:]
             return F.layer_norm(x[0], shape, x[1], x[2] if len(x) > 2 else None, a.get("epsilon", 1e-5))
         if op == "Shape":
-            return torch.tensor(list(x[0].shape), dtype=torch.int64, device=self.device)
+            return torch.tensor(list(x[0].shape), dtype=torch.int64)  # host-resident shape
         if op == "Slice":
             starts, ends = x[1].tolist(), x[2].tolist()
             axes = x[3].tolist() if len(x) > 3 and x[3] is not None else list(range(len(starts)))
@@ -601,9 +689,10 @@ class OnnxGraph:
             return torch.full([int(s) for s in x[0].tolist()], arr[0].item(),
                               dtype=torch.from_numpy(arr[:1].copy()).dtype, device=self.device)
         if op == "Range":
-            return torch.arange(x[0].item(), x[1].item(), x[2].item(), device=self.device).to(x[0].dtype)
+            r = torch.arange(x[0].item(), x[1].item(), x[2].item()).to(x[0].dtype)
+            return self._place(r)
         if op == "Size":
-            return torch.tensor(x[0].numel(), dtype=torch.int64, device=self.device)
+            return torch.tensor(x[0].numel(), dtype=torch.int64)
         if op == "Resize":
             def sa(k, d):
                 v = a.get(k, d)
@@ -995,7 +1084,7 @@ class OnnxGraph:
                 vals = np.take(vals, order, axis=ax if ax is not None else 0)
                 first, cnt, inv = first[order], cnt[order], rank[inv]
             dev = x[0].device
-            return [torch.from_numpy(np.ascontiguousarray(vals)).to(dev),
+            return [torch.from_numpy(_contig(vals)).to(dev),
                     torch.from_numpy(first.astype(np.int64)).to(dev), torch.from_numpy(inv.astype(np.int64)).to(dev),
                     torch.from_numpy(cnt.astype(np.int64)).to(dev)]
         if op == "Det":

@@ -37,31 +37,24 @@ class OnnxBackend(Engine):
         self.device = device or ("cuda:0" if torch.cuda.is_available() else "cpu")
         self.max_buckets = max_buckets or int(os.environ.get("KAPSL_ORT_SESSION_BUCKETS", "4"))
         self.model = None
-        self.buckets: "collections.OrderedDict" = collections.OrderedDict()
+        self.graph = None
         self._lock = threading.Lock()
         self._m = EngineMetrics()
         self._times: list = []
 
     def load(self, model_path: str) -> None:
+        """Decodes the graph; the interpreter keeps one plan per input-shape set (the
+        values that depend only on initializers and input shapes, computed on the
+        first request of that shape), an LRU of ``KAPSL_ORT_SESSION_BUCKETS`` entries:
+        the counterpart of the reference's per-shape-bucket ORT sessions
+        (crates/kapsl-backends/src/onnx.rs:367-441)."""
         from ..loaders.onnx import OnnxGraph, read_model
 
         try:
             self.model = read_model(model_path)
-            self.graph = OnnxGraph(self.model, self.device)
+            self.graph = OnnxGraph(self.model, self.device, plan_cache=self.max_buckets)
         except (OSError, ValueError) as e:
             raise EngineError.model_load(model_path, str(e))
-
-    def _graph_for(self, key):
-        with self._lock:
-            g = self.buckets.get(key)
-            if g is None:
-                g = self.graph
-                self.buckets[key] = g
-                if len(self.buckets) > self.max_buckets:
-                    self.buckets.popitem(last=False)
-            else:
-                self.buckets.move_to_end(key)
-            return g
 
     def infer(self, request: InferenceRequest) -> BinaryTensorPacket:
         import torch
@@ -79,10 +72,9 @@ class OnnxBackend(Engine):
         if missing:
             raise EngineError.invalid_input(f"missing model inputs: {missing}")
         t0 = time.perf_counter()
-        g = self._graph_for(tuple(tuple(v.shape) for v in feeds.values()))
         try:
-            with torch.no_grad():
-                out = g.run(feeds)[self.model.outputs[0]]
+            with torch.no_grad(), self._lock:  # one run at a time: plans and stats are shared
+                out = self.graph.run(feeds)[self.model.outputs[0]]
         except Exception as e:
             raise EngineError.inference(str(e))
         dt = time.perf_counter() - t0
@@ -108,7 +100,7 @@ class OnnxBackend(Engine):
 
     def unload(self) -> None:
         self.model = None
-        self.buckets.clear()
+        self.graph = None
 
 
 class BackendFactory:
