@@ -106,6 +106,7 @@ class Node:
     outputs: list
     name: str = ""
     attrs: dict = field(default_factory=dict)
+    domain: str = ""  # "" / "ai.onnx" for standard operators, e.g. "com.microsoft" for contrib ones
 
 
 @dataclass
@@ -229,6 +230,8 @@ def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
                 elif ff == 5:
                     k, a = _attr(vv, base)
                     n.attrs[k] = a
+                elif ff == 7:
+                    n.domain = vv.decode()
             nodes.append(n)
         elif f == 5:
             k, a = _tensor(v, base)
@@ -297,7 +300,7 @@ class OnnxGraph:
                  # transformer graphs (standard opset 23 and the com.microsoft fused ops)
                  "Attention", "RotaryEmbedding", "SkipLayerNormalization", "SimplifiedLayerNormalization",
                  "SkipSimplifiedLayerNormalization", "FastGelu", "BiasGelu", "QuickGelu", "BiasAdd",
-                 "MultiHeadAttention", "MatMulNBits"}
+                 "MultiHeadAttention", "MatMulNBits", "GroupQueryAttention"}
 
     CONTROL = {"If", "Loop", "Scan"}
     # a Loop whose trip count and condition are both absent runs until this many
@@ -1183,27 +1186,20 @@ class OnnxGraph:
 
         if op == "Attention":
             return self._attention(x, a)
+        if op == "RotaryEmbedding" and n.domain == "com.microsoft":
+            # contrib form: (input, position_ids, cos_cache, sin_cache); position_ids of
+            # one element is the start position of every row
+            X, pos, cos, sin = x[0], x[1], x[2], x[3]
+            seq = X.shape[-2] if X.dim() == 4 else X.shape[1]
+            if pos.numel() == 1:
+                pos = (pos.reshape(1, 1).long() + torch.arange(seq, device=pos.device)[None, :]).expand(X.shape[0], -1)
+            return self._rotary(X, cos, sin, pos.long(), a.get("interleaved", 0), a.get("num_heads", 0),
+                                a.get("rotary_embedding_dim", 0))
+        if op == "GroupQueryAttention":
+            return self._gqa(x, a)
         if op == "RotaryEmbedding":
-            X, cos, sin, pos = x[0], x[1], x[2], opt(3)
-            three = X.dim() == 3
-            if three:  # [B, S, hidden] -> [B, H, S, D]
-                B_, S_, hid = X.shape
-                H_ = a["num_heads"]
-                X = X.reshape(B_, S_, H_, hid // H_).transpose(1, 2)
-            if pos is not None:
-                cos, sin = cos[pos.long()], sin[pos.long()]
-            cos, sin = cos.unsqueeze(1), sin.unsqueeze(1)  # [B, 1, S, rot/2]
-            rot = a.get("rotary_embedding_dim", 0) or X.shape[-1]
-            xr, rest = X[..., :rot], X[..., rot:]
-            if a.get("interleaved", 0):
-                x1, x2 = xr[..., 0::2], xr[..., 1::2]
-                o1, o2 = x1 * cos - x2 * sin, x2 * cos + x1 * sin
-                y = torch.stack([o1, o2], -1).reshape(xr.shape)
-            else:
-                x1, x2 = xr[..., :rot // 2], xr[..., rot // 2:]
-                y = torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
-            y = torch.cat([y, rest], -1)
-            return y.transpose(1, 2).reshape(x[0].shape) if three else y
+            return self._rotary(x[0], x[1], x[2], opt(3), a.get("interleaved", 0), a.get("num_heads", 0),
+                                a.get("rotary_embedding_dim", 0))
         if op in ("SkipLayerNormalization", "SkipSimplifiedLayerNormalization"):
             s_ = x[0] + x[1]
             bias = opt(4) if op == "SkipLayerNormalization" else opt(3)
@@ -1244,6 +1240,89 @@ class OnnxGraph:
             y = torch.matmul(x[0], w.to(x[0].dtype).T)
             return y + x[5] if opt(5) is not None else y
         raise ValueError(f"unsupported ONNX op {op}")
+
+    @staticmethod
+    def _rotary(X, cos, sin, pos, interleaved, num_heads, rot):
+        """Rotary position embedding of [B, H, S, D] or [B, S, H * D] (num_heads) input:
+        cos / sin rows [positions, rot / 2] picked by ``pos`` [B, S] (or already
+        [B, S, rot / 2]); the first ``rot`` dims of each head rotate, as pairs
+        (2i, 2i+1) when interleaved, else as halves; the rest pass through."""
+        three = X.dim() == 3
+        Xh = X
+        if three:
+            B_, S_, hid = X.shape
+            Xh = X.reshape(B_, S_, num_heads, hid // num_heads).transpose(1, 2)
+        if pos is not None:
+            cos, sin = cos[pos], sin[pos]
+        cos, sin = cos.unsqueeze(1).to(Xh.dtype), sin.unsqueeze(1).to(Xh.dtype)  # [B, 1, S, rot/2]
+        rot = rot or Xh.shape[-1]
+        xr, rest = Xh[..., :rot], Xh[..., rot:]
+        if interleaved:
+            x1, x2 = xr[..., 0::2], xr[..., 1::2]
+            y = torch.stack([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1).reshape(xr.shape)
+        else:
+            x1, x2 = xr[..., :rot // 2], xr[..., rot // 2:]
+            y = torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], -1)
+        y = torch.cat([y, rest], -1)
+        return y.transpose(1, 2).reshape(X.shape) if three else y
+
+    def _gqa(self, x: list, a: dict):
+        """com.microsoft GroupQueryAttention: query [B, S, Hq * D] (or packed q|k|v
+        when key is absent), key / value [B, S, Hkv * D], past key / value
+        [B, Hkv, P, D] of which the first seqlens_k[b] + 1 - S positions are valid,
+        optional rotary on q and k at positions past_len.. (do_rotary, cos / sin
+        caches), causal attention over past + new keys with an optional local
+        window, softcap and scale (default 1/sqrt(D)); present key / value hold the
+        valid past and the new keys ([B, Hkv, total, D], rows past a sequence's
+        length zero)."""
+        def opt(i):
+            return x[i] if len(x) > i and x[i] is not None else None
+
+        hq, hk = a["num_heads"], a["kv_num_heads"]
+        q, k, v = x[0], opt(1), opt(2)
+        pk, pv, seqlens, total = opt(3), opt(4), x[5].long(), int(x[6].reshape(-1)[0])
+        cos, sin = opt(7), opt(8)
+        B_, S_ = q.shape[0], q.shape[1]
+        if k is None:  # packed q | k | v
+            D = q.shape[-1] // (hq + 2 * hk)
+            q, k, v = q[..., :hq * D], q[..., hq * D:(hq + hk) * D], q[..., (hq + hk) * D:]
+        D = q.shape[-1] // hq
+        qh = q.reshape(B_, S_, hq, D).transpose(1, 2)
+        kh = k.reshape(B_, S_, hk, D).transpose(1, 2)
+        vh = v.reshape(B_, S_, hk, D).transpose(1, 2)
+        past_len = seqlens + 1 - S_  # [B]
+        if a.get("do_rotary", 0):
+            pos = past_len[:, None] + torch.arange(S_, device=q.device)[None, :]
+            il = a.get("rotary_interleaved", 0)
+            qh = self._rotary(qh, cos, sin, pos, il, hq, 0)
+            kh = self._rotary(kh, cos, sin, pos, il, hk, 0)
+        Tn = max(total, int((past_len + S_).max()))
+        pres_k = q.new_zeros(B_, hk, Tn, D)
+        pres_v = q.new_zeros(B_, hk, Tn, D)
+        for b in range(B_):
+            P = int(past_len[b])
+            if P > 0:
+                pres_k[b, :, :P] = pk[b, :, :P]
+                pres_v[b, :, :P] = pv[b, :, :P]
+            pres_k[b, :, P:P + S_] = kh[b]
+            pres_v[b, :, P:P + S_] = vh[b]
+        rep = hq // hk
+        kk = pres_k.repeat_interleave(rep, 1).float()
+        vv = pres_v.repeat_interleave(rep, 1).float()
+        scale = a.get("scale", 0.0) or 1.0 / np.sqrt(D)
+        scores = qh.float() @ kk.transpose(-1, -2) * scale
+        sc = a.get("softcap", 0.0)
+        if sc and sc > 0:
+            scores = sc * torch.tanh(scores / sc)
+        qpos = past_len[:, None] + torch.arange(S_, device=q.device)[None, :]  # [B, S]
+        kpos = torch.arange(Tn, device=q.device)
+        keep = kpos[None, None, :] <= qpos[:, :, None]
+        win = a.get("local_window_size", -1)
+        if win is not None and win > 0:
+            keep = keep & (kpos[None, None, :] > qpos[:, :, None] - win)
+        scores = scores.masked_fill(~keep[:, None], float("-inf"))
+        y = torch.softmax(scores, -1) @ vv
+        return [y.transpose(1, 2).reshape(B_, S_, hq * D).to(q.dtype), pres_k, pres_v]
 
     @staticmethod
     def _nbits_weight(x: list, a: dict) -> torch.Tensor:
@@ -1603,6 +1682,8 @@ def _encode_graph(nodes: list, inputs: list, outputs: list, initializers: dict) 
     for n in nodes:
         nb = b"".join(_ld(1, i.encode()) for i in n.inputs) + b"".join(_ld(2, o.encode()) for o in n.outputs)
         nb += _ld(3, (n.name or n.op).encode()) + _ld(4, n.op.encode())
+        if n.domain:
+            nb += _ld(7, n.domain.encode())
         for k, v in n.attrs.items():
             ab = _ld(1, k.encode())
             if isinstance(v, float):

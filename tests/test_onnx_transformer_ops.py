@@ -177,3 +177,69 @@ def test_matmul_nbits(bits, with_zp):
         names.append("z")
     got = run1("MatMulNBits", {"A": A}, {"K": K, "N": N, "bits": bits, "block_size": bs}, inits, names=names)
     assert np.allclose(got, A @ W.T, atol=1e-4)
+
+
+def np_rotary(x, cos, sin, pos):  # x [B, H, S, D] non-interleaved over the full head
+    c, s_ = cos[pos][:, None], sin[pos][:, None]
+    h = x.shape[-1] // 2
+    return np.concatenate([x[..., :h] * c - x[..., h:] * s_, x[..., h:] * c + x[..., :h] * s_], -1)
+
+
+def test_contrib_rotary_embedding_with_start_position():
+    B, S, H, D = 2, 3, 2, 8
+    x = rng.standard_normal((B, S, H * D)).astype(np.float32)
+    ang = np.arange(16)[:, None] * (1.0 / 10000 ** (np.arange(D // 2) / (D // 2)))[None]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    blob = encode_model([Node("RotaryEmbedding", ["x", "p", "c", "s"], ["y"], attrs={"num_heads": H},
+                              domain="com.microsoft")], ["x", "p", "c", "s"], ["y"], {})
+    p = os.path.join(tempfile.mkdtemp(), "m.onnx")
+    open(p, "wb").write(blob)
+    m = read_model(p)
+    assert m.nodes[0].domain == "com.microsoft"
+    got = OnnxGraph(m).run({"x": x, "p": np.array([4], np.int64), "c": cos, "s": sin})["y"].numpy()
+    pos = np.tile(np.arange(4, 4 + S), (B, 1))
+    xh = x.reshape(B, S, H, D).transpose(0, 2, 1, 3)
+    want = np_rotary(xh, cos, sin, pos).transpose(0, 2, 1, 3).reshape(B, S, H * D)
+    assert np.allclose(got, want, atol=1e-5)
+
+
+@pytest.mark.parametrize("S,window", [(1, -1), (3, -1), (1, 3)])
+def test_group_query_attention(S, window):
+    B, hq, hk, D, Pmax = 2, 4, 2, 8, 6
+    past_len = np.array([4, 2]) if S == 1 else np.array([0, 0])
+    seqlens = (past_len + S - 1).astype(np.int32)
+    total = int((past_len + S).max())
+    q = rng.standard_normal((B, S, hq * D)).astype(np.float32)
+    k = rng.standard_normal((B, S, hk * D)).astype(np.float32)
+    v = rng.standard_normal((B, S, hk * D)).astype(np.float32)
+    pk = rng.standard_normal((B, hk, Pmax, D)).astype(np.float32)
+    pv = rng.standard_normal((B, hk, Pmax, D)).astype(np.float32)
+    ang = np.arange(16)[:, None] * (1.0 / 10000 ** (np.arange(D // 2) / (D // 2)))[None]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    feeds = {"q": q, "k": k, "v": v, "pk": pk, "pv": pv, "sl": seqlens, "tot": np.array(total, np.int32),
+             "c": cos, "s": sin}
+    attrs = {"num_heads": hq, "kv_num_heads": hk, "do_rotary": 1, "local_window_size": window}
+    blob = encode_model([Node("GroupQueryAttention", list(feeds), ["y", "pk_o", "pv_o"], attrs=attrs,
+                              domain="com.microsoft")], list(feeds), ["y", "pk_o", "pv_o"], {})
+    p = os.path.join(tempfile.mkdtemp(), "m.onnx")
+    open(p, "wb").write(blob)
+    res = OnnxGraph(read_model(p)).run(feeds)
+    y = res["y"].numpy()
+    for b in range(B):
+        P = past_len[b]
+        pos = (P + np.arange(S))[None]
+        qh = np_rotary(q[b:b + 1].reshape(1, S, hq, D).transpose(0, 2, 1, 3), cos, sin, pos)[0]
+        kh = np_rotary(k[b:b + 1].reshape(1, S, hk, D).transpose(0, 2, 1, 3), cos, sin, pos)[0]
+        vh = v[b].reshape(S, hk, D).transpose(1, 0, 2)
+        kk = np.concatenate([pk[b, :, :P], kh], 1)
+        vv = np.concatenate([pv[b, :, :P], vh], 1)
+        assert np.allclose(res["pk_o"].numpy()[b, :, :P + S], kk, atol=1e-5)
+        kk, vv = np.repeat(kk, hq // hk, 0), np.repeat(vv, hq // hk, 0)
+        sc = qh @ np.swapaxes(kk, -1, -2) / np.sqrt(D)
+        qpos, kpos = P + np.arange(S), np.arange(P + S)
+        keep = kpos[None, :] <= qpos[:, None]
+        if window > 0:
+            keep &= kpos[None, :] > qpos[:, None] - window
+        sc = np.where(keep[None], sc, -np.inf)
+        want = (softmax(sc) @ vv).transpose(1, 0, 2).reshape(S, hq * D)
+        assert np.allclose(y[b], want, atol=1e-5)
