@@ -1607,6 +1607,9 @@ def load_onnx_llm(path: str, root: str, device, tp: int = 1, rank: int = 0):
     from ..models.llama import weights_from_full
 
     model = read_model(path)
+    if "model.embed_tokens.weight" not in model.initializers:
+        raise ValueError("ONNX export lacks initializer model.embed_tokens.weight; only exports keeping HF tensor "
+                         "names are supported")
     cfg = ModelConfig.from_hf_config(os.path.join(root, "config.json"))
     W = {k: torch.from_numpy(np.ascontiguousarray(v)).float() for k, v in model.initializers.items()}
 

@@ -254,7 +254,20 @@ def build_llm_engine(model_path: str, device: Optional[str] = None, tp_comm=None
         want_cpu = (hw.preferred_provider or "").lower() == "cpu"
         device = "cpu" if want_cpu or not torch.cuda.is_available() else f"cuda:{hw.device_id or 0}"
     dev = torch.device(device)
-    cfg, weights, tokenizer = load_model_weights(pkg.model_path, pkg.root, hints, dev, tp_comm)
+    try:
+        cfg, weights, tokenizer = load_model_weights(pkg.model_path, pkg.root, hints, dev, tp_comm)
+    except OnnxNotMappable:
+        # a decoder export whose weights do not map onto the native model: the graph
+        # itself serves (interpreter, per-sequence KV as its present tensors)
+        from ..llm.onnx_decoder import OnnxDecoderEngine
+
+        if tp_comm is not None and tp_comm.world_size > 1:
+            raise ValueError("ONNX decoder graphs without Hugging Face weight names serve on one device")
+        engine = OnnxDecoderEngine(pkg.model_path, pkg.root, device=str(dev),
+                                   max_model_len=engine_config_from_hints(hints, dev.type).max_model_len)
+        c = engine.cfg
+        return engine, load_tokenizer(pkg.root, c.vocab_size, c.bos_token_id, c.eos_token_id), \
+            load_runtime_config(pkg.root)
     ecfg = engine_config_from_hints(hints, dev.type)
     ecfg.max_model_len = min(ecfg.max_model_len, cfg.max_position)
     engine = LLMEngine(cfg, weights=weights, device=dev, engine_cfg=ecfg, tp_comm=tp_comm)
@@ -265,6 +278,10 @@ def build_llm_engine(model_path: str, device: Optional[str] = None, tp_comm=None
         rc.use_chat_template = False  # GGUF prompts are raw UTF-8, greedy (gguf_backend.rs:65-76)
         rc.sampling.temperature = 0.0
     return engine, tokenizer, rc
+
+
+class OnnxNotMappable(ValueError):
+    """An ONNX decoder export whose initializers do not carry Hugging Face weight names."""
 
 
 def load_model_weights(model_path: str, root: str, hints: dict, device, tp_comm=None):
@@ -280,7 +297,12 @@ def load_model_weights(model_path: str, root: str, hints: dict, device, tp_comm=
     if model_path.endswith(".onnx"):
         from ..loaders.onnx import load_onnx_llm
 
-        return load_onnx_llm(model_path, root, device, tp, rank)
+        try:
+            return load_onnx_llm(model_path, root, device, tp, rank)
+        except ValueError as e:
+            if "lacks initializer" in str(e):
+                raise OnnxNotMappable(str(e)) from e
+            raise
     cfg_path = os.path.join(root, "config.json")
     if os.path.isdir(model_path) or model_path.endswith(".safetensors"):
         from ..loaders.hf import load_hf_model
