@@ -187,8 +187,9 @@ std::string encode_request(const Request& req) {
   return w.buf;
 }
 
-static Request decode_request_layout(const std::string& payload, int layout) {
-  // layout 0: full; 1: metadata without auth_token; 2: legacy (no metadata)
+static Request decode_request_layout(const std::string& payload, int layout, bool exact) {
+  // layout 0: full; 1: metadata without auth_token; 2: legacy (no metadata).
+  // exact: the layout must consume the whole payload.
   Reader r(payload);
   Request req;
   req.input = decode_packet(r);
@@ -204,23 +205,28 @@ static Request decode_request_layout(const std::string& payload, int layout) {
   if (layout != 2) {
     if (r.tag()) req.metadata = decode_metadata(r, layout == 0);
   }
+  if (exact && r.remaining() != 0) throw DecodeError("trailing bytes after InferenceRequest");
   return req;
 }
 
+// Metadata serialised without its auth_token (the field is skipped when None) is
+// one Option tag shorter, and the full layout can read such a payload without an
+// error while misplacing every later field (a seed read as repetition_penalty, the
+// seed itself dropped).  So the layouts are first tried in order where they must
+// consume the payload exactly, then in the same order as a plain prefix parse
+// (legacy payloads with trailing bytes).
 Request decode_request(const std::string& payload) {
-  try {
-    return decode_request_layout(payload, 0);
-  } catch (const DecodeError& e0) {
-    try {
-      return decode_request_layout(payload, 1);
-    } catch (const DecodeError&) {
+  std::string first;
+  for (bool exact : {true, false}) {
+    for (int layout = 0; layout < 3; ++layout) {
       try {
-        return decode_request_layout(payload, 2);
-      } catch (const DecodeError&) {
-        throw DecodeError(std::string("failed to decode InferenceRequest: ") + e0.what());
+        return decode_request_layout(payload, layout, exact);
+      } catch (const DecodeError& e) {
+        if (first.empty()) first = e.what();
       }
     }
   }
+  throw DecodeError(std::string("failed to decode InferenceRequest: ") + first);
 }
 
 static void enc_tmeta(Writer& w, const TransportRequestMeta& m) {
