@@ -54,12 +54,16 @@ def _saturate(v: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
 def _varint(b: bytes, i: int):
     shift = v = 0
     while True:
+        if i >= len(b):
+            raise ValueError("malformed protobuf: truncated varint")
         x = b[i]
         i += 1
         v |= (x & 0x7F) << shift
         if x < 0x80:
             return v, i
         shift += 7
+        if shift > 63:
+            raise ValueError("malformed protobuf: varint longer than 10 bytes")
 
 
 def _fields(b: bytes):
@@ -70,19 +74,20 @@ def _fields(b: bytes):
         f, wt = key >> 3, key & 7
         if wt == 0:
             v, i = _varint(b, i)
-        elif wt == 1:
-            v = b[i:i + 8]
-            i += 8
+            yield f, wt, v
+            continue
+        if wt == 1:
+            ln = 8
         elif wt == 2:
             ln, i = _varint(b, i)
-            v = b[i:i + ln]
-            i += ln
         elif wt == 5:
-            v = b[i:i + 4]
-            i += 4
+            ln = 4
         else:
             raise ValueError(f"unsupported protobuf wire type {wt}")
-        yield f, wt, v
+        if i + ln > n:
+            raise ValueError(f"malformed protobuf: field {f} runs {i + ln - n} bytes past the message")
+        yield f, wt, b[i:i + ln]
+        i += ln
 
 
 def _packed_varints(v, wt):
@@ -245,8 +250,20 @@ def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
 
 
 def read_model(path: str) -> OnnxModel:
+    """Decodes an ONNX file; any malformed content raises ValueError."""
     with open(path, "rb") as fh:
         data = fh.read()
+    try:
+        return _read_model_bytes(data, path)
+    except (IndexError, struct.error, UnicodeDecodeError, TypeError, OverflowError) as e:
+        raise ValueError(f"malformed ONNX file {path}: {e}") from e
+    except ValueError as e:
+        if "malformed" in str(e) or "protobuf" in str(e):
+            raise
+        raise ValueError(f"malformed ONNX file {path}: {e}") from e
+
+
+def _read_model_bytes(data: bytes, path: str) -> OnnxModel:
     base = os.path.dirname(os.path.abspath(path))
     graph = None
     opset = 13

@@ -93,3 +93,29 @@ def test_onnx_backend_serves_with_plans():
         out = be.infer(InferenceRequest(input=BinaryTensorPacket.from_numpy(x))).to_numpy()
         assert np.allclose(out, (x @ w.T).reshape(2, -1), atol=1e-5)
     assert be.graph.stats["plans_built"] == 1 and be.graph.stats["plan_hits"] == 2
+
+
+def test_malformed_files_raise_value_error(tmp_path):
+    """Truncated and corrupted models end in ValueError (never another exception type or a hang)."""
+    import random
+
+    nodes, inits, _ = flatten_graph()
+    good = encode_model(nodes, ["x"], ["y"], inits)
+    rng = random.Random(0)
+    p = tmp_path / "m.onnx"
+    outcomes = {"ok": 0, "rejected": 0}
+    for i in range(600):
+        b = bytearray(good)
+        if i % 3 == 0:
+            b = b[:rng.randrange(len(b))]
+        else:
+            for _ in range(rng.randint(1, 3)):
+                b[rng.randrange(len(b))] = rng.randrange(256)
+        p.write_bytes(bytes(b))
+        try:
+            m = read_model(str(p))
+            OnnxGraph(m)
+            outcomes["ok"] += 1
+        except ValueError:
+            outcomes["rejected"] += 1
+    assert outcomes["rejected"] > 100
