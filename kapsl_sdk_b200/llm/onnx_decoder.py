@@ -18,6 +18,7 @@ drives (``add_request`` / ``step`` / ``abort`` / ``has_unfinished`` / ``kv_stats
 """
 from __future__ import annotations
 
+import collections
 import json
 import os
 import re
@@ -107,11 +108,13 @@ def _geometry(root: str, model: OnnxModel) -> dict:
 @dataclass
 class _Seq:
     request_id: str
-    prompt_ids: list
+    prompt_ids: list      # this turn's prompt, after any session history
     params: SamplingParams
     rng: int
     output_ids: list = field(default_factory=list)
-    past: Optional[list] = None
+    past: Optional[list] = None   # [(key, value)] per layer covering the first `cached` tokens
+    cached: int = 0
+    session_id: Optional[str] = None
     finish_reason: Optional[str] = None
 
     @property
@@ -121,7 +124,7 @@ class _Seq:
 
 class OnnxDecoderEngine:
     def __init__(self, model_path: str, root: Optional[str] = None, device: str = "cpu",
-                 max_model_len: Optional[int] = None):
+                 max_model_len: Optional[int] = None, max_sessions: int = 64, max_session_tokens: int = 0):
         self.model = read_model(model_path)
         io = inspect_decoder(self.model)
         if io is None:
@@ -137,6 +140,10 @@ class OnnxDecoderEngine:
         self.stop_ids = set(x for x in (g.get("eos"), g.get("bos")) if x is not None) | set(g.get("eos_list", []))
         self.live: "dict[str, _Seq]" = {}
         self._next_seq_id = 1
+        # session id -> (token ids, past KV covering all but the last, cached count); LRU
+        self.sessions: "collections.OrderedDict[str, tuple]" = collections.OrderedDict()
+        self.max_sessions = max_sessions
+        self.max_session_tokens = max_session_tokens or self.max_model_len
 
     # ------------------------------------------------------------ requests
     def add_request(self, request_id: str, prompt_ids: list, params: SamplingParams, session_id=None,
@@ -145,12 +152,21 @@ class OnnxDecoderEngine:
             raise EngineError.invalid_input("empty prompt")
         if self.cfg.vocab_size and any(not 0 <= t < self.cfg.vocab_size for t in prompt_ids):
             raise EngineError.invalid_input("prompt token id outside the vocabulary")
-        if len(prompt_ids) >= self.max_model_len:
-            raise EngineError.invalid_input(f"prompt of {len(prompt_ids)} tokens exceeds the context "
-                                            f"({self.max_model_len})")
         seq_id = self._next_seq_id
         self._next_seq_id += 1
-        s = _Seq(request_id, list(prompt_ids), params, ref.seed_state(params.seed, request_id, seq_id))
+        ids, past, cached = list(prompt_ids), None, 0
+        prev = self.sessions.get(session_id) if session_id is not None else None
+        if prev is not None:
+            # continue the session: the new turn follows the previous turn's tokens, whose
+            # KV (all but the last token) is reused
+            hist, hpast, hcached = prev
+            if len(hist) + len(ids) + params.max_new_tokens <= self.max_session_tokens:
+                ids, past, cached = hist + ids, hpast, hcached
+            self.sessions.move_to_end(session_id)
+        if len(ids) >= self.max_model_len:
+            raise EngineError.invalid_input(f"prompt of {len(ids)} tokens exceeds the context ({self.max_model_len})")
+        s = _Seq(request_id, ids, params, ref.seed_state(params.seed, request_id, seq_id), past=past, cached=cached,
+                 session_id=session_id)
         self.live[request_id] = s
         return s
 
@@ -164,8 +180,8 @@ class OnnxDecoderEngine:
 
     # ---------------------------------------------------------------- step
     def _feeds(self, s: _Seq) -> dict:
-        new = s.prompt_ids if s.past is None else s.output_ids[-1:]
-        past_len = 0 if s.past is None else s.length - 1
+        new = (s.prompt_ids + s.output_ids)[s.cached:]
+        past_len = s.cached
         n = len(new)
         feeds = {self.io.input_ids: torch.tensor([new], dtype=torch.int64)}
         if self.io.attention_mask:
@@ -195,6 +211,7 @@ class OnnxDecoderEngine:
             with torch.no_grad():
                 res = self.graph.run(self._feeds(s))
             s.past = [(res[kn], res[vn]) for kn, vn in self.io.present]
+            s.cached = s.length
             logits = res[self.io.logits][0, -1].float().cpu().numpy()
             p = s.params
             if p.repetition_penalty != 1.0:
@@ -205,6 +222,11 @@ class OnnxDecoderEngine:
             if reason is not None:
                 s.finish_reason = reason
                 del self.live[rid]
+                if s.session_id is not None:
+                    self.sessions[s.session_id] = (s.prompt_ids + s.output_ids, s.past, s.cached)
+                    self.sessions.move_to_end(s.session_id)
+                    while len(self.sessions) > self.max_sessions:
+                        self.sessions.popitem(last=False)
             outs.append(types.SimpleNamespace(request_id=rid, new_token=tok, finished=reason is not None, seq=s))
         return outs
 
@@ -223,3 +245,4 @@ class OnnxDecoderEngine:
 
     def shutdown(self) -> None:
         self.live.clear()
+        self.sessions.clear()

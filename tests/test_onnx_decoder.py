@@ -139,3 +139,20 @@ def test_loader_routes_unmapped_exports_and_backend_serves(export_dir):
         assert out.dtype.as_str() == "string"
     finally:
         be.unload()
+
+
+def test_session_continuation_reuses_the_previous_turn(export_dir):
+    """A second turn of a session continues after the first turn's tokens, reusing
+    their KV; the tokens equal a single request over the concatenated history."""
+    path = os.path.join(export_dir, "model.onnx")
+    eng = OnnxDecoderEngine(path)
+    g = SamplingParams.greedy(4, ignore_eos=True)
+    s1 = eng.add_request("t1", [5, 9, 13], g, session_id="chat")
+    while eng.has_unfinished():
+        eng.step()
+    s2 = eng.add_request("t2", [7, 3], g, session_id="chat")
+    assert s2.cached == len(s1.prompt_ids) + len(s1.output_ids) - 1
+    while eng.has_unfinished():
+        eng.step()
+    hist = [5, 9, 13] + s1.output_ids + [7, 3]
+    assert s2.output_ids == recompute_greedy(path, hist, 4)
