@@ -92,3 +92,24 @@ class HeartbeatMonitor:
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=2 * self.interval_s + 1)
+
+
+def init_distributed(backend: str, timeout_s: float = 120.0, device=None):
+    """``torch.distributed.init_process_group`` for serving groups, with the NCCL
+    watchdog configured to abort: ``TORCH_NCCL_ASYNC_ERROR_HANDLING=1`` makes the
+    process group's watchdog thread poll each communicator's asynchronous error
+    state and abort the communicators of a collective that failed or outlived
+    ``timeout_s``, so the waiting ranks get an exception instead of blocking (the
+    reference's plan of non-blocking communicators polled for async errors and
+    aborted on timeout).  A value already in the environment is kept."""
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    if backend == "nccl":
+        os.environ.setdefault("TORCH_NCCL_ASYNC_ERROR_HANDLING", "1")
+    kw = {"timeout": timedelta(seconds=timeout_s)}
+    if device is not None and backend == "nccl":
+        kw["device_id"] = device
+    dist.init_process_group(backend, **kw)

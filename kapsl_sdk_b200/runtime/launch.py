@@ -46,6 +46,8 @@ def parse_args(argv: Optional[list] = None) -> argparse.Namespace:
     p.add_argument("--tp", type=int, default=int(os.environ.get("KAPSL_TP", "0")),
                    help="tensor-parallel degree; must equal WORLD_SIZE (0 = WORLD_SIZE)")
     p.add_argument("--tp-mode", default=os.environ.get("KAPSL_TP_MODE", "fused"), choices=["fused", "nccl"])
+    p.add_argument("--pg-timeout", type=float, default=float(os.environ.get("KAPSL_PG_TIMEOUT", "120")),
+                   help="seconds after which a stuck collective of the serving group is aborted")
     p.add_argument("--max-num-seqs", type=int, default=0)
     p.add_argument("--max-batched-tokens", type=int, default=0)
     p.add_argument("--max-model-len", type=int, default=0)
@@ -120,14 +122,10 @@ def main(argv: Optional[list] = None) -> int:
         torch.cuda.set_device(dev)
     tp_comm = None
     if world > 1:
-        from datetime import timedelta
-
-        import torch.distributed as dist
-
+        from ..parallel.health import init_distributed
         from ..parallel.tp import TPComm
 
-        dist.init_process_group("nccl" if cuda else "gloo", timeout=timedelta(seconds=120),
-                                device_id=dev if cuda else None)
+        init_distributed("nccl" if cuda else "gloo", a.pg_timeout, dev if cuda else None)
         tp_comm = TPComm.from_world(mode=a.tp_mode) if cuda else None
     from .._ext import cuda_ops
 

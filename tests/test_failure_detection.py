@@ -224,3 +224,22 @@ def test_peer_wait_runs_out_and_engine_reports_failure():
     assert int(err.max()) == 0  # the status was consumed
     eng.failed = None
     eng.shutdown()
+
+
+def test_init_distributed_configures_the_collective_watchdog(monkeypatch):
+    """The serving group's process group gets the timeout, and NCCL groups the
+    watchdog setting that aborts failed or timed-out communicators."""
+    import torch.distributed as dist
+
+    from kapsl_sdk_b200.parallel import health
+
+    seen = {}
+    monkeypatch.setattr(dist, "init_process_group", lambda backend, **kw: seen.update(backend=backend, **kw))
+    monkeypatch.delenv("TORCH_NCCL_ASYNC_ERROR_HANDLING", raising=False)
+    health.init_distributed("nccl", 7.5, device="cuda:0")
+    assert seen["backend"] == "nccl" and seen["timeout"].total_seconds() == 7.5 and seen["device_id"] == "cuda:0"
+    import os
+    assert os.environ["TORCH_NCCL_ASYNC_ERROR_HANDLING"] == "1"
+    seen.clear()
+    health.init_distributed("gloo", 3.0, device="cpu")
+    assert seen == {"backend": "gloo", "timeout": seen["timeout"]} and seen["timeout"].total_seconds() == 3.0
