@@ -472,10 +472,13 @@ PYBIND11_MODULE(_native, m) {
                           const std::vector<bool>& fin) {
     if (chans.size() != toks.size() || chans.size() != fin.size()) throw std::invalid_argument("push_tokens: lengths");
     py::gil_scoped_release nogil;
+    std::vector<std::shared_ptr<TokenChannel>> wake;
+    wake.reserve(chans.size());
     for (size_t i = 0; i < chans.size(); ++i) {
-      chans[i]->push(toks[i]);
-      if (fin[i]) chans[i]->finish();
+      chans[i]->push_quiet(toks[i], fin[i]);
+      wake.push_back(chans[i]);
     }
+    TokenNotifier::get().post(std::move(wake));  // the wakeups run off this thread
   });
   m.def("encode_packet", [](py::object shape, std::string dtype, py::bytes data) {
     return py::bytes(wire::encode_packet(packet_from_py(py::make_tuple(shape, dtype, data))));

@@ -28,6 +28,7 @@
 #include "hnsw.h"
 #include "shm.h"
 #include "text_index.h"
+#include "token_channel.h"
 #include "wasm.h"
 #include "wire.h"
 
@@ -535,11 +536,53 @@ static void test_hnsw() {
   std::remove(path.c_str());
 }
 
+// A producer feeds 64 token channels in batches (append quietly, one post to the
+// notifier thread per batch, like the engine loop); 64 consumers pop with bounded
+// waits.  Every token arrives once and in order, and every stream ends.
+static void test_token_channels() {
+  constexpr int kChans = 64, kToks = 300;
+  std::vector<std::shared_ptr<TokenChannel>> chans;
+  for (int i = 0; i < kChans; ++i) chans.push_back(std::make_shared<TokenChannel>());
+  std::vector<std::vector<int32_t>> got(kChans);
+  std::vector<int> ends(kChans, 0);
+  std::vector<std::thread> cons;
+  for (int c = 0; c < kChans; ++c)
+    cons.emplace_back([&, c] {
+      std::vector<int32_t> out;
+      std::string err;
+      for (int spins = 0; spins < 20000; ++spins) {
+        out.clear();
+        const int r = chans[c]->pop(out, err, 50);
+        got[c].insert(got[c].end(), out.begin(), out.end());
+        if (r == TokenChannel::kEnd) {
+          ends[c] = 1;
+          return;
+        }
+      }
+    });
+  for (int t = 0; t < kToks; ++t) {
+    std::vector<std::shared_ptr<TokenChannel>> batch;
+    for (int c = 0; c < kChans; ++c) {
+      chans[c]->push_quiet(c * 1000 + t, t == kToks - 1);
+      batch.push_back(chans[c]);
+    }
+    TokenNotifier::get().post(std::move(batch));
+  }
+  for (auto& th : cons) th.join();
+  for (int c = 0; c < kChans; ++c) {
+    CHECK(ends[c] == 1, "channel %d did not end", c);
+    bool ok = (int)got[c].size() == kToks;
+    for (int t = 0; ok && t < kToks; ++t) ok = got[c][t] == c * 1000 + t;
+    CHECK(ok, "channel %d: %zu tokens, wrong order or count", c, got[c].size());
+  }
+}
+
 int main(int argc, char** argv) {
   const std::pair<const char*, void (*)()> tests[] = {
       {"ring_mpmc", test_ring_mpmc},         {"ring_repush", test_ring_repush}, {"model_pools", test_model_pools},
       {"shared_leases", test_shared_leases}, {"block_allocator", test_block_allocator}, {"wire", test_wire},
-      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm},               {"text_index", test_text_index}, {"hnsw", test_hnsw}};
+      {"cpu_pool", test_cpu_pool},           {"wasm", test_wasm},               {"text_index", test_text_index}, {"hnsw", test_hnsw},
+      {"token_channels", test_token_channels}};
   for (auto& [name, fn] : tests) {
     if (argc > 1 && std::string(argv[1]) != name) continue;
     const auto t0 = std::chrono::steady_clock::now();
