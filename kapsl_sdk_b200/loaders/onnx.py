@@ -470,8 +470,8 @@ class OnnxGraph:
             while (trip is None or i < trip) and keep:
                 if trip is None and (len(x) < 2 or x[1] is None) and i >= self.MAX_LOOP_ITERS:
                     raise ValueError("Loop without trip count or condition did not end")
-                bind = {body.inputs[0]: torch.tensor(i, dtype=torch.int64, device=self.device),
-                        body.inputs[1]: torch.tensor(keep, device=self.device)}
+                # iteration number and condition are host values, like other shape arithmetic
+                bind = {body.inputs[0]: torch.tensor(i, dtype=torch.int64), body.inputs[1]: torch.tensor(keep)}
                 bind.update({name: v for name, v in zip(body.inputs[2:], vs)})
                 out = self._sub(body, env, bind)
                 keep = bool(out[0].reshape(-1)[0])
