@@ -1,7 +1,8 @@
-"""Corrupted-file fuzzing of the native HNSW index loader (a saved vector index is
-read back from disk): truncations and byte mutations of a saved index must load
-into an index that answers searches, or raise, never crash the process.  Runs in
-a child process so that a crash fails the test with the mutation that caused it."""
+"""Fuzzing of native code that reads untrusted bytes, each run in a child process so
+that a crash fails the test with the input that caused it: the HNSW index loader
+(truncated and mutated saved indexes load into an index that answers searches, or
+raise) and the shared-memory server (garbage requests from a client that shares
+the region get error responses and the server keeps serving)."""
 import os
 import subprocess
 import sys
@@ -47,3 +48,74 @@ def test_corrupted_index_files_never_crash_the_process():
         last = p.stdout.strip().splitlines()[-1] if p.stdout.strip() else "none"
         assert p.returncode == 0 and last == "done", \
             f"seed {seed}: child ended with {p.returncode} after mutation {last}: {p.stderr[-2000:]}"
+
+
+SHM_CHILD = textwrap.dedent(r'''
+    import random, struct, sys, time, uuid
+    from kapsl_sdk_b200._ext import native
+    from kapsl_sdk_b200.server.dispatch import Dispatcher
+
+    class Echo:
+        def infer(self, request, priority="throughput"):
+            return request.input
+
+    nat = native()
+    name = f"kapsl-fuzz-{uuid.uuid4().hex[:8]}"
+    srv = nat.ShmServer(Dispatcher(lambda i: Echo()), name, 16 << 20, 1)
+    srv.start()
+    region = nat.ShmRegion.open(name)
+    pool = region.header()["tensor_pool_offset"]
+    rng = random.Random(int(sys.argv[1]))
+    junk = bytes(rng.randrange(256) for _ in range(1 << 16))
+    region.write_tensor(pool, [len(junk)], "uint8", junk)  # a pool full of random bytes to point into
+
+    def drain(wait_s):
+        got, t0 = [], time.time()
+        while time.time() - t0 < wait_s:
+            r = region.pop_response()
+            if r is None:
+                time.sleep(0.0005)
+                continue
+            got.append(r)
+            if r[1] == 0:  # read results and error messages, as a client does, so their slots free up
+                region.mark_result_read(r[2])
+            elif r[4] > 0:
+                region.read_error(r[4])
+                region.mark_result_read(r[4])
+        return got
+
+    sizes = [0, 1, 7, 80, 4096, 1 << 20, 1 << 40, (1 << 64) - 1]
+    sent = 0
+    for i in range(int(sys.argv[2])):
+        off = rng.choice([pool + rng.randrange(1 << 16), rng.randrange(1 << 25), (1 << 64) - 1 - rng.randrange(64),
+                          pool + rng.randrange(64)])
+        size = rng.choice(sizes + [rng.randrange(1 << 17)])
+        if region.push_request(i + 1, rng.randrange(4), rng.randrange(256), off, size):
+            sent += 1
+        if i % 64 == 63:
+            drain(0.01)
+        sys.stdout.write(f"{i}\n")
+        sys.stdout.flush()
+    drain(0.5)
+    # the server still serves a well-formed request
+    payload = struct.pack("<4i", 1, 2, 3, 4)
+    region.write_tensor(pool + (1 << 20), [4], "int32", payload)
+    assert region.push_request(10 ** 9, 0, 0, pool + (1 << 20), 96)
+    ok = [r for r in drain(3.0) if r[0] == 10 ** 9]
+    assert ok and ok[0][1] == 0 and region.read_tensor(ok[0][2])[2] == payload, ok
+    srv.stop()
+    print("done")
+''')
+
+
+def test_garbage_shared_memory_requests_never_crash_the_server():
+    """Requests whose tensor offsets and sizes point at random bytes, past the
+    region or at absurd lengths get error responses; the server keeps running and
+    answers a well-formed request afterwards."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for seed in (1, 2):
+        p = subprocess.run([sys.executable, "-c", SHM_CHILD, str(seed), "1500"], capture_output=True, text=True,
+                           timeout=600, cwd=root)
+        last = p.stdout.strip().splitlines()[-1] if p.stdout.strip() else "none"
+        assert p.returncode == 0 and last == "done", \
+            f"seed {seed}: child ended with {p.returncode} after request {last}: {p.stderr[-2000:]}"
