@@ -1,5 +1,6 @@
 #include "server.h"
 
+#include <algorithm>
 #include <arpa/inet.h>
 #include <errno.h>
 #include <netinet/in.h>
@@ -277,8 +278,20 @@ void WireServer::serve_connection(int fd) {
     std::memcpy(&op, hdr + 4, 4);
     std::memcpy(&size, hdr + 8, 4);
     if (size > kMaxPayload) break;
-    std::string payload(size, '\0');
-    if (size && !net::read_exact(fd, payload.data(), size)) break;
+    // grow the buffer with the bytes that actually arrive (1 MiB at a time), so a
+    // header that declares a huge payload and sends nothing holds no memory for it
+    std::string payload;
+    bool complete = true;
+    for (uint32_t got = 0; got < size;) {
+      const uint32_t n = std::min<uint32_t>(size - got, 1u << 20);
+      payload.resize((size_t)got + n);
+      if (!net::read_exact(fd, payload.data() + got, n)) {
+        complete = false;
+        break;
+      }
+      got += n;
+    }
+    if (!complete) break;
     if (!handle_frame(fd, model_id, op, payload)) break;
     served_.fetch_add(1);
   }

@@ -1,8 +1,9 @@
 """Fuzzing of native code that reads untrusted bytes, each run in a child process so
 that a crash fails the test with the input that caused it: the HNSW index loader
 (truncated and mutated saved indexes load into an index that answers searches, or
-raise) and the shared-memory server (garbage requests from a client that shares
-the region get error responses and the server keeps serving)."""
+raise), the shared-memory server (garbage requests from a client that shares
+the region get error responses and the server keeps serving) and the socket
+server's frame reader."""
 import os
 import subprocess
 import sys
@@ -119,3 +120,76 @@ def test_garbage_shared_memory_requests_never_crash_the_server():
         last = p.stdout.strip().splitlines()[-1] if p.stdout.strip() else "none"
         assert p.returncode == 0 and last == "done", \
             f"seed {seed}: child ended with {p.returncode} after request {last}: {p.stderr[-2000:]}"
+
+
+SOCK_CHILD = textwrap.dedent(r'''
+    import os, random, resource, socket, struct, sys, tempfile, time
+    from kapsl_sdk_b200.engine_api import EngineError
+    from kapsl_sdk_b200.server import KapslServer
+    from kapsl_sdk_b200.server import wire as pyw
+
+    class Echo:
+        def infer(self, request, priority="throughput"):
+            return request.input
+
+        def infer_stream(self, request):
+            def gen():
+                for b in request.input.data[:4]:
+                    yield type(request.input)(shape=[1], dtype=request.input.dtype, data=bytes([b]))
+            return gen()
+
+    sock = os.path.join(tempfile.mkdtemp(), "k.sock")
+    srv = KapslServer(models={0: Echo()}).listen_unix(sock).start()
+    rng = random.Random(int(sys.argv[1]))
+    good = pyw.encode_request(([4], "uint8", b"abcd"))
+    rss0 = resource.getrusage(resource.RUSAGE_SELF).ru_maxrss
+    for i in range(int(sys.argv[2])):
+        s = socket.socket(socket.AF_UNIX, socket.SOCK_STREAM)
+        s.settimeout(0.2)
+        s.connect(sock)
+        try:
+            for _ in range(rng.randint(1, 3)):
+                k = rng.random()
+                body = bytearray(good)
+                if k < 0.4:
+                    for _ in range(rng.randint(1, 4)):
+                        body[rng.randrange(len(body))] = rng.randrange(256)
+                elif k < 0.6:
+                    body = body[:rng.randrange(len(body))]
+                elif k < 0.75:
+                    body = bytearray(rng.randrange(256) for _ in range(rng.randrange(64)))
+                op = rng.choice([1, 2, 3, 4, 0, 7, 0xFFFFFFFF])
+                size = len(body) if rng.random() < 0.85 else rng.choice([len(body) + 5, 1 << 30, (1 << 31) + 1])
+                s.sendall(struct.pack("<III", rng.randrange(3), op, size) + bytes(body))
+                if size != len(body):
+                    break  # the server waits for bytes that never come: hang up
+                try:
+                    s.recv(1 << 16)
+                except OSError:
+                    pass
+        except OSError:
+            pass
+        finally:
+            s.close()
+        sys.stdout.write(f"{i}\n")
+        sys.stdout.flush()
+    grown_mb = (resource.getrusage(resource.RUSAGE_SELF).ru_maxrss - rss0) / 1024
+    from kapsl_sdk import KapslClient
+    assert KapslClient(sock).infer(0, [4], "uint8", b"wxyz") == b"wxyz"
+    assert grown_mb < 512, grown_mb  # declared 1-2 GiB payloads were never allocated
+    srv.stop()
+    print("done")
+''')
+
+
+def test_malformed_socket_frames_never_crash_the_server():
+    """Mutated, truncated and random request frames, unknown ops and headers that
+    declare up to 2 GiB of payload get errors or a closed connection; the server
+    keeps serving and never allocates a payload that did not arrive."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for seed in (1, 2):
+        p = subprocess.run([sys.executable, "-c", SOCK_CHILD, str(seed), "400"], capture_output=True, text=True,
+                           timeout=600, cwd=root)
+        last = p.stdout.strip().splitlines()[-1] if p.stdout.strip() else "none"
+        assert p.returncode == 0 and last == "done", \
+            f"seed {seed}: child ended with {p.returncode} after connection {last}: {p.stderr[-2000:]}"
