@@ -121,6 +121,8 @@ class OnnxModel:
     outputs: list
     initializers: dict
     opset: int = 13
+    # declared input types: name -> (TensorProto element type or None, dims with None for symbolic ones)
+    input_types: dict = field(default_factory=dict)
 
 
 def _tensor(b: bytes, base_dir: Optional[str]) -> tuple:
@@ -208,6 +210,29 @@ def _attr(b: bytes, base_dir):
     return name, val
 
 
+def _value_info_type(b: bytes) -> tuple:
+    """ValueInfoProto -> (element type or None, [dim or None]) of a tensor type."""
+    elem, dims = None, []
+    for f, _, v in _fields(b):
+        if f != 2:  # TypeProto
+            continue
+        for ft, _, tv in _fields(v):
+            if ft != 1:  # TypeProto.Tensor
+                continue
+            for fe, _, ev in _fields(tv):
+                if fe == 1:
+                    elem = ev
+                elif fe == 2:  # TensorShapeProto
+                    for fd, _, dv in _fields(ev):
+                        if fd == 1:
+                            d = None
+                            for fv, _, vv in _fields(dv):
+                                if fv == 1:
+                                    d = _signed64(vv)
+                            dims.append(d)
+    return elem, dims
+
+
 def _value_info_name(b: bytes) -> str:
     for f, _, v in _fields(b):
         if f == 1:
@@ -219,7 +244,7 @@ def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
     """GraphProto -> OnnxModel (nodes, declared inputs and outputs, initializers).
     Subgraphs keep their initializer-backed inputs out of ``inputs`` like the
     main graph; names they use without defining come from the enclosing scope."""
-    nodes, inputs, outputs, inits = [], [], [], {}
+    nodes, inputs, outputs, inits, types = [], [], [], {}, {}
     for f, _, v in _fields(graph):
         if f == 1:
             n = Node("", [], [])
@@ -243,10 +268,11 @@ def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
             inits[k] = a
         elif f == 11:
             inputs.append(_value_info_name(v))
+            types[inputs[-1]] = _value_info_type(v)
         elif f == 12:
             outputs.append(_value_info_name(v))
     inputs = [i for i in inputs if i not in inits]
-    return OnnxModel(nodes, inputs, outputs, inits, opset)
+    return OnnxModel(nodes, inputs, outputs, inits, opset, {k: t for k, t in types.items() if k in inputs})
 
 
 def read_model(path: str) -> OnnxModel:
@@ -393,7 +419,10 @@ class OnnxGraph:
     def run(self, feeds: dict) -> dict:
         env = dict(self.consts)
         for k, v in feeds.items():
-            env[k] = v if isinstance(v, torch.Tensor) else torch.from_numpy(_contig(v))
+            if not isinstance(v, torch.Tensor):
+                v = _contig(v)
+                v = torch.from_numpy(v if v.flags.writeable else v.copy())  # request buffers are read-only
+            env[k] = v
             env[k] = env[k].to(self.device)
         key = tuple((k, tuple(v.shape), str(v.dtype)) for k, v in sorted(env.items()) if k in feeds)
         plan = self._plans.get(key) if self.plan_cache else None
@@ -1690,14 +1719,16 @@ def encode_tensor(name: str, a: np.ndarray) -> bytes:
     return b
 
 
-def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, opset: int = 13) -> bytes:
+def encode_model(nodes: list, inputs: list, outputs: list, initializers: dict, opset: int = 13,
+                 input_types: Optional[dict] = None) -> bytes:
     """Minimal ModelProto writer (for tests and synthetic exports).  A node
     attribute given as an :class:`OnnxModel` is written as a subgraph."""
-    g = _encode_graph(nodes, inputs, outputs, initializers)
+    g = _encode_graph(nodes, inputs, outputs, initializers, input_types)
     return _key(1, 0) + _enc_varint(8) + _ld(2, b"kapsl") + _ld(7, g) + _ld(8, _key(2, 0) + _enc_varint(opset))
 
 
-def _encode_graph(nodes: list, inputs: list, outputs: list, initializers: dict) -> bytes:
+def _encode_graph(nodes: list, inputs: list, outputs: list, initializers: dict, input_types: Optional[dict] = None
+                  ) -> bytes:
     g = b""
     for n in nodes:
         nb = b"".join(_ld(1, i.encode()) for i in n.inputs) + b"".join(_ld(2, o.encode()) for o in n.outputs)
@@ -1724,7 +1755,12 @@ def _encode_graph(nodes: list, inputs: list, outputs: list, initializers: dict) 
     for k, v in initializers.items():
         g += _ld(5, encode_tensor(k, v))
     for i in inputs:
-        g += _ld(11, _ld(1, i.encode()))
+        vi = _ld(1, i.encode())
+        if input_types and i in input_types:  # TypeProto.Tensor: element type and shape
+            elem, dims = input_types[i]
+            shp = b"".join(_ld(1, _key(1, 0) + _enc_varint(d) if d is not None else _ld(2, b"n")) for d in dims)
+            vi += _ld(2, _ld(1, _key(1, 0) + _enc_varint(elem) + _ld(2, shp)))
+        g += _ld(11, vi)
     for o in outputs:
         g += _ld(12, _ld(1, o.encode()))
     return g

@@ -68,6 +68,7 @@ class OnnxBackend(Engine):
         for nt in request.additional_inputs:
             nt.tensor.validate()
             feeds[nt.name] = nt.tensor.to_numpy()
+        self._fill_decoder_inputs(feeds)
         missing = [n for n in self.model.inputs if n not in feeds]
         if missing:
             raise EngineError.invalid_input(f"missing model inputs: {missing}")
@@ -85,6 +86,31 @@ class OnnxBackend(Engine):
         if arr.dtype == np.bool_:
             arr = arr.astype(np.uint8)
         return BinaryTensorPacket.from_numpy(arr)
+
+    def _fill_decoder_inputs(self, feeds: dict) -> None:
+        """Inputs of decoder exports that the request leaves out, filled as the
+        reference backend fills them (crates/kapsl-backends/src/onnx.rs:903-1000), with
+        batch and sequence length from the main input [batch, seq]: ``*attention_mask*``
+        all ones [batch, seq] int64, ``*position_ids*`` 0..seq-1 per row int64, and
+        ``past_key_values*`` empty [batch, heads, 0, head_dim] caches, heads and head_dim
+        from the declared input shape (1 and 64 where it is symbolic)."""
+        main = feeds[self.model.inputs[0]]
+        batch = int(main.shape[0]) if main.ndim > 0 else 1
+        seq = int(main.shape[1]) if main.ndim > 1 else 1
+        dtypes = {1: np.float32, 10: np.float16, 11: np.float64}
+        for name in self.model.inputs[1:]:
+            if name in feeds:
+                continue
+            if "attention_mask" in name:
+                feeds[name] = np.ones((batch, seq), np.int64)
+            elif "position_ids" in name:
+                feeds[name] = np.tile(np.arange(seq, dtype=np.int64), (batch, 1))
+            elif name.startswith("past_key_values"):
+                elem, dims = self.model.input_types.get(name, (None, []))
+                if len(dims) == 4:
+                    h = dims[1] if dims[1] and dims[1] > 0 else 1
+                    d = dims[3] if dims[3] and dims[3] > 0 else 64
+                    feeds[name] = np.zeros((batch, h, 0, d), dtypes.get(elem, np.float32))
 
     def model_info(self) -> EngineModelInfo:
         if self.model is None:

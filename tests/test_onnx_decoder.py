@@ -156,3 +156,34 @@ def test_session_continuation_reuses_the_previous_turn(export_dir):
         eng.step()
     hist = [5, 9, 13] + s1.output_ids + [7, 3]
     assert s2.output_ids == recompute_greedy(path, hist, 4)
+
+
+def test_unary_onnx_backend_fills_decoder_inputs(tmp_path):
+    """Sent only input_ids, the generic ONNX backend fills attention_mask,
+    position_ids and empty past caches (shapes from the declared inputs) and
+    returns the logits, equal to a run with those inputs given explicitly."""
+    from kapsl_sdk_b200.engine_api import BinaryTensorPacket, InferenceRequest
+    from kapsl_sdk_b200.runtime.backends import OnnxBackend
+
+    rng = np.random.default_rng(1)
+    emb = rng.standard_normal((16, 8)).astype(np.float32)
+    nodes = [Node("Gather", ["emb", "input_ids"], ["h"]),
+             Node("Cast", ["position_ids"], ["pf"], attrs={"to": 1}), Node("Unsqueeze", ["pf", "ax"], ["p3"]),
+             Node("Add", ["h", "p3"], ["hp"]),
+             Node("Cast", ["attention_mask"], ["mf"], attrs={"to": 1}), Node("Unsqueeze", ["mf", "ax"], ["m3"]),
+             Node("Mul", ["hp", "m3"], ["logits"]),
+             Node("Concat", ["past_key_values.0.key", "kv"], ["present.0.key"], attrs={"axis": 2}),
+             Node("Concat", ["past_key_values.0.value", "kv"], ["present.0.value"], attrs={"axis": 2})]
+    inits = {"emb": emb, "ax": np.array([-1], np.int64), "kv": np.zeros((1, 2, 1, 4), np.float32)}
+    types = {"input_ids": (7, [None, None]), "attention_mask": (7, [None, None]), "position_ids": (7, [None, None]),
+             "past_key_values.0.key": (1, [None, 2, None, 4]), "past_key_values.0.value": (1, [None, 2, None, 4])}
+    inputs = list(types)
+    p = str(tmp_path / "m.onnx")
+    open(p, "wb").write(encode_model(nodes, inputs, ["logits", "present.0.key", "present.0.value"], inits,
+                                     input_types=types))
+    assert read_model(p).input_types["past_key_values.0.key"] == (1, [None, 2, None, 4])
+    be = OnnxBackend(device="cpu")
+    be.load(p)
+    ids = np.array([[3, 5, 7]], np.int64)
+    out = be.infer(InferenceRequest(input=BinaryTensorPacket.from_numpy(ids))).to_numpy()
+    assert np.allclose(out, emb[ids] + np.arange(3, dtype=np.float32)[None, :, None])
