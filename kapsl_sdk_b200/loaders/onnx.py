@@ -123,6 +123,7 @@ class OnnxModel:
     opset: int = 13
     # declared input types: name -> (TensorProto element type or None, dims with None for symbolic ones)
     input_types: dict = field(default_factory=dict)
+    output_types: dict = field(default_factory=dict)
 
 
 def _tensor(b: bytes, base_dir: Optional[str]) -> tuple:
@@ -244,7 +245,7 @@ def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
     """GraphProto -> OnnxModel (nodes, declared inputs and outputs, initializers).
     Subgraphs keep their initializer-backed inputs out of ``inputs`` like the
     main graph; names they use without defining come from the enclosing scope."""
-    nodes, inputs, outputs, inits, types = [], [], [], {}, {}
+    nodes, inputs, outputs, inits, types, out_types = [], [], [], {}, {}, {}
     for f, _, v in _fields(graph):
         if f == 1:
             n = Node("", [], [])
@@ -271,8 +272,9 @@ def _graph(graph: bytes, base: Optional[str], opset: int = 13) -> OnnxModel:
             types[inputs[-1]] = _value_info_type(v)
         elif f == 12:
             outputs.append(_value_info_name(v))
+            out_types[outputs[-1]] = _value_info_type(v)
     inputs = [i for i in inputs if i not in inits]
-    return OnnxModel(nodes, inputs, outputs, inits, opset, {k: t for k, t in types.items() if k in inputs})
+    return OnnxModel(nodes, inputs, outputs, inits, opset, {k: t for k, t in types.items() if k in inputs}, out_types)
 
 
 def read_model(path: str) -> OnnxModel:

@@ -115,8 +115,19 @@ class OnnxBackend(Engine):
     def model_info(self) -> EngineModelInfo:
         if self.model is None:
             return EngineModelInfo()
+        names = {1: "float32", 11: "float64", 10: "float16", 6: "int32", 7: "int64", 2: "uint8", 8: "string"}
+
+        def describe(types, keys):  # declared shapes (-1 for symbolic dims) and dtype names, as ORT reports them
+            shapes = [[-1 if d is None else d for d in types.get(k, (None, []))[1]] for k in keys]
+            dts = [names.get(types.get(k, (None, []))[0], "unknown") for k in keys]
+            return shapes, dts
+
+        ins, in_dt = describe(self.model.input_types, self.model.inputs)
+        outs, out_dt = describe(self.model.output_types, self.model.outputs)
+        peak = os.environ.get("KAPSL_MODEL_PEAK_CONCURRENCY")
         return EngineModelInfo(input_names=list(self.model.inputs), output_names=list(self.model.outputs),
-                               framework="onnx")
+                               input_shapes=ins, output_shapes=outs, input_dtypes=in_dt, output_dtypes=out_dt,
+                               framework="onnx", peak_concurrency=max(1, int(peak)) if peak else None)
 
     def metrics(self) -> EngineMetrics:
         return self._m

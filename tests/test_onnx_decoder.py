@@ -187,3 +187,17 @@ def test_unary_onnx_backend_fills_decoder_inputs(tmp_path):
     ids = np.array([[3, 5, 7]], np.int64)
     out = be.infer(InferenceRequest(input=BinaryTensorPacket.from_numpy(ids))).to_numpy()
     assert np.allclose(out, emb[ids] + np.arange(3, dtype=np.float32)[None, :, None])
+
+
+def test_onnx_backend_model_info_reports_declared_types(tmp_path, monkeypatch):
+    from kapsl_sdk_b200.runtime.backends import OnnxBackend
+
+    p = str(tmp_path / "m.onnx")
+    open(p, "wb").write(encode_model([Node("Relu", ["x"], ["y"])], ["x"], ["y"], {},
+                                     input_types={"x": (1, [None, 4])}))
+    monkeypatch.setenv("KAPSL_MODEL_PEAK_CONCURRENCY", "3")
+    be = OnnxBackend(device="cpu")
+    be.load(p)
+    info = be.model_info()
+    assert info.input_shapes == [[-1, 4]] and info.input_dtypes == ["float32"]
+    assert info.output_dtypes == ["unknown"] and info.framework == "onnx" and info.peak_concurrency == 3
