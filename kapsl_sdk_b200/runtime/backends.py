@@ -65,6 +65,11 @@ class OnnxBackend(Engine):
         if request.input.dtype is TensorDtype.UTF8:
             raise EngineError.invalid_input("ONNX backend expects numeric input")
         feeds = {self.model.inputs[0]: request.input.to_numpy()}
+        seen = set()
+        for nt in request.additional_inputs:  # reference onnx.rs:747-764
+            if nt.name in seen:
+                raise EngineError.invalid_input(f"Duplicate additional input name: {nt.name}")
+            seen.add(nt.name)
         for nt in request.additional_inputs:
             nt.tensor.validate()
             feeds[nt.name] = nt.tensor.to_numpy()

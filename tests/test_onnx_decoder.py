@@ -201,3 +201,19 @@ def test_onnx_backend_model_info_reports_declared_types(tmp_path, monkeypatch):
     info = be.model_info()
     assert info.input_shapes == [[-1, 4]] and info.input_dtypes == ["float32"]
     assert info.output_dtypes == ["unknown"] and info.framework == "onnx" and info.peak_concurrency == 3
+
+
+def test_onnx_backend_rejects_duplicate_additional_inputs(tmp_path):
+    from kapsl_sdk_b200.engine_api import (BinaryTensorPacket, EngineError, InferenceRequest, NamedTensor)
+    from kapsl_sdk_b200.runtime.backends import OnnxBackend
+
+    p = str(tmp_path / "m.onnx")
+    open(p, "wb").write(encode_model([Node("Add", ["x", "b"], ["y"])], ["x", "b"], ["y"], {}))
+    be = OnnxBackend(device="cpu")
+    be.load(p)
+    one = BinaryTensorPacket.from_numpy(np.ones(2, np.float32))
+    req = InferenceRequest(input=one, additional_inputs=[NamedTensor("b", one), NamedTensor("b", one)])
+    with pytest.raises(EngineError, match="Duplicate additional input name: b"):
+        be.infer(req)
+    req = InferenceRequest(input=one, additional_inputs=[NamedTensor("b", one)])
+    assert np.allclose(be.infer(req).to_numpy(), 2.0)
