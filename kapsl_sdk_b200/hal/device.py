@@ -56,18 +56,45 @@ class DeviceInfo:
     def gpus(self) -> list:
         return [d for d in self.devices if d.backend is DeviceBackend.CUDA]
 
+    def cuda_devices(self) -> list:
+        return self.gpus()
+
+    def _has(self, backend: DeviceBackend) -> bool:
+        return any(d.backend is backend for d in self.devices)
+
     def has_cuda(self) -> bool:
-        return bool(self.gpus())
+        return self._has(DeviceBackend.CUDA)
 
     def best_gpu(self) -> Optional[Device]:
-        g = self.gpus()
+        """The accelerator (any backend but the CPU) with the most memory, then the
+        highest compute capability (reference device.rs:770-793)."""
+        g = [d for d in self.devices if d.backend is not DeviceBackend.CPU]
         if not g:
             return None
         return max(g, key=lambda d: (d.total_memory_mb, d.compute_capability or (0, 0), -d.id))
 
+    def best_gpu_with_preference(self, preference: "GpuPreference") -> Optional[Device]:
+        """The first accelerator the preference matches, or None."""
+        return next((d for d in self.devices if d.backend is not DeviceBackend.CPU and preference.matches(d)), None)
+
     def get_best_provider(self) -> str:
-        """cuda > metal > rocm > oneapi > directml > cpu (only cuda/cpu exist here)."""
-        return "cuda" if self.has_cuda() else "cpu"
+        """cuda > metal > rocm > oneapi > directml > cpu over the backends present
+        (reference device.rs:807-826)."""
+        for b in (DeviceBackend.CUDA, DeviceBackend.METAL, DeviceBackend.ROCM, DeviceBackend.ONEAPI,
+                  DeviceBackend.DIRECTML):
+            if self._has(b):
+                return b.value
+        return "cpu"
+
+    def has_provider(self, provider: str) -> bool:
+        """Whether an execution provider can run here; ``coreml`` rides on Metal
+        and ``cpu`` is always there (reference device.rs:828-850)."""
+        key = provider.strip().lower()
+        if key == "cpu":
+            return True
+        if key == "coreml":
+            key = "metal"
+        return any(d.backend.value == key for d in self.devices)
 
     def select(self, preference: Optional[str]) -> Optional[Device]:
         p = GpuPreference.parse(preference or "")

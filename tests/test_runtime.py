@@ -415,3 +415,31 @@ def test_native_work_queue_under_concurrent_producers_and_consumers():
     assert q2.put("c", 0, False) == (False, None)     # non-blocking put on a full queue
     assert q2.put("d", 2, True) == (True, "a")        # drop oldest: "a" evicted
     assert q2.take(4, 0.0) == ["d"]
+
+
+def test_device_info_helpers_follow_the_reference():
+    from kapsl_sdk_b200.hal.device import Device, DeviceBackend, DeviceInfo, GpuPreference
+
+    def dev(i, b, mem, **kw):
+        return Device(i, f"dev{i}", b, mem, **kw)
+
+    info = DeviceInfo(8, 1000, [dev(0, DeviceBackend.CPU, 1024), dev(1, DeviceBackend.CUDA, 12000),
+                                dev(2, DeviceBackend.METAL, 8000)])
+    assert info.best_gpu().id == 1 and [d.id for d in info.cuda_devices()] == [1]
+    assert DeviceInfo(8, 1000, [dev(0, DeviceBackend.CPU, 1024)]).best_gpu() is None
+    assert DeviceInfo(8, 1000, [dev(0, DeviceBackend.METAL, 9000)]).best_gpu().id == 0  # any accelerator
+    assert info.get_best_provider() == "cuda"
+    assert all(info.has_provider(p) for p in ("cuda", "metal", "coreml", "cpu", " CUDA "))
+    assert not info.has_provider("rocm")
+    assert DeviceInfo(8, 1000, [dev(0, DeviceBackend.ROCM, 9000)]).get_best_provider() == "rocm"
+    parts = DeviceInfo(8, 1000, [dev(0, DeviceBackend.CPU, 1), dev(0, DeviceBackend.CUDA, 8000, partition_id="GPU-aaa"),
+                                 dev(1, DeviceBackend.CUDA, 8000, partition_id="GPU-bbb")])
+    assert parts.best_gpu_with_preference(GpuPreference.parse("partition:GPU-BBB")).id == 1
+    assert parts.best_gpu_with_preference(GpuPreference.parse("mig:GPU-ccc")) is None
+    a100 = Device(0, "NVIDIA A100 80GB PCIe", DeviceBackend.CUDA, 8000, pci_bus_id="0000:03:00.0")
+    assert GpuPreference.parse("a100").matches(a100) and GpuPreference.parse("80GB").matches(a100)
+    assert not GpuPreference.parse("H100").matches(a100)
+    assert GpuPreference.parse("0000:03:00.0".upper()).matches(a100)
+    assert not GpuPreference.parse("0000:04:00.0").matches(a100)
+    assert GpuPreference.parse("cuda:0").matches(a100) and not GpuPreference.parse("cuda:2").matches(a100)
+    assert GpuPreference.parse("") is None and GpuPreference.parse("  ") is None
