@@ -172,6 +172,66 @@ class BackendFactory:
             seen.append("cpu")
         return seen
 
+    @staticmethod
+    def check_requirements(req: HardwareRequirements, info: DeviceInfo) -> Optional[str]:
+        """The reference's requirement check (crates/kapsl-backends/src/factory.rs:414-586)
+        with its error texts: None when the host memory suffices and one of the
+        preferred / fallback providers has a device that meets the VRAM and CUDA
+        version minimums (any device of the backend under a multi-device strategy,
+        else ``device_id``, default 0); otherwise the reason(s).  CUDA versions are
+        compared numerically (the reference compares the strings)."""
+        if req.min_memory_mb is not None and info.total_memory_mb < req.min_memory_mb:
+            return f"Insufficient memory: need {req.min_memory_mb}MB, have {info.total_memory_mb}MB"
+        providers = ([req.preferred_provider] if req.preferred_provider else []) + list(req.fallback_providers)
+        if not providers:
+            return None
+        strategy = (req.strategy or "").lower()
+        multi = strategy in ("pool", "round-robin", "data-parallel", "pipeline", "pipeline-parallel",
+                             "tensor-parallel", "auto")
+
+        def ver(v):
+            return tuple(int(x) for x in str(v).split(".") if x.isdigit())
+
+        def too_old(backend) -> Optional[str]:
+            if backend != "cuda" or not req.min_cuda_version:
+                return None
+            if not info.cuda_version:
+                return "Unknown CUDA version on device"
+            if ver(info.cuda_version) < ver(req.min_cuda_version):
+                return f"CUDA version too old: {info.cuda_version} < required {req.min_cuda_version}"
+            return None
+
+        reasons = []
+        for provider in providers:
+            backend = {"tensorrt": "cuda", "coreml": "metal"}.get(provider.lower(), provider.lower())
+            if backend == "cpu":
+                return None
+            if not info.has_provider(backend):
+                reasons.append(f"Provider {provider} not available")
+                continue
+            devs = [d for d in info.devices if d.backend.value == backend]
+            if multi:
+                if any((req.min_vram_mb is None or d.total_memory_mb >= req.min_vram_mb) and too_old(backend) is None
+                       for d in devs):
+                    return None
+                reasons.append(f"No devices meet requirements for provider {provider}")
+                continue
+            dev_id = req.device_id or 0
+            d = next((d for d in devs if d.id == dev_id), None)
+            if d is None:
+                reasons.append(f"Device ID {dev_id} not found for provider {provider}")
+                continue
+            if req.min_vram_mb is not None and d.total_memory_mb < req.min_vram_mb:
+                reasons.append(f"Provider {provider} (Device {dev_id}) has insufficient VRAM: "
+                               f"{d.total_memory_mb}MB < required {req.min_vram_mb}MB")
+                continue
+            old = too_old(backend)
+            if old:
+                reasons.append(old)
+                continue
+            return None
+        return "No compatible provider found. Reasons: " + repr(reasons)
+
     def validate_requirements(self, manifest: Manifest, provider: str = "cuda") -> list:
         """Unmet requirements as messages (empty list = OK)."""
         hw = manifest.hardware_requirements

@@ -443,3 +443,29 @@ def test_device_info_helpers_follow_the_reference():
     assert not GpuPreference.parse("0000:04:00.0").matches(a100)
     assert GpuPreference.parse("cuda:0").matches(a100) and not GpuPreference.parse("cuda:2").matches(a100)
     assert GpuPreference.parse("") is None and GpuPreference.parse("  ") is None
+
+
+def test_requirement_check_matches_the_reference_cases():
+    """The reference factory tests' cases: host memory, VRAM and CUDA version
+    minimums on the requested device, missing providers and their fallbacks,
+    unknown device ids and multi-device strategies, with its error texts."""
+    from kapsl_sdk_b200.hal.device import Device, DeviceBackend, DeviceInfo
+    from kapsl_sdk_b200.runtime.backends import BackendFactory
+    from kapsl_sdk_b200.runtime.loader import HardwareRequirements as HR
+
+    info = DeviceInfo(8, 16 * 1024, [Device(0, "cpu", DeviceBackend.CPU, 16 * 1024),
+                                     Device(1, "RTX 3080", DeviceBackend.CUDA, 10 * 1024)], cuda_version="12.0")
+    check = BackendFactory.check_requirements
+    assert check(HR(min_memory_mb=8 * 1024), info) is None
+    assert "Insufficient memory" in check(HR(min_memory_mb=32 * 1024), info)
+    assert check(HR(preferred_provider="cuda", device_id=1, min_vram_mb=8 * 1024), info) is None
+    assert "insufficient VRAM" in check(HR(preferred_provider="cuda", device_id=1, min_vram_mb=12 * 1024), info)
+    assert check(HR(preferred_provider="cuda", device_id=1, min_cuda_version="11.8"), info) is None
+    assert "CUDA version too old" in check(HR(preferred_provider="cuda", device_id=1, min_cuda_version="12.1"), info)
+    assert "Provider metal not available" in check(HR(preferred_provider="metal"), info)
+    assert check(HR(preferred_provider="metal", fallback_providers=["cpu"]), info) is None
+    assert "Device ID 99 not found" in check(HR(preferred_provider="cuda", device_id=99), info)
+    assert check(HR(preferred_provider="cuda", min_vram_mb=9 * 1024, strategy="pool"), info) is None
+    assert "No devices meet requirements" in check(HR(preferred_provider="cuda", min_vram_mb=20000, strategy="pool"),
+                                                  info)
+    assert check(HR(), info) is None
