@@ -293,6 +293,7 @@ class EnginePool:
         self._lock = threading.RLock()
         self._stop = threading.Event()
         self._thread = None
+        self._stats = {"hit": 0, "failure": 0, "evictions": 0}
 
     def put(self, model_id: int, device_id: int, engine: Engine, warmup: bool = False) -> None:
         if warmup:
@@ -302,7 +303,28 @@ class EnginePool:
             self._m.move_to_end((model_id, device_id))
             while len(self._m) > self.capacity:
                 key, old = self._m.popitem(last=False)
+                self._stats["evictions"] += 1
                 self._evict(key, old)
+
+    def warmup(self, configs: list, factory: Callable) -> None:
+        """Pre-create engines: ``factory(model_id, device_id)`` for each pair; one
+        whose creation fails is skipped and the others still load (reference
+        engine_pool.rs:250-285)."""
+        for model_id, device_id in configs:
+            try:
+                eng = factory(model_id, device_id)
+            except Exception:
+                continue
+            self.put(model_id, device_id, eng)
+
+    def pool_metrics(self) -> dict:
+        """Hits (healthy gets), failures (gets that found an unhealthy engine, which
+        is removed), LRU evictions and the hit rate (reference engine_pool.rs:14-19, 287-291)."""
+        with self._lock:
+            m = dict(self._stats)
+        tot = m["hit"] + m["failure"]
+        m["hit_rate"] = m["hit"] / tot if tot else 0.0
+        return m
 
     def _evict(self, key, eng) -> None:
         try:
@@ -318,9 +340,11 @@ class EnginePool:
                 return None
             if not eng.health_check():
                 del self._m[(model_id, device_id)]
+                self._stats["failure"] += 1
                 self._evict((model_id, device_id), eng)
                 return None
             self._m.move_to_end((model_id, device_id))
+            self._stats["hit"] += 1
             return eng
 
     def remove(self, model_id: int, device_id: int) -> bool:

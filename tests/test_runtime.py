@@ -469,3 +469,35 @@ def test_requirement_check_matches_the_reference_cases():
     assert "No devices meet requirements" in check(HR(preferred_provider="cuda", min_vram_mb=20000, strategy="pool"),
                                                   info)
     assert check(HR(), info) is None
+
+
+def test_engine_pool_warmup_skips_failures_and_reports_metrics():
+    from kapsl_sdk_b200.engine_api import EngineError
+    from kapsl_sdk_b200.runtime.backends import EnginePool
+
+    class Eng:
+        def __init__(self):
+            self.healthy = True
+
+        def health_check(self):
+            return self.healthy
+
+        def unload(self):
+            pass
+
+    def factory(model_id, device_id):
+        if model_id == 1:
+            raise EngineError.backend("warmup failed")
+        return Eng()
+
+    evicted = []
+    pool = EnginePool(capacity=2, on_evict=evicted.append)
+    pool.warmup([(1, 0), (2, 0)], factory)
+    assert len(pool) == 1 and pool.get(2, 0) is not None and pool.get(1, 0) is None
+    pool.put(3, 0, Eng())
+    pool.put(4, 0, Eng())  # capacity 2: (2, 0) is least recently used
+    assert evicted == [(2, 0)]
+    pool.get(4, 0).healthy = False
+    assert pool.get(4, 0) is None  # unhealthy: removed on get
+    m = pool.pool_metrics()
+    assert m["hit"] == 2 and m["failure"] == 1 and m["evictions"] == 1 and abs(m["hit_rate"] - 2 / 3) < 1e-9
